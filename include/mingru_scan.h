@@ -1,0 +1,93 @@
+/*
+ * mingru_scan.h -- C ABI of the B200 (sm_100a) scan kernels behind the mingru
+ * scan family.
+ *
+ * Every entry point takes plain device pointers, int64 sizes, a dtype code, a
+ * caller-owned workspace and a CUDA stream (as `void*`), and returns an
+ * `mgs_status`. Nothing here allocates device memory, synchronises the host
+ * or keeps per-call global state: outputs, gradients, saved carries and
+ * workspaces are allocated by the caller (the torch extension uses torch's
+ * caching allocator on the current stream). All tensors are dense, C-ordered
+ * and 16-byte aligned where the kernels vectorise; the wrappers check this
+ * and return MGS_BAD_ALIGNMENT / MGS_BAD_SHAPE instead of launching.
+ *
+ * Each function cites the reference interface it replaces (paths are inside
+ * the chris-santiago/minGRU project, package `mingru`, files
+ * src/mingru/min_gru.py = "min_gru.py" and src/mingru/triton_scans.py =
+ * "triton_scans.py").
+ */
+#ifndef MINGRU_SCAN_H
+#define MINGRU_SCAN_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Status codes. The reference signals a declined kernel with
+ * `ScanFallback` (triton_scans.py:166) and silently runs eager; this ABI has
+ * no fallback: every failure is returned and raised by the caller. */
+typedef enum mgs_status {
+  MGS_OK = 0,
+  MGS_BAD_SHAPE = 1,          /* inconsistent / negative sizes            */
+  MGS_BAD_DTYPE = 2,          /* dtype code not supported by this op      */
+  MGS_BAD_ALIGNMENT = 3,      /* a pointer is not aligned as required     */
+  MGS_UNSUPPORTED = 4,        /* shape outside the kernel envelope        */
+  MGS_LAUNCH_FAILED = 5,      /* cudaLaunch / cudaMemsetAsync error       */
+  MGS_LOOKBACK_TIMEOUT = 6,   /* a decoupled look-back wait hit its bound */
+  MGS_WORKSPACE_TOO_SMALL = 7 /* workspace / carry buffer under-sized     */
+} mgs_status;
+
+/* Element type of the tensors an op reads and writes. Arithmetic and every
+ * carried state are fp32 regardless (the reference kernels load, upcast to
+ * fp32, accumulate in fp32 and store in the input dtype: triton_scans.py:1312). */
+typedef enum mgs_dtype { MGS_F32 = 0, MGS_BF16 = 1, MGS_F16 = 2 } mgs_dtype;
+
+/* Library version (major*10000 + minor*100 + patch). */
+int mgs_version(void);
+
+/* Human-readable name of a status code (static storage). */
+const char* mgs_status_string(int status);
+
+/* Sticky device-side error word of the current device (look-back timeouts).
+ * Synchronises `stream`, returns the accumulated MGS_* bits (0 if clean) and
+ * clears them. Kernels never trap: a bounded wait that runs out records
+ * MGS_LOOKBACK_TIMEOUT here and lets the launch finish. */
+int mgs_take_device_error(void* stream);
+
+/* ------------------------------------------------------------------------ */
+/* linear_scan: h_t = a_t * h_{t-1} + b_t, returns (A, Bc) with
+ * A_t = prod_{s<=t} a_s and Bc_t the h_0 = 0 solution.
+ * Replaces min_gru.py:1454 `linear_scan(a, b)` (eager doubling at
+ * min_gru.py:1501-1510) and its Triton kernels triton_scans.py:702-751
+ * (forward) / 961-1036 (backward), ops linear_scan_fwd / linear_scan_bwd
+ * (triton_scans.py:1318, 1392) and their autograd (triton_scans.py:1465-1487).
+ * Layout: a, b, A, Bc, da, db, gA, gBc are (B, T, D) C-contiguous.           */
+
+/* Bytes of look-back workspace one forward or backward call needs. */
+size_t mgs_linear_scan_workspace_size(int64_t B, int64_t T, int64_t D, int dtype);
+/* Bytes of the forward carries the backward consumes (fp32 chunk-start
+ * states, a few percent of one input tensor). */
+size_t mgs_linear_scan_carry_size(int64_t B, int64_t T, int64_t D, int dtype);
+
+/* Forward. `carries` may be NULL (no backward will follow). */
+int mgs_linear_scan_fwd(const void* a, const void* b, void* A, void* Bc,
+                        void* carries, int64_t B, int64_t T, int64_t D,
+                        int dtype, void* workspace, size_t workspace_bytes,
+                        void* stream);
+
+/* Backward: given the forward inputs (a, b), the carries the forward wrote
+ * and the output grads (gA, gBc), write (da, db). Recomputes A_{t-1},
+ * Bc_{t-1} in registers from the carries instead of reading saved outputs. */
+int mgs_linear_scan_bwd(const void* a, const void* b, const void* gA,
+                        const void* gBc, const void* carries, void* da,
+                        void* db, int64_t B, int64_t T, int64_t D, int dtype,
+                        void* workspace, size_t workspace_bytes, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* MINGRU_SCAN_H */

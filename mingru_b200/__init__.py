@@ -1,0 +1,18 @@
+"""mingru_b200 -- the mingru scan hot path as hand-written sm_100a CUDA kernels.
+
+A drop-in for the scan family of chris-santiago/minGRU (``mingru`` 0.2.1):
+the four public scan functions and the modules that call them run on the
+B200 kernels of ``libmingru_scan.so`` through its C ABI
+(``include/mingru_scan.h``). There is no Triton, no backend switch and no CPU
+fallback: CPU tensors raise.
+"""
+
+from .scan_ops import linear_scan, raise_device_error, take_device_error
+
+__version__ = "0.1.0"
+
+__all__ = [
+    "linear_scan",
+    "raise_device_error",
+    "take_device_error",
+]

@@ -1,0 +1,264 @@
+// common.cuh -- shared device machinery for the chunked look-back scans.
+//
+// Every scan in this library is a first-order affine recurrence over a time
+// axis, x_t = M_t x_{t-1} + u_t, whose per-segment aggregates form a monoid
+// under composition. The kernels tile (time x channels): a CTA takes one tile
+// from an atomic tile counter (so every tile it waits on was handed out
+// earlier and is already running), reduces its segment locally in registers,
+// publishes the aggregate, and walks back over the preceding tiles of the same
+// channel strip until it meets an inclusive prefix ("decoupled look-back",
+// Merrill & Garland 2016). Waits are bounded: a wait that runs out records
+// MGS_LOOKBACK_TIMEOUT in the per-call workspace header and in a sticky device
+// word, then proceeds, so no launch can hang a GPU.
+#pragma once
+
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "../../include/mingru_scan.h"
+
+namespace mgs {
+
+// ---------------------------------------------------------------- dtypes --
+
+template <typename T>
+__device__ __forceinline__ float to_f32(T v);
+template <>
+__device__ __forceinline__ float to_f32<float>(float v) { return v; }
+template <>
+__device__ __forceinline__ float to_f32<__nv_bfloat16>(__nv_bfloat16 v) {
+  return __bfloat162float(v);
+}
+template <>
+__device__ __forceinline__ float to_f32<__half>(__half v) { return __half2float(v); }
+
+template <typename T>
+__device__ __forceinline__ T from_f32(float v);
+template <>
+__device__ __forceinline__ float from_f32<float>(float v) { return v; }
+template <>
+__device__ __forceinline__ __nv_bfloat16 from_f32<__nv_bfloat16>(float v) {
+  return __float2bfloat16_rn(v);
+}
+template <>
+__device__ __forceinline__ __half from_f32<__half>(float v) { return __float2half_rn(v); }
+
+template <int BYTES>
+struct VecOf;
+template <>
+struct VecOf<16> { using type = uint4; };
+template <>
+struct VecOf<8> { using type = uint2; };
+template <>
+struct VecOf<4> { using type = unsigned; };
+template <>
+struct VecOf<2> { using type = unsigned short; };
+
+// Load N consecutive elements (one vector access of N*sizeof(T) <= 16 bytes;
+// the caller guarantees alignment) and widen to fp32. Streaming hint: every
+// input element is read exactly once per kernel.
+template <typename T, int N>
+__device__ __forceinline__ void load_vec(const T* __restrict__ p, float (&out)[N]) {
+  static_assert(N * sizeof(T) <= 16, "vector too wide");
+  using V = typename VecOf<N * sizeof(T)>::type;
+  V v = __ldcs(reinterpret_cast<const V*>(p));
+  const T* e = reinterpret_cast<const T*>(&v);
+#pragma unroll
+  for (int i = 0; i < N; ++i) out[i] = to_f32<T>(e[i]);
+}
+
+template <typename T, int N>
+__device__ __forceinline__ void store_vec(T* __restrict__ p, const float (&in)[N]) {
+  static_assert(N * sizeof(T) <= 16, "vector too wide");
+  using V = typename VecOf<N * sizeof(T)>::type;
+  V v;
+  T* e = reinterpret_cast<T*>(&v);
+#pragma unroll
+  for (int i = 0; i < N; ++i) e[i] = from_f32<T>(in[i]);
+  __stcs(reinterpret_cast<V*>(p), v);
+}
+
+// ------------------------------------------------------- memory ordering --
+
+__device__ __forceinline__ unsigned ld_acquire_u32(const unsigned* p) {
+  unsigned v;
+  asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
+__device__ __forceinline__ void st_release_u32(unsigned* p, unsigned v) {
+  asm volatile("st.release.gpu.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+
+__device__ __forceinline__ unsigned ld_relaxed_u32(const unsigned* p) {
+  unsigned v;
+  asm volatile("ld.relaxed.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
+// ------------------------------------------------------------- workspace --
+//
+// Per-call look-back workspace (caller allocated, header + flags zeroed by
+// the launcher with one cudaMemsetAsync):
+//   [0]          u32 tile counter
+//   [1]          u32 per-call error bits
+//   [256 ..)     u32 flags[ntiles]              0 = empty, 1 = aggregate, 2 = inclusive
+//   [..)         f32 agg[ntiles][NF][32]
+//   [..)         f32 incl[ntiles][NF][32]
+// NF = floats each lane of the look-back warp carries.
+
+constexpr unsigned kFlagEmpty = 0u;
+constexpr unsigned kFlagAgg = 1u;
+constexpr unsigned kFlagIncl = 2u;
+constexpr unsigned kErrTimeout = 1u << MGS_LOOKBACK_TIMEOUT;
+
+// Upper bound on polls of one flag (~ a second with the backoff below).
+constexpr long long kSpinLimit = 1ll << 24;
+
+struct Lookback {
+  unsigned* counter;
+  unsigned* err;
+  unsigned* flags;
+  float* agg;
+  float* incl;
+};
+
+// Sticky error word of this translation unit (each .cu file that includes
+// this header owns one); read and cleared by the file's take_sticky_error().
+static __device__ unsigned g_sticky_err = 0u;
+
+static inline unsigned take_sticky_error(cudaStream_t stream) {
+  unsigned v = 0u, zero = 0u;
+  if (cudaMemcpyFromSymbolAsync(&v, g_sticky_err, sizeof(v), 0, cudaMemcpyDeviceToHost, stream) !=
+      cudaSuccess)
+    return 1u << MGS_LAUNCH_FAILED;
+  if (cudaMemcpyToSymbolAsync(g_sticky_err, &zero, sizeof(zero), 0, cudaMemcpyHostToDevice,
+                              stream) != cudaSuccess)
+    return 1u << MGS_LAUNCH_FAILED;
+  if (cudaStreamSynchronize(stream) != cudaSuccess) return 1u << MGS_LAUNCH_FAILED;
+  return v;
+}
+
+__host__ __device__ inline size_t align_up(size_t x, size_t a) { return (x + a - 1) / a * a; }
+
+inline size_t lookback_bytes(long long ntiles, int nf) {
+  size_t flags = align_up((size_t)ntiles * 4, 256);
+  size_t elem = (size_t)ntiles * nf * 32 * 4;
+  return 256 + flags + 2 * elem;
+}
+
+inline size_t lookback_zero_bytes(long long ntiles) {
+  return 256 + align_up((size_t)ntiles * 4, 256);
+}
+
+inline Lookback lookback_view(void* ws, long long ntiles, int nf) {
+  char* base = static_cast<char*>(ws);
+  Lookback lb;
+  lb.counter = reinterpret_cast<unsigned*>(base);
+  lb.err = reinterpret_cast<unsigned*>(base) + 1;
+  lb.flags = reinterpret_cast<unsigned*>(base + 256);
+  size_t flags = align_up((size_t)ntiles * 4, 256);
+  lb.agg = reinterpret_cast<float*>(base + 256 + flags);
+  lb.incl = lb.agg + (size_t)ntiles * nf * 32;
+  return lb;
+}
+
+// Publish this lane's NF floats of `val` for `tile` and raise its flag.
+template <int NF>
+__device__ __forceinline__ void lb_publish(const Lookback& lb, long long tile, unsigned flag,
+                                           const float (&val)[NF]) {
+  const int lane = threadIdx.x & 31;
+  float* dst = (flag == kFlagIncl ? lb.incl : lb.agg) + (size_t)tile * NF * 32;
+#pragma unroll
+  for (int f = 0; f < NF; ++f) __stcg(dst + f * 32 + lane, val[f]);
+  __threadfence();
+  __syncwarp();
+  if (lane == 0) st_release_u32(lb.flags + tile, flag);
+}
+
+// Wait (bounded) until `tile` has published; returns the flag the whole warp
+// agrees on (the minimum any lane acquired: an aggregate stays valid once the
+// inclusive value also exists).
+__device__ __forceinline__ unsigned lb_wait(const Lookback& lb, long long tile) {
+  unsigned f = ld_acquire_u32(lb.flags + tile);
+  long long it = 0;
+  while (f == kFlagEmpty) {
+    if (++it > kSpinLimit) {
+      atomicOr(lb.err, kErrTimeout);
+      atomicOr(&g_sticky_err, kErrTimeout);
+      f = kFlagIncl;  // proceed with whatever is there; the host raises
+      break;
+    }
+    if ((it & 255) == 0 && ld_relaxed_u32(lb.err) != 0u) {
+      f = kFlagIncl;
+      break;
+    }
+    __nanosleep(32);
+    f = ld_acquire_u32(lb.flags + tile);
+  }
+  return __reduce_min_sync(0xffffffffu, f);
+}
+
+// Decoupled look-back run by one full warp. `Monoid` supplies
+//   static void identity(float (&x)[NF]);
+//   static void combine(const float (&earlier)[NF], const float (&later)[NF], float (&out)[NF]);
+// `tile` is the tile's position in processing order, `stride` the distance to
+// its predecessor in the same strip, `pos` its index along the strip (0 = the
+// first segment: no predecessor). On return `excl` holds the composition of
+// every earlier segment of the strip and the tile's inclusive value has been
+// published.
+template <class Monoid, int NF>
+__device__ __forceinline__ void warp_lookback(const Lookback& lb, long long tile, long long stride,
+                                              long long pos, const float (&agg)[NF],
+                                              float (&excl)[NF]) {
+  const int lane = threadIdx.x & 31;
+  if (pos == 0) {
+    Monoid::identity(excl);
+    lb_publish<NF>(lb, tile, kFlagIncl, agg);
+    return;
+  }
+  lb_publish<NF>(lb, tile, kFlagAgg, agg);
+  float run[NF];
+  Monoid::identity(run);
+  long long p = tile - stride;
+  while (true) {
+    const unsigned f = lb_wait(lb, p);
+    const float* src = (f == kFlagIncl ? lb.incl : lb.agg) + (size_t)p * NF * 32;
+    float e[NF], tmp[NF];
+#pragma unroll
+    for (int i = 0; i < NF; ++i) e[i] = __ldcg(src + i * 32 + lane);
+    Monoid::combine(e, run, tmp);
+#pragma unroll
+    for (int i = 0; i < NF; ++i) run[i] = tmp[i];
+    if (f == kFlagIncl || p < stride) break;
+    p -= stride;
+  }
+#pragma unroll
+  for (int i = 0; i < NF; ++i) excl[i] = run[i];
+  float inc[NF];
+  Monoid::combine(excl, agg, inc);
+  lb_publish<NF>(lb, tile, kFlagIncl, inc);
+}
+
+// Error-word helpers shared by the per-file launchers.
+#define MGS_CUDA_OK(expr)                          \
+  do {                                             \
+    if ((expr) != cudaSuccess) return MGS_LAUNCH_FAILED; \
+  } while (0)
+
+inline bool aligned(const void* p, size_t a) {
+  return (reinterpret_cast<uintptr_t>(p) % a) == 0;
+}
+
+inline int dtype_size(int dtype) {
+  switch (dtype) {
+    case MGS_F32: return 4;
+    case MGS_BF16: return 2;
+    case MGS_F16: return 2;
+    default: return 0;
+  }
+}
+
+}  // namespace mgs

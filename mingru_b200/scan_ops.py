@@ -1,0 +1,192 @@
+"""The public scan ops, backed only by the sm_100a kernels of ``libmingru_scan.so``.
+
+Drop-in replacements for the reference's four public scan functions
+(``parallel_scan_log``, ``linear_scan``, ``matrix_scan``,
+``matrix_affine_scan``; reference ``src/mingru/min_gru.py:755, 1454, 1513,
+1584``) and for its two module fast paths (``angle_scan_impl``,
+``delta_scan_impl``; reference ``src/mingru/triton_scans.py:1743, 2403``):
+same argument order, shapes, dtypes and return values. What the reference's
+``MINGRU_SCAN`` seam did (``min_gru.py:85-704``: choose Triton or eager per
+call, warn, fall back) does not exist here: the ops always run the CUDA
+kernels, raise ``ValueError`` for CPU tensors or inputs outside the kernels'
+envelope, and ``RuntimeError`` for device-side failures.
+
+Each op is a ``torch.library.custom_op`` with a registered fake (shape)
+function and a ``register_autograd`` backward that calls the op's own
+backward kernel, so ``torch.compile`` sees opaque ops (the reference wires
+its Triton ops the same way, ``triton_scans.py:1465-1552``). Second-order
+autograd is not supported and raises, as in the reference
+(``triton_scans.py:1523-1532``).
+"""
+
+from __future__ import annotations
+
+import torch
+
+from . import _lib
+
+_DTYPE_CODES = {torch.float32: 0, torch.bfloat16: 1, torch.float16: 2}
+
+
+def _dtype_code(op: str, t: torch.Tensor) -> int:
+    try:
+        return _DTYPE_CODES[t.dtype]
+    except KeyError:
+        raise ValueError(
+            f"{op}: dtype {t.dtype} is not supported (float32, bfloat16, float16; "
+            "arithmetic is always fp32)"
+        ) from None
+
+
+def _require_cuda(op: str, *ts: torch.Tensor) -> None:
+    dev = ts[0].device
+    for t in ts:
+        if not t.is_cuda:
+            raise ValueError(
+                f"{op}: expected CUDA tensors (this library has no CPU path), got {t.device}"
+            )
+        if t.device != dev:
+            raise ValueError(f"{op}: tensors on different devices ({dev} vs {t.device})")
+
+
+def _dense(t: torch.Tensor) -> torch.Tensor:
+    """C-contiguous with a 16-byte aligned base (what the vector loads need)."""
+    t = t.contiguous()
+    if t.data_ptr() % 16 != 0:
+        t = t.clone()
+    return t
+
+
+def _stream(t: torch.Tensor) -> int:
+    return torch.cuda.current_stream(t.device).cuda_stream
+
+
+def _ptr(t: torch.Tensor | None):
+    return None if t is None else t.data_ptr()
+
+
+def _workspace(nbytes: int, device) -> torch.Tensor:
+    return torch.empty(max(int(nbytes), 256), dtype=torch.uint8, device=device)
+
+
+def take_device_error(device=None) -> int:
+    """Synchronise and return/clear the sticky device error bits (0 = clean).
+
+    A look-back wait that exhausts its bound records ``MGS_LOOKBACK_TIMEOUT``
+    there instead of hanging; call this after a step to turn such a record
+    into an exception (see ``raise_device_error``).
+    """
+    device = torch.device("cuda", torch.cuda.current_device()) if device is None else device
+    with torch.cuda.device(device):
+        return int(_lib.load().mgs_take_device_error(torch.cuda.current_stream(device).cuda_stream))
+
+
+def raise_device_error(device=None) -> None:
+    bits = take_device_error(device)
+    if bits:
+        names = [n for s, n in _lib.STATUS_NAMES.items() if s and bits & (1 << s)]
+        raise RuntimeError(f"scan kernels reported device errors: {', '.join(names)}")
+
+
+# =========================================================== linear_scan ==
+
+
+@torch.library.custom_op("mingru_b200::linear_scan_fwd", mutates_args=())
+def _linear_scan_fwd(
+    a: torch.Tensor, b: torch.Tensor, save_carries: bool
+) -> tuple[torch.Tensor, torch.Tensor, torch.Tensor]:
+    lib = _lib.load()
+    a, b = _dense(a), _dense(b)
+    Bn, T, D = a.shape
+    code = _dtype_code("linear_scan", a)
+    A, Bc = torch.empty_like(a), torch.empty_like(b)
+    csz = lib.mgs_linear_scan_carry_size(Bn, T, D, code) if save_carries else 0
+    carries = torch.empty(csz // 4, dtype=torch.float32, device=a.device)
+    ws = _workspace(lib.mgs_linear_scan_workspace_size(Bn, T, D, code), a.device)
+    with torch.cuda.device(a.device):
+        st = lib.mgs_linear_scan_fwd(
+            _ptr(a), _ptr(b), _ptr(A), _ptr(Bc), _ptr(carries) if save_carries else None,
+            Bn, T, D, code, _ptr(ws), ws.numel(), _stream(a),
+        )
+    _lib.check(st, "linear_scan forward")
+    return A, Bc, carries
+
+
+@_linear_scan_fwd.register_fake
+def _(a, b, save_carries):
+    Bn, T, D = a.shape
+    csz = _lib.load().mgs_linear_scan_carry_size(Bn, T, D, _dtype_code("linear_scan", a))
+    n = csz // 4 if save_carries else 0
+    return torch.empty_like(a), torch.empty_like(b), a.new_empty((n,), dtype=torch.float32)
+
+
+@torch.library.custom_op("mingru_b200::linear_scan_bwd", mutates_args=())
+def _linear_scan_bwd(
+    a: torch.Tensor, b: torch.Tensor, gA: torch.Tensor, gBc: torch.Tensor, carries: torch.Tensor
+) -> tuple[torch.Tensor, torch.Tensor]:
+    lib = _lib.load()
+    a, b, gA, gBc = (_dense(x) for x in (a, b, gA.to(a.dtype), gBc.to(a.dtype)))
+    Bn, T, D = a.shape
+    code = _dtype_code("linear_scan", a)
+    if carries.numel() * 4 < lib.mgs_linear_scan_carry_size(Bn, T, D, code):
+        raise RuntimeError("linear_scan backward: forward carries were not saved")
+    da, db = torch.empty_like(a), torch.empty_like(b)
+    ws = _workspace(lib.mgs_linear_scan_workspace_size(Bn, T, D, code), a.device)
+    with torch.cuda.device(a.device):
+        st = lib.mgs_linear_scan_bwd(
+            _ptr(a), _ptr(b), _ptr(gA), _ptr(gBc), _ptr(carries), _ptr(da), _ptr(db),
+            Bn, T, D, code, _ptr(ws), ws.numel(), _stream(a),
+        )
+    _lib.check(st, "linear_scan backward")
+    return da, db
+
+
+@_linear_scan_bwd.register_fake
+def _(a, b, gA, gBc, carries):
+    return torch.empty_like(a), torch.empty_like(b)
+
+
+def _linear_setup(ctx, inputs, output):
+    a, b, _ = inputs
+    ctx.save_for_backward(a, b, output[2])
+    ctx.mark_non_differentiable(output[2])
+
+
+def _linear_backward(ctx, gA, gBc, _gcarries):
+    if torch.is_grad_enabled():
+        raise RuntimeError("linear_scan does not support second-order autograd (create_graph=True)")
+    a, b, carries = ctx.saved_tensors
+    if gA is None:
+        gA = torch.zeros_like(a)
+    if gBc is None:
+        gBc = torch.zeros_like(a)
+    da, db = _linear_scan_bwd(a, b, gA, gBc, carries)
+    return da, db, None
+
+
+torch.library.register_autograd(
+    "mingru_b200::linear_scan_fwd", _linear_backward, setup_context=_linear_setup
+)
+
+
+def linear_scan(a: torch.Tensor, b: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
+    """Scan ``h_t = a_t h_{t-1} + b_t`` over ``dim=1``; returns ``(A, Bc)``.
+
+    ``a``, ``b``: ``(B, T, D)`` CUDA tensors of one dtype (float32, bfloat16 or
+    float16). ``A_t = prod_{s<=t} a_s`` and ``Bc_t`` is the ``h_0 = 0``
+    solution, so ``h_t = A_t h_0 + Bc_t``; outputs have the input dtype,
+    arithmetic is fp32. Same contract as the reference's
+    ``min_gru.linear_scan`` (``min_gru.py:1454-1510``).
+    """
+    op = "linear_scan"
+    if a.ndim != 3 or b.ndim != 3 or a.shape != b.shape:
+        raise ValueError(
+            f"{op}: need matching (B, T, D) a and b (got a={tuple(a.shape)}, b={tuple(b.shape)})"
+        )
+    _require_cuda(op, a, b)
+    if a.dtype != b.dtype:
+        raise ValueError(f"{op}: a and b must share a dtype ({a.dtype} vs {b.dtype})")
+    _dtype_code(op, a)
+    need = torch.is_grad_enabled() and (a.requires_grad or b.requires_grad)
+    A, Bc, _ = _linear_scan_fwd(a, b, need)
+    return A, Bc
