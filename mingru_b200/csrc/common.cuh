@@ -12,6 +12,7 @@
 // word, then proceeds, so no launch can hang a GPU.
 #pragma once
 
+#include <cuda.h>
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
@@ -240,6 +241,226 @@ __device__ __forceinline__ void warp_lookback(const Lookback& lb, long long tile
   float inc[NF];
   Monoid::combine(excl, agg, inc);
   lb_publish<NF>(lb, tile, kFlagIncl, inc);
+}
+
+// Windowed decoupled look-back: lanes inspect up to 32 predecessors at once
+// (lane i looks at predecessor i+1 of the strip), so the walk back to the
+// nearest inclusive prefix costs one L2 round trip per 32 predecessors
+// instead of one per predecessor. Same contract as warp_lookback.
+template <class Monoid, int NF>
+__device__ __forceinline__ void warp_lookback_win(const Lookback& lb, long long tile,
+                                                  long long stride, long long pos,
+                                                  const float (&agg)[NF], float (&excl)[NF]) {
+  const int lane = threadIdx.x & 31;
+  if (pos == 0) {
+    Monoid::identity(excl);
+    lb_publish<NF>(lb, tile, kFlagIncl, agg);
+    return;
+  }
+  lb_publish<NF>(lb, tile, kFlagAgg, agg);
+  float run[NF];
+  Monoid::identity(run);
+  long long remaining = pos;        // predecessors left: tile - k*stride, k = 1..remaining
+  long long base = tile - stride;   // predecessor k = 1
+  while (remaining > 0) {
+    const int nwin = remaining < 32 ? (int)remaining : 32;
+    const bool valid = lane < nwin;
+    const unsigned* fp = lb.flags + (valid ? base - (long long)lane * stride : 0);
+    unsigned f = valid ? ld_acquire_u32(fp) : kFlagIncl;
+    int last;
+    long long it = 0;
+    while (true) {
+      const unsigned im = __ballot_sync(0xffffffffu, valid && f == kFlagIncl);
+      last = im ? (__ffs(im) - 1) : nwin - 1;
+      const bool need = lane <= last;
+      const unsigned em = __ballot_sync(0xffffffffu, need && f == kFlagEmpty);
+      if (em == 0u) break;
+      if (++it > kSpinLimit) {
+        if (lane == 0) {
+          atomicOr(lb.err, kErrTimeout);
+          atomicOr(&g_sticky_err, kErrTimeout);
+        }
+        if (f == kFlagEmpty) f = kFlagIncl;  // proceed; the host raises
+        continue;
+      }
+      if ((it & 255) == 0 && ld_relaxed_u32(lb.err) != 0u && f == kFlagEmpty) f = kFlagIncl;
+      if (need && f == kFlagEmpty) {
+        __nanosleep(32);
+        f = ld_acquire_u32(fp);
+      }
+    }
+    __syncwarp();
+    // Compose predecessors nearest-first: run = e_i o run.
+#pragma unroll 1
+    for (int i = 0; i <= last; ++i) {
+      const unsigned fi = __shfl_sync(0xffffffffu, f, i);
+      const float* src = (fi == kFlagIncl ? lb.incl : lb.agg) + (size_t)(base - (long long)i * stride) * NF * 32;
+      float e[NF], tmp[NF];
+#pragma unroll
+      for (int q = 0; q < NF; ++q) e[q] = __ldcg(src + q * 32 + lane);
+      Monoid::combine(e, run, tmp);
+#pragma unroll
+      for (int q = 0; q < NF; ++q) run[q] = tmp[q];
+    }
+    const unsigned flast = __shfl_sync(0xffffffffu, f, last);
+    if (flast == kFlagIncl) break;
+    remaining -= nwin;
+    base -= (long long)nwin * stride;
+  }
+#pragma unroll
+  for (int i = 0; i < NF; ++i) excl[i] = run[i];
+  float inc[NF];
+  Monoid::combine(excl, agg, inc);
+  lb_publish<NF>(lb, tile, kFlagIncl, inc);
+}
+
+// ------------------------------------------------- TMA bulk copy + mbarrier --
+//
+// Tiles are streamed into shared memory with the bulk-copy engine
+// (cp.async.bulk global -> shared, completion counted on an mbarrier; no
+// tensor map and no multicast). Every wait on an mbarrier is bounded.
+
+__device__ __forceinline__ unsigned smem_u32(const void* p) {
+  return static_cast<unsigned>(__cvta_generic_to_shared(p));
+}
+
+__device__ __forceinline__ void mbar_init(uint64_t* bar, unsigned count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");
+}
+
+__device__ __forceinline__ void mbar_fence_init() {
+  asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, unsigned bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)),
+               "r"(bytes)
+               : "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+
+__device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, unsigned parity) {
+  unsigned ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0u;
+}
+
+// Bounded wait for an mbarrier phase; returns false (after recording a
+// timeout) if the phase never completes.
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, unsigned parity, unsigned* err) {
+  long long it = 0;
+  while (!mbar_try_wait(bar, parity)) {
+    if (++it > kSpinLimit) {
+      atomicOr(err, kErrTimeout);
+      atomicOr(&g_sticky_err, kErrTimeout);
+      return false;
+    }
+  }
+  return true;
+}
+
+// One bulk copy of `bytes` (multiple of 16, both addresses 16-byte aligned)
+// from global to this CTA's shared memory, completing on `bar`.
+__device__ __forceinline__ void bulk_g2s(void* dst, const void* src, unsigned bytes, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+          smem_u32(dst)),
+      "l"(src), "r"(bytes), "r"(smem_u32(bar))
+      : "memory");
+}
+
+__device__ __forceinline__ void named_bar(int id, int nthreads) {
+  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(nthreads) : "memory");
+}
+
+// Named barrier that also ORs a predicate over the participating threads, so
+// a group of warps can leave a loop together (no warp is ever left waiting
+// at a barrier that another warp has abandoned).
+__device__ __forceinline__ bool bar_any(int id, int nthreads, bool pred) {
+  unsigned r;
+  asm volatile(
+      "{\n\t.reg .pred p, q;\n\t"
+      "setp.ne.u32 p, %1, 0;\n\t"
+      "bar.red.or.pred q, %2, %3, p;\n\t"
+      "selp.u32 %0, 1, 0, q;\n\t}"
+      : "=r"(r)
+      : "r"((unsigned)pred), "r"(id), "r"(nthreads)
+      : "memory");
+  return r != 0u;
+}
+
+// ------------------------------------------------------ TMA tensor maps --
+//
+// Host: encode a 3-D tiled tensor map for a C-contiguous (Z, Y, X) tensor
+// (X innermost) with a box of (bx, by, 1), no swizzle, zero fill outside the
+// tensor. The driver function is fetched through the runtime's entry-point
+// query, so the library does not link libcuda directly.
+
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
+                                  const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
+                                  const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
+                                  CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+inline EncodeTiledFn encode_tiled_fn() {
+  static EncodeTiledFn fn = nullptr;
+  if (fn == nullptr) {
+    void* ptr = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) ==
+            cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFn>(ptr);
+  }
+  return fn;
+}
+
+template <typename E>
+inline CUtensorMapDataType tma_dtype();
+template <>
+inline CUtensorMapDataType tma_dtype<float>() { return CU_TENSOR_MAP_DATA_TYPE_FLOAT32; }
+template <>
+inline CUtensorMapDataType tma_dtype<__nv_bfloat16>() { return CU_TENSOR_MAP_DATA_TYPE_BFLOAT16; }
+template <>
+inline CUtensorMapDataType tma_dtype<__half>() { return CU_TENSOR_MAP_DATA_TYPE_FLOAT16; }
+
+// Returns false if the map cannot be encoded (the caller reports MGS_LAUNCH_FAILED).
+template <typename E>
+inline bool make_tmap_3d(CUtensorMap* map, const void* base, long long X, long long Y, long long Z,
+                         unsigned bx, unsigned by) {
+  EncodeTiledFn fn = encode_tiled_fn();
+  if (fn == nullptr) return false;
+  const cuuint64_t dims[3] = {(cuuint64_t)X, (cuuint64_t)Y, (cuuint64_t)Z};
+  const cuuint64_t strides[2] = {(cuuint64_t)(X * (long long)sizeof(E)),
+                                 (cuuint64_t)(X * Y * (long long)sizeof(E))};
+  const cuuint32_t box[3] = {bx, by, 1u};
+  const cuuint32_t estr[3] = {1u, 1u, 1u};
+  return fn(map, tma_dtype<E>(), 3, const_cast<void*>(base), dims, strides, box, estr,
+            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+            CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+// Device: one tiled box load (no multicast) completing on `bar`. The x
+// coordinate times the element size is always a multiple of 16 bytes here.
+__device__ __forceinline__ void tma_load_3d(void* dst, const CUtensorMap* map, int x, int y, int z,
+                                            uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%2, %3, %4}], [%5];" ::"r"(smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(z), "r"(smem_u32(bar))
+      : "memory");
+}
+
+__device__ __forceinline__ void tma_prefetch_desc(const CUtensorMap* map) {
+  asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
 }
 
 // Error-word helpers shared by the per-file launchers.

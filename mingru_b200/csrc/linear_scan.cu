@@ -8,51 +8,87 @@
 //   G^A_t = gA_t + a_{t+1} G^A_{t+1},  G^B_t = gB_t + a_{t+1} G^B_{t+1},
 //   da_t  = G^A_t A_{t-1} + G^B_t Bc_{t-1},  db_t = G^B_t.
 //
-// Design. A tile is L = S*NW time steps x 32*CPT channels: warp w owns steps
-// [w*S, (w+1)*S) of the tile, lane l owns CPT adjacent channels (one 16-byte
-// vector access per step), so every warp access is a fully coalesced row
-// segment. Each thread reduces its S steps serially in registers; the NW warp
-// aggregates are composed through shared memory; warp 0 runs the decoupled
-// look-back across the strip's earlier tiles; every thread then replays its
-// S steps from its exact carry and streams the outputs. The forward also
-// writes each tile's chunk-start state ("carries", fp32), which lets the
-// backward recompute A_{t-1}, Bc_{t-1} in registers instead of reading the
-// saved outputs: the backward reads a, b, gA, gBc and writes da, db -- the
-// algorithmic minimum -- and runs its own reverse look-back for G.
+// Three algorithms, chosen per shape (the same choice for forward and
+// backward, since the forward's carries feed the backward):
+//  * strip (wide problems, B*ceil(D/32) >= 2 x #SMs, rows 16-byte aligned):
+//    every CTA owns 32-channel strips and walks them through all of T. A
+//    producer warp streams 32-step chunks of the strip into a shared-memory
+//    ring with cp.async.bulk (mbarrier completion); four consumer warps scan
+//    a chunk (8 steps each, serial in registers), compose the per-warp
+//    aggregates through shared memory and carry the strip state on-chip from
+//    chunk to chunk. No global synchronisation at all.
+//  * direct-vec (narrow problems, rows 16-byte aligned): one tile (64 steps x
+//    128 channels, 4 channels per lane, 16-byte accesses) per CTA, chunk
+//    carries across CTAs by windowed decoupled look-back.
+//  * direct-scalar (any D): the same with one channel per lane.
+// The forward writes the state at every carry-chunk start ("carries", fp32,
+// ~6% of one input); the backward's tiles are exactly those chunks, so it
+// recomputes A_{t-1}, Bc_{t-1} in registers from them instead of reading the
+// saved outputs: it reads a, b, gA, gBc and writes da, db -- the algorithmic
+// minimum -- and carries the adjoint G in reverse time order.
 #include "common.cuh"
 
 namespace mgs {
 namespace linear {
 
-// Tile geometry, shared by forward, backward, size queries and carries.
-constexpr int kFwdS = 8, kFwdNW = 4;   // L = 32
-constexpr int kBwdS = 4, kBwdNW = 8;   // L = 32
-constexpr int kL = kFwdS * kFwdNW;
-static_assert(kBwdS * kBwdNW == kL, "forward and backward tiles must match");
+constexpr int kLc = 32;  // carry-chunk length = backward tile length (all algorithms)
+
+// direct paths
+constexpr int kVecCpt = 4;                       // channels per lane, direct-vec
+constexpr int kVecFwdS = 8, kVecFwdNW = 8;       // forward tile 64 steps
+constexpr int kSclFwdS = 8, kSclFwdNW = 4;       // forward tile 32 steps
+constexpr int kBwdS = 4, kBwdNW = 8;             // backward tile 32 steps
+static_assert(kBwdS * kBwdNW == kLc, "backward tile must be one carry chunk");
+static_assert((kVecFwdS * kVecFwdNW) % kLc == 0 && kLc % kVecFwdS == 0, "vec carry grid");
+static_assert((kSclFwdS * kSclFwdNW) % kLc == 0 && kLc % kSclFwdS == 0, "scalar carry grid");
+
+// strip path
+constexpr int kStripNW = 4;                      // consumer warps
+constexpr int kStripS = kLc / kStripNW;          // steps per consumer warp and chunk
+constexpr int kRingBytes = 50 * 1024;            // shared-memory ring per CTA (4 CTAs per SM)
+
+enum Algo { kStrip = 0, kDirectVec = 1, kDirectScalar = 2 };
+
+inline int sm_count() {
+  int dev = 0, n = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return 148;
+  if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0)
+    return 148;
+  return n;
+}
 
 struct Geometry {
+  Algo algo;
   int cpt;             // channels per lane
   long long sper;      // strips per batch row
   long long nstrips;   // B * sper
-  long long nchunks;   // ceil(T / L)
-  long long ntiles;
+  long long nchunks;   // ceil(T / kLc): carry chunks = backward tiles per strip
+  long long ntiles;    // nstrips * nchunks
+  long long fchunks;   // forward tiles per strip (direct paths)
+  long long ftiles;
 };
-
-inline int vec_cpt(int dtype) { return 16 / dtype_size(dtype); }
 
 inline Geometry geometry(long long B, long long T, long long D, int dtype) {
   Geometry g;
-  const int vec = vec_cpt(dtype);
-  g.cpt = (D % vec == 0) ? vec : 1;
+  const bool rows16 = ((D * dtype_size(dtype)) % 16) == 0;
+  const long long strips32 = B * ((D + 31) / 32);
+  if (rows16 && strips32 >= 2LL * sm_count())
+    g.algo = kStrip;
+  else
+    g.algo = rows16 ? kDirectVec : kDirectScalar;
+  g.cpt = g.algo == kDirectVec ? kVecCpt : 1;
   const long long w = 32LL * g.cpt;
   g.sper = (D + w - 1) / w;
   g.nstrips = B * g.sper;
-  g.nchunks = (T + kL - 1) / kL;
+  g.nchunks = (T + kLc - 1) / kLc;
   g.ntiles = g.nstrips * g.nchunks;
+  const int fl = g.algo == kDirectVec ? kVecFwdS * kVecFwdNW : (g.algo == kDirectScalar ? kSclFwdS * kSclFwdNW : kLc);
+  g.fchunks = (T + fl - 1) / fl;
+  g.ftiles = g.nstrips * g.fchunks;
   return g;
 }
 
-// Forward monoid over (A, B) pairs, CPT channels per lane: x = [A0..A_{C-1}, B0..B_{C-1}].
+// Forward monoid over (A, B) pairs, C channels per lane: x = [A0..A_{C-1}, B0..B_{C-1}].
 template <int C>
 struct FwdMonoid {
   static constexpr int NF = 2 * C;
@@ -89,6 +125,14 @@ struct RevMonoid {
   }
 };
 
+template <class M, int NF>
+__device__ __forceinline__ void combine_into(float (&acc)[NF], const float (&later)[NF]) {
+  float tmp[NF];
+  M::combine(acc, later, tmp);
+#pragma unroll
+  for (int f = 0; f < NF; ++f) acc[f] = tmp[f];
+}
+
 template <typename E>
 struct Args {
   const E* a;
@@ -100,12 +144,113 @@ struct Args {
   E* da;
   E* db;
   float* carries;  // forward: written (may be null); backward: read
-  long long T_, D, sper, nstrips, nchunks;
+  long long T_, D, sper, nstrips;
+  long long nchunks;  // tiles (direct) or chunks (strip) per strip for this launch
+  long long ntiles;
   Lookback lb;
 };
 
+// Strip-path tensor maps of the streamed inputs: (B, T, D) boxes of
+// 32 channels x kLc steps (forward: a, b; backward: a, b, gA, gBc).
+struct StripMaps {
+  CUtensorMap m[4];
+};
+
+// ------------------------------------------------------ shared step maths --
+
+template <int C, int S>
+__device__ __forceinline__ void fwd_agg(const float (&av)[S][C], const float (&bv)[S][C],
+                                        float (&agg)[2 * C]) {
+  FwdMonoid<C>::identity(agg);
+#pragma unroll
+  for (int s = 0; s < S; ++s)
+#pragma unroll
+    for (int c = 0; c < C; ++c) {
+      agg[C + c] = fmaf(av[s][c], agg[C + c], bv[s][c]);
+      agg[c] *= av[s][c];
+    }
+}
+
+template <int C, int S>
+__device__ __forceinline__ void rev_agg(const float (&av)[S][C], const float (&ga)[S][C],
+                                        const float (&gb)[S][C], float (&ragg)[3 * C]) {
+  RevMonoid<C>::identity(ragg);
+#pragma unroll
+  for (int s = S - 1; s >= 0; --s)
+#pragma unroll
+    for (int c = 0; c < C; ++c) {
+      ragg[C + c] = av[s][c] * (ga[s][c] + ragg[C + c]);
+      ragg[2 * C + c] = av[s][c] * (gb[s][c] + ragg[2 * C + c]);
+      ragg[c] *= av[s][c];
+    }
+}
+
+// Replay S forward steps from `cur`, storing A and Bc.
+template <typename E, int C, int S>
+__device__ __forceinline__ void fwd_emit(const Args<E>& p, const float (&av)[S][C],
+                                         const float (&bv)[S][C], float (&cur)[2 * C], bool dok,
+                                         long long t0, size_t base) {
+#pragma unroll
+  for (int s = 0; s < S; ++s) {
+    float oa[C], ob[C];
+#pragma unroll
+    for (int c = 0; c < C; ++c) {
+      cur[C + c] = fmaf(av[s][c], cur[C + c], bv[s][c]);
+      cur[c] *= av[s][c];
+      oa[c] = cur[c];
+      ob[c] = cur[C + c];
+    }
+    const long long t = t0 + s;
+    if (dok && t < p.T_) {
+      store_vec<E, C>(p.A + base + t * p.D, oa);
+      store_vec<E, C>(p.Bc + base + t * p.D, ob);
+    }
+  }
+}
+
+// Per-thread backward of S steps given its forward start state (fcur) and
+// the adjoint entering from later steps (ya, yb): writes da, db.
+template <typename E, int C, int S>
+__device__ __forceinline__ void bwd_emit(const Args<E>& p, const float (&av)[S][C],
+                                         const float (&bv)[S][C], const float (&ga)[S][C],
+                                         const float (&gb)[S][C], float (&fcur)[2 * C],
+                                         float (&ya)[C], float (&yb)[C], bool dok, long long t0,
+                                         size_t base) {
+  float ap[S][C], bp[S][C];
+#pragma unroll
+  for (int s = 0; s < S; ++s)
+#pragma unroll
+    for (int c = 0; c < C; ++c) {
+      ap[s][c] = fcur[c];
+      bp[s][c] = fcur[C + c];
+      fcur[C + c] = fmaf(av[s][c], fcur[C + c], bv[s][c]);
+      fcur[c] *= av[s][c];
+    }
+#pragma unroll
+  for (int s = S - 1; s >= 0; --s) {
+    float oda[C], odb[C];
+#pragma unroll
+    for (int c = 0; c < C; ++c) {
+      const float GA = ga[s][c] + ya[c];
+      const float GB = gb[s][c] + yb[c];
+      oda[c] = fmaf(GA, ap[s][c], GB * bp[s][c]);
+      odb[c] = GB;
+      ya[c] = av[s][c] * GA;
+      yb[c] = av[s][c] * GB;
+    }
+    const long long t = t0 + s;
+    if (dok && t < p.T_) {
+      const size_t o = base + t * p.D;
+      store_vec<E, C>(p.da + o, oda);
+      store_vec<E, C>(p.db + o, odb);
+    }
+  }
+}
+
+// ------------------------------------------------------------ direct path --
+
 template <typename E, int C, int S, int NW>
-__global__ void __launch_bounds__(NW * 32) fwd_kernel(Args<E> p) {
+__global__ void __launch_bounds__(NW * 32) fwd_direct_kernel(Args<E> p) {
   using M = FwdMonoid<C>;
   constexpr int NF = M::NF;
   constexpr int L = S * NW;
@@ -137,76 +282,51 @@ __global__ void __launch_bounds__(NW * 32) fwd_kernel(Args<E> p) {
     }
   }
   float agg[NF];
-  M::identity(agg);
-#pragma unroll
-  for (int s = 0; s < S; ++s)
-#pragma unroll
-    for (int c = 0; c < C; ++c) {
-      agg[C + c] = fmaf(av[s][c], agg[C + c], bv[s][c]);
-      agg[c] *= av[s][c];
-    }
+  fwd_agg<C, S>(av, bv, agg);
 #pragma unroll
   for (int f = 0; f < NF; ++f) s_agg[warp][f][lane] = agg[f];
   __syncthreads();
 
   if (warp == 0) {
-    float tot[NF], tmp[NF], w_[NF];
+    float tot[NF], w_[NF];
 #pragma unroll
     for (int f = 0; f < NF; ++f) tot[f] = s_agg[0][f][lane];
 #pragma unroll
     for (int w = 1; w < NW; ++w) {
 #pragma unroll
       for (int f = 0; f < NF; ++f) w_[f] = s_agg[w][f][lane];
-      M::combine(tot, w_, tmp);
-#pragma unroll
-      for (int f = 0; f < NF; ++f) tot[f] = tmp[f];
+      combine_into<M, NF>(tot, w_);
     }
     float ex[NF];
-    warp_lookback<M, NF>(p.lb, tile, p.nstrips, chunk, tot, ex);
+    warp_lookback_win<M, NF>(p.lb, tile, p.nstrips, chunk, tot, ex);
 #pragma unroll
     for (int f = 0; f < NF; ++f) s_ex[f][lane] = ex[f];
-    if (p.carries != nullptr) {
-      float* dst = p.carries + (size_t)tile * NF * 32;
-#pragma unroll
-      for (int f = 0; f < NF; ++f) __stcs(dst + f * 32 + lane, ex[f]);
-    }
   }
   __syncthreads();
 
-  float cur[NF], tmp[NF], w_[NF];
+  float cur[NF], w_[NF];
 #pragma unroll
   for (int f = 0; f < NF; ++f) cur[f] = s_ex[f][lane];
   for (int w = 0; w < warp; ++w) {
 #pragma unroll
     for (int f = 0; f < NF; ++f) w_[f] = s_agg[w][f][lane];
-    M::combine(cur, w_, tmp);
-#pragma unroll
-    for (int f = 0; f < NF; ++f) cur[f] = tmp[f];
+    combine_into<M, NF>(cur, w_);
   }
+  if (p.carries != nullptr && ((warp * S) % kLc) == 0 && t0 < p.T_) {
+    float* dst = p.carries + (size_t)((t0 / kLc) * p.nstrips + strip) * NF * 32;
 #pragma unroll
-  for (int s = 0; s < S; ++s) {
-    float oa[C], ob[C];
-#pragma unroll
-    for (int c = 0; c < C; ++c) {
-      cur[C + c] = fmaf(av[s][c], cur[C + c], bv[s][c]);
-      cur[c] *= av[s][c];
-      oa[c] = cur[c];
-      ob[c] = cur[C + c];
-    }
-    const long long t = t0 + s;
-    if (dok && t < p.T_) {
-      store_vec<E, C>(p.A + base + t * p.D, oa);
-      store_vec<E, C>(p.Bc + base + t * p.D, ob);
-    }
+    for (int f = 0; f < NF; ++f) __stcs(dst + f * 32 + lane, cur[f]);
   }
+  fwd_emit<E, C, S>(p, av, bv, cur, dok, t0, base);
 }
 
 template <typename E, int C, int S, int NW>
-__global__ void __launch_bounds__(NW * 32) bwd_kernel(Args<E> p) {
+__global__ void __launch_bounds__(NW * 32) bwd_direct_kernel(Args<E> p) {
   using FM = FwdMonoid<C>;
   using RM = RevMonoid<C>;
   constexpr int NFF = FM::NF, NFR = RM::NF;
   constexpr int L = S * NW;
+  static_assert(L == kLc, "backward tile = carry chunk");
   __shared__ unsigned s_tile;
   __shared__ float s_fagg[NW][NFF][32];
   __shared__ float s_ragg[NW][NFR][32];
@@ -215,7 +335,7 @@ __global__ void __launch_bounds__(NW * 32) bwd_kernel(Args<E> p) {
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   if (threadIdx.x == 0) s_tile = atomicAdd(p.lb.counter, 1u);
   __syncthreads();
-  const long long tile = s_tile;                 // position in reverse processing order
+  const long long tile = s_tile;                   // position in reverse processing order
   const long long rchunk = tile / p.nstrips;
   const long long strip = tile - rchunk * p.nstrips;
   const long long chunk = p.nchunks - 1 - rchunk;  // time chunk
@@ -240,26 +360,9 @@ __global__ void __launch_bounds__(NW * 32) bwd_kernel(Args<E> p) {
       for (int c = 0; c < C; ++c) { av[s][c] = 1.f; bv[s][c] = 0.f; ga[s][c] = 0.f; gb[s][c] = 0.f; }
     }
   }
-  // Local forward aggregate (for this warp's chunk-start state) and local
-  // reverse aggregate (for the adjoint entering from later steps).
   float fagg[NFF], ragg[NFR];
-  FM::identity(fagg);
-  RM::identity(ragg);
-#pragma unroll
-  for (int s = 0; s < S; ++s)
-#pragma unroll
-    for (int c = 0; c < C; ++c) {
-      fagg[C + c] = fmaf(av[s][c], fagg[C + c], bv[s][c]);
-      fagg[c] *= av[s][c];
-    }
-#pragma unroll
-  for (int s = S - 1; s >= 0; --s)
-#pragma unroll
-    for (int c = 0; c < C; ++c) {
-      ragg[C + c] = av[s][c] * (ga[s][c] + ragg[C + c]);
-      ragg[2 * C + c] = av[s][c] * (gb[s][c] + ragg[2 * C + c]);
-      ragg[c] *= av[s][c];
-    }
+  fwd_agg<C, S>(av, bv, fagg);
+  rev_agg<C, S>(av, ga, gb, ragg);
 #pragma unroll
   for (int f = 0; f < NFF; ++f) s_fagg[warp][f][lane] = fagg[f];
 #pragma unroll
@@ -267,19 +370,17 @@ __global__ void __launch_bounds__(NW * 32) bwd_kernel(Args<E> p) {
   __syncthreads();
 
   if (warp == 0) {
-    float tot[NFR], tmp[NFR], w_[NFR];
+    float tot[NFR], w_[NFR];
 #pragma unroll
     for (int f = 0; f < NFR; ++f) tot[f] = s_ragg[NW - 1][f][lane];
 #pragma unroll
     for (int w = NW - 2; w >= 0; --w) {
 #pragma unroll
       for (int f = 0; f < NFR; ++f) w_[f] = s_ragg[w][f][lane];
-      RM::combine(tot, w_, tmp);
-#pragma unroll
-      for (int f = 0; f < NFR; ++f) tot[f] = tmp[f];
+      combine_into<RM, NFR>(tot, w_);
     }
     float ex[NFR];
-    warp_lookback<RM, NFR>(p.lb, tile, p.nstrips, rchunk, tot, ex);
+    warp_lookback_win<RM, NFR>(p.lb, tile, p.nstrips, rchunk, tot, ex);
 #pragma unroll
     for (int f = 0; f < NFR; ++f) s_rex[f][lane] = ex[f];
   } else if (warp == 1) {
@@ -291,77 +392,285 @@ __global__ void __launch_bounds__(NW * 32) bwd_kernel(Args<E> p) {
 
   float fcur[NFF], rcur[NFR];
   {
-    float tmp[NFF], w_[NFF];
+    float w_[NFF];
 #pragma unroll
     for (int f = 0; f < NFF; ++f) fcur[f] = s_fex[f][lane];
     for (int w = 0; w < warp; ++w) {
 #pragma unroll
       for (int f = 0; f < NFF; ++f) w_[f] = s_fagg[w][f][lane];
-      FM::combine(fcur, w_, tmp);
-#pragma unroll
-      for (int f = 0; f < NFF; ++f) fcur[f] = tmp[f];
+      combine_into<FM, NFF>(fcur, w_);
     }
   }
   {
-    float tmp[NFR], w_[NFR];
+    float w_[NFR];
 #pragma unroll
     for (int f = 0; f < NFR; ++f) rcur[f] = s_rex[f][lane];
     for (int w = NW - 1; w > warp; --w) {
 #pragma unroll
       for (int f = 0; f < NFR; ++f) w_[f] = s_ragg[w][f][lane];
-      RM::combine(rcur, w_, tmp);
-#pragma unroll
-      for (int f = 0; f < NFR; ++f) rcur[f] = tmp[f];
+      combine_into<RM, NFR>(rcur, w_);
     }
   }
-  // States before each step: A_{t-1}, Bc_{t-1} (bv is dead afterwards).
-  float ap[S][C], bp[S][C];
-#pragma unroll
-  for (int s = 0; s < S; ++s)
-#pragma unroll
-    for (int c = 0; c < C; ++c) {
-      ap[s][c] = fcur[c];
-      bp[s][c] = fcur[C + c];
-      fcur[C + c] = fmaf(av[s][c], fcur[C + c], bv[s][c]);
-      fcur[c] *= av[s][c];
-    }
   float ya[C], yb[C];
 #pragma unroll
   for (int c = 0; c < C; ++c) { ya[c] = rcur[C + c]; yb[c] = rcur[2 * C + c]; }
+  bwd_emit<E, C, S>(p, av, bv, ga, gb, fcur, ya, yb, dok, t0, base);
+}
+
+// ------------------------------------------------------------- strip path --
+//
+// One CTA = kStripNW consumer warps + 1 producer warp, persistent over
+// strips (strip = blockIdx.x, blockIdx.x + gridDim.x, ...). For each strip
+// the producer streams the kLc-step chunks, in time order (forward) or
+// reverse time order (backward), into an NSTAGE-deep ring: one bulk copy
+// per (array, time row) of 32 channels, plus (backward) the chunk's forward
+// carry. Consumers and producer walk the same (strip, chunk) sequence, so no
+// per-stage metadata is needed.
+
+template <typename E, int NIN, bool WITH_CARRY>
+struct StripStage {
+  static constexpr int kRowElems = 32;
+  static constexpr size_t kArrayBytes = (size_t)kLc * kRowElems * sizeof(E);
+  static constexpr size_t kCarryBytes = WITH_CARRY ? 2 * 32 * sizeof(float) : 0;
+  static constexpr size_t kBytes = (NIN * kArrayBytes + kCarryBytes + 127) / 128 * 128;
+  static constexpr int kStages = (int)(kRingBytes / kBytes);
+};
+
+template <typename E, int NIN, bool WITH_CARRY, bool REVERSE>
+__device__ __forceinline__ void strip_produce(const Args<E>& p, const StripMaps& maps,
+                                              unsigned char* ring, uint64_t* full,
+                                              uint64_t* empty) {
+  using SS = StripStage<E, NIN, WITH_CARRY>;
+  constexpr int NSTAGE = SS::kStages;
+  const int lane = threadIdx.x & 31;
+  if (lane == 0)
+    for (int i = 0; i < NIN; ++i) tma_prefetch_desc(&maps.m[i]);
+  int s = 0;
+  unsigned ph = 0, pending = 0u, pend_ph = 0u;
+  for (long long strip = blockIdx.x; strip < p.nstrips; strip += gridDim.x) {
+    const long long bi = strip / p.sper;
+    const int d0 = (int)((strip - bi * p.sper) * 32);
+    for (long long q = 0; q < p.nchunks; ++q) {
+      const long long chunk = REVERSE ? p.nchunks - 1 - q : q;
+      if (!mbar_wait(&empty[s], ph ^ 1u, p.lb.err)) goto drain;
+      pending &= ~(1u << s);
+      if (lane == 0) {
+        unsigned char* stage = ring + (size_t)s * SS::kBytes;
+        mbar_arrive_expect_tx(&full[s], (unsigned)(NIN * SS::kArrayBytes + SS::kCarryBytes));
 #pragma unroll
-  for (int s = S - 1; s >= 0; --s) {
-    float oda[C], odb[C];
-#pragma unroll
-    for (int c = 0; c < C; ++c) {
-      const float GA = ga[s][c] + ya[c];
-      const float GB = gb[s][c] + yb[c];
-      oda[c] = fmaf(GA, ap[s][c], GB * bp[s][c]);
-      odb[c] = GB;
-      ya[c] = av[s][c] * GA;
-      yb[c] = av[s][c] * GB;
+        for (int arr = 0; arr < NIN; ++arr)
+          tma_load_3d(stage + arr * SS::kArrayBytes, &maps.m[arr], d0, (int)(chunk * kLc), (int)bi,
+                      &full[s]);
+        if (WITH_CARRY)
+          bulk_g2s(stage + NIN * SS::kArrayBytes,
+                   p.carries + (size_t)(chunk * p.nstrips + strip) * 2 * 32,
+                   (unsigned)SS::kCarryBytes, &full[s]);
+      }
+      __syncwarp();
+      pending |= 1u << s;
+      pend_ph = (pend_ph & ~(1u << s)) | (ph << s);
+      if (++s == NSTAGE) {
+        s = 0;
+        ph ^= 1u;
+      }
     }
-    const long long t = t0 + s;
-    if (dok && t < p.T_) {
-      const size_t o = base + t * p.D;
-      store_vec<E, C>(p.da + o, oda);
-      store_vec<E, C>(p.db + o, odb);
+  }
+drain:
+  for (int i = 0; i < NSTAGE; ++i)
+    if (pending & (1u << i)) mbar_wait(&full[i], (pend_ph >> i) & 1u, p.lb.err);
+}
+
+template <typename E, int S>
+__device__ __forceinline__ void strip_rows(const unsigned char* arr_base, int row0, long long t0,
+                                           long long T, bool dok, float fill, float (&out)[S][1]) {
+  const int lane = threadIdx.x & 31;
+  const E* base = reinterpret_cast<const E*>(arr_base) + lane;
+#pragma unroll
+  for (int s = 0; s < S; ++s)
+    out[s][0] = (dok && t0 + s < T) ? to_f32<E>(base[(row0 + s) * 32]) : fill;
+}
+
+template <typename E>
+__global__ void __launch_bounds__((kStripNW + 1) * 32)
+    fwd_strip_kernel(Args<E> p, const __grid_constant__ StripMaps maps) {
+  using SS = StripStage<E, 2, false>;
+  constexpr int NSTAGE = SS::kStages;
+  constexpr int NW = kStripNW, S = kStripS, NF = 2;
+  using M = FwdMonoid<1>;
+  extern __shared__ __align__(128) unsigned char ring[];
+  __shared__ __align__(8) uint64_t full[NSTAGE], empty[NSTAGE];
+  __shared__ float s_agg[2][NW][NF][32];
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < NSTAGE; ++i) {
+      mbar_init(&full[i], 1);
+      mbar_init(&empty[i], NW);
+    }
+    mbar_fence_init();
+  }
+  __syncthreads();
+  if (warp == NW) {
+    strip_produce<E, 2, false, false>(p, maps, ring, full, empty);
+    return;
+  }
+  int s = 0, buf = 0;
+  unsigned ph = 0;
+  for (long long strip = blockIdx.x; strip < p.nstrips; strip += gridDim.x) {
+    const long long bi = strip / p.sper;
+    const long long d = (strip - bi * p.sper) * 32 + lane;
+    const bool dok = d < p.D;
+    const size_t base = (size_t)bi * p.T_ * p.D + d;
+    float carry[NF];
+    M::identity(carry);
+    for (long long chunk = 0; chunk < p.nchunks; ++chunk) {
+      const bool ok = mbar_wait(&full[s], ph, p.lb.err);
+      if (bar_any(1, NW * 32, !ok)) return;
+      const unsigned char* stage = ring + (size_t)s * SS::kBytes;
+      const long long t0 = chunk * kLc + (long long)warp * S;
+      float av[S][1], bv[S][1];
+      strip_rows<E, S>(stage, warp * S, t0, p.T_, dok, 1.f, av);
+      strip_rows<E, S>(stage + SS::kArrayBytes, warp * S, t0, p.T_, dok, 0.f, bv);
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&empty[s]);
+      if (++s == NSTAGE) {
+        s = 0;
+        ph ^= 1u;
+      }
+      float agg[NF];
+      fwd_agg<1, S>(av, bv, agg);
+      s_agg[buf][warp][0][lane] = agg[0];
+      s_agg[buf][warp][1][lane] = agg[1];
+      named_bar(2, NW * 32);
+      if (warp == 0 && p.carries != nullptr) {
+        float* dst = p.carries + (size_t)(chunk * p.nstrips + strip) * NF * 32;
+        __stcs(dst + lane, carry[0]);
+        __stcs(dst + 32 + lane, carry[1]);
+      }
+      float cur[NF] = {carry[0], carry[1]};
+#pragma unroll
+      for (int w = 0; w < NW; ++w) {
+        const float e[NF] = {s_agg[buf][w][0][lane], s_agg[buf][w][1][lane]};
+        if (w == warp) {
+          cur[0] = carry[0];
+          cur[1] = carry[1];
+        }
+        combine_into<M, NF>(carry, e);
+      }
+      // cur currently = prefix before warp `warp` (captured above)
+      fwd_emit<E, 1, S>(p, av, bv, cur, dok, t0, base);
+      buf ^= 1;
     }
   }
 }
 
-template <typename E, int C>
-int launch_fwd(Args<E> p, const Geometry& g, cudaStream_t st) {
-  fwd_kernel<E, C, kFwdS, kFwdNW><<<(unsigned)g.ntiles, kFwdNW * 32, 0, st>>>(p);
-  return cudaGetLastError() == cudaSuccess ? MGS_OK : MGS_LAUNCH_FAILED;
+template <typename E>
+__global__ void __launch_bounds__((kStripNW + 1) * 32)
+    bwd_strip_kernel(Args<E> p, const __grid_constant__ StripMaps maps) {
+  using SS = StripStage<E, 4, true>;
+  constexpr int NSTAGE = SS::kStages;
+  constexpr int NW = kStripNW, S = kStripS;
+  using FM = FwdMonoid<1>;
+  using RM = RevMonoid<1>;
+  extern __shared__ __align__(128) unsigned char ring[];
+  __shared__ __align__(8) uint64_t full[NSTAGE], empty[NSTAGE];
+  __shared__ float s_fagg[2][NW][2][32];
+  __shared__ float s_ragg[2][NW][3][32];
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < NSTAGE; ++i) {
+      mbar_init(&full[i], 1);
+      mbar_init(&empty[i], NW);
+    }
+    mbar_fence_init();
+  }
+  __syncthreads();
+  if (warp == NW) {
+    strip_produce<E, 4, true, true>(p, maps, ring, full, empty);
+    return;
+  }
+  int s = 0, buf = 0;
+  unsigned ph = 0;
+  for (long long strip = blockIdx.x; strip < p.nstrips; strip += gridDim.x) {
+    const long long bi = strip / p.sper;
+    const long long d = (strip - bi * p.sper) * 32 + lane;
+    const bool dok = d < p.D;
+    const size_t base = (size_t)bi * p.T_ * p.D + d;
+    float rcarry[3];
+    RM::identity(rcarry);
+    for (long long q = 0; q < p.nchunks; ++q) {
+      const long long chunk = p.nchunks - 1 - q;
+      const bool ok = mbar_wait(&full[s], ph, p.lb.err);
+      if (bar_any(1, NW * 32, !ok)) return;
+      const unsigned char* stage = ring + (size_t)s * SS::kBytes;
+      const long long t0 = chunk * kLc + (long long)warp * S;
+      float av[S][1], bv[S][1], ga[S][1], gb[S][1];
+      strip_rows<E, S>(stage, warp * S, t0, p.T_, dok, 1.f, av);
+      strip_rows<E, S>(stage + SS::kArrayBytes, warp * S, t0, p.T_, dok, 0.f, bv);
+      strip_rows<E, S>(stage + 2 * SS::kArrayBytes, warp * S, t0, p.T_, dok, 0.f, ga);
+      strip_rows<E, S>(stage + 3 * SS::kArrayBytes, warp * S, t0, p.T_, dok, 0.f, gb);
+      const float* fc = reinterpret_cast<const float*>(stage + 4 * SS::kArrayBytes);
+      float fcur[2] = {fc[lane], fc[32 + lane]};
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&empty[s]);
+      if (++s == NSTAGE) {
+        s = 0;
+        ph ^= 1u;
+      }
+      float fagg[2], ragg[3];
+      fwd_agg<1, S>(av, bv, fagg);
+      rev_agg<1, S>(av, ga, gb, ragg);
+      s_fagg[buf][warp][0][lane] = fagg[0];
+      s_fagg[buf][warp][1][lane] = fagg[1];
+      s_ragg[buf][warp][0][lane] = ragg[0];
+      s_ragg[buf][warp][1][lane] = ragg[1];
+      s_ragg[buf][warp][2][lane] = ragg[2];
+      named_bar(2, NW * 32);
+      for (int w = 0; w < warp; ++w) {
+        const float e[2] = {s_fagg[buf][w][0][lane], s_fagg[buf][w][1][lane]};
+        combine_into<FM, 2>(fcur, e);
+      }
+      float rcur[3] = {rcarry[0], rcarry[1], rcarry[2]};
+#pragma unroll
+      for (int w = NW - 1; w >= 0; --w) {
+        if (w == warp) {
+          rcur[0] = rcarry[0];
+          rcur[1] = rcarry[1];
+          rcur[2] = rcarry[2];
+        }
+        const float e[3] = {s_ragg[buf][w][0][lane], s_ragg[buf][w][1][lane], s_ragg[buf][w][2][lane]};
+        combine_into<RM, 3>(rcarry, e);
+      }
+      float ya[1] = {rcur[1]}, yb[1] = {rcur[2]};
+      bwd_emit<E, 1, S>(p, av, bv, ga, gb, fcur, ya, yb, dok, t0, base);
+      buf ^= 1;
+    }
+  }
 }
 
-template <typename E, int C>
-int launch_bwd(Args<E> p, const Geometry& g, cudaStream_t st) {
-  bwd_kernel<E, C, kBwdS, kBwdNW><<<(unsigned)g.ntiles, kBwdNW * 32, 0, st>>>(p);
-  return cudaGetLastError() == cudaSuccess ? MGS_OK : MGS_LAUNCH_FAILED;
+// ---------------------------------------------------------------- launch --
+
+template <class K>
+int launch_persistent(K kernel, int threads, size_t dyn_smem, long long units, void** kargs,
+                      cudaStream_t st) {
+  // Static + dynamic shared memory above 48 KB needs the opt-in attribute.
+  MGS_CUDA_OK(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                   (int)dyn_smem));
+  int per_sm = 0;
+  MGS_CUDA_OK(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kernel, threads, dyn_smem));
+  if (per_sm < 1) return MGS_LAUNCH_FAILED;
+  long long grid = (long long)per_sm * sm_count();
+  if (grid > units) grid = units;
+  MGS_CUDA_OK(cudaLaunchKernel((const void*)kernel, dim3((unsigned)grid), dim3(threads), kargs,
+                               dyn_smem, st));
+  return MGS_OK;
 }
 
 inline int nf_max(const Geometry& g) { return 3 * g.cpt; }
+
+inline size_t workspace_bytes(const Geometry& g) {
+  if (g.algo == kStrip) return 256;  // no look-back
+  return lookback_bytes(g.ntiles > g.ftiles ? g.ntiles : g.ftiles, nf_max(g));
+}
 
 template <typename E>
 int run(bool fwd, const void* a, const void* b, void* A, void* Bc, const void* gA,
@@ -370,16 +679,14 @@ int run(bool fwd, const void* a, const void* b, void* A, void* Bc, const void* g
   const Geometry g = geometry(B, T, D, dtype);
   if (g.ntiles == 0) return MGS_OK;
   if (g.ntiles > 0x7fffffffLL) return MGS_UNSUPPORTED;
-  if (ws == nullptr || ws_bytes < lookback_bytes(g.ntiles, nf_max(g)))
-    return MGS_WORKSPACE_TOO_SMALL;
-  const size_t va = (size_t)g.cpt * sizeof(E);
-  const void* ptrs[8] = {a, b, fwd ? A : gA, fwd ? Bc : gB, fwd ? nullptr : da,
-                         fwd ? nullptr : db, nullptr, nullptr};
+  if (ws == nullptr || ws_bytes < workspace_bytes(g)) return MGS_WORKSPACE_TOO_SMALL;
+  const size_t va = g.algo == kDirectScalar ? sizeof(E) : 16;
+  const void* ptrs[6] = {a, b, fwd ? A : gA, fwd ? Bc : gB, fwd ? nullptr : da,
+                         fwd ? nullptr : db};
   for (const void* q : ptrs)
     if (q != nullptr && !aligned(q, va)) return MGS_BAD_ALIGNMENT;
   if (!aligned(ws, 256) || (carries != nullptr && !aligned(carries, 16))) return MGS_BAD_ALIGNMENT;
   if (!fwd && carries == nullptr) return MGS_BAD_SHAPE;
-  MGS_CUDA_OK(cudaMemsetAsync(ws, 0, lookback_zero_bytes(g.ntiles), st));
   Args<E> p;
   p.a = static_cast<const E*>(a);
   p.b = static_cast<const E*>(b);
@@ -394,11 +701,44 @@ int run(bool fwd, const void* a, const void* b, void* A, void* Bc, const void* g
   p.D = D;
   p.sper = g.sper;
   p.nstrips = g.nstrips;
-  p.nchunks = g.nchunks;
-  p.lb = lookback_view(ws, g.ntiles, nf_max(g));
-  constexpr int V = 16 / sizeof(E);
-  if (g.cpt == V) return fwd ? launch_fwd<E, V>(p, g, st) : launch_bwd<E, V>(p, g, st);
-  return fwd ? launch_fwd<E, 1>(p, g, st) : launch_bwd<E, 1>(p, g, st);
+  if (g.algo == kStrip) {
+    p.nchunks = g.nchunks;
+    p.ntiles = g.ntiles;
+    MGS_CUDA_OK(cudaMemsetAsync(ws, 0, 256, st));  // error word
+    p.lb = lookback_view(ws, 0, 0);
+    StripMaps maps;
+    const void* src[4] = {a, b, gA, gB};
+    for (int i = 0; i < (fwd ? 2 : 4); ++i)
+      if (!make_tmap_3d<E>(&maps.m[i], src[i], D, T, B, 32u, (unsigned)kLc)) return MGS_LAUNCH_FAILED;
+    void* kargs[] = {&p, &maps};
+    if (fwd)
+      return launch_persistent(fwd_strip_kernel<E>, (kStripNW + 1) * 32,
+                               StripStage<E, 2, false>::kStages * StripStage<E, 2, false>::kBytes,
+                               g.nstrips, kargs, st);
+    return launch_persistent(bwd_strip_kernel<E>, (kStripNW + 1) * 32,
+                             StripStage<E, 4, true>::kStages * StripStage<E, 4, true>::kBytes,
+                             g.nstrips, kargs, st);
+  }
+  const long long lbt = g.ntiles > g.ftiles ? g.ntiles : g.ftiles;
+  MGS_CUDA_OK(cudaMemsetAsync(ws, 0, lookback_zero_bytes(lbt), st));
+  p.lb = lookback_view(ws, lbt, nf_max(g));
+  if (fwd) {
+    p.nchunks = g.fchunks;
+    p.ntiles = g.ftiles;
+    if (g.algo == kDirectVec)
+      fwd_direct_kernel<E, kVecCpt, kVecFwdS, kVecFwdNW>
+          <<<(unsigned)g.ftiles, kVecFwdNW * 32, 0, st>>>(p);
+    else
+      fwd_direct_kernel<E, 1, kSclFwdS, kSclFwdNW><<<(unsigned)g.ftiles, kSclFwdNW * 32, 0, st>>>(p);
+  } else {
+    p.nchunks = g.nchunks;
+    p.ntiles = g.ntiles;
+    if (g.algo == kDirectVec)
+      bwd_direct_kernel<E, kVecCpt, kBwdS, kBwdNW><<<(unsigned)g.ntiles, kBwdNW * 32, 0, st>>>(p);
+    else
+      bwd_direct_kernel<E, 1, kBwdS, kBwdNW><<<(unsigned)g.ntiles, kBwdNW * 32, 0, st>>>(p);
+  }
+  return cudaGetLastError() == cudaSuccess ? MGS_OK : MGS_LAUNCH_FAILED;
 }
 
 int dispatch(bool fwd, const void* a, const void* b, void* A, void* Bc, const void* gA,
@@ -430,7 +770,7 @@ extern "C" {
 size_t mgs_linear_scan_workspace_size(int64_t B, int64_t T, int64_t D, int dtype) {
   if (mgs::dtype_size(dtype) == 0 || B < 0 || T < 0 || D < 0) return 0;
   const auto g = mgs::linear::geometry(B, T, D, dtype);
-  return mgs::lookback_bytes(g.ntiles, mgs::linear::nf_max(g));
+  return mgs::linear::workspace_bytes(g);
 }
 
 size_t mgs_linear_scan_carry_size(int64_t B, int64_t T, int64_t D, int dtype) {
