@@ -86,6 +86,31 @@ int mgs_linear_scan_bwd(const void* a, const void* b, const void* gA,
                         void* db, int64_t B, int64_t T, int64_t D, int dtype,
                         void* workspace, size_t workspace_bytes, void* stream);
 
+/* ------------------------------------------------------------------------ */
+/* parallel_scan_log: h_t = a_t h_{t-1} + b_t in log space, a_t =
+ * exp(log_coeffs[:, t-1]), b_t = exp(log_values[:, t]), h_0 =
+ * exp(log_values[:, 0]); returns h_1..h_T.
+ * Replaces min_gru.py:755 `parallel_scan_log(log_coeffs, log_values)`
+ * (eager cumsum + logcumsumexp, min_gru.py:804-807), its Triton forward
+ * triton_scans.py:753-821 / op parallel_scan_log_fwd (triton_scans.py:1336)
+ * and its recompute-through-eager backward (triton_scans.py:1489-1552).
+ * Layout: log_coeffs, h, grad_h, dlog_coeffs (B, T, D); log_values,
+ * dlog_values (B, T+1, D); all C-contiguous.                                 */
+
+size_t mgs_log_scan_workspace_size(int64_t B, int64_t T, int64_t D, int dtype);
+size_t mgs_log_scan_carry_size(int64_t B, int64_t T, int64_t D, int dtype);
+
+int mgs_log_scan_fwd(const void* log_coeffs, const void* log_values, void* h, void* carries,
+                     int64_t B, int64_t T, int64_t D, int dtype, void* workspace,
+                     size_t workspace_bytes, void* stream);
+
+/* Backward: (dlog_coeffs, dlog_values) of sum(h * grad_h), recomputing the
+ * log-states from the forward carries (hand-derived adjoint, no autograd). */
+int mgs_log_scan_bwd(const void* log_coeffs, const void* log_values, const void* grad_h,
+                     const void* carries, void* dlog_coeffs, void* dlog_values, int64_t B,
+                     int64_t T, int64_t D, int dtype, void* workspace, size_t workspace_bytes,
+                     void* stream);
+
 #ifdef __cplusplus
 }
 #endif

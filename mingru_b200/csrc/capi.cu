@@ -7,6 +7,7 @@
 namespace mgs {
 // One sticky error word per translation unit; each kernel file exports its reader.
 unsigned take_error_linear(cudaStream_t s);
+unsigned take_error_log(cudaStream_t s);
 }  // namespace mgs
 
 extern "C" {
@@ -31,6 +32,7 @@ int mgs_take_device_error(void* stream) {
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   unsigned bits = 0u;
   bits |= mgs::take_error_linear(s);
+  bits |= mgs::take_error_log(s);
   return (int)bits;
 }
 

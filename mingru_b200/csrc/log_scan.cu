@@ -1,0 +1,793 @@
+// log_scan.cu -- Heinsen log-space scan (parallel_scan_log) forward and
+// backward for (B, T, D) log_coeffs and (B, T+1, D) log_values, fp32 / bf16 /
+// fp16 storage, fp32 math.
+//
+// Reference behaviour: min_gru.py:755-807 `parallel_scan_log` solves
+// h_t = a_t h_{t-1} + b_t with a_t = exp(log_coeffs[t-1]), b_t =
+// exp(log_values[t]), h_0 = exp(log_values[0]), returning h_1..h_T, via
+// a* = cumsum(log a) and logcumsumexp(log_values - a*) (min_gru.py:804-807);
+// the Triton forward (triton_scans.py:753-821) walks T per channel with an
+// online max-shifted log-sum-exp and its backward recomputes through the
+// eager maths (triton_scans.py:1489-1552).
+//
+// Here the state is x_t = log h_t and each step is the log-space affine map
+// x_t = logaddexp(x_{t-1} + lc_t, lv_t). A segment's aggregate is the pair
+// (alpha, nu) acting as x -> logaddexp(x + alpha, nu); composition is
+// (a1, n1) then (a2, n2) = (a1 + a2, logaddexp(n1 + a2, n2)), identity
+// (0, -inf). The initial state enters as the element (-inf, log h_0), which
+// resets any state it is applied to (it is idempotent). Every quantity stays
+// local to a 32-step chunk, so unlike the reference's global cumulative sum
+// (|a*| grows ~T) nothing large cancels: the result tracks the fp64 oracle
+// more closely than the reference's own fp32 path does.
+//
+// Backward (hand-derived, exact): with G_t = dL/dh_t accumulated in reverse,
+//   G_t = g_t + a_{t+1} G_{t+1},  dlc_t = G_t exp(lc_t + x_{t-1}),
+//   dlv_t = G_t exp(lv_t) (t >= 1),  dlv_0 = a_1 G_1 h_0,
+// using the same chunk/strip machinery as linear_scan: the forward writes
+// chunk-start states ("carries"), the backward recomputes x_{t-1} from them
+// and carries Y_t = a_t G_t in reverse time order.
+#include "common.cuh"
+
+namespace mgs {
+namespace logscan {
+
+constexpr int kLc = 32;  // carry-chunk length = backward tile length
+
+constexpr int kVecCpt = 4;
+constexpr int kVecFwdS = 8, kVecFwdNW = 8;
+constexpr int kSclFwdS = 8, kSclFwdNW = 4;
+constexpr int kBwdS = 4, kBwdNW = 8;
+static_assert(kBwdS * kBwdNW == kLc, "backward tile must be one carry chunk");
+static_assert((kVecFwdS * kVecFwdNW) % kLc == 0 && kLc % kVecFwdS == 0, "vec carry grid");
+static_assert((kSclFwdS * kSclFwdNW) % kLc == 0 && kLc % kSclFwdS == 0, "scalar carry grid");
+
+constexpr int kStripNW = 4;
+constexpr int kStripS = kLc / kStripNW;
+constexpr int kRingBytes = 50 * 1024;
+
+enum Algo { kStrip = 0, kDirectVec = 1, kDirectScalar = 2 };
+
+inline int sm_count() {
+  int dev = 0, n = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return 148;
+  if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0)
+    return 148;
+  return n;
+}
+
+struct Geometry {
+  Algo algo;
+  int cpt;
+  long long sper, nstrips, nchunks, ntiles, fchunks, ftiles;
+};
+
+inline Geometry geometry(long long B, long long T, long long D, int dtype) {
+  Geometry g;
+  const bool rows16 = ((D * dtype_size(dtype)) % 16) == 0;
+  const long long strips32 = B * ((D + 31) / 32);
+  if (rows16 && strips32 >= 2LL * sm_count())
+    g.algo = kStrip;
+  else
+    g.algo = rows16 ? kDirectVec : kDirectScalar;
+  g.cpt = g.algo == kDirectVec ? kVecCpt : 1;
+  const long long w = 32LL * g.cpt;
+  g.sper = (D + w - 1) / w;
+  g.nstrips = B * g.sper;
+  g.nchunks = (T + kLc - 1) / kLc;
+  g.ntiles = g.nstrips * g.nchunks;
+  const int fl = g.algo == kDirectVec ? kVecFwdS * kVecFwdNW
+                                      : (g.algo == kDirectScalar ? kSclFwdS * kSclFwdNW : kLc);
+  g.fchunks = (T + fl - 1) / fl;
+  g.ftiles = g.nstrips * g.fchunks;
+  return g;
+}
+
+__device__ __forceinline__ float logaddexp(float p, float q) {
+  const float m = fmaxf(p, q);
+  if (m == -INFINITY || m == INFINITY) return m;
+  return m + log1pf(expf(fminf(p, q) - m));
+}
+
+// Forward monoid over (alpha, nu), C channels per lane: x = [alpha_0.., nu_0..].
+template <int C>
+struct FwdMonoid {
+  static constexpr int NF = 2 * C;
+  __device__ static void identity(float (&x)[NF]) {
+#pragma unroll
+    for (int c = 0; c < C; ++c) { x[c] = 0.f; x[C + c] = -INFINITY; }
+  }
+  __device__ static void combine(const float (&e)[NF], const float (&l)[NF], float (&o)[NF]) {
+#pragma unroll
+    for (int c = 0; c < C; ++c) {
+      o[C + c] = logaddexp(e[C + c] + l[c], l[C + c]);
+      o[c] = e[c] + l[c];
+    }
+  }
+};
+
+// Reverse monoid over Y_t = a_t (g_t + Y_{t+1}): x = [P, Q] per channel.
+template <int C>
+struct RevMonoid {
+  static constexpr int NF = 2 * C;
+  __device__ static void identity(float (&x)[NF]) {
+#pragma unroll
+    for (int c = 0; c < C; ++c) { x[c] = 1.f; x[C + c] = 0.f; }
+  }
+  __device__ static void combine(const float (&e)[NF], const float (&l)[NF], float (&o)[NF]) {
+#pragma unroll
+    for (int c = 0; c < C; ++c) {
+      o[C + c] = fmaf(l[c], e[C + c], l[C + c]);
+      o[c] = l[c] * e[c];
+    }
+  }
+};
+
+template <class M, int NF>
+__device__ __forceinline__ void combine_into(float (&acc)[NF], const float (&later)[NF]) {
+  float tmp[NF];
+  M::combine(acc, later, tmp);
+#pragma unroll
+  for (int f = 0; f < NF; ++f) acc[f] = tmp[f];
+}
+
+template <typename E>
+struct Args {
+  const E* lc;   // (B, T, D)
+  const E* lv;   // (B, T+1, D)
+  E* h;          // (B, T, D)
+  const E* gh;   // (B, T, D)
+  E* dlc;        // (B, T, D)
+  E* dlv;        // (B, T+1, D)
+  float* carries;
+  long long T_, D, sper, nstrips;
+  long long nchunks, ntiles;
+  Lookback lb;
+};
+
+struct StripMaps {
+  CUtensorMap m[3];
+};
+
+// Offsets of step t (0-based, output index) in the three layouts.
+struct Idx {
+  size_t tdb;   // (B, T, D) base of channel: bi*T*D + d
+  size_t t1db;  // (B, T+1, D) base of channel: bi*(T+1)*D + d
+};
+
+// Fold the h_0 element (-inf, lv0) into the running element: it resets the state.
+template <int C>
+__device__ __forceinline__ void fold_h0(float (&x)[2 * C], const float (&lv0)[C]) {
+#pragma unroll
+  for (int c = 0; c < C; ++c) { x[c] = -INFINITY; x[C + c] = lv0[c]; }
+}
+
+template <int C, int S>
+__device__ __forceinline__ void fwd_agg(const float (&lc)[S][C], const float (&lv)[S][C],
+                                        float (&agg)[2 * C]) {
+#pragma unroll
+  for (int s = 0; s < S; ++s)
+#pragma unroll
+    for (int c = 0; c < C; ++c) {
+      agg[C + c] = logaddexp(agg[C + c] + lc[s][c], lv[s][c]);
+      agg[c] += lc[s][c];
+    }
+}
+
+template <int C, int S>
+__device__ __forceinline__ void rev_agg(const float (&lc)[S][C], const float (&g)[S][C],
+                                        float (&ragg)[2 * C]) {
+  RevMonoid<C>::identity(ragg);
+#pragma unroll
+  for (int s = S - 1; s >= 0; --s)
+#pragma unroll
+    for (int c = 0; c < C; ++c) {
+      const float a = expf(lc[s][c]);
+      ragg[C + c] = a * (g[s][c] + ragg[C + c]);
+      ragg[c] *= a;
+    }
+}
+
+template <typename E, int C, int S>
+__device__ __forceinline__ void fwd_emit(const Args<E>& p, const float (&lc)[S][C],
+                                         const float (&lv)[S][C], float (&cur)[2 * C], bool dok,
+                                         long long t0, size_t base) {
+#pragma unroll
+  for (int s = 0; s < S; ++s) {
+    float oh[C];
+#pragma unroll
+    for (int c = 0; c < C; ++c) {
+      cur[C + c] = logaddexp(cur[C + c] + lc[s][c], lv[s][c]);
+      cur[c] += lc[s][c];
+      oh[c] = expf(cur[C + c]);
+    }
+    const long long t = t0 + s;
+    if (dok && t < p.T_) store_vec<E, C>(p.h + base + t * p.D, oh);
+  }
+}
+
+// Backward of S steps: fcur = forward element before the first step (its nu
+// is x_{t0-1}), y = adjoint Y entering from later steps.
+template <typename E, int C, int S>
+__device__ __forceinline__ void bwd_emit(const Args<E>& p, const float (&lc)[S][C],
+                                         const float (&lv)[S][C], const float (&g)[S][C],
+                                         float (&fcur)[2 * C], float (&y)[C], bool dok,
+                                         long long t0, size_t base, size_t base1,
+                                         const float (&lv0)[C]) {
+  float xp[S][C];
+#pragma unroll
+  for (int s = 0; s < S; ++s)
+#pragma unroll
+    for (int c = 0; c < C; ++c) {
+      xp[s][c] = fcur[C + c];
+      fcur[C + c] = logaddexp(fcur[C + c] + lc[s][c], lv[s][c]);
+    }
+#pragma unroll
+  for (int s = S - 1; s >= 0; --s) {
+    float odc[C], odv[C];
+#pragma unroll
+    for (int c = 0; c < C; ++c) {
+      const float G = g[s][c] + y[c];
+      odc[c] = G * expf(lc[s][c] + xp[s][c]);
+      odv[c] = G * expf(lv[s][c]);
+      y[c] = expf(lc[s][c]) * G;
+    }
+    const long long t = t0 + s;
+    if (dok && t < p.T_) {
+      store_vec<E, C>(p.dlc + base + t * p.D, odc);
+      store_vec<E, C>(p.dlv + base1 + (t + 1) * p.D, odv);
+    }
+  }
+  if (dok && t0 == 0) {
+    float o0[C];
+#pragma unroll
+    for (int c = 0; c < C; ++c) o0[c] = y[c] * expf(lv0[c]);
+    store_vec<E, C>(p.dlv + base1, o0);
+  }
+}
+
+template <typename E, int C, int S>
+__device__ __forceinline__ void load_steps(const E* src, size_t base, long long t0, long long T,
+                                           long long D, bool dok, float fill, float (&out)[S][C]) {
+#pragma unroll
+  for (int s = 0; s < S; ++s) {
+    const long long t = t0 + s;
+    if (dok && t < T)
+      load_vec<E, C>(src + base + t * D, out[s]);
+    else
+#pragma unroll
+      for (int c = 0; c < C; ++c) out[s][c] = fill;
+  }
+}
+
+// ------------------------------------------------------------ direct path --
+
+template <typename E, int C, int S, int NW>
+__global__ void __launch_bounds__(NW * 32) fwd_direct_kernel(Args<E> p) {
+  using M = FwdMonoid<C>;
+  constexpr int NF = M::NF;
+  constexpr int L = S * NW;
+  __shared__ unsigned s_tile;
+  __shared__ float s_agg[NW][NF][32];
+  __shared__ float s_ex[NF][32];
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  if (threadIdx.x == 0) s_tile = atomicAdd(p.lb.counter, 1u);
+  __syncthreads();
+  const long long tile = s_tile;
+  const long long chunk = tile / p.nstrips;
+  const long long strip = tile - chunk * p.nstrips;
+  const long long bi = strip / p.sper;
+  const long long d0 = (strip - bi * p.sper) * (32LL * C) + (long long)lane * C;
+  const bool dok = d0 < p.D;
+  const long long t0 = chunk * L + (long long)warp * S;
+  const size_t base = (size_t)bi * p.T_ * p.D + d0;
+  const size_t base1 = (size_t)bi * (p.T_ + 1) * p.D + d0;
+
+  float lc[S][C], lv[S][C], lv0[C];
+  load_steps<E, C, S>(p.lc, base, t0, p.T_, p.D, dok, 0.f, lc);
+  load_steps<E, C, S>(p.lv, base1 + p.D, t0, p.T_, p.D, dok, -INFINITY, lv);
+  if (t0 == 0 && dok) load_vec<E, C>(p.lv + base1, lv0);
+  float agg[NF];
+  M::identity(agg);
+  if (t0 == 0 && dok) fold_h0<C>(agg, lv0);
+  fwd_agg<C, S>(lc, lv, agg);
+#pragma unroll
+  for (int f = 0; f < NF; ++f) s_agg[warp][f][lane] = agg[f];
+  __syncthreads();
+
+  if (warp == 0) {
+    float tot[NF], w_[NF];
+#pragma unroll
+    for (int f = 0; f < NF; ++f) tot[f] = s_agg[0][f][lane];
+#pragma unroll
+    for (int w = 1; w < NW; ++w) {
+#pragma unroll
+      for (int f = 0; f < NF; ++f) w_[f] = s_agg[w][f][lane];
+      combine_into<M, NF>(tot, w_);
+    }
+    float ex[NF];
+    warp_lookback_win<M, NF>(p.lb, tile, p.nstrips, chunk, tot, ex);
+#pragma unroll
+    for (int f = 0; f < NF; ++f) s_ex[f][lane] = ex[f];
+  }
+  __syncthreads();
+
+  float cur[NF], w_[NF];
+#pragma unroll
+  for (int f = 0; f < NF; ++f) cur[f] = s_ex[f][lane];
+  for (int w = 0; w < warp; ++w) {
+#pragma unroll
+    for (int f = 0; f < NF; ++f) w_[f] = s_agg[w][f][lane];
+    combine_into<M, NF>(cur, w_);
+  }
+  if (t0 == 0 && dok) fold_h0<C>(cur, lv0);
+  if (p.carries != nullptr && ((warp * S) % kLc) == 0 && t0 < p.T_) {
+    float* dst = p.carries + (size_t)((t0 / kLc) * p.nstrips + strip) * NF * 32;
+#pragma unroll
+    for (int f = 0; f < NF; ++f) __stcs(dst + f * 32 + lane, cur[f]);
+  }
+  fwd_emit<E, C, S>(p, lc, lv, cur, dok, t0, base);
+}
+
+template <typename E, int C, int S, int NW>
+__global__ void __launch_bounds__(NW * 32) bwd_direct_kernel(Args<E> p) {
+  using FM = FwdMonoid<C>;
+  using RM = RevMonoid<C>;
+  constexpr int NFF = FM::NF, NFR = RM::NF;
+  constexpr int L = S * NW;
+  static_assert(L == kLc, "backward tile = carry chunk");
+  __shared__ unsigned s_tile;
+  __shared__ float s_fagg[NW][NFF][32];
+  __shared__ float s_ragg[NW][NFR][32];
+  __shared__ float s_fex[NFF][32];
+  __shared__ float s_rex[NFR][32];
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  if (threadIdx.x == 0) s_tile = atomicAdd(p.lb.counter, 1u);
+  __syncthreads();
+  const long long tile = s_tile;
+  const long long rchunk = tile / p.nstrips;
+  const long long strip = tile - rchunk * p.nstrips;
+  const long long chunk = p.nchunks - 1 - rchunk;
+  const long long bi = strip / p.sper;
+  const long long d0 = (strip - bi * p.sper) * (32LL * C) + (long long)lane * C;
+  const bool dok = d0 < p.D;
+  const long long t0 = chunk * L + (long long)warp * S;
+  const size_t base = (size_t)bi * p.T_ * p.D + d0;
+  const size_t base1 = (size_t)bi * (p.T_ + 1) * p.D + d0;
+
+  float lc[S][C], lv[S][C], g[S][C], lv0[C];
+  load_steps<E, C, S>(p.lc, base, t0, p.T_, p.D, dok, 0.f, lc);
+  load_steps<E, C, S>(p.lv, base1 + p.D, t0, p.T_, p.D, dok, -INFINITY, lv);
+  load_steps<E, C, S>(p.gh, base, t0, p.T_, p.D, dok, 0.f, g);
+  if (t0 == 0 && dok) load_vec<E, C>(p.lv + base1, lv0);
+  float fagg[NFF], ragg[NFR];
+  FM::identity(fagg);
+  if (t0 == 0 && dok) fold_h0<C>(fagg, lv0);
+  fwd_agg<C, S>(lc, lv, fagg);
+  rev_agg<C, S>(lc, g, ragg);
+#pragma unroll
+  for (int f = 0; f < NFF; ++f) s_fagg[warp][f][lane] = fagg[f];
+#pragma unroll
+  for (int f = 0; f < NFR; ++f) s_ragg[warp][f][lane] = ragg[f];
+  __syncthreads();
+
+  if (warp == 0) {
+    float tot[NFR], w_[NFR];
+#pragma unroll
+    for (int f = 0; f < NFR; ++f) tot[f] = s_ragg[NW - 1][f][lane];
+#pragma unroll
+    for (int w = NW - 2; w >= 0; --w) {
+#pragma unroll
+      for (int f = 0; f < NFR; ++f) w_[f] = s_ragg[w][f][lane];
+      combine_into<RM, NFR>(tot, w_);
+    }
+    float ex[NFR];
+    warp_lookback_win<RM, NFR>(p.lb, tile, p.nstrips, rchunk, tot, ex);
+#pragma unroll
+    for (int f = 0; f < NFR; ++f) s_rex[f][lane] = ex[f];
+  } else if (warp == 1) {
+    const float* src = p.carries + (size_t)(chunk * p.nstrips + strip) * NFF * 32;
+#pragma unroll
+    for (int f = 0; f < NFF; ++f) s_fex[f][lane] = __ldcs(src + f * 32 + lane);
+  }
+  __syncthreads();
+
+  float fcur[NFF], rcur[NFR];
+  {
+    float w_[NFF];
+#pragma unroll
+    for (int f = 0; f < NFF; ++f) fcur[f] = s_fex[f][lane];
+    for (int w = 0; w < warp; ++w) {
+#pragma unroll
+      for (int f = 0; f < NFF; ++f) w_[f] = s_fagg[w][f][lane];
+      combine_into<FM, NFF>(fcur, w_);
+    }
+  }
+  if (t0 == 0 && dok) fold_h0<C>(fcur, lv0);
+  {
+    float w_[NFR];
+#pragma unroll
+    for (int f = 0; f < NFR; ++f) rcur[f] = s_rex[f][lane];
+    for (int w = NW - 1; w > warp; --w) {
+#pragma unroll
+      for (int f = 0; f < NFR; ++f) w_[f] = s_ragg[w][f][lane];
+      combine_into<RM, NFR>(rcur, w_);
+    }
+  }
+  float y[C];
+#pragma unroll
+  for (int c = 0; c < C; ++c) y[c] = rcur[C + c];
+  bwd_emit<E, C, S>(p, lc, lv, g, fcur, y, dok, t0, base, base1, lv0);
+}
+
+// ------------------------------------------------------------- strip path --
+
+template <typename E, int NIN, bool WITH_CARRY>
+struct StripStage {
+  static constexpr size_t kArrayBytes = (size_t)kLc * 32 * sizeof(E);
+  static constexpr size_t kCarryBytes = WITH_CARRY ? 2 * 32 * sizeof(float) : 0;
+  static constexpr size_t kBytes = (NIN * kArrayBytes + kCarryBytes + 127) / 128 * 128;
+  static constexpr int kStages = (int)(kRingBytes / kBytes);
+};
+
+// Arrays: 0 = lc (rows t), 1 = lv (rows t+1), 2 = gh (rows t).
+template <typename E, int NIN, bool WITH_CARRY, bool REVERSE>
+__device__ __forceinline__ void strip_produce(const Args<E>& p, const StripMaps& maps,
+                                              unsigned char* ring, uint64_t* full,
+                                              uint64_t* empty) {
+  using SS = StripStage<E, NIN, WITH_CARRY>;
+  constexpr int NSTAGE = SS::kStages;
+  const int lane = threadIdx.x & 31;
+  if (lane == 0)
+    for (int i = 0; i < NIN; ++i) tma_prefetch_desc(&maps.m[i]);
+  int s = 0;
+  unsigned ph = 0, pending = 0u, pend_ph = 0u;
+  for (long long strip = blockIdx.x; strip < p.nstrips; strip += gridDim.x) {
+    const long long bi = strip / p.sper;
+    const int d0 = (int)((strip - bi * p.sper) * 32);
+    for (long long q = 0; q < p.nchunks; ++q) {
+      const long long chunk = REVERSE ? p.nchunks - 1 - q : q;
+      if (!mbar_wait(&empty[s], ph ^ 1u, p.lb.err)) goto drain;
+      pending &= ~(1u << s);
+      if (lane == 0) {
+        unsigned char* stage = ring + (size_t)s * SS::kBytes;
+        mbar_arrive_expect_tx(&full[s], (unsigned)(NIN * SS::kArrayBytes + SS::kCarryBytes));
+#pragma unroll
+        for (int arr = 0; arr < NIN; ++arr)
+          tma_load_3d(stage + arr * SS::kArrayBytes, &maps.m[arr], d0,
+                      (int)(chunk * kLc) + (arr == 1 ? 1 : 0), (int)bi, &full[s]);
+        if (WITH_CARRY)
+          bulk_g2s(stage + NIN * SS::kArrayBytes,
+                   p.carries + (size_t)(chunk * p.nstrips + strip) * 2 * 32,
+                   (unsigned)SS::kCarryBytes, &full[s]);
+      }
+      __syncwarp();
+      pending |= 1u << s;
+      pend_ph = (pend_ph & ~(1u << s)) | (ph << s);
+      if (++s == NSTAGE) {
+        s = 0;
+        ph ^= 1u;
+      }
+    }
+  }
+drain:
+  for (int i = 0; i < NSTAGE; ++i)
+    if (pending & (1u << i)) mbar_wait(&full[i], (pend_ph >> i) & 1u, p.lb.err);
+}
+
+template <typename E, int S>
+__device__ __forceinline__ void strip_rows(const unsigned char* arr_base, int row0, long long t0,
+                                           long long T, bool dok, float fill, float (&out)[S][1]) {
+  const int lane = threadIdx.x & 31;
+  const E* base = reinterpret_cast<const E*>(arr_base) + lane;
+#pragma unroll
+  for (int s = 0; s < S; ++s)
+    out[s][0] = (dok && t0 + s < T) ? to_f32<E>(base[(row0 + s) * 32]) : fill;
+}
+
+template <typename E>
+__global__ void __launch_bounds__((kStripNW + 1) * 32)
+    fwd_strip_kernel(Args<E> p, const __grid_constant__ StripMaps maps) {
+  using SS = StripStage<E, 2, false>;
+  constexpr int NSTAGE = SS::kStages;
+  constexpr int NW = kStripNW, S = kStripS, NF = 2;
+  using M = FwdMonoid<1>;
+  extern __shared__ __align__(128) unsigned char ring[];
+  __shared__ __align__(8) uint64_t full[NSTAGE], empty[NSTAGE];
+  __shared__ float s_agg[2][NW][NF][32];
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < NSTAGE; ++i) {
+      mbar_init(&full[i], 1);
+      mbar_init(&empty[i], NW);
+    }
+    mbar_fence_init();
+  }
+  __syncthreads();
+  if (warp == NW) {
+    strip_produce<E, 2, false, false>(p, maps, ring, full, empty);
+    return;
+  }
+  int s = 0, buf = 0;
+  unsigned ph = 0;
+  for (long long strip = blockIdx.x; strip < p.nstrips; strip += gridDim.x) {
+    const long long bi = strip / p.sper;
+    const long long d = (strip - bi * p.sper) * 32 + lane;
+    const bool dok = d < p.D;
+    const size_t base = (size_t)bi * p.T_ * p.D + d;
+    const size_t base1 = (size_t)bi * (p.T_ + 1) * p.D + d;
+    float carry[NF] = {-INFINITY, dok ? to_f32<E>(p.lv[base1]) : -INFINITY};
+    for (long long chunk = 0; chunk < p.nchunks; ++chunk) {
+      const bool ok = mbar_wait(&full[s], ph, p.lb.err);
+      if (bar_any(1, NW * 32, !ok)) return;
+      const unsigned char* stage = ring + (size_t)s * SS::kBytes;
+      const long long t0 = chunk * kLc + (long long)warp * S;
+      float lc[S][1], lv[S][1];
+      strip_rows<E, S>(stage, warp * S, t0, p.T_, dok, 0.f, lc);
+      strip_rows<E, S>(stage + SS::kArrayBytes, warp * S, t0, p.T_, dok, -INFINITY, lv);
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&empty[s]);
+      if (++s == NSTAGE) {
+        s = 0;
+        ph ^= 1u;
+      }
+      float agg[NF];
+      M::identity(agg);
+      fwd_agg<1, S>(lc, lv, agg);
+      s_agg[buf][warp][0][lane] = agg[0];
+      s_agg[buf][warp][1][lane] = agg[1];
+      named_bar(2, NW * 32);
+      if (warp == 0 && p.carries != nullptr) {
+        float* dst = p.carries + (size_t)(chunk * p.nstrips + strip) * NF * 32;
+        __stcs(dst + lane, carry[0]);
+        __stcs(dst + 32 + lane, carry[1]);
+      }
+      float cur[NF] = {carry[0], carry[1]};
+#pragma unroll
+      for (int w = 0; w < NW; ++w) {
+        const float e[NF] = {s_agg[buf][w][0][lane], s_agg[buf][w][1][lane]};
+        if (w == warp) {
+          cur[0] = carry[0];
+          cur[1] = carry[1];
+        }
+        combine_into<M, NF>(carry, e);
+      }
+      fwd_emit<E, 1, S>(p, lc, lv, cur, dok, t0, base);
+      buf ^= 1;
+    }
+  }
+}
+
+template <typename E>
+__global__ void __launch_bounds__((kStripNW + 1) * 32)
+    bwd_strip_kernel(Args<E> p, const __grid_constant__ StripMaps maps) {
+  using SS = StripStage<E, 3, true>;
+  constexpr int NSTAGE = SS::kStages;
+  constexpr int NW = kStripNW, S = kStripS;
+  using FM = FwdMonoid<1>;
+  using RM = RevMonoid<1>;
+  extern __shared__ __align__(128) unsigned char ring[];
+  __shared__ __align__(8) uint64_t full[NSTAGE], empty[NSTAGE];
+  __shared__ float s_fagg[2][NW][2][32];
+  __shared__ float s_ragg[2][NW][2][32];
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < NSTAGE; ++i) {
+      mbar_init(&full[i], 1);
+      mbar_init(&empty[i], NW);
+    }
+    mbar_fence_init();
+  }
+  __syncthreads();
+  if (warp == NW) {
+    strip_produce<E, 3, true, true>(p, maps, ring, full, empty);
+    return;
+  }
+  int s = 0, buf = 0;
+  unsigned ph = 0;
+  for (long long strip = blockIdx.x; strip < p.nstrips; strip += gridDim.x) {
+    const long long bi = strip / p.sper;
+    const long long d = (strip - bi * p.sper) * 32 + lane;
+    const bool dok = d < p.D;
+    const size_t base = (size_t)bi * p.T_ * p.D + d;
+    const size_t base1 = (size_t)bi * (p.T_ + 1) * p.D + d;
+    float lv0[1] = {dok ? to_f32<E>(p.lv[base1]) : -INFINITY};
+    float rcarry[2];
+    RM::identity(rcarry);
+    for (long long q = 0; q < p.nchunks; ++q) {
+      const long long chunk = p.nchunks - 1 - q;
+      const bool ok = mbar_wait(&full[s], ph, p.lb.err);
+      if (bar_any(1, NW * 32, !ok)) return;
+      const unsigned char* stage = ring + (size_t)s * SS::kBytes;
+      const long long t0 = chunk * kLc + (long long)warp * S;
+      float lc[S][1], lv[S][1], g[S][1];
+      strip_rows<E, S>(stage, warp * S, t0, p.T_, dok, 0.f, lc);
+      strip_rows<E, S>(stage + SS::kArrayBytes, warp * S, t0, p.T_, dok, -INFINITY, lv);
+      strip_rows<E, S>(stage + 2 * SS::kArrayBytes, warp * S, t0, p.T_, dok, 0.f, g);
+      const float* fc = reinterpret_cast<const float*>(stage + 3 * SS::kArrayBytes);
+      float fcur[2] = {fc[lane], fc[32 + lane]};
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&empty[s]);
+      if (++s == NSTAGE) {
+        s = 0;
+        ph ^= 1u;
+      }
+      float fagg[2], ragg[2];
+      FM::identity(fagg);
+      fwd_agg<1, S>(lc, lv, fagg);
+      rev_agg<1, S>(lc, g, ragg);
+      s_fagg[buf][warp][0][lane] = fagg[0];
+      s_fagg[buf][warp][1][lane] = fagg[1];
+      s_ragg[buf][warp][0][lane] = ragg[0];
+      s_ragg[buf][warp][1][lane] = ragg[1];
+      named_bar(2, NW * 32);
+      for (int w = 0; w < warp; ++w) {
+        const float e[2] = {s_fagg[buf][w][0][lane], s_fagg[buf][w][1][lane]};
+        combine_into<FM, 2>(fcur, e);
+      }
+      float rcur[2] = {rcarry[0], rcarry[1]};
+#pragma unroll
+      for (int w = NW - 1; w >= 0; --w) {
+        if (w == warp) {
+          rcur[0] = rcarry[0];
+          rcur[1] = rcarry[1];
+        }
+        const float e[2] = {s_ragg[buf][w][0][lane], s_ragg[buf][w][1][lane]};
+        combine_into<RM, 2>(rcarry, e);
+      }
+      float y[1] = {rcur[1]};
+      bwd_emit<E, 1, S>(p, lc, lv, g, fcur, y, dok, t0, base, base1, lv0);
+      buf ^= 1;
+    }
+  }
+}
+
+// ---------------------------------------------------------------- launch --
+
+template <class K>
+int launch_persistent(K kernel, int threads, size_t dyn_smem, long long units, void** kargs,
+                      cudaStream_t st) {
+  MGS_CUDA_OK(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                   (int)dyn_smem));
+  int per_sm = 0;
+  MGS_CUDA_OK(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kernel, threads, dyn_smem));
+  if (per_sm < 1) return MGS_LAUNCH_FAILED;
+  long long grid = (long long)per_sm * sm_count();
+  if (grid > units) grid = units;
+  MGS_CUDA_OK(cudaLaunchKernel((const void*)kernel, dim3((unsigned)grid), dim3(threads), kargs,
+                               dyn_smem, st));
+  return MGS_OK;
+}
+
+inline int nf_max(const Geometry& g) { return 2 * g.cpt; }
+
+inline size_t workspace_bytes(const Geometry& g) {
+  if (g.algo == kStrip) return 256;
+  return lookback_bytes(g.ntiles > g.ftiles ? g.ntiles : g.ftiles, nf_max(g));
+}
+
+template <typename E>
+int run(bool fwd, const void* lc, const void* lv, void* h, const void* gh, void* dlc, void* dlv,
+        void* carries, long long B, long long T, long long D, int dtype, void* ws,
+        size_t ws_bytes, cudaStream_t st) {
+  const Geometry g = geometry(B, T, D, dtype);
+  if (g.ntiles == 0) {
+    // T == 0: the only gradient is dlv[:, 0] = 0 (h_0 feeds no output).
+    if (!fwd && B > 0 && D > 0 && dlv != nullptr)
+      MGS_CUDA_OK(cudaMemsetAsync(dlv, 0, (size_t)(B * D) * sizeof(E), st));
+    return MGS_OK;
+  }
+  if (g.ntiles > 0x7fffffffLL) return MGS_UNSUPPORTED;
+  if (ws == nullptr || ws_bytes < workspace_bytes(g)) return MGS_WORKSPACE_TOO_SMALL;
+  const size_t va = g.algo == kDirectScalar ? sizeof(E) : 16;
+  const void* ptrs[6] = {lc, lv, fwd ? h : gh, fwd ? nullptr : dlc, fwd ? nullptr : dlv, nullptr};
+  for (const void* q : ptrs)
+    if (q != nullptr && !aligned(q, va)) return MGS_BAD_ALIGNMENT;
+  if (!aligned(ws, 256) || (carries != nullptr && !aligned(carries, 16))) return MGS_BAD_ALIGNMENT;
+  if (!fwd && carries == nullptr) return MGS_BAD_SHAPE;
+  Args<E> p;
+  p.lc = static_cast<const E*>(lc);
+  p.lv = static_cast<const E*>(lv);
+  p.h = static_cast<E*>(h);
+  p.gh = static_cast<const E*>(gh);
+  p.dlc = static_cast<E*>(dlc);
+  p.dlv = static_cast<E*>(dlv);
+  p.carries = static_cast<float*>(carries);
+  p.T_ = T;
+  p.D = D;
+  p.sper = g.sper;
+  p.nstrips = g.nstrips;
+  if (g.algo == kStrip) {
+    p.nchunks = g.nchunks;
+    p.ntiles = g.ntiles;
+    MGS_CUDA_OK(cudaMemsetAsync(ws, 0, 256, st));
+    p.lb = lookback_view(ws, 0, 0);
+    StripMaps maps;
+    if (!make_tmap_3d<E>(&maps.m[0], lc, D, T, B, 32u, (unsigned)kLc) ||
+        !make_tmap_3d<E>(&maps.m[1], lv, D, T + 1, B, 32u, (unsigned)kLc) ||
+        (!fwd && !make_tmap_3d<E>(&maps.m[2], gh, D, T, B, 32u, (unsigned)kLc)))
+      return MGS_LAUNCH_FAILED;
+    void* kargs[] = {&p, &maps};
+    if (fwd)
+      return launch_persistent(fwd_strip_kernel<E>, (kStripNW + 1) * 32,
+                               StripStage<E, 2, false>::kStages * StripStage<E, 2, false>::kBytes,
+                               g.nstrips, kargs, st);
+    return launch_persistent(bwd_strip_kernel<E>, (kStripNW + 1) * 32,
+                             StripStage<E, 3, true>::kStages * StripStage<E, 3, true>::kBytes,
+                             g.nstrips, kargs, st);
+  }
+  const long long lbt = g.ntiles > g.ftiles ? g.ntiles : g.ftiles;
+  MGS_CUDA_OK(cudaMemsetAsync(ws, 0, lookback_zero_bytes(lbt), st));
+  p.lb = lookback_view(ws, lbt, nf_max(g));
+  if (fwd) {
+    p.nchunks = g.fchunks;
+    p.ntiles = g.ftiles;
+    if (g.algo == kDirectVec)
+      fwd_direct_kernel<E, kVecCpt, kVecFwdS, kVecFwdNW>
+          <<<(unsigned)g.ftiles, kVecFwdNW * 32, 0, st>>>(p);
+    else
+      fwd_direct_kernel<E, 1, kSclFwdS, kSclFwdNW><<<(unsigned)g.ftiles, kSclFwdNW * 32, 0, st>>>(p);
+  } else {
+    p.nchunks = g.nchunks;
+    p.ntiles = g.ntiles;
+    if (g.algo == kDirectVec)
+      bwd_direct_kernel<E, kVecCpt, kBwdS, kBwdNW><<<(unsigned)g.ntiles, kBwdNW * 32, 0, st>>>(p);
+    else
+      bwd_direct_kernel<E, 1, kBwdS, kBwdNW><<<(unsigned)g.ntiles, kBwdNW * 32, 0, st>>>(p);
+  }
+  return cudaGetLastError() == cudaSuccess ? MGS_OK : MGS_LAUNCH_FAILED;
+}
+
+int dispatch(bool fwd, const void* lc, const void* lv, void* h, const void* gh, void* dlc,
+             void* dlv, void* carries, long long B, long long T, long long D, int dtype, void* ws,
+             size_t ws_bytes, cudaStream_t st) {
+  if (B < 0 || T < 0 || D < 0) return MGS_BAD_SHAPE;
+  switch (dtype) {
+    case MGS_F32:
+      return run<float>(fwd, lc, lv, h, gh, dlc, dlv, carries, B, T, D, dtype, ws, ws_bytes, st);
+    case MGS_BF16:
+      return run<__nv_bfloat16>(fwd, lc, lv, h, gh, dlc, dlv, carries, B, T, D, dtype, ws,
+                                ws_bytes, st);
+    case MGS_F16:
+      return run<__half>(fwd, lc, lv, h, gh, dlc, dlv, carries, B, T, D, dtype, ws, ws_bytes, st);
+    default:
+      return MGS_BAD_DTYPE;
+  }
+}
+
+}  // namespace logscan
+
+unsigned take_error_log(cudaStream_t s) { return take_sticky_error(s); }
+
+}  // namespace mgs
+
+extern "C" {
+
+size_t mgs_log_scan_workspace_size(int64_t B, int64_t T, int64_t D, int dtype) {
+  if (mgs::dtype_size(dtype) == 0 || B < 0 || T < 0 || D < 0) return 0;
+  return mgs::logscan::workspace_bytes(mgs::logscan::geometry(B, T, D, dtype));
+}
+
+size_t mgs_log_scan_carry_size(int64_t B, int64_t T, int64_t D, int dtype) {
+  if (mgs::dtype_size(dtype) == 0 || B < 0 || T < 0 || D < 0) return 0;
+  const auto g = mgs::logscan::geometry(B, T, D, dtype);
+  return (size_t)g.ntiles * 2 * g.cpt * 32 * sizeof(float);
+}
+
+int mgs_log_scan_fwd(const void* log_coeffs, const void* log_values, void* h, void* carries,
+                     int64_t B, int64_t T, int64_t D, int dtype, void* workspace,
+                     size_t workspace_bytes, void* stream) {
+  return mgs::logscan::dispatch(true, log_coeffs, log_values, h, nullptr, nullptr, nullptr,
+                                carries, B, T, D, dtype, workspace, workspace_bytes,
+                                static_cast<cudaStream_t>(stream));
+}
+
+int mgs_log_scan_bwd(const void* log_coeffs, const void* log_values, const void* grad_h,
+                     const void* carries, void* dlog_coeffs, void* dlog_values, int64_t B,
+                     int64_t T, int64_t D, int dtype, void* workspace, size_t workspace_bytes,
+                     void* stream) {
+  return mgs::logscan::dispatch(false, log_coeffs, log_values, nullptr, grad_h, dlog_coeffs,
+                                dlog_values, const_cast<void*>(carries), B, T, D, dtype,
+                                workspace, workspace_bytes, static_cast<cudaStream_t>(stream));
+}
+
+}  // extern "C"

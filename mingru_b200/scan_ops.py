@@ -150,6 +150,7 @@ def _linear_setup(ctx, inputs, output):
     a, b, _ = inputs
     ctx.save_for_backward(a, b, output[2])
     ctx.mark_non_differentiable(output[2])
+    ctx.set_materialize_grads(False)
 
 
 def _linear_backward(ctx, gA, gBc, _gcarries):
@@ -190,3 +191,109 @@ def linear_scan(a: torch.Tensor, b: torch.Tensor) -> tuple[torch.Tensor, torch.T
     need = torch.is_grad_enabled() and (a.requires_grad or b.requires_grad)
     A, Bc, _ = _linear_scan_fwd(a, b, need)
     return A, Bc
+
+
+# ===================================================== parallel_scan_log ==
+
+
+@torch.library.custom_op("mingru_b200::log_scan_fwd", mutates_args=())
+def _log_scan_fwd(
+    log_coeffs: torch.Tensor, log_values: torch.Tensor, save_carries: bool
+) -> tuple[torch.Tensor, torch.Tensor]:
+    lib = _lib.load()
+    lc, lv = _dense(log_coeffs), _dense(log_values)
+    Bn, T, D = lc.shape
+    code = _dtype_code("parallel_scan_log", lc)
+    h = torch.empty_like(lc)
+    csz = lib.mgs_log_scan_carry_size(Bn, T, D, code) if save_carries else 0
+    carries = torch.empty(csz // 4, dtype=torch.float32, device=lc.device)
+    ws = _workspace(lib.mgs_log_scan_workspace_size(Bn, T, D, code), lc.device)
+    with torch.cuda.device(lc.device):
+        st = lib.mgs_log_scan_fwd(
+            _ptr(lc), _ptr(lv), _ptr(h), _ptr(carries) if save_carries else None,
+            Bn, T, D, code, _ptr(ws), ws.numel(), _stream(lc),
+        )
+    _lib.check(st, "parallel_scan_log forward")
+    return h, carries
+
+
+@_log_scan_fwd.register_fake
+def _(log_coeffs, log_values, save_carries):
+    Bn, T, D = log_coeffs.shape
+    csz = _lib.load().mgs_log_scan_carry_size(Bn, T, D, _dtype_code("parallel_scan_log", log_coeffs))
+    n = csz // 4 if save_carries else 0
+    return torch.empty_like(log_coeffs), log_coeffs.new_empty((n,), dtype=torch.float32)
+
+
+@torch.library.custom_op("mingru_b200::log_scan_bwd", mutates_args=())
+def _log_scan_bwd(
+    log_coeffs: torch.Tensor, log_values: torch.Tensor, grad_h: torch.Tensor, carries: torch.Tensor
+) -> tuple[torch.Tensor, torch.Tensor]:
+    lib = _lib.load()
+    lc, lv = _dense(log_coeffs), _dense(log_values)
+    gh = _dense(grad_h.to(lc.dtype))
+    Bn, T, D = lc.shape
+    code = _dtype_code("parallel_scan_log", lc)
+    if carries.numel() * 4 < lib.mgs_log_scan_carry_size(Bn, T, D, code):
+        raise RuntimeError("parallel_scan_log backward: forward carries were not saved")
+    dlc, dlv = torch.empty_like(lc), torch.empty_like(lv)
+    ws = _workspace(lib.mgs_log_scan_workspace_size(Bn, T, D, code), lc.device)
+    with torch.cuda.device(lc.device):
+        st = lib.mgs_log_scan_bwd(
+            _ptr(lc), _ptr(lv), _ptr(gh), _ptr(carries), _ptr(dlc), _ptr(dlv),
+            Bn, T, D, code, _ptr(ws), ws.numel(), _stream(lc),
+        )
+    _lib.check(st, "parallel_scan_log backward")
+    return dlc, dlv
+
+
+@_log_scan_bwd.register_fake
+def _(log_coeffs, log_values, grad_h, carries):
+    return torch.empty_like(log_coeffs), torch.empty_like(log_values)
+
+
+def _log_setup(ctx, inputs, output):
+    lc, lv, _ = inputs
+    ctx.save_for_backward(lc, lv, output[1])
+    ctx.mark_non_differentiable(output[1])
+    ctx.set_materialize_grads(False)
+
+
+def _log_backward(ctx, grad_h, _gcarries):
+    if torch.is_grad_enabled():
+        raise RuntimeError(
+            "parallel_scan_log does not support second-order autograd (create_graph=True)"
+        )
+    lc, lv, carries = ctx.saved_tensors
+    if grad_h is None:
+        return None, None, None
+    dlc, dlv = _log_scan_bwd(lc, lv, grad_h, carries)
+    return dlc, dlv, None
+
+
+torch.library.register_autograd("mingru_b200::log_scan_fwd", _log_backward, setup_context=_log_setup)
+
+
+def parallel_scan_log(log_coeffs: torch.Tensor, log_values: torch.Tensor) -> torch.Tensor:
+    """Heinsen log-space scan: ``h_t = a_t h_{t-1} + b_t`` given logs.
+
+    ``log_coeffs`` ``(B, T, D)`` holds ``log a_t``; ``log_values``
+    ``(B, T+1, D)`` holds ``log h_0`` in slot 0 and ``log b_t`` after it.
+    Returns ``h_1..h_T`` as ``(B, T, D)`` in the input dtype (fp32 maths).
+    Same contract as the reference's ``min_gru.parallel_scan_log``
+    (``min_gru.py:755-807``).
+    """
+    op = "parallel_scan_log"
+    lc, lv = log_coeffs, log_values
+    if lc.ndim != 3 or lv.ndim != 3 or tuple(lv.shape) != (lc.shape[0], lc.shape[1] + 1, lc.shape[2]):
+        raise ValueError(
+            f"{op}: need (B, T, D) log_coeffs and (B, T+1, D) log_values "
+            f"(got log_coeffs={tuple(lc.shape)}, log_values={tuple(lv.shape)})"
+        )
+    _require_cuda(op, lc, lv)
+    if lc.dtype != lv.dtype:
+        raise ValueError(f"{op}: log_coeffs and log_values must share a dtype ({lc.dtype} vs {lv.dtype})")
+    _dtype_code(op, lc)
+    need = torch.is_grad_enabled() and (lc.requires_grad or lv.requires_grad)
+    h, _ = _log_scan_fwd(lc, lv, need)
+    return h
