@@ -111,6 +111,35 @@ int mgs_log_scan_bwd(const void* log_coeffs, const void* log_values, const void*
                      int64_t T, int64_t D, int dtype, void* workspace, size_t workspace_bytes,
                      void* stream);
 
+/* ------------------------------------------------------------------------ */
+/* matrix_affine_scan / matrix_scan: H_t = A_t H_{t-1} + B_t per block,
+ * A (B, T, n, k, k), Bm (B, T, n, k, v); returns Abar_t (running product,
+ * Abar_0 = I) and Bbar_t (the H_0 = 0 solution). matrix_scan is k = 2, v = 1
+ * with b (B, T, n, 2) viewed as (B, T, n, 2, 1).
+ * Replaces min_gru.py:1584 `matrix_affine_scan(A, Bm)` and min_gru.py:1513
+ * `matrix_scan(M, b)` (eager doubling, min_gru.py:1570-1581, 1647-1655), the
+ * Triton kernels triton_scans.py:629-700 / 823-959, ops affine_scan_fwd /
+ * affine_scan_bwd (triton_scans.py:1293, 1359) and the SCAN_IMPLS wrappers
+ * (triton_scans.py:2492-2563). k, v in {1, 2, 4, 8, 16} with k (k + v) <= 72
+ * use register-resident look-back kernels; any other 1 <= k, v <= 64 uses a
+ * sequential per-block kernel whose backward reads the saved outputs.       */
+
+size_t mgs_affine_scan_workspace_size(int64_t B, int64_t T, int64_t n, int k, int v, int dtype);
+/* 0 when the (k, v) uses the sequential kernels: then the backward needs
+ * Abar, Bbar (the saved forward outputs) instead of carries. */
+size_t mgs_affine_scan_carry_size(int64_t B, int64_t T, int64_t n, int k, int v, int dtype);
+
+int mgs_affine_scan_fwd(const void* A, const void* Bm, void* Abar, void* Bbar, void* carries,
+                        int64_t B, int64_t T, int64_t n, int k, int v, int dtype, void* workspace,
+                        size_t workspace_bytes, void* stream);
+
+/* Backward: (dA, dBm) of sum(Abar * gAbar) + sum(Bbar * gBbar). Abar/Bbar may
+ * be NULL when carries are used (register path). */
+int mgs_affine_scan_bwd(const void* A, const void* Bm, const void* Abar, const void* Bbar,
+                        const void* gAbar, const void* gBbar, const void* carries, void* dA,
+                        void* dBm, int64_t B, int64_t T, int64_t n, int k, int v, int dtype,
+                        void* workspace, size_t workspace_bytes, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -7,12 +7,21 @@ B200 kernels of ``libmingru_scan.so`` through its C ABI
 fallback: CPU tensors raise.
 """
 
-from .scan_ops import linear_scan, parallel_scan_log, raise_device_error, take_device_error
+from .scan_ops import (
+    linear_scan,
+    matrix_affine_scan,
+    matrix_scan,
+    parallel_scan_log,
+    raise_device_error,
+    take_device_error,
+)
 
 __version__ = "0.1.0"
 
 __all__ = [
     "linear_scan",
+    "matrix_affine_scan",
+    "matrix_scan",
     "parallel_scan_log",
     "raise_device_error",
     "take_device_error",

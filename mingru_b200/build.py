@@ -29,7 +29,7 @@ ARCH_FLAGS = ["-gencode", "arch=compute_100a,code=sm_100a"]
 NVCC_FLAGS = [
     "-O3",
     "-lineinfo",
-    "-std=c++17",
+    "-std=c++20",
     "--expt-relaxed-constexpr",
     "-Xcompiler",
     "-fPIC,-O3",

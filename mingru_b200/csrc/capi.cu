@@ -8,6 +8,7 @@ namespace mgs {
 // One sticky error word per translation unit; each kernel file exports its reader.
 unsigned take_error_linear(cudaStream_t s);
 unsigned take_error_log(cudaStream_t s);
+unsigned take_error_affine(cudaStream_t s);
 }  // namespace mgs
 
 extern "C" {
@@ -33,6 +34,7 @@ int mgs_take_device_error(void* stream) {
   unsigned bits = 0u;
   bits |= mgs::take_error_linear(s);
   bits |= mgs::take_error_log(s);
+  bits |= mgs::take_error_affine(s);
   return (int)bits;
 }
 

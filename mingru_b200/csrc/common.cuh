@@ -464,9 +464,14 @@ __device__ __forceinline__ void tma_prefetch_desc(const CUtensorMap* map) {
 }
 
 // Error-word helpers shared by the per-file launchers.
-#define MGS_CUDA_OK(expr)                          \
-  do {                                             \
-    if ((expr) != cudaSuccess) return MGS_LAUNCH_FAILED; \
+// On failure, clear the runtime's last-error state so the failure is
+// reported once, by this call, and does not leak into the next launch check.
+#define MGS_CUDA_OK(expr)              \
+  do {                                 \
+    if ((expr) != cudaSuccess) {       \
+      (void)cudaGetLastError();        \
+      return MGS_LAUNCH_FAILED;        \
+    }                                  \
   } while (0)
 
 inline bool aligned(const void* p, size_t a) {

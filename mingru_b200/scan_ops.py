@@ -297,3 +297,149 @@ def parallel_scan_log(log_coeffs: torch.Tensor, log_values: torch.Tensor) -> tor
     need = torch.is_grad_enabled() and (lc.requires_grad or lv.requires_grad)
     h, _ = _log_scan_fwd(lc, lv, need)
     return h
+
+
+# ================================================ matrix(_affine)_scan ==
+
+
+@torch.library.custom_op("mingru_b200::affine_scan_fwd", mutates_args=())
+def _affine_scan_fwd(
+    A: torch.Tensor, Bm: torch.Tensor, save_carries: bool
+) -> tuple[torch.Tensor, torch.Tensor, torch.Tensor]:
+    lib = _lib.load()
+    A, Bm = _dense(A), _dense(Bm)
+    Bn, T, n, k, _ = A.shape
+    v = Bm.shape[-1]
+    code = _dtype_code("matrix_affine_scan", A)
+    Abar, Bbar = torch.empty_like(A), torch.empty_like(Bm)
+    csz = lib.mgs_affine_scan_carry_size(Bn, T, n, k, v, code) if save_carries else 0
+    carries = torch.empty(csz // 4, dtype=torch.float32, device=A.device)
+    ws = _workspace(lib.mgs_affine_scan_workspace_size(Bn, T, n, k, v, code), A.device)
+    with torch.cuda.device(A.device):
+        st = lib.mgs_affine_scan_fwd(
+            _ptr(A), _ptr(Bm), _ptr(Abar), _ptr(Bbar), _ptr(carries) if csz else None,
+            Bn, T, n, k, v, code, _ptr(ws), ws.numel(), _stream(A),
+        )
+    _lib.check(st, "matrix_affine_scan forward")
+    return Abar, Bbar, carries
+
+
+@_affine_scan_fwd.register_fake
+def _(A, Bm, save_carries):
+    Bn, T, n, k, _ = A.shape
+    v = Bm.shape[-1]
+    csz = _lib.load().mgs_affine_scan_carry_size(Bn, T, n, k, v, _dtype_code("matrix_affine_scan", A))
+    nfl = csz // 4 if save_carries else 0
+    return torch.empty_like(A), torch.empty_like(Bm), A.new_empty((nfl,), dtype=torch.float32)
+
+
+@torch.library.custom_op("mingru_b200::affine_scan_bwd", mutates_args=())
+def _affine_scan_bwd(
+    A: torch.Tensor, Bm: torch.Tensor, Abar: torch.Tensor, Bbar: torch.Tensor,
+    gAbar: torch.Tensor, gBbar: torch.Tensor, carries: torch.Tensor,
+) -> tuple[torch.Tensor, torch.Tensor]:
+    lib = _lib.load()
+    A, Bm, Abar, Bbar = (_dense(x) for x in (A, Bm, Abar, Bbar))
+    gA, gB = _dense(gAbar.to(A.dtype)), _dense(gBbar.to(A.dtype))
+    Bn, T, n, k, _ = A.shape
+    v = Bm.shape[-1]
+    code = _dtype_code("matrix_affine_scan", A)
+    csz = lib.mgs_affine_scan_carry_size(Bn, T, n, k, v, code)
+    if carries.numel() * 4 < csz:
+        raise RuntimeError("matrix_affine_scan backward: forward carries were not saved")
+    dA, dB = torch.empty_like(A), torch.empty_like(Bm)
+    ws = _workspace(lib.mgs_affine_scan_workspace_size(Bn, T, n, k, v, code), A.device)
+    with torch.cuda.device(A.device):
+        st = lib.mgs_affine_scan_bwd(
+            _ptr(A), _ptr(Bm), _ptr(Abar), _ptr(Bbar), _ptr(gA), _ptr(gB),
+            _ptr(carries) if csz else None, _ptr(dA), _ptr(dB),
+            Bn, T, n, k, v, code, _ptr(ws), ws.numel(), _stream(A),
+        )
+    _lib.check(st, "matrix_affine_scan backward")
+    return dA, dB
+
+
+@_affine_scan_bwd.register_fake
+def _(A, Bm, Abar, Bbar, gAbar, gBbar, carries):
+    return torch.empty_like(A), torch.empty_like(Bm)
+
+
+def _affine_setup(ctx, inputs, output):
+    A, Bm, _ = inputs
+    Abar, Bbar, carries = output
+    ctx.save_for_backward(A, Bm, Abar, Bbar, carries)
+    ctx.mark_non_differentiable(carries)
+    ctx.set_materialize_grads(False)
+
+
+def _affine_backward(ctx, gAbar, gBbar, _gcarries):
+    if torch.is_grad_enabled():
+        raise RuntimeError(
+            "matrix_affine_scan does not support second-order autograd (create_graph=True)"
+        )
+    A, Bm, Abar, Bbar, carries = ctx.saved_tensors
+    if gAbar is None and gBbar is None:
+        return None, None, None
+    if gAbar is None:
+        gAbar = torch.zeros_like(A)
+    if gBbar is None:
+        gBbar = torch.zeros_like(Bm)
+    dA, dB = _affine_scan_bwd(A, Bm, Abar, Bbar, gAbar, gBbar, carries)
+    return dA, dB, None
+
+
+torch.library.register_autograd(
+    "mingru_b200::affine_scan_fwd", _affine_backward, setup_context=_affine_setup
+)
+
+_MAX_KV = 64
+
+
+def matrix_affine_scan(A: torch.Tensor, Bm: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
+    """Scan ``H_t = A_t H_{t-1} + B_t`` per block; returns ``(Abar, Bbar)``.
+
+    ``A`` ``(B, T, n, k, k)`` and ``Bm`` ``(B, T, n, k, v)`` CUDA tensors of one
+    dtype. ``Abar_t`` is the running product ``A_t ... A_1`` and ``Bbar_t``
+    the ``H_0 = 0`` solution, so ``H_t = Abar_t H_0 + Bbar_t``. Same contract
+    as the reference's ``min_gru.matrix_affine_scan`` (``min_gru.py:1584-1655``).
+    """
+    op = "matrix_affine_scan"
+    if A.ndim != 5 or Bm.ndim != 5:
+        raise ValueError(
+            f"{op}: need 5-D (B, T, n, k, k) A and (B, T, n, k, v) Bm "
+            f"(got A={tuple(A.shape)}, Bm={tuple(Bm.shape)})"
+        )
+    k, v = A.shape[-1], Bm.shape[-1]
+    if A.shape[-2] != k or Bm.shape[-2] != k or A.shape[:3] != Bm.shape[:3]:
+        raise ValueError(
+            f"{op}: need a square A (A.shape[-2:] == (k, k)), Bm with k rows and A/Bm sharing "
+            f"the (B, T, n) grid (got A={tuple(A.shape)}, Bm={tuple(Bm.shape)})"
+        )
+    if not (1 <= k <= _MAX_KV and 1 <= v <= _MAX_KV):
+        raise ValueError(f"{op}: k and v must be in [1, {_MAX_KV}] (got k={k}, v={v})")
+    _require_cuda(op, A, Bm)
+    if A.dtype != Bm.dtype:
+        raise ValueError(f"{op}: A and Bm must share a dtype ({A.dtype} vs {Bm.dtype})")
+    _dtype_code(op, A)
+    need = torch.is_grad_enabled() and (A.requires_grad or Bm.requires_grad)
+    Abar, Bbar, _ = _affine_scan_fwd(A, Bm, need)
+    return Abar, Bbar
+
+
+def matrix_scan(M: torch.Tensor, b: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
+    """2x2-block scan ``h_t = M_t h_{t-1} + b_t``; returns ``(A, Bc)``.
+
+    ``M`` ``(B, T, n, 2, 2)``, ``b`` ``(B, T, n, 2)``; ``A`` is the running
+    product and ``Bc`` the ``h_0 = 0`` solution. Same contract as the
+    reference's ``min_gru.matrix_scan`` (``min_gru.py:1513-1581``); it is the
+    ``k = 2, v = 1`` case of :func:`matrix_affine_scan`.
+    """
+    op = "matrix_scan"
+    if M.ndim != 5 or b.ndim != 4 or M.shape[-2:] != (2, 2) or b.shape[-1] != 2 \
+            or M.shape[:3] != b.shape[:3]:
+        raise ValueError(
+            f"{op}: need (B, T, n, 2, 2) M and (B, T, n, 2) b sharing the (B, T, n) grid "
+            f"(got M={tuple(M.shape)}, b={tuple(b.shape)})"
+        )
+    Abar, Bbar = matrix_affine_scan(M, b.unsqueeze(-1))
+    return Abar, Bbar.squeeze(-1)
