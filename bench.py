@@ -19,6 +19,7 @@ from __future__ import annotations
 
 import argparse
 import json
+import math
 import os
 import statistics
 import subprocess
@@ -57,111 +58,235 @@ def load_traffic() -> dict[str, float]:
 # ------------------------------------------------------------ workloads --
 
 
-class LinearScanWorkload:
-    """SignedMinGRU linear_scan fwd+bwd.
+class ScanWorkload:
+    """One BASELINE configuration: seeded inputs, one fwd+bwd step through the
+    public op + autograd, the algorithmic bytes of each kernel, and the
+    CPU-oracle step used for the CPU baseline."""
+
+    name = "?"
+    metric_elems_doc = "B*T*D"
+    kernels = {"fwd": "?", "bwd": "?"}
+    launches_per_step = 2  # one forward kernel + one backward kernel
+
+    def __init__(self, dtype=torch.float32):
+        self.dtype = dtype
+        self.esize = torch.finfo(dtype).bits // 8
+
+    # --- to define per workload
+    def make_host(self, rows: int, seed: int):  # -> (inputs, cotangents), fp32 CPU tensors
+        raise NotImplementedError
+
+    def forward(self, *inputs):
+        raise NotImplementedError
+
+    def cpu_step(self, sample):
+        raise NotImplementedError
+
+    # --- shared plumbing
+    @property
+    def elems(self) -> int:
+        return self.B * self.T * self.D
+
+    def host_inputs(self, rank: int):
+        ins, cots = self.make_host(self.B, seed=rank)
+        return [x.to(self.dtype) for x in ins], [c.to(self.dtype) for c in cots]
+
+    def device_setup(self, host, dev):
+        ins, cots = host
+        return {"ins": [x.to(dev).requires_grad_(True) for x in ins],
+                "cots": [c.to(dev) for c in cots]}
+
+    def step(self, st, events=None):
+        if events:
+            events[0].record()
+        outs = self.forward(*st["ins"])
+        if events:
+            events[1].record()
+        grads = torch.autograd.grad(outs, st["ins"], st["cots"])
+        if events:
+            events[2].record()
+        return outs, grads
+
+    def e2e_setup(self, host, dev):
+        ins, cots = host
+        pins = [x.pin_memory() for x in ins]
+        pcots = [c.pin_memory() for c in cots]
+        outs = [torch.empty_like(c).pin_memory() for c in cots] + [torch.empty_like(x).pin_memory() for x in ins]
+        return {"ins": pins, "cots": pcots, "out": outs, "dev": dev}
+
+    def e2e_step(self, st):
+        dev = st["dev"]
+        ins = [x.to(dev, non_blocking=True).requires_grad_(True) for x in st["ins"]]
+        cots = [c.to(dev, non_blocking=True) for c in st["cots"]]
+        outs = self.forward(*ins)
+        grads = torch.autograd.grad(outs, ins, cots)
+        for o, r in zip(st["out"], list(outs) + list(grads)):
+            o.copy_(r.detach(), non_blocking=True)
+
+    def _bytes(self, tensors) -> int:
+        return sum(t.numel() for t in tensors) * self.esize
+
+    @property
+    def h2d_bytes(self) -> int:
+        ins, cots = self._shape_probe
+        return self._bytes(ins) + self._bytes(cots)
+
+    @property
+    def d2h_bytes(self) -> int:
+        ins, cots = self._shape_probe
+        return self._bytes(cots) + self._bytes(ins)  # outputs (shaped like cots) + grads
+
+    @property
+    def _shape_probe(self):
+        if not hasattr(self, "_probe"):
+            ins, cots = self.make_host(self.B, seed=0)
+            self._probe = ([torch.empty(x.shape, device="meta") for x in ins],
+                           [torch.empty(c.shape, device="meta") for c in cots])
+        return self._probe
+
+    def cpu_sample(self, rows: int):
+        ins, cots = self.make_host(rows, seed=0)
+        return [x.numpy() for x in ins], [c.numpy() for c in cots]
+
+    def config(self, n_gpus: int) -> dict:
+        return {
+            "workload": self.workload,
+            "B_per_gpu": self.B,
+            "global_batch": self.B * n_gpus,
+            "T": self.T,
+            "D": self.D,
+            "elem": self.metric_elems_doc,
+            "input_dtype": str(self.dtype).replace("torch.", ""),
+            "l2": f"inputs {self.elems * self.esize / 1e6:.0f} MB per tensor vs 126 MB L2; no flush",
+            "parallelism": f"batch-sharded x{n_gpus}, no collective",
+        }
+
+
+class LinearScanWorkload(ScanWorkload):
+    """SignedMinGRU linear_scan fwd+bwd, B=16, T=4096, D=1024.
 
     a = tanh(N(0,1)), b ~ N(0,1) (seed 0); upstream grads gBc ~ N(0,1)
     (seed 1234, the reference parity harness's cotangent seed) and gA = 0
     (h_0 = 0 in SignedMinGRU, so dL/dA = dL/dh * h_0 = 0).
     """
 
-    def __init__(self, B=16, T=4096, D=1024, dtype=torch.float32, name="cfg2"):
-        self.B, self.T, self.D, self.dtype, self.name = B, T, D, dtype, name
-        self.esize = torch.finfo(dtype).bits // 8
-        # algorithmic bytes per element: fwd reads a, b and writes A, Bc;
-        # bwd reads a, b, gA, gBc and writes da, db.
-        self.fwd_bytes = 4 * self.esize
-        self.bwd_bytes = 6 * self.esize
-        self.kernels = {"fwd": "linear_scan_fwd", "bwd": "linear_scan_bwd"}
+    kernels = {"fwd": "linear_scan_fwd", "bwd": "linear_scan_bwd"}
 
-    @property
-    def elems(self) -> int:
-        return self.B * self.T * self.D
+    def __init__(self, dtype=torch.float32, name="cfg2", B=16, T=4096, D=1024):
+        super().__init__(dtype)
+        self.B, self.T, self.D, self.name = B, T, D, name
+        self.fwd_bytes = 4 * self.esize  # a, b read; A, Bc written
+        self.bwd_bytes = 6 * self.esize  # a, b, gA, gBc read; da, db written
+        self.workload = ("linear_scan fwd+bwd (SignedMinGRU scan, BASELINE config 2"
+                         + ("" if dtype == torch.float32 else ", bf16 inputs / fp32 state") + ")")
 
-    def config(self, n_gpus: int) -> dict:
-        return {
-            "workload": f"linear_scan fwd+bwd (SignedMinGRU scan, BASELINE config 2"
-            f"{'' if self.dtype == torch.float32 else ', bf16 inputs / fp32 state'})",
-            "B_per_gpu": self.B,
-            "global_batch": self.B * n_gpus,
-            "T": self.T,
-            "D": self.D,
-            "input_dtype": str(self.dtype).replace("torch.", ""),
-            "l2": f"inputs {self.elems * self.esize / 1e6:.0f} MB each > 126 MB L2; no flush",
-            "parallelism": f"batch-sharded x{n_gpus}, no collective",
-        }
+    def make_host(self, rows, seed):
+        g = torch.Generator().manual_seed(seed)
+        a = torch.tanh(torch.randn(rows, self.T, self.D, generator=g))
+        b = torch.randn(rows, self.T, self.D, generator=g)
+        gB = torch.randn(rows, self.T, self.D, generator=torch.Generator().manual_seed(1234 + seed))
+        return [a, b], [torch.zeros_like(a), gB]
 
-    def host_inputs(self, rank: int):
-        g = torch.Generator().manual_seed(rank)
-        a = torch.tanh(torch.randn(self.B, self.T, self.D, generator=g))
-        b = torch.randn(self.B, self.T, self.D, generator=g)
-        gB = torch.randn(self.B, self.T, self.D, generator=torch.Generator().manual_seed(1234 + rank))
-        gA = torch.zeros(self.B, self.T, self.D)
-        return [x.to(self.dtype) for x in (a, b, gA, gB)]
-
-    def device_setup(self, host, dev):
-        a, b, gA, gB = (x.to(dev) for x in host)
-        return {"a": a.requires_grad_(True), "b": b.requires_grad_(True), "gA": gA, "gB": gB}
-
-    def step(self, st, events=None):
+    def forward(self, a, b):
         import mingru_b200 as mb
 
-        if events:
-            events[0].record()
-        A, Bc = mb.linear_scan(st["a"], st["b"])
-        if events:
-            events[1].record()
-        da, db = torch.autograd.grad((A, Bc), (st["a"], st["b"]), (st["gA"], st["gB"]))
-        if events:
-            events[2].record()
-        return A, Bc, da, db
-
-    launches_per_step = 2  # linear_scan fwd kernel + bwd kernel
-
-    def e2e_setup(self, host, dev):
-        pinned = [x.pin_memory() for x in host]
-        outs = [torch.empty_like(pinned[0]).pin_memory() for _ in range(4)]
-        return {"host": pinned, "out": outs, "dev": dev}
-
-    def e2e_step(self, st):
-        import mingru_b200 as mb
-
-        dev = st["dev"]
-        a, b, gA, gB = (x.to(dev, non_blocking=True) for x in st["host"])
-        a.requires_grad_(True)
-        b.requires_grad_(True)
-        A, Bc = mb.linear_scan(a, b)
-        da, db = torch.autograd.grad((A, Bc), (a, b), (gA, gB))
-        for o, r in zip(st["out"], (A, Bc, da, db)):
-            o.copy_(r.detach(), non_blocking=True)
-
-    @property
-    def h2d_bytes(self) -> int:
-        return 4 * self.elems * self.esize
-
-    @property
-    def d2h_bytes(self) -> int:
-        return 4 * self.elems * self.esize
-
-    # --- CPU baseline: the oracle port of the reference algorithm (fp32 C, OpenMP)
-    def cpu_sample(self, rows: int):
-        g = torch.Generator().manual_seed(0)
-        a = torch.tanh(torch.randn(rows, self.T, self.D, generator=g)).numpy()
-        b = torch.randn(rows, self.T, self.D, generator=g).numpy()
-        gB = torch.randn(rows, self.T, self.D, generator=g).numpy()
-        return a, b, np.zeros_like(a), gB
+        return mb.linear_scan(a, b)
 
     def cpu_step(self, sample):
         from oracle import oracle
 
-        a, b, gA, gB = sample
+        (a, b), (gA, gB) = sample
         A, Bc = oracle.linear_scan(a, b, dtype=np.float32)
         oracle.linear_scan_bwd(a, A, Bc, gA, gB, dtype=np.float32)
 
 
+class LogScanWorkload(ScanWorkload):
+    """MinGRU parallel_scan_log fwd+bwd, B=8, T=1024, D=256.
+
+    k, x ~ N(0,1); log_coeffs = -softplus(k); log_values = [log h0,
+    -softplus(-k) + log_g(x)] with h0 = 0 taken as log(float32 tiny) (a finite
+    numerically-zero state, as MinGRU clamps it); grad_h ~ N(0,1) (seed 1234).
+    """
+
+    kernels = {"fwd": "log_scan_fwd", "bwd": "log_scan_bwd"}
+    workload = "parallel_scan_log fwd+bwd (MinGRU scan, BASELINE config 1)"
+
+    def __init__(self, dtype=torch.float32, name="cfg1", B=8, T=1024, D=256):
+        super().__init__(dtype)
+        self.B, self.T, self.D, self.name = B, T, D, name
+        self.fwd_bytes = 3 * self.esize  # lc, lv read; h written
+        self.bwd_bytes = 5 * self.esize  # lc, lv, grad_h read; dlc, dlv written
+
+    def make_host(self, rows, seed):
+        g = torch.Generator().manual_seed(seed)
+        k = torch.randn(rows, self.T, self.D, generator=g)
+        x = torch.randn(rows, self.T, self.D, generator=g)
+        log_g = torch.where(x >= 0, (x.clamp_min(0) + 0.5).log(), -torch.nn.functional.softplus(-x))
+        lc = -torch.nn.functional.softplus(k)
+        lh0 = torch.full((rows, 1, self.D), math.log(torch.finfo(torch.float32).tiny))
+        lv = torch.cat([lh0, -torch.nn.functional.softplus(-k) + log_g], 1)
+        gh = torch.randn(rows, self.T, self.D, generator=torch.Generator().manual_seed(1234 + seed))
+        return [lc, lv], [gh]
+
+    def forward(self, lc, lv):
+        import mingru_b200 as mb
+
+        return (mb.parallel_scan_log(lc, lv),)
+
+    def cpu_step(self, sample):
+        from oracle import oracle
+
+        (lc, lv), (gh,) = sample
+        oracle.parallel_scan_log(lc, lv, dtype=np.float32)
+        oracle.parallel_scan_log_bwd(lc, lv, gh, dtype=np.float32)
+
+
+class MatrixScanWorkload(ScanWorkload):
+    """RotationMinGRU matrix_scan (2x2 blocks) fwd+bwd,
+    B=16, T=2048, D=512 (n=256 blocks): M = sigmoid(N(0,1)) * R(theta),
+    theta ~ U(-pi, pi), b ~ N(0,1); grad_Bc ~ N(0,1), grad_A = 0 (h0 fixed)."""
+
+    kernels = {"fwd": "affine_scan_fwd", "bwd": "affine_scan_bwd"}
+    workload = "matrix_scan 2x2 fwd+bwd (RotationMinGRU scan, BASELINE config 3)"
+    metric_elems_doc = "B*T*D with D = 2n"
+
+    def __init__(self, dtype=torch.float32, name="cfg3", B=16, T=2048, D=512):
+        super().__init__(dtype)
+        self.B, self.T, self.D, self.name = B, T, D, name
+        # per element (half a block): fwd reads M (2) + b (1), writes A (2) + Bc (1)
+        self.fwd_bytes = 6 * self.esize
+        # bwd reads M, b, gA, gBc (6) and writes dM, db (3)
+        self.bwd_bytes = 9 * self.esize
+
+    def make_host(self, rows, seed):
+        n = self.D // 2
+        g = torch.Generator().manual_seed(seed)
+        th = (torch.rand(rows, self.T, n, generator=g) * 2 - 1) * math.pi
+        sc = torch.sigmoid(torch.randn(rows, self.T, n, generator=g))
+        c, sn = torch.cos(th), torch.sin(th)
+        M = sc[..., None, None] * torch.stack([torch.stack([c, -sn], -1), torch.stack([sn, c], -1)], -2)
+        b = torch.randn(rows, self.T, n, 2, generator=g)
+        gB = torch.randn(rows, self.T, n, 2, generator=torch.Generator().manual_seed(1234 + seed))
+        return [M, b], [torch.zeros_like(M), gB]
+
+    def forward(self, M, b):
+        import mingru_b200 as mb
+
+        return mb.matrix_scan(M, b)
+
+    def cpu_step(self, sample):
+        from oracle import oracle
+
+        (M, b), (gA, gB) = sample
+        A, Bc = oracle.matrix_scan(M, b, dtype=np.float32)
+        oracle.matrix_scan_bwd(M, A, Bc, gA, gB, dtype=np.float32)
+
+
 WORKLOADS = {
+    "cfg1": lambda: LogScanWorkload(),
     "cfg2": lambda: LinearScanWorkload(),
     "cfg2-bf16": lambda: LinearScanWorkload(dtype=torch.bfloat16, name="cfg2-bf16"),
+    "cfg3": lambda: MatrixScanWorkload(),
 }
 
 
@@ -286,6 +411,7 @@ def time_cpu_baseline(w, target_s: float = 12.0) -> dict:
     os.environ.setdefault("OMP_NUM_THREADS", str(threads))
     rows = 1
     sample = w.cpu_sample(rows)
+    w.cpu_step(sample)  # first call also loads the oracle library
     t0 = time.perf_counter()
     w.cpu_step(sample)
     one = time.perf_counter() - t0
@@ -302,6 +428,7 @@ def time_cpu_baseline(w, target_s: float = 12.0) -> dict:
     return {"value": elems / dt / 1e9, "unit": "Gelem/s", "cores": threads, "kind": "port",
             "sample": f"{rows} of {w.B} batch rows (T={w.T}, D={w.D}) fwd+bwd, fp32 C oracle "
                       f"(OpenMP {threads} threads), best of 2 after 1 warm-up"}
+
 
 
 def run_reference(args, w) -> None:
@@ -437,7 +564,7 @@ def run_ours(args, w) -> None:
             "unit": "Gelem/s",
             "h2d_bytes_per_step": w.h2d_bytes,
             "d2h_bytes_per_step": w.d2h_bytes,
-            "path": "mingru_b200.linear_scan + autograd (C ABI) from pinned host buffers",
+            "path": "public op + autograd (C ABI) from pinned host buffers",
         },
         "gpu_launches": w.launches_per_step * args.steps,
         "clocks": clk.summary(),

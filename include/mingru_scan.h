@@ -140,6 +140,46 @@ int mgs_affine_scan_bwd(const void* A, const void* Bm, const void* Abar, const v
                         void* dBm, int64_t B, int64_t T, int64_t n, int k, int v, int dtype,
                         void* workspace, size_t workspace_bytes, void* stream);
 
+/* ------------------------------------------------------------------------ */
+/* Angle-fused Givens / rotation scan (GivensMinGRU, RotationMinGRU).
+ * Per (b, block): [v[1] *= scale], R rounds of plane rotations
+ * v'[p] = cos v[p] + sgn[r,p] sin v[perm[r,p]] with angle
+ * theta[b,t,blk,r,p2p[r,p]], [v *= gamma], v += b; h_t = v.
+ * Layouts: theta (B, T, n, R, k/2); scale, gamma (B, T, n); b, h (B, T, n, k);
+ * h0 (B, n, k); perm, p2p int32 (R, k); sgn float32 (R, k) -- device memory.
+ * Replaces angle_scan_impl (triton_scans.py:1743-1812), the ops angle_scan_fwd /
+ * angle_scan_bwd (triton_scans.py:1579-1704) and their Triton kernels
+ * (triton_scans.py:1038-1291), called from GivensMinGRU / RotationMinGRU
+ * (min_gru.py:2727-2774, 2269-2314).
+ * `brickwall` != 0 states that perm/sgn/p2p are the brick-wall layout both
+ * mixers build (round r pairs (i, i+1 mod k), i = r%2, r%2+2, ...; sgn -1 on
+ * i, +1 on i+1; p2p = plane index): k in {2, 4, 8} with R <= 4 then runs the
+ * register look-back kernels, which derive the planes from (k, r) and do not
+ * read the metadata. Otherwise (or brickwall == 0) a sequential per-block
+ * kernel reads the metadata; its backward reads the stored states `h`.    */
+
+size_t mgs_angle_scan_workspace_size(int64_t B, int64_t T, int64_t n, int R, int k,
+                                     int brickwall, int dtype);
+/* 0 when the sequential kernels are used (the backward then needs `h`). */
+size_t mgs_angle_scan_carry_size(int64_t B, int64_t T, int64_t n, int R, int k, int brickwall,
+                                 int dtype);
+
+int mgs_angle_scan_fwd(const void* theta, const void* scale, const void* gamma, const void* b,
+                       const void* h0, const int32_t* perm, const float* sgn, const int32_t* p2p,
+                       void* h, void* carries, int64_t B, int64_t T, int64_t n, int R, int k,
+                       int has_scale, int has_decay, int brickwall, int dtype, void* workspace,
+                       size_t workspace_bytes, void* stream);
+
+/* Backward: (dtheta, dscale, dgamma, db, dh0) of sum(h * grad_h). dscale /
+ * dgamma are written only when has_scale / has_decay (the caller zeroes them
+ * otherwise). `h` may be NULL on the register path (it uses `carries`). */
+int mgs_angle_scan_bwd(const void* theta, const void* scale, const void* gamma, const void* b,
+                       const void* h0, const int32_t* perm, const float* sgn, const int32_t* p2p,
+                       const void* h, const void* grad_h, const void* carries, void* dtheta,
+                       void* dscale, void* dgamma, void* db, void* dh0, int64_t B, int64_t T,
+                       int64_t n, int R, int k, int has_scale, int has_decay, int brickwall,
+                       int dtype, void* workspace, size_t workspace_bytes, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -8,6 +8,8 @@ fallback: CPU tensors raise.
 """
 
 from .scan_ops import (
+    angle_scan_impl,
+    brickwall_meta,
     linear_scan,
     matrix_affine_scan,
     matrix_scan,
@@ -19,6 +21,8 @@ from .scan_ops import (
 __version__ = "0.1.0"
 
 __all__ = [
+    "angle_scan_impl",
+    "brickwall_meta",
     "linear_scan",
     "matrix_affine_scan",
     "matrix_scan",

@@ -46,6 +46,16 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
         _int, [_p, _p, _p, _p, _p, _i64, _i64, _i64, _int, _int, _int, _p, _sz, _p]),
     "mgs_affine_scan_bwd": (
         _int, [_p, _p, _p, _p, _p, _p, _p, _p, _p, _i64, _i64, _i64, _int, _int, _int, _p, _sz, _p]),
+    "mgs_angle_scan_workspace_size": (_sz, [_i64, _i64, _i64, _int, _int, _int, _int]),
+    "mgs_angle_scan_carry_size": (_sz, [_i64, _i64, _i64, _int, _int, _int, _int]),
+    "mgs_angle_scan_fwd": (
+        _int,
+        [_p, _p, _p, _p, _p, _p, _p, _p, _p, _p, _i64, _i64, _i64, _int, _int, _int, _int, _int,
+         _int, _p, _sz, _p]),
+    "mgs_angle_scan_bwd": (
+        _int,
+        [_p, _p, _p, _p, _p, _p, _p, _p, _p, _p, _p, _p, _p, _p, _p, _p, _i64, _i64, _i64, _int,
+         _int, _int, _int, _int, _int, _p, _sz, _p]),
 }
 
 _lock = threading.Lock()

@@ -128,17 +128,21 @@ struct FwdMonoid {
 #pragma unroll
       for (int j = 0; j < W; ++j) x[i * W + j] = (i == j) ? 1.f : 0.f;
   }
-  // earlier e then later l: [Pl Pe | Pl Qe + Ql]
+  // earlier e then later l: [Pl Pe | Pl Qe + Ql]; column by column, so o may alias e.
   __device__ static void combine(const float (&e)[NF], const float (&l)[NF], float (&o)[NF]) {
 #pragma unroll
-    for (int i = 0; i < K; ++i)
+    for (int j = 0; j < W; ++j) {
+      float col[K];
 #pragma unroll
-      for (int j = 0; j < W; ++j) {
+      for (int i = 0; i < K; ++i) {
         float s = j >= K ? l[i * W + j] : 0.f;
 #pragma unroll
         for (int q = 0; q < K; ++q) s = fmaf(l[i * W + q], e[q * W + j], s);
-        o[i * W + j] = s;
+        col[i] = s;
       }
+#pragma unroll
+      for (int i = 0; i < K; ++i) o[i * W + j] = col[i];
+    }
   }
 };
 
@@ -156,34 +160,41 @@ struct RevMonoid {
 #pragma unroll
     for (int i = 0; i < K * W; ++i) x[K * K + i] = 0.f;
   }
-  // earlier e then later l: (Pl Pe, Pl Qe + Ql)
+  // earlier e then later l: (Pl Pe, Pl Qe + Ql); column by column, so o may alias e.
   __device__ static void combine(const float (&e)[NF], const float (&l)[NF], float (&o)[NF]) {
 #pragma unroll
-    for (int i = 0; i < K; ++i) {
+    for (int j = 0; j < K; ++j) {
+      float col[K];
 #pragma unroll
-      for (int j = 0; j < K; ++j) {
+      for (int i = 0; i < K; ++i) {
         float s = 0.f;
 #pragma unroll
         for (int q = 0; q < K; ++q) s = fmaf(l[i * K + q], e[q * K + j], s);
-        o[i * K + j] = s;
+        col[i] = s;
       }
 #pragma unroll
-      for (int j = 0; j < W; ++j) {
+      for (int i = 0; i < K; ++i) o[i * K + j] = col[i];
+    }
+#pragma unroll
+    for (int j = 0; j < W; ++j) {
+      float col[K];
+#pragma unroll
+      for (int i = 0; i < K; ++i) {
         float s = l[K * K + i * W + j];
 #pragma unroll
         for (int q = 0; q < K; ++q) s = fmaf(l[i * K + q], e[K * K + q * W + j], s);
-        o[K * K + i * W + j] = s;
+        col[i] = s;
       }
+#pragma unroll
+      for (int i = 0; i < K; ++i) o[K * K + i * W + j] = col[i];
     }
   }
 };
 
+// acc <- acc then later (the monoids' combine may write over its earlier operand).
 template <class M, int NF>
 __device__ __forceinline__ void combine_into(float (&acc)[NF], const float (&later)[NF]) {
-  float tmp[NF];
-  M::combine(acc, later, tmp);
-#pragma unroll
-  for (int f = 0; f < NF; ++f) acc[f] = tmp[f];
+  M::combine(acc, later, acc);
 }
 
 // Reverse step on the adjoint aggregate: Q <- A^T (g + Q), P <- A^T P.

@@ -9,6 +9,7 @@ namespace mgs {
 unsigned take_error_linear(cudaStream_t s);
 unsigned take_error_log(cudaStream_t s);
 unsigned take_error_affine(cudaStream_t s);
+unsigned take_error_angle(cudaStream_t s);
 }  // namespace mgs
 
 extern "C" {
@@ -35,6 +36,7 @@ int mgs_take_device_error(void* stream) {
   bits |= mgs::take_error_linear(s);
   bits |= mgs::take_error_log(s);
   bits |= mgs::take_error_affine(s);
+  bits |= mgs::take_error_angle(s);
   return (int)bits;
 }
 

@@ -205,6 +205,7 @@ __device__ __forceinline__ unsigned lb_wait(const Lookback& lb, long long tile) 
 // Decoupled look-back run by one full warp. `Monoid` supplies
 //   static void identity(float (&x)[NF]);
 //   static void combine(const float (&earlier)[NF], const float (&later)[NF], float (&out)[NF]);
+// where `out` may alias `earlier` (never `later`).
 // `tile` is the tile's position in processing order, `stride` the distance to
 // its predecessor in the same strip, `pos` its index along the strip (0 = the
 // first segment: no predecessor). On return `excl` holds the composition of
@@ -295,12 +296,12 @@ __device__ __forceinline__ void warp_lookback_win(const Lookback& lb, long long 
     for (int i = 0; i <= last; ++i) {
       const unsigned fi = __shfl_sync(0xffffffffu, f, i);
       const float* src = (fi == kFlagIncl ? lb.incl : lb.agg) + (size_t)(base - (long long)i * stride) * NF * 32;
-      float e[NF], tmp[NF];
+      float e[NF];
 #pragma unroll
       for (int q = 0; q < NF; ++q) e[q] = __ldcg(src + q * 32 + lane);
-      Monoid::combine(e, run, tmp);
+      Monoid::combine(e, run, e);  // combine may write over its earlier operand
 #pragma unroll
-      for (int q = 0; q < NF; ++q) run[q] = tmp[q];
+      for (int q = 0; q < NF; ++q) run[q] = e[q];
     }
     const unsigned flast = __shfl_sync(0xffffffffu, f, last);
     if (flast == kFlagIncl) break;
@@ -312,6 +313,87 @@ __device__ __forceinline__ void warp_lookback_win(const Lookback& lb, long long 
   float inc[NF];
   Monoid::combine(excl, agg, inc);
   lb_publish<NF>(lb, tile, kFlagIncl, inc);
+}
+
+// Same look-back for large elements: the tile aggregate is read from shared
+// memory (agg_s[NF][32]) and the exclusive prefix is written back to shared
+// memory (excl_s[NF][32]), so only two NF-float elements are live in
+// registers at any time (the k x (k+1) maps of the block scans are 72 floats
+// at k = 8).
+template <class Monoid, int NF>
+__device__ __forceinline__ void warp_lookback_win_smem(const Lookback& lb, long long tile,
+                                                       long long stride, long long pos,
+                                                       const float (*agg_s)[32],
+                                                       float (*excl_s)[32]) {
+  const int lane = threadIdx.x & 31;
+  float run[NF];
+#pragma unroll
+  for (int q = 0; q < NF; ++q) run[q] = agg_s[q][lane];
+  if (pos == 0) {
+    lb_publish<NF>(lb, tile, kFlagIncl, run);
+    Monoid::identity(run);
+#pragma unroll
+    for (int q = 0; q < NF; ++q) excl_s[q][lane] = run[q];
+    return;
+  }
+  lb_publish<NF>(lb, tile, kFlagAgg, run);
+  Monoid::identity(run);
+  long long remaining = pos;
+  long long base = tile - stride;
+  while (remaining > 0) {
+    const int nwin = remaining < 32 ? (int)remaining : 32;
+    const bool valid = lane < nwin;
+    const unsigned* fp = lb.flags + (valid ? base - (long long)lane * stride : 0);
+    unsigned f = valid ? ld_acquire_u32(fp) : kFlagIncl;
+    int last;
+    long long it = 0;
+    while (true) {
+      const unsigned im = __ballot_sync(0xffffffffu, valid && f == kFlagIncl);
+      last = im ? (__ffs(im) - 1) : nwin - 1;
+      const bool need = lane <= last;
+      const unsigned em = __ballot_sync(0xffffffffu, need && f == kFlagEmpty);
+      if (em == 0u) break;
+      if (++it > kSpinLimit) {
+        if (lane == 0) {
+          atomicOr(lb.err, kErrTimeout);
+          atomicOr(&g_sticky_err, kErrTimeout);
+        }
+        if (f == kFlagEmpty) f = kFlagIncl;
+        continue;
+      }
+      if ((it & 255) == 0 && ld_relaxed_u32(lb.err) != 0u && f == kFlagEmpty) f = kFlagIncl;
+      if (need && f == kFlagEmpty) {
+        __nanosleep(32);
+        f = ld_acquire_u32(fp);
+      }
+    }
+    __syncwarp();
+#pragma unroll 1
+    for (int i = 0; i <= last; ++i) {
+      const unsigned fi = __shfl_sync(0xffffffffu, f, i);
+      const float* src = (fi == kFlagIncl ? lb.incl : lb.agg) +
+                         (size_t)(base - (long long)i * stride) * NF * 32;
+      float e[NF];
+#pragma unroll
+      for (int q = 0; q < NF; ++q) e[q] = __ldcg(src + q * 32 + lane);
+      Monoid::combine(e, run, e);
+#pragma unroll
+      for (int q = 0; q < NF; ++q) run[q] = e[q];
+    }
+    const unsigned flast = __shfl_sync(0xffffffffu, f, last);
+    if (flast == kFlagIncl) break;
+    remaining -= nwin;
+    base -= (long long)nwin * stride;
+  }
+#pragma unroll
+  for (int q = 0; q < NF; ++q) excl_s[q][lane] = run[q];
+  {
+    float a[NF];
+#pragma unroll
+    for (int q = 0; q < NF; ++q) a[q] = agg_s[q][lane];
+    Monoid::combine(run, a, run);
+  }
+  lb_publish<NF>(lb, tile, kFlagIncl, run);
 }
 
 // ------------------------------------------------- TMA bulk copy + mbarrier --

@@ -125,12 +125,10 @@ struct RevMonoid {
   }
 };
 
+// acc <- acc then later (the monoids' combine may write over its earlier operand).
 template <class M, int NF>
 __device__ __forceinline__ void combine_into(float (&acc)[NF], const float (&later)[NF]) {
-  float tmp[NF];
-  M::combine(acc, later, tmp);
-#pragma unroll
-  for (int f = 0; f < NF; ++f) acc[f] = tmp[f];
+  M::combine(acc, later, acc);
 }
 
 template <typename E>

@@ -443,3 +443,195 @@ def matrix_scan(M: torch.Tensor, b: torch.Tensor) -> tuple[torch.Tensor, torch.T
         )
     Abar, Bbar = matrix_affine_scan(M, b.unsqueeze(-1))
     return Abar, Bbar.squeeze(-1)
+
+
+# ====================================================== angle-fused scan ==
+
+
+def brickwall_meta(rounds: int, k: int, device=None):
+    """The (perm, sgn, p2p) plane metadata of the brick-wall layout that
+    GivensMinGRU / RotationMinGRU build (reference ``min_gru.py:2544-2549``,
+    ``2649-2678``, ``2202-2219``): round r pairs (i, i+1 mod k) for
+    i = r%2, r%2+2, ...; sgn is -1 on i and +1 on i+1; p2p is the plane index."""
+    perm = torch.empty(rounds, k, dtype=torch.int32)
+    sgn = torch.empty(rounds, k, dtype=torch.float32)
+    p2p = torch.empty(rounds, k, dtype=torch.int32)
+    for r in range(rounds):
+        i_idx = [(i % k) for i in range(r % 2, k, 2)]
+        for m, i in enumerate(i_idx):
+            j = (i + 1) % k
+            perm[r, i], perm[r, j] = j, i
+            sgn[r, i], sgn[r, j] = -1.0, 1.0
+            p2p[r, i], p2p[r, j] = m, m
+    if device is not None:
+        perm, sgn, p2p = perm.to(device), sgn.to(device), p2p.to(device)
+    return perm, sgn, p2p
+
+
+def _is_brickwall(perm: torch.Tensor, sgn: torch.Tensor, p2p: torch.Tensor) -> bool:
+    """Whether the metadata is the brick-wall layout. Checked once per tensor
+    (one device-to-host copy) and remembered on the tensor object."""
+    key = (perm._version, sgn._version, p2p._version, sgn.data_ptr(), p2p.data_ptr())
+    memo = getattr(perm, "_mgs_brickwall", None)
+    if memo is not None and memo[0] == key:
+        return memo[1]
+    R, k = perm.shape
+    rp, rs, rq = brickwall_meta(R, k)
+    ok = (torch.equal(perm.detach().cpu().to(torch.int32), rp)
+          and torch.equal(sgn.detach().cpu().to(torch.float32), rs)
+          and torch.equal(p2p.detach().cpu().to(torch.int32), rq))
+    try:
+        perm._mgs_brickwall = (key, ok)
+    except (AttributeError, RuntimeError):
+        pass
+    return ok
+
+
+@torch.library.custom_op("mingru_b200::angle_scan_fwd", mutates_args=())
+def _angle_scan_fwd(
+    theta: torch.Tensor, scale: torch.Tensor, gamma: torch.Tensor, b: torch.Tensor,
+    h0: torch.Tensor, perm: torch.Tensor, sgn: torch.Tensor, p2p: torch.Tensor,
+    has_scale: int, has_decay: int, brickwall: int, save_carries: bool,
+) -> tuple[torch.Tensor, torch.Tensor]:
+    lib = _lib.load()
+    theta, scale, gamma, b, h0 = (_dense(x) for x in (theta, scale, gamma, b, h0))
+    Bn, T, n, R, half = theta.shape
+    k = b.shape[-1]
+    code = _dtype_code("angle_scan", b)
+    h = torch.empty_like(b)
+    csz = lib.mgs_angle_scan_carry_size(Bn, T, n, R, k, brickwall, code) if save_carries else 0
+    carries = torch.empty(csz // 4, dtype=torch.float32, device=b.device)
+    ws = _workspace(lib.mgs_angle_scan_workspace_size(Bn, T, n, R, k, brickwall, code), b.device)
+    with torch.cuda.device(b.device):
+        st = lib.mgs_angle_scan_fwd(
+            _ptr(theta), _ptr(scale), _ptr(gamma), _ptr(b), _ptr(h0),
+            _ptr(perm), _ptr(sgn), _ptr(p2p), _ptr(h), _ptr(carries) if csz else None,
+            Bn, T, n, R, k, int(has_scale), int(has_decay), int(brickwall), code,
+            _ptr(ws), ws.numel(), _stream(b),
+        )
+    _lib.check(st, "angle_scan forward")
+    return h, carries
+
+
+@_angle_scan_fwd.register_fake
+def _(theta, scale, gamma, b, h0, perm, sgn, p2p, has_scale, has_decay, brickwall, save_carries):
+    Bn, T, n, R, half = theta.shape
+    k = b.shape[-1]
+    csz = _lib.load().mgs_angle_scan_carry_size(Bn, T, n, R, k, brickwall, _dtype_code("angle_scan", b))
+    return torch.empty_like(b), b.new_empty((csz // 4 if save_carries else 0,), dtype=torch.float32)
+
+
+@torch.library.custom_op("mingru_b200::angle_scan_bwd", mutates_args=())
+def _angle_scan_bwd(
+    theta: torch.Tensor, scale: torch.Tensor, gamma: torch.Tensor, b: torch.Tensor,
+    h0: torch.Tensor, perm: torch.Tensor, sgn: torch.Tensor, p2p: torch.Tensor,
+    h: torch.Tensor, grad_h: torch.Tensor, carries: torch.Tensor,
+    has_scale: int, has_decay: int, brickwall: int,
+) -> tuple[torch.Tensor, torch.Tensor, torch.Tensor, torch.Tensor, torch.Tensor]:
+    lib = _lib.load()
+    theta, scale, gamma, b, h0, h = (_dense(x) for x in (theta, scale, gamma, b, h0, h))
+    gh = _dense(grad_h.to(b.dtype))
+    Bn, T, n, R, half = theta.shape
+    k = b.shape[-1]
+    code = _dtype_code("angle_scan", b)
+    csz = lib.mgs_angle_scan_carry_size(Bn, T, n, R, k, brickwall, code)
+    if carries.numel() * 4 < csz:
+        raise RuntimeError("angle_scan backward: forward carries were not saved")
+    dtheta, db, dh0 = torch.empty_like(theta), torch.empty_like(b), torch.empty_like(h0)
+    dscale = torch.empty_like(scale) if has_scale else torch.zeros_like(scale)
+    dgamma = torch.empty_like(gamma) if has_decay else torch.zeros_like(gamma)
+    ws = _workspace(lib.mgs_angle_scan_workspace_size(Bn, T, n, R, k, brickwall, code), b.device)
+    with torch.cuda.device(b.device):
+        st = lib.mgs_angle_scan_bwd(
+            _ptr(theta), _ptr(scale), _ptr(gamma), _ptr(b), _ptr(h0),
+            _ptr(perm), _ptr(sgn), _ptr(p2p), _ptr(h), _ptr(gh), _ptr(carries) if csz else None,
+            _ptr(dtheta), _ptr(dscale), _ptr(dgamma), _ptr(db), _ptr(dh0),
+            Bn, T, n, R, k, int(has_scale), int(has_decay), int(brickwall), code,
+            _ptr(ws), ws.numel(), _stream(b),
+        )
+    _lib.check(st, "angle_scan backward")
+    return dtheta, dscale, dgamma, db, dh0
+
+
+@_angle_scan_bwd.register_fake
+def _(theta, scale, gamma, b, h0, perm, sgn, p2p, h, grad_h, carries, has_scale, has_decay, brickwall):
+    return (torch.empty_like(theta), torch.empty_like(scale), torch.empty_like(gamma),
+            torch.empty_like(b), torch.empty_like(h0))
+
+
+def _angle_setup(ctx, inputs, output):
+    theta, scale, gamma, b, h0, perm, sgn, p2p, has_scale, has_decay, brickwall, _ = inputs
+    h, carries = output
+    ctx.save_for_backward(theta, scale, gamma, b, h0, perm, sgn, p2p, h, carries)
+    ctx.flags = (has_scale, has_decay, brickwall)
+    ctx.mark_non_differentiable(carries)
+    ctx.set_materialize_grads(False)
+
+
+def _angle_backward(ctx, grad_h, _gcarries):
+    if torch.is_grad_enabled():
+        raise RuntimeError("angle_scan does not support second-order autograd (create_graph=True)")
+    if grad_h is None:
+        return (None,) * 12
+    theta, scale, gamma, b, h0, perm, sgn, p2p, h, carries = ctx.saved_tensors
+    has_scale, has_decay, brickwall = ctx.flags
+    dth, dsc, dga, db, dh0 = _angle_scan_bwd(
+        theta, scale, gamma, b, h0, perm, sgn, p2p, h, grad_h, carries, has_scale, has_decay,
+        brickwall,
+    )
+    return dth, dsc, dga, db, dh0, None, None, None, None, None, None, None
+
+
+torch.library.register_autograd(
+    "mingru_b200::angle_scan_fwd", _angle_backward, setup_context=_angle_setup
+)
+
+
+def angle_scan_impl(
+    theta: torch.Tensor, scale: torch.Tensor, gamma: torch.Tensor, b: torch.Tensor,
+    h0: torch.Tensor, perm: torch.Tensor, sgn: torch.Tensor, p2p: torch.Tensor,
+    *, has_scale: int, has_decay: int,
+) -> torch.Tensor:
+    """Angle-fused Givens / rotation scan; returns the states ``h`` ``(B, T, n, k)``.
+
+    Same arguments and contract as the reference's
+    ``triton_scans.angle_scan_impl`` (``triton_scans.py:1743-1812``):
+    ``theta`` ``(B, T, n, R, k/2)``, ``scale`` / ``gamma`` ``(B, T, n)``
+    (read only when ``has_scale`` / ``has_decay``), ``b`` ``(B, T, n, k)``,
+    ``h0`` ``(B, n, k)``, plane metadata ``perm`` / ``sgn`` / ``p2p`` ``(R, k)``.
+    Differentiable w.r.t. theta, scale, gamma, b and h0.
+    """
+    op = "angle_scan"
+    if theta.ndim != 5 or b.ndim != 4:
+        raise ValueError(
+            f"{op}: need 5-D (B, T, n, R, half) theta and 4-D (B, T, n, k) b "
+            f"(got theta={tuple(theta.shape)}, b={tuple(b.shape)})"
+        )
+    Bn, T, n, R, half = theta.shape
+    k = b.shape[-1]
+    if (k < 2 or k % 2 or 2 * half != k or b.shape[:3] != (Bn, T, n)
+            or tuple(scale.shape) != (Bn, T, n) or tuple(gamma.shape) != (Bn, T, n)
+            or tuple(h0.shape) != (Bn, n, k) or tuple(perm.shape) != (R, k)
+            or tuple(sgn.shape) != (R, k) or tuple(p2p.shape) != (R, k)):
+        raise ValueError(
+            f"{op}: shapes disagree (theta={tuple(theta.shape)}, scale={tuple(scale.shape)}, "
+            f"gamma={tuple(gamma.shape)}, b={tuple(b.shape)}, h0={tuple(h0.shape)}, "
+            f"perm={tuple(perm.shape)}): need an even k = 2 * half and scale/gamma/b/h0/"
+            "perm/sgn/p2p agreeing with theta's (B, T, n, R, half) on (B, T, n, R, k)"
+        )
+    if k > 64 or R > 16:
+        raise ValueError(f"{op}: k <= 64 and R <= 16 supported (got k={k}, R={R})")
+    _require_cuda(op, theta, scale, gamma, b, h0, perm, sgn, p2p)
+    dt = b.dtype
+    if any(x.dtype != dt for x in (theta, scale, gamma, h0)):
+        raise ValueError(f"{op}: theta, scale, gamma, b and h0 must share a dtype")
+    _dtype_code(op, b)
+    perm = perm.to(torch.int32).contiguous()
+    p2p = p2p.to(torch.int32).contiguous()
+    sgn = sgn.to(torch.float32).contiguous()
+    brick = 1 if _is_brickwall(perm, sgn, p2p) else 0
+    need = torch.is_grad_enabled() and any(
+        x.requires_grad for x in (theta, scale, gamma, b, h0))
+    h, _ = _angle_scan_fwd(theta, scale, gamma, b, h0, perm, sgn, p2p,
+                           int(has_scale), int(has_decay), brick, need)
+    return h
