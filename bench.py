@@ -282,11 +282,80 @@ class MatrixScanWorkload(ScanWorkload):
         oracle.matrix_scan_bwd(M, A, Bc, gA, gB, dtype=np.float32)
 
 
+class AngleScanWorkload(ScanWorkload):
+    """GivensMinGRU angle-fused scan fwd+bwd, B=8, T=4096,
+    D=1024 (n=128 blocks of k=8), R=2 brick-wall rounds with the wrap-around
+    plane (7, 0) angle fixed to 0, i.e. the 7 nearest-neighbour Givens
+    rotations, theta ~ U(-pi, pi); gamma = sigmoid(N(0,1)) (decay on),
+    b ~ N(0,1), h0 = 0; grad_h ~ N(0,1). The matrices are never built."""
+
+    kernels = {"fwd": "angle_scan_fwd", "bwd": "angle_scan_bwd"}
+    workload = "angle-fused Givens scan k=8 R=2 fwd+bwd (GivensMinGRU, BASELINE config 4)"
+    metric_elems_doc = "B*T*D with D = n*k"
+
+    def __init__(self, dtype=torch.float32, name="cfg4", B=8, T=4096, D=1024, k=8, R=2):
+        super().__init__(dtype)
+        self.B, self.T, self.D, self.k, self.R, self.name = B, T, D, k, R, name
+        self.n = D // k
+        # per block-step: fwd reads theta (R*k/2), gamma (1), b (k), writes h (k);
+        # bwd reads theta, gamma, b, grad_h and writes dtheta, dgamma, db (h0/dh0 per lane only)
+        na = R * k // 2
+        self.fwd_bytes = (na + 1 + 2 * k) * self.esize / k
+        self.bwd_bytes = (2 * na + 2 + 3 * k) * self.esize / k
+
+    def make_host(self, rows, seed):
+        g = torch.Generator().manual_seed(seed)
+        n, k, R = self.n, self.k, self.R
+        theta = (torch.rand(rows, self.T, n, R, k // 2, generator=g) * 2 - 1) * math.pi
+        theta[:, :, :, 1, k // 2 - 1] = 0.0  # plane (k-1, 0) of round 1 fixed: 7 live rotations
+        gamma = torch.sigmoid(torch.randn(rows, self.T, n, generator=g))
+        b = torch.randn(rows, self.T, n, k, generator=g)
+        h0 = torch.zeros(rows, n, k)
+        gh = torch.randn(rows, self.T, n, k, generator=torch.Generator().manual_seed(1234 + seed))
+        return [theta, gamma, b, h0], [gh]
+
+    def device_setup(self, host, dev):
+        import mingru_b200 as mb
+
+        st = super().device_setup(host, dev)
+        self._const(dev)
+        return st
+
+    def _const(self, dev):
+        import mingru_b200 as mb
+
+        if getattr(self, "_dev", None) != dev:
+            self._dev = dev
+            self.scale = torch.ones(self.B, self.T, self.n, dtype=self.dtype, device=dev)
+            self.meta = mb.brickwall_meta(self.R, self.k, dev)
+
+    def forward(self, theta, gamma, b, h0):
+        import mingru_b200 as mb
+
+        self._const(theta.device)
+        scale = self.scale if self.scale.shape[0] == theta.shape[0] else torch.ones(
+            theta.shape[:3], dtype=theta.dtype, device=theta.device)
+        return (mb.angle_scan_impl(theta, scale, gamma, b, h0, *self.meta,
+                                   has_scale=0, has_decay=1),)
+
+    def cpu_step(self, sample):
+        import mingru_b200 as mb
+        from oracle import oracle
+
+        (theta, gamma, b, h0), (gh,) = sample
+        perm, sgn, p2p = (x.numpy() for x in mb.brickwall_meta(self.R, self.k))
+        scale = np.ones(theta.shape[:3], dtype=np.float32)
+        kw = dict(has_scale=0, has_decay=1, dtype=np.float32)
+        h = oracle.angle_scan(theta, scale, gamma, b, h0, perm, sgn, p2p, **kw)
+        oracle.angle_scan_bwd(theta, scale, gamma, h0, h, gh, perm, sgn, p2p, **kw)
+
+
 WORKLOADS = {
     "cfg1": lambda: LogScanWorkload(),
     "cfg2": lambda: LinearScanWorkload(),
     "cfg2-bf16": lambda: LinearScanWorkload(dtype=torch.bfloat16, name="cfg2-bf16"),
     "cfg3": lambda: MatrixScanWorkload(),
+    "cfg4": lambda: AngleScanWorkload(),
 }
 
 
@@ -462,6 +531,33 @@ def run_reference(args, w) -> None:
     print(json.dumps(line), flush=True)
 
 
+def capture(fn, dev, warm: int = 2, stream=None):
+    """Capture fn() (a fixed sequence of launches on the current stream) in a CUDA graph."""
+    side = stream if stream is not None else torch.cuda.Stream(dev)
+    side.wait_stream(torch.cuda.current_stream(dev))
+    with torch.cuda.stream(side):
+        for _ in range(warm):
+            fn()
+    torch.cuda.current_stream(dev).wait_stream(side)
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g, stream=side):
+        keep = fn()
+    return g, keep
+
+
+def time_graph(g, reps: int, dev) -> float:
+    """Average device ms per replay of graph g (events on the replay stream)."""
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    g.replay()
+    torch.cuda.synchronize(dev)
+    e0.record()
+    for _ in range(reps):
+        g.replay()
+    e1.record()
+    torch.cuda.synchronize(dev)
+    return e0.elapsed_time(e1) / reps
+
+
 def run_ours(args, w) -> None:
     rank, world, local = dist_setup(args.gpus)
     dev = torch.device("cuda", local)
@@ -475,25 +571,45 @@ def run_ours(args, w) -> None:
     torch.cuda.synchronize(dev)
     mb.raise_device_error(dev)
 
-    # ---- timed region: device-resident inputs
-    n_ev = args.steps
-    evs = [[torch.cuda.Event(enable_timing=True) for _ in range(3)] for _ in range(n_ev)]
+    # One step = forward + backward of the op, replayed as a CUDA graph so the
+    # device, not Python dispatch, sets the pace (every kernel of the step runs
+    # on every replay; inputs stay resident in HBM).
+    graph = None
+    if not args.no_graph:
+        graph, _keep = capture(lambda: w.step(st), dev)
+
     start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     barrier(world, dev)
     torch.cuda.synchronize(dev)
     with ClockSampler(dev.index) as clk:
         clk.mark_start()
         start.record()
-        for i in range(args.steps):
-            w.step(st, evs[i])
+        for _ in range(args.steps):
+            if graph is not None:
+                graph.replay()
+            else:
+                w.step(st)
         stop.record()
         torch.cuda.synchronize(dev)
         clk.mark_stop()
     barrier(world, dev)
     ms = max_over_ranks(start.elapsed_time(stop), world, dev)
     mb.raise_device_error(dev)
-    fwd_ms = statistics.mean(e[0].elapsed_time(e[1]) for e in evs)
-    bwd_ms = statistics.mean(e[1].elapsed_time(e[2]) for e in evs)
+
+    # Per-kernel device time: each op captured alone and replayed.
+    ins, cots = st["ins"], st["cots"]
+    with torch.no_grad():
+        gf, _kf = capture(lambda: w.forward(*ins), dev)
+    bstream = torch.cuda.Stream(dev)
+    bstream.wait_stream(torch.cuda.current_stream(dev))
+    with torch.cuda.stream(bstream):  # backward nodes replay on the forward's stream
+        outs = w.forward(*ins)
+    gb, _kb = capture(lambda: torch.autograd.grad(outs, ins, cots, retain_graph=True), dev,
+                      stream=bstream)
+    reps = max(10, min(200, args.steps))
+    fwd_ms = time_graph(gf, reps, dev)
+    bwd_ms = time_graph(gb, reps, dev)
+    del gf, gb, _kf, _kb, outs, graph
 
     # ---- e2e: public API with pinned host buffers, copies inside the timed region
     est = w.e2e_setup(host, dev)
@@ -524,7 +640,6 @@ def run_ours(args, w) -> None:
     traffic = load_traffic()
     per_step_ms = ms / args.steps
     total_elems = w.elems * world
-    # dominant kernel: the one with the larger share of the step
     dom = "bwd" if bwd_ms >= fwd_ms else "fwd"
     dom_ms = bwd_ms if dom == "bwd" else fwd_ms
     dom_bytes = (w.bwd_bytes if dom == "bwd" else w.fwd_bytes) * w.elems
@@ -543,7 +658,7 @@ def run_ours(args, w) -> None:
         "vs_baseline": None,
         "dtype": "f32",
         "data": "synthetic (seeded, BASELINE shapes)",
-        "config": w.config(world),
+        "config": dict(w.config(world), step="cuda-graph replay" if not args.no_graph else "eager"),
         "kernel_ms": {"fwd": fwd_ms, "bwd": bwd_ms},
         "roofline": {
             "bound": "hbm",
@@ -564,7 +679,7 @@ def run_ours(args, w) -> None:
             "unit": "Gelem/s",
             "h2d_bytes_per_step": w.h2d_bytes,
             "d2h_bytes_per_step": w.d2h_bytes,
-            "path": "public op + autograd (C ABI) from pinned host buffers",
+            "path": "public op + autograd (C ABI) from pinned host buffers, eager",
         },
         "gpu_launches": w.launches_per_step * args.steps,
         "clocks": clk.summary(),
@@ -582,6 +697,7 @@ def main() -> None:
     ap.add_argument("--e2e-steps", type=int, default=5)
     ap.add_argument("--ref-rows", type=int, default=2, help="batch rows per reference step")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
+    ap.add_argument("--no-graph", action="store_true", help="time eager steps instead of graph replay")
     ap.add_argument("--batch", type=int, default=None,
                     help="override the per-GPU batch (small ncu captures only; not a bench line)")
     args = ap.parse_args()

@@ -180,6 +180,36 @@ int mgs_angle_scan_bwd(const void* theta, const void* scale, const void* gamma, 
                        int64_t n, int R, int k, int has_scale, int has_decay, int brickwall,
                        int dtype, void* workspace, size_t workspace_bytes, void* stream);
 
+/* ------------------------------------------------------------------------ */
+/* DeltaMinGRU chunked-WY delta rule (decay off).
+ * Q (B, H, T, dk); K (B, H, T, nh, dk); V (B, H, T, nh, dv); beta (B, H, T, nh)
+ * in the op dtype; H0, H_T (B, H, dk, dv) fp32; y (B, H, T, dv) op dtype.
+ * Per chunk of `chunk` tokens (M = nh * chunk micro-steps):
+ *   T = I + strict_lower(K K^T) * beta[col];  U = T^{-1} (V - K S);
+ *   y = Q S + ((Q K^T) * beta[col] * read_mask) U;  S <- S + K^T (beta * U).
+ * Replaces delta_scan_impl (triton_scans.py:2403-2447) -- the Triton forward
+ * trio (triton_scans.py:1859-2322), _DeltaScanFn (triton_scans.py:2324-2401)
+ * and the torch backward _delta_backward_torch (triton_scans.py:473-605) --
+ * called from DeltaMinGRU._delta_fused_forward (min_gru.py:3565-3609); eager
+ * oracle DeltaMinGRU._forward_chunked (min_gru.py:3152-3255).
+ * Envelope: nh * chunk <= 64, dk <= 64, dv <= 64.
+ * `saved` (mgs_delta_saved_size bytes) is written by the forward and read by
+ * the backward (chunk transitions and chunk-start states, fp32).          */
+
+size_t mgs_delta_saved_size(int64_t B, int H, int64_t T, int nh, int dk, int dv, int chunk);
+size_t mgs_delta_workspace_size(int64_t B, int H, int64_t T, int nh, int dk, int dv, int chunk);
+
+int mgs_delta_fwd(const void* Q, const void* K, const void* V, const void* beta, const float* H0,
+                  void* y, float* H_T, void* saved, int64_t B, int H, int64_t T, int nh, int dk,
+                  int dv, int chunk, int dtype, void* workspace, size_t workspace_bytes,
+                  void* stream);
+
+/* Backward: (dQ, dK, dV, dbeta, dH0) of sum(y * dy) + sum(H_T * dH_T). */
+int mgs_delta_bwd(const void* Q, const void* K, const void* V, const void* beta, const void* saved,
+                  const void* dy, const float* dH_T, void* dQ, void* dK, void* dV, void* dbeta,
+                  float* dH0, int64_t B, int H, int64_t T, int nh, int dk, int dv, int chunk,
+                  int dtype, void* workspace, size_t workspace_bytes, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -8,6 +8,7 @@ fallback: CPU tensors raise.
 """
 
 from .scan_ops import (
+    delta_scan_impl,
     angle_scan_impl,
     brickwall_meta,
     linear_scan,
@@ -21,6 +22,7 @@ from .scan_ops import (
 __version__ = "0.1.0"
 
 __all__ = [
+    "delta_scan_impl",
     "angle_scan_impl",
     "brickwall_meta",
     "linear_scan",

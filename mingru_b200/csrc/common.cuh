@@ -291,17 +291,30 @@ __device__ __forceinline__ void warp_lookback_win(const Lookback& lb, long long 
       }
     }
     __syncwarp();
-    // Compose predecessors nearest-first: run = e_i o run.
+    // Compose predecessors nearest-first: run = e_i o run. Loads of G
+    // predecessors are issued together so a small element costs one L2 round
+    // trip per G predecessors instead of one per predecessor.
+    constexpr int G = NF <= 4 ? 8 : (NF <= 8 ? 4 : (NF <= 16 ? 2 : 1));
 #pragma unroll 1
-    for (int i = 0; i <= last; ++i) {
-      const unsigned fi = __shfl_sync(0xffffffffu, f, i);
-      const float* src = (fi == kFlagIncl ? lb.incl : lb.agg) + (size_t)(base - (long long)i * stride) * NF * 32;
-      float e[NF];
+    for (int i0 = 0; i0 <= last; i0 += G) {
+      float e[G][NF];
 #pragma unroll
-      for (int q = 0; q < NF; ++q) e[q] = __ldcg(src + q * 32 + lane);
-      Monoid::combine(e, run, e);  // combine may write over its earlier operand
+      for (int gi = 0; gi < G; ++gi) {
+        const int i = i0 + gi < last ? i0 + gi : last;  // clamp: duplicates are never combined
+        const unsigned fi = __shfl_sync(0xffffffffu, f, i);
+        const float* src = (fi == kFlagIncl ? lb.incl : lb.agg) +
+                           (size_t)(base - (long long)i * stride) * NF * 32;
 #pragma unroll
-      for (int q = 0; q < NF; ++q) run[q] = e[q];
+        for (int q = 0; q < NF; ++q) e[gi][q] = __ldcg(src + q * 32 + lane);
+      }
+#pragma unroll
+      for (int gi = 0; gi < G; ++gi) {
+        if (i0 + gi <= last) {
+          Monoid::combine(e[gi], run, e[gi]);  // combine may write over its earlier operand
+#pragma unroll
+          for (int q = 0; q < NF; ++q) run[q] = e[gi][q];
+        }
+      }
     }
     const unsigned flast = __shfl_sync(0xffffffffu, f, last);
     if (flast == kFlagIncl) break;

@@ -1,0 +1,631 @@
+// delta.cu -- DeltaMinGRU chunked-WY delta rule, forward and backward.
+//
+// Reference behaviour: DeltaMinGRU._forward_chunked (min_gru.py:3152-3255),
+// the Triton forward trio + torch backward reached through delta_scan_impl
+// (triton_scans.py:1859-2447; backward _delta_backward_torch,
+// triton_scans.py:473-605). Layout (per (b, h), M = nh * C micro-steps per
+// chunk of C tokens): Q (B,H,T,dk); K (B,H,T,nh,dk); V (B,H,T,nh,dv);
+// beta (B,H,T,nh); H0 (B,H,dk,dv) fp32. Per chunk, with S the state entering
+// it:
+//   T  = I + L,  L = strict_lower(K K^T) * beta[col]           (M x M)
+//   U  = T^{-1} (V - K S)                                       (M x dv)
+//   y  = Q S + P U,  P = (Q K^T) * beta[col] * read_mask        (C x dv)
+//   S' = S + K^T (beta * U)
+// read_mask[t, m] = 1 iff micro-step m belongs to a token <= t.
+//
+// Structure. The chunk-to-chunk state map is affine in S:
+//   S' = A_c S + B_c,  A_c = I - K^T diag(beta) T^{-1} K,  B_c = K^T diag(beta) T^{-1} V,
+// and A_c, B_c depend only on the chunk's own inputs. So the forward is
+//   (1) chunk-parallel: A_c, B_c                                  [prepass]
+//   (2) per (b, h), serial over chunks: S_{c+1} = A_c S_c + B_c   [state pass]
+//       (writes the chunk-start states "Hbound" and H_T)
+//   (3) chunk-parallel: U and y from S_c                           [readout]
+// and the backward, with dS_c = A_c^T dS_{c+1} + E_c and
+// E_c = Q^T dy - K^T T^{-T} P^T dy (independent of S), is
+//   (1) chunk-parallel: E_c
+//   (2) per (b, h), serial in reverse: dS_c (the gradient leaving each chunk's
+//       output state, and dH0)
+//   (3) chunk-parallel: dQ, dK, dV, dbeta of every chunk from S_c and
+//       dS_{c+1}, restating the per-chunk adjoint of the reference backward.
+// All arithmetic is fp32 on CUDA cores in this version (shared-memory tiles,
+// 4x4 register-blocked products, forward / back substitution for the unit
+// triangular solves); inputs may be fp32 / bf16 / fp16.
+#include "common.cuh"
+
+namespace mgs {
+namespace delta {
+
+constexpr int kThreads = 256;
+constexpr int kMaxM = 64;   // nh * chunk micro-steps per chunk
+constexpr int kMaxD = 64;   // d_k, d_v
+
+template <typename E>
+struct Args {
+  const E* Q;
+  const E* K;
+  const E* V;
+  const E* beta;
+  const float* H0;
+  E* y;
+  float* HT;
+  const E* dy;
+  const float* dHT;
+  E* dQ;
+  E* dK;
+  E* dV;
+  E* dbeta;
+  float* dH0;
+  float* Ac;      // (BH, nchunks, dk, dk)  chunk transition, saved for the backward
+  float* Bc;      // (BH, nchunks, dk, dv)  chunk injection (forward scratch)
+  float* Hb;      // (BH, nchunks, dk, dv)  chunk-start states, saved for the backward
+  float* Ec;      // (BH, nchunks, dk, dv)  backward scratch
+  float* dSo;     // (BH, nchunks, dk, dv)  gradient w.r.t. each chunk's output state
+  long long T_;
+  int H, nh, dk, dv, C, nchunks;
+};
+
+// C (m x n, ldc) = (acc ? C : 0) + alpha * opA (m x kk) * opB (kk x n), all in
+// shared memory; opA(i,l) = TA ? A[l*lda+i] : A[i*lda+l], opB(l,j) = TB ?
+// B[j*ldb+l] : B[l*ldb+j]. Every thread of the block participates; ends with a
+// barrier. Each thread accumulates 4x4 output blocks in registers.
+template <bool TA, bool TB>
+__device__ void bgemm(int m, int n, int kk, const float* A, int lda, const float* B, int ldb,
+                      float* C, int ldc, bool acc, float alpha = 1.f) {
+  const int nbi = (m + 3) >> 2, nbj = (n + 3) >> 2;
+  for (int blk = threadIdx.x; blk < nbi * nbj; blk += blockDim.x) {
+    const int bi = blk / nbj, bj = blk - bi * nbj;
+    float r[4][4];
+#pragma unroll
+    for (int u = 0; u < 4; ++u)
+#pragma unroll
+      for (int v = 0; v < 4; ++v) r[u][v] = 0.f;
+    for (int l = 0; l < kk; ++l) {
+      float a[4], b[4];
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        const int i = bi * 4 + u;
+        a[u] = i < m ? (TA ? A[l * lda + i] : A[i * lda + l]) : 0.f;
+      }
+#pragma unroll
+      for (int v = 0; v < 4; ++v) {
+        const int j = bj * 4 + v;
+        b[v] = j < n ? (TB ? B[j * ldb + l] : B[l * ldb + j]) : 0.f;
+      }
+#pragma unroll
+      for (int u = 0; u < 4; ++u)
+#pragma unroll
+        for (int v = 0; v < 4; ++v) r[u][v] = fmaf(a[u], b[v], r[u][v]);
+    }
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      const int i = bi * 4 + u;
+      if (i >= m) continue;
+#pragma unroll
+      for (int v = 0; v < 4; ++v) {
+        const int j = bj * 4 + v;
+        if (j < n) C[i * ldc + j] = (acc ? C[i * ldc + j] : 0.f) + alpha * r[u][v];
+      }
+    }
+  }
+  __syncthreads();
+}
+
+// Solve (I + L) X = X in place (forward substitution), L strictly lower (M x M,
+// ldl), X (M x n, ldx). Columns run in parallel, rows in sequence.
+__device__ void solve_lower_unit(int M, int n, const float* L, int ldl, float* X, int ldx) {
+  for (int i = 1; i < M; ++i) {
+    for (int j = threadIdx.x; j < n; j += blockDim.x) {
+      float s = X[i * ldx + j];
+      for (int l = 0; l < i; ++l) s = fmaf(-L[i * ldl + l], X[l * ldx + j], s);
+      X[i * ldx + j] = s;
+    }
+    __syncthreads();
+  }
+}
+
+// Solve (I + L)^T X = X in place (back substitution).
+__device__ void solve_lower_unit_t(int M, int n, const float* L, int ldl, float* X, int ldx) {
+  for (int i = M - 2; i >= 0; --i) {
+    for (int j = threadIdx.x; j < n; j += blockDim.x) {
+      float s = X[i * ldx + j];
+      for (int l = i + 1; l < M; ++l) s = fmaf(-L[l * ldl + i], X[l * ldx + j], s);
+      X[i * ldx + j] = s;
+    }
+    __syncthreads();
+  }
+}
+
+// Chunk geometry helpers -----------------------------------------------------
+
+struct Chunk {
+  long long bh, c, t0;
+  int Ct, M;  // tokens, micro-steps in this chunk
+};
+
+__device__ __forceinline__ Chunk chunk_of(long long T, int C, int nh, int c, long long bh) {
+  Chunk k;
+  k.bh = bh;
+  k.c = c;
+  k.t0 = (long long)c * C;
+  k.Ct = (int)((T - k.t0) < C ? (T - k.t0) : C);
+  k.M = k.Ct * nh;
+  return k;
+}
+
+// Load the chunk's K (M x dk), V (M x dv), beta (M) and optionally Q (Ct x dk).
+template <typename E>
+__device__ void load_chunk(const Args<E>& p, const Chunk& ck, float* sK, float* sV, float* sb,
+                           float* sQ) {
+  const size_t tok0 = (size_t)ck.bh * p.T_ + ck.t0;
+  const E* K = p.K + tok0 * p.nh * p.dk;
+  const E* V = p.V + tok0 * p.nh * p.dv;
+  const E* bt = p.beta + tok0 * p.nh;
+  for (int i = threadIdx.x; i < ck.M * p.dk; i += blockDim.x) sK[i] = to_f32<E>(K[i]);
+  if (sV)
+    for (int i = threadIdx.x; i < ck.M * p.dv; i += blockDim.x) sV[i] = to_f32<E>(V[i]);
+  for (int i = threadIdx.x; i < ck.M; i += blockDim.x) sb[i] = to_f32<E>(bt[i]);
+  if (sQ) {
+    const E* Q = p.Q + tok0 * p.dk;
+    for (int i = threadIdx.x; i < ck.Ct * p.dk; i += blockDim.x) sQ[i] = to_f32<E>(Q[i]);
+  }
+  __syncthreads();
+}
+
+// L = strict_lower(K K^T) * beta[col]; also keeps KK (unmasked) when wanted.
+__device__ void build_L(int M, int dk, const float* sK, const float* sb, float* sL, float* sKK) {
+  float* dst = sKK ? sKK : sL;
+  bgemm<false, true>(M, M, dk, sK, dk, sK, dk, dst, M, false);
+  for (int i = threadIdx.x; i < M * M; i += blockDim.x) {
+    const int r = i / M, c = i - r * M;
+    sL[i] = c < r ? dst[i] * sb[c] : 0.f;
+  }
+  __syncthreads();
+}
+
+// P = (Q K^T) * beta[col] * read_mask  (Ct x M); keeps Sm = Q K^T when wanted.
+__device__ void build_P(int Ct, int M, int nh, int dk, const float* sQ, const float* sK,
+                        const float* sb, float* sP, float* sSm) {
+  float* dst = sSm ? sSm : sP;
+  bgemm<false, true>(Ct, M, dk, sQ, dk, sK, dk, dst, M, false);
+  for (int i = threadIdx.x; i < Ct * M; i += blockDim.x) {
+    const int t = i / M, m = i - t * M;
+    sP[i] = (m / nh) <= t ? dst[i] * sb[m] : 0.f;
+  }
+  __syncthreads();
+}
+
+// ------------------------------------------------------------ forward (1) --
+// A_c = I - K^T diag(beta) W, B_c = K^T diag(beta) Ut with [W | Ut] = T^{-1} [K | V].
+template <typename E>
+__global__ void __launch_bounds__(kThreads) fwd_prepass_kernel(Args<E> p) {
+  extern __shared__ __align__(16) float sm[];
+  const Chunk ck = chunk_of(p.T_, p.C, p.nh, blockIdx.x, blockIdx.y);
+  const int M = ck.M, dk = p.dk, dv = p.dv, W = dk + dv;
+  float* sK = sm;                   // M x dk
+  float* sb = sK + kMaxM * kMaxD;   // M
+  float* sL = sb + kMaxM;           // M x M
+  float* sX = sL + kMaxM * kMaxM;   // M x (dk + dv): [W | Ut]
+  float* sA = sX + kMaxM * 2 * kMaxD;  // dk x dk
+  float* sB = sA + kMaxD * kMaxD;      // dk x dv
+  load_chunk<E>(p, ck, sK, nullptr, sb, nullptr);
+  {
+    const size_t tok0 = (size_t)ck.bh * p.T_ + ck.t0;
+    const E* V = p.V + tok0 * p.nh * dv;
+    for (int i = threadIdx.x; i < M * W; i += blockDim.x) {
+      const int r = i / W, c = i - r * W;
+      sX[i] = c < dk ? sK[r * dk + c] : to_f32<E>(V[r * dv + c - dk]);
+    }
+  }
+  build_L(M, dk, sK, sb, sL, nullptr);
+  solve_lower_unit(M, W, sL, M, sX, W);
+  // scale rows of [W | Ut] by beta
+  for (int i = threadIdx.x; i < M * W; i += blockDim.x) sX[i] *= sb[i / W];
+  __syncthreads();
+  // A = I - K^T (beta W), B = K^T (beta Ut)
+  bgemm<true, false>(dk, dk, M, sK, dk, sX, W, sA, dk, false, -1.f);
+  bgemm<true, false>(dk, dv, M, sK, dk, sX + dk, W, sB, dv, false);
+  const size_t o = ((size_t)ck.bh * p.nchunks + ck.c);
+  float* Ag = p.Ac + o * dk * dk;
+  float* Bg = p.Bc + o * dk * dv;
+  for (int i = threadIdx.x; i < dk * dk; i += blockDim.x)
+    Ag[i] = sA[i] + ((i / dk) == (i % dk) ? 1.f : 0.f);
+  for (int i = threadIdx.x; i < dk * dv; i += blockDim.x) Bg[i] = sB[i];
+}
+
+// ------------------------------------------------------------ forward (2) --
+// One block per (b, h): S_{c+1} = A_c S_c + B_c; Hb[c] = S_c; HT = S_last.
+__global__ void __launch_bounds__(kThreads) state_pass_kernel(const float* Ac, const float* Bc,
+                                                             const float* H0, float* Hb, float* HT,
+                                                             int nchunks, int dk, int dv) {
+  extern __shared__ __align__(16) float sm[];
+  float* sS = sm;                  // dk x dv
+  float* sA = sS + kMaxD * kMaxD;  // dk x dk
+  float* sN = sA + kMaxD * kMaxD;  // dk x dv (new state)
+  const long long bh = blockIdx.x;
+  for (int i = threadIdx.x; i < dk * dv; i += blockDim.x) sS[i] = H0[(size_t)bh * dk * dv + i];
+  __syncthreads();
+  for (int c = 0; c < nchunks; ++c) {
+    const size_t o = (size_t)bh * nchunks + c;
+    for (int i = threadIdx.x; i < dk * dk; i += blockDim.x) sA[i] = Ac[o * dk * dk + i];
+    for (int i = threadIdx.x; i < dk * dv; i += blockDim.x) {
+      Hb[o * dk * dv + i] = sS[i];
+      sN[i] = Bc[o * dk * dv + i];
+    }
+    __syncthreads();
+    bgemm<false, false>(dk, dv, dk, sA, dk, sS, dv, sN, dv, true);
+    for (int i = threadIdx.x; i < dk * dv; i += blockDim.x) sS[i] = sN[i];
+    __syncthreads();
+  }
+  for (int i = threadIdx.x; i < dk * dv; i += blockDim.x) HT[(size_t)bh * dk * dv + i] = sS[i];
+}
+
+// ------------------------------------------------------------ forward (3) --
+template <typename E>
+__global__ void __launch_bounds__(kThreads) fwd_readout_kernel(Args<E> p) {
+  extern __shared__ __align__(16) float sm[];
+  const Chunk ck = chunk_of(p.T_, p.C, p.nh, blockIdx.x, blockIdx.y);
+  const int M = ck.M, Ct = ck.Ct, dk = p.dk, dv = p.dv, nh = p.nh;
+  float* sK = sm;                     // M x dk
+  float* sV = sK + kMaxM * kMaxD;     // M x dv -> U
+  float* sb = sV + kMaxM * kMaxD;     // M
+  float* sQ = sb + kMaxM;             // Ct x dk
+  float* sS = sQ + kMaxM * kMaxD;     // dk x dv
+  float* sL = sS + kMaxD * kMaxD;     // M x M
+  float* sP = sL + kMaxM * kMaxM;     // Ct x M
+  float* sY = sP + kMaxM * kMaxM;     // Ct x dv
+  load_chunk<E>(p, ck, sK, sV, sb, sQ);
+  const size_t o = (size_t)ck.bh * p.nchunks + ck.c;
+  for (int i = threadIdx.x; i < dk * dv; i += blockDim.x) sS[i] = p.Hb[o * dk * dv + i];
+  __syncthreads();
+  build_L(M, dk, sK, sb, sL, nullptr);
+  bgemm<false, false>(M, dv, dk, sK, dk, sS, dv, sV, dv, true, -1.f);  // V - K S
+  solve_lower_unit(M, dv, sL, M, sV, dv);                              // U
+  build_P(Ct, M, nh, dk, sQ, sK, sb, sP, nullptr);
+  bgemm<false, false>(Ct, dv, dk, sQ, dk, sS, dv, sY, dv, false);      // Q S
+  bgemm<false, false>(Ct, dv, M, sP, M, sV, dv, sY, dv, true);         // + P U
+  E* y = p.y + ((size_t)ck.bh * p.T_ + ck.t0) * dv;
+  for (int i = threadIdx.x; i < Ct * dv; i += blockDim.x) y[i] = from_f32<E>(sY[i]);
+}
+
+// ----------------------------------------------------------- backward (1) --
+// E_c = Q^T dy - K^T T^{-T} (P^T dy)
+template <typename E>
+__global__ void __launch_bounds__(kThreads) bwd_e_kernel(Args<E> p) {
+  extern __shared__ __align__(16) float sm[];
+  const Chunk ck = chunk_of(p.T_, p.C, p.nh, blockIdx.x, blockIdx.y);
+  const int M = ck.M, Ct = ck.Ct, dk = p.dk, dv = p.dv, nh = p.nh;
+  float* sK = sm;
+  float* sb = sK + kMaxM * kMaxD;
+  float* sQ = sb + kMaxM;
+  float* sdy = sQ + kMaxM * kMaxD;   // Ct x dv
+  float* sL = sdy + kMaxM * kMaxD;   // M x M
+  float* sP = sL + kMaxM * kMaxM;    // Ct x M
+  float* sZ = sP + kMaxM * kMaxM;    // M x dv
+  float* sE = sZ + kMaxM * kMaxD;    // dk x dv
+  load_chunk<E>(p, ck, sK, nullptr, sb, sQ);
+  {
+    const E* dy = p.dy + ((size_t)ck.bh * p.T_ + ck.t0) * dv;
+    for (int i = threadIdx.x; i < Ct * dv; i += blockDim.x) sdy[i] = to_f32<E>(dy[i]);
+  }
+  __syncthreads();
+  build_L(M, dk, sK, sb, sL, nullptr);
+  build_P(Ct, M, nh, dk, sQ, sK, sb, sP, nullptr);
+  bgemm<true, false>(M, dv, Ct, sP, M, sdy, dv, sZ, dv, false);   // P^T dy
+  solve_lower_unit_t(M, dv, sL, M, sZ, dv);                       // T^{-T} P^T dy
+  bgemm<true, false>(dk, dv, Ct, sQ, dk, sdy, dv, sE, dv, false);  // Q^T dy
+  bgemm<true, false>(dk, dv, M, sK, dk, sZ, dv, sE, dv, true, -1.f);
+  float* Eg = p.Ec + ((size_t)ck.bh * p.nchunks + ck.c) * dk * dv;
+  for (int i = threadIdx.x; i < dk * dv; i += blockDim.x) Eg[i] = sE[i];
+}
+
+// ----------------------------------------------------------- backward (2) --
+// dS_c = A_c^T dS_{c+1} + E_c in reverse; dSo[c] = dS_{c+1}; dH0 = dS_0.
+__global__ void __launch_bounds__(kThreads) adj_pass_kernel(const float* Ac, const float* Ec,
+                                                           const float* dHT, float* dSo, float* dH0,
+                                                           int nchunks, int dk, int dv) {
+  extern __shared__ __align__(16) float sm[];
+  float* sS = sm;
+  float* sA = sS + kMaxD * kMaxD;
+  float* sN = sA + kMaxD * kMaxD;
+  const long long bh = blockIdx.x;
+  for (int i = threadIdx.x; i < dk * dv; i += blockDim.x) sS[i] = dHT[(size_t)bh * dk * dv + i];
+  __syncthreads();
+  for (int c = nchunks - 1; c >= 0; --c) {
+    const size_t o = (size_t)bh * nchunks + c;
+    for (int i = threadIdx.x; i < dk * dk; i += blockDim.x) sA[i] = Ac[o * dk * dk + i];
+    for (int i = threadIdx.x; i < dk * dv; i += blockDim.x) {
+      dSo[o * dk * dv + i] = sS[i];
+      sN[i] = Ec[o * dk * dv + i];
+    }
+    __syncthreads();
+    bgemm<true, false>(dk, dv, dk, sA, dk, sS, dv, sN, dv, true);
+    for (int i = threadIdx.x; i < dk * dv; i += blockDim.x) sS[i] = sN[i];
+    __syncthreads();
+  }
+  for (int i = threadIdx.x; i < dk * dv; i += blockDim.x) dH0[(size_t)bh * dk * dv + i] = sS[i];
+}
+
+// ----------------------------------------------------------- backward (3) --
+// Per-chunk adjoint (the reference's _delta_backward_torch body, restated).
+template <typename E>
+__global__ void __launch_bounds__(kThreads) bwd_grads_kernel(Args<E> p) {
+  extern __shared__ __align__(16) float sm[];
+  const Chunk ck = chunk_of(p.T_, p.C, p.nh, blockIdx.x, blockIdx.y);
+  const int M = ck.M, Ct = ck.Ct, dk = p.dk, dv = p.dv, nh = p.nh;
+  const int MD = kMaxM * kMaxD, MM = kMaxM * kMaxM, DD = kMaxD * kMaxD;
+  float* sK = sm;            // M x dk
+  float* sU = sK + MD;       // M x dv: V, then U
+  float* sb = sU + MD;       // M
+  float* sQ = sb + kMaxM;    // Ct x dk
+  float* sS = sQ + MD;       // dk x dv   (chunk-start state)
+  float* sdS = sS + DD;      // dk x dv   (grad of the chunk's output state)
+  float* sdy = sdS + DD;     // Ct x dv   (dy; after its last use: dbU = K dSo, M x dv)
+  float* sL = sdy + MD;      // M x M
+  float* sSm = sL + MM;      // Ct x M
+  float* sP = sSm + MM;      // Ct x M  (later dSm)
+  float* sdP = sP + MM;      // Ct x M  (later dT / dKK, M x M)
+  float* sdU = sdP + MM;     // M x dv  (dU, then G)
+  float* sdK = sdU + MD;     // M x dk
+  float* sdQ = sdK + MD;     // Ct x dk
+  float* sdb = sdQ + MD;     // M
+  float* sdbU = sdy;
+  load_chunk<E>(p, ck, sK, sU, sb, sQ);
+  {
+    const size_t o = (size_t)ck.bh * p.nchunks + ck.c;
+    for (int i = threadIdx.x; i < dk * dv; i += blockDim.x) {
+      sS[i] = p.Hb[o * dk * dv + i];
+      sdS[i] = p.dSo[o * dk * dv + i];
+    }
+    const E* dy = p.dy + ((size_t)ck.bh * p.T_ + ck.t0) * dv;
+    for (int i = threadIdx.x; i < Ct * dv; i += blockDim.x) sdy[i] = to_f32<E>(dy[i]);
+  }
+  __syncthreads();
+  build_L(M, dk, sK, sb, sL, nullptr);
+  bgemm<false, false>(M, dv, dk, sK, dk, sS, dv, sU, dv, true, -1.f);  // V - K S
+  solve_lower_unit(M, dv, sL, M, sU, dv);                              // U
+  build_P(Ct, M, nh, dk, sQ, sK, sb, sP, sSm);
+  bgemm<false, true>(Ct, dk, dv, sdy, dv, sS, dv, sdQ, dk, false);     // dQ = dy S^T
+  bgemm<false, true>(Ct, M, dv, sdy, dv, sU, dv, sdP, M, false);       // dP = dy U^T
+  bgemm<true, false>(M, dv, Ct, sP, M, sdy, dv, sdU, dv, false);       // dU = P^T dy
+  bgemm<false, false>(M, dv, dk, sK, dk, sdS, dv, sdbU, dv, false);    // dbU = K dSo
+  for (int i = threadIdx.x; i < M * dk; i += blockDim.x) sdK[i] = 0.f;
+  __syncthreads();
+  // dK = (beta U) dSo^T
+  for (int i = threadIdx.x; i < M * dv; i += blockDim.x) sdU[i] += sb[i / dv] * sdbU[i];
+  __syncthreads();
+  {
+    // beta-scaled U into sdbU's slot would clobber dbU; compute dK directly.
+    for (int i = threadIdx.x; i < M * dk; i += blockDim.x) {
+      const int m = i / dk, k = i - m * dk;
+      float s = 0.f;
+      for (int v = 0; v < dv; ++v) s = fmaf(sU[m * dv + v], sdS[k * dv + v], s);
+      sdK[i] = sb[m] * s;
+    }
+    for (int m = threadIdx.x; m < M; m += blockDim.x) {
+      float s = 0.f;
+      for (int v = 0; v < dv; ++v) s = fmaf(sU[m * dv + v], sdbU[m * dv + v], s);
+      sdb[m] = s;
+    }
+    __syncthreads();
+  }
+  // dSm = dP * beta[col] * read (into sP); dbeta += sum_t dP * Sm * read
+  for (int m = threadIdx.x; m < M; m += blockDim.x) {
+    float s = 0.f;
+    for (int t = m / nh; t < Ct; ++t) s = fmaf(sdP[t * M + m], sSm[t * M + m], s);
+    sdb[m] += s;
+  }
+  __syncthreads();
+  for (int i = threadIdx.x; i < Ct * M; i += blockDim.x) {
+    const int t = i / M, m = i - t * M;
+    sP[i] = (m / nh) <= t ? sdP[i] * sb[m] : 0.f;
+  }
+  __syncthreads();
+  bgemm<false, false>(Ct, dk, M, sP, M, sK, dk, sdQ, dk, true);   // dQ += dSm K
+  bgemm<true, false>(M, dk, Ct, sP, M, sQ, dk, sdK, dk, true);    // dK += dSm^T Q
+  solve_lower_unit_t(M, dv, sL, M, sdU, dv);                      // G = T^{-T} dU
+  bgemm<false, true>(M, M, dv, sdU, dv, sU, dv, sdP, M, false, -1.f);  // dT = -G U^T
+  bgemm<false, true>(M, dk, dv, sdU, dv, sS, dv, sdK, dk, true, -1.f); // dK -= G S^T
+  // dKK = dT * beta[col] * strict; dbeta += sum_i dT * KK * strict (KK[i][l] = k_i . k_l)
+  for (int l = threadIdx.x; l < M; l += blockDim.x) {
+    float s = 0.f;
+    for (int i = l + 1; i < M; ++i) {
+      float kk = 0.f;
+      for (int q = 0; q < dk; ++q) kk = fmaf(sK[i * dk + q], sK[l * dk + q], kk);
+      s = fmaf(sdP[i * M + l], kk, s);
+    }
+    sdb[l] += s;
+  }
+  __syncthreads();
+  for (int i = threadIdx.x; i < M * M; i += blockDim.x) {
+    const int r = i / M, c = i - r * M;
+    sdP[i] = c < r ? sdP[i] * sb[c] : 0.f;
+  }
+  __syncthreads();
+  bgemm<false, false>(M, dk, M, sdP, M, sK, dk, sdK, dk, true);   // dK += dKK K
+  bgemm<true, false>(M, dk, M, sdP, M, sK, dk, sdK, dk, true);    // dK += dKK^T K
+  const size_t tok0 = (size_t)ck.bh * p.T_ + ck.t0;
+  E* dQ = p.dQ + tok0 * dk;
+  E* dK = p.dK + tok0 * nh * dk;
+  E* dV = p.dV + tok0 * nh * dv;
+  E* db = p.dbeta + tok0 * nh;
+  for (int i = threadIdx.x; i < Ct * dk; i += blockDim.x) dQ[i] = from_f32<E>(sdQ[i]);
+  for (int i = threadIdx.x; i < M * dk; i += blockDim.x) dK[i] = from_f32<E>(sdK[i]);
+  for (int i = threadIdx.x; i < M * dv; i += blockDim.x) dV[i] = from_f32<E>(sdU[i]);
+  for (int i = threadIdx.x; i < M; i += blockDim.x) db[i] = from_f32<E>(sdb[i]);
+}
+
+// ---------------------------------------------------------------- launch --
+
+constexpr size_t kPrepassSmem =
+    (kMaxM * kMaxD + kMaxM + kMaxM * kMaxM + kMaxM * 2 * kMaxD + 2 * kMaxD * kMaxD) * 4;
+constexpr size_t kReadoutSmem =
+    (3 * kMaxM * kMaxD + kMaxM + kMaxD * kMaxD + 2 * kMaxM * kMaxM + kMaxM * kMaxD) * 4;
+constexpr size_t kStateSmem = 3 * kMaxD * kMaxD * 4;
+constexpr size_t kBwdESmem =
+    (3 * kMaxM * kMaxD + kMaxM + 2 * kMaxM * kMaxM + kMaxM * kMaxD + kMaxD * kMaxD) * 4;
+constexpr size_t kBwdGSmem =
+    (7 * kMaxM * kMaxD + 2 * kMaxM + 2 * kMaxD * kMaxD + 4 * kMaxM * kMaxM) * 4;
+static_assert(kBwdGSmem <= 227 * 1024, "backward-grads tiles exceed shared memory");
+
+struct Geometry {
+  int nchunks;
+  size_t ac, hb;  // floats per (b, h) of A_c and of Hbound / B_c / E_c / dSo
+};
+
+inline bool geometry(long long B, int H, long long T, int nh, int dk, int dv, int C, Geometry* g) {
+  if (B < 0 || H < 0 || T < 0 || nh < 1 || C < 1 || dk < 1 || dv < 1) return false;
+  if (nh * C > kMaxM || dk > kMaxD || dv > kMaxD) return false;
+  g->nchunks = (int)((T + C - 1) / C);
+  g->ac = (size_t)g->nchunks * dk * dk;
+  g->hb = (size_t)g->nchunks * dk * dv;
+  return true;
+}
+
+template <class K>
+int launch(K kernel, dim3 grid, size_t smem, cudaStream_t st, void** args) {
+  MGS_CUDA_OK(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+  MGS_CUDA_OK(cudaLaunchKernel((const void*)kernel, grid, dim3(kThreads), args, smem, st));
+  return MGS_OK;
+}
+
+template <typename E>
+int run(bool fwd, Args<E> p, long long B, int H, long long T, int nh, int dk, int dv, int C,
+        float* saved, void* ws, size_t ws_bytes, cudaStream_t st) {
+  Geometry g;
+  if (!geometry(B, H, T, nh, dk, dv, C, &g)) return MGS_UNSUPPORTED;
+  const long long BH = B * (long long)H;
+  p.T_ = T;
+  p.H = H;
+  p.nh = nh;
+  p.dk = dk;
+  p.dv = dv;
+  p.C = C;
+  p.nchunks = g.nchunks;
+  if (BH == 0) return MGS_OK;
+  if (saved == nullptr) return MGS_BAD_SHAPE;
+  // saved (kept from forward to backward): A_c then Hbound
+  p.Ac = saved;
+  p.Hb = saved + BH * g.ac;
+  float* scratch = static_cast<float*>(ws);
+  if (ws == nullptr || ws_bytes < (size_t)BH * 2 * g.hb * sizeof(float)) return MGS_WORKSPACE_TOO_SMALL;
+  if (fwd) {
+    p.Bc = scratch;
+    if (T == 0) {
+      MGS_CUDA_OK(cudaMemcpyAsync(p.HT, p.H0, (size_t)BH * dk * dv * sizeof(float),
+                                  cudaMemcpyDeviceToDevice, st));
+      return MGS_OK;
+    }
+    void* a1[] = {&p};
+    int rc = launch(fwd_prepass_kernel<E>, dim3(g.nchunks, (unsigned)BH), kPrepassSmem, st, a1);
+    if (rc != MGS_OK) return rc;
+    const float* Ac = p.Ac;
+    const float* Bc = p.Bc;
+    const float* H0 = p.H0;
+    float* Hb = p.Hb;
+    float* HT = p.HT;
+    int nc = g.nchunks;
+    void* a2[] = {&Ac, &Bc, &H0, &Hb, &HT, &nc, &dk, &dv};
+    rc = launch(state_pass_kernel, dim3((unsigned)BH), kStateSmem, st, a2);
+    if (rc != MGS_OK) return rc;
+    return launch(fwd_readout_kernel<E>, dim3(g.nchunks, (unsigned)BH), kReadoutSmem, st, a1);
+  }
+  p.Ec = scratch;
+  p.dSo = scratch + BH * g.hb;
+  if (T == 0) {
+    MGS_CUDA_OK(cudaMemcpyAsync(p.dH0, p.dHT, (size_t)BH * dk * dv * sizeof(float),
+                                cudaMemcpyDeviceToDevice, st));
+    return MGS_OK;
+  }
+  void* a1[] = {&p};
+  int rc = launch(bwd_e_kernel<E>, dim3(g.nchunks, (unsigned)BH), kBwdESmem, st, a1);
+  if (rc != MGS_OK) return rc;
+  const float* Ac = p.Ac;
+  const float* Ec = p.Ec;
+  const float* dHT = p.dHT;
+  float* dSo = p.dSo;
+  float* dH0 = p.dH0;
+  int nc = g.nchunks;
+  void* a2[] = {&Ac, &Ec, &dHT, &dSo, &dH0, &nc, &dk, &dv};
+  rc = launch(adj_pass_kernel, dim3((unsigned)BH), kStateSmem, st, a2);
+  if (rc != MGS_OK) return rc;
+  return launch(bwd_grads_kernel<E>, dim3(g.nchunks, (unsigned)BH), kBwdGSmem, st, a1);
+}
+
+}  // namespace delta
+}  // namespace mgs
+
+extern "C" {
+
+size_t mgs_delta_saved_size(int64_t B, int H, int64_t T, int nh, int dk, int dv, int chunk) {
+  mgs::delta::Geometry g;
+  if (!mgs::delta::geometry(B, H, T, nh, dk, dv, chunk, &g)) return 0;
+  return (size_t)B * H * (g.ac + g.hb) * sizeof(float);
+}
+
+size_t mgs_delta_workspace_size(int64_t B, int H, int64_t T, int nh, int dk, int dv, int chunk) {
+  mgs::delta::Geometry g;
+  if (!mgs::delta::geometry(B, H, T, nh, dk, dv, chunk, &g)) return 0;
+  const size_t n = (size_t)B * H * 2 * g.hb * sizeof(float);
+  return n < 256 ? 256 : n;
+}
+
+int mgs_delta_fwd(const void* Q, const void* K, const void* V, const void* beta, const float* H0,
+                  void* y, float* H_T, void* saved, int64_t B, int H, int64_t T, int nh, int dk,
+                  int dv, int chunk, int dtype, void* workspace, size_t workspace_bytes,
+                  void* stream) {
+  auto st = static_cast<cudaStream_t>(stream);
+#define MGS_DELTA_FWD(E)                                                                        \
+  {                                                                                             \
+    mgs::delta::Args<E> p{};                                                                    \
+    p.Q = static_cast<const E*>(Q);                                                             \
+    p.K = static_cast<const E*>(K);                                                             \
+    p.V = static_cast<const E*>(V);                                                             \
+    p.beta = static_cast<const E*>(beta);                                                       \
+    p.H0 = H0;                                                                                  \
+    p.y = static_cast<E*>(y);                                                                   \
+    p.HT = H_T;                                                                                 \
+    return mgs::delta::run<E>(true, p, B, H, T, nh, dk, dv, chunk, static_cast<float*>(saved), \
+                              workspace, workspace_bytes, st);                                  \
+  }
+  switch (dtype) {
+    case MGS_F32: MGS_DELTA_FWD(float)
+    case MGS_BF16: MGS_DELTA_FWD(__nv_bfloat16)
+    case MGS_F16: MGS_DELTA_FWD(__half)
+    default: return MGS_BAD_DTYPE;
+  }
+#undef MGS_DELTA_FWD
+}
+
+int mgs_delta_bwd(const void* Q, const void* K, const void* V, const void* beta, const void* saved,
+                  const void* dy, const float* dH_T, void* dQ, void* dK, void* dV, void* dbeta,
+                  float* dH0, int64_t B, int H, int64_t T, int nh, int dk, int dv, int chunk,
+                  int dtype, void* workspace, size_t workspace_bytes, void* stream) {
+  auto st = static_cast<cudaStream_t>(stream);
+#define MGS_DELTA_BWD(E)                                                                        \
+  {                                                                                             \
+    mgs::delta::Args<E> p{};                                                                    \
+    p.Q = static_cast<const E*>(Q);                                                             \
+    p.K = static_cast<const E*>(K);                                                             \
+    p.V = static_cast<const E*>(V);                                                             \
+    p.beta = static_cast<const E*>(beta);                                                       \
+    p.dy = static_cast<const E*>(dy);                                                           \
+    p.dHT = dH_T;                                                                               \
+    p.dQ = static_cast<E*>(dQ);                                                                 \
+    p.dK = static_cast<E*>(dK);                                                                 \
+    p.dV = static_cast<E*>(dV);                                                                 \
+    p.dbeta = static_cast<E*>(dbeta);                                                           \
+    p.dH0 = dH0;                                                                                \
+    return mgs::delta::run<E>(false, p, B, H, T, nh, dk, dv, chunk,                            \
+                              static_cast<float*>(const_cast<void*>(saved)), workspace,         \
+                              workspace_bytes, st);                                             \
+  }
+  switch (dtype) {
+    case MGS_F32: MGS_DELTA_BWD(float)
+    case MGS_BF16: MGS_DELTA_BWD(__nv_bfloat16)
+    case MGS_F16: MGS_DELTA_BWD(__half)
+    default: return MGS_BAD_DTYPE;
+  }
+#undef MGS_DELTA_BWD
+}
+
+}  // extern "C"

@@ -635,3 +635,153 @@ def angle_scan_impl(
     h, _ = _angle_scan_fwd(theta, scale, gamma, b, h0, perm, sgn, p2p,
                            int(has_scale), int(has_decay), brick, need)
     return h
+
+
+# ================================================ DeltaMinGRU chunked-WY ==
+
+
+def _delta_dims(Q, K, V):
+    Bn, H, T, dk = Q.shape
+    return Bn, H, T, K.shape[3], dk, V.shape[4]
+
+
+@torch.library.custom_op("mingru_b200::delta_fwd", mutates_args=())
+def _delta_fwd(
+    Q: torch.Tensor, K: torch.Tensor, V: torch.Tensor, beta: torch.Tensor, H0: torch.Tensor,
+    chunk_size: int,
+) -> tuple[torch.Tensor, torch.Tensor, torch.Tensor]:
+    lib = _lib.load()
+    Q, K, V, beta = (_dense(x) for x in (Q, K, V, beta))
+    H0 = _dense(H0.float())
+    Bn, H, T, nh, dk, dv = _delta_dims(Q, K, V)
+    code = _dtype_code("delta_scan", Q)
+    y = torch.empty(Bn, H, T, dv, dtype=Q.dtype, device=Q.device)
+    HT = torch.empty(Bn, H, dk, dv, dtype=torch.float32, device=Q.device)
+    saved = torch.empty(lib.mgs_delta_saved_size(Bn, H, T, nh, dk, dv, chunk_size) // 4,
+                        dtype=torch.float32, device=Q.device)
+    ws = _workspace(lib.mgs_delta_workspace_size(Bn, H, T, nh, dk, dv, chunk_size), Q.device)
+    with torch.cuda.device(Q.device):
+        st = lib.mgs_delta_fwd(
+            _ptr(Q), _ptr(K), _ptr(V), _ptr(beta), _ptr(H0), _ptr(y), _ptr(HT), _ptr(saved),
+            Bn, H, T, nh, dk, dv, chunk_size, code, _ptr(ws), ws.numel(), _stream(Q),
+        )
+    _lib.check(st, "delta_scan forward")
+    return y, HT, saved
+
+
+@_delta_fwd.register_fake
+def _(Q, K, V, beta, H0, chunk_size):
+    Bn, H, T, nh, dk, dv = _delta_dims(Q, K, V)
+    n = _lib.load().mgs_delta_saved_size(Bn, H, T, nh, dk, dv, chunk_size) // 4
+    return (Q.new_empty((Bn, H, T, dv)), Q.new_empty((Bn, H, dk, dv), dtype=torch.float32),
+            Q.new_empty((n,), dtype=torch.float32))
+
+
+@torch.library.custom_op("mingru_b200::delta_bwd", mutates_args=())
+def _delta_bwd(
+    Q: torch.Tensor, K: torch.Tensor, V: torch.Tensor, beta: torch.Tensor, saved: torch.Tensor,
+    dy: torch.Tensor, dHT: torch.Tensor, chunk_size: int,
+) -> tuple[torch.Tensor, torch.Tensor, torch.Tensor, torch.Tensor, torch.Tensor]:
+    lib = _lib.load()
+    Q, K, V, beta = (_dense(x) for x in (Q, K, V, beta))
+    dy = _dense(dy.to(Q.dtype))
+    dHT = _dense(dHT.float())
+    Bn, H, T, nh, dk, dv = _delta_dims(Q, K, V)
+    code = _dtype_code("delta_scan", Q)
+    dQ, dK, dV, db = (torch.empty_like(x) for x in (Q, K, V, beta))
+    dH0 = torch.empty(Bn, H, dk, dv, dtype=torch.float32, device=Q.device)
+    ws = _workspace(lib.mgs_delta_workspace_size(Bn, H, T, nh, dk, dv, chunk_size), Q.device)
+    with torch.cuda.device(Q.device):
+        st = lib.mgs_delta_bwd(
+            _ptr(Q), _ptr(K), _ptr(V), _ptr(beta), _ptr(saved), _ptr(dy), _ptr(dHT),
+            _ptr(dQ), _ptr(dK), _ptr(dV), _ptr(db), _ptr(dH0),
+            Bn, H, T, nh, dk, dv, chunk_size, code, _ptr(ws), ws.numel(), _stream(Q),
+        )
+    _lib.check(st, "delta_scan backward")
+    return dQ, dK, dV, db, dH0
+
+
+@_delta_bwd.register_fake
+def _(Q, K, V, beta, saved, dy, dHT, chunk_size):
+    Bn, H, T, nh, dk, dv = _delta_dims(Q, K, V)
+    return (torch.empty_like(Q), torch.empty_like(K), torch.empty_like(V), torch.empty_like(beta),
+            Q.new_empty((Bn, H, dk, dv), dtype=torch.float32))
+
+
+def _delta_setup(ctx, inputs, output):
+    Q, K, V, beta, H0, chunk_size = inputs
+    y, HT, saved = output
+    ctx.save_for_backward(Q, K, V, beta, saved)
+    ctx.chunk_size = chunk_size
+    ctx.h0_dtype = H0.dtype
+    ctx.mark_non_differentiable(saved)
+    ctx.set_materialize_grads(False)
+
+
+def _delta_backward(ctx, dy, dHT, _gsaved):
+    if torch.is_grad_enabled():
+        raise RuntimeError("delta_scan does not support second-order autograd (create_graph=True)")
+    Q, K, V, beta, saved = ctx.saved_tensors
+    if dy is None and dHT is None:
+        return None, None, None, None, None, None
+    Bn, H, T, nh, dk, dv = _delta_dims(Q, K, V)
+    if dy is None:
+        dy = torch.zeros(Bn, H, T, dv, dtype=Q.dtype, device=Q.device)
+    if dHT is None:
+        dHT = torch.zeros(Bn, H, dk, dv, dtype=torch.float32, device=Q.device)
+    dQ, dK, dV, db, dH0 = _delta_bwd(Q, K, V, beta, saved, dy, dHT, ctx.chunk_size)
+    return dQ, dK, dV, db, dH0.to(ctx.h0_dtype), None
+
+
+torch.library.register_autograd("mingru_b200::delta_fwd", _delta_backward, setup_context=_delta_setup)
+
+_DELTA_MAX_MICROSTEPS = 64
+_DELTA_MAX_D = 64
+
+
+def delta_scan_impl(
+    Q: torch.Tensor, K: torch.Tensor, V: torch.Tensor, beta: torch.Tensor, H0: torch.Tensor,
+    *, chunk_size: int,
+) -> tuple[torch.Tensor, torch.Tensor]:
+    """DeltaMinGRU chunked-WY delta rule; returns ``(y, H_T)``.
+
+    Same arguments and layout as the reference's
+    ``triton_scans.delta_scan_impl`` (``triton_scans.py:2403-2447``): ``Q``
+    ``(B, n_heads, T, d_k)``, ``K`` ``(B, n_heads, T, nh, d_k)``, ``V``
+    ``(B, n_heads, T, nh, d_v)``, ``beta`` ``(B, n_heads, T, nh)``, ``H0``
+    ``(B, n_heads, d_k, d_v)``. ``y`` ``(B, n_heads, T, d_v)`` has the inputs'
+    dtype; the state ``H_T`` is fp32 (``H0``'s dtype if that is wider).
+    Differentiable w.r.t. all five tensors. Envelope: ``nh * chunk_size <= 64``,
+    ``d_k, d_v <= 64``; fp32, bf16 or fp16 inputs (fp32 arithmetic).
+    """
+    op = "delta_scan"
+    if Q.ndim != 4 or K.ndim != 5 or V.ndim != 5 or beta.ndim != 4 or H0.ndim != 4:
+        raise ValueError(
+            f"{op}: need 4-D Q (B, n_heads, T, d_k), 5-D K (B, n_heads, T, nh, d_k), 5-D V "
+            "(B, n_heads, T, nh, d_v), 4-D beta (B, n_heads, T, nh) and 4-D H0 (B, n_heads, d_k, "
+            f"d_v); got ranks Q={Q.ndim}, K={K.ndim}, V={V.ndim}, beta={beta.ndim}, H0={H0.ndim}"
+        )
+    Bn, H, T, dk = Q.shape
+    nh, dv = K.shape[3], V.shape[4]
+    if (K.shape[:3] != (Bn, H, T) or K.shape[4] != dk or V.shape[:3] != (Bn, H, T)
+            or V.shape[3] != nh or tuple(beta.shape) != (Bn, H, T, nh)
+            or tuple(H0.shape) != (Bn, H, dk, dv)):
+        raise ValueError(
+            f"{op}: shapes disagree: from Q={tuple(Q.shape)} expected K={(Bn, H, T, nh, dk)}, "
+            f"V={(Bn, H, T, nh, dv)}, beta={(Bn, H, T, nh)}, H0={(Bn, H, dk, dv)}; got "
+            f"K={tuple(K.shape)}, V={tuple(V.shape)}, beta={tuple(beta.shape)}, H0={tuple(H0.shape)}"
+        )
+    if chunk_size < 1 or nh * chunk_size > _DELTA_MAX_MICROSTEPS or dk > _DELTA_MAX_D \
+            or dv > _DELTA_MAX_D:
+        raise ValueError(
+            f"{op}: outside the kernel envelope: need nh * chunk_size <= {_DELTA_MAX_MICROSTEPS} and "
+            f"d_k, d_v <= {_DELTA_MAX_D} (got nh={nh}, chunk_size={chunk_size}, d_k={dk}, d_v={dv})"
+        )
+    _require_cuda(op, Q, K, V, beta, H0)
+    if any(x.dtype != Q.dtype for x in (K, V, beta)):
+        raise ValueError(f"{op}: Q, K, V and beta must share a dtype")
+    _dtype_code(op, Q)
+    y, HT, _ = _delta_fwd(Q, K, V, beta, H0, int(chunk_size))
+    if H0.dtype == torch.float64:
+        HT = HT.double()
+    return y, HT
