@@ -148,6 +148,12 @@ class ScanWorkload:
         ins, cots = self.make_host(rows, seed=0)
         return [x.numpy() for x in ins], [c.numpy() for c in cots]
 
+    def sample_elems(self, rows: int) -> int:
+        return rows * self.T * self.D
+
+    def sample_desc(self, rows: int) -> str:
+        return f"{rows} of {self.B} batch rows (T={self.T}, D={self.D})"
+
     def config(self, n_gpus: int) -> dict:
         return {
             "workload": self.workload,
@@ -350,12 +356,106 @@ class AngleScanWorkload(ScanWorkload):
         oracle.angle_scan_bwd(theta, scale, gamma, h0, h, gh, perm, sgn, p2p, **kw)
 
 
+class DeltaWorkload(ScanWorkload):
+    """DeltaMinGRU chunked-WY delta rule fwd+bwd, H=8 heads,
+    d_k=d_v=64, chunk=64, nh=1, T=8192, B=8 per GPU. K ~ N(0,1) L2-normalised
+    over d_k, V, Q ~ N(0,1), beta = sigmoid(N(0,1)), H0 = 0; bf16 inputs with an
+    fp32 state (y in bf16, H_T fp32); grad_y ~ N(0,1), grad_H_T = 0."""
+
+    kernels = {"fwd": "delta_fwd (prepass+state+readout)", "bwd": "delta_bwd (E+adjoint+grads)"}
+    workload = "DeltaMinGRU chunked-WY fwd+bwd (BASELINE config 5, bf16 in / fp32 state)"
+    metric_elems_doc = "B*T*H*d_v"
+    launches_per_step = 6  # three forward kernels + three backward kernels
+
+    def __init__(self, dtype=torch.bfloat16, name="cfg5", B=8, T=8192, H=8, d=64, chunk=64):
+        super().__init__(dtype)
+        self.B, self.T, self.H, self.d, self.chunk, self.name = B, T, H, d, chunk, name
+        self.D = H * d  # elems = B*T*H*d_v
+        e = self.esize
+        # per (token, head): fwd reads Q, K, V (d each) + beta, writes y (d);
+        # bwd reads Q, K, V, beta, dy and writes dQ, dK, dV, dbeta.
+        self.fwd_bytes = (4 * d + 1) * e / d
+        self.bwd_bytes = (7 * d + 2) * e / d
+        # FLOPs of the reference chunked-WY algorithm per (b, h, chunk): fwd 3.40 M, bwd 8.90 M
+        self.flops = (3.40e6 + 8.90e6) * B * H * (T // chunk)
+
+    def make_host(self, rows, seed):
+        g = torch.Generator().manual_seed(seed)
+        H, T, d = self.H, self.T, self.d
+        Q = torch.randn(rows, H, T, d, generator=g)
+        K = torch.nn.functional.normalize(torch.randn(rows, H, T, 1, d, generator=g), dim=-1)
+        V = torch.randn(rows, H, T, 1, d, generator=g)
+        beta = torch.sigmoid(torch.randn(rows, H, T, 1, generator=g))
+        gy = torch.randn(rows, H, T, d, generator=torch.Generator().manual_seed(1234 + seed))
+        return [Q, K, V, beta], [gy, torch.zeros(rows, H, d, d)]
+
+    def device_setup(self, host, dev):
+        ins, cots = host
+        st = {"ins": [x.to(dev).requires_grad_(True) for x in ins],
+              "cots": [cots[0].to(dev), cots[1].to(dev, torch.float32)]}
+        self.H0 = torch.zeros(self.B, self.H, self.d, self.d, device=dev)
+        return st
+
+    def forward(self, Q, K, V, beta):
+        import mingru_b200 as mb
+
+        H0 = self.H0 if self.H0.shape[0] == Q.shape[0] else torch.zeros(
+            Q.shape[0], self.H, self.d, self.d, device=Q.device)
+        return mb.delta_scan_impl(Q, K, V, beta, H0, chunk_size=self.chunk)
+
+    def e2e_setup(self, host, dev):
+        ins, cots = host
+        st = super().e2e_setup((ins, [cots[0]]), dev)
+        st["dHT"] = torch.zeros(self.B, self.H, self.d, self.d, device=dev)
+        return st
+
+    def e2e_step(self, st):
+        dev = st["dev"]
+        ins = [x.to(dev, non_blocking=True).requires_grad_(True) for x in st["ins"]]
+        gy = st["cots"][0].to(dev, non_blocking=True)
+        y, HT = self.forward(*ins)
+        grads = torch.autograd.grad((y, HT), ins, (gy, st["dHT"]))
+        for o, r in zip(st["out"], [y] + list(grads)):
+            o.copy_(r.detach(), non_blocking=True)
+
+    @property
+    def h2d_bytes(self) -> int:
+        return int((self.fwd_bytes + self.esize) * self.elems)  # Q, K, V, beta, grad_y
+
+    @property
+    def d2h_bytes(self) -> int:
+        return int((self.fwd_bytes) * self.elems)  # y, dQ, dK, dV, dbeta
+
+    cpu_heads = 1  # the fp64 numpy oracle is slow: one head of one batch row per sample
+
+    def cpu_sample(self, rows: int):
+        (Q, K, V, beta), (gy, gHT) = self.make_host(rows, seed=0)
+        h = self.cpu_heads
+        return ([Q[:, :h].numpy(), K[:, :h].numpy(), V[:, :h].numpy(), beta[:, :h].numpy()],
+                [gy[:, :h].numpy(), gHT[:, :h].numpy()])
+
+    def sample_elems(self, rows: int) -> int:
+        return rows * self.cpu_heads * self.T * self.d
+
+    def sample_desc(self, rows: int) -> str:
+        return f"{rows} batch row x {self.cpu_heads} of {self.H} heads (T={self.T}, d={self.d})"
+
+    def cpu_step(self, sample):
+        from oracle import delta_oracle
+
+        (Q, K, V, beta), (gy, gHT) = sample
+        H0 = np.zeros((Q.shape[0], Q.shape[1], self.d, self.d))
+        delta_oracle.delta_forward(Q, K, V, beta, H0, self.chunk)
+        delta_oracle.delta_backward(Q, K, V, beta, H0, gy, gHT, self.chunk)
+
+
 WORKLOADS = {
     "cfg1": lambda: LogScanWorkload(),
     "cfg2": lambda: LinearScanWorkload(),
     "cfg2-bf16": lambda: LinearScanWorkload(dtype=torch.bfloat16, name="cfg2-bf16"),
     "cfg3": lambda: MatrixScanWorkload(),
     "cfg4": lambda: AngleScanWorkload(),
+    "cfg5": lambda: DeltaWorkload(),
 }
 
 
@@ -493,10 +593,11 @@ def time_cpu_baseline(w, target_s: float = 12.0) -> dict:
         w.cpu_step(sample)
         times.append(time.perf_counter() - t0)
     dt = min(times)
-    elems = rows * w.T * w.D
+    elems = w.sample_elems(rows)
     return {"value": elems / dt / 1e9, "unit": "Gelem/s", "cores": threads, "kind": "port",
-            "sample": f"{rows} of {w.B} batch rows (T={w.T}, D={w.D}) fwd+bwd, fp32 C oracle "
-                      f"(OpenMP {threads} threads), best of 2 after 1 warm-up"}
+            "sample": f"{w.sample_desc(rows)} fwd+bwd through the CPU oracle "
+                      f"(restatement of the reference algorithm, {threads} threads), "
+                      "best of 2 after 1 warm-up"}
 
 
 
@@ -514,7 +615,7 @@ def run_reference(args, w) -> None:
     for _ in range(args.steps):
         w.cpu_step(sample)
     dt = (time.perf_counter() - t0) / args.steps
-    elems = rows * w.T * w.D
+    elems = w.sample_elems(rows)
     val = elems / dt / 1e9
     line = {
         "impl": "reference", "metric": "scan fwd+bwd Gelem/s", "value": val, "unit": "Gelem/s",
@@ -523,9 +624,9 @@ def run_reference(args, w) -> None:
         "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded, BASELINE shapes)",
         "config": w.config(args.gpus),
         "cpu_baseline": {"value": val, "unit": "Gelem/s", "cores": threads, "kind": "port",
-                         "sample": f"{rows} of {w.B} batch rows per step (T={w.T}, D={w.D}); "
-                                   "sequential fp32 C restatement of the reference algorithm "
-                                   f"(oracle/scan_oracle.c), OpenMP {threads} threads"},
+                         "sample": f"{w.sample_desc(rows)} per step; CPU restatement of the "
+                                   "reference algorithm (oracle/), "
+                                   f"{threads} threads"},
         "e2e": {"value": val, "unit": "Gelem/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
@@ -659,6 +760,7 @@ def run_ours(args, w) -> None:
         "dtype": "f32",
         "data": "synthetic (seeded, BASELINE shapes)",
         "config": dict(w.config(world), step="cuda-graph replay" if not args.no_graph else "eager"),
+        "tflops": (w.flops / (per_step_ms * 1e-3) / 1e12) if hasattr(w, "flops") else None,
         "kernel_ms": {"fwd": fwd_ms, "bwd": bwd_ms},
         "roofline": {
             "bound": "hbm",
