@@ -86,6 +86,27 @@ int mgs_linear_scan_bwd(const void* a, const void* b, const void* gA,
                         void* db, int64_t B, int64_t T, int64_t D, int dtype,
                         void* workspace, size_t workspace_bytes, void* stream);
 
+/* Size of the fixed device scratch behind mgs_linear_scan_fwd_noalloc. */
+#define MGS_NOALLOC_SCRATCH_BYTES (32u << 20)
+
+/* linear_scan forward that allocates nothing. No counterpart in the reference
+ * (which has no C ABI); it exists for callers that cannot hand the library a
+ * workspace -- code inside a region where allocation is forbidden or would
+ * synchronise (a latency-critical serving loop, a pre-reserved memory pool,
+ * an FFI host with no device allocator of its own). Same arguments and
+ * results as mgs_linear_scan_fwd minus the workspace: the look-back scratch
+ * lives in a file-scope device array of MGS_NOALLOC_SCRATCH_BYTES that every
+ * GPU which loads the library keeps until the process exits.
+ *  - The first call on a device resolves that array's device address (with
+ *    the device current); make that first call before any stream capture.
+ *  - Every call on a device shares the one array; the call clears what must
+ *    start at zero. Calls whose executions overlap on the GPU (other streams,
+ *    other host threads) race on it: serialise them.
+ *  - Shapes whose scratch would exceed MGS_NOALLOC_SCRATCH_BYTES return
+ *    MGS_WORKSPACE_TOO_SMALL (use mgs_linear_scan_fwd for those). */
+int mgs_linear_scan_fwd_noalloc(const void* a, const void* b, void* A, void* Bc, void* carries,
+                                int64_t B, int64_t T, int64_t D, int dtype, void* stream);
+
 /* ------------------------------------------------------------------------ */
 /* parallel_scan_log: h_t = a_t h_{t-1} + b_t in log space, a_t =
  * exp(log_coeffs[:, t-1]), b_t = exp(log_values[:, t]), h_0 =

@@ -761,6 +761,37 @@ int dispatch(bool fwd, const void* a, const void* b, void* A, void* Bc, const vo
 
 unsigned take_error_linear(cudaStream_t s) { return take_sticky_error(s); }
 
+// ------------------------------------------------ allocation-free variant --
+//
+// Scratch for mgs_linear_scan_fwd_noalloc: one fixed array per device, part
+// of the library's device image, so the entry point needs no allocation.
+// Host code cannot use `g_noalloc_scratch` as a device address (on the host
+// the name is only a stand-in); the device address comes from
+// cudaGetSymbolAddress, resolved once per device with that device current.
+static __device__ __align__(256) unsigned char g_noalloc_scratch[MGS_NOALLOC_SCRATCH_BYTES];
+
+namespace {
+constexpr int kMaxDevices = 64;
+void* g_scratch_addr[kMaxDevices] = {};
+
+void* noalloc_scratch_address() {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) {
+    (void)cudaGetLastError();
+    return nullptr;
+  }
+  void* addr = __atomic_load_n(&g_scratch_addr[dev], __ATOMIC_ACQUIRE);
+  if (addr == nullptr) {
+    if (cudaGetSymbolAddress(&addr, g_noalloc_scratch) != cudaSuccess) {
+      (void)cudaGetLastError();
+      return nullptr;
+    }
+    __atomic_store_n(&g_scratch_addr[dev], addr, __ATOMIC_RELEASE);
+  }
+  return addr;
+}
+}  // namespace
+
 }  // namespace mgs
 
 extern "C" {
@@ -791,6 +822,20 @@ int mgs_linear_scan_bwd(const void* a, const void* b, const void* gA, const void
   return mgs::linear::dispatch(false, a, b, nullptr, nullptr, gA, gBc, da, db,
                                const_cast<void*>(carries), B, T, D, dtype, workspace,
                                workspace_bytes, static_cast<cudaStream_t>(stream));
+}
+
+int mgs_linear_scan_fwd_noalloc(const void* a, const void* b, void* A, void* Bc, void* carries,
+                                int64_t B, int64_t T, int64_t D, int dtype, void* stream) {
+  if (mgs::dtype_size(dtype) == 0) return MGS_BAD_DTYPE;
+  if (B < 0 || T < 0 || D < 0) return MGS_BAD_SHAPE;
+  const auto g = mgs::linear::geometry(B, T, D, dtype);
+  if (mgs::linear::workspace_bytes(g) > (size_t)MGS_NOALLOC_SCRATCH_BYTES)
+    return MGS_WORKSPACE_TOO_SMALL;  // shape too large for the fixed scratch: use mgs_linear_scan_fwd
+  void* scratch = mgs::noalloc_scratch_address();
+  if (scratch == nullptr) return MGS_LAUNCH_FAILED;
+  return mgs::linear::dispatch(true, a, b, A, Bc, nullptr, nullptr, nullptr, nullptr, carries, B,
+                               T, D, dtype, scratch, (size_t)MGS_NOALLOC_SCRATCH_BYTES,
+                               static_cast<cudaStream_t>(stream));
 }
 
 }  // extern "C"
