@@ -7,6 +7,17 @@ B200 kernels of ``libmingru_scan.so`` through its C ABI
 fallback: CPU tensors raise.
 """
 
+from .modules import (
+    DeltaMinGRU,
+    GivensMinGRU,
+    MinGRU,
+    MinGRUBlock,
+    MinGRUStack,
+    RotationMinGRU,
+    SignedMinGRU,
+    g,
+    log_g,
+)
 from .scan_ops import (
     delta_scan_impl,
     angle_scan_impl,
@@ -22,6 +33,13 @@ from .scan_ops import (
 __version__ = "0.1.0"
 
 __all__ = [
+    "MinGRU",
+    "SignedMinGRU",
+    "RotationMinGRU",
+    "GivensMinGRU",
+    "DeltaMinGRU",
+    "MinGRUBlock",
+    "MinGRUStack",
     "delta_scan_impl",
     "angle_scan_impl",
     "brickwall_meta",

@@ -20,6 +20,9 @@ Cases and the reference code each one exercises:
   delta_*    DeltaMinGRU._forward_chunked (min_gru.py:3152-3255) through the
              raw-tensor shim the reference's own parity harness uses
              (triton_scans.py:3383-3451)
+  module_*   whole reference modules (MinGRU ... MinGRUStack, min_gru.py:1213-4336)
+             built with a seed: constructor kwargs, state_dict, input, output
+             and the gradients w.r.t. the input and every parameter
 Every case stores the inputs, the outputs and the gradients of
 ``sum(out * cotangent)`` w.r.t. every input, with a seeded cotangent.
 """
@@ -199,6 +202,59 @@ def main() -> None:
         (gy, gHT), (dQ, dK, dV, dbeta, dH0) = grads([y, HT], [Q, K, V, beta, H0], 1234)
         save(name, Q=Q, K=K, V=V, beta=beta, H0=H0, y=y, H_T=HT, grad_y=gy, grad_H_T=gHT,
              dQ=dQ, dK=dK, dV=dV, dbeta=dbeta, dH0=dH0, chunk=torch.tensor(chunk))
+
+    # ------------------------------------------------------------ modules
+    import json
+
+    module_cases = {
+        "module_mingru": ("MinGRU", dict(input_size=8, hidden_size=16, learnable_h0=True), False),
+        "module_mingru_decay": ("MinGRU", dict(input_size=8, hidden_size=16, decay="learnable",
+                                                decay_rate=0.5), True),
+        "module_signed": ("SignedMinGRU", dict(input_size=8, hidden_size=16, coupled=True,
+                                                learnable_h0=True, decay="fixed"), True),
+        "module_rotation": ("RotationMinGRU", dict(input_size=8, hidden_size=16, decay="fixed"), True),
+        "module_rotation_nosnap": ("RotationMinGRU", dict(input_size=8, hidden_size=12, snap=None), False),
+        "module_givens": ("GivensMinGRU", dict(input_size=8, hidden_size=32, block_size=8, rounds=3,
+                                               decay="learnable"), True),
+        "module_givens_k4": ("GivensMinGRU", dict(input_size=8, hidden_size=16, block_size=4,
+                                                  rounds=2), False),
+        "module_delta": ("DeltaMinGRU", dict(input_size=8, hidden_size=32, n_heads=2, chunk_size=8), False),
+        "module_stack_mixed": ("MinGRUStack", dict(input_size=6, d_model=16, n_layers=3,
+                                                   mixer=["log", "signed", "givens"],
+                                                   mixer_kwargs={"givens": {"block_size": 4,
+                                                                            "rounds": 2}}), False),
+        "module_stack_delta": ("MinGRUStack", dict(input_size=8, d_model=16, n_layers=2,
+                                                   mixer=["delta", "rotation"],
+                                                   mixer_kwargs={"delta": {"n_heads": 2,
+                                                                           "chunk_size": 16}}), False),
+    }
+    for name, (cls_name, kwargs, use_dt) in module_cases.items():
+        torch.manual_seed(101)
+        mod = getattr(mg, cls_name)(**kwargs).double()
+        B, T = 3, 37
+        g = torch.Generator().manual_seed(102)
+        x = torch.randn(B, T, kwargs["input_size"], generator=g, dtype=dt).requires_grad_(True)
+        dtv = (torch.rand(B, T, generator=g, dtype=dt) * 2) if use_dt else None
+        if cls_name == "MinGRUStack":
+            out, _ = mod(x)
+        elif cls_name == "DeltaMinGRU":
+            out = mod(x)
+        else:
+            out = mod(x, None, dtv)
+        cot = torch.randn(out.shape, generator=torch.Generator().manual_seed(1234), dtype=dt)
+        params = list(mod.named_parameters())
+        grads = torch.autograd.grad((out * cot).sum(), [x] + [p for _, p in params],
+                                    allow_unused=True)
+        arrays = {"x": x, "out": out, "cot": cot, "dx": grads[0]}
+        if dtv is not None:
+            arrays["delta_t"] = dtv
+        for (pn, pv), gp in zip(params, grads[1:]):
+            arrays["grad." + pn] = torch.zeros_like(pv) if gp is None else gp
+        for k, v in mod.state_dict().items():
+            arrays["sd." + k] = v
+        np.savez_compressed(HERE / f"{name}.npz",
+                            meta=np.array(json.dumps({"cls": cls_name, "kwargs": kwargs})),
+                            **{k: _np(v) for k, v in arrays.items()})
 
     print(f"wrote {len(list(HERE.glob('*.npz')))} fixtures to {HERE}")
 

@@ -1,0 +1,74 @@
+"""Drop-in checks of the module layer that need no GPU: every reference
+module's state_dict (from the golden fixtures) loads strictly into the
+corresponding mingru_b200 module built with the same constructor kwargs,
+same-seed construction reproduces the reference's initial weights, and the
+constructor / spec validation matches the reference's errors."""
+
+from __future__ import annotations
+
+import json
+
+import numpy as np
+import pytest
+import torch
+
+from conftest import golden_names, load_golden
+
+
+def build(meta):
+    import mingru_b200 as mb
+
+    return getattr(mb, meta["cls"])(**meta["kwargs"])
+
+
+@pytest.mark.parametrize("name", golden_names("module_"))
+def test_state_dict_loads_strictly(name):
+    g = load_golden(name)
+    meta = json.loads(str(g["meta"]))
+    mod = build(meta).double()
+    sd = {k[3:]: torch.from_numpy(v) for k, v in g.items() if k.startswith("sd.")}
+    mod.load_state_dict(sd, strict=True)
+    assert list(mod.state_dict().keys()) == list(sd.keys())  # same names, same order
+
+
+@pytest.mark.parametrize("name", golden_names("module_"))
+def test_same_seed_same_init(name):
+    g = load_golden(name)
+    meta = json.loads(str(g["meta"]))
+    prev = torch.get_default_dtype()
+    torch.set_default_dtype(torch.float64)  # the fixtures were built with fp64 as default
+    try:
+        torch.manual_seed(101)
+        mod = build(meta)
+    finally:
+        torch.set_default_dtype(prev)
+    for k, v in mod.state_dict().items():
+        np.testing.assert_array_equal(v.numpy(), g["sd." + k], err_msg=k)
+
+
+def test_validation_errors():
+    import mingru_b200 as mb
+
+    with pytest.raises(ValueError, match="even hidden_size"):
+        mb.RotationMinGRU(4, 7)
+    with pytest.raises(ValueError, match="divisible by block_size"):
+        mb.GivensMinGRU(4, 10, block_size=4)
+    with pytest.raises(ValueError, match="decay must be"):
+        mb.MinGRU(4, 8, decay="nope")
+    with pytest.raises(ValueError, match="unknown mixer"):
+        mb.MinGRUBlock(8, mixer="gru")
+    with pytest.raises(ValueError, match="list length"):
+        mb.MinGRUStack(4, 8, 2, mixer=["log"])
+    with pytest.raises(ValueError, match="mixer type name"):
+        mb.MinGRUStack(4, 8, 2, mixer="log", mixer_kwargs={"signed": {}})
+    with pytest.raises(ValueError, match="requires delta_t"):
+        mb.MinGRU(4, 8, decay="fixed").step(torch.randn(2, 4))
+
+
+def test_step_runs_on_cpu_forward_does_not():
+    import mingru_b200 as mb
+
+    m = mb.MinGRU(4, 8)
+    assert m.step(torch.randn(2, 4)).shape == (2, 8)
+    with pytest.raises(ValueError, match="CUDA"):
+        m(torch.randn(2, 5, 4))
