@@ -34,6 +34,9 @@ import numpy as np  # noqa: E402
 import torch  # noqa: E402
 
 PEAKS_FALLBACK = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0}
+L2_BYTES = 126 * 1024 * 1024
+L2_FLUSH_THRESHOLD = 2 * L2_BYTES   # per-step footprint below this is timed with L2 flushes
+FLUSH_BYTES = 256 * 1024 * 1024
 
 
 def load_peaks() -> tuple[dict, str]:
@@ -123,6 +126,11 @@ class ScanWorkload:
         for o, r in zip(st["out"], list(outs) + list(grads)):
             o.copy_(r.detach(), non_blocking=True)
 
+    @property
+    def footprint_bytes(self) -> int:
+        """Bytes one fwd+bwd step touches (inputs, cotangents, outputs, grads)."""
+        return int((self.fwd_bytes + self.bwd_bytes) * self.elems)
+
     def _bytes(self, tensors) -> int:
         return sum(t.numel() for t in tensors) * self.esize
 
@@ -163,7 +171,10 @@ class ScanWorkload:
             "D": self.D,
             "elem": self.metric_elems_doc,
             "input_dtype": str(self.dtype).replace("torch.", ""),
-            "l2": f"inputs {self.elems * self.esize / 1e6:.0f} MB per tensor vs 126 MB L2; no flush",
+            "l2": (f"step footprint {self.footprint_bytes / 1e6:.0f} MB > 2 x 126 MB L2: no flush"
+                   if self.footprint_bytes >= L2_FLUSH_THRESHOLD else
+                   f"step footprint {self.footprint_bytes / 1e6:.0f} MB fits L2: each step timed "
+                   "alone after writing a 256 MB buffer"),
             "parallelism": f"batch-sharded x{n_gpus}, no collective",
         }
 
@@ -575,9 +586,21 @@ def max_over_ranks(x: float, world: int, dev) -> float:
     return float(t.item())
 
 
+def host_threads() -> int:
+    """All host cores this process may run on; also applied to the oracle and torch."""
+    try:
+        n = len(os.sched_getaffinity(0))
+    except AttributeError:
+        n = os.cpu_count() or 1
+    from oracle import oracle
+
+    n = oracle.set_threads(n)
+    torch.set_num_threads(n)
+    return n
+
+
 def time_cpu_baseline(w, target_s: float = 12.0) -> dict:
-    threads = os.cpu_count() or 1
-    os.environ.setdefault("OMP_NUM_THREADS", str(threads))
+    threads = host_threads()
     rows = 1
     sample = w.cpu_sample(rows)
     w.cpu_step(sample)  # first call also loads the oracle library
@@ -605,8 +628,7 @@ def run_reference(args, w) -> None:
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return
-    threads = os.cpu_count() or 1
-    os.environ.setdefault("OMP_NUM_THREADS", str(threads))
+    threads = host_threads()
     rows = max(1, min(w.B, args.ref_rows))
     sample = w.cpu_sample(rows)
     for _ in range(args.warmup):
@@ -646,11 +668,22 @@ def capture(fn, dev, warm: int = 2, stream=None):
     return g, keep
 
 
-def time_graph(g, reps: int, dev) -> float:
-    """Average device ms per replay of graph g (events on the replay stream)."""
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+def time_graph(g, reps: int, dev, flush=None) -> float:
+    """Average device ms per replay of graph g (events on the replay stream);
+    with `flush`, each replay is timed alone after overwriting L2."""
     g.replay()
     torch.cuda.synchronize(dev)
+    if flush is not None:
+        evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+               for _ in range(reps)]
+        for i, (a, b) in enumerate(evs):
+            flush.fill_(i & 255)
+            a.record()
+            g.replay()
+            b.record()
+        torch.cuda.synchronize(dev)
+        return sum(a.elapsed_time(b) for a, b in evs) / reps
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record()
     for _ in range(reps):
         g.replay()
@@ -679,22 +712,34 @@ def run_ours(args, w) -> None:
     if not args.no_graph:
         graph, _keep = capture(lambda: w.step(st), dev)
 
+    # Inputs smaller than L2 would be served from cache on back-to-back steps:
+    # then every step is timed alone, after writing a buffer larger than L2.
+    flush = None
+    if w.footprint_bytes < L2_FLUSH_THRESHOLD:
+        flush = torch.empty(FLUSH_BYTES, dtype=torch.uint8, device=dev)
+    run_step = (graph.replay if graph is not None else (lambda: w.step(st)))
     start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+           for _ in range(args.steps)] if flush is not None else []
     barrier(world, dev)
     torch.cuda.synchronize(dev)
     with ClockSampler(dev.index) as clk:
         clk.mark_start()
         start.record()
-        for _ in range(args.steps):
-            if graph is not None:
-                graph.replay()
-            else:
-                w.step(st)
+        for i in range(args.steps):
+            if flush is not None:
+                flush.fill_(i & 255)
+                evs[i][0].record()
+            run_step()
+            if flush is not None:
+                evs[i][1].record()
         stop.record()
         torch.cuda.synchronize(dev)
         clk.mark_stop()
     barrier(world, dev)
-    ms = max_over_ranks(start.elapsed_time(stop), world, dev)
+    local_ms = (sum(a.elapsed_time(b) for a, b in evs) if flush is not None
+                else start.elapsed_time(stop))
+    ms = max_over_ranks(local_ms, world, dev)
     mb.raise_device_error(dev)
 
     # Per-kernel device time: each op captured alone and replayed.
@@ -708,8 +753,8 @@ def run_ours(args, w) -> None:
     gb, _kb = capture(lambda: torch.autograd.grad(outs, ins, cots, retain_graph=True), dev,
                       stream=bstream)
     reps = max(10, min(200, args.steps))
-    fwd_ms = time_graph(gf, reps, dev)
-    bwd_ms = time_graph(gb, reps, dev)
+    fwd_ms = time_graph(gf, reps, dev, flush)
+    bwd_ms = time_graph(gb, reps, dev, flush)
     del gf, gb, _kf, _kb, outs, graph
 
     # ---- e2e: public API with pinned host buffers, copies inside the timed region

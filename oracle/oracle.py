@@ -38,6 +38,12 @@ def lib() -> ctypes.CDLL:
     return _lib
 
 
+def set_threads(n: int) -> int:
+    """Use n OpenMP threads in the oracle loops; returns the count in effect."""
+    lib().orc_set_threads(ctypes.c_int(int(n)))
+    return int(lib().orc_get_threads())
+
+
 def _suffix(dtype) -> str:
     dt = np.dtype(dtype)
     if dt == np.float64:

@@ -324,3 +324,14 @@ DEF_ANGLE_SCAN(double, f64)
 DEF_ANGLE_SCAN(float, f32)
 
 int orc_version(void) { return 1; }
+
+/* Thread count of the OpenMP loops (launchers such as torchrun export
+ * OMP_NUM_THREADS=1; the CPU baseline wants every host core). */
+#ifdef _OPENMP
+#include <omp.h>
+void orc_set_threads(int n) { if (n > 0) omp_set_num_threads(n); }
+int orc_get_threads(void) { return omp_get_max_threads(); }
+#else
+void orc_set_threads(int n) { (void)n; }
+int orc_get_threads(void) { return 1; }
+#endif
