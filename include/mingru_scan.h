@@ -217,8 +217,10 @@ int mgs_angle_scan_bwd(const void* theta, const void* scale, const void* gamma, 
  * `saved` (mgs_delta_saved_size bytes) is written by the forward and read by
  * the backward (chunk transitions and chunk-start states, fp32).          */
 
-size_t mgs_delta_saved_size(int64_t B, int H, int64_t T, int nh, int dk, int dv, int chunk);
-size_t mgs_delta_workspace_size(int64_t B, int H, int64_t T, int nh, int dk, int dv, int chunk);
+size_t mgs_delta_saved_size(int64_t B, int H, int64_t T, int nh, int dk, int dv, int chunk,
+                            int dtype);
+size_t mgs_delta_workspace_size(int64_t B, int H, int64_t T, int nh, int dk, int dv, int chunk,
+                                int dtype);
 
 int mgs_delta_fwd(const void* Q, const void* K, const void* V, const void* beta, const float* H0,
                   void* y, float* H_T, void* saved, int64_t B, int H, int64_t T, int nh, int dk,

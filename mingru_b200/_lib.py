@@ -57,8 +57,8 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
         _int,
         [_p, _p, _p, _p, _p, _p, _p, _p, _p, _p, _p, _p, _p, _p, _p, _p, _i64, _i64, _i64, _int,
          _int, _int, _int, _int, _int, _p, _sz, _p]),
-    "mgs_delta_saved_size": (_sz, [_i64, _int, _i64, _int, _int, _int, _int]),
-    "mgs_delta_workspace_size": (_sz, [_i64, _int, _i64, _int, _int, _int, _int]),
+    "mgs_delta_saved_size": (_sz, [_i64, _int, _i64, _int, _int, _int, _int, _int]),
+    "mgs_delta_workspace_size": (_sz, [_i64, _int, _i64, _int, _int, _int, _int, _int]),
     "mgs_delta_fwd": (
         _int,
         [_p, _p, _p, _p, _p, _p, _p, _p, _i64, _int, _i64, _int, _int, _int, _int, _int, _p, _sz,

@@ -30,39 +30,14 @@
 // All arithmetic is fp32 on CUDA cores in this version (shared-memory tiles,
 // 4x4 register-blocked products, forward / back substitution for the unit
 // triangular solves); inputs may be fp32 / bf16 / fp16.
-#include "common.cuh"
+#include "delta_args.cuh"
+
+#include <type_traits>
 
 namespace mgs {
 namespace delta {
 
 constexpr int kThreads = 256;
-constexpr int kMaxM = 64;   // nh * chunk micro-steps per chunk
-constexpr int kMaxD = 64;   // d_k, d_v
-
-template <typename E>
-struct Args {
-  const E* Q;
-  const E* K;
-  const E* V;
-  const E* beta;
-  const float* H0;
-  E* y;
-  float* HT;
-  const E* dy;
-  const float* dHT;
-  E* dQ;
-  E* dK;
-  E* dV;
-  E* dbeta;
-  float* dH0;
-  float* Ac;      // (BH, nchunks, dk, dk)  chunk transition, saved for the backward
-  float* Bc;      // (BH, nchunks, dk, dv)  chunk injection (forward scratch)
-  float* Hb;      // (BH, nchunks, dk, dv)  chunk-start states, saved for the backward
-  float* Ec;      // (BH, nchunks, dk, dv)  backward scratch
-  float* dSo;     // (BH, nchunks, dk, dv)  gradient w.r.t. each chunk's output state
-  long long T_;
-  int H, nh, dk, dv, C, nchunks;
-};
 
 // C (m x n, ldc) = (acc ? C : 0) + alpha * opA (m x kk) * opB (kk x n), all in
 // shared memory; opA(i,l) = TA ? A[l*lda+i] : A[i*lda+l], opB(l,j) = TB ?
@@ -493,6 +468,10 @@ int run(bool fwd, Args<E> p, long long B, int H, long long T, int nh, int dk, in
         float* saved, void* ws, size_t ws_bytes, cudaStream_t st) {
   Geometry g;
   if (!geometry(B, H, T, nh, dk, dv, C, &g)) return MGS_UNSUPPORTED;
+  if constexpr (std::is_same_v<E, __nv_bfloat16>) {
+    if (tc_eligible(MGS_BF16, nh, dk, dv, C))
+      return run_tc(fwd, p, B, H, T, nh, dk, dv, C, saved, ws, ws_bytes, st);
+  }
   const long long BH = B * (long long)H;
   p.T_ = T;
   p.H = H;
@@ -556,16 +535,22 @@ int run(bool fwd, Args<E> p, long long B, int H, long long T, int nh, int dk, in
 
 extern "C" {
 
-size_t mgs_delta_saved_size(int64_t B, int H, int64_t T, int nh, int dk, int dv, int chunk) {
+size_t mgs_delta_saved_size(int64_t B, int H, int64_t T, int nh, int dk, int dv, int chunk,
+                            int dtype) {
   mgs::delta::Geometry g;
   if (!mgs::delta::geometry(B, H, T, nh, dk, dv, chunk, &g)) return 0;
+  if (mgs::delta::tc_eligible(dtype, nh, dk, dv, chunk))
+    return mgs::delta::tc_saved_floats(B * (int64_t)H, T, dk, dv, chunk) * sizeof(float);
   return (size_t)B * H * (g.ac + g.hb) * sizeof(float);
 }
 
-size_t mgs_delta_workspace_size(int64_t B, int H, int64_t T, int nh, int dk, int dv, int chunk) {
+size_t mgs_delta_workspace_size(int64_t B, int H, int64_t T, int nh, int dk, int dv, int chunk,
+                                int dtype) {
   mgs::delta::Geometry g;
   if (!mgs::delta::geometry(B, H, T, nh, dk, dv, chunk, &g)) return 0;
-  const size_t n = (size_t)B * H * 2 * g.hb * sizeof(float);
+  size_t n = (size_t)B * H * 2 * g.hb * sizeof(float);
+  if (mgs::delta::tc_eligible(dtype, nh, dk, dv, chunk))
+    n = mgs::delta::tc_workspace_floats(B * (int64_t)H, T, dk, dv, chunk) * sizeof(float);
   return n < 256 ? 256 : n;
 }
 

@@ -1,0 +1,829 @@
+// delta_tc.cu -- DeltaMinGRU chunked-WY delta rule on the tensor cores (bf16
+// inputs, fp32 state and accumulation).
+//
+// Same mathematics as delta.cu (reference: DeltaMinGRU._forward_chunked,
+// min_gru.py:3152-3255; backward _delta_backward_torch, triton_scans.py:
+// 473-605). Per chunk of C tokens (M = nh * C micro-steps), S the state
+// entering it, Ti = T^{-1}, T = I + strict_lower(K K^T) diag(beta):
+//   W = Ti K,  U' = Ti V,  U = U' - W S
+//   y = Q S + P U,  P = (Q K^T) diag(beta) * read_mask
+//   S' = S + K^T diag(beta) U
+// and, for the backward with dS' the gradient of the chunk's output state:
+//   dbU = K dS',  dU = P^T dy + diag(beta) dbU,  G = Ti^T dU  (= dV)
+//   dS  = dS' + Q^T dy - K^T G
+//   dQ  = dy S^T + dS_ K,            dS_ = (dy U^T) diag(beta) * read_mask
+//   dK  = diag(beta) U dS'^T + dS_^T Q - G S^T + dKK K + dKK^T K,
+//         dKK = (-G U^T) diag(beta) * strict_lower
+//   dbeta = rowsum(U * dbU) + colsum((dy U^T) * QK^T * read) + colsum((-G U^T) * KK^T * strict)
+//
+// Kernels (all 64 x 64 chunk products are bf16 mma.sync with split hi/lo
+// operands, mma_bf16.cuh; Ti by blocked substitution in fp32):
+//   fwd_kernel        one CTA per (b, h, value-column split): walks the chunks
+//                     in order with the state slice in registers; writes y,
+//                     H_T and every chunk-start state (saved for the backward).
+//   bwd_chain_kernel  one CTA per (b, h, split): walks the chunks in reverse,
+//                     carrying dS; writes dS' of every chunk and dH0.
+//   bwd_grads_kernel  one CTA per (b, h, chunk): every gradient of the chunk
+//                     from its saved S and dS'.
+// Inputs are staged with cp.async (next chunk prefetched during the current
+// one in the two chunk-serial kernels); out-of-range rows and columns are
+// zero-filled, which makes every padded product exact (a zero K row gives an
+// identity row of T, a zero U row and no state update).
+#include "delta_args.cuh"
+#include "mma_bf16.cuh"
+
+namespace mgs {
+namespace delta {
+namespace {
+
+using bf16 = __nv_bfloat16;
+using tc::kLd;
+using tc::Op;
+
+constexpr int kTcThreads = 256;
+constexpr int kTile = 64 * kLd;            // bf16 elements of one 64 x 64 tile
+constexpr int kTileBytes = kTile * 2;      // 9216
+constexpr int kTld = 66;                   // fp32 leading dimension of T / T^{-1}
+constexpr int kF32Bytes = 64 * kTld * 4;   // 16896
+constexpr int kYsBytes = 3 * 256 * 4;      // inverse scratch
+constexpr int kStageBytes = 3 * kTileBytes + 256;  // 3 tiles + beta[64] (fp32)
+
+__device__ __forceinline__ void cp_async16(void* dst, const void* src, int src_bytes) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;\n" ::"r"(tc::smem_addr(dst)),
+               "l"(src), "r"(src_bytes)
+               : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() {
+  asm volatile("cp.async.commit_group;\n" ::: "memory");
+}
+__device__ __forceinline__ void cp_async_wait_all() {
+  asm volatile("cp.async.wait_group 0;\n" ::: "memory");
+}
+
+__device__ __forceinline__ int up16(int x) { return (x + 15) & ~15; }
+
+// rows x (cols = nch * 8) bf16 block of a row-major global matrix (leading
+// dimension ld elements) into a tile; rows >= nrows / chunks >= ncols8 zero.
+__device__ __forceinline__ void stage_rows(bf16* tile, const bf16* g, long long ld, int nrows,
+                                           int nch, int valid_ch) {
+  for (int i = threadIdx.x; i < 64 * nch; i += kTcThreads) {
+    const int row = i / nch, ch = i - row * nch;
+    const bool ok = row < nrows && ch < valid_ch;
+    cp_async16(tile + row * kLd + ch * 8, ok ? g + row * ld + ch * 8 : g, ok ? 16 : 0);
+  }
+}
+
+// X = T^{-1} for T = I + strict_lower(Tf) (64 x 64, fp32, leading dim kTld).
+// Diagonal 16 x 16 blocks by forward substitution (one thread per column),
+// then the off-diagonal blocks by block distance d: X_ij = -X_ii sum_k T_ik X_kj.
+// Xf receives the lower triangle (diagonal blocks complete, upper blocks unset).
+__device__ void tri_inv64(const float* Tf, float* Xf, float* Ys) {
+  const int tid = threadIdx.x;
+  if (tid < 64) {
+    const int o = (tid >> 4) * 16, j = tid & 15;
+    float x[16];
+#pragma unroll
+    for (int i = 0; i < 16; ++i) {
+      float s = 0.f;
+#pragma unroll
+      for (int k = 0; k < i; ++k) s = fmaf(Tf[(o + i) * kTld + o + k], x[k], s);
+      x[i] = i == j ? 1.f : (i > j ? -s : 0.f);
+    }
+#pragma unroll
+    for (int i = 0; i < 16; ++i) Xf[(o + i) * kTld + o + j] = x[i];
+  }
+  __syncthreads();
+  for (int d = 1; d < 4; ++d) {
+    const int nb = 4 - d;
+    for (int e = tid; e < nb * 256; e += kTcThreads) {
+      const int b = e >> 8, r = (e >> 4) & 15, cc = e & 15, i = b + d;
+      float s = 0.f;
+      for (int k = 16 * b; k < 16 * i; ++k)
+        s = fmaf(Tf[(16 * i + r) * kTld + k], Xf[k * kTld + 16 * b + cc], s);
+      Ys[e] = s;
+    }
+    __syncthreads();
+    for (int e = tid; e < nb * 256; e += kTcThreads) {
+      const int b = e >> 8, r = (e >> 4) & 15, cc = e & 15, i = b + d;
+      float s = 0.f;
+#pragma unroll
+      for (int l = 0; l < 16; ++l)
+        s = fmaf(Xf[(16 * i + r) * kTld + 16 * i + l], Ys[(b << 8) + (l << 4) + cc], s);
+      Xf[(16 * i + r) * kTld + 16 * b + cc] = -s;
+    }
+    __syncthreads();
+  }
+}
+
+// Lower triangle of Xf (upper part zero) -> split bf16 tiles.
+__device__ void tri_to_split(const float* Xf, bf16* hi, bf16* lo) {
+  for (int i = threadIdx.x; i < 64 * 32; i += kTcThreads) {
+    const int row = i >> 5, col = (i & 31) << 1;
+    const float x0 = col <= row ? Xf[row * kTld + col] : 0.f;
+    const float x1 = col + 1 <= row ? Xf[row * kTld + col + 1] : 0.f;
+    uint32_t ph, pl;
+    tc::split_pack(x0, x1, ph, pl);
+    *reinterpret_cast<uint32_t*>(hi + row * kLd + col) = ph;
+    *reinterpret_cast<uint32_t*>(lo + row * kLd + col) = pl;
+  }
+}
+
+struct Ident {
+  __device__ float operator()(int, int, float x) const { return x; }
+};
+
+// c[nt] tile rows m0, cols n0 (fragment layout) -> fp32 global matrix (ld),
+// rows < nrows, cols < ncols.
+template <int NT>
+__device__ __forceinline__ void frag_to_global(const float (&c)[NT][4], float* g, long long ld,
+                                               int m0, int n0, int nrows, int ncols) {
+#pragma unroll
+  for (int j = 0; j < NT; ++j)
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      const int row = tc::frag_row(m0, 2 * h), col = tc::frag_col(n0, j, 0);
+      if (row < nrows && col < ncols)
+        *reinterpret_cast<float2*>(g + row * ld + col) = make_float2(c[j][2 * h], c[j][2 * h + 1]);
+    }
+}
+
+template <int NT>
+__device__ __forceinline__ void frag_to_global_bf16(const float (&c)[NT][4], bf16* g, long long ld,
+                                                    int m0, int n0, int nrows, int ncols) {
+#pragma unroll
+  for (int j = 0; j < NT; ++j)
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      const int row = tc::frag_row(m0, 2 * h), col = tc::frag_col(n0, j, 0);
+      if (row < nrows && col < ncols)
+        *reinterpret_cast<uint32_t*>(g + row * ld + col) = tc::pack_bf16(c[j][2 * h], c[j][2 * h + 1]);
+    }
+}
+
+template <int NT>
+__device__ __forceinline__ void frag_from_global(float (&c)[NT][4], const float* g, long long ld,
+                                                 int m0, int n0, int nrows, int ncols) {
+#pragma unroll
+  for (int j = 0; j < NT; ++j)
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      const int row = tc::frag_row(m0, 2 * h), col = tc::frag_col(n0, j, 0);
+      float2 v = make_float2(0.f, 0.f);
+      if (row < nrows && col < ncols) v = *reinterpret_cast<const float2*>(g + row * ld + col);
+      c[j][2 * h] = v.x;
+      c[j][2 * h + 1] = v.y;
+    }
+}
+
+// ---- step 1 shared by the three kernels: T (fp32, strict lower, beta on
+// columns) from K K^T and the split P = (Q K^T) diag(beta) * read from Q K^T.
+// Optionally keeps KK and QK (fp32) for the dbeta terms. Warp w: matrix w >> 2,
+// row tile w & 3.
+__device__ __forceinline__ void build_T_P(const bf16* Kt, const bf16* Qt, const float* bs, int kd,
+                                          int nh, int Mc, float* Tf, bf16* PH, bf16* PL, float* KKf,
+                                          float* QKf) {
+  const int warp = threadIdx.x >> 5, mt = warp & 3, m0 = 16 * mt;
+  float acc[8][4];
+  tc::zero(acc);
+  if ((warp >> 2) == 0) {
+    // K K^T, tiles left of and on the diagonal
+    for (int k0 = 0; k0 < kd; k0 += 16) {
+      uint32_t a[4];
+      tc::load_a<false>(Kt, m0, k0, a);
+#pragma unroll
+      for (int j = 0; j < 8; j += 2) {
+        if (j / 2 > mt) break;
+        uint32_t b[4];
+        tc::load_b<false>(Kt, k0, 8 * j, b);
+        tc::mma(acc[j], a, b[0], b[1]);
+        tc::mma(acc[j + 1], a, b[2], b[3]);
+      }
+    }
+#pragma unroll
+    for (int j = 0; j < 8; ++j)
+#pragma unroll
+      for (int v = 0; v < 4; ++v) {
+        const int row = tc::frag_row(m0, v), col = tc::frag_col(0, j, v);
+        if (col <= row) {
+          Tf[row * kTld + col] = acc[j][v] * bs[col];
+          if (KKf) KKf[row * kTld + col] = acc[j][v];
+        }
+      }
+  } else {
+    // Q K^T over the readable columns (micro-steps of tokens <= row)
+    const int ncol = min(64, (m0 + 16) * nh);
+    for (int k0 = 0; k0 < kd; k0 += 16) {
+      uint32_t a[4];
+      tc::load_a<false>(Qt, m0, k0, a);
+#pragma unroll
+      for (int j = 0; j < 8; j += 2) {
+        if (8 * j >= ncol) break;
+        uint32_t b[4];
+        tc::load_b<false>(Kt, k0, 8 * j, b);
+        tc::mma(acc[j], a, b[0], b[1]);
+        tc::mma(acc[j + 1], a, b[2], b[3]);
+      }
+    }
+    if (QKf)
+#pragma unroll
+      for (int j = 0; j < 8; ++j)
+#pragma unroll
+        for (int v = 0; v < 4; ++v)
+          QKf[tc::frag_row(m0, v) * kTld + tc::frag_col(0, j, v)] = acc[j][v];
+    tc::store_split(acc, PH, PL, m0, 0, [&](int r, int cl, float x) {
+      return (cl < (r + 1) * nh && cl < Mc) ? x * bs[cl] : 0.f;
+    });
+  }
+}
+
+struct TcArgs {
+  const bf16* Q;
+  const bf16* K;
+  const bf16* V;
+  const bf16* beta;
+  const float* H0;
+  bf16* y;
+  float* HT;
+  const bf16* dy;
+  const float* dHT;
+  bf16* dQ;
+  bf16* dK;
+  bf16* dV;
+  bf16* dbeta;
+  float* dH0;
+  float* Hs;    // (BH, nchunks, dk, dv) chunk-start states
+  float* dHs;   // (BH, nchunks, dk, dv) gradient of each chunk's output state
+  long long T;
+  int nh, dk, dv, C, nchunks, S, dvs;
+};
+
+// ------------------------------------------------------------ forward --
+// smem: 2 stages {K, Q, V_s, beta} | Ti h/l | W h/l (T^{-1} fp32 first) | P h/l |
+//       S h/l | U h/l | bU h/l (T fp32 + inverse scratch first)
+constexpr size_t kFwdSmem = 2 * kStageBytes + 12 * (size_t)kTileBytes;
+
+template <int DVS>
+__global__ void __launch_bounds__(kTcThreads, 1) fwd_kernel(const TcArgs p) {
+  constexpr int NTV = DVS / 16;  // n-tiles of a warp's half of the value columns
+  extern __shared__ __align__(128) unsigned char smem[];
+  unsigned char* rest = smem + 2 * kStageBytes;
+  bf16* TiH = reinterpret_cast<bf16*>(rest);
+  bf16* TiL = TiH + kTile;
+  bf16* WH = TiL + kTile;
+  bf16* WL = WH + kTile;
+  bf16* PH = WL + kTile;
+  bf16* PL = PH + kTile;
+  bf16* SH = PL + kTile;
+  bf16* SL = SH + kTile;
+  bf16* UH = SL + kTile;
+  bf16* UL = UH + kTile;
+  bf16* BUH = UL + kTile;
+  bf16* BUL = BUH + kTile;
+  float* Xf = reinterpret_cast<float*>(WH);
+  float* Tf = reinterpret_cast<float*>(UH);
+  float* Ys = reinterpret_cast<float*>(reinterpret_cast<unsigned char*>(UH) + kF32Bytes);
+  auto Kt = [&](int s) { return reinterpret_cast<bf16*>(smem + s * kStageBytes); };
+  auto Qt = [&](int s) { return Kt(s) + kTile; };
+  auto Vt = [&](int s) { return Kt(s) + 2 * kTile; };
+  auto Bt = [&](int s) { return reinterpret_cast<float*>(smem + s * kStageBytes + 3 * kTileBytes); };
+
+  const int tid = threadIdx.x, warp = tid >> 5, mt = warp & 3, half = warp >> 2;
+  const int m0 = 16 * mt, n0 = half * (DVS / 2);
+  const int split = blockIdx.x % p.S;
+  const long long bh = blockIdx.x / p.S;
+  const int c0 = split * p.dvs, ncols = min(p.dvs, p.dv - c0);
+  const int kd = up16(p.dk);
+  const long long rows = p.T * p.nh;
+  const bf16* Kg = p.K + bh * rows * p.dk;
+  const bf16* Vg = p.V + bh * rows * p.dv + c0;
+  const bf16* Qg = p.Q + bh * p.T * p.dk;
+  const bf16* bg = p.beta + bh * rows;
+  bf16* yg = p.y + bh * p.T * p.dv + c0;
+  float* Hsg = p.Hs + bh * (long long)p.nchunks * p.dk * p.dv + c0;
+
+  auto stage = [&](int c, int s) {
+    const long long t0 = (long long)c * p.C;
+    const int Cc = (int)min((long long)p.C, p.T - t0), Mc = Cc * p.nh;
+    stage_rows(Kt(s), Kg + t0 * p.nh * p.dk, p.dk, Mc, 8, p.dk >> 3);
+    stage_rows(Qt(s), Qg + t0 * p.dk, p.dk, Cc, 8, p.dk >> 3);
+    stage_rows(Vt(s), Vg + t0 * p.nh * p.dv, p.dv, Mc, DVS / 8, ncols >> 3);
+    cp_async_commit();
+  };
+  auto beta_of = [&](int c) {
+    const long long r0 = (long long)c * p.C * p.nh;
+    const int Mc = (int)min((long long)p.C * p.nh, rows - r0);
+    return tid < Mc ? __bfloat162float(bg[r0 + tid]) : 0.f;
+  };
+
+  // state slice: rows m0.. of d_k, value columns n0.. of this split
+  float hs[NTV][4];
+  if (p.H0)
+    frag_from_global(hs, p.H0 + bh * p.dk * p.dv + c0, p.dv, m0, n0, p.dk, ncols);
+  else
+    tc::zero(hs);
+  tc::store_split(hs, SH, SL, m0, n0, Ident());
+  stage(0, 0);
+  if (tid < 64) Bt(0)[tid] = beta_of(0);
+  float bnext = 0.f;
+
+  for (int c = 0; c < p.nchunks; ++c) {
+    const int s = c & 1;
+    const long long t0 = (long long)c * p.C;
+    const int Cc = (int)min((long long)p.C, p.T - t0), Mc = Cc * p.nh;
+    cp_async_wait_all();
+    __syncthreads();
+    if (c + 1 < p.nchunks) {
+      stage(c + 1, s ^ 1);
+      if (tid < 64) bnext = beta_of(c + 1);
+    }
+    const bf16* K = Kt(s);
+    const bf16* Q = Qt(s);
+    const bf16* V = Vt(s);
+    const float* bs = Bt(s);
+    frag_to_global(hs, Hsg + (long long)c * p.dk * p.dv, p.dv, m0, n0, p.dk, ncols);
+
+    build_T_P(K, Q, bs, kd, p.nh, Mc, Tf, PH, PL, nullptr, nullptr);
+    __syncthreads();
+    tri_inv64(Tf, Xf, Ys);
+    tri_to_split(Xf, TiH, TiL);
+    __syncthreads();
+
+    // W = Ti K (this warp: rows m0, d_k columns 32*half..), U' = Ti V
+    {
+      float w[4][4];
+      tc::zero(w);
+      tc::gemm<4, false, true>(w, Op{TiH, TiL}, m0, Op{K, nullptr}, 32 * half, 0, m0 + 16);
+      tc::store_split(w, WH, WL, m0, 32 * half, Ident());
+    }
+    float u[NTV][4];
+    tc::zero(u);
+    tc::gemm<NTV, false, true>(u, Op{TiH, TiL}, m0, Op{V, nullptr}, n0, 0, m0 + 16);
+    __syncthreads();
+
+    // U = U' - W S
+    {
+      float ws[NTV][4];
+      tc::zero(ws);
+      tc::gemm<NTV, false, true>(ws, Op{WH, WL}, m0, Op{SH, SL}, n0, 0, kd);
+#pragma unroll
+      for (int j = 0; j < NTV; ++j)
+#pragma unroll
+        for (int v = 0; v < 4; ++v) u[j][v] -= ws[j][v];
+    }
+    tc::store_split(u, UH, UL, m0, n0, Ident());
+    tc::store_split(u, BUH, BUL, m0, n0, [&](int r, int, float x) { return x * bs[r]; });
+    __syncthreads();
+
+    // y = Q S + P U (token rows m0..)
+    {
+      float yv[NTV][4];
+      tc::zero(yv);
+      tc::gemm<NTV, false, true>(yv, Op{Q, nullptr}, m0, Op{SH, SL}, n0, 0, kd);
+      tc::gemm<NTV, false, true>(yv, Op{PH, PL}, m0, Op{UH, UL}, n0, 0,
+                                 min(64, up16((m0 + 16) * p.nh)));
+      frag_to_global_bf16(yv, yg + t0 * p.dv, p.dv, m0, n0, Cc, ncols);
+    }
+    // S += K^T (beta U) (d_k rows m0..)
+    tc::gemm<NTV, true, true>(hs, Op{K, nullptr}, m0, Op{BUH, BUL}, n0, 0, up16(Mc));
+    __syncthreads();
+    tc::store_split(hs, SH, SL, m0, n0, Ident());
+    if (tid < 64 && c + 1 < p.nchunks) Bt(s ^ 1)[tid] = bnext;
+  }
+  frag_to_global(hs, p.HT + bh * p.dk * p.dv + c0, p.dv, m0, n0, p.dk, ncols);
+}
+
+// ----------------------------------------------------- backward: chain --
+// smem: 2 stages {K, Q, dy_s, beta} | Ti h/l | P h/l | dS h/l | dU h/l (T fp32) |
+//       Gn h/l (T^{-1} fp32) | inverse scratch
+constexpr size_t kChainSmem = 2 * kStageBytes + 10 * (size_t)kTileBytes + kYsBytes;
+
+template <int DVS>
+__global__ void __launch_bounds__(kTcThreads, 1) bwd_chain_kernel(const TcArgs p) {
+  constexpr int NTV = DVS / 16;
+  extern __shared__ __align__(128) unsigned char smem[];
+  unsigned char* rest = smem + 2 * kStageBytes;
+  bf16* TiH = reinterpret_cast<bf16*>(rest);
+  bf16* TiL = TiH + kTile;
+  bf16* PH = TiL + kTile;
+  bf16* PL = PH + kTile;
+  bf16* DH = PL + kTile;
+  bf16* DL = DH + kTile;
+  bf16* dUH = DL + kTile;
+  bf16* dUL = dUH + kTile;
+  bf16* GH = dUL + kTile;
+  bf16* GL = GH + kTile;
+  float* Tf = reinterpret_cast<float*>(dUH);
+  float* Xf = reinterpret_cast<float*>(GH);
+  float* Ys = reinterpret_cast<float*>(reinterpret_cast<unsigned char*>(GL + kTile));
+  auto Kt = [&](int s) { return reinterpret_cast<bf16*>(smem + s * kStageBytes); };
+  auto Qt = [&](int s) { return Kt(s) + kTile; };
+  auto Dt = [&](int s) { return Kt(s) + 2 * kTile; };
+  auto Bt = [&](int s) { return reinterpret_cast<float*>(smem + s * kStageBytes + 3 * kTileBytes); };
+
+  const int tid = threadIdx.x, warp = tid >> 5, mt = warp & 3, half = warp >> 2;
+  const int m0 = 16 * mt, n0 = half * (DVS / 2);
+  const int split = blockIdx.x % p.S;
+  const long long bh = blockIdx.x / p.S;
+  const int c0 = split * p.dvs, ncols = min(p.dvs, p.dv - c0);
+  const int kd = up16(p.dk);
+  const long long rows = p.T * p.nh;
+  const bf16* Kg = p.K + bh * rows * p.dk;
+  const bf16* Qg = p.Q + bh * p.T * p.dk;
+  const bf16* dyg = p.dy + bh * p.T * p.dv + c0;
+  const bf16* bg = p.beta + bh * rows;
+  float* dHsg = p.dHs + bh * (long long)p.nchunks * p.dk * p.dv + c0;
+
+  auto stage = [&](int c, int s) {
+    const long long t0 = (long long)c * p.C;
+    const int Cc = (int)min((long long)p.C, p.T - t0), Mc = Cc * p.nh;
+    stage_rows(Kt(s), Kg + t0 * p.nh * p.dk, p.dk, Mc, 8, p.dk >> 3);
+    stage_rows(Qt(s), Qg + t0 * p.dk, p.dk, Cc, 8, p.dk >> 3);
+    stage_rows(Dt(s), dyg + t0 * p.dv, p.dv, Cc, DVS / 8, ncols >> 3);
+    cp_async_commit();
+  };
+  auto beta_of = [&](int c) {
+    const long long r0 = (long long)c * p.C * p.nh;
+    const int Mc = (int)min((long long)p.C * p.nh, rows - r0);
+    return tid < Mc ? __bfloat162float(bg[r0 + tid]) : 0.f;
+  };
+
+  float ds[NTV][4];
+  if (p.dHT)
+    frag_from_global(ds, p.dHT + bh * p.dk * p.dv + c0, p.dv, m0, n0, p.dk, ncols);
+  else
+    tc::zero(ds);
+  tc::store_split(ds, DH, DL, m0, n0, Ident());
+  const int last = p.nchunks - 1;
+  stage(last, 0);
+  if (tid < 64) Bt(0)[tid] = beta_of(last);
+  float bnext = 0.f;
+
+  for (int q = 0; q < p.nchunks; ++q) {
+    const int c = last - q, s = q & 1;
+    const long long t0 = (long long)c * p.C;
+    const int Cc = (int)min((long long)p.C, p.T - t0), Mc = Cc * p.nh;
+    cp_async_wait_all();
+    __syncthreads();
+    if (c > 0) {
+      stage(c - 1, s ^ 1);
+      if (tid < 64) bnext = beta_of(c - 1);
+    }
+    const bf16* K = Kt(s);
+    const bf16* Q = Qt(s);
+    const bf16* dY = Dt(s);
+    const float* bs = Bt(s);
+    frag_to_global(ds, dHsg + (long long)c * p.dk * p.dv, p.dv, m0, n0, p.dk, ncols);
+
+    build_T_P(K, Q, bs, kd, p.nh, Mc, Tf, PH, PL, nullptr, nullptr);
+    __syncthreads();
+    tri_inv64(Tf, Xf, Ys);
+    tri_to_split(Xf, TiH, TiL);
+    __syncthreads();
+
+    // dU = P^T dy + beta * (K dS')   (micro-step rows m0..)
+    {
+      float du[NTV][4], db[NTV][4];
+      tc::zero(du);
+      tc::zero(db);
+      tc::gemm<NTV, false, true>(db, Op{K, nullptr}, m0, Op{DH, DL}, n0, 0, kd);
+      tc::gemm<NTV, true, true>(du, Op{PH, PL}, m0, Op{dY, nullptr}, n0, (m0 / p.nh) & ~15,
+                                up16(Cc));
+#pragma unroll
+      for (int j = 0; j < NTV; ++j)
+#pragma unroll
+        for (int v = 0; v < 4; ++v) du[j][v] += bs[tc::frag_row(m0, v)] * db[j][v];
+      tc::store_split(du, dUH, dUL, m0, n0, Ident());
+    }
+    __syncthreads();
+    // Gn = -Ti^T dU
+    {
+      float g[NTV][4];
+      tc::zero(g);
+      tc::gemm<NTV, true, true>(g, Op{TiH, TiL}, m0, Op{dUH, dUL}, n0, m0, 64);
+      tc::store_split(g, GH, GL, m0, n0, [](int, int, float x) { return -x; });
+    }
+    __syncthreads();
+    // dS = dS' + Q^T dy + K^T Gn   (d_k rows m0..)
+    tc::gemm<NTV, true, true>(ds, Op{Q, nullptr}, m0, Op{dY, nullptr}, n0, 0, up16(Cc));
+    tc::gemm<NTV, true, true>(ds, Op{K, nullptr}, m0, Op{GH, GL}, n0, 0, up16(Mc));
+    tc::store_split(ds, DH, DL, m0, n0, Ident());
+    if (tid < 64 && c > 0) Bt(s ^ 1)[tid] = bnext;
+  }
+  frag_to_global(ds, p.dH0 + bh * p.dk * p.dv + c0, p.dv, m0, n0, p.dk, ncols);
+}
+
+// ----------------------------------------------------- backward: grads --
+// smem: K | Q | dy | V | beta, dbeta | S h/l | dS' h/l | KK f32 | QK f32 |
+//       R8 (T f32 -> U h/l) | R9 (T^{-1} f32 -> W h/l -> Gn h/l) |
+//       R10 (Ti h/l -> dKK h/l) | R11 (P h/l -> dS_ h/l) | bU h/l | dU h/l | scratch
+constexpr size_t kGradSmem = 4 * (size_t)kTileBytes + 512 + 4 * (size_t)kTileBytes +
+                             2 * (size_t)kF32Bytes + 12 * (size_t)kTileBytes + kYsBytes;
+
+__global__ void __launch_bounds__(kTcThreads, 1) bwd_grads_kernel(const TcArgs p) {
+  extern __shared__ __align__(128) unsigned char smem[];
+  bf16* K = reinterpret_cast<bf16*>(smem);
+  bf16* Q = K + kTile;
+  bf16* dY = Q + kTile;
+  bf16* V = dY + kTile;
+  float* bs = reinterpret_cast<float*>(V + kTile);
+  float* dbs = bs + 64;
+  bf16* SH = reinterpret_cast<bf16*>(dbs + 64);
+  bf16* SL = SH + kTile;
+  bf16* DH = SL + kTile;
+  bf16* DL = DH + kTile;
+  float* KKf = reinterpret_cast<float*>(DL + kTile);
+  float* QKf = KKf + 64 * kTld;
+  bf16* R8 = reinterpret_cast<bf16*>(QKf + 64 * kTld);
+  bf16* R9 = R8 + 2 * kTile;
+  bf16* R10 = R9 + 2 * kTile;
+  bf16* R11 = R10 + 2 * kTile;
+  bf16* BUH = R11 + 2 * kTile;
+  bf16* BUL = BUH + kTile;
+  bf16* dUH = BUL + kTile;
+  bf16* dUL = dUH + kTile;
+  float* Ys = reinterpret_cast<float*>(dUL + kTile);
+  float* Tf = reinterpret_cast<float*>(R8);
+  float* Xf = reinterpret_cast<float*>(R9);
+  bf16 *UH = R8, *UL = R8 + kTile;
+  bf16 *WH = R9, *WL = R9 + kTile, *GH = R9, *GL = R9 + kTile;
+  bf16 *TiH = R10, *TiL = R10 + kTile, *dKH = R10, *dKL = R10 + kTile;
+  bf16 *PH = R11, *PL = R11 + kTile, *dSH = R11, *dSL = R11 + kTile;
+
+  const int tid = threadIdx.x, warp = tid >> 5, mt = warp & 3, half = warp >> 2;
+  const int m0 = 16 * mt, n0 = 32 * half;
+  const int c = blockIdx.x % p.nchunks;
+  const long long bh = blockIdx.x / p.nchunks;
+  const long long t0 = (long long)c * p.C;
+  const int Cc = (int)min((long long)p.C, p.T - t0), Mc = Cc * p.nh;
+  const int kd = up16(p.dk), kv = up16(p.dv);
+  const long long r0 = t0 * p.nh;
+  const long long rows = p.T * p.nh;
+  const long long sofs = (bh * p.nchunks + c) * (long long)p.dk * p.dv;
+
+  stage_rows(K, p.K + (bh * rows + r0) * p.dk, p.dk, Mc, 8, p.dk >> 3);
+  stage_rows(Q, p.Q + (bh * p.T + t0) * p.dk, p.dk, Cc, 8, p.dk >> 3);
+  stage_rows(dY, p.dy + (bh * p.T + t0) * p.dv, p.dv, Cc, 8, p.dv >> 3);
+  stage_rows(V, p.V + (bh * rows + r0) * p.dv, p.dv, Mc, 8, p.dv >> 3);
+  cp_async_commit();
+  if (tid < 64) {
+    bs[tid] = tid < Mc ? __bfloat162float(p.beta[bh * rows + r0 + tid]) : 0.f;
+    dbs[tid] = 0.f;
+  }
+  // S (chunk-start state) and dS' -> split tiles (rows d_k, cols d_v)
+  for (int i = tid; i < 64 * 32; i += kTcThreads) {
+    const int row = i >> 5, col = (i & 31) << 1;
+    float2 a = make_float2(0.f, 0.f), b = make_float2(0.f, 0.f);
+    if (row < p.dk && col < p.dv) {
+      a = *reinterpret_cast<const float2*>(p.Hs + sofs + row * p.dv + col);
+      b = *reinterpret_cast<const float2*>(p.dHs + sofs + row * p.dv + col);
+    }
+    uint32_t h, l;
+    tc::split_pack(a.x, a.y, h, l);
+    *reinterpret_cast<uint32_t*>(SH + row * kLd + col) = h;
+    *reinterpret_cast<uint32_t*>(SL + row * kLd + col) = l;
+    tc::split_pack(b.x, b.y, h, l);
+    *reinterpret_cast<uint32_t*>(DH + row * kLd + col) = h;
+    *reinterpret_cast<uint32_t*>(DL + row * kLd + col) = l;
+  }
+  cp_async_wait_all();
+  __syncthreads();
+
+  build_T_P(K, Q, bs, kd, p.nh, Mc, Tf, PH, PL, KKf, QKf);
+  __syncthreads();
+  tri_inv64(Tf, Xf, Ys);
+  tri_to_split(Xf, TiH, TiL);
+  __syncthreads();
+
+  // W = Ti K, U' = Ti V (rows m0, columns n0..n0+31)
+  float u[4][4];
+  {
+    float w[4][4];
+    tc::zero(w);
+    tc::gemm<4, false, true>(w, Op{TiH, TiL}, m0, Op{K, nullptr}, n0, 0, m0 + 16);
+    tc::store_split(w, WH, WL, m0, n0, Ident());
+    tc::zero(u);
+    tc::gemm<4, false, true>(u, Op{TiH, TiL}, m0, Op{V, nullptr}, n0, 0, m0 + 16);
+  }
+  __syncthreads();
+  // U = U' - W S;  dbU = K dS';  dU = P^T dy + beta dbU;  dbeta += rowsum(U * dbU)
+  {
+    float ws[4][4], db[4][4], du[4][4];
+    tc::zero(ws);
+    tc::zero(db);
+    tc::zero(du);
+    tc::gemm<4, false, true>(ws, Op{WH, WL}, m0, Op{SH, SL}, n0, 0, kd);
+    tc::gemm<4, false, true>(db, Op{K, nullptr}, m0, Op{DH, DL}, n0, 0, kd);
+    tc::gemm<4, true, true>(du, Op{PH, PL}, m0, Op{dY, nullptr}, n0, (m0 / p.nh) & ~15, up16(Cc));
+    float rs[2] = {0.f, 0.f};
+#pragma unroll
+    for (int j = 0; j < 4; ++j)
+#pragma unroll
+      for (int v = 0; v < 4; ++v) {
+        u[j][v] -= ws[j][v];
+        rs[v >> 1] += u[j][v] * db[j][v];
+        du[j][v] += bs[tc::frag_row(m0, v)] * db[j][v];
+      }
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      rs[h] += __shfl_xor_sync(0xffffffffu, rs[h], 1);
+      rs[h] += __shfl_xor_sync(0xffffffffu, rs[h], 2);
+    }
+    if ((tid & 3) == 0) {
+      atomicAdd(&dbs[tc::frag_row(m0, 0)], rs[0]);
+      atomicAdd(&dbs[tc::frag_row(m0, 2)], rs[1]);
+    }
+    tc::store_split(u, UH, UL, m0, n0, Ident());
+    tc::store_split(u, BUH, BUL, m0, n0, [&](int r, int, float x) { return x * bs[r]; });
+    tc::store_split(du, dUH, dUL, m0, n0, Ident());
+  }
+  __syncthreads();
+  // G = Ti^T dU -> dV; Gn = -G
+  {
+    float g[4][4];
+    tc::zero(g);
+    tc::gemm<4, true, true>(g, Op{TiH, TiL}, m0, Op{dUH, dUL}, n0, m0, 64);
+    frag_to_global_bf16(g, p.dV + (bh * rows + r0) * p.dv, p.dv, m0, n0, Mc, p.dv);
+    tc::store_split(g, GH, GL, m0, n0, [](int, int, float x) { return -x; });
+  }
+  __syncthreads();
+  // warp (mat, mt): mat 0: dS_ = (dy U^T) beta * read; mat 1: dKK = (Gn U^T) beta * strict
+  {
+    float acc[8][4];
+    tc::zero(acc);
+    const bool m1 = (warp >> 2) != 0;
+    const int ncol = m1 ? min(64, m0 + 16) : min(64, (m0 + 16) * p.nh);
+    const Op A = m1 ? Op{GH, GL} : Op{dY, nullptr};
+    for (int k0 = 0; k0 < kv; k0 += 16) {
+      uint32_t ah[4], al[4];
+      tc::load_a<false>(A.hi, m0, k0, ah);
+      if (A.lo) tc::load_a<false>(A.lo, m0, k0, al);
+#pragma unroll
+      for (int j = 0; j < 8; j += 2) {
+        if (8 * j >= ncol) break;
+        uint32_t bh_[4], bl[4];
+        tc::load_b<false>(UH, k0, 8 * j, bh_);
+        tc::load_b<false>(UL, k0, 8 * j, bl);
+        tc::mma(acc[j], ah, bh_[0], bh_[1]);
+        tc::mma(acc[j + 1], ah, bh_[2], bh_[3]);
+        tc::mma(acc[j], ah, bl[0], bl[1]);
+        tc::mma(acc[j + 1], ah, bl[2], bl[3]);
+        if (A.lo) {
+          tc::mma(acc[j], al, bh_[0], bh_[1]);
+          tc::mma(acc[j + 1], al, bh_[2], bh_[3]);
+        }
+      }
+    }
+    // masked product, dbeta column terms, split store
+    float cs[8][2];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      cs[j][0] = cs[j][1] = 0.f;
+#pragma unroll
+      for (int v = 0; v < 4; ++v) {
+        const int row = tc::frag_row(m0, v), col = tc::frag_col(0, j, v);
+        const bool keep = m1 ? (col < row && col < Mc) : (col < (row + 1) * p.nh && col < Mc);
+        const float x = keep ? acc[j][v] : 0.f;
+        cs[j][v & 1] += x * (m1 ? KKf[row * kTld + col] : QKf[row * kTld + col]);
+        acc[j][v] = x * bs[col];
+      }
+    }
+#pragma unroll
+    for (int j = 0; j < 8; ++j)
+#pragma unroll
+      for (int e = 0; e < 2; ++e) {
+        float x = cs[j][e];
+        x += __shfl_xor_sync(0xffffffffu, x, 4);
+        x += __shfl_xor_sync(0xffffffffu, x, 8);
+        x += __shfl_xor_sync(0xffffffffu, x, 16);
+        if ((tid & 31) < 4) atomicAdd(&dbs[tc::frag_col(0, j, e)], x);
+      }
+    tc::store_split(acc, m1 ? dKH : dSH, m1 ? dKL : dSL, m0, 0, Ident());
+  }
+  __syncthreads();
+  // dQ (token rows m0, d_k columns n0..) = dy S^T + dS_ K
+  {
+    float dq[4][4];
+    tc::zero(dq);
+    tc::gemm<4, false, false>(dq, Op{dY, nullptr}, m0, Op{SH, SL}, n0, 0, kv);
+    tc::gemm<4, false, true>(dq, Op{dSH, dSL}, m0, Op{K, nullptr}, n0, 0,
+                             min(64, up16((m0 + 16) * p.nh)));
+    frag_to_global_bf16(dq, p.dQ + (bh * p.T + t0) * p.dk, p.dk, m0, n0, Cc, p.dk);
+  }
+  // dK (micro-step rows m0, d_k columns n0..) =
+  //   (beta U) dS'^T + dS_^T Q + Gn S^T + dKK K + dKK^T K
+  {
+    float dk[4][4];
+    tc::zero(dk);
+    tc::gemm<4, false, false>(dk, Op{BUH, BUL}, m0, Op{DH, DL}, n0, 0, kv);
+    tc::gemm<4, true, true>(dk, Op{dSH, dSL}, m0, Op{Q, nullptr}, n0, (m0 / p.nh) & ~15, up16(Cc));
+    tc::gemm<4, false, false>(dk, Op{GH, GL}, m0, Op{SH, SL}, n0, 0, kv);
+    tc::gemm<4, false, true>(dk, Op{dKH, dKL}, m0, Op{K, nullptr}, n0, 0, m0 + 16);
+    tc::gemm<4, true, true>(dk, Op{dKH, dKL}, m0, Op{K, nullptr}, n0, m0, 64);
+    frag_to_global_bf16(dk, p.dK + (bh * rows + r0) * p.dk, p.dk, m0, n0, Mc, p.dk);
+  }
+  __syncthreads();
+  if (tid < Mc) p.dbeta[bh * rows + r0 + tid] = __float2bfloat16_rn(dbs[tid]);
+}
+
+// ---------------------------------------------------------------- host --
+
+int sm_count() {
+  int dev = 0, n = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return 148;
+  if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0)
+    return 148;
+  return n;
+}
+
+// Value-column splits per (b, h) for the chunk-serial kernels: two when that
+// still fits one wave of SMs (halves each CTA's serial work), else one.
+int splits_for(long long BH, int dv) {
+  return (dv > 32 && 2 * BH <= (long long)sm_count()) ? 2 : 1;
+}
+
+template <class K>
+int launch_tc(K kernel, long long grid, size_t smem, cudaStream_t st, const TcArgs& a) {
+  MGS_CUDA_OK(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+  TcArgs args = a;
+  void* kargs[] = {&args};
+  MGS_CUDA_OK(cudaLaunchKernel((const void*)kernel, dim3((unsigned)grid), dim3(kTcThreads), kargs,
+                               smem, st));
+  return MGS_OK;
+}
+
+}  // namespace
+
+bool tc_eligible(int dtype, int nh, int dk, int dv, int C) {
+  return dtype == MGS_BF16 && nh >= 1 && C >= 1 && nh * C <= 64 && dk >= 8 && dk <= 64 &&
+         dv >= 8 && dv <= 64 && dk % 8 == 0 && dv % 8 == 0;
+}
+
+size_t tc_saved_floats(long long BH, long long T, int dk, int dv, int C) {
+  return (size_t)BH * (size_t)((T + C - 1) / C) * dk * dv;
+}
+
+size_t tc_workspace_floats(long long BH, long long T, int dk, int dv, int C) {
+  return tc_saved_floats(BH, T, dk, dv, C);
+}
+
+int run_tc(bool fwd, const Args<__nv_bfloat16>& p, long long B, int H, long long T, int nh, int dk,
+           int dv, int C, float* saved, void* ws, size_t ws_bytes, cudaStream_t st) {
+  const long long BH = B * (long long)H;
+  TcArgs a{};
+  a.Q = p.Q;
+  a.K = p.K;
+  a.V = p.V;
+  a.beta = p.beta;
+  a.H0 = p.H0;
+  a.y = p.y;
+  a.HT = p.HT;
+  a.dy = p.dy;
+  a.dHT = p.dHT;
+  a.dQ = p.dQ;
+  a.dK = p.dK;
+  a.dV = p.dV;
+  a.dbeta = p.dbeta;
+  a.dH0 = p.dH0;
+  a.T = T;
+  a.nh = nh;
+  a.dk = dk;
+  a.dv = dv;
+  a.C = C;
+  a.nchunks = (int)((T + C - 1) / C);
+  a.S = splits_for(BH, dv);
+  a.dvs = ((dv + a.S - 1) / a.S + 7) & ~7;
+  const bool narrow = a.dvs <= 32;
+  if (BH == 0) return MGS_OK;
+  if (saved == nullptr) return MGS_BAD_SHAPE;
+  a.Hs = saved;
+  if (fwd) {
+    if (T == 0) {
+      if (p.H0)
+        MGS_CUDA_OK(cudaMemcpyAsync(p.HT, p.H0, (size_t)BH * dk * dv * sizeof(float),
+                                    cudaMemcpyDeviceToDevice, st));
+      else
+        MGS_CUDA_OK(cudaMemsetAsync(p.HT, 0, (size_t)BH * dk * dv * sizeof(float), st));
+      return MGS_OK;
+    }
+    return narrow ? launch_tc(fwd_kernel<32>, BH * a.S, kFwdSmem, st, a)
+                  : launch_tc(fwd_kernel<64>, BH * a.S, kFwdSmem, st, a);
+  }
+  if (T == 0) {
+    if (p.dHT)
+      MGS_CUDA_OK(cudaMemcpyAsync(p.dH0, p.dHT, (size_t)BH * dk * dv * sizeof(float),
+                                  cudaMemcpyDeviceToDevice, st));
+    else
+      MGS_CUDA_OK(cudaMemsetAsync(p.dH0, 0, (size_t)BH * dk * dv * sizeof(float), st));
+    return MGS_OK;
+  }
+  if (ws == nullptr || ws_bytes < tc_workspace_floats(BH, T, dk, dv, C) * sizeof(float))
+    return MGS_WORKSPACE_TOO_SMALL;
+  a.dHs = static_cast<float*>(ws);
+  int rc = narrow ? launch_tc(bwd_chain_kernel<32>, BH * a.S, kChainSmem, st, a)
+                  : launch_tc(bwd_chain_kernel<64>, BH * a.S, kChainSmem, st, a);
+  if (rc != MGS_OK) return rc;
+  return launch_tc(bwd_grads_kernel, BH * a.nchunks, kGradSmem, st, a);
+}
+
+}  // namespace delta
+}  // namespace mgs

@@ -657,9 +657,9 @@ def _delta_fwd(
     code = _dtype_code("delta_scan", Q)
     y = torch.empty(Bn, H, T, dv, dtype=Q.dtype, device=Q.device)
     HT = torch.empty(Bn, H, dk, dv, dtype=torch.float32, device=Q.device)
-    saved = torch.empty(lib.mgs_delta_saved_size(Bn, H, T, nh, dk, dv, chunk_size) // 4,
+    saved = torch.empty(lib.mgs_delta_saved_size(Bn, H, T, nh, dk, dv, chunk_size, code) // 4,
                         dtype=torch.float32, device=Q.device)
-    ws = _workspace(lib.mgs_delta_workspace_size(Bn, H, T, nh, dk, dv, chunk_size), Q.device)
+    ws = _workspace(lib.mgs_delta_workspace_size(Bn, H, T, nh, dk, dv, chunk_size, code), Q.device)
     with torch.cuda.device(Q.device):
         st = lib.mgs_delta_fwd(
             _ptr(Q), _ptr(K), _ptr(V), _ptr(beta), _ptr(H0), _ptr(y), _ptr(HT), _ptr(saved),
@@ -672,7 +672,8 @@ def _delta_fwd(
 @_delta_fwd.register_fake
 def _(Q, K, V, beta, H0, chunk_size):
     Bn, H, T, nh, dk, dv = _delta_dims(Q, K, V)
-    n = _lib.load().mgs_delta_saved_size(Bn, H, T, nh, dk, dv, chunk_size) // 4
+    n = _lib.load().mgs_delta_saved_size(Bn, H, T, nh, dk, dv, chunk_size,
+                                         _dtype_code("delta_scan", Q)) // 4
     return (Q.new_empty((Bn, H, T, dv)), Q.new_empty((Bn, H, dk, dv), dtype=torch.float32),
             Q.new_empty((n,), dtype=torch.float32))
 
@@ -690,7 +691,7 @@ def _delta_bwd(
     code = _dtype_code("delta_scan", Q)
     dQ, dK, dV, db = (torch.empty_like(x) for x in (Q, K, V, beta))
     dH0 = torch.empty(Bn, H, dk, dv, dtype=torch.float32, device=Q.device)
-    ws = _workspace(lib.mgs_delta_workspace_size(Bn, H, T, nh, dk, dv, chunk_size), Q.device)
+    ws = _workspace(lib.mgs_delta_workspace_size(Bn, H, T, nh, dk, dv, chunk_size, code), Q.device)
     with torch.cuda.device(Q.device):
         st = lib.mgs_delta_bwd(
             _ptr(Q), _ptr(K), _ptr(V), _ptr(beta), _ptr(saved), _ptr(dy), _ptr(dHT),

@@ -107,6 +107,61 @@ def test_bf16_inputs_fp32_state(cuda):
         np.testing.assert_allclose(got, ref, rtol=2e-2, atol=5e-2, err_msg=key)
 
 
+def bf16_data(case, seed):
+    B, H, T, nh, dk, dv, chunk = case
+    d = make(B, H, T, nh, dk, dv, seed=seed)
+    rnd = lambda x: torch.as_tensor(x, dtype=torch.float32).to(torch.bfloat16).double().numpy()
+    for k in ("Q", "K", "V", "beta", "grad_y"):
+        d[k] = rnd(d[k])
+    return d
+
+
+# bf16 inputs run on the tensor-core kernels (d_k, d_v multiples of 8,
+# nh * chunk <= 64): value-column splits of 2 (d_v > 32, few heads) and 1
+# (many heads, or d_v <= 32), padded d_k / d_v / chunk rows, nh > 1, ragged T.
+TC_CASES = [  # (B, H, T, nh, dk, dv, chunk)
+    (1, 2, 100, 1, 64, 64, 64), (2, 1, 77, 2, 32, 32, 32), (1, 2, 130, 1, 16, 16, 16),
+    (2, 2, 19, 1, 8, 8, 8), (1, 1, 65, 1, 64, 32, 64), (1, 3, 40, 4, 8, 16, 16),
+    (1, 2, 90, 1, 48, 40, 64), (10, 8, 70, 1, 64, 64, 64), (1, 1, 1, 1, 8, 8, 64),
+]
+# The bar for bf16 inputs is rtol 2e-2 (outputs and input gradients are bf16).
+# The fp32 outputs (H_T, dH0) are held to 1e-3: the split hi/lo tensor-core
+# products keep the state chain fp32-grade, so a precision regression there
+# shows up long before the 2e-2 bar.
+BF16_TOL = dict(rtol=2e-2, atol=2e-2)
+BF16_GRAD_TOL = dict(rtol=2e-2, atol=5e-2)
+FP32_STATE_TOL = dict(rtol=1e-3, atol=1e-3)
+
+
+@pytest.mark.parametrize("case", TC_CASES)
+def test_bf16_tensor_core_vs_oracle(cuda, case):
+    d = bf16_data(case, seed=sum(case) + 1)
+    ry, rHT, rg = oracle_ref(d, case[-1])
+    y, HT, *grads = run(d, case[-1], cuda, torch.bfloat16)
+    np.testing.assert_allclose(y, ry, **BF16_TOL)
+    np.testing.assert_allclose(HT, rHT, **FP32_STATE_TOL)
+    for got, ref, key in zip(grads, rg, NAMES):
+        tol = FP32_STATE_TOL if key == "dH0" else BF16_GRAD_TOL
+        np.testing.assert_allclose(got, ref, **tol, err_msg=key)
+
+
+def test_full_length_config5_bf16(cuda):
+    """BASELINE config 5 per (b, h) at full length in its own dtype: bf16 Q/K/V/beta,
+    fp32 state, H=8, d_k=d_v=64, chunk=64, T=8192 (B=1 for the fp64 oracle)."""
+    case = (1, 8, 8192, 1, 64, 64, 64)
+    d = bf16_data(case, seed=5)
+    d["H0"][:] = 0.0
+    ry, rHT, rg = oracle_ref(d, 64)
+    y, HT, *grads = run(d, 64, cuda, torch.bfloat16)
+    np.testing.assert_allclose(y, ry, **BF16_TOL)
+    np.testing.assert_allclose(HT, rHT, **FP32_STATE_TOL)
+    for got, ref, key in zip(grads, rg, NAMES):
+        # sums over up to 8192 tokens: the absolute floor follows the gradient's magnitude
+        tol = dict(BF16_GRAD_TOL)
+        tol["atol"] = max(tol["atol"], 1e-3 * float(np.abs(ref).max()))
+        np.testing.assert_allclose(got, ref, **tol, err_msg=key)
+
+
 def test_full_length_config5_fp32(cuda):
     """BASELINE config 5 shape per (b, h) at full length: H=8, d_k=d_v=64,
     chunk=64, T=8192 (B=1 to keep the fp64 oracle quick)."""
