@@ -45,7 +45,6 @@ constexpr int kTile = 64 * kLd;            // bf16 elements of one 64 x 64 tile
 constexpr int kTileBytes = kTile * 2;      // 9216
 constexpr int kTld = 66;                   // fp32 leading dimension of T / T^{-1}
 constexpr int kF32Bytes = 64 * kTld * 4;   // 16896
-constexpr int kYsBytes = 3 * 256 * 4;      // inverse scratch
 constexpr int kStageBytes = 3 * kTileBytes + 256;  // 3 tiles + beta[64] (fp32)
 
 __device__ __forceinline__ void cp_async16(void* dst, const void* src, int src_bytes) {
@@ -62,23 +61,36 @@ __device__ __forceinline__ void cp_async_wait_all() {
 
 __device__ __forceinline__ int up16(int x) { return (x + 15) & ~15; }
 
-// rows x (cols = nch * 8) bf16 block of a row-major global matrix (leading
+// 64 rows x (NCH * 8 columns) bf16 block of a row-major global matrix (leading
 // dimension ld elements) into a tile; rows >= nrows / chunks >= ncols8 zero.
+template <int NCH>
 __device__ __forceinline__ void stage_rows(bf16* tile, const bf16* g, long long ld, int nrows,
-                                           int nch, int valid_ch) {
-  for (int i = threadIdx.x; i < 64 * nch; i += kTcThreads) {
-    const int row = i / nch, ch = i - row * nch;
+                                           int valid_ch) {
+  for (int i = threadIdx.x; i < 64 * NCH; i += kTcThreads) {
+    const int row = i / NCH, ch = i - row * NCH;
     const bool ok = row < nrows && ch < valid_ch;
     cp_async16(tile + row * kLd + ch * 8, ok ? g + row * ld + ch * 8 : g, ok ? 16 : 0);
   }
 }
 
-// X = T^{-1} for T = I + strict_lower(Tf) (64 x 64, fp32, leading dim kTld).
-// Diagonal 16 x 16 blocks by forward substitution (one thread per column),
-// then the off-diagonal blocks by block distance d: X_ij = -X_ii sum_k T_ik X_kj.
-// Xf receives the lower triangle (diagonal blocks complete, upper blocks unset).
-__device__ void tri_inv64(const float* Tf, float* Xf, float* Ys) {
-  const int tid = threadIdx.x;
+struct Ident {
+  __device__ float operator()(int, int, float x) const { return x; }
+};
+struct Neg {
+  __device__ float operator()(int, int, float x) const { return -x; }
+};
+
+// Ti = T^{-1} for the unit lower-triangular T = I + strict_lower(T) of a chunk,
+// as split bf16 tiles (X). Inputs: the strictly-lower part of T as split tiles
+// (TS) and in fp32 (Tf, only its four diagonal 16 x 16 blocks are read).
+//   1. diagonal blocks D_b^{-1} by forward substitution (one thread per column)
+//   2. X_10 = -D_1^{-1} T_10 D_0^{-1} and X_32 = -D_3^{-1} T_32 D_2^{-1} (warps 0, 1)
+//   3. X[32:64, 0:32] = -X[32:64, 32:64] (T[32:64, 0:32] X[0:32, 0:32])  (warps 0-3)
+// with every block product on the tensor cores (split operands, fp32 accumulate).
+// X's strictly-upper 16 x 16 blocks must be zero on entry (they are never
+// written); Y is scratch (two tiles).
+__device__ void tri_inv_tc(const float* Tf, Op TS, bf16* XH, bf16* XL, bf16* YH, bf16* YL) {
+  const int tid = threadIdx.x, warp = tid >> 5;
   if (tid < 64) {
     const int o = (tid >> 4) * 16, j = tid & 15;
     float x[16];
@@ -90,47 +102,70 @@ __device__ void tri_inv64(const float* Tf, float* Xf, float* Ys) {
       x[i] = i == j ? 1.f : (i > j ? -s : 0.f);
     }
 #pragma unroll
-    for (int i = 0; i < 16; ++i) Xf[(o + i) * kTld + o + j] = x[i];
+    for (int i = 0; i < 16; ++i) {
+      const bf16 h = __float2bfloat16_rn(x[i]);
+      XH[(o + i) * kLd + o + j] = h;
+      XL[(o + i) * kLd + o + j] = __float2bfloat16_rn(x[i] - __bfloat162float(h));
+    }
   }
   __syncthreads();
-  for (int d = 1; d < 4; ++d) {
-    const int nb = 4 - d;
-    for (int e = tid; e < nb * 256; e += kTcThreads) {
-      const int b = e >> 8, r = (e >> 4) & 15, cc = e & 15, i = b + d;
-      float s = 0.f;
-      for (int k = 16 * b; k < 16 * i; ++k)
-        s = fmaf(Tf[(16 * i + r) * kTld + k], Xf[k * kTld + 16 * b + cc], s);
-      Ys[e] = s;
+  const Op X{XH, XL}, Y{YH, YL};
+  if (warp < 2) {
+    const int i = 1 + 2 * warp, j = i - 1;
+    float y[2][4];
+    tc::zero(y);
+    tc::gemm<2, false, true>(y, TS, 16 * i, X, 16 * j, 16 * j, 16 * j + 16);
+    tc::store_split(y, YH, YL, 16 * i, 16 * j, Ident());
+    __syncwarp();
+    float x[2][4];
+    tc::zero(x);
+    tc::gemm<2, false, true>(x, X, 16 * i, Y, 16 * j, 16 * i, 16 * i + 16);
+    tc::store_split(x, XH, XL, 16 * i, 16 * j, Neg());
+  }
+  __syncthreads();
+  const int m0 = 32 + 16 * ((warp >> 1) & 1), n0 = 16 * (warp & 1);
+  if (warp < 4) {
+    float y[2][4];
+    tc::zero(y);
+    tc::gemm<2, false, true>(y, TS, m0, X, n0, 0, 32);
+    tc::store_split(y, YH, YL, m0, n0, Ident());
+  }
+  __syncthreads();
+  if (warp < 4) {
+    float x[2][4];
+    tc::zero(x);
+    tc::gemm<2, false, true>(x, X, m0, Y, n0, 32, 64);
+    tc::store_split(x, XH, XL, m0, n0, Neg());
+  }
+  __syncthreads();
+}
+
+// Zero the strictly-upper 16 x 16 blocks of a split tile pair (once per kernel).
+__device__ void zero_upper_blocks(bf16* H, bf16* L) {
+  for (int i = threadIdx.x; i < 64 * 64; i += kTcThreads) {
+    const int row = i >> 6, col = i & 63;
+    if ((col >> 4) > (row >> 4)) {
+      H[row * kLd + col] = __float2bfloat16_rn(0.f);
+      L[row * kLd + col] = __float2bfloat16_rn(0.f);
     }
-    __syncthreads();
-    for (int e = tid; e < nb * 256; e += kTcThreads) {
-      const int b = e >> 8, r = (e >> 4) & 15, cc = e & 15, i = b + d;
-      float s = 0.f;
-#pragma unroll
-      for (int l = 0; l < 16; ++l)
-        s = fmaf(Xf[(16 * i + r) * kTld + 16 * i + l], Ys[(b << 8) + (l << 4) + cc], s);
-      Xf[(16 * i + r) * kTld + 16 * b + cc] = -s;
-    }
-    __syncthreads();
   }
 }
 
-// Lower triangle of Xf (upper part zero) -> split bf16 tiles.
-__device__ void tri_to_split(const float* Xf, bf16* hi, bf16* lo) {
-  for (int i = threadIdx.x; i < 64 * 32; i += kTcThreads) {
-    const int row = i >> 5, col = (i & 31) << 1;
-    const float x0 = col <= row ? Xf[row * kTld + col] : 0.f;
-    const float x1 = col + 1 <= row ? Xf[row * kTld + col + 1] : 0.f;
-    uint32_t ph, pl;
-    tc::split_pack(x0, x1, ph, pl);
-    *reinterpret_cast<uint32_t*>(hi + row * kLd + col) = ph;
-    *reinterpret_cast<uint32_t*>(lo + row * kLd + col) = pl;
+// 64 x 64 bf16 tile <-> dense global 64 x 64 (16-byte vectors, all threads).
+__device__ __forceinline__ void tile_to_global(const bf16* t, bf16* g) {
+  for (int i = threadIdx.x; i < 64 * 8; i += kTcThreads) {
+    const int row = i >> 3, ch = i & 7;
+    *reinterpret_cast<uint4*>(g + row * 64 + ch * 8) =
+        *reinterpret_cast<const uint4*>(t + row * kLd + ch * 8);
+  }
+}
+__device__ __forceinline__ void tile_from_global_async(bf16* t, const bf16* g) {
+  for (int i = threadIdx.x; i < 64 * 8; i += kTcThreads) {
+    const int row = i >> 3, ch = i & 7;
+    cp_async16(t + row * kLd + ch * 8, g + row * 64 + ch * 8, 16);
   }
 }
 
-struct Ident {
-  __device__ float operator()(int, int, float x) const { return x; }
-};
 
 // c[nt] tile rows m0, cols n0 (fragment layout) -> fp32 global matrix (ld),
 // rows < nrows, cols < ncols.
@@ -175,65 +210,43 @@ __device__ __forceinline__ void frag_from_global(float (&c)[NT][4], const float*
     }
 }
 
-// ---- step 1 shared by the three kernels: T (fp32, strict lower, beta on
-// columns) from K K^T and the split P = (Q K^T) diag(beta) * read from Q K^T.
-// Optionally keeps KK and QK (fp32) for the dbeta terms. Warp w: matrix w >> 2,
-// row tile w & 3.
-__device__ __forceinline__ void build_T_P(const bf16* Kt, const bf16* Qt, const float* bs, int kd,
-                                          int nh, int Mc, float* Tf, bf16* PH, bf16* PL, float* KKf,
-                                          float* QKf) {
-  const int warp = threadIdx.x >> 5, mt = warp & 3, m0 = 16 * mt;
-  float acc[8][4];
+// ---- chunk matrices from K K^T and Q K^T (exact bf16 products, fp32 sums).
+// Warp w: row tile w & 3; warps 0-3 one product, warps 4-7 the other.
+
+// K K^T of row tile m0, the column tiles left of and on the diagonal.
+__device__ __forceinline__ void kk_rows(const bf16* Kt, int m0, int kd, float (&acc)[8][4]) {
   tc::zero(acc);
-  if ((warp >> 2) == 0) {
-    // K K^T, tiles left of and on the diagonal
-    for (int k0 = 0; k0 < kd; k0 += 16) {
-      uint32_t a[4];
-      tc::load_a<false>(Kt, m0, k0, a);
+  tc::gemm<8, false, false>(acc, Op{Kt, nullptr}, m0, Op{Kt, nullptr}, 0, 0, kd, m0 / 16 + 1);
+}
+
+// Q K^T of token row tile m0 over the readable micro-step columns.
+__device__ __forceinline__ void qk_rows(const bf16* Qt, const bf16* Kt, int m0, int kd, int nh,
+                                       float (&acc)[8][4]) {
+  tc::zero(acc);
+  tc::gemm<8, false, false>(acc, Op{Qt, nullptr}, m0, Op{Kt, nullptr}, 0, 0, kd,
+                            (min(64, (m0 + 16) * nh) + 15) / 16);
+}
+
+// P = (Q K^T) diag(beta) * read  as split tiles
+__device__ __forceinline__ void store_P(const float (&acc)[8][4], const float* bs, int nh, int Mc,
+                                        int m0, bf16* PH, bf16* PL) {
+  tc::store_split(acc, PH, PL, m0, 0, [&](int r, int cl, float x) {
+    return (cl < (r + 1) * nh && cl < Mc) ? x * bs[cl] : 0.f;
+  });
+}
+
+// T's strict lower part (K K^T diag(beta)) as fp32 (diagonal blocks) and split tiles.
+__device__ __forceinline__ void store_T(const float (&acc)[8][4], const float* bs, int m0,
+                                        float* Tf, bf16* TH, bf16* TL) {
 #pragma unroll
-      for (int j = 0; j < 8; j += 2) {
-        if (j / 2 > mt) break;
-        uint32_t b[4];
-        tc::load_b<false>(Kt, k0, 8 * j, b);
-        tc::mma(acc[j], a, b[0], b[1]);
-        tc::mma(acc[j + 1], a, b[2], b[3]);
-      }
+  for (int j = 0; j < 8; ++j)
+#pragma unroll
+    for (int v = 0; v < 4; ++v) {
+      const int row = tc::frag_row(m0, v), col = tc::frag_col(0, j, v);
+      if ((col >> 4) == (row >> 4)) Tf[row * kTld + col] = col < row ? acc[j][v] * bs[col] : 0.f;
     }
-#pragma unroll
-    for (int j = 0; j < 8; ++j)
-#pragma unroll
-      for (int v = 0; v < 4; ++v) {
-        const int row = tc::frag_row(m0, v), col = tc::frag_col(0, j, v);
-        if (col <= row) {
-          Tf[row * kTld + col] = acc[j][v] * bs[col];
-          if (KKf) KKf[row * kTld + col] = acc[j][v];
-        }
-      }
-  } else {
-    // Q K^T over the readable columns (micro-steps of tokens <= row)
-    const int ncol = min(64, (m0 + 16) * nh);
-    for (int k0 = 0; k0 < kd; k0 += 16) {
-      uint32_t a[4];
-      tc::load_a<false>(Qt, m0, k0, a);
-#pragma unroll
-      for (int j = 0; j < 8; j += 2) {
-        if (8 * j >= ncol) break;
-        uint32_t b[4];
-        tc::load_b<false>(Kt, k0, 8 * j, b);
-        tc::mma(acc[j], a, b[0], b[1]);
-        tc::mma(acc[j + 1], a, b[2], b[3]);
-      }
-    }
-    if (QKf)
-#pragma unroll
-      for (int j = 0; j < 8; ++j)
-#pragma unroll
-        for (int v = 0; v < 4; ++v)
-          QKf[tc::frag_row(m0, v) * kTld + tc::frag_col(0, j, v)] = acc[j][v];
-    tc::store_split(acc, PH, PL, m0, 0, [&](int r, int cl, float x) {
-      return (cl < (r + 1) * nh && cl < Mc) ? x * bs[cl] : 0.f;
-    });
-  }
+  tc::store_split(acc, TH, TL, m0, 0,
+                  [&](int r, int cl, float x) { return cl < r ? x * bs[cl] : 0.f; });
 }
 
 struct TcArgs {
@@ -252,14 +265,15 @@ struct TcArgs {
   bf16* dbeta;
   float* dH0;
   float* Hs;    // (BH, nchunks, dk, dv) chunk-start states
+  bf16* Ti;     // (BH, nchunks, 2, 64, 64) T^{-1} of every chunk, split hi / lo
   float* dHs;   // (BH, nchunks, dk, dv) gradient of each chunk's output state
   long long T;
   int nh, dk, dv, C, nchunks, S, dvs;
 };
 
 // ------------------------------------------------------------ forward --
-// smem: 2 stages {K, Q, V_s, beta} | Ti h/l | W h/l (T^{-1} fp32 first) | P h/l |
-//       S h/l | U h/l | bU h/l (T fp32 + inverse scratch first)
+// smem: 2 stages {K, Q, V_s, beta} | Ti h/l | W h/l (inverse scratch first) |
+//       P h/l | S h/l | U h/l (T fp32 first) | bU h/l (T split first)
 constexpr size_t kFwdSmem = 2 * kStageBytes + 12 * (size_t)kTileBytes;
 
 template <int DVS>
@@ -279,9 +293,8 @@ __global__ void __launch_bounds__(kTcThreads, 1) fwd_kernel(const TcArgs p) {
   bf16* UL = UH + kTile;
   bf16* BUH = UL + kTile;
   bf16* BUL = BUH + kTile;
-  float* Xf = reinterpret_cast<float*>(WH);
   float* Tf = reinterpret_cast<float*>(UH);
-  float* Ys = reinterpret_cast<float*>(reinterpret_cast<unsigned char*>(UH) + kF32Bytes);
+  bf16 *TH = BUH, *TL = BUL, *YH = WH, *YL = WL;
   auto Kt = [&](int s) { return reinterpret_cast<bf16*>(smem + s * kStageBytes); };
   auto Qt = [&](int s) { return Kt(s) + kTile; };
   auto Vt = [&](int s) { return Kt(s) + 2 * kTile; };
@@ -300,13 +313,14 @@ __global__ void __launch_bounds__(kTcThreads, 1) fwd_kernel(const TcArgs p) {
   const bf16* bg = p.beta + bh * rows;
   bf16* yg = p.y + bh * p.T * p.dv + c0;
   float* Hsg = p.Hs + bh * (long long)p.nchunks * p.dk * p.dv + c0;
+  bf16* Tig = p.Ti + bh * (long long)p.nchunks * 2 * 4096;
 
   auto stage = [&](int c, int s) {
     const long long t0 = (long long)c * p.C;
     const int Cc = (int)min((long long)p.C, p.T - t0), Mc = Cc * p.nh;
-    stage_rows(Kt(s), Kg + t0 * p.nh * p.dk, p.dk, Mc, 8, p.dk >> 3);
-    stage_rows(Qt(s), Qg + t0 * p.dk, p.dk, Cc, 8, p.dk >> 3);
-    stage_rows(Vt(s), Vg + t0 * p.nh * p.dv, p.dv, Mc, DVS / 8, ncols >> 3);
+    stage_rows<8>(Kt(s), Kg + t0 * p.nh * p.dk, p.dk, Mc, p.dk >> 3);
+    stage_rows<8>(Qt(s), Qg + t0 * p.dk, p.dk, Cc, p.dk >> 3);
+    stage_rows<DVS / 8>(Vt(s), Vg + t0 * p.nh * p.dv, p.dv, Mc, ncols >> 3);
     cp_async_commit();
   };
   auto beta_of = [&](int c) {
@@ -322,6 +336,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) fwd_kernel(const TcArgs p) {
   else
     tc::zero(hs);
   tc::store_split(hs, SH, SL, m0, n0, Ident());
+  zero_upper_blocks(TiH, TiL);
   stage(0, 0);
   if (tid < 64) Bt(0)[tid] = beta_of(0);
   float bnext = 0.f;
@@ -342,11 +357,22 @@ __global__ void __launch_bounds__(kTcThreads, 1) fwd_kernel(const TcArgs p) {
     const float* bs = Bt(s);
     frag_to_global(hs, Hsg + (long long)c * p.dk * p.dv, p.dv, m0, n0, p.dk, ncols);
 
-    build_T_P(K, Q, bs, kd, p.nh, Mc, Tf, PH, PL, nullptr, nullptr);
+    {
+      float acc[8][4];
+      if (half == 0) {
+        kk_rows(K, m0, kd, acc);
+        store_T(acc, bs, m0, Tf, TH, TL);
+      } else {
+        qk_rows(Q, K, m0, kd, p.nh, acc);
+        store_P(acc, bs, p.nh, Mc, m0, PH, PL);
+      }
+    }
     __syncthreads();
-    tri_inv64(Tf, Xf, Ys);
-    tri_to_split(Xf, TiH, TiL);
-    __syncthreads();
+    tri_inv_tc(Tf, Op{TH, TL}, TiH, TiL, YH, YL);
+    if (split == 0) {
+      tile_to_global(TiH, Tig + (long long)c * 8192);
+      tile_to_global(TiL, Tig + (long long)c * 8192 + 4096);
+    }
 
     // W = Ti K (this warp: rows m0, d_k columns 32*half..), U' = Ti V
     {
@@ -393,18 +419,16 @@ __global__ void __launch_bounds__(kTcThreads, 1) fwd_kernel(const TcArgs p) {
 }
 
 // ----------------------------------------------------- backward: chain --
-// smem: 2 stages {K, Q, dy_s, beta} | Ti h/l | P h/l | dS h/l | dU h/l (T fp32) |
-//       Gn h/l (T^{-1} fp32) | inverse scratch
-constexpr size_t kChainSmem = 2 * kStageBytes + 10 * (size_t)kTileBytes + kYsBytes;
+// smem: 2 stages {K, Q, dy_s, Ti h, Ti l, beta} | P h/l | dS h/l | dU h/l | Gn h/l
+constexpr int kChainStage = 5 * kTileBytes + 256;
+constexpr size_t kChainSmem = 2 * (size_t)kChainStage + 8 * (size_t)kTileBytes;
 
 template <int DVS>
 __global__ void __launch_bounds__(kTcThreads, 1) bwd_chain_kernel(const TcArgs p) {
   constexpr int NTV = DVS / 16;
   extern __shared__ __align__(128) unsigned char smem[];
-  unsigned char* rest = smem + 2 * kStageBytes;
-  bf16* TiH = reinterpret_cast<bf16*>(rest);
-  bf16* TiL = TiH + kTile;
-  bf16* PH = TiL + kTile;
+  unsigned char* rest = smem + 2 * kChainStage;
+  bf16* PH = reinterpret_cast<bf16*>(rest);
   bf16* PL = PH + kTile;
   bf16* DH = PL + kTile;
   bf16* DL = DH + kTile;
@@ -412,13 +436,12 @@ __global__ void __launch_bounds__(kTcThreads, 1) bwd_chain_kernel(const TcArgs p
   bf16* dUL = dUH + kTile;
   bf16* GH = dUL + kTile;
   bf16* GL = GH + kTile;
-  float* Tf = reinterpret_cast<float*>(dUH);
-  float* Xf = reinterpret_cast<float*>(GH);
-  float* Ys = reinterpret_cast<float*>(reinterpret_cast<unsigned char*>(GL + kTile));
-  auto Kt = [&](int s) { return reinterpret_cast<bf16*>(smem + s * kStageBytes); };
+  auto Kt = [&](int s) { return reinterpret_cast<bf16*>(smem + s * kChainStage); };
   auto Qt = [&](int s) { return Kt(s) + kTile; };
   auto Dt = [&](int s) { return Kt(s) + 2 * kTile; };
-  auto Bt = [&](int s) { return reinterpret_cast<float*>(smem + s * kStageBytes + 3 * kTileBytes); };
+  auto TiHt = [&](int s) { return Kt(s) + 3 * kTile; };
+  auto TiLt = [&](int s) { return Kt(s) + 4 * kTile; };
+  auto Bt = [&](int s) { return reinterpret_cast<float*>(smem + s * kChainStage + 5 * kTileBytes); };
 
   const int tid = threadIdx.x, warp = tid >> 5, mt = warp & 3, half = warp >> 2;
   const int m0 = 16 * mt, n0 = half * (DVS / 2);
@@ -431,14 +454,17 @@ __global__ void __launch_bounds__(kTcThreads, 1) bwd_chain_kernel(const TcArgs p
   const bf16* Qg = p.Q + bh * p.T * p.dk;
   const bf16* dyg = p.dy + bh * p.T * p.dv + c0;
   const bf16* bg = p.beta + bh * rows;
+  const bf16* Tig = p.Ti + bh * (long long)p.nchunks * 2 * 4096;
   float* dHsg = p.dHs + bh * (long long)p.nchunks * p.dk * p.dv + c0;
 
   auto stage = [&](int c, int s) {
     const long long t0 = (long long)c * p.C;
     const int Cc = (int)min((long long)p.C, p.T - t0), Mc = Cc * p.nh;
-    stage_rows(Kt(s), Kg + t0 * p.nh * p.dk, p.dk, Mc, 8, p.dk >> 3);
-    stage_rows(Qt(s), Qg + t0 * p.dk, p.dk, Cc, 8, p.dk >> 3);
-    stage_rows(Dt(s), dyg + t0 * p.dv, p.dv, Cc, DVS / 8, ncols >> 3);
+    stage_rows<8>(Kt(s), Kg + t0 * p.nh * p.dk, p.dk, Mc, p.dk >> 3);
+    stage_rows<8>(Qt(s), Qg + t0 * p.dk, p.dk, Cc, p.dk >> 3);
+    stage_rows<DVS / 8>(Dt(s), dyg + t0 * p.dv, p.dv, Cc, ncols >> 3);
+    tile_from_global_async(TiHt(s), Tig + (long long)c * 8192);
+    tile_from_global_async(TiLt(s), Tig + (long long)c * 8192 + 4096);
     cp_async_commit();
   };
   auto beta_of = [&](int c) {
@@ -471,13 +497,21 @@ __global__ void __launch_bounds__(kTcThreads, 1) bwd_chain_kernel(const TcArgs p
     const bf16* K = Kt(s);
     const bf16* Q = Qt(s);
     const bf16* dY = Dt(s);
+    const Op Ti{TiHt(s), TiLt(s)};
     const float* bs = Bt(s);
     frag_to_global(ds, dHsg + (long long)c * p.dk * p.dv, p.dv, m0, n0, p.dk, ncols);
 
-    build_T_P(K, Q, bs, kd, p.nh, Mc, Tf, PH, PL, nullptr, nullptr);
-    __syncthreads();
-    tri_inv64(Tf, Xf, Ys);
-    tri_to_split(Xf, TiH, TiL);
+    // P (token rows m0, micro-step columns 32*half..)
+    {
+      float acc[4][4];
+      tc::zero(acc);
+      const int ncol = min(64, (m0 + 16) * p.nh) - 32 * half;
+      tc::gemm<4, false, false>(acc, Op{Q, nullptr}, m0, Op{K, nullptr}, 32 * half, 0, kd,
+                                ncol <= 0 ? 0 : min(2, (ncol + 15) / 16));
+      tc::store_split(acc, PH, PL, m0, 32 * half, [&](int r, int cl, float x) {
+        return (cl < (r + 1) * p.nh && cl < Mc) ? x * bs[cl] : 0.f;
+      });
+    }
     __syncthreads();
 
     // dU = P^T dy + beta * (K dS')   (micro-step rows m0..)
@@ -499,8 +533,8 @@ __global__ void __launch_bounds__(kTcThreads, 1) bwd_chain_kernel(const TcArgs p
     {
       float g[NTV][4];
       tc::zero(g);
-      tc::gemm<NTV, true, true>(g, Op{TiH, TiL}, m0, Op{dUH, dUL}, n0, m0, 64);
-      tc::store_split(g, GH, GL, m0, n0, [](int, int, float x) { return -x; });
+      tc::gemm<NTV, true, true>(g, Ti, m0, Op{dUH, dUL}, n0, m0, 64);
+      tc::store_split(g, GH, GL, m0, n0, Neg());
     }
     __syncthreads();
     // dS = dS' + Q^T dy + K^T Gn   (d_k rows m0..)
@@ -514,10 +548,10 @@ __global__ void __launch_bounds__(kTcThreads, 1) bwd_chain_kernel(const TcArgs p
 
 // ----------------------------------------------------- backward: grads --
 // smem: K | Q | dy | V | beta, dbeta | S h/l | dS' h/l | KK f32 | QK f32 |
-//       R8 (T f32 -> U h/l) | R9 (T^{-1} f32 -> W h/l -> Gn h/l) |
-//       R10 (Ti h/l -> dKK h/l) | R11 (P h/l -> dS_ h/l) | bU h/l | dU h/l | scratch
+//       R8 U h/l | R9 (W h/l -> Gn h/l) | R10 (Ti h/l -> dKK h/l) |
+//       R11 (P h/l -> dS_ h/l) | bU h/l | dU h/l
 constexpr size_t kGradSmem = 4 * (size_t)kTileBytes + 512 + 4 * (size_t)kTileBytes +
-                             2 * (size_t)kF32Bytes + 12 * (size_t)kTileBytes + kYsBytes;
+                             2 * (size_t)kF32Bytes + 12 * (size_t)kTileBytes;
 
 __global__ void __launch_bounds__(kTcThreads, 1) bwd_grads_kernel(const TcArgs p) {
   extern __shared__ __align__(128) unsigned char smem[];
@@ -541,9 +575,6 @@ __global__ void __launch_bounds__(kTcThreads, 1) bwd_grads_kernel(const TcArgs p
   bf16* BUL = BUH + kTile;
   bf16* dUH = BUL + kTile;
   bf16* dUL = dUH + kTile;
-  float* Ys = reinterpret_cast<float*>(dUL + kTile);
-  float* Tf = reinterpret_cast<float*>(R8);
-  float* Xf = reinterpret_cast<float*>(R9);
   bf16 *UH = R8, *UL = R8 + kTile;
   bf16 *WH = R9, *WL = R9 + kTile, *GH = R9, *GL = R9 + kTile;
   bf16 *TiH = R10, *TiL = R10 + kTile, *dKH = R10, *dKL = R10 + kTile;
@@ -560,10 +591,12 @@ __global__ void __launch_bounds__(kTcThreads, 1) bwd_grads_kernel(const TcArgs p
   const long long rows = p.T * p.nh;
   const long long sofs = (bh * p.nchunks + c) * (long long)p.dk * p.dv;
 
-  stage_rows(K, p.K + (bh * rows + r0) * p.dk, p.dk, Mc, 8, p.dk >> 3);
-  stage_rows(Q, p.Q + (bh * p.T + t0) * p.dk, p.dk, Cc, 8, p.dk >> 3);
-  stage_rows(dY, p.dy + (bh * p.T + t0) * p.dv, p.dv, Cc, 8, p.dv >> 3);
-  stage_rows(V, p.V + (bh * rows + r0) * p.dv, p.dv, Mc, 8, p.dv >> 3);
+  stage_rows<8>(K, p.K + (bh * rows + r0) * p.dk, p.dk, Mc, p.dk >> 3);
+  stage_rows<8>(Q, p.Q + (bh * p.T + t0) * p.dk, p.dk, Cc, p.dk >> 3);
+  stage_rows<8>(dY, p.dy + (bh * p.T + t0) * p.dv, p.dv, Cc, p.dv >> 3);
+  stage_rows<8>(V, p.V + (bh * rows + r0) * p.dv, p.dv, Mc, p.dv >> 3);
+  tile_from_global_async(TiH, p.Ti + (bh * p.nchunks + c) * 8192);
+  tile_from_global_async(TiL, p.Ti + (bh * p.nchunks + c) * 8192 + 4096);
   cp_async_commit();
   if (tid < 64) {
     bs[tid] = tid < Mc ? __bfloat162float(p.beta[bh * rows + r0 + tid]) : 0.f;
@@ -588,11 +621,25 @@ __global__ void __launch_bounds__(kTcThreads, 1) bwd_grads_kernel(const TcArgs p
   cp_async_wait_all();
   __syncthreads();
 
-  build_T_P(K, Q, bs, kd, p.nh, Mc, Tf, PH, PL, KKf, QKf);
-  __syncthreads();
-  tri_inv64(Tf, Xf, Ys);
-  tri_to_split(Xf, TiH, TiL);
-  __syncthreads();
+  {
+    float acc[8][4];
+    if (half == 0) {
+      kk_rows(K, m0, kd, acc);
+#pragma unroll
+      for (int j = 0; j < 8; ++j)
+#pragma unroll
+        for (int v = 0; v < 4; ++v)
+          KKf[tc::frag_row(m0, v) * kTld + tc::frag_col(0, j, v)] = acc[j][v];
+    } else {
+      qk_rows(Q, K, m0, kd, p.nh, acc);
+#pragma unroll
+      for (int j = 0; j < 8; ++j)
+#pragma unroll
+        for (int v = 0; v < 4; ++v)
+          QKf[tc::frag_row(m0, v) * kTld + tc::frag_col(0, j, v)] = acc[j][v];
+      store_P(acc, bs, p.nh, Mc, m0, PH, PL);
+    }
+  }
 
   // W = Ti K, U' = Ti V (rows m0, columns n0..n0+31)
   float u[4][4];
@@ -758,12 +805,14 @@ bool tc_eligible(int dtype, int nh, int dk, int dv, int C) {
          dv >= 8 && dv <= 64 && dk % 8 == 0 && dv % 8 == 0;
 }
 
+// saved: chunk-start states (fp32) then every chunk's T^{-1} (split bf16, 64 x 64 x 2)
 size_t tc_saved_floats(long long BH, long long T, int dk, int dv, int C) {
-  return (size_t)BH * (size_t)((T + C - 1) / C) * dk * dv;
+  const size_t nc = (size_t)BH * (size_t)((T + C - 1) / C);
+  return nc * dk * dv + nc * 4096;
 }
 
 size_t tc_workspace_floats(long long BH, long long T, int dk, int dv, int C) {
-  return tc_saved_floats(BH, T, dk, dv, C);
+  return (size_t)BH * (size_t)((T + C - 1) / C) * dk * dv;
 }
 
 int run_tc(bool fwd, const Args<__nv_bfloat16>& p, long long B, int H, long long T, int nh, int dk,
@@ -796,6 +845,7 @@ int run_tc(bool fwd, const Args<__nv_bfloat16>& p, long long B, int H, long long
   if (BH == 0) return MGS_OK;
   if (saved == nullptr) return MGS_BAD_SHAPE;
   a.Hs = saved;
+  a.Ti = reinterpret_cast<bf16*>(saved + (size_t)BH * a.nchunks * dk * dv);
   if (fwd) {
     if (T == 0) {
       if (p.H0)

@@ -109,9 +109,10 @@ __device__ __forceinline__ void load_b(const __nv_bfloat16* t, int k0, int n0, u
 
 // c[NT] (a 16 x 8*NT tile at rows m0, cols n0) += A(m0.., k) * B(k, n0..) for
 // k in [k_begin, k_end) (multiples of 16). NT even.
+// Only the first np_end n-tile pairs are computed (the rest of c is untouched).
 template <int NT, bool ACOL, bool BKN>
 __device__ __forceinline__ void gemm(float (&c)[NT][4], Op A, int m0, Op B, int n0, int k_begin,
-                                     int k_end) {
+                                     int k_end, int np_end = NT / 2) {
   static_assert(NT % 2 == 0, "n-tiles come in pairs");
   for (int k0 = k_begin; k0 < k_end; k0 += 16) {
     uint32_t ah[4], al[4];
@@ -119,6 +120,7 @@ __device__ __forceinline__ void gemm(float (&c)[NT][4], Op A, int m0, Op B, int 
     if (A.lo) load_a<ACOL>(A.lo, m0, k0, al);
 #pragma unroll
     for (int j = 0; j < NT; j += 2) {
+      if (j / 2 >= np_end) break;
       uint32_t bh[4], bl[4];
       load_b<BKN>(B.hi, k0, n0 + 8 * j, bh);
       mma(c[j], ah, bh[0], bh[1]);
