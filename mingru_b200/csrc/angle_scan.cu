@@ -42,14 +42,6 @@ namespace angle {
 
 constexpr int kMaxK = 64, kMaxR = 16;  // sequential-kernel limits
 
-template <int K>
-struct Shape {
-  static constexpr int NF = K * (K + 1);
-  static constexpr int S = K <= 2 ? 8 : (K <= 4 ? 4 : 2);
-  static constexpr int NW = 4;
-  static constexpr int L = S * NW;
-};
-
 template <typename E>
 struct Args {
   const E* theta;   // (B, T, n, R, K/2)
@@ -231,241 +223,292 @@ __device__ __forceinline__ void store_k(E* dst, const float (&o)[K]) {
 }
 
 // ----------------------------------------------------------- fast kernels --
+//
+// One thread owns one (b, block) lane over a time tile of L steps; a CTA is
+// 128 consecutive lanes of one tile (a work item, handed out in order by an
+// atomic counter: all lanes' tile 0 first). Per item:
+//   1. aggregate: push the k+1 columns of [I | 0] through the tile's steps
+//      (forward: M_t, backward: M_t^T with the upstream gradient injected);
+//   2. publish it, then look back along the lane's own chain for the nearest
+//      earlier tile whose carried vector (state, or adjoint) is published,
+//      and apply the aggregates in between to it (k x (k+1) times a vector:
+//      no k x k compositions); publish this tile's outgoing vector;
+//   3. replay the tile from its incoming vector, writing the outputs.
+// Per lane and tile the workspace holds a flag, the aggregate and the
+// outgoing vector, 128 lanes interleaved so a warp's accesses coalesce.
+
+template <int W>
+struct VecWord;  // the vector type moving W bytes
+template <> struct VecWord<16> { using T = uint4; };
+template <> struct VecWord<8> { using T = uint2; };
+template <> struct VecWord<4> { using T = unsigned; };
+template <> struct VecWord<2> { using T = unsigned short; };
+
+template <typename E, int N>
+struct Vec {  // N elements of E as the widest aligned vector chunks
+  static constexpr int kBytes = N * (int)sizeof(E);
+  static constexpr int kW = (kBytes % 16 == 0) ? 16 : (kBytes % 8 == 0) ? 8 : (kBytes % 4 == 0) ? 4 : 2;
+  static constexpr int kPer = kW / (int)sizeof(E);
+  using W = typename VecWord<kW>::T;
+  union U {
+    W w;
+    E e[kPer];
+  };
+  __device__ static void load(const E* src, float (&o)[N]) {
+#pragma unroll
+    for (int c = 0; c < N / kPer; ++c) {
+      U u;
+      u.w = __ldcs(reinterpret_cast<const W*>(src) + c);
+#pragma unroll
+      for (int i = 0; i < kPer; ++i) o[c * kPer + i] = to_f32<E>(u.e[i]);
+    }
+  }
+  __device__ static void store(E* dst, const float (&v)[N]) {
+#pragma unroll
+    for (int c = 0; c < N / kPer; ++c) {
+      U u;
+#pragma unroll
+      for (int i = 0; i < kPer; ++i) u.e[i] = from_f32<E>(v[c * kPer + i]);
+      __stcs(reinterpret_cast<W*>(dst) + c, u.w);
+    }
+  }
+};
 
 template <typename E, int K, int R>
-__global__ void __launch_bounds__(Shape<K>::NW * 32, 1) fwd_kernel(Args<E> p) {
-  using SH = Shape<K>;
-  using M = AffMonoid<K>;
-  constexpr int NF = M::NF, S = SH::S, NW = SH::NW, L = SH::L;
-  extern __shared__ __align__(16) float smem[];
-  float(*s_agg)[NF][32] = reinterpret_cast<float(*)[NF][32]>(smem);
-  float(*s_ex)[32] = reinterpret_cast<float(*)[32]>(smem + NW * NF * 32);
-  float(*s_tot)[32] = reinterpret_cast<float(*)[32]>(smem + (NW + 1) * NF * 32);
-  __shared__ unsigned s_tile;
-  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  const bool hs = p.has_scale != 0, hd = p.has_decay != 0;
-  if (threadIdx.x == 0) s_tile = atomicAdd(p.lb.counter, 1u);
-  __syncthreads();
-  const long long tile = s_tile;
-  const long long chunk = tile / p.nstrips;
-  const long long strip = tile - chunk * p.nstrips;
-  const long long bi = strip / p.sper;
-  const long long blk = (strip - bi * p.sper) * 32 + lane;
-  const bool ok = blk < p.n;
-  const long long t0 = chunk * L + (long long)warp * S;
-  const size_t lane0 = (size_t)bi * p.T_ * p.n + blk;  // (b, t, blk) = lane0 + t * n
+__device__ __forceinline__ void load_coef_v(const Args<E>& p, size_t st, StepCoef<K, R>& cf) {
+  constexpr int NA = R * (K / 2);
+  float th[NA];
+  Vec<E, NA>::load(p.theta + st * NA, th);
+#pragma unroll
+  for (int i = 0; i < NA; ++i) sincosf(th[i], &cf.s[i], &cf.c[i]);
+  cf.gamma = p.has_decay ? to_f32<E>(__ldcs(p.gamma + st)) : 1.f;
+  cf.scale = p.has_scale ? to_f32<E>(__ldcs(p.scale + st)) : 1.f;
+}
 
-  StepCoef<K, R> cf[S];
-  float bv[S][K];
-  bool live[S];
-#pragma unroll
-  for (int s = 0; s < S; ++s) {
-    const long long t = t0 + s;
-    live[s] = ok && t < p.T_;
-    if (live[s]) {
-      const size_t st = lane0 + t * p.n;
-      load_coef<E, K, R>(p, st, cf[s]);
-      load_k<E, K>(p.b + st * K, bv[s]);
+constexpr int kLanes = 128;  // lanes (threads) per work item
+
+struct TileRec {  // one work item's records in the workspace
+  unsigned* flag;  // [128]
+  float* agg;      // [NF][128]
+  float* vec;      // [K][128]
+};
+
+// Workspace: 256-byte header (counter, error word), then the flags of every
+// item (zeroed per launch), then the aggregates, then the carried vectors.
+template <int K>
+__device__ __forceinline__ TileRec rec_of(unsigned char* ws, long long items, long long item) {
+  constexpr int NF = K * (K + 1);
+  unsigned char* flags = ws + 256;
+  float* aggs = reinterpret_cast<float*>(flags + (size_t)items * kLanes * 4);
+  float* vecs = aggs + (size_t)items * NF * kLanes;
+  TileRec r;
+  r.flag = reinterpret_cast<unsigned*>(flags) + (size_t)item * kLanes;
+  r.agg = aggs + (size_t)item * NF * kLanes;
+  r.vec = vecs + (size_t)item * K * kLanes;
+  return r;
+}
+
+// Bounded wait on one lane's flag; on time-out the error words are set and
+// the caller proceeds with what is there (the host raises).
+__device__ __forceinline__ unsigned wait_flag(const unsigned* f, unsigned* err) {
+  unsigned v = ld_acquire_u32(f);
+  long long it = 0;
+  while (v == 0u) {
+    if (++it > kSpinLimit) {
+      atomicOr(err, kErrTimeout);
+      atomicOr(&g_sticky_err, kErrTimeout);
+      return 2u;
     }
+    __nanosleep(32);
+    v = ld_acquire_u32(f);
   }
-  float h0v[K];
-  if (ok && t0 == 0) load_k<E, K>(p.h0 + ((size_t)bi * p.n + blk) * K, h0v);
-  float X[NF];
-  M::identity(X);
-  if (ok && t0 == 0) fold_state<K>(X, h0v);
+  return v;
+}
+
+// Carried vector entering `item`: walk back along the lane's chain (stride
+// `G` items) to the nearest published vector, then apply the aggregates of
+// the items in between, oldest first: v <- P v + q.
+template <int K>
+__device__ __forceinline__ void look_back(unsigned char* ws, long long items, unsigned* err,
+                                          long long item, long long G, float (&v)[K]) {
+  constexpr int W = K + 1;
+  const int t = threadIdx.x;
+  long long j = item - G;
+  int nagg = 0;
+  while (true) {
+    const TileRec r = rec_of<K>(ws, items, j);
+    const unsigned f = wait_flag(r.flag + t, err);
+    if (f == 2u || j < G) {
 #pragma unroll
-  for (int s = 0; s < S; ++s)
-    if (live[s]) agg_step<K, R>(X, cf[s], bv[s], hs, hd);
+      for (int i = 0; i < K; ++i) v[i] = f == 2u ? r.vec[i * kLanes + t] : 0.f;
+      break;
+    }
+    ++nagg;
+    j -= G;
+  }
+  for (int q = nagg; q >= 1; --q) {
+    const TileRec r = rec_of<K>(ws, items, item - q * G);
+    float o[K];
 #pragma unroll
-  for (int f = 0; f < NF; ++f) s_agg[warp][f][lane] = X[f];
-  __syncthreads();
-  if (warp == 0) {
-    float tot[NF], w_[NF];
+    for (int i = 0; i < K; ++i) {
+      float s = r.agg[(i * W + K) * kLanes + t];
 #pragma unroll
-    for (int f = 0; f < NF; ++f) tot[f] = s_agg[0][f][lane];
-#pragma unroll 1
-    for (int w = 1; w < NW; ++w) {
-#pragma unroll
-      for (int f = 0; f < NF; ++f) w_[f] = s_agg[w][f][lane];
-      combine_into<M, NF>(tot, w_);
+      for (int c = 0; c < K; ++c) s = fmaf(r.agg[(i * W + c) * kLanes + t], v[c], s);
+      o[i] = s;
     }
 #pragma unroll
-    for (int f = 0; f < NF; ++f) s_tot[f][lane] = tot[f];
-    __syncwarp();
-    warp_lookback_win_smem<M, NF>(p.lb, tile, p.nstrips, chunk, s_tot, s_ex);
+    for (int i = 0; i < K; ++i) v[i] = o[i];
   }
-  __syncthreads();
-  {
-    float w_[NF];
+}
+
+template <int K>
+__device__ __forceinline__ void publish_agg(const TileRec& r, const float (&X)[K * (K + 1)]) {
+  const int t = threadIdx.x;
 #pragma unroll
-    for (int f = 0; f < NF; ++f) X[f] = s_ex[f][lane];
-#pragma unroll 1
-    for (int w = 0; w < warp; ++w) {
+  for (int f = 0; f < K * (K + 1); ++f) r.agg[f * kLanes + t] = X[f];
+  st_release_u32(r.flag + t, 1u);
+}
+
+template <int K>
+__device__ __forceinline__ void publish_vec(const TileRec& r, const float (&v)[K]) {
+  const int t = threadIdx.x;
 #pragma unroll
-      for (int f = 0; f < NF; ++f) w_[f] = s_agg[w][f][lane];
-      combine_into<M, NF>(X, w_);
-    }
-  }
-  float v[K];
+  for (int i = 0; i < K; ++i) r.vec[i * kLanes + t] = v[i];
+  st_release_u32(r.flag + t, 2u);
+}
+
+// v_out = P v_in + q for the aggregate X = [P | q].
+template <int K>
+__device__ __forceinline__ void apply_agg(const float (&X)[K * (K + 1)], const float (&vi)[K],
+                                          float (&vo)[K]) {
 #pragma unroll
-  for (int i = 0; i < K; ++i) v[i] = (ok && t0 == 0) ? h0v[i] : X[i * (K + 1) + K];
-  if (p.carries != nullptr && warp == 0 && t0 < p.T_) {
-    float* dst = p.carries + (size_t)tile * K * 32;
+  for (int i = 0; i < K; ++i) {
+    float s = X[i * (K + 1) + K];
 #pragma unroll
-    for (int i = 0; i < K; ++i) __stcs(dst + i * 32 + lane, v[i]);
-  }
-#pragma unroll
-  for (int s = 0; s < S; ++s) {
-    if (live[s]) {
-      apply_M<K, R>(v, cf[s], hs, hd);
-#pragma unroll
-      for (int i = 0; i < K; ++i) v[i] += bv[s][i];
-      store_k<E, K>(p.out + (lane0 + (t0 + s) * p.n) * K, v);
-    }
+    for (int c = 0; c < K; ++c) s = fmaf(X[i * (K + 1) + c], vi[c], s);
+    vo[i] = s;
   }
 }
 
 template <typename E, int K, int R>
-__global__ void __launch_bounds__(Shape<K>::NW * 32, 1) bwd_kernel(Args<E> p) {
-  using SH = Shape<K>;
-  using M = AffMonoid<K>;
-  constexpr int NF = M::NF, S = SH::S, NW = SH::NW, L = SH::L;
-  constexpr int H = K / 2;
-  extern __shared__ __align__(16) float smem[];
-  float(*s_fagg)[NF][32] = reinterpret_cast<float(*)[NF][32]>(smem);
-  float(*s_ragg)[NF][32] = reinterpret_cast<float(*)[NF][32]>(smem + NW * NF * 32);
-  float(*s_rex)[32] = reinterpret_cast<float(*)[32]>(smem + 2 * NW * NF * 32);
-  float(*s_fex)[32] = reinterpret_cast<float(*)[32]>(smem + 2 * NW * NF * 32 + NF * 32);
-  float(*s_tot)[32] = reinterpret_cast<float(*)[32]>(smem + 2 * NW * NF * 32 + 2 * NF * 32);
-  __shared__ unsigned s_tile;
-  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+__global__ void __launch_bounds__(kLanes) fwd_tile_kernel(Args<E> p) {
+  constexpr int NF = K * (K + 1);
+  __shared__ unsigned s_item;
   const bool hs = p.has_scale != 0, hd = p.has_decay != 0;
-  if (threadIdx.x == 0) s_tile = atomicAdd(p.lb.counter, 1u);
+  if (threadIdx.x == 0) s_item = atomicAdd(p.lb.counter, 1u);
   __syncthreads();
-  const long long tile = s_tile;
-  const long long rchunk = tile / p.nstrips;
-  const long long strip = tile - rchunk * p.nstrips;
-  const long long chunk = p.nchunks - 1 - rchunk;
-  const long long bi = strip / p.sper;
-  const long long blk = (strip - bi * p.sper) * 32 + lane;
-  const bool ok = blk < p.n;
-  const long long t0 = chunk * L + (long long)warp * S;
+  const long long item = s_item;
+  const long long G = p.nstrips;  // lane groups
+  const long long tile = item / G, grp = item - tile * G;
+  const long long lane = grp * kLanes + threadIdx.x;
+  const bool ok = lane < p.sper;  // sper = B * n lanes
+  if (!ok) return;                // nobody reads this lane's records
+  const long long bi = lane / p.n, blk = lane - bi * p.n;
+  const long long t0 = tile * p.nchunks, t1 = min(p.T_, t0 + p.nchunks);  // nchunks = L
   const size_t lane0 = (size_t)bi * p.T_ * p.n + blk;
+  unsigned char* ws = reinterpret_cast<unsigned char*>(p.lb.counter);
+  const long long items = p.ntiles * G;
+  const TileRec me = rec_of<K>(ws, items, item);
 
-  StepCoef<K, R> cf[S];
-  float bv[S][K], gv[S][K];
-  bool live[S];
-#pragma unroll
-  for (int s = 0; s < S; ++s) {
-    const long long t = t0 + s;
-    live[s] = ok && t < p.T_;
-    if (live[s]) {
-      const size_t st = lane0 + t * p.n;
-      load_coef<E, K, R>(p, st, cf[s]);
-      load_k<E, K>(p.b + st * K, bv[s]);
-      load_k<E, K>(p.gout + st * K, gv[s]);
-    }
+  float X[NF];
+  AffMonoid<K>::identity(X);
+  for (long long t = t0; t < t1; ++t) {
+    const size_t st = lane0 + t * p.n;
+    StepCoef<K, R> cf;
+    load_coef_v<E, K, R>(p, st, cf);
+    float bv[K];
+    Vec<E, K>::load(p.b + st * K, bv);
+    agg_step<K, R>(X, cf, bv, hs, hd);
   }
-  float h0v[K];
-  if (ok && t0 == 0) load_k<E, K>(p.h0 + ((size_t)bi * p.n + blk) * K, h0v);
-  {
-    float X[NF];
-    M::identity(X);
-    if (ok && t0 == 0) fold_state<K>(X, h0v);
-#pragma unroll
-    for (int s = 0; s < S; ++s)
-      if (live[s]) agg_step<K, R>(X, cf[s], bv[s], hs, hd);
-#pragma unroll
-    for (int f = 0; f < NF; ++f) s_fagg[warp][f][lane] = X[f];
-    M::identity(X);
-#pragma unroll
-    for (int s = S - 1; s >= 0; --s)
-      if (live[s]) ragg_step<K, R>(X, cf[s], gv[s], hs, hd);
-#pragma unroll
-    for (int f = 0; f < NF; ++f) s_ragg[warp][f][lane] = X[f];
-  }
-  __syncthreads();
-  if (warp == 0) {
-    float tot[NF], w_[NF];
-#pragma unroll
-    for (int f = 0; f < NF; ++f) tot[f] = s_ragg[NW - 1][f][lane];
-#pragma unroll 1
-    for (int w = NW - 2; w >= 0; --w) {
-#pragma unroll
-      for (int f = 0; f < NF; ++f) w_[f] = s_ragg[w][f][lane];
-      combine_into<M, NF>(tot, w_);
-    }
-#pragma unroll
-    for (int f = 0; f < NF; ++f) s_tot[f][lane] = tot[f];
-    __syncwarp();
-    warp_lookback_win_smem<M, NF>(p.lb, tile, p.nstrips, rchunk, s_tot, s_rex);
-  } else if (warp == 1) {
-    const float* src = p.carries + (size_t)(chunk * p.nstrips + strip) * K * 32;
-#pragma unroll
-    for (int f = 0; f < NF; ++f) s_fex[f][lane] = 0.f;
-#pragma unroll
-    for (int i = 0; i < K; ++i) s_fex[i * (K + 1) + K][lane] = __ldcs(src + i * 32 + lane);
-  }
-  __syncthreads();
-  // forward state entering this warp's steps
   float v[K];
-  {
-    float X[NF], w_[NF];
-#pragma unroll
-    for (int f = 0; f < NF; ++f) X[f] = s_fex[f][lane];
-#pragma unroll 1
-    for (int w = 0; w < warp; ++w) {
-#pragma unroll
-      for (int f = 0; f < NF; ++f) w_[f] = s_fagg[w][f][lane];
-      combine_into<M, NF>(X, w_);
-    }
-#pragma unroll
-    for (int i = 0; i < K; ++i) v[i] = (ok && t0 == 0) ? h0v[i] : X[i * (K + 1) + K];
+  if (tile == 0) {
+    Vec<E, K>::load(p.h0 + ((size_t)bi * p.n + blk) * K, v);
+  } else {
+    publish_agg<K>(me, X);
+    look_back<K>(ws, items, p.lb.err, item, G, v);
   }
-  // adjoint entering from later steps
+  {
+    float vo[K];
+    apply_agg<K>(X, v, vo);
+    publish_vec<K>(me, vo);
+  }
+  for (long long t = t0; t < t1; ++t) {
+    const size_t st = lane0 + t * p.n;
+    StepCoef<K, R> cf;
+    load_coef_v<E, K, R>(p, st, cf);
+    float bv[K];
+    Vec<E, K>::load(p.b + st * K, bv);
+    apply_M<K, R>(v, cf, hs, hd);
+#pragma unroll
+    for (int i = 0; i < K; ++i) v[i] += bv[i];
+    Vec<E, K>::store(p.out + st * K, v);
+  }
+}
+
+template <typename E, int K, int R>
+__global__ void __launch_bounds__(kLanes) bwd_tile_kernel(Args<E> p) {
+  constexpr int NF = K * (K + 1), H = K / 2;
+  __shared__ unsigned s_item;
+  const bool hs = p.has_scale != 0, hd = p.has_decay != 0;
+  if (threadIdx.x == 0) s_item = atomicAdd(p.lb.counter, 1u);
+  __syncthreads();
+  const long long item = s_item;
+  const long long G = p.nstrips;
+  const long long rtile = item / G, grp = item - rtile * G;
+  const long long tile = p.ntiles - 1 - rtile;  // ntiles = tiles per lane here
+  const long long lane = grp * kLanes + threadIdx.x;
+  if (lane >= p.sper) return;
+  const long long bi = lane / p.n, blk = lane - bi * p.n;
+  const long long t0 = tile * p.nchunks, t1 = min(p.T_, t0 + p.nchunks);
+  const size_t lane0 = (size_t)bi * p.T_ * p.n + blk;
+  const size_t h0off = ((size_t)bi * p.n + blk) * K;
+  unsigned char* ws = reinterpret_cast<unsigned char*>(p.lb.counter);
+  const long long items = p.ntiles * G;
+  const TileRec me = rec_of<K>(ws, items, item);
+
+  float X[NF];
+  AffMonoid<K>::identity(X);
+  for (long long t = t1 - 1; t >= t0; --t) {
+    const size_t st = lane0 + t * p.n;
+    StepCoef<K, R> cf;
+    load_coef_v<E, K, R>(p, st, cf);
+    float g[K];
+    Vec<E, K>::load(p.gout + st * K, g);
+    ragg_step<K, R>(X, cf, g, hs, hd);
+  }
   float y[K];
+  if (rtile == 0) {
+#pragma unroll
+    for (int i = 0; i < K; ++i) y[i] = 0.f;
+  } else {
+    publish_agg<K>(me, X);
+    look_back<K>(ws, items, p.lb.err, item, G, y);
+  }
   {
-    float X[NF], w_[NF];
-#pragma unroll
-    for (int f = 0; f < NF; ++f) X[f] = s_rex[f][lane];
-#pragma unroll 1
-    for (int w = NW - 1; w > warp; --w) {
-#pragma unroll
-      for (int f = 0; f < NF; ++f) w_[f] = s_ragg[w][f][lane];
-      combine_into<M, NF>(X, w_);
-    }
-#pragma unroll
-    for (int i = 0; i < K; ++i) y[i] = X[i * (K + 1) + K];
+    float yo[K];
+    apply_agg<K>(X, y, yo);
+    publish_vec<K>(me, yo);
   }
-  float hp[S][K];
+  for (long long t = t1 - 1; t >= t0; --t) {
+    const size_t st = lane0 + t * p.n;
+    StepCoef<K, R> cf;
+    load_coef_v<E, K, R>(p, st, cf);
+    float a[K], hp[K];
+    Vec<E, K>::load(p.gout + st * K, a);
+    Vec<E, K>::load(t > 0 ? p.out + (st - p.n) * K : p.h0 + h0off, hp);
 #pragma unroll
-  for (int s = 0; s < S; ++s) {
-#pragma unroll
-    for (int i = 0; i < K; ++i) hp[s][i] = v[i];
-    if (live[s]) {
-      apply_M<K, R>(v, cf[s], hs, hd);
-#pragma unroll
-      for (int i = 0; i < K; ++i) v[i] += bv[s][i];
-    }
-  }
-#pragma unroll
-  for (int s = S - 1; s >= 0; --s) {
-    if (!live[s]) continue;
-    const size_t st = lane0 + (t0 + s) * p.n;
-    float a[K];
-#pragma unroll
-    for (int i = 0; i < K; ++i) a[i] = gv[s][i] + y[i];
-    store_k<E, K>(p.db + st * K, a);
-    // per-round states vv[r] (state entering round r)
+    for (int i = 0; i < K; ++i) a[i] += y[i];
+    Vec<E, K>::store(p.db + st * K, a);
+    // state entering each round
     float vv[R + 1][K];
 #pragma unroll
-    for (int i = 0; i < K; ++i) vv[0][i] = hp[s][i];
-    if (hs) vv[0][1] *= cf[s].scale;
+    for (int i = 0; i < K; ++i) vv[0][i] = hp[i];
+    if (hs) vv[0][1] *= cf.scale;
 #pragma unroll
     for (int r = 0; r < R; ++r) {
 #pragma unroll
       for (int i = 0; i < K; ++i) vv[r + 1][i] = vv[r][i];
-      rotate<K>(vv[r + 1], cf[s].c + r * H, cf[s].s + r * H, r);
+      rotate<K>(vv[r + 1], cf.c + r * H, cf.s + r * H, r);
     }
     if (hd) {
       float dg = 0.f;
@@ -473,7 +516,7 @@ __global__ void __launch_bounds__(Shape<K>::NW * 32, 1) bwd_kernel(Args<E> p) {
       for (int i = 0; i < K; ++i) dg = fmaf(a[i], vv[R][i], dg);
       p.dgamma[st] = from_f32<E>(dg);
 #pragma unroll
-      for (int i = 0; i < K; ++i) a[i] *= cf[s].gamma;
+      for (int i = 0; i < K; ++i) a[i] *= cf.gamma;
     }
     float dth[R * H];
 #pragma unroll
@@ -483,25 +526,21 @@ __global__ void __launch_bounds__(Shape<K>::NW * 32, 1) bwd_kernel(Args<E> p) {
       for (int m = 0; m < H; ++m) {
         const int i = par ? ((1 + 2 * m) % K) : (2 * m);
         const int j = (i + 1) % K;
-        const float c = cf[s].c[r * H + m], sn = cf[s].s[r * H + m];
+        const float c = cf.c[r * H + m], sn = cf.s[r * H + m];
         const float vi = vv[r][i], vj = vv[r][j];
         dth[r * H + m] = a[i] * (-sn * vi - c * vj) + a[j] * (c * vi - sn * vj);
       }
-      rotate_t<K>(a, cf[s].c + r * H, cf[s].s + r * H, r);
+      rotate_t<K>(a, cf.c + r * H, cf.s + r * H, r);
     }
-    {
-      E* dp = p.dtheta + st * (R * H);
-#pragma unroll
-      for (int q = 0; q < R * H; ++q) __stcs(dp + q, from_f32<E>(dth[q]));
-    }
+    Vec<E, R * H>::store(p.dtheta + st * (R * H), dth);
     if (hs) {
-      p.dscale[st] = from_f32<E>(a[1] * hp[s][1]);
-      a[1] *= cf[s].scale;
+      p.dscale[st] = from_f32<E>(a[1] * hp[1]);
+      a[1] *= cf.scale;
     }
 #pragma unroll
     for (int i = 0; i < K; ++i) y[i] = a[i];
   }
-  if (ok && t0 == 0) store_k<E, K>(p.dh0 + ((size_t)bi * p.n + blk) * K, y);
+  if (t0 == 0) Vec<E, K>::store(p.dh0 + h0off, y);
 }
 
 // ---------------------------------------------------- sequential kernels --
@@ -601,8 +640,8 @@ __global__ void seq_bwd_kernel(Args<E> p) {
 
 struct Geometry {
   bool fast;
-  int nf, L;
-  long long sper, nstrips, nchunks, ntiles;
+  int nf;
+  long long G, L, ntiles, items;  // fast path: lane groups, steps per tile, tiles per lane
 };
 
 template <class F>
@@ -616,53 +655,54 @@ inline bool with_kr(int k, int R, F&& f) {
   return false;
 }
 
+// Steps per tile: long enough to amortise the per-tile aggregate and records,
+// short enough to leave several work items per SM.
+inline long long tile_steps(long long lanes, long long T) {
+  const long long G = (lanes + kLanes - 1) / kLanes;
+  long long L = 64;
+  while (L > 8 && G * ((T + L - 1) / L) < 4LL * 148) L >>= 1;
+  return L;
+}
+
 inline bool geometry(long long B, long long T, long long n, int R, int k, int brickwall,
                      Geometry* g) {
   if (k < 2 || k % 2 != 0 || k > kMaxK || R < 1 || R > kMaxR) return false;
   g->fast = false;
-  if (brickwall)
-    with_kr(k, R, [&]<int K, int RR>() {
-      g->fast = true;
-      g->nf = AffMonoid<K>::NF;
-      g->L = Shape<K>::L;
-    });
-  g->sper = (n + 31) / 32;
-  g->nstrips = B * g->sper;
-  g->nchunks = g->fast ? (T + g->L - 1) / g->L : 0;
-  g->ntiles = g->nstrips * g->nchunks;
-  if (!g->fast) g->nf = 0;
+  if (brickwall) with_kr(k, R, [&]<int K, int RR>() { g->fast = true; g->nf = K * (K + 1); });
+  if (!g->fast) {
+    g->nf = 0;
+    g->G = g->L = g->ntiles = g->items = 0;
+    return true;
+  }
+  const long long lanes = B * n;
+  g->G = (lanes + kLanes - 1) / kLanes;
+  g->L = tile_steps(lanes, T);
+  g->ntiles = (T + g->L - 1) / g->L;
+  g->items = g->G * g->ntiles;
   return true;
 }
 
 template <typename E, int K, int R>
 int launch_fast(bool fwd, Args<E>& p, const Geometry& g, void* ws, cudaStream_t st) {
-  using SH = Shape<K>;
-  constexpr int NF = AffMonoid<K>::NF;
-  MGS_CUDA_OK(cudaMemsetAsync(ws, 0, lookback_zero_bytes(g.ntiles), st));
-  p.lb = lookback_view(ws, g.ntiles, NF);
-  p.nchunks = g.nchunks;
+  MGS_CUDA_OK(cudaMemsetAsync(ws, 0, 256 + (size_t)g.items * kLanes * 4, st));
+  p.lb.counter = static_cast<unsigned*>(ws);
+  p.lb.err = static_cast<unsigned*>(ws) + 1;
+  p.nstrips = g.G;
+  p.nchunks = g.L;
   p.ntiles = g.ntiles;
-  if (fwd) {
-    const size_t smem = (size_t)(SH::NW + 2) * NF * 32 * sizeof(float);
-    MGS_CUDA_OK(cudaFuncSetAttribute(fwd_kernel<E, K, R>,
-                                     cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
-    fwd_kernel<E, K, R><<<(unsigned)g.ntiles, SH::NW * 32, smem, st>>>(p);
-  } else {
-    const size_t smem = (size_t)(2 * SH::NW + 3) * NF * 32 * sizeof(float);
-    MGS_CUDA_OK(cudaFuncSetAttribute(bwd_kernel<E, K, R>,
-                                     cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
-    bwd_kernel<E, K, R><<<(unsigned)g.ntiles, SH::NW * 32, smem, st>>>(p);
-  }
+  if (fwd)
+    fwd_tile_kernel<E, K, R><<<(unsigned)g.items, kLanes, 0, st>>>(p);
+  else
+    bwd_tile_kernel<E, K, R><<<(unsigned)g.items, kLanes, 0, st>>>(p);
   return cudaGetLastError() == cudaSuccess ? MGS_OK : MGS_LAUNCH_FAILED;
 }
 
-inline size_t workspace_bytes(const Geometry& g) {
-  return g.fast ? lookback_bytes(g.ntiles, g.nf) : 256;
+inline size_t workspace_bytes(const Geometry& g, int k) {
+  return g.fast ? 256 + (size_t)g.items * kLanes * 4 * (1 + g.nf + k) : 256;
 }
 
-inline size_t carry_bytes(const Geometry& g, int k) {
-  return g.fast ? (size_t)g.ntiles * k * 32 * sizeof(float) : 0;
-}
+// The fast backward reads the forward's stored states: no carries.
+inline size_t carry_bytes(const Geometry&, int) { return 0; }
 
 template <typename E>
 int run(bool fwd, const Args<E>& a0, long long B, long long T, long long n, int R, int k,
@@ -681,13 +721,12 @@ int run(bool fwd, const Args<E>& a0, long long B, long long T, long long n, int 
     }
     return MGS_OK;
   }
-  if (ws == nullptr || ws_bytes < workspace_bytes(g) || !aligned(ws, 256))
+  if (ws == nullptr || ws_bytes < workspace_bytes(g, k) || !aligned(ws, 256))
     return MGS_WORKSPACE_TOO_SMALL;
   if (g.fast) {
-    if (g.ntiles > 0x7fffffffLL) return MGS_UNSUPPORTED;
-    if (!fwd && p.carries == nullptr) return MGS_BAD_SHAPE;
-    p.sper = g.sper;
-    p.nstrips = g.nstrips;
+    if (g.items > 0x7fffffffLL) return MGS_UNSUPPORTED;
+    if (!fwd && p.out == nullptr) return MGS_BAD_SHAPE;
+    p.sper = B * n;
     int rc = MGS_UNSUPPORTED;
     with_kr(k, R, [&]<int K, int RR>() { rc = launch_fast<E, K, RR>(fwd, p, g, ws, st); });
     return rc;
@@ -766,7 +805,7 @@ size_t mgs_angle_scan_workspace_size(int64_t B, int64_t T, int64_t n, int R, int
   if (mgs::dtype_size(dtype) == 0 || B < 0 || T < 0 || n < 0 ||
       !mgs::angle::geometry(B, T, n, R, k, brickwall, &g))
     return 0;
-  return mgs::angle::workspace_bytes(g);
+  return mgs::angle::workspace_bytes(g, k);
 }
 
 size_t mgs_angle_scan_carry_size(int64_t B, int64_t T, int64_t n, int R, int k, int brickwall,
