@@ -285,6 +285,70 @@ __device__ __forceinline__ void load_coef_v(const Args<E>& p, size_t st, StepCoe
   cf.scale = p.has_scale ? to_f32<E>(__ldcs(p.scale + st)) : 1.f;
 }
 
+// Loaded-but-unconverted inputs of one step, so the loads of later steps can
+// be issued before the current step is computed (software prefetch).
+template <typename E, int N>
+struct Raw {
+  using V = Vec<E, N>;
+  typename V::W w[N / V::kPer];
+  __device__ __forceinline__ void load(const E* src) {
+#pragma unroll
+    for (int c = 0; c < N / V::kPer; ++c)
+      w[c] = __ldcs(reinterpret_cast<const typename V::W*>(src) + c);
+  }
+  __device__ __forceinline__ void get(float (&o)[N]) const {
+#pragma unroll
+    for (int c = 0; c < N / V::kPer; ++c) {
+      typename V::U u;
+      u.w = w[c];
+#pragma unroll
+      for (int i = 0; i < V::kPer; ++i) o[c * V::kPer + i] = to_f32<E>(u.e[i]);
+    }
+  }
+};
+
+template <typename E, int K, int R, bool TWO>
+struct StepIn {
+  Raw<E, R*(K / 2)> th;
+  E gam, sc;
+  Raw<E, K> x;  // b (forward) or grad_h (backward)
+  Raw<E, K> y;  // h_{t-1} (backward replay)
+  __device__ __forceinline__ void load(const Args<E>& p, size_t st, const E* xs, const E* ys,
+                                       bool hs, bool hd) {
+    th.load(p.theta + st * (R * (K / 2)));
+    if (hd) gam = __ldcs(p.gamma + st);
+    if (hs) sc = __ldcs(p.scale + st);
+    x.load(xs);
+    if (TWO) y.load(ys);
+  }
+  __device__ __forceinline__ void coef(StepCoef<K, R>& cf, bool hs, bool hd) const {
+    float a[R * (K / 2)];
+    th.get(a);
+#pragma unroll
+    for (int i = 0; i < R * (K / 2); ++i) sincosf(a[i], &cf.s[i], &cf.c[i]);
+    cf.gamma = hd ? to_f32<E>(gam) : 1.f;
+    cf.scale = hs ? to_f32<E>(sc) : 1.f;
+  }
+};
+
+// body(step_in, t) for t = first, first + dir, ... (n steps), with the
+// inputs of the next D steps already in flight.
+template <int D, class SI, class LoadF, class BodyF>
+__device__ __forceinline__ void stream_steps(long long first, long long n, int dir, LoadF load,
+                                             BodyF body) {
+  SI ring[D];
+#pragma unroll
+  for (int d = 0; d < D; ++d)
+    if (d < n) load(ring[d], first + dir * d);
+  for (long long i = 0; i < n; ++i) {
+    SI cur = ring[0];
+#pragma unroll
+    for (int d = 0; d + 1 < D; ++d) ring[d] = ring[d + 1];
+    if (i + D < n) load(ring[D - 1], first + dir * (i + D));
+    body(cur, first + dir * i);
+  }
+}
+
 constexpr int kLanes = 128;  // lanes (threads) per work item
 
 struct TileRec {  // one work item's records in the workspace
@@ -410,16 +474,20 @@ __global__ void __launch_bounds__(kLanes) fwd_tile_kernel(Args<E> p) {
   const long long items = p.ntiles * G;
   const TileRec me = rec_of<K>(ws, items, item);
 
+  using SI = StepIn<E, K, R, false>;
+  auto load = [&](SI& q, long long t) {
+    const size_t st = lane0 + t * p.n;
+    q.load(p, st, p.b + st * K, nullptr, hs, hd);
+  };
   float X[NF];
   AffMonoid<K>::identity(X);
-  for (long long t = t0; t < t1; ++t) {
-    const size_t st = lane0 + t * p.n;
+  stream_steps<1, SI>(t0, t1 - t0, 1, load, [&](const SI& q, long long) {
     StepCoef<K, R> cf;
-    load_coef_v<E, K, R>(p, st, cf);
+    q.coef(cf, hs, hd);
     float bv[K];
-    Vec<E, K>::load(p.b + st * K, bv);
+    q.x.get(bv);
     agg_step<K, R>(X, cf, bv, hs, hd);
-  }
+  });
   float v[K];
   if (tile == 0) {
     Vec<E, K>::load(p.h0 + ((size_t)bi * p.n + blk) * K, v);
@@ -432,17 +500,16 @@ __global__ void __launch_bounds__(kLanes) fwd_tile_kernel(Args<E> p) {
     apply_agg<K>(X, v, vo);
     publish_vec<K>(me, vo);
   }
-  for (long long t = t0; t < t1; ++t) {
-    const size_t st = lane0 + t * p.n;
+  stream_steps<2, SI>(t0, t1 - t0, 1, load, [&](const SI& q, long long t) {
     StepCoef<K, R> cf;
-    load_coef_v<E, K, R>(p, st, cf);
+    q.coef(cf, hs, hd);
     float bv[K];
-    Vec<E, K>::load(p.b + st * K, bv);
+    q.x.get(bv);
     apply_M<K, R>(v, cf, hs, hd);
 #pragma unroll
     for (int i = 0; i < K; ++i) v[i] += bv[i];
-    Vec<E, K>::store(p.out + st * K, v);
-  }
+    Vec<E, K>::store(p.out + (lane0 + t * p.n) * K, v);
+  });
 }
 
 template <typename E, int K, int R>
@@ -466,16 +533,20 @@ __global__ void __launch_bounds__(kLanes) bwd_tile_kernel(Args<E> p) {
   const long long items = p.ntiles * G;
   const TileRec me = rec_of<K>(ws, items, item);
 
+  using SA = StepIn<E, K, R, false>;
+  auto load_a = [&](SA& q, long long t) {
+    const size_t st = lane0 + t * p.n;
+    q.load(p, st, p.gout + st * K, nullptr, hs, hd);
+  };
   float X[NF];
   AffMonoid<K>::identity(X);
-  for (long long t = t1 - 1; t >= t0; --t) {
-    const size_t st = lane0 + t * p.n;
+  stream_steps<1, SA>(t1 - 1, t1 - t0, -1, load_a, [&](const SA& q, long long) {
     StepCoef<K, R> cf;
-    load_coef_v<E, K, R>(p, st, cf);
+    q.coef(cf, hs, hd);
     float g[K];
-    Vec<E, K>::load(p.gout + st * K, g);
+    q.x.get(g);
     ragg_step<K, R>(X, cf, g, hs, hd);
-  }
+  });
   float y[K];
   if (rtile == 0) {
 #pragma unroll
@@ -489,13 +560,18 @@ __global__ void __launch_bounds__(kLanes) bwd_tile_kernel(Args<E> p) {
     apply_agg<K>(X, y, yo);
     publish_vec<K>(me, yo);
   }
-  for (long long t = t1 - 1; t >= t0; --t) {
+  using SB = StepIn<E, K, R, true>;
+  auto load_b = [&](SB& q, long long t) {
+    const size_t st = lane0 + t * p.n;
+    q.load(p, st, p.gout + st * K, t > 0 ? p.out + (st - p.n) * K : p.h0 + h0off, hs, hd);
+  };
+  stream_steps<2, SB>(t1 - 1, t1 - t0, -1, load_b, [&](const SB& q, long long t) {
     const size_t st = lane0 + t * p.n;
     StepCoef<K, R> cf;
-    load_coef_v<E, K, R>(p, st, cf);
+    q.coef(cf, hs, hd);
     float a[K], hp[K];
-    Vec<E, K>::load(p.gout + st * K, a);
-    Vec<E, K>::load(t > 0 ? p.out + (st - p.n) * K : p.h0 + h0off, hp);
+    q.x.get(a);
+    q.y.get(hp);
 #pragma unroll
     for (int i = 0; i < K; ++i) a[i] += y[i];
     Vec<E, K>::store(p.db + st * K, a);
@@ -539,7 +615,7 @@ __global__ void __launch_bounds__(kLanes) bwd_tile_kernel(Args<E> p) {
     }
 #pragma unroll
     for (int i = 0; i < K; ++i) y[i] = a[i];
-  }
+  });
   if (t0 == 0) Vec<E, K>::store(p.dh0 + h0off, y);
 }
 
