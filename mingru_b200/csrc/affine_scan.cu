@@ -508,6 +508,360 @@ __global__ void __launch_bounds__(Shape<K, V>::NW * 32, 1) bwd_kernel(Args<E> p)
   }
 }
 
+// ------------------------------------------------------------ strip path --
+//
+// Small elements (32 k^2 and 32 k v elements per time row fit one TMA box:
+// k <= 2, k v <= 8 -- matrix_scan is k = 2, v = 1): persistent CTAs of
+// kStripNW consumer warps + 1 producer warp, each CTA walking 32-block strips
+// through all of T. The producer streams 32-step chunks of A and Bm (backward:
+// also gA, gB and the chunk's forward carry) into a shared-memory ring with
+// TMA; consumer warp w takes steps w*8 .. w*8+7 of each chunk with its lane's
+// inputs in registers, warp aggregates combine through shared memory and the
+// strip state is carried on chip from chunk to chunk: no look-back, every
+// input read once. The forward writes each chunk's start state (the carries);
+// the backward walks the chunks in reverse, rebuilds X_{t-1} from them and
+// carries the adjoint like the register kernels.
+
+constexpr int kLc = 32;          // steps per chunk (= carry granularity of the strip path)
+constexpr int kStripNW = 4;      // consumer warps
+constexpr int kStripS = kLc / kStripNW;
+constexpr int kMaxStages = 16;
+
+template <int K, int V>
+struct StripOK {
+  static constexpr bool value = 32 * K * K <= 256 && 32 * K * V <= 256 && K * (K + V) <= 8;
+};
+
+template <typename E, int K, int V, bool BWD>
+struct AStage {
+  static constexpr int kA = 32 * K * K, kB = 32 * K * V;  // elements per time row
+  static constexpr int NF = K * (K + V);
+  static constexpr size_t kABytes = (size_t)kLc * kA * sizeof(E);
+  static constexpr size_t kBBytes = (size_t)kLc * kB * sizeof(E);
+  static constexpr size_t kCarryBytes = BWD ? (size_t)NF * 32 * sizeof(float) : 0;
+  static constexpr size_t kBytes =
+      ((BWD ? 2 : 1) * (kABytes + kBBytes) + kCarryBytes + 127) / 128 * 128;
+};
+
+struct AStripMaps {
+  CUtensorMap m[4];  // A, Bm, gA, gB
+};
+
+struct StripArgs {
+  long long T_, n, sper, nstrips, nchunks;
+  int nstage;
+  float* carries;  // (nchunks, nstrips, NF, 32) chunk-start states
+  unsigned* err;
+};
+
+template <typename E, int K, int V, bool BWD>
+__device__ __forceinline__ void astrip_produce(const StripArgs& a, const AStripMaps& maps,
+                                               unsigned char* ring, uint64_t* full,
+                                               uint64_t* empty) {
+  using SS = AStage<E, K, V, BWD>;
+  constexpr int NIN = BWD ? 4 : 2;
+  const int lane = threadIdx.x & 31;
+  if (lane == 0)
+    for (int i = 0; i < NIN; ++i) tma_prefetch_desc(&maps.m[i]);
+  int s = 0;
+  unsigned ph = 0, pending = 0u, pend_ph = 0u;
+  for (long long strip = blockIdx.x; strip < a.nstrips; strip += gridDim.x) {
+    const long long bi = strip / a.sper;
+    const int g0 = (int)(strip - bi * a.sper);
+    for (long long q = 0; q < a.nchunks; ++q) {
+      const long long chunk = BWD ? a.nchunks - 1 - q : q;
+      if (!mbar_wait(&empty[s], ph ^ 1u, a.err)) goto drain;
+      pending &= ~(1u << s);
+      if (lane == 0) {
+        unsigned char* st = ring + (size_t)s * SS::kBytes;
+        mbar_arrive_expect_tx(&full[s], (unsigned)((BWD ? 2 : 1) * (SS::kABytes + SS::kBBytes) +
+                                                   SS::kCarryBytes));
+        const int y = (int)(chunk * kLc);
+        tma_load_3d(st, &maps.m[0], g0 * SS::kA, y, (int)bi, &full[s]);
+        tma_load_3d(st + SS::kABytes, &maps.m[1], g0 * SS::kB, y, (int)bi, &full[s]);
+        if (BWD) {
+          tma_load_3d(st + SS::kABytes + SS::kBBytes, &maps.m[2], g0 * SS::kA, y, (int)bi,
+                      &full[s]);
+          tma_load_3d(st + 2 * SS::kABytes + SS::kBBytes, &maps.m[3], g0 * SS::kB, y, (int)bi,
+                      &full[s]);
+          bulk_g2s(st + 2 * (SS::kABytes + SS::kBBytes),
+                   a.carries + (size_t)(chunk * a.nstrips + strip) * SS::NF * 32,
+                   (unsigned)SS::kCarryBytes, &full[s]);
+        }
+      }
+      __syncwarp();
+      pending |= 1u << s;
+      pend_ph = (pend_ph & ~(1u << s)) | (ph << s);
+      if (++s == a.nstage) {
+        s = 0;
+        ph ^= 1u;
+      }
+    }
+  }
+drain:
+  for (int i = 0; i < a.nstage; ++i)
+    if (pending & (1u << i)) mbar_wait(&full[i], (pend_ph >> i) & 1u, a.err);
+}
+
+// Lane `lane`'s N elements of time row `row` of a staged (rows x 32 N) block.
+template <typename E, int N>
+__device__ __forceinline__ void stage_get(const unsigned char* base, int row, float (&o)[N]) {
+  const E* p = reinterpret_cast<const E*>(base) + (size_t)row * 32 * N + (threadIdx.x & 31) * N;
+#pragma unroll
+  for (int i = 0; i < N; ++i) o[i] = to_f32<E>(p[i]);
+}
+
+template <typename E, int K, int V>
+__global__ void __launch_bounds__((kStripNW + 1) * 32)
+    fwd_strip_kernel(Args<E> p, StripArgs a, const __grid_constant__ AStripMaps maps) {
+  using SS = AStage<E, K, V, false>;
+  using M = FwdMonoid<K, V>;
+  constexpr int NF = M::NF, NW = kStripNW, S = kStripS, W = K + V;
+  extern __shared__ __align__(128) unsigned char ring[];
+  __shared__ __align__(8) uint64_t full[kMaxStages], empty[kMaxStages];
+  __shared__ float s_agg[2][NW][NF][32];
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < a.nstage; ++i) {
+      mbar_init(&full[i], 1);
+      mbar_init(&empty[i], NW);
+    }
+    mbar_fence_init();
+  }
+  __syncthreads();
+  if (warp == NW) {
+    astrip_produce<E, K, V, false>(a, maps, ring, full, empty);
+    return;
+  }
+  int s = 0, buf = 0;
+  unsigned ph = 0;
+  for (long long strip = blockIdx.x; strip < a.nstrips; strip += gridDim.x) {
+    const long long bi = strip / a.sper;
+    const long long blk = (strip - bi * a.sper) * 32 + lane;
+    const bool ok = blk < a.n;
+    const size_t lane0 = (size_t)bi * a.T_ * a.n + blk;
+    float carry[NF];
+    M::identity(carry);
+    for (long long chunk = 0; chunk < a.nchunks; ++chunk) {
+      const bool okw = mbar_wait(&full[s], ph, a.err);
+      if (bar_any(1, NW * 32, !okw)) return;
+      const unsigned char* st = ring + (size_t)s * SS::kBytes;
+      float Av[S][K * K], Bv[S][K * V];
+#pragma unroll
+      for (int i = 0; i < S; ++i) {
+        stage_get<E, K * K>(st, warp * S + i, Av[i]);
+        stage_get<E, K * V>(st + SS::kABytes, warp * S + i, Bv[i]);
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&empty[s]);
+      if (++s == a.nstage) {
+        s = 0;
+        ph ^= 1u;
+      }
+      const long long t0 = chunk * kLc + (long long)warp * S;
+      float agg[NF];
+      M::identity(agg);
+#pragma unroll
+      for (int i = 0; i < S; ++i)
+        if (t0 + i < a.T_) step_fwd<K, V>(agg, Av[i], Bv[i]);
+#pragma unroll
+      for (int f = 0; f < NF; ++f) s_agg[buf][warp][f][lane] = agg[f];
+      named_bar(2, NW * 32);
+      if (warp == 0 && a.carries != nullptr) {
+        float* dst = a.carries + (size_t)(chunk * a.nstrips + strip) * NF * 32;
+#pragma unroll
+        for (int f = 0; f < NF; ++f) __stcs(dst + f * 32 + lane, carry[f]);
+      }
+      float X[NF];
+#pragma unroll
+      for (int w = 0; w < NW; ++w) {
+        float e[NF];
+#pragma unroll
+        for (int f = 0; f < NF; ++f) e[f] = s_agg[buf][w][f][lane];
+        if (w == warp)
+#pragma unroll
+          for (int f = 0; f < NF; ++f) X[f] = carry[f];
+        combine_into<M, NF>(carry, e);
+      }
+#pragma unroll
+      for (int i = 0; i < S; ++i) {
+        const long long t = t0 + i;
+        if (t < a.T_) {
+          step_fwd<K, V>(X, Av[i], Bv[i]);
+          if (ok) {
+            const size_t off = lane0 + t * a.n;
+            float oa[K * K], ob[K * V];
+#pragma unroll
+            for (int r = 0; r < K; ++r) {
+#pragma unroll
+              for (int c = 0; c < K; ++c) oa[r * K + c] = X[r * W + c];
+#pragma unroll
+              for (int c = 0; c < V; ++c) ob[r * V + c] = X[r * W + K + c];
+            }
+            store_n<E, K * K>(p.Abar + off * K * K, oa);
+            store_n<E, K * V>(p.Bbar + off * K * V, ob);
+          }
+        }
+      }
+      buf ^= 1;
+    }
+  }
+}
+
+template <typename E, int K, int V>
+__global__ void __launch_bounds__((kStripNW + 1) * 32)
+    bwd_strip_kernel(Args<E> p, StripArgs a, const __grid_constant__ AStripMaps maps) {
+  using SS = AStage<E, K, V, true>;
+  using FM = FwdMonoid<K, V>;
+  using RM = RevMonoid<K, V>;
+  constexpr int NFF = FM::NF, NFR = RM::NF, NW = kStripNW, S = kStripS, W = K + V;
+  extern __shared__ __align__(128) unsigned char ring[];
+  __shared__ __align__(8) uint64_t full[kMaxStages], empty[kMaxStages];
+  __shared__ float s_fagg[2][NW][NFF][32];
+  __shared__ float s_ragg[2][NW][NFR][32];
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < a.nstage; ++i) {
+      mbar_init(&full[i], 1);
+      mbar_init(&empty[i], NW);
+    }
+    mbar_fence_init();
+  }
+  __syncthreads();
+  if (warp == NW) {
+    astrip_produce<E, K, V, true>(a, maps, ring, full, empty);
+    return;
+  }
+  int s = 0, buf = 0;
+  unsigned ph = 0;
+  for (long long strip = blockIdx.x; strip < a.nstrips; strip += gridDim.x) {
+    const long long bi = strip / a.sper;
+    const long long blk = (strip - bi * a.sper) * 32 + lane;
+    const bool ok = blk < a.n;
+    const size_t lane0 = (size_t)bi * a.T_ * a.n + blk;
+    float rcarry[NFR];
+    RM::identity(rcarry);
+    for (long long q = 0; q < a.nchunks; ++q) {
+      const long long chunk = a.nchunks - 1 - q;
+      const bool okw = mbar_wait(&full[s], ph, a.err);
+      if (bar_any(1, NW * 32, !okw)) return;
+      const unsigned char* st = ring + (size_t)s * SS::kBytes;
+      float Av[S][K * K], Bv[S][K * V], Ga[S][K * W];
+#pragma unroll
+      for (int i = 0; i < S; ++i) {
+        stage_get<E, K * K>(st, warp * S + i, Av[i]);
+        stage_get<E, K * V>(st + SS::kABytes, warp * S + i, Bv[i]);
+        float ga[K * K], gb[K * V];
+        stage_get<E, K * K>(st + SS::kABytes + SS::kBBytes, warp * S + i, ga);
+        stage_get<E, K * V>(st + 2 * SS::kABytes + SS::kBBytes, warp * S + i, gb);
+#pragma unroll
+        for (int r = 0; r < K; ++r) {
+#pragma unroll
+          for (int c = 0; c < K; ++c) Ga[i][r * W + c] = ga[r * K + c];
+#pragma unroll
+          for (int c = 0; c < V; ++c) Ga[i][r * W + K + c] = gb[r * V + c];
+        }
+      }
+      float fcur[NFF];
+      {
+        const float* fc = reinterpret_cast<const float*>(st + 2 * (SS::kABytes + SS::kBBytes));
+#pragma unroll
+        for (int f = 0; f < NFF; ++f) fcur[f] = fc[f * 32 + lane];
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&empty[s]);
+      if (++s == a.nstage) {
+        s = 0;
+        ph ^= 1u;
+      }
+      const long long t0 = chunk * kLc + (long long)warp * S;
+      {
+        float fagg[NFF], ragg[NFR];
+        FM::identity(fagg);
+        RM::identity(ragg);
+#pragma unroll
+        for (int i = 0; i < S; ++i)
+          if (t0 + i < a.T_) step_fwd<K, V>(fagg, Av[i], Bv[i]);
+#pragma unroll
+        for (int i = S - 1; i >= 0; --i)
+          if (t0 + i < a.T_) step_rev<K, V>(ragg, Av[i], Ga[i]);
+#pragma unroll
+        for (int f = 0; f < NFF; ++f) s_fagg[buf][warp][f][lane] = fagg[f];
+#pragma unroll
+        for (int f = 0; f < NFR; ++f) s_ragg[buf][warp][f][lane] = ragg[f];
+      }
+      named_bar(2, NW * 32);
+      for (int w = 0; w < warp; ++w) {
+        float e[NFF];
+#pragma unroll
+        for (int f = 0; f < NFF; ++f) e[f] = s_fagg[buf][w][f][lane];
+        combine_into<FM, NFF>(fcur, e);
+      }
+      float rcur[NFR];
+#pragma unroll
+      for (int w = NW - 1; w >= 0; --w) {
+        if (w == warp)
+#pragma unroll
+          for (int f = 0; f < NFR; ++f) rcur[f] = rcarry[f];
+        float e[NFR];
+#pragma unroll
+        for (int f = 0; f < NFR; ++f) e[f] = s_ragg[buf][w][f][lane];
+        combine_into<RM, NFR>(rcarry, e);
+      }
+      // forward states entering each step, then the reverse sweep
+      float Xs[S][NFF];
+#pragma unroll
+      for (int i = 0; i < S; ++i) {
+#pragma unroll
+        for (int f = 0; f < NFF; ++f) Xs[i][f] = fcur[f];
+        if (i + 1 < S) step_fwd<K, V>(fcur, Av[i], Bv[i]);
+      }
+      float Y[K * W];
+#pragma unroll
+      for (int f = 0; f < K * W; ++f) Y[f] = rcur[K * K + f];
+#pragma unroll
+      for (int i = S - 1; i >= 0; --i) {
+        const long long t = t0 + i;
+        if (t >= a.T_) continue;
+#pragma unroll
+        for (int f = 0; f < K * W; ++f) Y[f] += Ga[i][f];
+        if (ok) {
+          const size_t off = lane0 + t * a.n;
+          float oa[K * K], ob[K * V];
+#pragma unroll
+          for (int r = 0; r < K; ++r) {
+#pragma unroll
+            for (int c = 0; c < K; ++c) {
+              float s2 = 0.f;
+#pragma unroll
+              for (int j = 0; j < W; ++j) s2 = fmaf(Y[r * W + j], Xs[i][c * W + j], s2);
+              oa[r * K + c] = s2;
+            }
+#pragma unroll
+            for (int c = 0; c < V; ++c) ob[r * V + c] = Y[r * W + K + c];
+          }
+          store_n<E, K * K>(p.dA + off * K * K, oa);
+          store_n<E, K * V>(p.dB + off * K * V, ob);
+        }
+#pragma unroll
+        for (int j = 0; j < W; ++j) {
+          float col[K];
+#pragma unroll
+          for (int c = 0; c < K; ++c) {
+            float s2 = 0.f;
+#pragma unroll
+            for (int r = 0; r < K; ++r) s2 = fmaf(Av[i][r * K + c], Y[r * W + j], s2);
+            col[c] = s2;
+          }
+#pragma unroll
+          for (int c = 0; c < K; ++c) Y[c * W + j] = col[c];
+        }
+      }
+      buf ^= 1;
+    }
+  }
+}
+
 // ------------------------------------------------- sequential (large k) --
 
 template <typename E>
@@ -589,16 +943,33 @@ __global__ void seq_bwd_kernel(Args<E> p, int K, int V, float* scratch) {
 // ---------------------------------------------------------------- launch --
 
 struct Geometry {
-  bool reg;
+  bool reg, strip;
   int nff, nfr, L;
   long long sper, nstrips, nchunks, ntiles;
 };
 
 template <int K, int V>
-inline Geometry geometry_kv(long long B, long long T, long long n) {
+inline Geometry geometry_kv(long long B, long long T, long long n, int dtype) {
   Geometry g;
   using SH = Shape<K, V>;
   g.reg = SH::kRegister;
+  // Strip-serial walk (no look-back, inputs read once) when the strips fill
+  // most SMs and the TMA row strides are 16-byte multiples.
+  const long long strips = B * ((n + 31) / 32);
+  const size_t es = (size_t)dtype_size(dtype);
+  g.strip = StripOK<K, V>::value && (n * K * K * es) % 16 == 0 && (n * K * V * es) % 16 == 0 &&
+            strips * 4 >= 3LL * sm_count() && T >= 2 * kLc;
+  if (g.strip) {
+    g.reg = false;
+    g.nff = FwdMonoid<K, V>::NF;
+    g.nfr = RevMonoid<K, V>::NF;
+    g.L = kLc;
+    g.sper = (n + 31) / 32;
+    g.nstrips = B * g.sper;
+    g.nchunks = (T + kLc - 1) / kLc;
+    g.ntiles = g.nstrips * g.nchunks;
+    return g;
+  }
   g.nff = FwdMonoid<K, V>::NF;
   g.nfr = RevMonoid<K, V>::NF;
   g.L = SH::L;
@@ -625,11 +996,14 @@ inline bool with_kv(int k, int v, F&& f) {
 // k (k + v) <= 72; any other k, v >= 1 (up to 64) runs the sequential kernels.
 constexpr int kMaxSeqKV = 64;
 
-inline bool geometry(long long B, long long T, long long n, int k, int v, Geometry* g) {
+inline bool geometry(long long B, long long T, long long n, int k, int v, int dtype,
+                     Geometry* g) {
   if (k < 1 || v < 1 || k > kMaxSeqKV || v > kMaxSeqKV) return false;
-  if (with_kv(k, v, [&]<int K, int V>() { *g = geometry_kv<K, V>(B, T, n); }) && g->reg)
+  if (with_kv(k, v, [&]<int K, int V>() { *g = geometry_kv<K, V>(B, T, n, dtype); }) &&
+      (g->reg || g->strip))
     return true;
   g->reg = false;
+  g->strip = false;
   g->nff = k * (k + v);
   g->nfr = k * k + k * (k + v);
   g->L = 0;
@@ -641,12 +1015,56 @@ inline bool geometry(long long B, long long T, long long n, int k, int v, Geomet
 }
 
 inline size_t workspace_bytes(const Geometry& g, long long B, long long n, int k, int v) {
+  if (g.strip) return 256;  // error word only: no look-back
   if (!g.reg) return 256 + align_up((size_t)(B * n) * 2 * k * (k + v) * sizeof(float), 256);
   return lookback_bytes(g.ntiles, g.nfr > g.nff ? g.nfr : g.nff);
 }
 
 inline size_t carry_bytes(const Geometry& g) {
-  return g.reg ? (size_t)g.ntiles * g.nff * 32 * sizeof(float) : 0;
+  return (g.reg || g.strip) ? (size_t)g.ntiles * g.nff * 32 * sizeof(float) : 0;
+}
+
+template <typename E, int K, int V>
+int launch_strip(bool fwd, Args<E>& p, const Geometry& g, void* ws, long long B, long long T,
+                 cudaStream_t st) {
+  if constexpr (!StripOK<K, V>::value) {
+    return MGS_UNSUPPORTED;
+  } else {
+    MGS_CUDA_OK(cudaMemsetAsync(ws, 0, 256, st));  // error word
+    StripArgs a;
+    a.T_ = T;
+    a.n = p.n;
+    a.sper = g.sper;
+    a.nstrips = g.nstrips;
+    a.nchunks = g.nchunks;
+    a.carries = p.carries;
+    a.err = static_cast<unsigned*>(ws) + 1;
+    AStripMaps maps;
+    const long long n = p.n;
+    if (!make_tmap_3d<E>(&maps.m[0], p.A, n * K * K, T, B, 32u * K * K, (unsigned)kLc) ||
+        !make_tmap_3d<E>(&maps.m[1], p.Bm, n * K * V, T, B, 32u * K * V, (unsigned)kLc))
+      return MGS_LAUNCH_FAILED;
+    if (!fwd && (!make_tmap_3d<E>(&maps.m[2], p.gA, n * K * K, T, B, 32u * K * K, (unsigned)kLc) ||
+                 !make_tmap_3d<E>(&maps.m[3], p.gB, n * K * V, T, B, 32u * K * V, (unsigned)kLc)))
+      return MGS_LAUNCH_FAILED;
+    // One CTA per SM gets a deep ring; two share an SM when strips outnumber SMs.
+    const int sms = sm_count();
+    const int per_sm = g.nstrips > sms ? 2 : 1;
+    const size_t ring_budget = per_sm == 1 ? 180 * 1024 : 88 * 1024;
+    const size_t sbytes = fwd ? AStage<E, K, V, false>::kBytes : AStage<E, K, V, true>::kBytes;
+    int nst = (int)(ring_budget / sbytes);
+    if (nst > kMaxStages) nst = kMaxStages;
+    if (nst < 2) nst = 2;
+    a.nstage = nst;
+    const size_t smem = (size_t)nst * sbytes;
+    long long grid = (long long)per_sm * sms;
+    if (grid > g.nstrips) grid = g.nstrips;
+    void* kargs[] = {&p, &a, &maps};
+    const void* fn = fwd ? (const void*)fwd_strip_kernel<E, K, V> : (const void*)bwd_strip_kernel<E, K, V>;
+    MGS_CUDA_OK(cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+    MGS_CUDA_OK(cudaLaunchKernel(fn, dim3((unsigned)grid), dim3((kStripNW + 1) * 32), kargs, smem, st));
+    return MGS_OK;
+  }
 }
 
 template <typename E, int K, int V>
@@ -679,7 +1097,7 @@ int run(bool fwd, const void* A, const void* Bm, void* Abar, void* Bbar, const v
         const void* gB, void* dA, void* dB, void* carries, long long B, long long T, long long n,
         int k, int v, void* ws, size_t ws_bytes, cudaStream_t st) {
   Geometry g;
-  if (!geometry(B, T, n, k, v, &g)) return MGS_UNSUPPORTED;
+  if (!geometry(B, T, n, k, v, dtype_of<E>(), &g)) return MGS_UNSUPPORTED;
   if (B * T * n == 0) return MGS_OK;
   if (g.ntiles > 0x7fffffffLL) return MGS_UNSUPPORTED;
   if (ws == nullptr || ws_bytes < workspace_bytes(g, B, n, k, v) || !aligned(ws, 256))
@@ -699,6 +1117,13 @@ int run(bool fwd, const void* A, const void* Bm, void* Abar, void* Bbar, const v
   p.carries = static_cast<float*>(carries);
   p.T_ = T;
   p.n = n;
+  if (g.strip) {
+    if (!fwd && carries == nullptr) return MGS_BAD_SHAPE;
+    if (carries != nullptr && !aligned(carries, 16)) return MGS_BAD_ALIGNMENT;
+    int rc = MGS_UNSUPPORTED;
+    with_kv(k, v, [&]<int K, int V>() { rc = launch_strip<E, K, V>(fwd, p, g, ws, B, T, st); });
+    return rc;
+  }
   if (g.reg) {
     if (!fwd && carries == nullptr) return MGS_BAD_SHAPE;
     if (carries != nullptr && !aligned(carries, 16)) return MGS_BAD_ALIGNMENT;
@@ -751,7 +1176,7 @@ extern "C" {
 size_t mgs_affine_scan_workspace_size(int64_t B, int64_t T, int64_t n, int k, int v, int dtype) {
   mgs::affine::Geometry g;
   if (mgs::dtype_size(dtype) == 0 || B < 0 || T < 0 || n < 0 ||
-      !mgs::affine::geometry(B, T, n, k, v, &g))
+      !mgs::affine::geometry(B, T, n, k, v, dtype, &g))
     return 0;
   return mgs::affine::workspace_bytes(g, B, n, k, v);
 }
@@ -759,7 +1184,7 @@ size_t mgs_affine_scan_workspace_size(int64_t B, int64_t T, int64_t n, int k, in
 size_t mgs_affine_scan_carry_size(int64_t B, int64_t T, int64_t n, int k, int v, int dtype) {
   mgs::affine::Geometry g;
   if (mgs::dtype_size(dtype) == 0 || B < 0 || T < 0 || n < 0 ||
-      !mgs::affine::geometry(B, T, n, k, v, &g))
+      !mgs::affine::geometry(B, T, n, k, v, dtype, &g))
     return 0;
   return mgs::affine::carry_bytes(g);
 }

@@ -12,6 +12,8 @@
 // word, then proceeds, so no launch can hang a GPU.
 #pragma once
 
+#include <type_traits>
+
 #include <cuda.h>
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
@@ -580,6 +582,14 @@ inline int dtype_size(int dtype) {
     case MGS_F16: return 2;
     default: return 0;
   }
+}
+
+// mgs_dtype code of a storage type.
+template <typename E>
+constexpr int dtype_of() {
+  if constexpr (std::is_same_v<E, float>) return MGS_F32;
+  else if constexpr (std::is_same_v<E, __nv_bfloat16>) return MGS_BF16;
+  else return MGS_F16;
 }
 
 }  // namespace mgs

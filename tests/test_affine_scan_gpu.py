@@ -94,8 +94,26 @@ def test_affine_vs_oracle(cuda, case):
     np.testing.assert_allclose(dB, rdB, **BWD)
 
 
+# Shapes that take the TMA strip path (k (k+v) <= 8, >= ~3/4 of the SMs'
+# worth of 32-block strips): a ragged T and a partial last strip (n = 250),
+# k = 1, and v = 2.
+STRIP_CASES = [(14, 77, 250, 2, 1), (4, 100, 1024, 1, 1), (8, 65, 512, 2, 2)]
+
+
+@pytest.mark.parametrize("case", STRIP_CASES)
+def test_affine_strip_path_vs_oracle(cuda, case):
+    A, Bm, gA, gB = contractive_inputs(*case, seed=sum(case))
+    rA, rB = oracle.matrix_affine_scan(A, Bm)
+    rdA, rdB = oracle.matrix_affine_scan_bwd(A, rA, rB, gA, gB)
+    Ab, Bb, dA, dB = run_affine(A, Bm, gA, gB, cuda)
+    np.testing.assert_allclose(Ab, rA, **FWD)
+    np.testing.assert_allclose(Bb, rB, **FWD)
+    np.testing.assert_allclose(dA, rdA, **BWD)
+    np.testing.assert_allclose(dB, rdB, **BWD)
+
+
 @pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
-@pytest.mark.parametrize("case", [(2, 40, 33, 2, 1), (1, 20, 9, 8, 1)])
+@pytest.mark.parametrize("case", [(2, 40, 33, 2, 1), (1, 20, 9, 8, 1), (16, 96, 256, 2, 1)])
 def test_affine_half_inputs(cuda, case, dtype):
     A, Bm, gA, gB = contractive_inputs(*case, seed=3)
     rnd = lambda x: torch.as_tensor(x, dtype=torch.float32).to(dtype).double().numpy()
