@@ -63,10 +63,10 @@ __device__ __forceinline__ int up16(int x) { return (x + 15) & ~15; }
 
 // 64 rows x (NCH * 8 columns) bf16 block of a row-major global matrix (leading
 // dimension ld elements) into a tile; rows >= nrows / chunks >= ncols8 zero.
-template <int NCH>
+template <int NCH, int NTHR = kTcThreads>
 __device__ __forceinline__ void stage_rows(bf16* tile, const bf16* g, long long ld, int nrows,
                                            int valid_ch) {
-  for (int i = threadIdx.x; i < 64 * NCH; i += kTcThreads) {
+  for (int i = threadIdx.x; i < 64 * NCH; i += NTHR) {
     const int row = i / NCH, ch = i - row * NCH;
     const bool ok = row < nrows && ch < valid_ch;
     cp_async16(tile + row * kLd + ch * 8, ok ? g + row * ld + ch * 8 : g, ok ? 16 : 0);
@@ -159,8 +159,9 @@ __device__ __forceinline__ void tile_to_global(const bf16* t, bf16* g) {
         *reinterpret_cast<const uint4*>(t + row * kLd + ch * 8);
   }
 }
+template <int NTHR = kTcThreads>
 __device__ __forceinline__ void tile_from_global_async(bf16* t, const bf16* g) {
-  for (int i = threadIdx.x; i < 64 * 8; i += kTcThreads) {
+  for (int i = threadIdx.x; i < 64 * 8; i += NTHR) {
     const int row = i >> 3, ch = i & 7;
     cp_async16(t + row * kLd + ch * 8, g + row * 64 + ch * 8, 16);
   }
@@ -553,7 +554,9 @@ __global__ void __launch_bounds__(kTcThreads, 1) bwd_chain_kernel(const TcArgs p
 constexpr size_t kGradSmem = 4 * (size_t)kTileBytes + 512 + 4 * (size_t)kTileBytes +
                              2 * (size_t)kF32Bytes + 12 * (size_t)kTileBytes;
 
-__global__ void __launch_bounds__(kTcThreads, 1) bwd_grads_kernel(const TcArgs p) {
+constexpr int kGradThreads = 512;  // 16 warps: warp (mt, q) = (w & 3, w >> 2)
+
+__global__ void __launch_bounds__(kGradThreads, 1) bwd_grads_kernel(const TcArgs p) {
   extern __shared__ __align__(128) unsigned char smem[];
   bf16* K = reinterpret_cast<bf16*>(smem);
   bf16* Q = K + kTile;
@@ -580,8 +583,10 @@ __global__ void __launch_bounds__(kTcThreads, 1) bwd_grads_kernel(const TcArgs p
   bf16 *TiH = R10, *TiL = R10 + kTile, *dKH = R10, *dKL = R10 + kTile;
   bf16 *PH = R11, *PL = R11 + kTile, *dSH = R11, *dSL = R11 + kTile;
 
-  const int tid = threadIdx.x, warp = tid >> 5, mt = warp & 3, half = warp >> 2;
-  const int m0 = 16 * mt, n0 = 32 * half;
+  constexpr int NTH = kGradThreads;
+  const int tid = threadIdx.x, warp = tid >> 5, mt = warp & 3, q = warp >> 2;
+  const int m0 = 16 * mt, n0 = 16 * q;       // 16 x 16 tiles of the 64 x 64 products
+  const int hf = q & 1, mat = q >> 1;        // 16 x 32 tiles of the masked products
   const int c = blockIdx.x % p.nchunks;
   const long long bh = blockIdx.x / p.nchunks;
   const long long t0 = (long long)c * p.C;
@@ -591,19 +596,19 @@ __global__ void __launch_bounds__(kTcThreads, 1) bwd_grads_kernel(const TcArgs p
   const long long rows = p.T * p.nh;
   const long long sofs = (bh * p.nchunks + c) * (long long)p.dk * p.dv;
 
-  stage_rows<8>(K, p.K + (bh * rows + r0) * p.dk, p.dk, Mc, p.dk >> 3);
-  stage_rows<8>(Q, p.Q + (bh * p.T + t0) * p.dk, p.dk, Cc, p.dk >> 3);
-  stage_rows<8>(dY, p.dy + (bh * p.T + t0) * p.dv, p.dv, Cc, p.dv >> 3);
-  stage_rows<8>(V, p.V + (bh * rows + r0) * p.dv, p.dv, Mc, p.dv >> 3);
-  tile_from_global_async(TiH, p.Ti + (bh * p.nchunks + c) * 8192);
-  tile_from_global_async(TiL, p.Ti + (bh * p.nchunks + c) * 8192 + 4096);
+  stage_rows<8, NTH>(K, p.K + (bh * rows + r0) * p.dk, p.dk, Mc, p.dk >> 3);
+  stage_rows<8, NTH>(Q, p.Q + (bh * p.T + t0) * p.dk, p.dk, Cc, p.dk >> 3);
+  stage_rows<8, NTH>(dY, p.dy + (bh * p.T + t0) * p.dv, p.dv, Cc, p.dv >> 3);
+  stage_rows<8, NTH>(V, p.V + (bh * rows + r0) * p.dv, p.dv, Mc, p.dv >> 3);
+  tile_from_global_async<NTH>(TiH, p.Ti + (bh * p.nchunks + c) * 8192);
+  tile_from_global_async<NTH>(TiL, p.Ti + (bh * p.nchunks + c) * 8192 + 4096);
   cp_async_commit();
   if (tid < 64) {
     bs[tid] = tid < Mc ? __bfloat162float(p.beta[bh * rows + r0 + tid]) : 0.f;
     dbs[tid] = 0.f;
   }
   // S (chunk-start state) and dS' -> split tiles (rows d_k, cols d_v)
-  for (int i = tid; i < 64 * 32; i += kTcThreads) {
+  for (int i = tid; i < 64 * 32; i += NTH) {
     const int row = i >> 5, col = (i & 31) << 1;
     float2 a = make_float2(0.f, 0.f), b = make_float2(0.f, 0.f);
     if (row < p.dk && col < p.dv) {
@@ -621,49 +626,49 @@ __global__ void __launch_bounds__(kTcThreads, 1) bwd_grads_kernel(const TcArgs p
   cp_async_wait_all();
   __syncthreads();
 
+  // K K^T (warps mat 0) / Q K^T (mat 1): row tile m0, columns 32*hf..
   {
-    float acc[8][4];
-    if (half == 0) {
-      kk_rows(K, m0, kd, acc);
+    float acc[4][4];
+    tc::zero(acc);
+    const int ncol = mat == 0 ? m0 + 16 : min(64, (m0 + 16) * p.nh);
+    const int np = min(2, max(0, (ncol - 32 * hf + 15) / 16));
+    tc::gemm<4, false, false>(acc, Op{mat == 0 ? K : Q, nullptr}, m0, Op{K, nullptr}, 32 * hf, 0,
+                              kd, np);
+    float* dst = mat == 0 ? KKf : QKf;
 #pragma unroll
-      for (int j = 0; j < 8; ++j)
+    for (int j = 0; j < 4; ++j)
 #pragma unroll
-        for (int v = 0; v < 4; ++v)
-          KKf[tc::frag_row(m0, v) * kTld + tc::frag_col(0, j, v)] = acc[j][v];
-    } else {
-      qk_rows(Q, K, m0, kd, p.nh, acc);
-#pragma unroll
-      for (int j = 0; j < 8; ++j)
-#pragma unroll
-        for (int v = 0; v < 4; ++v)
-          QKf[tc::frag_row(m0, v) * kTld + tc::frag_col(0, j, v)] = acc[j][v];
-      store_P(acc, bs, p.nh, Mc, m0, PH, PL);
-    }
+      for (int v = 0; v < 4; ++v)
+        dst[tc::frag_row(m0, v) * kTld + tc::frag_col(32 * hf, j, v)] = acc[j][v];
+    if (mat == 1)
+      tc::store_split(acc, PH, PL, m0, 32 * hf, [&](int r, int cl, float x) {
+        return (cl < (r + 1) * p.nh && cl < Mc) ? x * bs[cl] : 0.f;
+      });
   }
 
-  // W = Ti K, U' = Ti V (rows m0, columns n0..n0+31)
-  float u[4][4];
+  // W = Ti K, U' = Ti V (rows m0, columns n0..n0+15)
+  float u[2][4];
   {
-    float w[4][4];
+    float w[2][4];
     tc::zero(w);
-    tc::gemm<4, false, true>(w, Op{TiH, TiL}, m0, Op{K, nullptr}, n0, 0, m0 + 16);
+    tc::gemm<2, false, true>(w, Op{TiH, TiL}, m0, Op{K, nullptr}, n0, 0, m0 + 16);
     tc::store_split(w, WH, WL, m0, n0, Ident());
     tc::zero(u);
-    tc::gemm<4, false, true>(u, Op{TiH, TiL}, m0, Op{V, nullptr}, n0, 0, m0 + 16);
+    tc::gemm<2, false, true>(u, Op{TiH, TiL}, m0, Op{V, nullptr}, n0, 0, m0 + 16);
   }
   __syncthreads();
   // U = U' - W S;  dbU = K dS';  dU = P^T dy + beta dbU;  dbeta += rowsum(U * dbU)
   {
-    float ws[4][4], db[4][4], du[4][4];
+    float ws[2][4], db[2][4], du[2][4];
     tc::zero(ws);
     tc::zero(db);
     tc::zero(du);
-    tc::gemm<4, false, true>(ws, Op{WH, WL}, m0, Op{SH, SL}, n0, 0, kd);
-    tc::gemm<4, false, true>(db, Op{K, nullptr}, m0, Op{DH, DL}, n0, 0, kd);
-    tc::gemm<4, true, true>(du, Op{PH, PL}, m0, Op{dY, nullptr}, n0, (m0 / p.nh) & ~15, up16(Cc));
+    tc::gemm<2, false, true>(ws, Op{WH, WL}, m0, Op{SH, SL}, n0, 0, kd);
+    tc::gemm<2, false, true>(db, Op{K, nullptr}, m0, Op{DH, DL}, n0, 0, kd);
+    tc::gemm<2, true, true>(du, Op{PH, PL}, m0, Op{dY, nullptr}, n0, (m0 / p.nh) & ~15, up16(Cc));
     float rs[2] = {0.f, 0.f};
 #pragma unroll
-    for (int j = 0; j < 4; ++j)
+    for (int j = 0; j < 2; ++j)
 #pragma unroll
       for (int v = 0; v < 4; ++v) {
         u[j][v] -= ws[j][v];
@@ -686,48 +691,30 @@ __global__ void __launch_bounds__(kTcThreads, 1) bwd_grads_kernel(const TcArgs p
   __syncthreads();
   // G = Ti^T dU -> dV; Gn = -G
   {
-    float g[4][4];
+    float g[2][4];
     tc::zero(g);
-    tc::gemm<4, true, true>(g, Op{TiH, TiL}, m0, Op{dUH, dUL}, n0, m0, 64);
+    tc::gemm<2, true, true>(g, Op{TiH, TiL}, m0, Op{dUH, dUL}, n0, m0, 64);
     frag_to_global_bf16(g, p.dV + (bh * rows + r0) * p.dv, p.dv, m0, n0, Mc, p.dv);
     tc::store_split(g, GH, GL, m0, n0, [](int, int, float x) { return -x; });
   }
   __syncthreads();
-  // warp (mat, mt): mat 0: dS_ = (dy U^T) beta * read; mat 1: dKK = (Gn U^T) beta * strict
+  // warp (mat, mt, hf): mat 0: dS_ = (dy U^T) beta * read; mat 1: dKK = (Gn U^T) beta * strict
   {
-    float acc[8][4];
+    float acc[4][4];
     tc::zero(acc);
-    const bool m1 = (warp >> 2) != 0;
+    const bool m1 = mat != 0;
     const int ncol = m1 ? min(64, m0 + 16) : min(64, (m0 + 16) * p.nh);
-    const Op A = m1 ? Op{GH, GL} : Op{dY, nullptr};
-    for (int k0 = 0; k0 < kv; k0 += 16) {
-      uint32_t ah[4], al[4];
-      tc::load_a<false>(A.hi, m0, k0, ah);
-      if (A.lo) tc::load_a<false>(A.lo, m0, k0, al);
-#pragma unroll
-      for (int j = 0; j < 8; j += 2) {
-        if (8 * j >= ncol) break;
-        uint32_t bh_[4], bl[4];
-        tc::load_b<false>(UH, k0, 8 * j, bh_);
-        tc::load_b<false>(UL, k0, 8 * j, bl);
-        tc::mma(acc[j], ah, bh_[0], bh_[1]);
-        tc::mma(acc[j + 1], ah, bh_[2], bh_[3]);
-        tc::mma(acc[j], ah, bl[0], bl[1]);
-        tc::mma(acc[j + 1], ah, bl[2], bl[3]);
-        if (A.lo) {
-          tc::mma(acc[j], al, bh_[0], bh_[1]);
-          tc::mma(acc[j + 1], al, bh_[2], bh_[3]);
-        }
-      }
-    }
+    const int np = min(2, max(0, (ncol - 32 * hf + 15) / 16));
+    tc::gemm<4, false, false>(acc, m1 ? Op{GH, GL} : Op{dY, nullptr}, m0, Op{UH, UL}, 32 * hf, 0,
+                              kv, np);
     // masked product, dbeta column terms, split store
-    float cs[8][2];
+    float cs[4][2];
 #pragma unroll
-    for (int j = 0; j < 8; ++j) {
+    for (int j = 0; j < 4; ++j) {
       cs[j][0] = cs[j][1] = 0.f;
 #pragma unroll
       for (int v = 0; v < 4; ++v) {
-        const int row = tc::frag_row(m0, v), col = tc::frag_col(0, j, v);
+        const int row = tc::frag_row(m0, v), col = tc::frag_col(32 * hf, j, v);
         const bool keep = m1 ? (col < row && col < Mc) : (col < (row + 1) * p.nh && col < Mc);
         const float x = keep ? acc[j][v] : 0.f;
         cs[j][v & 1] += x * (m1 ? KKf[row * kTld + col] : QKf[row * kTld + col]);
@@ -735,37 +722,37 @@ __global__ void __launch_bounds__(kTcThreads, 1) bwd_grads_kernel(const TcArgs p
       }
     }
 #pragma unroll
-    for (int j = 0; j < 8; ++j)
+    for (int j = 0; j < 4; ++j)
 #pragma unroll
       for (int e = 0; e < 2; ++e) {
         float x = cs[j][e];
         x += __shfl_xor_sync(0xffffffffu, x, 4);
         x += __shfl_xor_sync(0xffffffffu, x, 8);
         x += __shfl_xor_sync(0xffffffffu, x, 16);
-        if ((tid & 31) < 4) atomicAdd(&dbs[tc::frag_col(0, j, e)], x);
+        if ((tid & 31) < 4) atomicAdd(&dbs[tc::frag_col(32 * hf, j, e)], x);
       }
-    tc::store_split(acc, m1 ? dKH : dSH, m1 ? dKL : dSL, m0, 0, Ident());
+    tc::store_split(acc, m1 ? dKH : dSH, m1 ? dKL : dSL, m0, 32 * hf, Ident());
   }
   __syncthreads();
   // dQ (token rows m0, d_k columns n0..) = dy S^T + dS_ K
   {
-    float dq[4][4];
+    float dq[2][4];
     tc::zero(dq);
-    tc::gemm<4, false, false>(dq, Op{dY, nullptr}, m0, Op{SH, SL}, n0, 0, kv);
-    tc::gemm<4, false, true>(dq, Op{dSH, dSL}, m0, Op{K, nullptr}, n0, 0,
+    tc::gemm<2, false, false>(dq, Op{dY, nullptr}, m0, Op{SH, SL}, n0, 0, kv);
+    tc::gemm<2, false, true>(dq, Op{dSH, dSL}, m0, Op{K, nullptr}, n0, 0,
                              min(64, up16((m0 + 16) * p.nh)));
     frag_to_global_bf16(dq, p.dQ + (bh * p.T + t0) * p.dk, p.dk, m0, n0, Cc, p.dk);
   }
   // dK (micro-step rows m0, d_k columns n0..) =
   //   (beta U) dS'^T + dS_^T Q + Gn S^T + dKK K + dKK^T K
   {
-    float dk[4][4];
+    float dk[2][4];
     tc::zero(dk);
-    tc::gemm<4, false, false>(dk, Op{BUH, BUL}, m0, Op{DH, DL}, n0, 0, kv);
-    tc::gemm<4, true, true>(dk, Op{dSH, dSL}, m0, Op{Q, nullptr}, n0, (m0 / p.nh) & ~15, up16(Cc));
-    tc::gemm<4, false, false>(dk, Op{GH, GL}, m0, Op{SH, SL}, n0, 0, kv);
-    tc::gemm<4, false, true>(dk, Op{dKH, dKL}, m0, Op{K, nullptr}, n0, 0, m0 + 16);
-    tc::gemm<4, true, true>(dk, Op{dKH, dKL}, m0, Op{K, nullptr}, n0, m0, 64);
+    tc::gemm<2, false, false>(dk, Op{BUH, BUL}, m0, Op{DH, DL}, n0, 0, kv);
+    tc::gemm<2, true, true>(dk, Op{dSH, dSL}, m0, Op{Q, nullptr}, n0, (m0 / p.nh) & ~15, up16(Cc));
+    tc::gemm<2, false, false>(dk, Op{GH, GL}, m0, Op{SH, SL}, n0, 0, kv);
+    tc::gemm<2, false, true>(dk, Op{dKH, dKL}, m0, Op{K, nullptr}, n0, 0, m0 + 16);
+    tc::gemm<2, true, true>(dk, Op{dKH, dKL}, m0, Op{K, nullptr}, n0, m0, 64);
     frag_to_global_bf16(dk, p.dK + (bh * rows + r0) * p.dk, p.dk, m0, n0, Mc, p.dk);
   }
   __syncthreads();
@@ -789,11 +776,12 @@ int splits_for(long long BH, int dv) {
 }
 
 template <class K>
-int launch_tc(K kernel, long long grid, size_t smem, cudaStream_t st, const TcArgs& a) {
+int launch_tc(K kernel, long long grid, size_t smem, cudaStream_t st, const TcArgs& a,
+              int threads = kTcThreads) {
   MGS_CUDA_OK(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
   TcArgs args = a;
   void* kargs[] = {&args};
-  MGS_CUDA_OK(cudaLaunchKernel((const void*)kernel, dim3((unsigned)grid), dim3(kTcThreads), kargs,
+  MGS_CUDA_OK(cudaLaunchKernel((const void*)kernel, dim3((unsigned)grid), dim3(threads), kargs,
                                smem, st));
   return MGS_OK;
 }
@@ -872,7 +860,7 @@ int run_tc(bool fwd, const Args<__nv_bfloat16>& p, long long B, int H, long long
   int rc = narrow ? launch_tc(bwd_chain_kernel<32>, BH * a.S, kChainSmem, st, a)
                   : launch_tc(bwd_chain_kernel<64>, BH * a.S, kChainSmem, st, a);
   if (rc != MGS_OK) return rc;
-  return launch_tc(bwd_grads_kernel, BH * a.nchunks, kGradSmem, st, a);
+  return launch_tc(bwd_grads_kernel, BH * a.nchunks, kGradSmem, st, a, kGradThreads);
 }
 
 }  // namespace delta
