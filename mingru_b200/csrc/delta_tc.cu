@@ -141,8 +141,9 @@ __device__ void tri_inv_tc(const float* Tf, Op TS, bf16* XH, bf16* XL, bf16* YH,
 }
 
 // Zero the strictly-upper 16 x 16 blocks of a split tile pair (once per kernel).
+template <int NTHR = kTcThreads>
 __device__ void zero_upper_blocks(bf16* H, bf16* L) {
-  for (int i = threadIdx.x; i < 64 * 64; i += kTcThreads) {
+  for (int i = threadIdx.x; i < 64 * 64; i += NTHR) {
     const int row = i >> 6, col = i & 63;
     if ((col >> 4) > (row >> 4)) {
       H[row * kLd + col] = __float2bfloat16_rn(0.f);
@@ -152,8 +153,9 @@ __device__ void zero_upper_blocks(bf16* H, bf16* L) {
 }
 
 // 64 x 64 bf16 tile <-> dense global 64 x 64 (16-byte vectors, all threads).
+template <int NTHR = kTcThreads>
 __device__ __forceinline__ void tile_to_global(const bf16* t, bf16* g) {
-  for (int i = threadIdx.x; i < 64 * 8; i += kTcThreads) {
+  for (int i = threadIdx.x; i < 64 * 8; i += NTHR) {
     const int row = i >> 3, ch = i & 7;
     *reinterpret_cast<uint4*>(g + row * 64 + ch * 8) =
         *reinterpret_cast<const uint4*>(t + row * kLd + ch * 8);
@@ -214,39 +216,27 @@ __device__ __forceinline__ void frag_from_global(float (&c)[NT][4], const float*
 // ---- chunk matrices from K K^T and Q K^T (exact bf16 products, fp32 sums).
 // Warp w: row tile w & 3; warps 0-3 one product, warps 4-7 the other.
 
-// K K^T of row tile m0, the column tiles left of and on the diagonal.
-__device__ __forceinline__ void kk_rows(const bf16* Kt, int m0, int kd, float (&acc)[8][4]) {
-  tc::zero(acc);
-  tc::gemm<8, false, false>(acc, Op{Kt, nullptr}, m0, Op{Kt, nullptr}, 0, 0, kd, m0 / 16 + 1);
-}
-
-// Q K^T of token row tile m0 over the readable micro-step columns.
-__device__ __forceinline__ void qk_rows(const bf16* Qt, const bf16* Kt, int m0, int kd, int nh,
-                                       float (&acc)[8][4]) {
-  tc::zero(acc);
-  tc::gemm<8, false, false>(acc, Op{Qt, nullptr}, m0, Op{Kt, nullptr}, 0, 0, kd,
-                            (min(64, (m0 + 16) * nh) + 15) / 16);
-}
-
-// P = (Q K^T) diag(beta) * read  as split tiles
-__device__ __forceinline__ void store_P(const float (&acc)[8][4], const float* bs, int nh, int Mc,
-                                        int m0, bf16* PH, bf16* PL) {
-  tc::store_split(acc, PH, PL, m0, 0, [&](int r, int cl, float x) {
+// P = (Q K^T) diag(beta) * read  as split tiles (NT n-tiles at columns n0..)
+template <int NT>
+__device__ __forceinline__ void store_P(const float (&acc)[NT][4], const float* bs, int nh, int Mc,
+                                        int m0, int n0, bf16* PH, bf16* PL) {
+  tc::store_split(acc, PH, PL, m0, n0, [&](int r, int cl, float x) {
     return (cl < (r + 1) * nh && cl < Mc) ? x * bs[cl] : 0.f;
   });
 }
 
 // T's strict lower part (K K^T diag(beta)) as fp32 (diagonal blocks) and split tiles.
-__device__ __forceinline__ void store_T(const float (&acc)[8][4], const float* bs, int m0,
+template <int NT>
+__device__ __forceinline__ void store_T(const float (&acc)[NT][4], const float* bs, int m0, int n0,
                                         float* Tf, bf16* TH, bf16* TL) {
 #pragma unroll
-  for (int j = 0; j < 8; ++j)
+  for (int j = 0; j < NT; ++j)
 #pragma unroll
     for (int v = 0; v < 4; ++v) {
-      const int row = tc::frag_row(m0, v), col = tc::frag_col(0, j, v);
+      const int row = tc::frag_row(m0, v), col = tc::frag_col(n0, j, v);
       if ((col >> 4) == (row >> 4)) Tf[row * kTld + col] = col < row ? acc[j][v] * bs[col] : 0.f;
     }
-  tc::store_split(acc, TH, TL, m0, 0,
+  tc::store_split(acc, TH, TL, m0, n0,
                   [&](int r, int cl, float x) { return cl < r ? x * bs[cl] : 0.f; });
 }
 
@@ -276,10 +266,15 @@ struct TcArgs {
 // smem: 2 stages {K, Q, V_s, beta} | Ti h/l | W h/l (inverse scratch first) |
 //       P h/l | S h/l | U h/l (T fp32 first) | bU h/l (T split first)
 constexpr size_t kFwdSmem = 2 * kStageBytes + 12 * (size_t)kTileBytes;
+constexpr int kSerialThreads = 512;  // 16 warps: warp (mt, q) = (w & 3, w >> 2)
 
+// Warp tiling of the chunk-serial kernels: rows 16*mt; 64-wide products in
+// 16-column quarters (q), the DVS value columns in quarters of DVS/4, and the
+// two masked K K^T / Q K^T products as (matrix q >> 1, 32-column half q & 1).
 template <int DVS>
-__global__ void __launch_bounds__(kTcThreads, 1) fwd_kernel(const TcArgs p) {
-  constexpr int NTV = DVS / 16;  // n-tiles of a warp's half of the value columns
+__global__ void __launch_bounds__(kSerialThreads, 1) fwd_kernel(const TcArgs p) {
+  constexpr int NTQ = DVS / 32;  // n-tiles of a warp's quarter of the value columns
+  constexpr int NTH = kSerialThreads;
   extern __shared__ __align__(128) unsigned char smem[];
   unsigned char* rest = smem + 2 * kStageBytes;
   bf16* TiH = reinterpret_cast<bf16*>(rest);
@@ -301,8 +296,8 @@ __global__ void __launch_bounds__(kTcThreads, 1) fwd_kernel(const TcArgs p) {
   auto Vt = [&](int s) { return Kt(s) + 2 * kTile; };
   auto Bt = [&](int s) { return reinterpret_cast<float*>(smem + s * kStageBytes + 3 * kTileBytes); };
 
-  const int tid = threadIdx.x, warp = tid >> 5, mt = warp & 3, half = warp >> 2;
-  const int m0 = 16 * mt, n0 = half * (DVS / 2);
+  const int tid = threadIdx.x, warp = tid >> 5, mt = warp & 3, q = warp >> 2;
+  const int m0 = 16 * mt, nv = q * (DVS / 4), mat = q >> 1, hf = q & 1;
   const int split = blockIdx.x % p.S;
   const long long bh = blockIdx.x / p.S;
   const int c0 = split * p.dvs, ncols = min(p.dvs, p.dv - c0);
@@ -319,9 +314,9 @@ __global__ void __launch_bounds__(kTcThreads, 1) fwd_kernel(const TcArgs p) {
   auto stage = [&](int c, int s) {
     const long long t0 = (long long)c * p.C;
     const int Cc = (int)min((long long)p.C, p.T - t0), Mc = Cc * p.nh;
-    stage_rows<8>(Kt(s), Kg + t0 * p.nh * p.dk, p.dk, Mc, p.dk >> 3);
-    stage_rows<8>(Qt(s), Qg + t0 * p.dk, p.dk, Cc, p.dk >> 3);
-    stage_rows<DVS / 8>(Vt(s), Vg + t0 * p.nh * p.dv, p.dv, Mc, ncols >> 3);
+    stage_rows<8, NTH>(Kt(s), Kg + t0 * p.nh * p.dk, p.dk, Mc, p.dk >> 3);
+    stage_rows<8, NTH>(Qt(s), Qg + t0 * p.dk, p.dk, Cc, p.dk >> 3);
+    stage_rows<DVS / 8, NTH>(Vt(s), Vg + t0 * p.nh * p.dv, p.dv, Mc, ncols >> 3);
     cp_async_commit();
   };
   auto beta_of = [&](int c) {
@@ -330,14 +325,14 @@ __global__ void __launch_bounds__(kTcThreads, 1) fwd_kernel(const TcArgs p) {
     return tid < Mc ? __bfloat162float(bg[r0 + tid]) : 0.f;
   };
 
-  // state slice: rows m0.. of d_k, value columns n0.. of this split
-  float hs[NTV][4];
+  // state slice: d_k rows m0.., value columns nv.. of this split
+  float hs[NTQ][4];
   if (p.H0)
-    frag_from_global(hs, p.H0 + bh * p.dk * p.dv + c0, p.dv, m0, n0, p.dk, ncols);
+    frag_from_global(hs, p.H0 + bh * p.dk * p.dv + c0, p.dv, m0, nv, p.dk, ncols);
   else
     tc::zero(hs);
-  tc::store_split(hs, SH, SL, m0, n0, Ident());
-  zero_upper_blocks(TiH, TiL);
+  tc::store_split(hs, SH, SL, m0, nv, Ident());
+  zero_upper_blocks<NTH>(TiH, TiL);
   stage(0, 0);
   if (tid < 64) Bt(0)[tid] = beta_of(0);
   float bnext = 0.f;
@@ -356,67 +351,69 @@ __global__ void __launch_bounds__(kTcThreads, 1) fwd_kernel(const TcArgs p) {
     const bf16* Q = Qt(s);
     const bf16* V = Vt(s);
     const float* bs = Bt(s);
-    frag_to_global(hs, Hsg + (long long)c * p.dk * p.dv, p.dv, m0, n0, p.dk, ncols);
+    frag_to_global(hs, Hsg + (long long)c * p.dk * p.dv, p.dv, m0, nv, p.dk, ncols);
 
     {
-      float acc[8][4];
-      if (half == 0) {
-        kk_rows(K, m0, kd, acc);
-        store_T(acc, bs, m0, Tf, TH, TL);
-      } else {
-        qk_rows(Q, K, m0, kd, p.nh, acc);
-        store_P(acc, bs, p.nh, Mc, m0, PH, PL);
-      }
+      float acc[4][4];
+      tc::zero(acc);
+      const int ncol = mat == 0 ? m0 + 16 : min(64, (m0 + 16) * p.nh);
+      const int np = min(2, max(0, (ncol - 32 * hf + 15) / 16));
+      tc::gemm<4, false, false>(acc, Op{mat == 0 ? K : Q, nullptr}, m0, Op{K, nullptr}, 32 * hf,
+                                0, kd, np);
+      if (mat == 0)
+        store_T(acc, bs, m0, 32 * hf, Tf, TH, TL);
+      else
+        store_P(acc, bs, p.nh, Mc, m0, 32 * hf, PH, PL);
     }
     __syncthreads();
     tri_inv_tc(Tf, Op{TH, TL}, TiH, TiL, YH, YL);
     if (split == 0) {
-      tile_to_global(TiH, Tig + (long long)c * 8192);
-      tile_to_global(TiL, Tig + (long long)c * 8192 + 4096);
+      tile_to_global<NTH>(TiH, Tig + (long long)c * 8192);
+      tile_to_global<NTH>(TiL, Tig + (long long)c * 8192 + 4096);
     }
 
-    // W = Ti K (this warp: rows m0, d_k columns 32*half..), U' = Ti V
+    // W = Ti K (rows m0, d_k columns 16q..), U' = Ti V (value columns nv..)
     {
-      float w[4][4];
+      float w[2][4];
       tc::zero(w);
-      tc::gemm<4, false, true>(w, Op{TiH, TiL}, m0, Op{K, nullptr}, 32 * half, 0, m0 + 16);
-      tc::store_split(w, WH, WL, m0, 32 * half, Ident());
+      tc::gemm<2, false, true>(w, Op{TiH, TiL}, m0, Op{K, nullptr}, 16 * q, 0, m0 + 16);
+      tc::store_split(w, WH, WL, m0, 16 * q, Ident());
     }
-    float u[NTV][4];
+    float u[NTQ][4];
     tc::zero(u);
-    tc::gemm<NTV, false, true>(u, Op{TiH, TiL}, m0, Op{V, nullptr}, n0, 0, m0 + 16);
+    tc::gemm<NTQ, false, true>(u, Op{TiH, TiL}, m0, Op{V, nullptr}, nv, 0, m0 + 16);
     __syncthreads();
 
     // U = U' - W S
     {
-      float ws[NTV][4];
+      float ws[NTQ][4];
       tc::zero(ws);
-      tc::gemm<NTV, false, true>(ws, Op{WH, WL}, m0, Op{SH, SL}, n0, 0, kd);
+      tc::gemm<NTQ, false, true>(ws, Op{WH, WL}, m0, Op{SH, SL}, nv, 0, kd);
 #pragma unroll
-      for (int j = 0; j < NTV; ++j)
+      for (int j = 0; j < NTQ; ++j)
 #pragma unroll
         for (int v = 0; v < 4; ++v) u[j][v] -= ws[j][v];
     }
-    tc::store_split(u, UH, UL, m0, n0, Ident());
-    tc::store_split(u, BUH, BUL, m0, n0, [&](int r, int, float x) { return x * bs[r]; });
+    tc::store_split(u, UH, UL, m0, nv, Ident());
+    tc::store_split(u, BUH, BUL, m0, nv, [&](int r, int, float x) { return x * bs[r]; });
     __syncthreads();
 
     // y = Q S + P U (token rows m0..)
     {
-      float yv[NTV][4];
+      float yv[NTQ][4];
       tc::zero(yv);
-      tc::gemm<NTV, false, true>(yv, Op{Q, nullptr}, m0, Op{SH, SL}, n0, 0, kd);
-      tc::gemm<NTV, false, true>(yv, Op{PH, PL}, m0, Op{UH, UL}, n0, 0,
+      tc::gemm<NTQ, false, true>(yv, Op{Q, nullptr}, m0, Op{SH, SL}, nv, 0, kd);
+      tc::gemm<NTQ, false, true>(yv, Op{PH, PL}, m0, Op{UH, UL}, nv, 0,
                                  min(64, up16((m0 + 16) * p.nh)));
-      frag_to_global_bf16(yv, yg + t0 * p.dv, p.dv, m0, n0, Cc, ncols);
+      frag_to_global_bf16(yv, yg + t0 * p.dv, p.dv, m0, nv, Cc, ncols);
     }
     // S += K^T (beta U) (d_k rows m0..)
-    tc::gemm<NTV, true, true>(hs, Op{K, nullptr}, m0, Op{BUH, BUL}, n0, 0, up16(Mc));
+    tc::gemm<NTQ, true, true>(hs, Op{K, nullptr}, m0, Op{BUH, BUL}, nv, 0, up16(Mc));
     __syncthreads();
-    tc::store_split(hs, SH, SL, m0, n0, Ident());
+    tc::store_split(hs, SH, SL, m0, nv, Ident());
     if (tid < 64 && c + 1 < p.nchunks) Bt(s ^ 1)[tid] = bnext;
   }
-  frag_to_global(hs, p.HT + bh * p.dk * p.dv + c0, p.dv, m0, n0, p.dk, ncols);
+  frag_to_global(hs, p.HT + bh * p.dk * p.dv + c0, p.dv, m0, nv, p.dk, ncols);
 }
 
 // ----------------------------------------------------- backward: chain --
@@ -425,8 +422,9 @@ constexpr int kChainStage = 5 * kTileBytes + 256;
 constexpr size_t kChainSmem = 2 * (size_t)kChainStage + 8 * (size_t)kTileBytes;
 
 template <int DVS>
-__global__ void __launch_bounds__(kTcThreads, 1) bwd_chain_kernel(const TcArgs p) {
-  constexpr int NTV = DVS / 16;
+__global__ void __launch_bounds__(kSerialThreads, 1) bwd_chain_kernel(const TcArgs p) {
+  constexpr int NTQ = DVS / 32;
+  constexpr int NTH = kSerialThreads;
   extern __shared__ __align__(128) unsigned char smem[];
   unsigned char* rest = smem + 2 * kChainStage;
   bf16* PH = reinterpret_cast<bf16*>(rest);
@@ -444,8 +442,8 @@ __global__ void __launch_bounds__(kTcThreads, 1) bwd_chain_kernel(const TcArgs p
   auto TiLt = [&](int s) { return Kt(s) + 4 * kTile; };
   auto Bt = [&](int s) { return reinterpret_cast<float*>(smem + s * kChainStage + 5 * kTileBytes); };
 
-  const int tid = threadIdx.x, warp = tid >> 5, mt = warp & 3, half = warp >> 2;
-  const int m0 = 16 * mt, n0 = half * (DVS / 2);
+  const int tid = threadIdx.x, warp = tid >> 5, mt = warp & 3, q = warp >> 2;
+  const int m0 = 16 * mt, nv = q * (DVS / 4);
   const int split = blockIdx.x % p.S;
   const long long bh = blockIdx.x / p.S;
   const int c0 = split * p.dvs, ncols = min(p.dvs, p.dv - c0);
@@ -461,11 +459,11 @@ __global__ void __launch_bounds__(kTcThreads, 1) bwd_chain_kernel(const TcArgs p
   auto stage = [&](int c, int s) {
     const long long t0 = (long long)c * p.C;
     const int Cc = (int)min((long long)p.C, p.T - t0), Mc = Cc * p.nh;
-    stage_rows<8>(Kt(s), Kg + t0 * p.nh * p.dk, p.dk, Mc, p.dk >> 3);
-    stage_rows<8>(Qt(s), Qg + t0 * p.dk, p.dk, Cc, p.dk >> 3);
-    stage_rows<DVS / 8>(Dt(s), dyg + t0 * p.dv, p.dv, Cc, ncols >> 3);
-    tile_from_global_async(TiHt(s), Tig + (long long)c * 8192);
-    tile_from_global_async(TiLt(s), Tig + (long long)c * 8192 + 4096);
+    stage_rows<8, NTH>(Kt(s), Kg + t0 * p.nh * p.dk, p.dk, Mc, p.dk >> 3);
+    stage_rows<8, NTH>(Qt(s), Qg + t0 * p.dk, p.dk, Cc, p.dk >> 3);
+    stage_rows<DVS / 8, NTH>(Dt(s), dyg + t0 * p.dv, p.dv, Cc, ncols >> 3);
+    tile_from_global_async<NTH>(TiHt(s), Tig + (long long)c * 8192);
+    tile_from_global_async<NTH>(TiLt(s), Tig + (long long)c * 8192 + 4096);
     cp_async_commit();
   };
   auto beta_of = [&](int c) {
@@ -474,19 +472,19 @@ __global__ void __launch_bounds__(kTcThreads, 1) bwd_chain_kernel(const TcArgs p
     return tid < Mc ? __bfloat162float(bg[r0 + tid]) : 0.f;
   };
 
-  float ds[NTV][4];
+  float ds[NTQ][4];
   if (p.dHT)
-    frag_from_global(ds, p.dHT + bh * p.dk * p.dv + c0, p.dv, m0, n0, p.dk, ncols);
+    frag_from_global(ds, p.dHT + bh * p.dk * p.dv + c0, p.dv, m0, nv, p.dk, ncols);
   else
     tc::zero(ds);
-  tc::store_split(ds, DH, DL, m0, n0, Ident());
+  tc::store_split(ds, DH, DL, m0, nv, Ident());
   const int last = p.nchunks - 1;
   stage(last, 0);
   if (tid < 64) Bt(0)[tid] = beta_of(last);
   float bnext = 0.f;
 
-  for (int q = 0; q < p.nchunks; ++q) {
-    const int c = last - q, s = q & 1;
+  for (int qq = 0; qq < p.nchunks; ++qq) {
+    const int c = last - qq, s = qq & 1;
     const long long t0 = (long long)c * p.C;
     const int Cc = (int)min((long long)p.C, p.T - t0), Mc = Cc * p.nh;
     cp_async_wait_all();
@@ -500,51 +498,49 @@ __global__ void __launch_bounds__(kTcThreads, 1) bwd_chain_kernel(const TcArgs p
     const bf16* dY = Dt(s);
     const Op Ti{TiHt(s), TiLt(s)};
     const float* bs = Bt(s);
-    frag_to_global(ds, dHsg + (long long)c * p.dk * p.dv, p.dv, m0, n0, p.dk, ncols);
+    frag_to_global(ds, dHsg + (long long)c * p.dk * p.dv, p.dv, m0, nv, p.dk, ncols);
 
-    // P (token rows m0, micro-step columns 32*half..)
+    // P (token rows m0, micro-step columns 16q..)
     {
-      float acc[4][4];
+      float acc[2][4];
       tc::zero(acc);
-      const int ncol = min(64, (m0 + 16) * p.nh) - 32 * half;
-      tc::gemm<4, false, false>(acc, Op{Q, nullptr}, m0, Op{K, nullptr}, 32 * half, 0, kd,
-                                ncol <= 0 ? 0 : min(2, (ncol + 15) / 16));
-      tc::store_split(acc, PH, PL, m0, 32 * half, [&](int r, int cl, float x) {
-        return (cl < (r + 1) * p.nh && cl < Mc) ? x * bs[cl] : 0.f;
-      });
+      const int ncol = min(64, (m0 + 16) * p.nh) - 16 * q;
+      tc::gemm<2, false, false>(acc, Op{Q, nullptr}, m0, Op{K, nullptr}, 16 * q, 0, kd,
+                                ncol <= 0 ? 0 : 1);
+      store_P(acc, bs, p.nh, Mc, m0, 16 * q, PH, PL);
     }
     __syncthreads();
 
     // dU = P^T dy + beta * (K dS')   (micro-step rows m0..)
     {
-      float du[NTV][4], db[NTV][4];
+      float du[NTQ][4], db[NTQ][4];
       tc::zero(du);
       tc::zero(db);
-      tc::gemm<NTV, false, true>(db, Op{K, nullptr}, m0, Op{DH, DL}, n0, 0, kd);
-      tc::gemm<NTV, true, true>(du, Op{PH, PL}, m0, Op{dY, nullptr}, n0, (m0 / p.nh) & ~15,
+      tc::gemm<NTQ, false, true>(db, Op{K, nullptr}, m0, Op{DH, DL}, nv, 0, kd);
+      tc::gemm<NTQ, true, true>(du, Op{PH, PL}, m0, Op{dY, nullptr}, nv, (m0 / p.nh) & ~15,
                                 up16(Cc));
 #pragma unroll
-      for (int j = 0; j < NTV; ++j)
+      for (int j = 0; j < NTQ; ++j)
 #pragma unroll
         for (int v = 0; v < 4; ++v) du[j][v] += bs[tc::frag_row(m0, v)] * db[j][v];
-      tc::store_split(du, dUH, dUL, m0, n0, Ident());
+      tc::store_split(du, dUH, dUL, m0, nv, Ident());
     }
     __syncthreads();
     // Gn = -Ti^T dU
     {
-      float g[NTV][4];
+      float g[NTQ][4];
       tc::zero(g);
-      tc::gemm<NTV, true, true>(g, Ti, m0, Op{dUH, dUL}, n0, m0, 64);
-      tc::store_split(g, GH, GL, m0, n0, Neg());
+      tc::gemm<NTQ, true, true>(g, Ti, m0, Op{dUH, dUL}, nv, m0, 64);
+      tc::store_split(g, GH, GL, m0, nv, Neg());
     }
     __syncthreads();
     // dS = dS' + Q^T dy + K^T Gn   (d_k rows m0..)
-    tc::gemm<NTV, true, true>(ds, Op{Q, nullptr}, m0, Op{dY, nullptr}, n0, 0, up16(Cc));
-    tc::gemm<NTV, true, true>(ds, Op{K, nullptr}, m0, Op{GH, GL}, n0, 0, up16(Mc));
-    tc::store_split(ds, DH, DL, m0, n0, Ident());
+    tc::gemm<NTQ, true, true>(ds, Op{Q, nullptr}, m0, Op{dY, nullptr}, nv, 0, up16(Cc));
+    tc::gemm<NTQ, true, true>(ds, Op{K, nullptr}, m0, Op{GH, GL}, nv, 0, up16(Mc));
+    tc::store_split(ds, DH, DL, m0, nv, Ident());
     if (tid < 64 && c > 0) Bt(s ^ 1)[tid] = bnext;
   }
-  frag_to_global(ds, p.dH0 + bh * p.dk * p.dv + c0, p.dv, m0, n0, p.dk, ncols);
+  frag_to_global(ds, p.dH0 + bh * p.dk * p.dv + c0, p.dv, m0, nv, p.dk, ncols);
 }
 
 // ----------------------------------------------------- backward: grads --
@@ -843,8 +839,8 @@ int run_tc(bool fwd, const Args<__nv_bfloat16>& p, long long B, int H, long long
         MGS_CUDA_OK(cudaMemsetAsync(p.HT, 0, (size_t)BH * dk * dv * sizeof(float), st));
       return MGS_OK;
     }
-    return narrow ? launch_tc(fwd_kernel<32>, BH * a.S, kFwdSmem, st, a)
-                  : launch_tc(fwd_kernel<64>, BH * a.S, kFwdSmem, st, a);
+    return narrow ? launch_tc(fwd_kernel<32>, BH * a.S, kFwdSmem, st, a, kSerialThreads)
+                  : launch_tc(fwd_kernel<64>, BH * a.S, kFwdSmem, st, a, kSerialThreads);
   }
   if (T == 0) {
     if (p.dHT)
@@ -857,8 +853,8 @@ int run_tc(bool fwd, const Args<__nv_bfloat16>& p, long long B, int H, long long
   if (ws == nullptr || ws_bytes < tc_workspace_floats(BH, T, dk, dv, C) * sizeof(float))
     return MGS_WORKSPACE_TOO_SMALL;
   a.dHs = static_cast<float*>(ws);
-  int rc = narrow ? launch_tc(bwd_chain_kernel<32>, BH * a.S, kChainSmem, st, a)
-                  : launch_tc(bwd_chain_kernel<64>, BH * a.S, kChainSmem, st, a);
+  int rc = narrow ? launch_tc(bwd_chain_kernel<32>, BH * a.S, kChainSmem, st, a, kSerialThreads)
+                  : launch_tc(bwd_chain_kernel<64>, BH * a.S, kChainSmem, st, a, kSerialThreads);
   if (rc != MGS_OK) return rc;
   return launch_tc(bwd_grads_kernel, BH * a.nchunks, kGradSmem, st, a, kGradThreads);
 }

@@ -91,6 +91,30 @@ __device__ __forceinline__ const __nv_bfloat16* b_src(const __nv_bfloat16* t, in
   return t + (k0 + r + ((q & 1) << 3)) * kLd + n0 + ((q >> 1) << 3);
 }
 
+__device__ __forceinline__ void ldsm2(const void* p, uint32_t (&r)[2]) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x2.shared.b16 {%0, %1}, [%2];\n"
+               : "=r"(r[0]), "=r"(r[1])
+               : "r"(smem_addr(p))
+               : "memory");
+}
+
+__device__ __forceinline__ void ldsm2t(const void* p, uint32_t (&r)[2]) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x2.trans.shared.b16 {%0, %1}, [%2];\n"
+               : "=r"(r[0]), "=r"(r[1])
+               : "r"(smem_addr(p))
+               : "memory");
+}
+
+// B fragment of one n-tile (n0..n0+7), k0..k0+15 (lanes 0-15 supply the addresses).
+template <bool KN>
+__device__ __forceinline__ void load_b1(const __nv_bfloat16* t, int k0, int n0, uint32_t (&r)[2]) {
+  const int lane = threadIdx.x & 31, rr = lane & 7, q = (lane >> 3) & 1;
+  if (KN)
+    ldsm2t(t + (k0 + rr + (q << 3)) * kLd + n0, r);  // stored [k][n]
+  else
+    ldsm2(t + (n0 + rr) * kLd + k0 + (q << 3), r);   // stored [n][k]
+}
+
 template <bool COL>
 __device__ __forceinline__ void load_a(const __nv_bfloat16* t, int m0, int k0, uint32_t (&r)[4]) {
   if (COL)
@@ -110,9 +134,24 @@ __device__ __forceinline__ void load_b(const __nv_bfloat16* t, int k0, int n0, u
 // c[NT] (a 16 x 8*NT tile at rows m0, cols n0) += A(m0.., k) * B(k, n0..) for
 // k in [k_begin, k_end) (multiples of 16). NT even.
 // Only the first np_end n-tile pairs are computed (the rest of c is untouched).
+// NT = 1 is a single 8-column tile.
 template <int NT, bool ACOL, bool BKN>
 __device__ __forceinline__ void gemm(float (&c)[NT][4], Op A, int m0, Op B, int n0, int k_begin,
                                      int k_end, int np_end = NT / 2) {
+  if constexpr (NT == 1) {
+    for (int k0 = k_begin; k0 < k_end; k0 += 16) {
+      uint32_t ah[4], al[4], bh[2], bl[2];
+      load_a<ACOL>(A.hi, m0, k0, ah);
+      if (A.lo) load_a<ACOL>(A.lo, m0, k0, al);
+      load_b1<BKN>(B.hi, k0, n0, bh);
+      mma(c[0], ah, bh[0], bh[1]);
+      if (B.lo) {
+        load_b1<BKN>(B.lo, k0, n0, bl);
+        mma(c[0], ah, bl[0], bl[1]);
+      }
+      if (A.lo) mma(c[0], al, bh[0], bh[1]);
+    }
+  } else {
   static_assert(NT % 2 == 0, "n-tiles come in pairs");
   for (int k0 = k_begin; k0 < k_end; k0 += 16) {
     uint32_t ah[4], al[4];
@@ -135,6 +174,7 @@ __device__ __forceinline__ void gemm(float (&c)[NT][4], Op A, int m0, Op B, int 
         mma(c[j + 1], al, bh[2], bh[3]);
       }
     }
+  }
   }
 }
 
