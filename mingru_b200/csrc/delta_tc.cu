@@ -319,11 +319,14 @@ __global__ void __launch_bounds__(kSerialThreads, 1) fwd_kernel(const TcArgs p) 
     stage_rows<DVS / 8, NTH>(Vt(s), Vg + t0 * p.nh * p.dv, p.dv, Mc, ncols >> 3);
     cp_async_commit();
   };
-  auto beta_of = [&](int c) {
+  // beta of a chunk, as raw bf16 bits: the next chunk's values are loaded a
+  // chunk ahead and converted only when stored, so no warp waits on the load.
+  auto beta_of = [&](int c) -> unsigned short {
     const long long r0 = (long long)c * p.C * p.nh;
     const int Mc = (int)min((long long)p.C * p.nh, rows - r0);
-    return tid < Mc ? __bfloat162float(bg[r0 + tid]) : 0.f;
+    return tid < Mc ? reinterpret_cast<const unsigned short*>(bg)[r0 + tid] : (unsigned short)0;
   };
+  auto bf = [](unsigned short raw) { return __uint_as_float((unsigned)raw << 16); };
 
   // state slice: d_k rows m0.., value columns nv.. of this split
   float hs[NTQ][4];
@@ -334,8 +337,8 @@ __global__ void __launch_bounds__(kSerialThreads, 1) fwd_kernel(const TcArgs p) 
   tc::store_split(hs, SH, SL, m0, nv, Ident());
   zero_upper_blocks<NTH>(TiH, TiL);
   stage(0, 0);
-  if (tid < 64) Bt(0)[tid] = beta_of(0);
-  float bnext = 0.f;
+  if (tid < 64) Bt(0)[tid] = bf(beta_of(0));
+  unsigned short bnext = 0;
 
   for (int c = 0; c < p.nchunks; ++c) {
     const int s = c & 1;
@@ -411,7 +414,7 @@ __global__ void __launch_bounds__(kSerialThreads, 1) fwd_kernel(const TcArgs p) 
     tc::gemm<NTQ, true, true>(hs, Op{K, nullptr}, m0, Op{BUH, BUL}, nv, 0, up16(Mc));
     __syncthreads();
     tc::store_split(hs, SH, SL, m0, nv, Ident());
-    if (tid < 64 && c + 1 < p.nchunks) Bt(s ^ 1)[tid] = bnext;
+    if (tid < 64 && c + 1 < p.nchunks) Bt(s ^ 1)[tid] = bf(bnext);
   }
   frag_to_global(hs, p.HT + bh * p.dk * p.dv + c0, p.dv, m0, nv, p.dk, ncols);
 }
@@ -466,11 +469,14 @@ __global__ void __launch_bounds__(kSerialThreads, 1) bwd_chain_kernel(const TcAr
     tile_from_global_async<NTH>(TiLt(s), Tig + (long long)c * 8192 + 4096);
     cp_async_commit();
   };
-  auto beta_of = [&](int c) {
+  // beta of a chunk, as raw bf16 bits: the next chunk's values are loaded a
+  // chunk ahead and converted only when stored, so no warp waits on the load.
+  auto beta_of = [&](int c) -> unsigned short {
     const long long r0 = (long long)c * p.C * p.nh;
     const int Mc = (int)min((long long)p.C * p.nh, rows - r0);
-    return tid < Mc ? __bfloat162float(bg[r0 + tid]) : 0.f;
+    return tid < Mc ? reinterpret_cast<const unsigned short*>(bg)[r0 + tid] : (unsigned short)0;
   };
+  auto bf = [](unsigned short raw) { return __uint_as_float((unsigned)raw << 16); };
 
   float ds[NTQ][4];
   if (p.dHT)
@@ -480,8 +486,8 @@ __global__ void __launch_bounds__(kSerialThreads, 1) bwd_chain_kernel(const TcAr
   tc::store_split(ds, DH, DL, m0, nv, Ident());
   const int last = p.nchunks - 1;
   stage(last, 0);
-  if (tid < 64) Bt(0)[tid] = beta_of(last);
-  float bnext = 0.f;
+  if (tid < 64) Bt(0)[tid] = bf(beta_of(last));
+  unsigned short bnext = 0;
 
   for (int qq = 0; qq < p.nchunks; ++qq) {
     const int c = last - qq, s = qq & 1;
@@ -538,7 +544,7 @@ __global__ void __launch_bounds__(kSerialThreads, 1) bwd_chain_kernel(const TcAr
     tc::gemm<NTQ, true, true>(ds, Op{Q, nullptr}, m0, Op{dY, nullptr}, nv, 0, up16(Cc));
     tc::gemm<NTQ, true, true>(ds, Op{K, nullptr}, m0, Op{GH, GL}, nv, 0, up16(Mc));
     tc::store_split(ds, DH, DL, m0, nv, Ident());
-    if (tid < 64 && c > 0) Bt(s ^ 1)[tid] = bnext;
+    if (tid < 64 && c > 0) Bt(s ^ 1)[tid] = bf(bnext);
   }
   frag_to_global(ds, p.dH0 + bh * p.dk * p.dv + c0, p.dv, m0, nv, p.dk, ncols);
 }
