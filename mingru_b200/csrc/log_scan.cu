@@ -264,7 +264,7 @@ __device__ __forceinline__ void load_steps(const E* src, size_t base, long long 
 // ------------------------------------------------------------ direct path --
 
 template <typename E, int C, int S, int NW>
-__global__ void __launch_bounds__(NW * 32) fwd_direct_kernel(Args<E> p) {
+__global__ void __launch_bounds__(NW * 32, 2) fwd_direct_kernel(Args<E> p) {
   using M = FwdMonoid<C>;
   constexpr int NF = M::NF;
   constexpr int L = S * NW;
@@ -331,7 +331,7 @@ __global__ void __launch_bounds__(NW * 32) fwd_direct_kernel(Args<E> p) {
 }
 
 template <typename E, int C, int S, int NW>
-__global__ void __launch_bounds__(NW * 32) bwd_direct_kernel(Args<E> p) {
+__global__ void __launch_bounds__(NW * 32, 2) bwd_direct_kernel(Args<E> p) {
   using FM = FwdMonoid<C>;
   using RM = RevMonoid<C>;
   constexpr int NFF = FM::NF, NFR = RM::NF;
