@@ -70,6 +70,7 @@ class ScanWorkload:
     metric_elems_doc = "B*T*D"
     kernels = {"fwd": "?", "bwd": "?"}
     launches_per_step = 2  # one forward kernel + one backward kernel
+    compute_dtype = "f32"  # arithmetic of the scan kernels (inputs may be bf16 / fp16)
 
     def __init__(self, dtype=torch.float32):
         self.dtype = dtype
@@ -373,10 +374,11 @@ class DeltaWorkload(ScanWorkload):
     over d_k, V, Q ~ N(0,1), beta = sigmoid(N(0,1)), H0 = 0; bf16 inputs with an
     fp32 state (y in bf16, H_T fp32); grad_y ~ N(0,1), grad_H_T = 0."""
 
-    kernels = {"fwd": "delta_fwd (prepass+state+readout)", "bwd": "delta_bwd (E+adjoint+grads)"}
+    kernels = {"fwd": "delta_fwd", "bwd": "delta_bwd"}
     workload = "DeltaMinGRU chunked-WY fwd+bwd (BASELINE config 5, bf16 in / fp32 state)"
     metric_elems_doc = "B*T*H*d_v"
-    launches_per_step = 6  # three forward kernels + three backward kernels
+    launches_per_step = 3  # forward chunk-serial kernel + backward chain and gradient kernels
+    compute_dtype = "bf16"  # tensor-core products (hi + lo split operands), fp32 accumulate / state
 
     def __init__(self, dtype=torch.bfloat16, name="cfg5", B=8, T=8192, H=8, d=64, chunk=64):
         super().__init__(dtype)
@@ -802,7 +804,7 @@ def run_ours(args, w) -> None:
         "higher_is_better": True,
         "scaling": "weak",
         "vs_baseline": None,
-        "dtype": "f32",
+        "dtype": w.compute_dtype,
         "data": "synthetic (seeded, BASELINE shapes)",
         "config": dict(w.config(world), step="cuda-graph replay" if not args.no_graph else "eager"),
         "tflops": (w.flops / (per_step_ms * 1e-3) / 1e12) if hasattr(w, "flops") else None,
