@@ -60,8 +60,14 @@ def test_golden(cuda, name):
     np.testing.assert_allclose(dlv, g["dlog_values"], **BWD)
 
 
+# Paths (B200, 148 SMs): column path when T <= 1024, D*size % 16 == 0 and
+# B*ceil(D/8) >= 148 (whole time axis per CTA: (3, 100, 1000) ... (2, 1024, 600),
+# ragged T, T < 32, a 4-channel fp32 tail group); strip path for longer T with
+# >= 296 32-channel strips ((10, 1500, 960)); direct tiles otherwise.
 SHAPES = [(1, 1, 1), (2, 13, 3), (3, 31, 4), (2, 33, 129), (1, 64, 256), (3, 100, 1000),
-          (2, 1000, 36), (2, 50, 40), (10, 100, 1000), (3, 70, 3200)]
+          (2, 1000, 36), (2, 50, 40), (10, 100, 1000), (3, 70, 3200),
+          (40, 77, 36), (150, 5, 8), (19, 1024, 64), (37, 1000, 40), (2, 1024, 600),
+          (10, 1500, 960), (3, 1100, 200)]
 
 
 @pytest.mark.parametrize("shape", SHAPES)
@@ -77,7 +83,8 @@ def test_vs_oracle_fp32(cuda, shape):
 
 
 @pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
-@pytest.mark.parametrize("shape", [(2, 13, 3), (2, 300, 256), (10, 45, 1000)])
+@pytest.mark.parametrize("shape", [(2, 13, 3), (2, 300, 256), (10, 45, 1000), (40, 77, 64),
+                                   (10, 1500, 960)])
 def test_half_inputs_fp32_state(cuda, shape, dtype):
     lc, lv, gh = log_space_inputs(*shape, seed=5)
     rnd = lambda x: torch.as_tensor(x, dtype=torch.float32).to(dtype).double().numpy()
@@ -91,10 +98,11 @@ def test_half_inputs_fp32_state(cuda, shape, dtype):
     np.testing.assert_allclose(dlv, rdlv, **tol)
 
 
-def test_zero_initial_state_and_empty(cuda):
+@pytest.mark.parametrize("shape", [(2, 40, 8), (40, 40, 36)])
+def test_zero_initial_state_and_empty(cuda, shape):
     import mingru_b200 as mb
 
-    lc, lv, gh = log_space_inputs(2, 40, 8, seed=3)
+    lc, lv, gh = log_space_inputs(*shape, seed=3)
     lv[:, 0] = np.log(np.finfo(np.float32).tiny)  # h0 numerically zero
     rh = oracle.parallel_scan_log(lc, lv)
     h, _, _ = run(lc, lv, gh, cuda)
@@ -116,6 +124,26 @@ def test_full_config1_fp32(cuda):
     """BASELINE config 1 at full size (B=8, T=1024, D=256), log h0 = log(tiny)."""
     lc, lv, gh = log_space_inputs(8, 1024, 256, seed=0)
     lv[:, 0] = np.log(np.finfo(np.float32).tiny)
+    lc, lv, gh = (x.astype(np.float32).astype(np.float64) for x in (lc, lv, gh))
+    rh = oracle.parallel_scan_log(lc, lv)
+    rdlc, rdlv = oracle.parallel_scan_log_bwd(lc, lv, gh)
+    h, dlc, dlv = run(lc, lv, gh, cuda)
+    np.testing.assert_allclose(h, rh, **FWD)
+    np.testing.assert_allclose(dlc, rdlc, **BWD)
+    np.testing.assert_allclose(dlv, rdlv, **BWD)
+
+
+@pytest.mark.parametrize("case", ["positive_log_coeff", "tiny_log_values", "mixed"])
+def test_column_path_log_space_fallback(cuda, case):
+    """Column-path CTAs whose data leaves the linear-domain envelope (a log
+    coefficient > 0, or a log value outside [-60, 80]) run the log-space
+    monoid; the other CTAs of the same launch stay linear."""
+    B, T, D = 40, 200, 64  # 320 column groups: column path
+    lc, lv, gh = log_space_inputs(B, T, D, seed=11)
+    if case in ("positive_log_coeff", "mixed"):
+        lc[3, 50:60, 9] = 0.05  # a_t > 1 in one channel of one group
+    if case in ("tiny_log_values", "mixed"):
+        lv[7, 1:120, 17] -= 70.0  # b_t ~ e^-70 for a stretch
     lc, lv, gh = (x.astype(np.float32).astype(np.float64) for x in (lc, lv, gh))
     rh = oracle.parallel_scan_log(lc, lv)
     rdlc, rdlv = oracle.parallel_scan_log_bwd(lc, lv, gh)
