@@ -57,7 +57,7 @@ inline int sm_count() {
 
 struct Geometry {
   Algo algo;
-  int cpt;
+  int cpt;   // channels per thread (direct paths) / per CTA (column path: 8 or 16)
   long long sper, nstrips, nchunks, ntiles, fchunks, ftiles;
 };
 
@@ -73,7 +73,9 @@ inline Geometry geometry(long long B, long long T, long long D, int dtype) {
   else
     g.algo = rows16 ? kDirectVec : kDirectScalar;
   g.cpt = g.algo == kDirectVec ? kVecCpt : 1;
-  const long long w = g.algo == kColumn ? 8LL : 32LL * g.cpt;
+  if (g.algo == kColumn)  // 16-channel groups (64-byte fp32 rows) while they fill 3/4 of the SMs
+    g.cpt = 4 * B * ((D + 15) / 16) >= 3LL * sm_count() ? 16 : 8;
+  const long long w = g.algo == kColumn ? (long long)g.cpt : 32LL * g.cpt;
   g.sper = (D + w - 1) / w;
   g.nstrips = B * g.sper;
   g.nchunks = (T + kLc - 1) / kLc;
@@ -425,29 +427,34 @@ __global__ void __launch_bounds__(NW * 32, 2) bwd_direct_kernel(Args<E> p) {
 }
 
 // ------------------------------------------------------------ column path --
-// One CTA per (batch row, 8-channel group) holds the whole time axis (T <= 1024)
-// in shared memory, brought in (and written back) by TMA boxes of 256 rows x 8
-// channels; rows stay dense [t][channel]. Lane (c = lane & 7, j = lane >> 3) of
-// warp w scans channel c over segment s = 4w + j; segment starts are staggered
-// (start = s*seg + (s & 3), seg a multiple of 4), so at every step the 32 lanes
-// of a warp read 32 distinct banks. Segment aggregates combine by warp shuffles
-// over j and through shared memory over warps; each lane then replays its
-// segment from the incoming state. No look-back and no carries: the backward
-// recomputes the forward states in the same CTA.
+// One CTA per (batch row, W-channel group), W = 8 or 16, holds the whole time
+// axis (T <= 1024) in shared memory, brought in (and written back) by TMA
+// boxes of 256 rows x W channels; rows stay dense [t][channel]. The CTA has
+// 32 * W threads: lane (c = lane % W, j = lane / W) of warp w scans channel c
+// over segment s = w * SPW + j (SPW = 32 / W segments per warp, 32 segments per
+// channel). Segment starts are staggered (start = s*seg + s % SPW, seg a
+// multiple of 4), so at every step the lanes of a warp read distinct banks.
+// Segment aggregates combine by warp shuffles over j and through shared
+// memory over warps; each lane then replays its segment from the incoming
+// state. No look-back and no carries: the backward recomputes the forward
+// states in the same CTA. W = 16 (64-byte fp32 rows, one CTA per SM) halves
+// the number of TMA row requests per byte; W = 8 keeps more CTAs when there
+// are few channel groups.
 //
-// Arithmetic: where every log coefficient is <= 0 and every log value (t >= 1)
-// lies in [-60, 80] (MinGRU's construction), the CTA runs the recurrence in
-// the linear domain, h_t = a_t h_{t-1} + b_t with a = exp(lc), b = exp(lv): all
-// terms are positive, each state is <= the output it feeds (so nothing
-// overflows unless h does) and >= e^-60 (so no state that matters underflows).
+// Arithmetic: where every log coefficient is <= 0, every log value (t >= 1)
+// lies in [-30, 20] and log h_0 <= 20 (MinGRU's construction gives log values
+// in about [-13, 2]), the CTA runs the recurrence in the linear domain,
+// h_t = a_t h_{t-1} + b_t with a = exp(lc), b = exp(lv). All terms are
+// positive, every state is <= (T + 1) e^20 <= e^27 and every state after
+// step 0 (and every segment's additive part) is >= e^-30, so a coefficient
+// product that underflows (< 2^-126) changes a result by < e^-30 relative.
 // Otherwise the CTA runs the log-space monoid (alpha, nu) of the other paths.
 
-constexpr int kColW = 8;        // channels per CTA
-constexpr int kColSegs = 32;    // segments per channel (4 per warp, 8 warps)
+constexpr int kColSegs = 32;    // segments per channel
 constexpr int kColBox = 256;    // rows per TMA box
 constexpr long long kColTmax = 1024;
 constexpr int kColMaxLen = (int)(kColTmax / kColSegs) + 1;
-constexpr int kColThreads = 256;
+constexpr float kColLinLo = -30.f, kColLinHi = 20.f;  // linear-domain envelope of log values
 
 struct ColMaps {
   CUtensorMap m[5];  // fwd: lc, lv, h; bwd: lc, lv, gh, dlc, dlv
@@ -464,63 +471,83 @@ __host__ __device__ __forceinline__ int col_boxes(long long T) {
 }
 
 template <typename E>
-inline size_t col_smem_bytes(long long T, int ntensors) {
-  return 128 + (size_t)ntensors * col_boxes(T) * kColBox * kColW * sizeof(E) +
-         4 * kColW * kColW * sizeof(float);
+inline size_t col_smem_bytes(long long T, int ntensors, int W) {
+  return 128 + (size_t)ntensors * col_boxes(T) * kColBox * W * sizeof(E) +
+         4 * (size_t)W * W * sizeof(float);
 }
 
-template <typename E>
+template <typename E, int W>
 struct ColSmem {
-  uint64_t* bar;
-  E* t[3];      // lc, lv (rows 1..T), gh: [rows][kColW]
-  float* tot;   // [4][warp][channel]
+  uint64_t* bar;  // one mbarrier per box (<= 4)
+  E* t[3];        // lc, lv (rows 1..T), gh: [rows][W]
+  float* tot;     // 4 x [warp][channel]
   __device__ ColSmem(unsigned char* sm, long long T, int nt) {
     bar = reinterpret_cast<uint64_t*>(sm);
-    const size_t tb = (size_t)col_boxes(T) * kColBox * kColW;
+    const size_t tb = (size_t)col_boxes(T) * kColBox * W;
     E* base = reinterpret_cast<E*>(sm + 128);
     for (int k = 0; k < 3; ++k) t[k] = base + (k < nt ? k : 0) * tb;
     tot = reinterpret_cast<float*>(base + nt * tb);
   }
 };
 
+template <int W>
 __device__ __forceinline__ void col_segment(long long T, int s, int& start, int& n) {
+  constexpr int SPW = 32 / W;
   const long long seg = col_seg(T);
-  const long long a = min((long long)s * seg + (s & 3), T);
-  const long long b = s == kColSegs - 1 ? T : min((long long)(s + 1) * seg + ((s + 1) & 3), T);
+  const long long a = min((long long)s * seg + (s % SPW), T);
+  const long long b =
+      s == kColSegs - 1 ? T : min((long long)(s + 1) * seg + ((s + 1) % SPW), T);
   start = (int)a;
   n = (int)(b - a);
 }
 
-template <typename E>
+template <typename E, int W>
 __device__ __forceinline__ float cld(const E* p, int i) {
-  return to_f32<E>(p[i * kColW]);
+  return to_f32<E>(p[i * W]);
 }
-template <typename E>
+template <typename E, int W>
 __device__ __forceinline__ void cst(E* p, int i, float v) {
-  p[i * kColW] = from_f32<E>(v);
+  p[i * W] = from_f32<E>(v);
 }
 
-// Thread 0: issue the TMA boxes of NT tensors (lv skips its h_0 row) and arm
-// the barrier; every thread then waits (bounded) for the bytes to land.
-template <typename E, int NT>
-__device__ __forceinline__ void col_fetch(const ColMaps& maps, const ColSmem<E>& sm, long long T,
-                                          int d0, int bi) {
+// e^x as 2^(x log2 e) on the hardware ex2 (denormal results flush to zero).
+// Relative error <= |x| 2^-24 (rounding of x log2 e) + ~2^-22 (ex2): about 2e-6
+// at the envelope's |x| <= 30; used only on the linear-domain path.
+__device__ __forceinline__ float col_exp(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x * 1.4426950408889634f));
+  return y;
+}
+
+// Thread 0: issue the TMA boxes of NT tensors in time order (lv skips its h_0
+// row), box b of every tensor completing on barrier b.
+template <typename E, int W, int NT>
+__device__ __forceinline__ void col_fetch(const ColMaps& maps, const ColSmem<E, W>& sm,
+                                          long long T, int d0, int bi) {
   const int nb = col_boxes(T);
   if (threadIdx.x == 0) {
-    mbar_init(sm.bar, 1);
+    for (int b = 0; b < nb; ++b) mbar_init(sm.bar + b, 1);
     mbar_fence_init();
-    mbar_arrive_expect_tx(sm.bar, (unsigned)(NT * nb * kColBox * kColW * sizeof(E)));
-    for (int k = 0; k < NT; ++k)
-      for (int b = 0; b < nb; ++b)
-        tma_load_3d(sm.t[k] + (size_t)b * kColBox * kColW, &maps.m[k], d0,
-                    b * kColBox + (k == 1 ? 1 : 0), bi, sm.bar);
+    for (int b = 0; b < nb; ++b) {
+      mbar_arrive_expect_tx(sm.bar + b, (unsigned)(NT * kColBox * W * sizeof(E)));
+      for (int k = 0; k < NT; ++k)
+        tma_load_3d(sm.t[k] + (size_t)b * kColBox * W, &maps.m[k], d0,
+                    b * kColBox + (k == 1 ? 1 : 0), bi, sm.bar + b);
+    }
   }
   __syncthreads();
-  mbar_wait(sm.bar, 0, &g_sticky_err);
+}
+
+// Bounded wait for the boxes holding rows [start, start + n).
+template <typename E, int W>
+__device__ __forceinline__ void col_wait_rows(const ColSmem<E, W>& sm, int start, int n) {
+  if (n <= 0) return;
+  for (int b = start / kColBox; b <= (start + n - 1) / kColBox; ++b)
+    mbar_wait(sm.bar + b, 0, &g_sticky_err);
 }
 
 // Store rows [0, T) of smem array `src` through map `m` (row offset y0).
-template <typename E>
+template <typename E, int W>
 __device__ __forceinline__ void col_put(const CUtensorMap* m, const E* src, long long T, int d0,
                                         int y0, int bi) {
   fence_proxy_async_smem();
@@ -528,19 +555,21 @@ __device__ __forceinline__ void col_put(const CUtensorMap* m, const E* src, long
   if (threadIdx.x == 0) {
     const int nb = col_boxes(T);
     for (int b = 0; b < nb; ++b)
-      tma_store_3d(m, d0, y0 + b * kColBox, bi, src + (size_t)b * kColBox * kColW);
+      tma_store_3d(m, d0, y0 + b * kColBox, bi, src + (size_t)b * kColBox * W);
     bulk_commit();
   }
 }
 
 // Does this lane's segment allow the linear-domain recurrence?
-template <typename E>
+template <typename E, int W>
 __device__ __forceinline__ bool col_linear_ok(const E* lc, const E* lv, int n) {
   bool ok = true;
-  for (int i = 0; i < n; ++i) {
-    const float c = cld(lc, i), v = cld(lv, i);
-    ok &= (c <= 0.f) & (v >= -60.f) & (v <= 80.f);
-  }
+#pragma unroll
+  for (int i = 0; i < kColMaxLen; ++i)
+    if (i < n) {
+      const float c = cld<E, W>(lc, i), v = cld<E, W>(lv, i);
+      ok &= (c <= 0.f) & (v >= kColLinLo) & (v <= kColLinHi);
+    }
   return ok;
 }
 
@@ -552,7 +581,6 @@ struct ColLin {
     B = fmaf(A, B2, B);
     A *= A2;
   }
-  __device__ static float state(float A, float B, float x) { return fmaf(A, x, B); }
 };
 struct ColLog {
   __device__ static void ident(float& A, float& B) { A = 0.f; B = -INFINITY; }
@@ -560,70 +588,72 @@ struct ColLog {
     B = logaddexp(B2 + A, B);
     A += A2;
   }
-  __device__ static float state(float A, float B, float x) { return logaddexp(x + A, B); }
 };
 
 // Forward aggregate of one segment (linear: caches a, b over lc, lv for fp32).
-template <typename E, bool LIN>
+template <typename E, int W, bool LIN>
 __device__ __forceinline__ void col_fwd_agg(E* lc, E* lv, int n, bool first, float s0, float& A,
                                             float& B) {
   if (LIN) {
     A = first ? 0.f : 1.f;
     B = first ? s0 : 0.f;
-    for (int i = 0; i < n; ++i) {
-      const float a = expf(cld(lc, i)), b = expf(cld(lv, i));
-      if constexpr (std::is_same<E, float>::value) {
-        lc[i * kColW] = a;
-        lv[i * kColW] = b;
+#pragma unroll
+    for (int i = 0; i < kColMaxLen; ++i)
+      if (i < n) {
+        const float a = col_exp(cld<E, W>(lc, i)), b = col_exp(cld<E, W>(lv, i));
+        if constexpr (std::is_same<E, float>::value) {
+          lc[i * W] = a;
+          lv[i * W] = b;
+        }
+        B = fmaf(a, B, b);
+        A *= a;
       }
-      B = fmaf(a, B, b);
-      A *= a;
-    }
   } else {
     A = first ? -INFINITY : 0.f;
     B = first ? s0 : -INFINITY;
     for (int i = 0; i < n; ++i) {
-      const float c = cld(lc, i);
-      B = logaddexp(B + c, cld(lv, i));
+      const float c = cld<E, W>(lc, i);
+      B = logaddexp(B + c, cld<E, W>(lv, i));
       A += c;
     }
   }
 }
 
 // a_t, b_t of step i on the linear path (cached for fp32, recomputed otherwise).
-template <typename E>
+template <typename E, int W>
 __device__ __forceinline__ void col_ab(const E* lc, const E* lv, int i, float& a, float& b) {
   if constexpr (std::is_same<E, float>::value) {
-    a = lc[i * kColW];
-    b = lv[i * kColW];
+    a = lc[i * W];
+    b = lv[i * W];
   } else {
-    a = expf(cld(lc, i));
-    b = expf(cld(lv, i));
+    a = col_exp(cld<E, W>(lc, i));
+    b = col_exp(cld<E, W>(lv, i));
   }
 }
 
 // Exclusive scan of segment elements over the CTA: returns the state entering
-// segment s (s0 = state entering segment 0). `tot` holds 2 x [warp][channel].
-template <class M>
+// this lane's segment (s0 = state entering segment 0). `tot` holds 2 x [warp][channel].
+template <class M, int W>
 __device__ __forceinline__ float col_scan_fwd(float A, float B, float s0, float* tot) {
-  const int lane = threadIdx.x & 31, w = threadIdx.x >> 5, c = lane & 7, j = lane >> 3;
+  constexpr int SPW = 32 / W;
+  const int lane = threadIdx.x & 31, w = threadIdx.x >> 5, c = lane % W, j = lane / W;
 #pragma unroll
-  for (int off = 8; off < 32; off <<= 1) {
+  for (int off = W; off < 32; off <<= 1) {
     const float A2 = __shfl_up_sync(0xffffffffu, A, off);
     const float B2 = __shfl_up_sync(0xffffffffu, B, off);
     if (lane >= off) M::after(A, B, A2, B2);
   }
-  if (j == 3) {
-    tot[w * kColW + c] = A;
-    tot[kColW * kColW + w * kColW + c] = B;
+  if (j == SPW - 1) {
+    tot[w * W + c] = A;
+    tot[W * W + w * W + c] = B;
   }
-  float Ae = __shfl_up_sync(0xffffffffu, A, 8), Be = __shfl_up_sync(0xffffffffu, B, 8);
+  float Ae = __shfl_up_sync(0xffffffffu, A, W), Be = __shfl_up_sync(0xffffffffu, B, W);
   if (j == 0) M::ident(Ae, Be);
   __syncthreads();
   float Ap, Bp;
   M::ident(Ap, Bp);
   for (int v = 0; v < w; ++v) {  // prefix <- prefix then warp v
-    float tA = tot[v * kColW + c], tB = tot[kColW * kColW + v * kColW + c];
+    float tA = tot[v * W + c], tB = tot[W * W + v * W + c];
     M::after(tA, tB, Ap, Bp);
     Ap = tA;
     Bp = tB;
@@ -632,69 +662,76 @@ __device__ __forceinline__ float col_scan_fwd(float A, float B, float s0, float*
   return (w == 0 && j == 0) ? s0 : Be;  // segments after 0 carry the h_0 reset: state = B
 }
 
-template <typename E>
-__global__ void __launch_bounds__(kColThreads, 2)
+template <typename E, int W>
+__global__ void __launch_bounds__(32 * W, 16 / W)
     fwd_col_kernel(Args<E> p, const __grid_constant__ ColMaps maps) {
   extern __shared__ __align__(128) unsigned char col_raw[];
-  const ColSmem<E> sm(col_raw, p.T_, 2);
+  const ColSmem<E, W> sm(col_raw, p.T_, 2);
   const int bi = (int)(blockIdx.x / p.sper);
-  const int d0 = (int)(blockIdx.x - (long long)bi * p.sper) * kColW;
-  const int lane = threadIdx.x & 31, c = lane & 7, s = (threadIdx.x >> 5) * 4 + (lane >> 3);
+  const int d0 = (int)(blockIdx.x - (long long)bi * p.sper) * W;
+  const int lane = threadIdx.x & 31, c = lane % W, s = (threadIdx.x >> 5) * (32 / W) + lane / W;
   const bool cok = d0 + c < p.D;
   const float lv0 = cok ? to_f32<E>(p.lv[(size_t)bi * (p.T_ + 1) * p.D + d0 + c]) : 0.f;
-  col_fetch<E, 2>(maps, sm, p.T_, d0, bi);
+  col_fetch<E, W, 2>(maps, sm, p.T_, d0, bi);
   int start, n;
-  col_segment(p.T_, s, start, n);
-  E* lc = sm.t[0] + (size_t)start * kColW + c;
-  E* lv = sm.t[1] + (size_t)start * kColW + c;
-  const bool lin = __syncthreads_and(col_linear_ok(lc, lv, n) && !(lv0 > 80.f)) != 0;
+  col_segment<W>(p.T_, s, start, n);
+  col_wait_rows(sm, start, n);
+  E* lc = sm.t[0] + (size_t)start * W + c;
+  E* lv = sm.t[1] + (size_t)start * W + c;
+  const bool lin = __syncthreads_and(col_linear_ok<E, W>(lc, lv, n) && !(lv0 > kColLinHi)) != 0;
   float A, B;
   if (lin) {
     const float h0 = expf(lv0);
-    col_fwd_agg<E, true>(lc, lv, n, s == 0, h0, A, B);
-    float h = col_scan_fwd<ColLin>(A, B, h0, sm.tot);
-    for (int i = 0; i < n; ++i) {
-      float a, b;
-      col_ab(lc, lv, i, a, b);
-      h = fmaf(a, h, b);
-      cst(lc, i, h);
-    }
+    col_fwd_agg<E, W, true>(lc, lv, n, s == 0, h0, A, B);
+    float h = col_scan_fwd<ColLin, W>(A, B, h0, sm.tot);
+#pragma unroll
+    for (int i = 0; i < kColMaxLen; ++i)
+      if (i < n) {
+        float a, b;
+        col_ab<E, W>(lc, lv, i, a, b);
+        h = fmaf(a, h, b);
+        cst<E, W>(lc, i, h);
+      }
   } else {
-    col_fwd_agg<E, false>(lc, lv, n, s == 0, lv0, A, B);
-    float x = col_scan_fwd<ColLog>(A, B, lv0, sm.tot);
+    col_fwd_agg<E, W, false>(lc, lv, n, s == 0, lv0, A, B);
+    float x = col_scan_fwd<ColLog, W>(A, B, lv0, sm.tot);
     for (int i = 0; i < n; ++i) {
-      x = logaddexp(x + cld(lc, i), cld(lv, i));
-      cst(lc, i, expf(x));
+      x = logaddexp(x + cld<E, W>(lc, i), cld<E, W>(lv, i));
+      cst<E, W>(lc, i, expf(x));
     }
   }
-  col_put<E>(&maps.m[2], sm.t[0], p.T_, d0, 0, bi);
+  col_put<E, W>(&maps.m[2], sm.t[0], p.T_, d0, 0, bi);
   if (threadIdx.x == 0) bulk_wait_read();
 }
 
-template <typename E, bool LIN>
-__device__ __forceinline__ void col_bwd_body(const Args<E>& p, const ColSmem<E>& sm, int start,
-                                             int n, int s, float lv0, bool cok, size_t row0) {
+template <typename E, int W, bool LIN>
+__device__ __forceinline__ void col_bwd_body(const Args<E>& p, const ColSmem<E, W>& sm,
+                                             int start, int n, int s, float lv0, bool cok,
+                                             size_t row0) {
   using M = typename std::conditional<LIN, ColLin, ColLog>::type;
-  const int lane = threadIdx.x & 31, w = threadIdx.x >> 5, c = lane & 7, j = lane >> 3;
-  E* lc = sm.t[0] + (size_t)start * kColW + c;
-  E* lv = sm.t[1] + (size_t)start * kColW + c;
-  const E* g = sm.t[2] + (size_t)start * kColW + c;
+  constexpr int SPW = 32 / W;
+  const int lane = threadIdx.x & 31, w = threadIdx.x >> 5, c = lane % W, j = lane / W;
+  E* lc = sm.t[0] + (size_t)start * W + c;
+  E* lv = sm.t[1] + (size_t)start * W + c;
+  const E* g = sm.t[2] + (size_t)start * W + c;
   const float s0 = LIN ? expf(lv0) : lv0;
   float A, B;
-  col_fwd_agg<E, LIN>(lc, lv, n, s == 0, s0, A, B);
+  col_fwd_agg<E, W, LIN>(lc, lv, n, s == 0, s0, A, B);
   // Reverse adjoint Y_t = a_t (g_t + Y_{t+1}) per segment: Y_start = P Y_after + Q.
   float P = 1.f, Q = 0.f;
-  for (int i = n - 1; i >= 0; --i) {
-    float a, b;
-    if (LIN)
-      col_ab(lc, lv, i, a, b);
-    else
-      a = __expf(cld(lc, i));
-    Q = a * (cld(g, i) + Q);
-    P *= a;
-  }
 #pragma unroll
-  for (int off = 8; off < 32; off <<= 1) {
+  for (int i = kColMaxLen - 1; i >= 0; --i)
+    if (i < n) {
+      float a, b;
+      if (LIN)
+        col_ab<E, W>(lc, lv, i, a, b);
+      else
+        a = __expf(cld<E, W>(lc, i));
+      Q = a * (cld<E, W>(g, i) + Q);
+      P *= a;
+    }
+#pragma unroll
+  for (int off = W; off < 32; off <<= 1) {
     const float P2 = __shfl_down_sync(0xffffffffu, P, off);
     const float Q2 = __shfl_down_sync(0xffffffffu, Q, off);
     if (lane + off < 32) {
@@ -702,16 +739,16 @@ __device__ __forceinline__ void col_bwd_body(const Args<E>& p, const ColSmem<E>&
       P *= P2;
     }
   }
-  float* rtot = sm.tot + 2 * kColW * kColW;
+  float* rtot = sm.tot + 2 * W * W;
   if (j == 0) {
-    rtot[w * kColW + c] = P;
-    rtot[kColW * kColW + w * kColW + c] = Q;
+    rtot[w * W + c] = P;
+    rtot[W * W + w * W + c] = Q;
   }
-  float Pe = __shfl_down_sync(0xffffffffu, P, 8), Qe = __shfl_down_sync(0xffffffffu, Q, 8);
-  if (j == 3) { Pe = 1.f; Qe = 0.f; }
-  const float xin = col_scan_fwd<M>(A, B, s0, sm.tot);  // synchronises the CTA
+  float Pe = __shfl_down_sync(0xffffffffu, P, W), Qe = __shfl_down_sync(0xffffffffu, Q, W);
+  if (j == SPW - 1) { Pe = 1.f; Qe = 0.f; }
+  const float xin = col_scan_fwd<M, W>(A, B, s0, sm.tot);  // synchronises the CTA
   float y = 0.f;
-  for (int v = kColW - 1; v > w; --v) y = fmaf(rtot[v * kColW + c], y, rtot[kColW * kColW + v * kColW + c]);
+  for (int v = W - 1; v > w; --v) y = fmaf(rtot[v * W + c], y, rtot[W * W + v * W + c]);
   y = fmaf(Pe, y, Qe);
 
   float xp[kColMaxLen];
@@ -722,58 +759,59 @@ __device__ __forceinline__ void col_bwd_body(const Args<E>& p, const ColSmem<E>&
       xp[i] = x;
       if (LIN) {
         float a, b;
-        col_ab(lc, lv, i, a, b);
+        col_ab<E, W>(lc, lv, i, a, b);
         x = fmaf(a, x, b);
       } else {
-        x = logaddexp(x + cld(lc, i), cld(lv, i));
+        x = logaddexp(x + cld<E, W>(lc, i), cld<E, W>(lv, i));
       }
     }
 #pragma unroll
   for (int i = kColMaxLen - 1; i >= 0; --i)
     if (i < n) {
-      const float G = cld(g, i) + y;
+      const float G = cld<E, W>(g, i) + y;
       float a, dc, dv;
       if (LIN) {
         float b;
-        col_ab(lc, lv, i, a, b);
+        col_ab<E, W>(lc, lv, i, a, b);
         dc = G * a * xp[i];
         dv = G * b;
       } else {
-        const float lci = cld(lc, i);
+        const float lci = cld<E, W>(lc, i);
         a = __expf(lci);
         dc = G * __expf(lci + xp[i]);
-        dv = G * __expf(cld(lv, i));
+        dv = G * __expf(cld<E, W>(lv, i));
       }
       y = a * G;
-      cst(lc, i, dc);  // dlc_t over lc_t, dlv_{t+1} over lv_t
-      cst(lv, i, dv);
+      cst<E, W>(lc, i, dc);  // dlc_t over lc_t, dlv_{t+1} over lv_t
+      cst<E, W>(lv, i, dv);
     }
   if (s == 0 && cok) p.dlv[row0] = from_f32<E>(y * (LIN ? s0 : expf(lv0)));
 }
 
-template <typename E>
-__global__ void __launch_bounds__(kColThreads, 2)
+template <typename E, int W>
+__global__ void __launch_bounds__(32 * W, 16 / W)
     bwd_col_kernel(Args<E> p, const __grid_constant__ ColMaps maps) {
   extern __shared__ __align__(128) unsigned char col_raw[];
-  const ColSmem<E> sm(col_raw, p.T_, 3);
+  const ColSmem<E, W> sm(col_raw, p.T_, 3);
   const int bi = (int)(blockIdx.x / p.sper);
-  const int d0 = (int)(blockIdx.x - (long long)bi * p.sper) * kColW;
-  const int lane = threadIdx.x & 31, c = lane & 7, s = (threadIdx.x >> 5) * 4 + (lane >> 3);
+  const int d0 = (int)(blockIdx.x - (long long)bi * p.sper) * W;
+  const int lane = threadIdx.x & 31, c = lane % W, s = (threadIdx.x >> 5) * (32 / W) + lane / W;
   const bool cok = d0 + c < p.D;
   const size_t row0 = (size_t)bi * (p.T_ + 1) * p.D + d0 + c;
   const float lv0 = cok ? to_f32<E>(p.lv[row0]) : 0.f;
-  col_fetch<E, 3>(maps, sm, p.T_, d0, bi);
+  col_fetch<E, W, 3>(maps, sm, p.T_, d0, bi);
   int start, n;
-  col_segment(p.T_, s, start, n);
-  const bool lin = __syncthreads_and(col_linear_ok(sm.t[0] + (size_t)start * kColW + c,
-                                                   sm.t[1] + (size_t)start * kColW + c, n) &&
-                                     !(lv0 > 80.f)) != 0;
+  col_segment<W>(p.T_, s, start, n);
+  col_wait_rows(sm, start, n);
+  const bool lin = __syncthreads_and(col_linear_ok<E, W>(sm.t[0] + (size_t)start * W + c,
+                                                         sm.t[1] + (size_t)start * W + c, n) &&
+                                     !(lv0 > kColLinHi)) != 0;
   if (lin)
-    col_bwd_body<E, true>(p, sm, start, n, s, lv0, cok, row0);
+    col_bwd_body<E, W, true>(p, sm, start, n, s, lv0, cok, row0);
   else
-    col_bwd_body<E, false>(p, sm, start, n, s, lv0, cok, row0);
-  col_put<E>(&maps.m[3], sm.t[0], p.T_, d0, 0, bi);
-  col_put<E>(&maps.m[4], sm.t[1], p.T_, d0, 1, bi);
+    col_bwd_body<E, W, false>(p, sm, start, n, s, lv0, cok, row0);
+  col_put<E, W>(&maps.m[3], sm.t[0], p.T_, d0, 0, bi);
+  col_put<E, W>(&maps.m[4], sm.t[1], p.T_, d0, 1, bi);
   if (threadIdx.x == 0) bulk_wait_read();
 }
 
@@ -1058,7 +1096,7 @@ int run(bool fwd, const void* lc, const void* lv, void* h, const void* gh, void*
     static_assert(kColTmax == 1024, "column geometry bound");
     if (g.nstrips > 0x7fffffffLL || B > 0x7fffffffLL) return MGS_UNSUPPORTED;
     ColMaps maps;
-    const unsigned bx = kColW, by = kColBox;
+    const unsigned bx = (unsigned)g.cpt, by = kColBox;
     bool ok = make_tmap_3d<E>(&maps.m[0], lc, D, T, B, bx, by) &&
               make_tmap_3d<E>(&maps.m[1], lv, D, T + 1, B, bx, by);
     if (fwd)
@@ -1068,10 +1106,12 @@ int run(bool fwd, const void* lc, const void* lv, void* h, const void* gh, void*
            make_tmap_3d<E>(&maps.m[3], dlc, D, T, B, bx, by) &&
            make_tmap_3d<E>(&maps.m[4], dlv, D, T + 1, B, bx, by);
     if (!ok) return MGS_LAUNCH_FAILED;
-    const size_t smem = col_smem_bytes<E>(T, fwd ? 2 : 3);
-    void (*kern)(Args<E>, const ColMaps) = fwd ? fwd_col_kernel<E> : bwd_col_kernel<E>;
+    const size_t smem = col_smem_bytes<E>(T, fwd ? 2 : 3, g.cpt);
+    void (*kern)(Args<E>, const ColMaps) =
+        g.cpt == 16 ? (fwd ? fwd_col_kernel<E, 16> : bwd_col_kernel<E, 16>)
+                    : (fwd ? fwd_col_kernel<E, 8> : bwd_col_kernel<E, 8>);
     MGS_CUDA_OK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
-    kern<<<(unsigned)g.nstrips, kColThreads, smem, st>>>(p, maps);
+    kern<<<(unsigned)g.nstrips, 32 * g.cpt, smem, st>>>(p, maps);
     return cudaGetLastError() == cudaSuccess ? MGS_OK : MGS_LAUNCH_FAILED;
   }
   if (g.algo == kStrip) {

@@ -61,9 +61,11 @@ def test_golden(cuda, name):
 
 
 # Paths (B200, 148 SMs): column path when T <= 1024, D*size % 16 == 0 and
-# B*ceil(D/8) >= 148 (whole time axis per CTA: (3, 100, 1000) ... (2, 1024, 600),
-# ragged T, T < 32, a 4-channel fp32 tail group); strip path for longer T with
-# >= 296 32-channel strips ((10, 1500, 960)); direct tiles otherwise.
+# B*ceil(D/8) >= 148 (whole time axis per CTA), with 16-channel CTAs when
+# B*ceil(D/16) >= 111 ((3, 100, 1000), (40, 77, 36) with a 4-channel tail,
+# (150, 5, 8) with T < 32) and 8-channel CTAs otherwise ((19, 1024, 64),
+# (2, 1024, 600)); strip path for longer T with >= 296 32-channel strips
+# ((10, 1500, 960)); direct tiles otherwise.
 SHAPES = [(1, 1, 1), (2, 13, 3), (3, 31, 4), (2, 33, 129), (1, 64, 256), (3, 100, 1000),
           (2, 1000, 36), (2, 50, 40), (10, 100, 1000), (3, 70, 3200),
           (40, 77, 36), (150, 5, 8), (19, 1024, 64), (37, 1000, 40), (2, 1024, 600),
@@ -84,7 +86,7 @@ def test_vs_oracle_fp32(cuda, shape):
 
 @pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
 @pytest.mark.parametrize("shape", [(2, 13, 3), (2, 300, 256), (10, 45, 1000), (40, 77, 64),
-                                   (10, 1500, 960)])
+                                   (2, 300, 600), (10, 1500, 960)])
 def test_half_inputs_fp32_state(cuda, shape, dtype):
     lc, lv, gh = log_space_inputs(*shape, seed=5)
     rnd = lambda x: torch.as_tensor(x, dtype=torch.float32).to(dtype).double().numpy()
@@ -133,17 +135,23 @@ def test_full_config1_fp32(cuda):
     np.testing.assert_allclose(dlv, rdlv, **BWD)
 
 
-@pytest.mark.parametrize("case", ["positive_log_coeff", "tiny_log_values", "mixed"])
-def test_column_path_log_space_fallback(cuda, case):
+@pytest.mark.parametrize("case", ["positive_log_coeff", "tiny_log_values", "large_log_values",
+                                  "large_h0", "mixed"])
+@pytest.mark.parametrize("B", [40, 19])  # 16- and 8-channel column CTAs
+def test_column_path_log_space_fallback(cuda, case, B):
     """Column-path CTAs whose data leaves the linear-domain envelope (a log
-    coefficient > 0, or a log value outside [-60, 80]) run the log-space
+    coefficient > 0, a log value outside [-30, 20], or log h_0 > 20) run the log-space
     monoid; the other CTAs of the same launch stay linear."""
-    B, T, D = 40, 200, 64  # 320 column groups: column path
+    T, D = 200, 64  # B*8 >= 148 column groups: column path
     lc, lv, gh = log_space_inputs(B, T, D, seed=11)
     if case in ("positive_log_coeff", "mixed"):
         lc[3, 50:60, 9] = 0.05  # a_t > 1 in one channel of one group
     if case in ("tiny_log_values", "mixed"):
-        lv[7, 1:120, 17] -= 70.0  # b_t ~ e^-70 for a stretch
+        lv[7, 1:120, 17] -= 40.0  # b_t ~ e^-40 for a stretch
+    if case == "large_log_values":
+        lv[5, 30:40, 40] += 24.0  # b_t ~ e^24
+    if case == "large_h0":
+        lv[2, 0, 3] = 25.0  # h_0 = e^25
     lc, lv, gh = (x.astype(np.float32).astype(np.float64) for x in (lc, lv, gh))
     rh = oracle.parallel_scan_log(lc, lv)
     rdlc, rdlv = oracle.parallel_scan_log_bwd(lc, lv, gh)
