@@ -377,7 +377,7 @@ class DeltaWorkload(ScanWorkload):
     kernels = {"fwd": "delta_fwd", "bwd": "delta_bwd"}
     workload = "DeltaMinGRU chunked-WY fwd+bwd (BASELINE config 5, bf16 in / fp32 state)"
     metric_elems_doc = "B*T*H*d_v"
-    launches_per_step = 3  # forward chunk-serial kernel + backward chain and gradient kernels
+    launches_per_step = 4  # forward prep + chain kernels, backward chain + gradient kernels
     compute_dtype = "bf16"  # tensor-core products (hi + lo split operands), fp32 accumulate / state
 
     def __init__(self, dtype=torch.bfloat16, name="cfg5", B=8, T=8192, H=8, d=64, chunk=64):

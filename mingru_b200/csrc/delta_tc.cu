@@ -16,17 +16,26 @@
 //         dKK = (-G U^T) diag(beta) * strict_lower
 //   dbeta = rowsum(U * dbU) + colsum((dy U^T) * QK^T * read) + colsum((-G U^T) * KK^T * strict)
 //
+// Each chunk is an affine map of the state, S' = S + Xn S + Bc with
+// Xn = -K^T diag(beta) W and Bc = K^T diag(beta) U', read out as
+// y = Qt S + Yp with Qt = Q - P W and Yp = P U'; the adjoint chain is
+// dS = dS' + Xn^T dS' + Qt^T dy. So every product that does not involve the
+// state runs in parallel over all chunks, and the two chunk-serial kernels do
+// one state product per chunk.
+//
 // Kernels (all 64 x 64 chunk products are bf16 mma.sync with split hi/lo
-// operands, mma_bf16.cuh; Ti by blocked substitution in fp32):
-//   fwd_kernel        one CTA per (b, h, value-column split): walks the chunks
-//                     in order with the state slice in registers; writes y,
-//                     H_T and every chunk-start state (saved for the backward).
-//   bwd_chain_kernel  one CTA per (b, h, split): walks the chunks in reverse,
-//                     carrying dS; writes dS' of every chunk and dH0.
+// operands, mma_bf16.cuh; T^{-1} by blocked substitution in fp32):
+//   prep_kernel       one CTA per (b, h, chunk): T^{-1} (saved), Xn, Qt
+//                     (saved), Bc, Yp (forward workspace).
+//   chain_fwd_kernel  one CTA per (b, h, value-column split): S in registers,
+//                     one chunk per step; writes y, H_T and every chunk-start
+//                     state (saved for the backward).
+//   chain_bwd_kernel  one CTA per (b, h, split): dS in reverse; writes dS' of
+//                     every chunk and dH0.
 //   bwd_grads_kernel  one CTA per (b, h, chunk): every gradient of the chunk
-//                     from its saved S and dS'.
-// Inputs are staged with cp.async (next chunk prefetched during the current
-// one in the two chunk-serial kernels); out-of-range rows and columns are
+//                     from its saved S, T^{-1} and dS'.
+// Inputs are staged with cp.async (the next chunk prefetched during the
+// current one in the chunk-serial kernels); out-of-range rows and columns are
 // zero-filled, which makes every padded product exact (a zero K row gives an
 // identity row of T, a zero U row and no state update).
 #include "delta_args.cuh"
@@ -45,7 +54,12 @@ constexpr int kTile = 64 * kLd;            // bf16 elements of one 64 x 64 tile
 constexpr int kTileBytes = kTile * 2;      // 9216
 constexpr int kTld = 66;                   // fp32 leading dimension of T / T^{-1}
 constexpr int kF32Bytes = 64 * kTld * 4;   // 16896
-constexpr int kStageBytes = 3 * kTileBytes + 256;  // 3 tiles + beta[64] (fp32)
+constexpr int kTdBytes = 4 * 16 * 17 * 4;  // T's four diagonal 16 x 16 blocks, fp32, padded rows
+// Tiles kept in `saved` (T^{-1}, Xn, Qt) use the shared-memory layout (64 rows
+// of kLd elements), so one contiguous bulk copy stages a tile.
+constexpr int kSavedTile = 64 * kLd;
+constexpr long long kSavedPair = 2 * kSavedTile;
+constexpr int kRing = 3;  // staging depth of the chunk-serial kernels
 
 __device__ __forceinline__ void cp_async16(void* dst, const void* src, int src_bytes) {
   asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;\n" ::"r"(tc::smem_addr(dst)),
@@ -82,14 +96,14 @@ struct Neg {
 
 // Ti = T^{-1} for the unit lower-triangular T = I + strict_lower(T) of a chunk,
 // as split bf16 tiles (X). Inputs: the strictly-lower part of T as split tiles
-// (TS) and in fp32 (Tf, only its four diagonal 16 x 16 blocks are read).
+// (TS) and its four diagonal 16 x 16 blocks in fp32 (Td: [block][16][17]).
 //   1. diagonal blocks D_b^{-1} by forward substitution (one thread per column)
 //   2. X_10 = -D_1^{-1} T_10 D_0^{-1} and X_32 = -D_3^{-1} T_32 D_2^{-1} (warps 0, 1)
 //   3. X[32:64, 0:32] = -X[32:64, 32:64] (T[32:64, 0:32] X[0:32, 0:32])  (warps 0-3)
 // with every block product on the tensor cores (split operands, fp32 accumulate).
 // X's strictly-upper 16 x 16 blocks must be zero on entry (they are never
 // written); Y is scratch (two tiles).
-__device__ void tri_inv_tc(const float* Tf, Op TS, bf16* XH, bf16* XL, bf16* YH, bf16* YL) {
+__device__ void tri_inv_tc(const float* Td, Op TS, bf16* XH, bf16* XL, bf16* YH, bf16* YL) {
   const int tid = threadIdx.x, warp = tid >> 5;
   if (tid < 64) {
     const int o = (tid >> 4) * 16, j = tid & 15;
@@ -98,7 +112,7 @@ __device__ void tri_inv_tc(const float* Tf, Op TS, bf16* XH, bf16* XL, bf16* YH,
     for (int i = 0; i < 16; ++i) {
       float s = 0.f;
 #pragma unroll
-      for (int k = 0; k < i; ++k) s = fmaf(Tf[(o + i) * kTld + o + k], x[k], s);
+      for (int k = 0; k < i; ++k) s = fmaf(Td[(o >> 4) * 272 + i * 17 + k], x[k], s);
       x[i] = i == j ? 1.f : (i > j ? -s : 0.f);
     }
 #pragma unroll
@@ -152,21 +166,15 @@ __device__ void zero_upper_blocks(bf16* H, bf16* L) {
   }
 }
 
-// 64 x 64 bf16 tile <-> dense global 64 x 64 (16-byte vectors, all threads).
+// Shared tile <-> saved global tile (same padded layout; 16-byte vectors, all threads).
 template <int NTHR = kTcThreads>
 __device__ __forceinline__ void tile_to_global(const bf16* t, bf16* g) {
-  for (int i = threadIdx.x; i < 64 * 8; i += NTHR) {
-    const int row = i >> 3, ch = i & 7;
-    *reinterpret_cast<uint4*>(g + row * 64 + ch * 8) =
-        *reinterpret_cast<const uint4*>(t + row * kLd + ch * 8);
-  }
+  for (int i = threadIdx.x; i < kTileBytes / 16; i += NTHR)
+    reinterpret_cast<uint4*>(g)[i] = reinterpret_cast<const uint4*>(t)[i];
 }
 template <int NTHR = kTcThreads>
 __device__ __forceinline__ void tile_from_global_async(bf16* t, const bf16* g) {
-  for (int i = threadIdx.x; i < 64 * 8; i += NTHR) {
-    const int row = i >> 3, ch = i & 7;
-    cp_async16(t + row * kLd + ch * 8, g + row * 64 + ch * 8, 16);
-  }
+  for (int i = threadIdx.x; i < kTileBytes / 16; i += NTHR) cp_async16(t + i * 8, g + i * 8, 16);
 }
 
 
@@ -225,16 +233,17 @@ __device__ __forceinline__ void store_P(const float (&acc)[NT][4], const float* 
   });
 }
 
-// T's strict lower part (K K^T diag(beta)) as fp32 (diagonal blocks) and split tiles.
+// T's strict lower part (K K^T diag(beta)) as fp32 (diagonal blocks, Td) and split tiles.
 template <int NT>
 __device__ __forceinline__ void store_T(const float (&acc)[NT][4], const float* bs, int m0, int n0,
-                                        float* Tf, bf16* TH, bf16* TL) {
+                                        float* Td, bf16* TH, bf16* TL) {
 #pragma unroll
   for (int j = 0; j < NT; ++j)
 #pragma unroll
     for (int v = 0; v < 4; ++v) {
       const int row = tc::frag_row(m0, v), col = tc::frag_col(n0, j, v);
-      if ((col >> 4) == (row >> 4)) Tf[row * kTld + col] = col < row ? acc[j][v] * bs[col] : 0.f;
+      if ((col >> 4) == (row >> 4))
+        Td[(row >> 4) * 272 + (row & 15) * 17 + (col & 15)] = col < row ? acc[j][v] * bs[col] : 0.f;
     }
   tc::store_split(acc, TH, TL, m0, n0,
                   [&](int r, int cl, float x) { return cl < r ? x * bs[cl] : 0.f; });
@@ -257,297 +266,16 @@ struct TcArgs {
   float* dH0;
   float* Hs;    // (BH, nchunks, dk, dv) chunk-start states
   bf16* Ti;     // (BH, nchunks, 2, 64, 64) T^{-1} of every chunk, split hi / lo
+  bf16* Xn;     // (BH, nchunks, 2, 64, 64) -K^T diag(beta) W, split
+  bf16* Qt;     // (BH, nchunks, 2, 64, 64) Q - P W, split
+  float* Bc;    // (BH, nchunks, 4096) K^T diag(beta) U' as [dk][dv] (forward workspace)
+  float* Yp;    // (BH, nchunks, 4096) P U' as [C][dv] (forward workspace)
   float* dHs;   // (BH, nchunks, dk, dv) gradient of each chunk's output state
   long long T;
   int nh, dk, dv, C, nchunks, S, dvs;
 };
 
-// ------------------------------------------------------------ forward --
-// smem: 2 stages {K, Q, V_s, beta} | Ti h/l | W h/l (inverse scratch first) |
-//       P h/l | S h/l | U h/l (T fp32 first) | bU h/l (T split first)
-constexpr size_t kFwdSmem = 2 * kStageBytes + 12 * (size_t)kTileBytes;
-constexpr int kSerialThreads = 512;  // 16 warps: warp (mt, q) = (w & 3, w >> 2)
-
-// Warp tiling of the chunk-serial kernels: rows 16*mt; 64-wide products in
-// 16-column quarters (q), the DVS value columns in quarters of DVS/4, and the
-// two masked K K^T / Q K^T products as (matrix q >> 1, 32-column half q & 1).
-template <int DVS>
-__global__ void __launch_bounds__(kSerialThreads, 1) fwd_kernel(const TcArgs p) {
-  constexpr int NTQ = DVS / 32;  // n-tiles of a warp's quarter of the value columns
-  constexpr int NTH = kSerialThreads;
-  extern __shared__ __align__(128) unsigned char smem[];
-  unsigned char* rest = smem + 2 * kStageBytes;
-  bf16* TiH = reinterpret_cast<bf16*>(rest);
-  bf16* TiL = TiH + kTile;
-  bf16* WH = TiL + kTile;
-  bf16* WL = WH + kTile;
-  bf16* PH = WL + kTile;
-  bf16* PL = PH + kTile;
-  bf16* SH = PL + kTile;
-  bf16* SL = SH + kTile;
-  bf16* UH = SL + kTile;
-  bf16* UL = UH + kTile;
-  bf16* BUH = UL + kTile;
-  bf16* BUL = BUH + kTile;
-  float* Tf = reinterpret_cast<float*>(UH);
-  bf16 *TH = BUH, *TL = BUL, *YH = WH, *YL = WL;
-  auto Kt = [&](int s) { return reinterpret_cast<bf16*>(smem + s * kStageBytes); };
-  auto Qt = [&](int s) { return Kt(s) + kTile; };
-  auto Vt = [&](int s) { return Kt(s) + 2 * kTile; };
-  auto Bt = [&](int s) { return reinterpret_cast<float*>(smem + s * kStageBytes + 3 * kTileBytes); };
-
-  const int tid = threadIdx.x, warp = tid >> 5, mt = warp & 3, q = warp >> 2;
-  const int m0 = 16 * mt, nv = q * (DVS / 4), mat = q >> 1, hf = q & 1;
-  const int split = blockIdx.x % p.S;
-  const long long bh = blockIdx.x / p.S;
-  const int c0 = split * p.dvs, ncols = min(p.dvs, p.dv - c0);
-  const int kd = up16(p.dk);
-  const long long rows = p.T * p.nh;
-  const bf16* Kg = p.K + bh * rows * p.dk;
-  const bf16* Vg = p.V + bh * rows * p.dv + c0;
-  const bf16* Qg = p.Q + bh * p.T * p.dk;
-  const bf16* bg = p.beta + bh * rows;
-  bf16* yg = p.y + bh * p.T * p.dv + c0;
-  float* Hsg = p.Hs + bh * (long long)p.nchunks * p.dk * p.dv + c0;
-  bf16* Tig = p.Ti + bh * (long long)p.nchunks * 2 * 4096;
-
-  auto stage = [&](int c, int s) {
-    const long long t0 = (long long)c * p.C;
-    const int Cc = (int)min((long long)p.C, p.T - t0), Mc = Cc * p.nh;
-    stage_rows<8, NTH>(Kt(s), Kg + t0 * p.nh * p.dk, p.dk, Mc, p.dk >> 3);
-    stage_rows<8, NTH>(Qt(s), Qg + t0 * p.dk, p.dk, Cc, p.dk >> 3);
-    stage_rows<DVS / 8, NTH>(Vt(s), Vg + t0 * p.nh * p.dv, p.dv, Mc, ncols >> 3);
-    cp_async_commit();
-  };
-  // beta of a chunk, as raw bf16 bits: the next chunk's values are loaded a
-  // chunk ahead and converted only when stored, so no warp waits on the load.
-  auto beta_of = [&](int c) -> unsigned short {
-    const long long r0 = (long long)c * p.C * p.nh;
-    const int Mc = (int)min((long long)p.C * p.nh, rows - r0);
-    return tid < Mc ? reinterpret_cast<const unsigned short*>(bg)[r0 + tid] : (unsigned short)0;
-  };
-  auto bf = [](unsigned short raw) { return __uint_as_float((unsigned)raw << 16); };
-
-  // state slice: d_k rows m0.., value columns nv.. of this split
-  float hs[NTQ][4];
-  if (p.H0)
-    frag_from_global(hs, p.H0 + bh * p.dk * p.dv + c0, p.dv, m0, nv, p.dk, ncols);
-  else
-    tc::zero(hs);
-  tc::store_split(hs, SH, SL, m0, nv, Ident());
-  zero_upper_blocks<NTH>(TiH, TiL);
-  stage(0, 0);
-  if (tid < 64) Bt(0)[tid] = bf(beta_of(0));
-  unsigned short bnext = 0;
-
-  for (int c = 0; c < p.nchunks; ++c) {
-    const int s = c & 1;
-    const long long t0 = (long long)c * p.C;
-    const int Cc = (int)min((long long)p.C, p.T - t0), Mc = Cc * p.nh;
-    cp_async_wait_all();
-    __syncthreads();
-    if (c + 1 < p.nchunks) {
-      stage(c + 1, s ^ 1);
-      if (tid < 64) bnext = beta_of(c + 1);
-    }
-    const bf16* K = Kt(s);
-    const bf16* Q = Qt(s);
-    const bf16* V = Vt(s);
-    const float* bs = Bt(s);
-    frag_to_global(hs, Hsg + (long long)c * p.dk * p.dv, p.dv, m0, nv, p.dk, ncols);
-
-    {
-      float acc[4][4];
-      tc::zero(acc);
-      const int ncol = mat == 0 ? m0 + 16 : min(64, (m0 + 16) * p.nh);
-      const int np = min(2, max(0, (ncol - 32 * hf + 15) / 16));
-      tc::gemm<4, false, false>(acc, Op{mat == 0 ? K : Q, nullptr}, m0, Op{K, nullptr}, 32 * hf,
-                                0, kd, np);
-      if (mat == 0)
-        store_T(acc, bs, m0, 32 * hf, Tf, TH, TL);
-      else
-        store_P(acc, bs, p.nh, Mc, m0, 32 * hf, PH, PL);
-    }
-    __syncthreads();
-    tri_inv_tc(Tf, Op{TH, TL}, TiH, TiL, YH, YL);
-    if (split == 0) {
-      tile_to_global<NTH>(TiH, Tig + (long long)c * 8192);
-      tile_to_global<NTH>(TiL, Tig + (long long)c * 8192 + 4096);
-    }
-
-    // W = Ti K (rows m0, d_k columns 16q..), U' = Ti V (value columns nv..)
-    {
-      float w[2][4];
-      tc::zero(w);
-      tc::gemm<2, false, true>(w, Op{TiH, TiL}, m0, Op{K, nullptr}, 16 * q, 0, m0 + 16);
-      tc::store_split(w, WH, WL, m0, 16 * q, Ident());
-    }
-    float u[NTQ][4];
-    tc::zero(u);
-    tc::gemm<NTQ, false, true>(u, Op{TiH, TiL}, m0, Op{V, nullptr}, nv, 0, m0 + 16);
-    __syncthreads();
-
-    // U = U' - W S
-    {
-      float ws[NTQ][4];
-      tc::zero(ws);
-      tc::gemm<NTQ, false, true>(ws, Op{WH, WL}, m0, Op{SH, SL}, nv, 0, kd);
-#pragma unroll
-      for (int j = 0; j < NTQ; ++j)
-#pragma unroll
-        for (int v = 0; v < 4; ++v) u[j][v] -= ws[j][v];
-    }
-    tc::store_split(u, UH, UL, m0, nv, Ident());
-    tc::store_split(u, BUH, BUL, m0, nv, [&](int r, int, float x) { return x * bs[r]; });
-    __syncthreads();
-
-    // y = Q S + P U (token rows m0..)
-    {
-      float yv[NTQ][4];
-      tc::zero(yv);
-      tc::gemm<NTQ, false, true>(yv, Op{Q, nullptr}, m0, Op{SH, SL}, nv, 0, kd);
-      tc::gemm<NTQ, false, true>(yv, Op{PH, PL}, m0, Op{UH, UL}, nv, 0,
-                                 min(64, up16((m0 + 16) * p.nh)));
-      frag_to_global_bf16(yv, yg + t0 * p.dv, p.dv, m0, nv, Cc, ncols);
-    }
-    // S += K^T (beta U) (d_k rows m0..)
-    tc::gemm<NTQ, true, true>(hs, Op{K, nullptr}, m0, Op{BUH, BUL}, nv, 0, up16(Mc));
-    __syncthreads();
-    tc::store_split(hs, SH, SL, m0, nv, Ident());
-    if (tid < 64 && c + 1 < p.nchunks) Bt(s ^ 1)[tid] = bf(bnext);
-  }
-  frag_to_global(hs, p.HT + bh * p.dk * p.dv + c0, p.dv, m0, nv, p.dk, ncols);
-}
-
-// ----------------------------------------------------- backward: chain --
-// smem: 2 stages {K, Q, dy_s, Ti h, Ti l, beta} | P h/l | dS h/l | dU h/l | Gn h/l
-constexpr int kChainStage = 5 * kTileBytes + 256;
-constexpr size_t kChainSmem = 2 * (size_t)kChainStage + 8 * (size_t)kTileBytes;
-
-template <int DVS>
-__global__ void __launch_bounds__(kSerialThreads, 1) bwd_chain_kernel(const TcArgs p) {
-  constexpr int NTQ = DVS / 32;
-  constexpr int NTH = kSerialThreads;
-  extern __shared__ __align__(128) unsigned char smem[];
-  unsigned char* rest = smem + 2 * kChainStage;
-  bf16* PH = reinterpret_cast<bf16*>(rest);
-  bf16* PL = PH + kTile;
-  bf16* DH = PL + kTile;
-  bf16* DL = DH + kTile;
-  bf16* dUH = DL + kTile;
-  bf16* dUL = dUH + kTile;
-  bf16* GH = dUL + kTile;
-  bf16* GL = GH + kTile;
-  auto Kt = [&](int s) { return reinterpret_cast<bf16*>(smem + s * kChainStage); };
-  auto Qt = [&](int s) { return Kt(s) + kTile; };
-  auto Dt = [&](int s) { return Kt(s) + 2 * kTile; };
-  auto TiHt = [&](int s) { return Kt(s) + 3 * kTile; };
-  auto TiLt = [&](int s) { return Kt(s) + 4 * kTile; };
-  auto Bt = [&](int s) { return reinterpret_cast<float*>(smem + s * kChainStage + 5 * kTileBytes); };
-
-  const int tid = threadIdx.x, warp = tid >> 5, mt = warp & 3, q = warp >> 2;
-  const int m0 = 16 * mt, nv = q * (DVS / 4);
-  const int split = blockIdx.x % p.S;
-  const long long bh = blockIdx.x / p.S;
-  const int c0 = split * p.dvs, ncols = min(p.dvs, p.dv - c0);
-  const int kd = up16(p.dk);
-  const long long rows = p.T * p.nh;
-  const bf16* Kg = p.K + bh * rows * p.dk;
-  const bf16* Qg = p.Q + bh * p.T * p.dk;
-  const bf16* dyg = p.dy + bh * p.T * p.dv + c0;
-  const bf16* bg = p.beta + bh * rows;
-  const bf16* Tig = p.Ti + bh * (long long)p.nchunks * 2 * 4096;
-  float* dHsg = p.dHs + bh * (long long)p.nchunks * p.dk * p.dv + c0;
-
-  auto stage = [&](int c, int s) {
-    const long long t0 = (long long)c * p.C;
-    const int Cc = (int)min((long long)p.C, p.T - t0), Mc = Cc * p.nh;
-    stage_rows<8, NTH>(Kt(s), Kg + t0 * p.nh * p.dk, p.dk, Mc, p.dk >> 3);
-    stage_rows<8, NTH>(Qt(s), Qg + t0 * p.dk, p.dk, Cc, p.dk >> 3);
-    stage_rows<DVS / 8, NTH>(Dt(s), dyg + t0 * p.dv, p.dv, Cc, ncols >> 3);
-    tile_from_global_async<NTH>(TiHt(s), Tig + (long long)c * 8192);
-    tile_from_global_async<NTH>(TiLt(s), Tig + (long long)c * 8192 + 4096);
-    cp_async_commit();
-  };
-  // beta of a chunk, as raw bf16 bits: the next chunk's values are loaded a
-  // chunk ahead and converted only when stored, so no warp waits on the load.
-  auto beta_of = [&](int c) -> unsigned short {
-    const long long r0 = (long long)c * p.C * p.nh;
-    const int Mc = (int)min((long long)p.C * p.nh, rows - r0);
-    return tid < Mc ? reinterpret_cast<const unsigned short*>(bg)[r0 + tid] : (unsigned short)0;
-  };
-  auto bf = [](unsigned short raw) { return __uint_as_float((unsigned)raw << 16); };
-
-  float ds[NTQ][4];
-  if (p.dHT)
-    frag_from_global(ds, p.dHT + bh * p.dk * p.dv + c0, p.dv, m0, nv, p.dk, ncols);
-  else
-    tc::zero(ds);
-  tc::store_split(ds, DH, DL, m0, nv, Ident());
-  const int last = p.nchunks - 1;
-  stage(last, 0);
-  if (tid < 64) Bt(0)[tid] = bf(beta_of(last));
-  unsigned short bnext = 0;
-
-  for (int qq = 0; qq < p.nchunks; ++qq) {
-    const int c = last - qq, s = qq & 1;
-    const long long t0 = (long long)c * p.C;
-    const int Cc = (int)min((long long)p.C, p.T - t0), Mc = Cc * p.nh;
-    cp_async_wait_all();
-    __syncthreads();
-    if (c > 0) {
-      stage(c - 1, s ^ 1);
-      if (tid < 64) bnext = beta_of(c - 1);
-    }
-    const bf16* K = Kt(s);
-    const bf16* Q = Qt(s);
-    const bf16* dY = Dt(s);
-    const Op Ti{TiHt(s), TiLt(s)};
-    const float* bs = Bt(s);
-    frag_to_global(ds, dHsg + (long long)c * p.dk * p.dv, p.dv, m0, nv, p.dk, ncols);
-
-    // P (token rows m0, micro-step columns 16q..)
-    {
-      float acc[2][4];
-      tc::zero(acc);
-      const int ncol = min(64, (m0 + 16) * p.nh) - 16 * q;
-      tc::gemm<2, false, false>(acc, Op{Q, nullptr}, m0, Op{K, nullptr}, 16 * q, 0, kd,
-                                ncol <= 0 ? 0 : 1);
-      store_P(acc, bs, p.nh, Mc, m0, 16 * q, PH, PL);
-    }
-    __syncthreads();
-
-    // dU = P^T dy + beta * (K dS')   (micro-step rows m0..)
-    {
-      float du[NTQ][4], db[NTQ][4];
-      tc::zero(du);
-      tc::zero(db);
-      tc::gemm<NTQ, false, true>(db, Op{K, nullptr}, m0, Op{DH, DL}, nv, 0, kd);
-      tc::gemm<NTQ, true, true>(du, Op{PH, PL}, m0, Op{dY, nullptr}, nv, (m0 / p.nh) & ~15,
-                                up16(Cc));
-#pragma unroll
-      for (int j = 0; j < NTQ; ++j)
-#pragma unroll
-        for (int v = 0; v < 4; ++v) du[j][v] += bs[tc::frag_row(m0, v)] * db[j][v];
-      tc::store_split(du, dUH, dUL, m0, nv, Ident());
-    }
-    __syncthreads();
-    // Gn = -Ti^T dU
-    {
-      float g[NTQ][4];
-      tc::zero(g);
-      tc::gemm<NTQ, true, true>(g, Ti, m0, Op{dUH, dUL}, nv, m0, 64);
-      tc::store_split(g, GH, GL, m0, nv, Neg());
-    }
-    __syncthreads();
-    // dS = dS' + Q^T dy + K^T Gn   (d_k rows m0..)
-    tc::gemm<NTQ, true, true>(ds, Op{Q, nullptr}, m0, Op{dY, nullptr}, nv, 0, up16(Cc));
-    tc::gemm<NTQ, true, true>(ds, Op{K, nullptr}, m0, Op{GH, GL}, nv, 0, up16(Mc));
-    tc::store_split(ds, DH, DL, m0, nv, Ident());
-    if (tid < 64 && c > 0) Bt(s ^ 1)[tid] = bf(bnext);
-  }
-  frag_to_global(ds, p.dH0 + bh * p.dk * p.dv + c0, p.dv, m0, nv, p.dk, ncols);
-}
+constexpr int kSerialThreads = 512;  // 16 warps in the chunk-serial kernels
 
 // ----------------------------------------------------- backward: grads --
 // smem: K | Q | dy | V | beta, dbeta | S h/l | dS' h/l | KK f32 | QK f32 |
@@ -602,8 +330,8 @@ __global__ void __launch_bounds__(kGradThreads, 1) bwd_grads_kernel(const TcArgs
   stage_rows<8, NTH>(Q, p.Q + (bh * p.T + t0) * p.dk, p.dk, Cc, p.dk >> 3);
   stage_rows<8, NTH>(dY, p.dy + (bh * p.T + t0) * p.dv, p.dv, Cc, p.dv >> 3);
   stage_rows<8, NTH>(V, p.V + (bh * rows + r0) * p.dv, p.dv, Mc, p.dv >> 3);
-  tile_from_global_async<NTH>(TiH, p.Ti + (bh * p.nchunks + c) * 8192);
-  tile_from_global_async<NTH>(TiL, p.Ti + (bh * p.nchunks + c) * 8192 + 4096);
+  tile_from_global_async<NTH>(TiH, p.Ti + (bh * p.nchunks + c) * kSavedPair);
+  tile_from_global_async<NTH>(TiL, p.Ti + (bh * p.nchunks + c) * kSavedPair + kSavedTile);
   cp_async_commit();
   if (tid < 64) {
     bs[tid] = tid < Mc ? __bfloat162float(p.beta[bh * rows + r0 + tid]) : 0.f;
@@ -761,6 +489,344 @@ __global__ void __launch_bounds__(kGradThreads, 1) bwd_grads_kernel(const TcArgs
   if (tid < Mc) p.dbeta[bh * rows + r0 + tid] = __float2bfloat16_rn(dbs[tid]);
 }
 
+// ------------------------------------------------------- forward: prep --
+// One CTA per (b, h, chunk), independent of the state: T, T^{-1} (saved for
+// the backward), and the chunk's affine state map and readout
+//   S' = S + Xn S + Bc,   Xn = -K^T (beta W),  Bc = K^T (beta U')
+//   y  = Qt S + Yp,       Qt = Q - P~ (beta W), Yp = P~ (beta U')
+// with W = Ti K, U' = Ti V, P~ = (Q K^T) * read_mask (P = P~ diag(beta)).
+// Xn and Qt (split bf16 tiles) go to `saved` (both chains read them); Bc and
+// Yp (fp32) go to the workspace for the forward chain. Two CTAs per SM.
+// smem: K | Q | V | beta | Td | T h/l (-> bW h/l) | Ti h/l | Y h/l (-> bU' h/l) | P~ h/l
+constexpr size_t kPrepSmem = 11 * (size_t)kTileBytes + 256 + kTdBytes;
+
+// 16 x 8*NT fragment tile -> split bf16 saved tiles (hi, lo; padded layout),
+// f(row, col, x) applied first.
+template <int NT, class F>
+__device__ __forceinline__ void frag_to_global_split(const float (&c)[NT][4], bf16* hi, bf16* lo,
+                                                     int m0, int n0, F f) {
+#pragma unroll
+  for (int j = 0; j < NT; ++j)
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      const int row = tc::frag_row(m0, 2 * h), col = tc::frag_col(n0, j, 0);
+      uint32_t ph, pl;
+      tc::split_pack(f(row, col, c[j][2 * h]), f(row, col + 1, c[j][2 * h + 1]), ph, pl);
+      *reinterpret_cast<uint32_t*>(hi + row * kLd + col) = ph;
+      *reinterpret_cast<uint32_t*>(lo + row * kLd + col) = pl;
+    }
+}
+
+__global__ void __launch_bounds__(kGradThreads, 2) prep_kernel(const TcArgs p) {
+  extern __shared__ __align__(128) unsigned char smem[];
+  bf16* K = reinterpret_cast<bf16*>(smem);
+  bf16* Q = K + kTile;
+  bf16* V = Q + kTile;
+  float* bs = reinterpret_cast<float*>(V + kTile);
+  float* Td = bs + 64;
+  bf16* TH = reinterpret_cast<bf16*>(reinterpret_cast<unsigned char*>(Td) + kTdBytes);
+  bf16* TL = TH + kTile;
+  bf16* TiH = TL + kTile;
+  bf16* TiL = TiH + kTile;
+  bf16* YH = TiL + kTile;
+  bf16* YL = YH + kTile;
+  bf16* PH = YL + kTile;
+  bf16* PL = PH + kTile;
+  bf16 *BWH = TH, *BWL = TL, *BUH = YH, *BUL = YL;  // reused once the inverse is done
+
+  constexpr int NTH = kGradThreads;
+  const int tid = threadIdx.x, warp = tid >> 5, mt = warp & 3, q = warp >> 2;
+  const int m0 = 16 * mt, n0 = 16 * q, hf = q & 1, mat = q >> 1;
+  const int c = blockIdx.x % p.nchunks;
+  const long long bh = blockIdx.x / p.nchunks;
+  const long long t0 = (long long)c * p.C;
+  const int Cc = (int)min((long long)p.C, p.T - t0), Mc = Cc * p.nh;
+  const int kd = up16(p.dk);
+  const long long r0 = t0 * p.nh, rows = p.T * p.nh;
+  const long long blk = bh * p.nchunks + c;
+
+  zero_upper_blocks<NTH>(TiH, TiL);
+  stage_rows<8, NTH>(K, p.K + (bh * rows + r0) * p.dk, p.dk, Mc, p.dk >> 3);
+  stage_rows<8, NTH>(Q, p.Q + (bh * p.T + t0) * p.dk, p.dk, Cc, p.dk >> 3);
+  stage_rows<8, NTH>(V, p.V + (bh * rows + r0) * p.dv, p.dv, Mc, p.dv >> 3);
+  cp_async_commit();
+  if (tid < 64) bs[tid] = tid < Mc ? __bfloat162float(p.beta[bh * rows + r0 + tid]) : 0.f;
+  cp_async_wait_all();
+  __syncthreads();
+
+  // K K^T -> T (warps mat 0), Q K^T -> P~ (mat 1): row tile m0, columns 32*hf..
+  {
+    float acc[4][4];
+    tc::zero(acc);
+    const int ncol = mat == 0 ? m0 + 16 : min(64, (m0 + 16) * p.nh);
+    const int np = min(2, max(0, (ncol - 32 * hf + 15) / 16));
+    tc::gemm<4, false, false>(acc, Op{mat == 0 ? K : Q, nullptr}, m0, Op{K, nullptr}, 32 * hf, 0,
+                              kd, np);
+    if (mat == 0)
+      store_T(acc, bs, m0, 32 * hf, Td, TH, TL);
+    else
+      tc::store_split(acc, PH, PL, m0, 32 * hf, [&](int r, int cl, float x) {
+        return (cl < (r + 1) * p.nh && cl < Mc) ? x : 0.f;
+      });
+  }
+  __syncthreads();
+  tri_inv_tc(Td, Op{TH, TL}, TiH, TiL, YH, YL);
+  tile_to_global<NTH>(TiH, p.Ti + blk * kSavedPair);
+  tile_to_global<NTH>(TiL, p.Ti + blk * kSavedPair + kSavedTile);
+
+  // beta W = diag(beta) Ti K (rows m0, d_k columns n0..), beta U' = diag(beta) Ti V
+  {
+    auto bscale = [&](int r, int, float x) { return x * bs[r]; };
+    float w[2][4];
+    tc::zero(w);
+    tc::gemm<2, false, true>(w, Op{TiH, TiL}, m0, Op{K, nullptr}, n0, 0, m0 + 16);
+    tc::store_split(w, BWH, BWL, m0, n0, bscale);
+    float u[2][4];
+    tc::zero(u);
+    tc::gemm<2, false, true>(u, Op{TiH, TiL}, m0, Op{V, nullptr}, n0, 0, m0 + 16);
+    tc::store_split(u, BUH, BUL, m0, n0, bscale);
+  }
+  __syncthreads();
+  const int kp = min(64, up16((m0 + 16) * p.nh));  // causal extent of P~'s row tile
+  bf16* Xg = p.Xn + blk * kSavedPair;
+  bf16* Qg = p.Qt + blk * kSavedPair;
+  {  // Xn = -K^T (beta W): d_k rows m0, d_k columns n0
+    float x[2][4];
+    tc::zero(x);
+    tc::gemm<2, true, true>(x, Op{K, nullptr}, m0, Op{BWH, BWL}, n0, 0, up16(Mc));
+    frag_to_global_split(x, Xg, Xg + kSavedTile, m0, n0, Neg());
+  }
+  {  // Bc = K^T (beta U'): d_k rows m0, d_v columns n0
+    float b[2][4];
+    tc::zero(b);
+    tc::gemm<2, true, true>(b, Op{K, nullptr}, m0, Op{BUH, BUL}, n0, 0, up16(Mc));
+    frag_to_global(b, p.Bc + blk * 4096, p.dv, m0, n0, p.dk, p.dv);
+  }
+  {  // Qt = Q - P~ (beta W): token rows m0, d_k columns n0
+    float a[2][4];
+    tc::zero(a);
+    tc::gemm<2, false, true>(a, Op{PH, PL}, m0, Op{BWH, BWL}, n0, 0, kp);
+    frag_to_global_split(a, Qg, Qg + kSavedTile, m0, n0,
+                         [&](int r, int cl, float v) { return __bfloat162float(Q[r * kLd + cl]) - v; });
+  }
+  {  // Yp = P~ (beta U'): token rows m0, d_v columns n0
+    float a[2][4];
+    tc::zero(a);
+    tc::gemm<2, false, true>(a, Op{PH, PL}, m0, Op{BUH, BUL}, n0, 0, kp);
+    frag_to_global(a, p.Yp + blk * 4096, p.dv, m0, n0, Cc, p.dv);
+  }
+}
+
+// Thread 0: stage the saved tile pairs Xn and Qt of one chunk with bulk copies
+// completing on `bar` (X receives Xn hi, Xn lo, Qt hi, Qt lo).
+__device__ __forceinline__ void stage_xq(bf16* X, const TcArgs& p, long long blk, uint64_t* bar) {
+  mbar_arrive_expect_tx(bar, 4 * kTileBytes);
+  bulk_g2s(X, p.Xn + blk * kSavedPair, kTileBytes, bar);
+  bulk_g2s(X + kTile, p.Xn + blk * kSavedPair + kSavedTile, kTileBytes, bar);
+  bulk_g2s(X + 2 * kTile, p.Qt + blk * kSavedPair, kTileBytes, bar);
+  bulk_g2s(X + 3 * kTile, p.Qt + blk * kSavedPair + kSavedTile, kTileBytes, bar);
+}
+
+// ------------------------------------------------------ forward: chain --
+// One CTA per (b, h, value-column split) walks the chunks in order:
+//   S_c saved;  y_c = Qt S_c + Yp;  S_{c+1} = S_c + Xn S_c + Bc
+// State warps (0-7) own 16 x DVS/2 tiles of S in fp32 registers; output warps
+// (8-15) the matching tiles of y. Xn, Qt tiles are staged kRing - 1 chunks
+// ahead by bulk copies; Bc / Yp fragments are loaded into registers a chunk ahead.
+constexpr int kCfStage = 4 * kTileBytes;  // Xn h/l, Qt h/l
+constexpr size_t kChainFwdSmem = 128 + kRing * (size_t)kCfStage + 2 * (size_t)kTileBytes;
+
+template <int DVS>
+__global__ void __launch_bounds__(kSerialThreads, 1) chain_fwd_kernel(const TcArgs p) {
+  constexpr int NT = DVS / 16;
+  extern __shared__ __align__(128) unsigned char smem[];
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem);
+  unsigned char* ring = smem + 128;
+  bf16* SH = reinterpret_cast<bf16*>(ring + kRing * kCfStage);
+  bf16* SL = SH + kTile;
+  auto Xt = [&](int s) { return reinterpret_cast<bf16*>(ring + s * kCfStage); };
+
+  const int tid = threadIdx.x, warp = tid >> 5, mt = warp & 3;
+  const bool state = warp < 8;
+  const int m0 = 16 * mt, n0 = ((warp >> 2) & 1) * (DVS / 2);
+  const int split = blockIdx.x % p.S;
+  const long long bh = blockIdx.x / p.S;
+  const int c0 = split * p.dvs, ncols = min(p.dvs, p.dv - c0);
+  const int kd = up16(p.dk);
+  const long long blk0 = bh * p.nchunks;
+  bf16* yg = p.y + bh * p.T * p.dv + c0;
+  float* Hsg = p.Hs + blk0 * p.dk * p.dv + c0;
+
+  // this warp's fragment of chunk c's additive term (Bc for state warps, Yp otherwise)
+  auto addend = [&](int c, float (&a)[NT][4]) {
+    const long long t0 = (long long)c * p.C;
+    if (state)
+      frag_from_global(a, p.Bc + (blk0 + c) * 4096 + c0, p.dv, m0, n0, p.dk, ncols);
+    else
+      frag_from_global(a, p.Yp + (blk0 + c) * 4096 + c0, p.dv, m0, n0,
+                       (int)min((long long)p.C, p.T - t0), ncols);
+  };
+
+  if (tid == 0) {
+    for (int s = 0; s < kRing; ++s) mbar_init(full + s, 1);
+    mbar_fence_init();
+  }
+  float hs[NT][4];
+  if (state) {
+    if (p.H0)
+      frag_from_global(hs, p.H0 + bh * p.dk * p.dv + c0, p.dv, m0, n0, p.dk, ncols);
+    else
+      tc::zero(hs);
+    tc::store_split(hs, SH, SL, m0, n0, Ident());
+  }
+  __syncthreads();
+  if (tid == 0)
+    for (int c = 0; c < kRing - 1 && c < p.nchunks; ++c) stage_xq(Xt(c), p, blk0 + c, full + c);
+  float nxt[NT][4];
+  addend(0, nxt);
+
+  for (int c = 0; c < p.nchunks; ++c) {
+    const int s = c % kRing;
+    const long long t0 = (long long)c * p.C;
+    const int Cc = (int)min((long long)p.C, p.T - t0);
+    mbar_wait(full + s, (unsigned)(c / kRing) & 1u, &g_sticky_err);
+    __syncthreads();  // every thread is past chunk c - 1: its stage may be refilled
+    if (tid == 0 && c + kRing - 1 < p.nchunks) {
+      const int cn = c + kRing - 1;
+      stage_xq(Xt(cn % kRing), p, blk0 + cn, full + cn % kRing);
+    }
+    float acc[NT][4];
+#pragma unroll
+    for (int j = 0; j < NT; ++j)
+#pragma unroll
+      for (int v = 0; v < 4; ++v) acc[j][v] = nxt[j][v];
+    if (c + 1 < p.nchunks) addend(c + 1, nxt);
+    const bf16* X = Xt(s);
+    if (state) {
+      frag_to_global(hs, Hsg + (long long)c * p.dk * p.dv, p.dv, m0, n0, p.dk, ncols);
+#pragma unroll
+      for (int j = 0; j < NT; ++j)
+#pragma unroll
+        for (int v = 0; v < 4; ++v) acc[j][v] += hs[j][v];
+      tc::gemm<NT, false, true>(acc, Op{X, X + kTile}, m0, Op{SH, SL}, n0, 0, kd);
+#pragma unroll
+      for (int j = 0; j < NT; ++j)
+#pragma unroll
+        for (int v = 0; v < 4; ++v) hs[j][v] = acc[j][v];
+    } else {
+      tc::gemm<NT, false, true>(acc, Op{X + 2 * kTile, X + 3 * kTile}, m0, Op{SH, SL}, n0, 0, kd);
+      frag_to_global_bf16(acc, yg + t0 * p.dv, p.dv, m0, n0, Cc, ncols);
+    }
+    __syncthreads();
+    if (state) tc::store_split(hs, SH, SL, m0, n0, Ident());
+  }
+  if (state) frag_to_global(hs, p.HT + bh * p.dk * p.dv + c0, p.dv, m0, n0, p.dk, ncols);
+}
+
+// ----------------------------------------------------- backward: chain --
+// One CTA per (b, h, split) walks the chunks in reverse carrying dS:
+//   dS'_c (= dS entering from chunk c + 1) saved;
+//   dS_c = dS'_c + Xn^T dS'_c + Qt^T dy_c
+// State warps (0-7) own dS tiles in fp32 registers; warps 8-15 form Qt^T dy
+// (independent of dS) into shared memory in the same step. Xn, Qt by bulk
+// copies and dy by cp.async, kRing - 1 chunks ahead.
+constexpr int kCbStage = 5 * kTileBytes;  // Xn h/l, Qt h/l, dy
+constexpr size_t kChainBwdSmem =
+    128 + kRing * (size_t)kCbStage + 2 * (size_t)kTileBytes + kF32Bytes;
+
+template <int DVS>
+__global__ void __launch_bounds__(kSerialThreads, 1) chain_bwd_kernel(const TcArgs p) {
+  constexpr int NT = DVS / 16;
+  constexpr int NTH = kSerialThreads;
+  extern __shared__ __align__(128) unsigned char smem[];
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem);
+  unsigned char* ring = smem + 128;
+  bf16* DH = reinterpret_cast<bf16*>(ring + kRing * kCbStage);
+  bf16* DL = DH + kTile;
+  float* Gf = reinterpret_cast<float*>(DL + kTile);  // Qt^T dy, [64][kTld]
+  auto Xt = [&](int s) { return reinterpret_cast<bf16*>(ring + s * kCbStage); };
+
+  const int tid = threadIdx.x, warp = tid >> 5, mt = warp & 3;
+  const bool state = warp < 8;
+  const int m0 = 16 * mt, n0 = ((warp >> 2) & 1) * (DVS / 2);
+  const int split = blockIdx.x % p.S;
+  const long long bh = blockIdx.x / p.S;
+  const int c0 = split * p.dvs, ncols = min(p.dvs, p.dv - c0);
+  const int kd = up16(p.dk);
+  const long long blk0 = bh * p.nchunks;
+  const bf16* dyg = p.dy + bh * p.T * p.dv + c0;
+  float* dHsg = p.dHs + blk0 * p.dk * p.dv + c0;
+  const int last = p.nchunks - 1;
+
+  // step qq handles chunk last - qq in ring slot qq % kRing
+  auto stage = [&](int qq) {
+    const int c = last - qq;
+    bf16* X = Xt(qq % kRing);
+    if (tid == 0) stage_xq(X, p, blk0 + c, full + qq % kRing);
+    const long long t0 = (long long)c * p.C;
+    stage_rows<DVS / 8, NTH>(X + 4 * kTile, dyg + t0 * p.dv, p.dv,
+                             (int)min((long long)p.C, p.T - t0), ncols >> 3);
+    cp_async_commit();
+  };
+
+  if (tid == 0) {
+    for (int s = 0; s < kRing; ++s) mbar_init(full + s, 1);
+    mbar_fence_init();
+  }
+  float ds[NT][4];
+  if (state) {
+    if (p.dHT)
+      frag_from_global(ds, p.dHT + bh * p.dk * p.dv + c0, p.dv, m0, n0, p.dk, ncols);
+    else
+      tc::zero(ds);
+    tc::store_split(ds, DH, DL, m0, n0, Ident());
+  }
+  __syncthreads();
+  for (int qq = 0; qq < kRing - 1 && qq <= last; ++qq) stage(qq);
+
+  for (int qq = 0; qq <= last; ++qq) {
+    const int c = last - qq, s = qq % kRing;
+    const long long t0 = (long long)c * p.C;
+    const int Cc = (int)min((long long)p.C, p.T - t0);
+    if (qq < last)  // the group of step qq + 1 may still be in flight
+      asm volatile("cp.async.wait_group 1;\n" ::: "memory");
+    else
+      cp_async_wait_all();
+    mbar_wait(full + s, (unsigned)(qq / kRing) & 1u, &g_sticky_err);
+    __syncthreads();
+    if (qq + kRing - 1 <= last) stage(qq + kRing - 1);
+    const bf16* X = Xt(s);
+    float acc[NT][4];
+    if (state) {
+      frag_to_global(ds, dHsg + (long long)c * p.dk * p.dv, p.dv, m0, n0, p.dk, ncols);
+#pragma unroll
+      for (int j = 0; j < NT; ++j)
+#pragma unroll
+        for (int v = 0; v < 4; ++v) acc[j][v] = ds[j][v];
+      tc::gemm<NT, true, true>(acc, Op{X, X + kTile}, m0, Op{DH, DL}, n0, 0, kd);
+    } else {
+      tc::zero(acc);
+      tc::gemm<NT, true, true>(acc, Op{X + 2 * kTile, X + 3 * kTile}, m0, Op{X + 4 * kTile, nullptr},
+                               n0, 0, up16(Cc));
+#pragma unroll
+      for (int j = 0; j < NT; ++j)
+#pragma unroll
+        for (int v = 0; v < 4; ++v)
+          Gf[tc::frag_row(m0, v) * kTld + tc::frag_col(n0, j, v)] = acc[j][v];
+    }
+    __syncthreads();
+    if (state) {
+#pragma unroll
+      for (int j = 0; j < NT; ++j)
+#pragma unroll
+        for (int v = 0; v < 4; ++v)
+          ds[j][v] = acc[j][v] + Gf[tc::frag_row(m0, v) * kTld + tc::frag_col(n0, j, v)];
+      tc::store_split(ds, DH, DL, m0, n0, Ident());
+    }
+  }
+  if (state) frag_to_global(ds, p.dH0 + bh * p.dk * p.dv + c0, p.dv, m0, n0, p.dk, ncols);
+}
+
 // ---------------------------------------------------------------- host --
 
 int sm_count() {
@@ -795,14 +861,18 @@ bool tc_eligible(int dtype, int nh, int dk, int dv, int C) {
          dv >= 8 && dv <= 64 && dk % 8 == 0 && dv % 8 == 0;
 }
 
-// saved: chunk-start states (fp32) then every chunk's T^{-1} (split bf16, 64 x 64 x 2)
+// saved: chunk-start states (fp32), then every chunk's T^{-1}, Xn and Qt
+// (split bf16 tile pairs in the padded shared-memory layout)
 size_t tc_saved_floats(long long BH, long long T, int dk, int dv, int C) {
   const size_t nc = (size_t)BH * (size_t)((T + C - 1) / C);
-  return nc * dk * dv + nc * 4096;
+  return nc * dk * dv + 3 * nc * (size_t)kSavedPair / 2;
 }
 
+// forward: Bc and Yp (4096 floats each per chunk); backward: dS' per chunk
 size_t tc_workspace_floats(long long BH, long long T, int dk, int dv, int C) {
-  return (size_t)BH * (size_t)((T + C - 1) / C) * dk * dv;
+  const size_t nc = (size_t)BH * (size_t)((T + C - 1) / C);
+  const size_t bwd = nc * dk * dv, fwd = 2 * nc * 4096;
+  return fwd > bwd ? fwd : bwd;
 }
 
 int run_tc(bool fwd, const Args<__nv_bfloat16>& p, long long B, int H, long long T, int nh, int dk,
@@ -834,8 +904,13 @@ int run_tc(bool fwd, const Args<__nv_bfloat16>& p, long long B, int H, long long
   const bool narrow = a.dvs <= 32;
   if (BH == 0) return MGS_OK;
   if (saved == nullptr) return MGS_BAD_SHAPE;
+  const size_t ncs = (size_t)BH * a.nchunks;
   a.Hs = saved;
-  a.Ti = reinterpret_cast<bf16*>(saved + (size_t)BH * a.nchunks * dk * dv);
+  a.Ti = reinterpret_cast<bf16*>(saved + ncs * dk * dv);
+  a.Xn = a.Ti + ncs * kSavedPair;
+  a.Qt = a.Xn + ncs * kSavedPair;
+  if (T > 0 && (ws == nullptr || ws_bytes < tc_workspace_floats(BH, T, dk, dv, C) * sizeof(float)))
+    return MGS_WORKSPACE_TOO_SMALL;
   if (fwd) {
     if (T == 0) {
       if (p.H0)
@@ -845,8 +920,12 @@ int run_tc(bool fwd, const Args<__nv_bfloat16>& p, long long B, int H, long long
         MGS_CUDA_OK(cudaMemsetAsync(p.HT, 0, (size_t)BH * dk * dv * sizeof(float), st));
       return MGS_OK;
     }
-    return narrow ? launch_tc(fwd_kernel<32>, BH * a.S, kFwdSmem, st, a, kSerialThreads)
-                  : launch_tc(fwd_kernel<64>, BH * a.S, kFwdSmem, st, a, kSerialThreads);
+    a.Bc = static_cast<float*>(ws);
+    a.Yp = a.Bc + ncs * 4096;
+    const int rc = launch_tc(prep_kernel, (long long)ncs, kPrepSmem, st, a, kGradThreads);
+    if (rc != MGS_OK) return rc;
+    return narrow ? launch_tc(chain_fwd_kernel<32>, BH * a.S, kChainFwdSmem, st, a, kSerialThreads)
+                  : launch_tc(chain_fwd_kernel<64>, BH * a.S, kChainFwdSmem, st, a, kSerialThreads);
   }
   if (T == 0) {
     if (p.dHT)
@@ -856,11 +935,9 @@ int run_tc(bool fwd, const Args<__nv_bfloat16>& p, long long B, int H, long long
       MGS_CUDA_OK(cudaMemsetAsync(p.dH0, 0, (size_t)BH * dk * dv * sizeof(float), st));
     return MGS_OK;
   }
-  if (ws == nullptr || ws_bytes < tc_workspace_floats(BH, T, dk, dv, C) * sizeof(float))
-    return MGS_WORKSPACE_TOO_SMALL;
   a.dHs = static_cast<float*>(ws);
-  int rc = narrow ? launch_tc(bwd_chain_kernel<32>, BH * a.S, kChainSmem, st, a, kSerialThreads)
-                  : launch_tc(bwd_chain_kernel<64>, BH * a.S, kChainSmem, st, a, kSerialThreads);
+  int rc = narrow ? launch_tc(chain_bwd_kernel<32>, BH * a.S, kChainBwdSmem, st, a, kSerialThreads)
+                  : launch_tc(chain_bwd_kernel<64>, BH * a.S, kChainBwdSmem, st, a, kSerialThreads);
   if (rc != MGS_OK) return rc;
   return launch_tc(bwd_grads_kernel, BH * a.nchunks, kGradSmem, st, a, kGradThreads);
 }
