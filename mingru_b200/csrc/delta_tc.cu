@@ -682,8 +682,11 @@ __global__ void __launch_bounds__(kSerialThreads, 1) chain_fwd_kernel(const TcAr
   __syncthreads();
   if (tid == 0)
     for (int c = 0; c < kRing - 1 && c < p.nchunks; ++c) stage_xq(Xt(c), p, blk0 + c, full + c);
-  float nxt[NT][4];
+  if (state) frag_to_global(hs, Hsg, p.dv, m0, n0, p.dk, ncols);
+  // additive terms of the next two chunks, loaded two chunks ahead
+  float nxt[NT][4], nxt2[NT][4];
   addend(0, nxt);
+  if (p.nchunks > 1) addend(1, nxt2);
 
   for (int c = 0; c < p.nchunks; ++c) {
     const int s = c % kRing;
@@ -699,26 +702,32 @@ __global__ void __launch_bounds__(kSerialThreads, 1) chain_fwd_kernel(const TcAr
 #pragma unroll
     for (int j = 0; j < NT; ++j)
 #pragma unroll
-      for (int v = 0; v < 4; ++v) acc[j][v] = nxt[j][v];
-    if (c + 1 < p.nchunks) addend(c + 1, nxt);
+      for (int v = 0; v < 4; ++v) {
+        acc[j][v] = nxt[j][v];
+        nxt[j][v] = nxt2[j][v];
+      }
+    if (c + 2 < p.nchunks) addend(c + 2, nxt2);
     const bf16* X = Xt(s);
     if (state) {
-      frag_to_global(hs, Hsg + (long long)c * p.dk * p.dv, p.dv, m0, n0, p.dk, ncols);
 #pragma unroll
       for (int j = 0; j < NT; ++j)
 #pragma unroll
         for (int v = 0; v < 4; ++v) acc[j][v] += hs[j][v];
-      tc::gemm<NT, false, true>(acc, Op{X, X + kTile}, m0, Op{SH, SL}, n0, 0, kd);
+      tc::gemm_k64<NT, false, true>(acc, Op{X, X + kTile}, m0, Op{SH, SL}, n0);
 #pragma unroll
       for (int j = 0; j < NT; ++j)
 #pragma unroll
         for (int v = 0; v < 4; ++v) hs[j][v] = acc[j][v];
     } else {
-      tc::gemm<NT, false, true>(acc, Op{X + 2 * kTile, X + 3 * kTile}, m0, Op{SH, SL}, n0, 0, kd);
+      tc::gemm_k64<NT, false, true>(acc, Op{X + 2 * kTile, X + 3 * kTile}, m0, Op{SH, SL}, n0);
       frag_to_global_bf16(acc, yg + t0 * p.dv, p.dv, m0, n0, Cc, ncols);
     }
     __syncthreads();
-    if (state) tc::store_split(hs, SH, SL, m0, n0, Ident());
+    if (state) {
+      tc::store_split(hs, SH, SL, m0, n0, Ident());
+      if (c + 1 < p.nchunks)  // S_{c+1}, off the critical path
+        frag_to_global(hs, Hsg + (long long)(c + 1) * p.dk * p.dv, p.dv, m0, n0, p.dk, ncols);
+    }
   }
   if (state) frag_to_global(hs, p.HT + bh * p.dk * p.dv + c0, p.dv, m0, n0, p.dk, ncols);
 }
@@ -783,6 +792,7 @@ __global__ void __launch_bounds__(kSerialThreads, 1) chain_bwd_kernel(const TcAr
   }
   __syncthreads();
   for (int qq = 0; qq < kRing - 1 && qq <= last; ++qq) stage(qq);
+  if (state) frag_to_global(ds, dHsg + (long long)last * p.dk * p.dv, p.dv, m0, n0, p.dk, ncols);
 
   for (int qq = 0; qq <= last; ++qq) {
     const int c = last - qq, s = qq % kRing;
@@ -798,16 +808,15 @@ __global__ void __launch_bounds__(kSerialThreads, 1) chain_bwd_kernel(const TcAr
     const bf16* X = Xt(s);
     float acc[NT][4];
     if (state) {
-      frag_to_global(ds, dHsg + (long long)c * p.dk * p.dv, p.dv, m0, n0, p.dk, ncols);
 #pragma unroll
       for (int j = 0; j < NT; ++j)
 #pragma unroll
         for (int v = 0; v < 4; ++v) acc[j][v] = ds[j][v];
-      tc::gemm<NT, true, true>(acc, Op{X, X + kTile}, m0, Op{DH, DL}, n0, 0, kd);
+      tc::gemm_k64<NT, true, true>(acc, Op{X, X + kTile}, m0, Op{DH, DL}, n0);
     } else {
       tc::zero(acc);
-      tc::gemm<NT, true, true>(acc, Op{X + 2 * kTile, X + 3 * kTile}, m0, Op{X + 4 * kTile, nullptr},
-                               n0, 0, up16(Cc));
+      tc::gemm_k64<NT, true, true>(acc, Op{X + 2 * kTile, X + 3 * kTile}, m0,
+                                   Op{X + 4 * kTile, nullptr}, n0);
 #pragma unroll
       for (int j = 0; j < NT; ++j)
 #pragma unroll
@@ -822,6 +831,8 @@ __global__ void __launch_bounds__(kSerialThreads, 1) chain_bwd_kernel(const TcAr
         for (int v = 0; v < 4; ++v)
           ds[j][v] = acc[j][v] + Gf[tc::frag_row(m0, v) * kTld + tc::frag_col(n0, j, v)];
       tc::store_split(ds, DH, DL, m0, n0, Ident());
+      if (c > 0)  // dS'_{c-1}, off the critical path
+        frag_to_global(ds, dHsg + (long long)(c - 1) * p.dk * p.dv, p.dv, m0, n0, p.dk, ncols);
     }
   }
   if (state) frag_to_global(ds, p.dH0 + bh * p.dk * p.dv + c0, p.dv, m0, n0, p.dk, ncols);
