@@ -40,6 +40,7 @@
 // identity row of T, a zero U row and no state update).
 #include "delta_args.cuh"
 #include "mma_bf16.cuh"
+#include "umma.cuh"
 
 namespace mgs {
 namespace delta {
@@ -278,215 +279,295 @@ struct TcArgs {
 constexpr int kSerialThreads = 512;  // 16 warps in the chunk-serial kernels
 
 // ----------------------------------------------------- backward: grads --
-// smem: K | Q | dy | V | beta, dbeta | S h/l | dS' h/l | KK f32 | QK f32 |
-//       R8 U h/l | R9 (W h/l -> Gn h/l) | R10 (Ti h/l -> dKK h/l) |
-//       R11 (P h/l -> dS_ h/l) | bU h/l | dU h/l
-constexpr size_t kGradSmem = 4 * (size_t)kTileBytes + 512 + 4 * (size_t)kTileBytes +
-                             2 * (size_t)kF32Bytes + 12 * (size_t)kTileBytes;
+// One CTA per (b, h, chunk): every gradient of the chunk from its saved S,
+// T^{-1} and dS', on the tcgen05 tensor cores (umma.cuh). Thread 0 issues each
+// level of products as one batch of 64 x 64 x 64 split MMAs into TMEM; all 16
+// warps then read the accumulators (warp w: rows 16*(w%4).., columns 16*(w/4)..)
+// and write the masked / scaled / split operands of the next level:
+//   1. K K^T, Q K^T, W = Ti K, U' = Ti V, dbU = K dS'
+//   2. U = U' + (-W) S (same accumulator), P^T dy          [P = Q K^T beta * read]
+//   3. G = Ti^T dU (-> dV)                                 [dU = P^T dy + beta dbU]
+//   4. dy U^T, Gn U^T (Gn = -G)                            [-> dS_, dKK, dbeta columns]
+//   5. dQ = dy S^T + dS_ K;  dK = (beta U) dS'^T + dS_^T Q + Gn S^T + dKK K + dKK^T K
+// TMEM columns: KK 0, QK 64, W -> G 128, U 192, dbU -> dKK 256, P^T dy -> dy U^T 320;
+// dQ reuses 0 and dK 64 once KK and QK have been read.
+// smem (blocked 8 KB tiles): K | Q | dY | V | S h/l | dS' h/l | Ti h/l | P h/l (-> Gn) |
+//   -W h/l (-> dS_) | U h/l | bU h/l | dU h/l (-> dKK) | beta, dbeta
+constexpr int kGradThreads = 512;
+constexpr size_t kGradSmem = 1024 + 20 * (size_t)umma::kTileBytes + 512;
+constexpr int kGradTmemCols = 512;
 
-constexpr int kGradThreads = 512;  // 16 warps: warp (mt, q) = (w & 3, w >> 2)
+// 64 rows x (8 * valid_ch) columns of a row-major global bf16 matrix into a
+// blocked tile (cp.async); rows >= nrows and chunks >= valid_ch are zero.
+template <int NTHR>
+__device__ __forceinline__ void stage_blocked(bf16* tile, const bf16* g, long long ld, int nrows,
+                                              int valid_ch) {
+  for (int i = threadIdx.x; i < 64 * 8; i += NTHR) {
+    const int row = i >> 3, ch = i & 7;
+    const bool ok = row < nrows && ch < valid_ch;
+    cp_async16(tile + umma::boff(row, ch * 8), ok ? g + row * ld + ch * 8 : g, ok ? 16 : 0);
+  }
+}
+
+// Padded shared tile -> blocked global tile (16-byte chunks, all threads).
+template <int NTHR>
+__device__ __forceinline__ void tile_to_global_blocked(const bf16* t, bf16* g) {
+  for (int i = threadIdx.x; i < 64 * 8; i += NTHR) {
+    const int row = i >> 3, ch = i & 7;
+    *reinterpret_cast<uint4*>(g + umma::boff(row, ch * 8)) =
+        *reinterpret_cast<const uint4*>(t + row * kLd + ch * 8);
+  }
+}
+
+// Row r, columns c0..c0+15 of an accumulator row -> bf16 global row (columns < ncols).
+__device__ __forceinline__ void row16_to_global(bf16* g, int c0, int ncols, const float (&v)[16]) {
+#pragma unroll
+  for (int h = 0; h < 2; ++h)
+    if (c0 + 8 * h < ncols) {
+      uint32_t w[4];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) w[i] = tc::pack_bf16(v[8 * h + 2 * i], v[8 * h + 2 * i + 1]);
+      *reinterpret_cast<uint4*>(g + c0 + 8 * h) = make_uint4(w[0], w[1], w[2], w[3]);
+    }
+}
 
 __global__ void __launch_bounds__(kGradThreads, 1) bwd_grads_kernel(const TcArgs p) {
-  extern __shared__ __align__(128) unsigned char smem[];
-  bf16* K = reinterpret_cast<bf16*>(smem);
-  bf16* Q = K + kTile;
-  bf16* dY = Q + kTile;
-  bf16* V = dY + kTile;
-  float* bs = reinterpret_cast<float*>(V + kTile);
+  namespace um = umma;
+  extern __shared__ __align__(1024) unsigned char smem[];
+  uint64_t* bar = reinterpret_cast<uint64_t*>(smem);  // [0] MMA batches, [1] T^{-1} copy
+  uint32_t* tbase_s = reinterpret_cast<uint32_t*>(smem + 64);
+  bf16* tiles = reinterpret_cast<bf16*>(smem + 1024);
+  auto T = [&](int i) { return tiles + i * (um::kTileBytes / 2); };
+  bf16 *K = T(0), *Q = T(1), *dY = T(2), *V = T(3), *SH = T(4), *SL = T(5), *DH = T(6),
+       *DL = T(7), *TiH = T(8), *TiL = T(9), *PH = T(10), *PL = T(11), *WH = T(12), *WL = T(13),
+       *UH = T(14), *UL = T(15), *BUH = T(16), *BUL = T(17), *dUH = T(18), *dUL = T(19);
+  bf16 *GH = PH, *GL = PL, *dSH = WH, *dSL = WL, *dKH = dUH, *dKL = dUL;
+  float* bs = reinterpret_cast<float*>(T(20));
   float* dbs = bs + 64;
-  bf16* SH = reinterpret_cast<bf16*>(dbs + 64);
-  bf16* SL = SH + kTile;
-  bf16* DH = SL + kTile;
-  bf16* DL = DH + kTile;
-  float* KKf = reinterpret_cast<float*>(DL + kTile);
-  float* QKf = KKf + 64 * kTld;
-  bf16* R8 = reinterpret_cast<bf16*>(QKf + 64 * kTld);
-  bf16* R9 = R8 + 2 * kTile;
-  bf16* R10 = R9 + 2 * kTile;
-  bf16* R11 = R10 + 2 * kTile;
-  bf16* BUH = R11 + 2 * kTile;
-  bf16* BUL = BUH + kTile;
-  bf16* dUH = BUL + kTile;
-  bf16* dUL = dUH + kTile;
-  bf16 *UH = R8, *UL = R8 + kTile;
-  bf16 *WH = R9, *WL = R9 + kTile, *GH = R9, *GL = R9 + kTile;
-  bf16 *TiH = R10, *TiL = R10 + kTile, *dKH = R10, *dKL = R10 + kTile;
-  bf16 *PH = R11, *PL = R11 + kTile, *dSH = R11, *dSL = R11 + kTile;
 
   constexpr int NTH = kGradThreads;
-  const int tid = threadIdx.x, warp = tid >> 5, mt = warp & 3, q = warp >> 2;
-  const int m0 = 16 * mt, n0 = 16 * q;       // 16 x 16 tiles of the 64 x 64 products
-  const int hf = q & 1, mat = q >> 1;        // 16 x 32 tiles of the masked products
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int q = warp & 3, col0 = 16 * (warp >> 2), row = 16 * q + lane;
+  const bool rv = lane < 16;  // this lane holds row `row` of the 64-row accumulators
   const int c = blockIdx.x % p.nchunks;
   const long long bh = blockIdx.x / p.nchunks;
   const long long t0 = (long long)c * p.C;
   const int Cc = (int)min((long long)p.C, p.T - t0), Mc = Cc * p.nh;
-  const int kd = up16(p.dk), kv = up16(p.dv);
-  const long long r0 = t0 * p.nh;
-  const long long rows = p.T * p.nh;
-  const long long sofs = (bh * p.nchunks + c) * (long long)p.dk * p.dv;
+  const long long r0 = t0 * p.nh, rows = p.T * p.nh;
+  const long long blk = bh * p.nchunks + c;
+  const long long sofs = blk * (long long)p.dk * p.dv;
 
-  stage_rows<8, NTH>(K, p.K + (bh * rows + r0) * p.dk, p.dk, Mc, p.dk >> 3);
-  stage_rows<8, NTH>(Q, p.Q + (bh * p.T + t0) * p.dk, p.dk, Cc, p.dk >> 3);
-  stage_rows<8, NTH>(dY, p.dy + (bh * p.T + t0) * p.dv, p.dv, Cc, p.dv >> 3);
-  stage_rows<8, NTH>(V, p.V + (bh * rows + r0) * p.dv, p.dv, Mc, p.dv >> 3);
-  tile_from_global_async<NTH>(TiH, p.Ti + (bh * p.nchunks + c) * kSavedPair);
-  tile_from_global_async<NTH>(TiL, p.Ti + (bh * p.nchunks + c) * kSavedPair + kSavedTile);
+  if (warp == 0) um::alloc(tbase_s, kGradTmemCols);
+  if (tid == 0) {
+    mbar_init(bar, 1);
+    mbar_init(bar + 1, 1);
+    mbar_fence_init();
+  }
+  stage_blocked<NTH>(K, p.K + (bh * rows + r0) * p.dk, p.dk, Mc, p.dk >> 3);
+  stage_blocked<NTH>(Q, p.Q + (bh * p.T + t0) * p.dk, p.dk, Cc, p.dk >> 3);
+  stage_blocked<NTH>(dY, p.dy + (bh * p.T + t0) * p.dv, p.dv, Cc, p.dv >> 3);
+  stage_blocked<NTH>(V, p.V + (bh * rows + r0) * p.dv, p.dv, Mc, p.dv >> 3);
   cp_async_commit();
+  um::fence_before();
+  __syncthreads();  // barriers initialised, TMEM base written
+  if (tid == 0) {
+    mbar_arrive_expect_tx(bar + 1, 2 * um::kTileBytes);
+    bulk_g2s(TiH, p.Ti + blk * kSavedPair, um::kTileBytes, bar + 1);
+    bulk_g2s(TiL, p.Ti + blk * kSavedPair + 4096, um::kTileBytes, bar + 1);
+  }
+  // S (chunk-start state) and dS' (fp32 [dk][dv]) -> split blocked tiles
+  for (int i = tid; i < 64 * 8; i += NTH) {
+    const int r = i >> 3, cb = i & 7;
+    float a[16], b[16];
+#pragma unroll
+    for (int j = 0; j < 16; ++j) a[j] = b[j] = 0.f;
+    if (r < p.dk && cb * 8 < p.dv) {
+      const float4* sa = reinterpret_cast<const float4*>(p.Hs + sofs + r * p.dv + cb * 8);
+      const float4* sb = reinterpret_cast<const float4*>(p.dHs + sofs + r * p.dv + cb * 8);
+      const float4 a0 = sa[0], a1 = sa[1], b0 = sb[0], b1 = sb[1];
+      a[0] = a0.x; a[1] = a0.y; a[2] = a0.z; a[3] = a0.w; a[4] = a1.x; a[5] = a1.y; a[6] = a1.z; a[7] = a1.w;
+      b[0] = b0.x; b[1] = b0.y; b[2] = b0.z; b[3] = b0.w; b[4] = b1.x; b[5] = b1.y; b[6] = b1.z; b[7] = b1.w;
+    }
+    // store_split16 writes two 8-column chunks: write this chunk and leave the next untouched
+    uint32_t ph[4], pl[4], qh[4], ql[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      tc::split_pack(a[2 * j], a[2 * j + 1], ph[j], pl[j]);
+      tc::split_pack(b[2 * j], b[2 * j + 1], qh[j], ql[j]);
+    }
+    const int o = um::boff(r, cb * 8);
+    *reinterpret_cast<uint4*>(SH + o) = make_uint4(ph[0], ph[1], ph[2], ph[3]);
+    *reinterpret_cast<uint4*>(SL + o) = make_uint4(pl[0], pl[1], pl[2], pl[3]);
+    *reinterpret_cast<uint4*>(DH + o) = make_uint4(qh[0], qh[1], qh[2], qh[3]);
+    *reinterpret_cast<uint4*>(DL + o) = make_uint4(ql[0], ql[1], ql[2], ql[3]);
+  }
   if (tid < 64) {
     bs[tid] = tid < Mc ? __bfloat162float(p.beta[bh * rows + r0 + tid]) : 0.f;
     dbs[tid] = 0.f;
   }
-  // S (chunk-start state) and dS' -> split tiles (rows d_k, cols d_v)
-  for (int i = tid; i < 64 * 32; i += NTH) {
-    const int row = i >> 5, col = (i & 31) << 1;
-    float2 a = make_float2(0.f, 0.f), b = make_float2(0.f, 0.f);
-    if (row < p.dk && col < p.dv) {
-      a = *reinterpret_cast<const float2*>(p.Hs + sofs + row * p.dv + col);
-      b = *reinterpret_cast<const float2*>(p.dHs + sofs + row * p.dv + col);
-    }
-    uint32_t h, l;
-    tc::split_pack(a.x, a.y, h, l);
-    *reinterpret_cast<uint32_t*>(SH + row * kLd + col) = h;
-    *reinterpret_cast<uint32_t*>(SL + row * kLd + col) = l;
-    tc::split_pack(b.x, b.y, h, l);
-    *reinterpret_cast<uint32_t*>(DH + row * kLd + col) = h;
-    *reinterpret_cast<uint32_t*>(DL + row * kLd + col) = l;
-  }
   cp_async_wait_all();
-  __syncthreads();
+  mbar_wait(bar + 1, 0, &g_sticky_err);
+  const uint32_t tb = *tbase_s;
+  const uint32_t lb = tb + ((uint32_t)(32 * q) << 16) + col0;  // this warp's accumulator window
 
-  // K K^T (warps mat 0) / Q K^T (mat 1): row tile m0, columns 32*hf..
-  {
-    float acc[4][4];
-    tc::zero(acc);
-    const int ncol = mat == 0 ? m0 + 16 : min(64, (m0 + 16) * p.nh);
-    const int np = min(2, max(0, (ncol - 32 * hf + 15) / 16));
-    tc::gemm<4, false, false>(acc, Op{mat == 0 ? K : Q, nullptr}, m0, Op{K, nullptr}, 32 * hf, 0,
-                              kd, np);
-    float* dst = mat == 0 ? KKf : QKf;
-#pragma unroll
-    for (int j = 0; j < 4; ++j)
-#pragma unroll
-      for (int v = 0; v < 4; ++v)
-        dst[tc::frag_row(m0, v) * kTld + tc::frag_col(32 * hf, j, v)] = acc[j][v];
-    if (mat == 1)
-      tc::store_split(acc, PH, PL, m0, 32 * hf, [&](int r, int cl, float x) {
-        return (cl < (r + 1) * p.nh && cl < Mc) ? x * bs[cl] : 0.f;
-      });
-  }
+  unsigned phase = 0;
+  // make this thread's shared-memory writes visible to the tensor cores and
+  // order its TMEM reads before the next batch of MMAs
+  auto to_mma = [&]() {
+    fence_proxy_async_smem();
+    um::fence_before();
+    __syncthreads();
+    um::fence_after();
+  };
+  auto wait_mma = [&]() {
+    mbar_wait(bar, phase, &g_sticky_err);
+    phase ^= 1u;
+    um::fence_after();
+  };
+  auto S_ = [](const bf16* t) { return um::saddr(t); };
+  const um::Opnd oK{S_(K), 0, false}, oKmn{S_(K), 0, true}, oQ{S_(Q), 0, false},
+      oQmn{S_(Q), 0, true}, odY{S_(dY), 0, false}, odYmn{S_(dY), 0, true}, oVmn{S_(V), 0, true};
+  const um::Opnd oS{S_(SH), S_(SL), false}, oSmn{S_(SH), S_(SL), true}, oD{S_(DH), S_(DL), false},
+      oDmn{S_(DH), S_(DL), true}, oTi{S_(TiH), S_(TiL), false}, oTimn{S_(TiH), S_(TiL), true};
 
-  // W = Ti K, U' = Ti V (rows m0, columns n0..n0+15)
-  float u[2][4];
-  {
-    float w[2][4];
-    tc::zero(w);
-    tc::gemm<2, false, true>(w, Op{TiH, TiL}, m0, Op{K, nullptr}, n0, 0, m0 + 16);
-    tc::store_split(w, WH, WL, m0, n0, Ident());
-    tc::zero(u);
-    tc::gemm<2, false, true>(u, Op{TiH, TiL}, m0, Op{V, nullptr}, n0, 0, m0 + 16);
+  // level 1
+  to_mma();
+  if (tid == 0) {
+    um::product(tb + 0, oK, oK, false);
+    um::product(tb + 64, oQ, oK, false);
+    um::product(tb + 128, oTi, oKmn, false);
+    um::product(tb + 192, oTi, oVmn, false);
+    um::product(tb + 256, oK, oDmn, false);
+    um::commit(bar);
   }
-  __syncthreads();
-  // U = U' - W S;  dbU = K dS';  dU = P^T dy + beta dbU;  dbeta += rowsum(U * dbU)
-  {
-    float ws[2][4], db[2][4], du[2][4];
-    tc::zero(ws);
-    tc::zero(db);
-    tc::zero(du);
-    tc::gemm<2, false, true>(ws, Op{WH, WL}, m0, Op{SH, SL}, n0, 0, kd);
-    tc::gemm<2, false, true>(db, Op{K, nullptr}, m0, Op{DH, DL}, n0, 0, kd);
-    tc::gemm<2, true, true>(du, Op{PH, PL}, m0, Op{dY, nullptr}, n0, (m0 / p.nh) & ~15, up16(Cc));
-    float rs[2] = {0.f, 0.f};
+  wait_mma();
+  {  // P = Q K^T beta[col] * read;  -W
+    float v[16];
+    um::ld16(lb + 64, v);
+    if (rv) {
 #pragma unroll
-    for (int j = 0; j < 2; ++j)
-#pragma unroll
-      for (int v = 0; v < 4; ++v) {
-        u[j][v] -= ws[j][v];
-        rs[v >> 1] += u[j][v] * db[j][v];
-        du[j][v] += bs[tc::frag_row(m0, v)] * db[j][v];
+      for (int i = 0; i < 16; ++i) {
+        const int cl = col0 + i;
+        v[i] = (cl < (row + 1) * p.nh && cl < Mc) ? v[i] * bs[cl] : 0.f;
       }
-#pragma unroll
-    for (int h = 0; h < 2; ++h) {
-      rs[h] += __shfl_xor_sync(0xffffffffu, rs[h], 1);
-      rs[h] += __shfl_xor_sync(0xffffffffu, rs[h], 2);
+      um::store_split16(PH, PL, row, col0, v);
     }
-    if ((tid & 3) == 0) {
-      atomicAdd(&dbs[tc::frag_row(m0, 0)], rs[0]);
-      atomicAdd(&dbs[tc::frag_row(m0, 2)], rs[1]);
+    um::ld16(lb + 128, v);
+    if (rv) {
+#pragma unroll
+      for (int i = 0; i < 16; ++i) v[i] = -v[i];
+      um::store_split16(WH, WL, row, col0, v);
     }
-    tc::store_split(u, UH, UL, m0, n0, Ident());
-    tc::store_split(u, BUH, BUL, m0, n0, [&](int r, int, float x) { return x * bs[r]; });
-    tc::store_split(du, dUH, dUL, m0, n0, Ident());
   }
-  __syncthreads();
-  // G = Ti^T dU -> dV; Gn = -G
-  {
-    float g[2][4];
-    tc::zero(g);
-    tc::gemm<2, true, true>(g, Op{TiH, TiL}, m0, Op{dUH, dUL}, n0, m0, 64);
-    frag_to_global_bf16(g, p.dV + (bh * rows + r0) * p.dv, p.dv, m0, n0, Mc, p.dv);
-    tc::store_split(g, GH, GL, m0, n0, [](int, int, float x) { return -x; });
+  // level 2
+  to_mma();
+  if (tid == 0) {
+    um::product(tb + 192, um::Opnd{S_(WH), S_(WL), false}, oSmn, true);
+    um::product(tb + 320, um::Opnd{S_(PH), S_(PL), true}, odYmn, false);
+    um::commit(bar);
   }
-  __syncthreads();
-  // warp (mat, mt, hf): mat 0: dS_ = (dy U^T) beta * read; mat 1: dKK = (Gn U^T) beta * strict
-  {
-    float acc[4][4];
-    tc::zero(acc);
-    const bool m1 = mat != 0;
-    const int ncol = m1 ? min(64, m0 + 16) : min(64, (m0 + 16) * p.nh);
-    const int np = min(2, max(0, (ncol - 32 * hf + 15) / 16));
-    tc::gemm<4, false, false>(acc, m1 ? Op{GH, GL} : Op{dY, nullptr}, m0, Op{UH, UL}, 32 * hf, 0,
-                              kv, np);
-    // masked product, dbeta column terms, split store
-    float cs[4][2];
+  wait_mma();
+  {  // U, beta U, dU = P^T dy + beta dbU; dbeta[row] += sum U * dbU
+    float u[16], db[16], pd[16];
+    um::ld16(lb + 192, u);
+    um::ld16(lb + 256, db);
+    um::ld16(lb + 320, pd);
+    if (rv) {
+      const float b = bs[row];
+      float rs = 0.f;
 #pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      cs[j][0] = cs[j][1] = 0.f;
-#pragma unroll
-      for (int v = 0; v < 4; ++v) {
-        const int row = tc::frag_row(m0, v), col = tc::frag_col(32 * hf, j, v);
-        const bool keep = m1 ? (col < row && col < Mc) : (col < (row + 1) * p.nh && col < Mc);
-        const float x = keep ? acc[j][v] : 0.f;
-        cs[j][v & 1] += x * (m1 ? KKf[row * kTld + col] : QKf[row * kTld + col]);
-        acc[j][v] = x * bs[col];
+      for (int i = 0; i < 16; ++i) {
+        rs += u[i] * db[i];
+        pd[i] += b * db[i];
       }
+      atomicAdd(&dbs[row], rs);
+      um::store_split16(UH, UL, row, col0, u);
+#pragma unroll
+      for (int i = 0; i < 16; ++i) u[i] *= b;
+      um::store_split16(BUH, BUL, row, col0, u);
+      um::store_split16(dUH, dUL, row, col0, pd);
     }
+  }
+  // level 3
+  to_mma();
+  if (tid == 0) {
+    um::product(tb + 128, oTimn, um::Opnd{S_(dUH), S_(dUL), true}, false);
+    um::commit(bar);
+  }
+  wait_mma();
+  {  // dV = G; Gn = -G
+    float g[16];
+    um::ld16(lb + 128, g);
+    if (rv) {
+      if (row < Mc) row16_to_global(p.dV + (bh * rows + r0 + row) * p.dv, col0, p.dv, g);
 #pragma unroll
-    for (int j = 0; j < 4; ++j)
+      for (int i = 0; i < 16; ++i) g[i] = -g[i];
+      um::store_split16(GH, GL, row, col0, g);
+    }
+  }
+  // level 4
+  to_mma();
+  if (tid == 0) {
+    const um::Opnd oU{S_(UH), S_(UL), false};
+    um::product(tb + 320, odY, oU, false);
+    um::product(tb + 256, um::Opnd{S_(GH), S_(GL), false}, oU, false);
+    um::commit(bar);
+  }
+  wait_mma();
+  {  // dS_ = (dy U^T) beta * read; dKK = (Gn U^T) beta * strict; dbeta column terms
+    float ds[16], dk[16], qk[16], kk[16];
+    um::ld16(lb + 320, ds);
+    um::ld16(lb + 256, dk);
+    um::ld16(lb + 64, qk);
+    um::ld16(lb + 0, kk);
 #pragma unroll
-      for (int e = 0; e < 2; ++e) {
-        float x = cs[j][e];
-        x += __shfl_xor_sync(0xffffffffu, x, 4);
-        x += __shfl_xor_sync(0xffffffffu, x, 8);
-        x += __shfl_xor_sync(0xffffffffu, x, 16);
-        if ((tid & 31) < 4) atomicAdd(&dbs[tc::frag_col(32 * hf, j, e)], x);
-      }
-    tc::store_split(acc, m1 ? dKH : dSH, m1 ? dKL : dSL, m0, 32 * hf, Ident());
+    for (int i = 0; i < 16; ++i) {
+      const int cl = col0 + i;
+      const float x = (rv && cl < (row + 1) * p.nh && cl < Mc) ? ds[i] : 0.f;
+      const float y = (rv && cl < row && cl < Mc) ? dk[i] : 0.f;
+      float s = rv ? x * qk[i] + y * kk[i] : 0.f;
+      s += __shfl_xor_sync(0xffffffffu, s, 1);
+      s += __shfl_xor_sync(0xffffffffu, s, 2);
+      s += __shfl_xor_sync(0xffffffffu, s, 4);
+      s += __shfl_xor_sync(0xffffffffu, s, 8);
+      if (lane == 0) atomicAdd(&dbs[cl], s);
+      ds[i] = x * bs[cl];
+      dk[i] = y * bs[cl];
+    }
+    if (rv) {
+      um::store_split16(dSH, dSL, row, col0, ds);
+      um::store_split16(dKH, dKL, row, col0, dk);
+    }
   }
-  __syncthreads();
-  // dQ (token rows m0, d_k columns n0..) = dy S^T + dS_ K
-  {
-    float dq[2][4];
-    tc::zero(dq);
-    tc::gemm<2, false, false>(dq, Op{dY, nullptr}, m0, Op{SH, SL}, n0, 0, kv);
-    tc::gemm<2, false, true>(dq, Op{dSH, dSL}, m0, Op{K, nullptr}, n0, 0,
-                             min(64, up16((m0 + 16) * p.nh)));
-    frag_to_global_bf16(dq, p.dQ + (bh * p.T + t0) * p.dk, p.dk, m0, n0, Cc, p.dk);
+  // level 5
+  to_mma();
+  if (tid == 0) {
+    const um::Opnd odS{S_(dSH), S_(dSL), false}, odSmn{S_(dSH), S_(dSL), true},
+        odK{S_(dKH), S_(dKL), false}, odKmn{S_(dKH), S_(dKL), true};
+    um::product(tb + 0, odY, oS, false);
+    um::product(tb + 0, odS, oKmn, true);
+    um::product(tb + 64, um::Opnd{S_(BUH), S_(BUL), false}, oD, false);
+    um::product(tb + 64, odSmn, oQmn, true);
+    um::product(tb + 64, um::Opnd{S_(GH), S_(GL), false}, oS, true);
+    um::product(tb + 64, odK, oKmn, true);
+    um::product(tb + 64, odKmn, oKmn, true);
+    um::commit(bar);
   }
-  // dK (micro-step rows m0, d_k columns n0..) =
-  //   (beta U) dS'^T + dS_^T Q + Gn S^T + dKK K + dKK^T K
-  {
-    float dk[2][4];
-    tc::zero(dk);
-    tc::gemm<2, false, false>(dk, Op{BUH, BUL}, m0, Op{DH, DL}, n0, 0, kv);
-    tc::gemm<2, true, true>(dk, Op{dSH, dSL}, m0, Op{Q, nullptr}, n0, (m0 / p.nh) & ~15, up16(Cc));
-    tc::gemm<2, false, false>(dk, Op{GH, GL}, m0, Op{SH, SL}, n0, 0, kv);
-    tc::gemm<2, false, true>(dk, Op{dKH, dKL}, m0, Op{K, nullptr}, n0, 0, m0 + 16);
-    tc::gemm<2, true, true>(dk, Op{dKH, dKL}, m0, Op{K, nullptr}, n0, m0, 64);
-    frag_to_global_bf16(dk, p.dK + (bh * rows + r0) * p.dk, p.dk, m0, n0, Mc, p.dk);
+  wait_mma();
+  {  // dQ (token rows), dK (micro-step rows)
+    float v[16];
+    um::ld16(lb + 0, v);
+    if (rv && row < Cc) row16_to_global(p.dQ + (bh * p.T + t0 + row) * p.dk, col0, p.dk, v);
+    um::ld16(lb + 64, v);
+    if (rv && row < Mc) row16_to_global(p.dK + (bh * rows + r0 + row) * p.dk, col0, p.dk, v);
   }
+  um::fence_before();
   __syncthreads();
   if (tid < Mc) p.dbeta[bh * rows + r0 + tid] = __float2bfloat16_rn(dbs[tid]);
+  if (warp == 0) {
+    um::fence_after();
+    um::dealloc(tb, kGradTmemCols);
+  }
 }
 
 // ------------------------------------------------------- forward: prep --
@@ -571,8 +652,8 @@ __global__ void __launch_bounds__(kGradThreads, 2) prep_kernel(const TcArgs p) {
   }
   __syncthreads();
   tri_inv_tc(Td, Op{TH, TL}, TiH, TiL, YH, YL);
-  tile_to_global<NTH>(TiH, p.Ti + blk * kSavedPair);
-  tile_to_global<NTH>(TiL, p.Ti + blk * kSavedPair + kSavedTile);
+  tile_to_global_blocked<NTH>(TiH, p.Ti + blk * kSavedPair);  // read by the tcgen05 grads kernel
+  tile_to_global_blocked<NTH>(TiL, p.Ti + blk * kSavedPair + 4096);
 
   // beta W = diag(beta) Ti K (rows m0, d_k columns n0..), beta U' = diag(beta) Ti V
   {

@@ -1,0 +1,150 @@
+// umma.cuh -- tcgen05 (5th-generation tensor core) building blocks for the
+// 64 x 64 chunk products of the delta rule: blocked shared-memory tiles,
+// matrix descriptors, MMA issue and commit, TMEM allocation and loads.
+//
+// Tile layout ("blocked"): a 64 x 64 bf16 tile is 8 x 8 core matrices of
+// 8 rows x 16 bytes; core matrix (r/8, c/8) sits at byte (r/8)*1024 + (c/8)*128
+// and row r%8 of it at +16*(r%8). The same bytes serve as a K-major operand
+// (contraction over the tile's columns: LBO = 128, SBO = 1024) and as an
+// MN-major operand (contraction over its rows: LBO = 1024, SBO = 128), so a
+// matrix and its transpose are both read from one copy. Products are
+// D[m][n] (+)= sum_k A(m, k) B(n, k) with M = N = 64, K = 64 in four 16-deep
+// MMAs, fp32 accumulators in TMEM: row m of D lives in TMEM lane
+// 32*(m/16) + m%16, column n in column n of the accumulator.
+#pragma once
+
+#include <cuda_bf16.h>
+#include <stdint.h>
+
+namespace mgs {
+namespace umma {
+
+constexpr int kTileBytes = 64 * 64 * 2;  // 8192
+
+// Element offset of (r, c) in a blocked 64-column tile.
+__device__ __forceinline__ int boff(int r, int c) {
+  return (r >> 3) * 512 + (c >> 3) * 64 + (r & 7) * 8 + (c & 7);
+}
+
+__device__ __forceinline__ uint32_t saddr(const void* p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+// Shared-memory matrix descriptor (no swizzle, sm_100 descriptor version 1).
+__device__ __forceinline__ uint64_t desc(uint32_t addr, uint32_t lbo, uint32_t sbo) {
+  return (uint64_t)((addr >> 4) & 0x3FFF) | ((uint64_t)((lbo >> 4) & 0x3FFF) << 16) |
+         ((uint64_t)((sbo >> 4) & 0x3FFF) << 32) | ((uint64_t)1 << 46);
+}
+// 16-deep k-step kk of a tile used K-major / MN-major.
+__device__ __forceinline__ uint64_t desc_k(uint32_t tile, int kk) {
+  return desc(tile + kk * 256, 128, 1024);
+}
+__device__ __forceinline__ uint64_t desc_mn(uint32_t tile, int kk) {
+  return desc(tile + kk * 2048, 1024, 128);
+}
+
+// Instruction descriptor: bf16 x bf16 -> fp32, M = N = 64, operand majors.
+__host__ __device__ constexpr uint32_t idesc64(bool a_mn, bool b_mn) {
+  return (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)a_mn << 15) | ((uint32_t)b_mn << 16) |
+         ((64u >> 3) << 17) | ((64u >> 4) << 24);
+}
+
+__device__ __forceinline__ void mma(uint32_t d, uint64_t a, uint64_t b, uint32_t idesc, bool acc) {
+  asm volatile(
+      "{\n.reg .pred p;\nsetp.ne.b32 p, %4, 0;\n"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, {%5, %6, %7, %8}, p;\n}\n" ::"r"(d),
+      "l"(a), "l"(b), "r"(idesc), "r"((uint32_t)acc), "r"(0), "r"(0), "r"(0), "r"(0)
+      : "memory");
+}
+
+// A split operand tile pair in shared memory: hi, lo (0: exact in bf16), and
+// whether the product contracts over its rows (MN-major) or columns (K-major).
+struct Opnd {
+  uint32_t hi, lo;
+  bool mn;
+};
+
+// D (+)= A B^T over K = 64 with the hi*hi, hi*lo and lo*hi terms (one thread).
+__device__ __forceinline__ void product(uint32_t d, Opnd A, Opnd B, bool accumulate) {
+  const uint32_t id = idesc64(A.mn, B.mn);
+  bool acc = accumulate;
+#pragma unroll
+  for (int kk = 0; kk < 4; ++kk) {
+    const uint64_t ah = A.mn ? desc_mn(A.hi, kk) : desc_k(A.hi, kk);
+    const uint64_t bh = B.mn ? desc_mn(B.hi, kk) : desc_k(B.hi, kk);
+    mma(d, ah, bh, id, acc);
+    acc = true;
+    if (B.lo) mma(d, ah, B.mn ? desc_mn(B.lo, kk) : desc_k(B.lo, kk), id, true);
+    if (A.lo) mma(d, A.mn ? desc_mn(A.lo, kk) : desc_k(A.lo, kk), bh, id, true);
+  }
+}
+
+// Arrive on `bar` once every MMA issued so far by this thread has completed.
+__device__ __forceinline__ void commit(uint64_t* bar) {
+  asm volatile(
+      "tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
+          saddr(bar))
+      : "memory");
+}
+
+__device__ __forceinline__ void fence_before() {
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+}
+__device__ __forceinline__ void fence_after() {
+  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+}
+
+// Warp-collective TMEM allocation of `ncols` columns (a power of two >= 32);
+// the base address is written to shared memory at `dst`.
+__device__ __forceinline__ void alloc(uint32_t* dst, int ncols) {
+  asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(saddr(dst)),
+               "r"(ncols)
+               : "memory");
+  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void dealloc(uint32_t base, int ncols) {
+  asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(base), "r"(ncols)
+               : "memory");
+}
+
+// Warp-collective load of 16 consecutive accumulator columns of this warp's
+// 32-lane quarter (lane i of the warp gets TMEM lane 32*(warp%4) + i).
+__device__ __forceinline__ void ld16(uint32_t taddr, float (&v)[16]) {
+  uint32_t r[16];
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,"
+      "%15}, [%16];\n"
+      "tcgen05.wait::ld.sync.aligned;"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
+        "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]),
+        "=r"(r[14]), "=r"(r[15])
+      : "r"(taddr)
+      : "memory");
+#pragma unroll
+  for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
+}
+
+// Split 16 consecutive values of row r (columns c0..c0+15, c0 % 8 == 0) into
+// bf16 hi / lo and store them into blocked tiles.
+__device__ __forceinline__ void store_split16(__nv_bfloat16* hi, __nv_bfloat16* lo, int r, int c0,
+                                              const float (&v)[16]) {
+#pragma unroll
+  for (int h = 0; h < 2; ++h) {
+    uint32_t ph[4], pl[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const float x0 = v[8 * h + 2 * i], x1 = v[8 * h + 2 * i + 1];
+      __nv_bfloat162 b = __floats2bfloat162_rn(x0, x1);
+      const float2 f = __bfloat1622float2(b);
+      __nv_bfloat162 l = __floats2bfloat162_rn(x0 - f.x, x1 - f.y);
+      ph[i] = *reinterpret_cast<uint32_t*>(&b);
+      pl[i] = *reinterpret_cast<uint32_t*>(&l);
+    }
+    const int o = boff(r, c0 + 8 * h);
+    *reinterpret_cast<uint4*>(hi + o) = make_uint4(ph[0], ph[1], ph[2], ph[3]);
+    if (lo) *reinterpret_cast<uint4*>(lo + o) = make_uint4(pl[0], pl[1], pl[2], pl[3]);
+  }
+}
+
+}  // namespace umma
+}  // namespace mgs
