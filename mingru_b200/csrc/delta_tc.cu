@@ -280,8 +280,10 @@ constexpr int kSerialThreads = 512;  // 16 warps in the chunk-serial kernels
 
 // ----------------------------------------------------- backward: grads --
 // One CTA per (b, h, chunk): every gradient of the chunk from its saved S,
-// T^{-1} and dS', on the tcgen05 tensor cores (umma.cuh). Thread 0 issues each
-// level of products as one batch of 64 x 64 x 64 split MMAs into TMEM; all 16
+// T^{-1} and dS', on the tcgen05 tensor cores (umma.cuh). Two threads (lane 0
+// of warps 0 and 1) issue each level of products, split by accumulator, as
+// batches of 64 x 64 x 64 split MMAs into TMEM and commit to one barrier of
+// arrival count 2 (MMA issue, not the tensor pipe, bounds these shapes); all 16
 // warps then read the accumulators (warp w: rows 16*(w%4).., columns 16*(w/4)..)
 // and write the masked / scaled / split operands of the next level:
 //   1. K K^T, Q K^T, W = Ti K, U' = Ti V, dbU = K dS'
@@ -289,12 +291,14 @@ constexpr int kSerialThreads = 512;  // 16 warps in the chunk-serial kernels
 //   3. G = Ti^T dU (-> dV)                                 [dU = P^T dy + beta dbU]
 //   4. dy U^T, Gn U^T (Gn = -G)                            [-> dS_, dKK, dbeta columns]
 //   5. dQ = dy S^T + dS_ K;  dK = (beta U) dS'^T + dS_^T Q + Gn S^T + dKK K + dKK^T K
-// TMEM columns: KK 0, QK 64, W -> G 128, U 192, dbU -> dKK 256, P^T dy -> dy U^T 320;
-// dQ reuses 0 and dK 64 once KK and QK have been read.
+// TMEM columns: KK 0, QK 64, W -> G 128 (+ 384), U 192, dbU -> dKK 256, P^T dy -> dy U^T 320;
+// level 5 reuses 0 (dQ) and 64, 128, 192 (three partial sums of dK). Each level's
+// products are issued interleaved by k-step (umma::products) so that
+// consecutive MMAs accumulate into different TMEM columns.
 // smem (blocked 8 KB tiles): K | Q | dY | V | S h/l | dS' h/l | Ti h/l | P h/l (-> Gn) |
 //   -W h/l (-> dS_) | U h/l | bU h/l | dU h/l (-> dKK) | beta, dbeta
 constexpr int kGradThreads = 512;
-constexpr size_t kGradSmem = 1024 + 20 * (size_t)umma::kTileBytes + 512;
+constexpr size_t kGradSmem = 1024 + 20 * (size_t)umma::kTileBytes + 3072;
 constexpr int kGradTmemCols = 512;
 
 // 64 rows x (8 * valid_ch) columns of a row-major global bf16 matrix into a
@@ -333,10 +337,10 @@ __device__ __forceinline__ void row16_to_global(bf16* g, int c0, int ncols, cons
 
 __global__ void __launch_bounds__(kGradThreads, 1) bwd_grads_kernel(const TcArgs p) {
   namespace um = umma;
-  extern __shared__ __align__(1024) unsigned char smem[];
-  uint64_t* bar = reinterpret_cast<uint64_t*>(smem);  // [0] MMA batches, [1] T^{-1} copy
-  uint32_t* tbase_s = reinterpret_cast<uint32_t*>(smem + 64);
-  bf16* tiles = reinterpret_cast<bf16*>(smem + 1024);
+  extern __shared__ __align__(1024) unsigned char gsmem[];
+  uint64_t* bar = reinterpret_cast<uint64_t*>(gsmem);  // [0] MMA batches, [1] T^{-1} copy
+  uint32_t* tbase_s = reinterpret_cast<uint32_t*>(gsmem + 64);
+  bf16* tiles = reinterpret_cast<bf16*>(gsmem + 1024);
   auto T = [&](int i) { return tiles + i * (um::kTileBytes / 2); };
   bf16 *K = T(0), *Q = T(1), *dY = T(2), *V = T(3), *SH = T(4), *SL = T(5), *DH = T(6),
        *DL = T(7), *TiH = T(8), *TiL = T(9), *PH = T(10), *PL = T(11), *WH = T(12), *WL = T(13),
@@ -344,6 +348,8 @@ __global__ void __launch_bounds__(kGradThreads, 1) bwd_grads_kernel(const TcArgs
   bf16 *GH = PH, *GL = PL, *dSH = WH, *dSL = WL, *dKH = dUH, *dKL = dUL;
   float* bs = reinterpret_cast<float*>(T(20));
   float* dbs = bs + 64;
+  float* rpart = dbs + 64;    // [4 column quarters][64 rows]: sum_col U * dbU
+  float* cpart = rpart + 256;  // [16 warps][16 columns]: masked-product column sums
 
   constexpr int NTH = kGradThreads;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -359,7 +365,7 @@ __global__ void __launch_bounds__(kGradThreads, 1) bwd_grads_kernel(const TcArgs
 
   if (warp == 0) um::alloc(tbase_s, kGradTmemCols);
   if (tid == 0) {
-    mbar_init(bar, 1);
+    mbar_init(bar, 2);  // MMA batches: one commit from each issuing thread
     mbar_init(bar + 1, 1);
     mbar_fence_init();
   }
@@ -370,25 +376,34 @@ __global__ void __launch_bounds__(kGradThreads, 1) bwd_grads_kernel(const TcArgs
   cp_async_commit();
   um::fence_before();
   __syncthreads();  // barriers initialised, TMEM base written
+  // S (chunk-start state) and dS' (fp32 [dk][dv]) arrive by bulk copies in a
+  // staging area over tiles 10-17 (first written after level 1).
+  float* stS = reinterpret_cast<float*>(T(10));
+  float* stD = stS + 64 * 64;
+  const unsigned sbytes = (unsigned)(p.dk * p.dv * 4);
   if (tid == 0) {
-    mbar_arrive_expect_tx(bar + 1, 2 * um::kTileBytes);
+    mbar_arrive_expect_tx(bar + 1, 2 * um::kTileBytes + 2 * sbytes);
     bulk_g2s(TiH, p.Ti + blk * kSavedPair, um::kTileBytes, bar + 1);
     bulk_g2s(TiL, p.Ti + blk * kSavedPair + 4096, um::kTileBytes, bar + 1);
+    bulk_g2s(stS, p.Hs + sofs, sbytes, bar + 1);
+    bulk_g2s(stD, p.dHs + sofs, sbytes, bar + 1);
   }
-  // S (chunk-start state) and dS' (fp32 [dk][dv]) -> split blocked tiles
+  if (tid < 64) bs[tid] = tid < Mc ? __bfloat162float(p.beta[bh * rows + r0 + tid]) : 0.f;
+  cp_async_wait_all();
+  mbar_wait(bar + 1, 0, &g_sticky_err);
+  // S, dS' -> split blocked tiles
   for (int i = tid; i < 64 * 8; i += NTH) {
     const int r = i >> 3, cb = i & 7;
-    float a[16], b[16];
+    float a[8], b[8];
 #pragma unroll
-    for (int j = 0; j < 16; ++j) a[j] = b[j] = 0.f;
+    for (int j = 0; j < 8; ++j) a[j] = b[j] = 0.f;
     if (r < p.dk && cb * 8 < p.dv) {
-      const float4* sa = reinterpret_cast<const float4*>(p.Hs + sofs + r * p.dv + cb * 8);
-      const float4* sb = reinterpret_cast<const float4*>(p.dHs + sofs + r * p.dv + cb * 8);
+      const float4* sa = reinterpret_cast<const float4*>(stS + r * p.dv + cb * 8);
+      const float4* sb = reinterpret_cast<const float4*>(stD + r * p.dv + cb * 8);
       const float4 a0 = sa[0], a1 = sa[1], b0 = sb[0], b1 = sb[1];
       a[0] = a0.x; a[1] = a0.y; a[2] = a0.z; a[3] = a0.w; a[4] = a1.x; a[5] = a1.y; a[6] = a1.z; a[7] = a1.w;
       b[0] = b0.x; b[1] = b0.y; b[2] = b0.z; b[3] = b0.w; b[4] = b1.x; b[5] = b1.y; b[6] = b1.z; b[7] = b1.w;
     }
-    // store_split16 writes two 8-column chunks: write this chunk and leave the next untouched
     uint32_t ph[4], pl[4], qh[4], ql[4];
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
@@ -401,12 +416,6 @@ __global__ void __launch_bounds__(kGradThreads, 1) bwd_grads_kernel(const TcArgs
     *reinterpret_cast<uint4*>(DH + o) = make_uint4(qh[0], qh[1], qh[2], qh[3]);
     *reinterpret_cast<uint4*>(DL + o) = make_uint4(ql[0], ql[1], ql[2], ql[3]);
   }
-  if (tid < 64) {
-    bs[tid] = tid < Mc ? __bfloat162float(p.beta[bh * rows + r0 + tid]) : 0.f;
-    dbs[tid] = 0.f;
-  }
-  cp_async_wait_all();
-  mbar_wait(bar + 1, 0, &g_sticky_err);
   const uint32_t tb = *tbase_s;
   const uint32_t lb = tb + ((uint32_t)(32 * q) << 16) + col0;  // this warp's accumulator window
 
@@ -425,19 +434,24 @@ __global__ void __launch_bounds__(kGradThreads, 1) bwd_grads_kernel(const TcArgs
     um::fence_after();
   };
   auto S_ = [](const bf16* t) { return um::saddr(t); };
-  const um::Opnd oK{S_(K), 0, false}, oKmn{S_(K), 0, true}, oQ{S_(Q), 0, false},
-      oQmn{S_(Q), 0, true}, odY{S_(dY), 0, false}, odYmn{S_(dY), 0, true}, oVmn{S_(V), 0, true};
-  const um::Opnd oS{S_(SH), S_(SL), false}, oSmn{S_(SH), S_(SL), true}, oD{S_(DH), S_(DL), false},
-      oDmn{S_(DH), S_(DL), true}, oTi{S_(TiH), S_(TiL), false}, oTimn{S_(TiH), S_(TiL), true};
+  const um::Opnd oK = um::opnd(S_(K), 0, false), oKmn = um::opnd(S_(K), 0, true),
+                 oQ = um::opnd(S_(Q), 0, false), oQmn = um::opnd(S_(Q), 0, true),
+                 odY = um::opnd(S_(dY), 0, false), odYmn = um::opnd(S_(dY), 0, true),
+                 oVmn = um::opnd(S_(V), 0, true);
+  const um::Opnd oS = um::opnd(S_(SH), S_(SL), false), oSmn = um::opnd(S_(SH), S_(SL), true),
+                 oD = um::opnd(S_(DH), S_(DL), false), oDmn = um::opnd(S_(DH), S_(DL), true),
+                 oTi = um::opnd(S_(TiH), S_(TiL), false), oTimn = um::opnd(S_(TiH), S_(TiL), true);
 
   // level 1
   to_mma();
   if (tid == 0) {
-    um::product(tb + 0, oK, oK, false);
-    um::product(tb + 64, oQ, oK, false);
-    um::product(tb + 128, oTi, oKmn, false);
-    um::product(tb + 192, oTi, oVmn, false);
-    um::product(tb + 256, oK, oDmn, false);
+    const um::Prod ps[3] = {{tb + 128, oTi, oKmn, false}, {tb + 192, oTi, oVmn, false},
+                            {tb + 0, oK, oK, false}};
+    um::products(ps);
+    um::commit(bar);
+  } else if (tid == 32) {
+    const um::Prod ps[2] = {{tb + 256, oK, oDmn, false}, {tb + 64, oQ, oK, false}};
+    um::products(ps);
     um::commit(bar);
   }
   wait_mma();
@@ -462,16 +476,25 @@ __global__ void __launch_bounds__(kGradThreads, 1) bwd_grads_kernel(const TcArgs
   // level 2
   to_mma();
   if (tid == 0) {
-    um::product(tb + 192, um::Opnd{S_(WH), S_(WL), false}, oSmn, true);
-    um::product(tb + 320, um::Opnd{S_(PH), S_(PL), true}, odYmn, false);
+    const um::Prod ps[1] = {{tb + 192, um::opnd(S_(WH), S_(WL), false), oSmn, true}};
+    um::products(ps);
+    um::commit(bar);
+  } else if (tid == 32) {
+    const um::Prod ps[1] = {{tb + 320, um::opnd(S_(PH), S_(PL), true), odYmn, false}};
+    um::products(ps);
     um::commit(bar);
   }
   wait_mma();
   {  // U, beta U, dU = P^T dy + beta dbU; dbeta[row] += sum U * dbU
     float u[16], db[16], pd[16];
-    um::ld16(lb + 192, u);
-    um::ld16(lb + 256, db);
-    um::ld16(lb + 320, pd);
+    uint32_t ru[16], rd[16], rp[16];
+    um::ld16_async(lb + 192, ru);
+    um::ld16_async(lb + 256, rd);
+    um::ld16_async(lb + 320, rp);
+    um::ld_wait();
+    um::ld_bind(ru, u);
+    um::ld_bind(rd, db);
+    um::ld_bind(rp, pd);
     if (rv) {
       const float b = bs[row];
       float rs = 0.f;
@@ -480,7 +503,7 @@ __global__ void __launch_bounds__(kGradThreads, 1) bwd_grads_kernel(const TcArgs
         rs += u[i] * db[i];
         pd[i] += b * db[i];
       }
-      atomicAdd(&dbs[row], rs);
+      rpart[(warp >> 2) * 64 + row] = rs;
       um::store_split16(UH, UL, row, col0, u);
 #pragma unroll
       for (int i = 0; i < 16; ++i) u[i] *= b;
@@ -490,14 +513,22 @@ __global__ void __launch_bounds__(kGradThreads, 1) bwd_grads_kernel(const TcArgs
   }
   // level 3
   to_mma();
-  if (tid == 0) {
-    um::product(tb + 128, oTimn, um::Opnd{S_(dUH), S_(dUL), true}, false);
+  if (tid == 0) {  // G = Ti^T dU as (Ti^T dU_hi) + (Ti_hi^T dU_lo) in two accumulators
+    const um::Prod ps[1] = {{tb + 128, oTimn, um::opnd(S_(dUH), 0, true), false}};
+    um::products(ps);
+    um::commit(bar);
+  } else if (tid == 32) {
+    const um::Prod ps[1] = {{tb + 384, um::opnd(S_(TiH), 0, true), um::opnd(S_(dUL), 0, true), false}};
+    um::products(ps);
     um::commit(bar);
   }
   wait_mma();
   {  // dV = G; Gn = -G
-    float g[16];
+    float g[16], g2[16];
     um::ld16(lb + 128, g);
+    um::ld16(lb + 384, g2);
+#pragma unroll
+    for (int i = 0; i < 16; ++i) g[i] += g2[i];
     if (rv) {
       if (row < Mc) row16_to_global(p.dV + (bh * rows + r0 + row) * p.dv, col0, p.dv, g);
 #pragma unroll
@@ -508,18 +539,28 @@ __global__ void __launch_bounds__(kGradThreads, 1) bwd_grads_kernel(const TcArgs
   // level 4
   to_mma();
   if (tid == 0) {
-    const um::Opnd oU{S_(UH), S_(UL), false};
-    um::product(tb + 320, odY, oU, false);
-    um::product(tb + 256, um::Opnd{S_(GH), S_(GL), false}, oU, false);
+    const um::Prod ps[1] = {{tb + 256, um::opnd(S_(GH), S_(GL), false), um::opnd(S_(UH), S_(UL), false), false}};
+    um::products(ps);
+    um::commit(bar);
+  } else if (tid == 32) {
+    const um::Prod ps[1] = {{tb + 320, odY, um::opnd(S_(UH), S_(UL), false), false}};
+    um::products(ps);
     um::commit(bar);
   }
   wait_mma();
   {  // dS_ = (dy U^T) beta * read; dKK = (Gn U^T) beta * strict; dbeta column terms
     float ds[16], dk[16], qk[16], kk[16];
-    um::ld16(lb + 320, ds);
-    um::ld16(lb + 256, dk);
-    um::ld16(lb + 64, qk);
-    um::ld16(lb + 0, kk);
+    uint32_t r1[16], r2[16], r3[16], r4[16];
+    um::ld16_async(lb + 320, r1);
+    um::ld16_async(lb + 256, r2);
+    um::ld16_async(lb + 64, r3);
+    um::ld16_async(lb + 0, r4);
+    um::ld_wait();
+    um::ld_bind(r1, ds);
+    um::ld_bind(r2, dk);
+    um::ld_bind(r3, qk);
+    um::ld_bind(r4, kk);
+    float cs = 0.f;  // after the reduction lane i < 16 holds column col0 + i
 #pragma unroll
     for (int i = 0; i < 16; ++i) {
       const int cl = col0 + i;
@@ -530,10 +571,11 @@ __global__ void __launch_bounds__(kGradThreads, 1) bwd_grads_kernel(const TcArgs
       s += __shfl_xor_sync(0xffffffffu, s, 2);
       s += __shfl_xor_sync(0xffffffffu, s, 4);
       s += __shfl_xor_sync(0xffffffffu, s, 8);
-      if (lane == 0) atomicAdd(&dbs[cl], s);
+      if (lane == i) cs = s;
       ds[i] = x * bs[cl];
       dk[i] = y * bs[cl];
     }
+    if (lane < 16) cpart[warp * 16 + lane] = cs;
     if (rv) {
       um::store_split16(dSH, dSL, row, col0, ds);
       um::store_split16(dKH, dKL, row, col0, dk);
@@ -541,29 +583,48 @@ __global__ void __launch_bounds__(kGradThreads, 1) bwd_grads_kernel(const TcArgs
   }
   // level 5
   to_mma();
-  if (tid == 0) {
-    const um::Opnd odS{S_(dSH), S_(dSL), false}, odSmn{S_(dSH), S_(dSL), true},
-        odK{S_(dKH), S_(dKL), false}, odKmn{S_(dKH), S_(dKL), true};
-    um::product(tb + 0, odY, oS, false);
-    um::product(tb + 0, odS, oKmn, true);
-    um::product(tb + 64, um::Opnd{S_(BUH), S_(BUL), false}, oD, false);
-    um::product(tb + 64, odSmn, oQmn, true);
-    um::product(tb + 64, um::Opnd{S_(GH), S_(GL), false}, oS, true);
-    um::product(tb + 64, odK, oKmn, true);
-    um::product(tb + 64, odKmn, oKmn, true);
+  if (tid == 0) {  // dK partial sums in columns 64 and 192
+    const um::Opnd odKmn = um::opnd(S_(dKH), S_(dKL), true);
+    const um::Prod ps[3] = {{tb + 64, um::opnd(S_(BUH), S_(BUL), false), oD, false},
+                            {tb + 192, odKmn, oKmn, false},
+                            {tb + 64, um::opnd(S_(GH), S_(GL), false), oS, true}};
+    um::products(ps);
+    um::commit(bar);
+  } else if (tid == 32) {  // dQ in columns 0, dK partial sum in columns 128
+    const um::Opnd odS = um::opnd(S_(dSH), S_(dSL), false), odSmn = um::opnd(S_(dSH), S_(dSL), true),
+                   odK = um::opnd(S_(dKH), S_(dKL), false);
+    const um::Prod ps[4] = {{tb + 0, odY, oS, false}, {tb + 128, odSmn, oQmn, false},
+                            {tb + 0, odS, oKmn, true}, {tb + 128, odK, oKmn, true}};
+    um::products(ps);
     um::commit(bar);
   }
   wait_mma();
   {  // dQ (token rows), dK (micro-step rows)
-    float v[16];
-    um::ld16(lb + 0, v);
+    float v[16], v1[16], v2[16], v3[16];
+    uint32_t r0_[16], r1[16], r2[16], r3[16];
+    um::ld16_async(lb + 0, r0_);
+    um::ld16_async(lb + 64, r1);
+    um::ld16_async(lb + 128, r2);
+    um::ld16_async(lb + 192, r3);
+    um::ld_wait();
+    um::ld_bind(r0_, v);
+    um::ld_bind(r1, v1);
+    um::ld_bind(r2, v2);
+    um::ld_bind(r3, v3);
     if (rv && row < Cc) row16_to_global(p.dQ + (bh * p.T + t0 + row) * p.dk, col0, p.dk, v);
-    um::ld16(lb + 64, v);
-    if (rv && row < Mc) row16_to_global(p.dK + (bh * rows + r0 + row) * p.dk, col0, p.dk, v);
+#pragma unroll
+    for (int i = 0; i < 16; ++i) v1[i] += v2[i] + v3[i];
+    if (rv && row < Mc) row16_to_global(p.dK + (bh * rows + r0 + row) * p.dk, col0, p.dk, v1);
   }
   um::fence_before();
   __syncthreads();
-  if (tid < Mc) p.dbeta[bh * rows + r0 + tid] = __float2bfloat16_rn(dbs[tid]);
+  if (tid < Mc) {  // dbeta = row sums of U * dbU + column sums of the masked products
+    const int g4 = (tid >> 4) * 4, cl = tid & 15;
+    const float d = (rpart[tid] + rpart[64 + tid]) + (rpart[128 + tid] + rpart[192 + tid]) +
+                    (cpart[g4 * 16 + cl] + cpart[(g4 + 1) * 16 + cl]) +
+                    (cpart[(g4 + 2) * 16 + cl] + cpart[(g4 + 3) * 16 + cl]);
+    p.dbeta[bh * rows + r0 + tid] = __float2bfloat16_rn(d);
+  }
   if (warp == 0) {
     um::fence_after();
     um::dealloc(tb, kGradTmemCols);

@@ -57,26 +57,52 @@ __device__ __forceinline__ void mma(uint32_t d, uint64_t a, uint64_t b, uint32_t
       : "memory");
 }
 
-// A split operand tile pair in shared memory: hi, lo (0: exact in bf16), and
-// whether the product contracts over its rows (MN-major) or columns (K-major).
+// A split operand tile pair in shared memory, as matrix descriptors of its
+// first k-step: hi, lo (lo == 0: exact in bf16), the per-k-step descriptor
+// increment (256 B K-major, 2048 B MN-major, in 16-byte units) and whether the
+// product contracts over the tile's rows (MN-major) or columns (K-major).
 struct Opnd {
-  uint32_t hi, lo;
+  uint64_t hi, lo;
+  uint32_t step;
   bool mn;
 };
 
-// D (+)= A B^T over K = 64 with the hi*hi, hi*lo and lo*hi terms (one thread).
-__device__ __forceinline__ void product(uint32_t d, Opnd A, Opnd B, bool accumulate) {
-  const uint32_t id = idesc64(A.mn, B.mn);
-  bool acc = accumulate;
+// Operand from tile addresses (lo_addr == 0: no lo term).
+__device__ __forceinline__ Opnd opnd(uint32_t hi_addr, uint32_t lo_addr, bool mn) {
+  Opnd o;
+  o.mn = mn;
+  o.step = mn ? 2048 / 16 : 256 / 16;
+  o.hi = mn ? desc(hi_addr, 1024, 128) : desc(hi_addr, 128, 1024);
+  o.lo = lo_addr == 0 ? 0 : (mn ? desc(lo_addr, 1024, 128) : desc(lo_addr, 128, 1024));
+  return o;
+}
+
+// One product of a batch: D (+)= A B^T over K = 64 with the hi*hi, hi*lo and
+// lo*hi terms.
+struct Prod {
+  uint32_t d;
+  Opnd A, B;
+  bool accumulate;
+};
+
+// Issue a batch of independent products (one thread) k-step by k-step,
+// round-robin over the products, so that consecutive MMAs go to different
+// accumulators. Descriptors only advance by a constant per k-step, which keeps
+// the issuing thread's instruction count per MMA small (issue, not the tensor
+// pipe, bounds 64 x 64 x 16 MMAs).
+template <int N>
+__device__ __forceinline__ void products(const Prod (&ps)[N]) {
 #pragma unroll
-  for (int kk = 0; kk < 4; ++kk) {
-    const uint64_t ah = A.mn ? desc_mn(A.hi, kk) : desc_k(A.hi, kk);
-    const uint64_t bh = B.mn ? desc_mn(B.hi, kk) : desc_k(B.hi, kk);
-    mma(d, ah, bh, id, acc);
-    acc = true;
-    if (B.lo) mma(d, ah, B.mn ? desc_mn(B.lo, kk) : desc_k(B.lo, kk), id, true);
-    if (A.lo) mma(d, A.mn ? desc_mn(A.lo, kk) : desc_k(A.lo, kk), bh, id, true);
-  }
+  for (int kk = 0; kk < 4; ++kk)
+#pragma unroll
+    for (int i = 0; i < N; ++i) {
+      const Prod& p = ps[i];
+      const uint32_t id = idesc64(p.A.mn, p.B.mn);
+      const uint64_t oa = (uint64_t)(kk * p.A.step), ob = (uint64_t)(kk * p.B.step);
+      mma(p.d, p.A.hi + oa, p.B.hi + ob, id, kk > 0 || p.accumulate);
+      if (p.B.lo) mma(p.d, p.A.hi + oa, p.B.lo + ob, id, true);
+      if (p.A.lo) mma(p.d, p.A.lo + oa, p.B.hi + ob, id, true);
+    }
 }
 
 // Arrive on `bar` once every MMA issued so far by this thread has completed.
@@ -120,6 +146,34 @@ __device__ __forceinline__ void ld16(uint32_t taddr, float (&v)[16]) {
         "=r"(r[14]), "=r"(r[15])
       : "r"(taddr)
       : "memory");
+#pragma unroll
+  for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
+}
+
+// As ld16 without the wait: the registers are valid only after ld_wait()
+// has been passed the same arrays (several loads share one wait).
+__device__ __forceinline__ void ld16_async(uint32_t taddr, uint32_t (&r)[16]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,"
+      "%15}, [%16];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
+        "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]),
+        "=r"(r[14]), "=r"(r[15])
+      : "r"(taddr)
+      : "memory");
+}
+// Wait for this thread's outstanding TMEM loads; the empty asm statements that
+// follow tie the loaded registers to the wait so no use moves above it.
+__device__ __forceinline__ void ld_wait() {
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void ld_bind(uint32_t (&r)[16], float (&v)[16]) {
+  asm volatile(""
+               : "+r"(r[0]), "+r"(r[1]), "+r"(r[2]), "+r"(r[3]), "+r"(r[4]), "+r"(r[5]),
+                 "+r"(r[6]), "+r"(r[7]), "+r"(r[8]), "+r"(r[9]), "+r"(r[10]), "+r"(r[11]),
+                 "+r"(r[12]), "+r"(r[13]), "+r"(r[14]), "+r"(r[15])
+               :
+               : "memory");
 #pragma unroll
   for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
 }
