@@ -279,27 +279,27 @@ struct TcArgs {
 constexpr int kSerialThreads = 512;  // 16 warps in the chunk-serial kernels
 
 // ----------------------------------------------------- backward: grads --
-// One CTA per (b, h, chunk): every gradient of the chunk from its saved S,
-// T^{-1} and dS', on the tcgen05 tensor cores (umma.cuh). Two threads (lane 0
-// of warps 0 and 1) issue each level of products, split by accumulator, as
-// batches of 64 x 64 x 64 split MMAs into TMEM and commit to one barrier of
-// arrival count 2 (MMA issue, not the tensor pipe, bounds these shapes); all 16
-// warps then read the accumulators (warp w: rows 16*(w%4).., columns 16*(w/4)..)
-// and write the masked / scaled / split operands of the next level:
-//   1. K K^T, Q K^T, W = Ti K, U' = Ti V, dbU = K dS'
-//   2. U = U' + (-W) S (same accumulator), P^T dy          [P = Q K^T beta * read]
-//   3. G = Ti^T dU (-> dV)                                 [dU = P^T dy + beta dbU]
-//   4. dy U^T, Gn U^T (Gn = -G)                            [-> dS_, dKK, dbeta columns]
-//   5. dQ = dy S^T + dS_ K;  dK = (beta U) dS'^T + dS_^T Q + Gn S^T + dKK K + dKK^T K
-// TMEM columns: KK 0, QK 64, W -> G 128 (+ 384), U 192, dbU -> dKK 256, P^T dy -> dy U^T 320;
-// level 5 reuses 0 (dQ) and 64, 128, 192 (three partial sums of dK). Each level's
-// products are issued interleaved by k-step (umma::products) so that
-// consecutive MMAs accumulate into different TMEM columns.
-// smem (blocked 8 KB tiles): K | Q | dY | V | S h/l | dS' h/l | Ti h/l | P h/l (-> Gn) |
-//   -W h/l (-> dS_) | U h/l | bU h/l | dU h/l (-> dKK) | beta, dbeta
-constexpr int kGradThreads = 512;
-constexpr size_t kGradSmem = 1024 + 20 * (size_t)umma::kTileBytes + 3072;
-constexpr int kGradTmemCols = 512;
+// One CTA per (b, h, chunk), two CTAs per SM: every gradient of the chunk from
+// its saved S, T^{-1} and dS', on the tcgen05 tensor cores (umma.cuh). Two
+// threads (lane 0 of warps 0 and 1) issue each level of products, split by
+// accumulator, as batches of 64 x 64 x 64 split MMAs into TMEM and commit to
+// one barrier of arrival count 2 (MMA issue, not the tensor pipe, bounds these
+// shapes, so the second CTA on the SM fills the gaps); all 8 warps then read
+// the accumulators (warp w: rows 16*(w%4).., columns 32*(w/4)..) and write the
+// masked / scaled / split operands of the next level:
+//   1. W = Ti K, U' = Ti V, dbU = K dS', Q K^T            [P = Q K^T beta * read]
+//   2. U = U' + (-W) S (same accumulator), P^T dy         [dU = P^T dy + beta dbU]
+//   3. G = Ti^T dU (two accumulators, -> dV), U dS'^T (held in registers)
+//   4. dy U^T, Gn U^T (Gn = -G), K K^T, Q K^T             [-> dS_, dKK, dbeta columns]
+//   5. dQ = dy S^T + dS_ K;  dK = beta * (U dS'^T) + dS_^T Q + dKK K + Gn S^T + dKK^T K
+// TMEM: four 64-column accumulators A, B, C, D (256 columns per CTA), each
+// reused once its previous contents have been read.
+// Shared tiles (blocked, 8 KB): 0 K | 1 Q | 2 dY | 3, 4 S | 5, 6 dS' -> dKK |
+//   7, 8 Ti -> Gn | 9 V -> -W hi -> U hi | 10, 11 P -> dU -> dS_ | 12 -W lo -> U lo
+constexpr int kGradThreads = 256;
+constexpr int kGradTiles = 13;
+constexpr size_t kGradSmem = 1024 + kGradTiles * (size_t)umma::kTileBytes + 2048;
+constexpr int kGradTmemCols = 256;
 
 // 64 rows x (8 * valid_ch) columns of a row-major global bf16 matrix into a
 // blocked tile (cp.async); rows >= nrows and chunks >= valid_ch are zero.
@@ -323,7 +323,7 @@ __device__ __forceinline__ void tile_to_global_blocked(const bf16* t, bf16* g) {
   }
 }
 
-// Row r, columns c0..c0+15 of an accumulator row -> bf16 global row (columns < ncols).
+// Columns c0..c0+15 of an accumulator row -> bf16 global row (columns < ncols).
 __device__ __forceinline__ void row16_to_global(bf16* g, int c0, int ncols, const float (&v)[16]) {
 #pragma unroll
   for (int h = 0; h < 2; ++h)
@@ -335,25 +335,25 @@ __device__ __forceinline__ void row16_to_global(bf16* g, int c0, int ncols, cons
     }
 }
 
-__global__ void __launch_bounds__(kGradThreads, 1) bwd_grads_kernel(const TcArgs p) {
+__global__ void __launch_bounds__(kGradThreads, 2) bwd_grads_kernel(const TcArgs p) {
   namespace um = umma;
   extern __shared__ __align__(1024) unsigned char gsmem[];
   uint64_t* bar = reinterpret_cast<uint64_t*>(gsmem);  // [0] MMA batches, [1] T^{-1} copy
   uint32_t* tbase_s = reinterpret_cast<uint32_t*>(gsmem + 64);
   bf16* tiles = reinterpret_cast<bf16*>(gsmem + 1024);
   auto T = [&](int i) { return tiles + i * (um::kTileBytes / 2); };
-  bf16 *K = T(0), *Q = T(1), *dY = T(2), *V = T(3), *SH = T(4), *SL = T(5), *DH = T(6),
-       *DL = T(7), *TiH = T(8), *TiL = T(9), *PH = T(10), *PL = T(11), *WH = T(12), *WL = T(13),
-       *UH = T(14), *UL = T(15), *BUH = T(16), *BUL = T(17), *dUH = T(18), *dUL = T(19);
-  bf16 *GH = PH, *GL = PL, *dSH = WH, *dSL = WL, *dKH = dUH, *dKL = dUL;
-  float* bs = reinterpret_cast<float*>(T(20));
-  float* dbs = bs + 64;
-  float* rpart = dbs + 64;    // [4 column quarters][64 rows]: sum_col U * dbU
-  float* cpart = rpart + 256;  // [16 warps][16 columns]: masked-product column sums
+  bf16 *K = T(0), *Q = T(1), *dY = T(2), *SH = T(3), *SL = T(4), *DH = T(5), *DL = T(6),
+       *TiH = T(7), *TiL = T(8), *V = T(9);
+  bf16 *dKH = T(5), *dKL = T(6), *GH = T(7), *GL = T(8), *WH = T(9), *WL = T(12), *UH = T(9),
+       *UL = T(12), *PH = T(10), *PL = T(11), *dUH = T(10), *dUL = T(11), *dSH = T(10),
+       *dSL = T(11);
+  float* bs = reinterpret_cast<float*>(T(kGradTiles));
+  float* rpart = bs + 64;      // [2 column halves][64 rows]: sum_col U * dbU
+  float* cpart = rpart + 128;  // [8 warps][32 columns]: masked-product column sums
 
   constexpr int NTH = kGradThreads;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int q = warp & 3, col0 = 16 * (warp >> 2), row = 16 * q + lane;
+  const int q = warp & 3, hh = warp >> 2, row = 16 * q + lane;
   const bool rv = lane < 16;  // this lane holds row `row` of the 64-row accumulators
   const int c = blockIdx.x % p.nchunks;
   const long long bh = blockIdx.x / p.nchunks;
@@ -376,48 +376,51 @@ __global__ void __launch_bounds__(kGradThreads, 1) bwd_grads_kernel(const TcArgs
   cp_async_commit();
   um::fence_before();
   __syncthreads();  // barriers initialised, TMEM base written
-  // S (chunk-start state) and dS' (fp32 [dk][dv]) arrive by bulk copies in a
-  // staging area over tiles 10-17 (first written after level 1).
-  float* stS = reinterpret_cast<float*>(T(10));
-  float* stD = stS + 64 * 64;
-  const unsigned sbytes = (unsigned)(p.dk * p.dv * 4);
   if (tid == 0) {
-    mbar_arrive_expect_tx(bar + 1, 2 * um::kTileBytes + 2 * sbytes);
+    mbar_arrive_expect_tx(bar + 1, 2 * um::kTileBytes);
     bulk_g2s(TiH, p.Ti + blk * kSavedPair, um::kTileBytes, bar + 1);
     bulk_g2s(TiL, p.Ti + blk * kSavedPair + 4096, um::kTileBytes, bar + 1);
-    bulk_g2s(stS, p.Hs + sofs, sbytes, bar + 1);
-    bulk_g2s(stD, p.dHs + sofs, sbytes, bar + 1);
+  }
+  {  // S (chunk-start state) and dS' (fp32 [dk][dv]) -> split blocked tiles
+    float4 a[2][2], b[2][2];
+#pragma unroll
+    for (int k = 0; k < 2; ++k) {
+      const int i = tid + k * NTH, r = i >> 3, cb = i & 7;
+      const bool ok = r < p.dk && cb * 8 < p.dv;
+      const float4 z = make_float4(0.f, 0.f, 0.f, 0.f);
+      const float4* sa = reinterpret_cast<const float4*>(p.Hs + sofs + r * p.dv + cb * 8);
+      const float4* sb = reinterpret_cast<const float4*>(p.dHs + sofs + r * p.dv + cb * 8);
+      a[k][0] = ok ? sa[0] : z;
+      a[k][1] = ok ? sa[1] : z;
+      b[k][0] = ok ? sb[0] : z;
+      b[k][1] = ok ? sb[1] : z;
+    }
+#pragma unroll
+    for (int k = 0; k < 2; ++k) {
+      const int i = tid + k * NTH, r = i >> 3, cb = i & 7;
+      const float av[8] = {a[k][0].x, a[k][0].y, a[k][0].z, a[k][0].w,
+                           a[k][1].x, a[k][1].y, a[k][1].z, a[k][1].w};
+      const float bv[8] = {b[k][0].x, b[k][0].y, b[k][0].z, b[k][0].w,
+                           b[k][1].x, b[k][1].y, b[k][1].z, b[k][1].w};
+      uint32_t ph[4], pl[4], qh[4], ql[4];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        tc::split_pack(av[2 * j], av[2 * j + 1], ph[j], pl[j]);
+        tc::split_pack(bv[2 * j], bv[2 * j + 1], qh[j], ql[j]);
+      }
+      const int o = um::boff(r, cb * 8);
+      *reinterpret_cast<uint4*>(SH + o) = make_uint4(ph[0], ph[1], ph[2], ph[3]);
+      *reinterpret_cast<uint4*>(SL + o) = make_uint4(pl[0], pl[1], pl[2], pl[3]);
+      *reinterpret_cast<uint4*>(DH + o) = make_uint4(qh[0], qh[1], qh[2], qh[3]);
+      *reinterpret_cast<uint4*>(DL + o) = make_uint4(ql[0], ql[1], ql[2], ql[3]);
+    }
   }
   if (tid < 64) bs[tid] = tid < Mc ? __bfloat162float(p.beta[bh * rows + r0 + tid]) : 0.f;
   cp_async_wait_all();
   mbar_wait(bar + 1, 0, &g_sticky_err);
-  // S, dS' -> split blocked tiles
-  for (int i = tid; i < 64 * 8; i += NTH) {
-    const int r = i >> 3, cb = i & 7;
-    float a[8], b[8];
-#pragma unroll
-    for (int j = 0; j < 8; ++j) a[j] = b[j] = 0.f;
-    if (r < p.dk && cb * 8 < p.dv) {
-      const float4* sa = reinterpret_cast<const float4*>(stS + r * p.dv + cb * 8);
-      const float4* sb = reinterpret_cast<const float4*>(stD + r * p.dv + cb * 8);
-      const float4 a0 = sa[0], a1 = sa[1], b0 = sb[0], b1 = sb[1];
-      a[0] = a0.x; a[1] = a0.y; a[2] = a0.z; a[3] = a0.w; a[4] = a1.x; a[5] = a1.y; a[6] = a1.z; a[7] = a1.w;
-      b[0] = b0.x; b[1] = b0.y; b[2] = b0.z; b[3] = b0.w; b[4] = b1.x; b[5] = b1.y; b[6] = b1.z; b[7] = b1.w;
-    }
-    uint32_t ph[4], pl[4], qh[4], ql[4];
-#pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      tc::split_pack(a[2 * j], a[2 * j + 1], ph[j], pl[j]);
-      tc::split_pack(b[2 * j], b[2 * j + 1], qh[j], ql[j]);
-    }
-    const int o = um::boff(r, cb * 8);
-    *reinterpret_cast<uint4*>(SH + o) = make_uint4(ph[0], ph[1], ph[2], ph[3]);
-    *reinterpret_cast<uint4*>(SL + o) = make_uint4(pl[0], pl[1], pl[2], pl[3]);
-    *reinterpret_cast<uint4*>(DH + o) = make_uint4(qh[0], qh[1], qh[2], qh[3]);
-    *reinterpret_cast<uint4*>(DL + o) = make_uint4(ql[0], ql[1], ql[2], ql[3]);
-  }
   const uint32_t tb = *tbase_s;
-  const uint32_t lb = tb + ((uint32_t)(32 * q) << 16) + col0;  // this warp's accumulator window
+  const uint32_t tA = tb, tB = tb + 64, tC = tb + 128, tD = tb + 192;
+  const uint32_t lb = tb + ((uint32_t)(32 * q) << 16) + 32 * hh;  // this warp's accumulator window
 
   unsigned phase = 0;
   // make this thread's shared-memory writes visible to the tensor cores and
@@ -433,196 +436,220 @@ __global__ void __launch_bounds__(kGradThreads, 1) bwd_grads_kernel(const TcArgs
     phase ^= 1u;
     um::fence_after();
   };
+  // load two 16-column halves of this thread's 32 columns from NA accumulators
+  // at column offsets off[] (one wait), as v[acc][half][16]
   auto S_ = [](const bf16* t) { return um::saddr(t); };
-  const um::Opnd oK = um::opnd(S_(K), 0, false), oKmn = um::opnd(S_(K), 0, true),
-                 oQ = um::opnd(S_(Q), 0, false), oQmn = um::opnd(S_(Q), 0, true),
-                 odY = um::opnd(S_(dY), 0, false), odYmn = um::opnd(S_(dY), 0, true),
-                 oVmn = um::opnd(S_(V), 0, true);
-  const um::Opnd oS = um::opnd(S_(SH), S_(SL), false), oSmn = um::opnd(S_(SH), S_(SL), true),
-                 oD = um::opnd(S_(DH), S_(DL), false), oDmn = um::opnd(S_(DH), S_(DL), true),
-                 oTi = um::opnd(S_(TiH), S_(TiL), false), oTimn = um::opnd(S_(TiH), S_(TiL), true);
 
   // level 1
   to_mma();
   if (tid == 0) {
-    const um::Prod ps[3] = {{tb + 128, oTi, oKmn, false}, {tb + 192, oTi, oVmn, false},
-                            {tb + 0, oK, oK, false}};
+    const um::Opnd oTi = um::opnd(S_(TiH), S_(TiL), false);
+    const um::Prod ps[2] = {{tA, oTi, um::opnd(S_(K), 0, true), false},
+                            {tB, oTi, um::opnd(S_(V), 0, true), false}};
     um::products(ps);
     um::commit(bar);
   } else if (tid == 32) {
-    const um::Prod ps[2] = {{tb + 256, oK, oDmn, false}, {tb + 64, oQ, oK, false}};
+    const um::Prod ps[2] = {{tC, um::opnd(S_(K), 0, false), um::opnd(S_(DH), S_(DL), true), false},
+                            {tD, um::opnd(S_(Q), 0, false), um::opnd(S_(K), 0, false), false}};
     um::products(ps);
     um::commit(bar);
   }
   wait_mma();
-  {  // P = Q K^T beta[col] * read;  -W
-    float v[16];
-    um::ld16(lb + 64, v);
+#pragma unroll
+  for (int half = 0; half < 2; ++half) {  // P = Q K^T beta[col] * read (D);  -W (A)
+    const int c0 = 32 * hh + 16 * half;
+    uint32_t r1[16], r2[16];
+    float v[16], w[16];
+    um::ld16_async(lb + 192 + 16 * half, r1);
+    um::ld16_async(lb + 0 + 16 * half, r2);
+    um::ld_wait();
+    um::ld_bind(r1, v);
+    um::ld_bind(r2, w);
     if (rv) {
 #pragma unroll
       for (int i = 0; i < 16; ++i) {
-        const int cl = col0 + i;
+        const int cl = c0 + i;
         v[i] = (cl < (row + 1) * p.nh && cl < Mc) ? v[i] * bs[cl] : 0.f;
+        w[i] = -w[i];
       }
-      um::store_split16(PH, PL, row, col0, v);
-    }
-    um::ld16(lb + 128, v);
-    if (rv) {
-#pragma unroll
-      for (int i = 0; i < 16; ++i) v[i] = -v[i];
-      um::store_split16(WH, WL, row, col0, v);
+      um::store_split16(PH, PL, row, c0, v);
+      um::store_split16(WH, WL, row, c0, w);
     }
   }
   // level 2
   to_mma();
   if (tid == 0) {
-    const um::Prod ps[1] = {{tb + 192, um::opnd(S_(WH), S_(WL), false), oSmn, true}};
+    const um::Prod ps[1] = {{tB, um::opnd(S_(WH), S_(WL), false), um::opnd(S_(SH), S_(SL), true), true}};
     um::products(ps);
     um::commit(bar);
   } else if (tid == 32) {
-    const um::Prod ps[1] = {{tb + 320, um::opnd(S_(PH), S_(PL), true), odYmn, false}};
+    const um::Prod ps[1] = {{tA, um::opnd(S_(PH), S_(PL), true), um::opnd(S_(dY), 0, true), false}};
     um::products(ps);
     um::commit(bar);
   }
   wait_mma();
-  {  // U, beta U, dU = P^T dy + beta dbU; dbeta[row] += sum U * dbU
-    float u[16], db[16], pd[16];
-    uint32_t ru[16], rd[16], rp[16];
-    um::ld16_async(lb + 192, ru);
-    um::ld16_async(lb + 256, rd);
-    um::ld16_async(lb + 320, rp);
-    um::ld_wait();
-    um::ld_bind(ru, u);
-    um::ld_bind(rd, db);
-    um::ld_bind(rp, pd);
-    if (rv) {
-      const float b = bs[row];
-      float rs = 0.f;
+  {  // U (B), beta U, dU = P^T dy (A) + beta dbU (C); row sums of U * dbU
+    float rs = 0.f;
 #pragma unroll
-      for (int i = 0; i < 16; ++i) {
-        rs += u[i] * db[i];
-        pd[i] += b * db[i];
+    for (int half = 0; half < 2; ++half) {
+      const int c0 = 32 * hh + 16 * half;
+      uint32_t r1[16], r2[16], r3[16];
+      float u[16], db[16], pd[16];
+      um::ld16_async(lb + 64 + 16 * half, r1);
+      um::ld16_async(lb + 128 + 16 * half, r2);
+      um::ld16_async(lb + 0 + 16 * half, r3);
+      um::ld_wait();
+      um::ld_bind(r1, u);
+      um::ld_bind(r2, db);
+      um::ld_bind(r3, pd);
+      if (rv) {
+        const float b = bs[row];
+#pragma unroll
+        for (int i = 0; i < 16; ++i) {
+          rs += u[i] * db[i];
+          pd[i] += b * db[i];
+        }
+        um::store_split16(UH, UL, row, c0, u);
+        um::store_split16(dUH, dUL, row, c0, pd);
       }
-      rpart[(warp >> 2) * 64 + row] = rs;
-      um::store_split16(UH, UL, row, col0, u);
-#pragma unroll
-      for (int i = 0; i < 16; ++i) u[i] *= b;
-      um::store_split16(BUH, BUL, row, col0, u);
-      um::store_split16(dUH, dUL, row, col0, pd);
     }
+    if (rv) rpart[hh * 64 + row] = rs;
   }
   // level 3
   to_mma();
-  if (tid == 0) {  // G = Ti^T dU as (Ti^T dU_hi) + (Ti_hi^T dU_lo) in two accumulators
-    const um::Prod ps[1] = {{tb + 128, oTimn, um::opnd(S_(dUH), 0, true), false}};
+  if (tid == 0) {  // G = Ti^T dU as (Ti^T dU_hi) + (Ti_hi^T dU_lo) in C and D
+    const um::Prod ps[2] = {
+        {tC, um::opnd(S_(TiH), S_(TiL), true), um::opnd(S_(dUH), 0, true), false},
+        {tD, um::opnd(S_(TiH), 0, true), um::opnd(S_(dUL), 0, true), false}};
     um::products(ps);
     um::commit(bar);
-  } else if (tid == 32) {
-    const um::Prod ps[1] = {{tb + 384, um::opnd(S_(TiH), 0, true), um::opnd(S_(dUL), 0, true), false}};
+  } else if (tid == 32) {  // U dS'^T in A
+    const um::Prod ps[1] = {{tA, um::opnd(S_(UH), S_(UL), false), um::opnd(S_(DH), S_(DL), false), false}};
     um::products(ps);
     um::commit(bar);
   }
   wait_mma();
-  {  // dV = G; Gn = -G
-    float g[16], g2[16];
-    um::ld16(lb + 128, g);
-    um::ld16(lb + 384, g2);
+  float uds[2][16];  // U dS'^T of this thread's row, held until the last epilogue
 #pragma unroll
-    for (int i = 0; i < 16; ++i) g[i] += g2[i];
+  for (int half = 0; half < 2; ++half) {  // dV = G; Gn = -G
+    const int c0 = 32 * hh + 16 * half;
+    uint32_t r1[16], r2[16], r3[16];
+    float g[16], g2[16];
+    um::ld16_async(lb + 128 + 16 * half, r1);
+    um::ld16_async(lb + 192 + 16 * half, r2);
+    um::ld16_async(lb + 0 + 16 * half, r3);
+    um::ld_wait();
+    um::ld_bind(r1, g);
+    um::ld_bind(r2, g2);
+    um::ld_bind(r3, uds[half]);
     if (rv) {
-      if (row < Mc) row16_to_global(p.dV + (bh * rows + r0 + row) * p.dv, col0, p.dv, g);
+#pragma unroll
+      for (int i = 0; i < 16; ++i) g[i] += g2[i];
+      if (row < Mc) row16_to_global(p.dV + (bh * rows + r0 + row) * p.dv, c0, p.dv, g);
 #pragma unroll
       for (int i = 0; i < 16; ++i) g[i] = -g[i];
-      um::store_split16(GH, GL, row, col0, g);
+      um::store_split16(GH, GL, row, c0, g);
     }
   }
   // level 4
   to_mma();
-  if (tid == 0) {
-    const um::Prod ps[1] = {{tb + 256, um::opnd(S_(GH), S_(GL), false), um::opnd(S_(UH), S_(UL), false), false}};
+  if (tid == 0) {  // Gn U^T in B, K K^T in C
+    const um::Prod ps[2] = {{tB, um::opnd(S_(GH), S_(GL), false), um::opnd(S_(UH), S_(UL), false), false},
+                            {tC, um::opnd(S_(K), 0, false), um::opnd(S_(K), 0, false), false}};
     um::products(ps);
     um::commit(bar);
-  } else if (tid == 32) {
-    const um::Prod ps[1] = {{tb + 320, odY, um::opnd(S_(UH), S_(UL), false), false}};
+  } else if (tid == 32) {  // dy U^T in A, Q K^T in D
+    const um::Prod ps[2] = {{tA, um::opnd(S_(dY), 0, false), um::opnd(S_(UH), S_(UL), false), false},
+                            {tD, um::opnd(S_(Q), 0, false), um::opnd(S_(K), 0, false), false}};
     um::products(ps);
     um::commit(bar);
   }
   wait_mma();
   {  // dS_ = (dy U^T) beta * read; dKK = (Gn U^T) beta * strict; dbeta column terms
-    float ds[16], dk[16], qk[16], kk[16];
-    uint32_t r1[16], r2[16], r3[16], r4[16];
-    um::ld16_async(lb + 320, r1);
-    um::ld16_async(lb + 256, r2);
-    um::ld16_async(lb + 64, r3);
-    um::ld16_async(lb + 0, r4);
-    um::ld_wait();
-    um::ld_bind(r1, ds);
-    um::ld_bind(r2, dk);
-    um::ld_bind(r3, qk);
-    um::ld_bind(r4, kk);
-    float cs = 0.f;  // after the reduction lane i < 16 holds column col0 + i
+    float cs = 0.f;  // after the reductions lane i < 32 holds column 32*hh + i
 #pragma unroll
-    for (int i = 0; i < 16; ++i) {
-      const int cl = col0 + i;
-      const float x = (rv && cl < (row + 1) * p.nh && cl < Mc) ? ds[i] : 0.f;
-      const float y = (rv && cl < row && cl < Mc) ? dk[i] : 0.f;
-      float s = rv ? x * qk[i] + y * kk[i] : 0.f;
-      s += __shfl_xor_sync(0xffffffffu, s, 1);
-      s += __shfl_xor_sync(0xffffffffu, s, 2);
-      s += __shfl_xor_sync(0xffffffffu, s, 4);
-      s += __shfl_xor_sync(0xffffffffu, s, 8);
-      if (lane == i) cs = s;
-      ds[i] = x * bs[cl];
-      dk[i] = y * bs[cl];
+    for (int half = 0; half < 2; ++half) {
+      const int c0 = 32 * hh + 16 * half;
+      uint32_t r1[16], r2[16], r3[16], r4[16];
+      float ds[16], dk[16], kk[16], qk[16];
+      um::ld16_async(lb + 0 + 16 * half, r1);
+      um::ld16_async(lb + 64 + 16 * half, r2);
+      um::ld16_async(lb + 128 + 16 * half, r3);
+      um::ld16_async(lb + 192 + 16 * half, r4);
+      um::ld_wait();
+      um::ld_bind(r1, ds);
+      um::ld_bind(r2, dk);
+      um::ld_bind(r3, kk);
+      um::ld_bind(r4, qk);
+#pragma unroll
+      for (int i = 0; i < 16; ++i) {
+        const int cl = c0 + i;
+        const float x = (rv && cl < (row + 1) * p.nh && cl < Mc) ? ds[i] : 0.f;
+        const float y = (rv && cl < row && cl < Mc) ? dk[i] : 0.f;
+        float s = rv ? x * qk[i] + y * kk[i] : 0.f;
+        s += __shfl_xor_sync(0xffffffffu, s, 1);
+        s += __shfl_xor_sync(0xffffffffu, s, 2);
+        s += __shfl_xor_sync(0xffffffffu, s, 4);
+        s += __shfl_xor_sync(0xffffffffu, s, 8);
+        s += __shfl_xor_sync(0xffffffffu, s, 16);  // lanes 16-31 hold no rows: every lane gets the sum
+        if (lane == 16 * half + i) cs = s;
+        ds[i] = x * bs[cl];
+        dk[i] = y * bs[cl];
+      }
+      if (rv) {
+        um::store_split16(dSH, dSL, row, c0, ds);
+        um::store_split16(dKH, dKL, row, c0, dk);
+      }
     }
-    if (lane < 16) cpart[warp * 16 + lane] = cs;
-    if (rv) {
-      um::store_split16(dSH, dSL, row, col0, ds);
-      um::store_split16(dKH, dKL, row, col0, dk);
-    }
+    cpart[warp * 32 + lane] = cs;
   }
   // level 5
   to_mma();
-  if (tid == 0) {  // dK partial sums in columns 64 and 192
-    const um::Opnd odKmn = um::opnd(S_(dKH), S_(dKL), true);
-    const um::Prod ps[3] = {{tb + 64, um::opnd(S_(BUH), S_(BUL), false), oD, false},
-                            {tb + 192, odKmn, oKmn, false},
-                            {tb + 64, um::opnd(S_(GH), S_(GL), false), oS, true}};
+  if (tid == 0) {  // dQ in A, Gn S^T in C
+    const um::Opnd oS = um::opnd(S_(SH), S_(SL), false);
+    const um::Prod ps[3] = {{tA, um::opnd(S_(dY), 0, false), oS, false},
+                            {tC, um::opnd(S_(GH), S_(GL), false), oS, false},
+                            {tA, um::opnd(S_(dSH), S_(dSL), false), um::opnd(S_(K), 0, true), true}};
     um::products(ps);
     um::commit(bar);
-  } else if (tid == 32) {  // dQ in columns 0, dK partial sum in columns 128
-    const um::Opnd odS = um::opnd(S_(dSH), S_(dSL), false), odSmn = um::opnd(S_(dSH), S_(dSL), true),
-                   odK = um::opnd(S_(dKH), S_(dKL), false);
-    const um::Prod ps[4] = {{tb + 0, odY, oS, false}, {tb + 128, odSmn, oQmn, false},
-                            {tb + 0, odS, oKmn, true}, {tb + 128, odK, oKmn, true}};
+  } else if (tid == 32) {  // dS_^T Q + dKK K in B, dKK^T K in D
+    const um::Opnd oKmn = um::opnd(S_(K), 0, true);
+    const um::Prod ps[3] = {{tB, um::opnd(S_(dSH), S_(dSL), true), um::opnd(S_(Q), 0, true), false},
+                            {tD, um::opnd(S_(dKH), S_(dKL), true), oKmn, false},
+                            {tB, um::opnd(S_(dKH), S_(dKL), false), oKmn, true}};
     um::products(ps);
     um::commit(bar);
   }
   wait_mma();
-  {  // dQ (token rows), dK (micro-step rows)
-    float v[16], v1[16], v2[16], v3[16];
-    uint32_t r0_[16], r1[16], r2[16], r3[16];
-    um::ld16_async(lb + 0, r0_);
-    um::ld16_async(lb + 64, r1);
-    um::ld16_async(lb + 128, r2);
-    um::ld16_async(lb + 192, r3);
+#pragma unroll
+  for (int half = 0; half < 2; ++half) {  // dQ (token rows), dK (micro-step rows)
+    const int c0 = 32 * hh + 16 * half;
+    uint32_t r1[16], r2[16], r3[16], r4[16];
+    float v[16], v2[16], v3[16], v4[16];
+    um::ld16_async(lb + 0 + 16 * half, r1);
+    um::ld16_async(lb + 64 + 16 * half, r2);
+    um::ld16_async(lb + 128 + 16 * half, r3);
+    um::ld16_async(lb + 192 + 16 * half, r4);
     um::ld_wait();
-    um::ld_bind(r0_, v);
-    um::ld_bind(r1, v1);
+    um::ld_bind(r1, v);
     um::ld_bind(r2, v2);
     um::ld_bind(r3, v3);
-    if (rv && row < Cc) row16_to_global(p.dQ + (bh * p.T + t0 + row) * p.dk, col0, p.dk, v);
+    um::ld_bind(r4, v4);
+    if (rv && row < Cc) row16_to_global(p.dQ + (bh * p.T + t0 + row) * p.dk, c0, p.dk, v);
+    if (rv && row < Mc) {
+      const float b = bs[row];
 #pragma unroll
-    for (int i = 0; i < 16; ++i) v1[i] += v2[i] + v3[i];
-    if (rv && row < Mc) row16_to_global(p.dK + (bh * rows + r0 + row) * p.dk, col0, p.dk, v1);
+      for (int i = 0; i < 16; ++i) v2[i] += v3[i] + v4[i] + b * uds[half][i];
+      row16_to_global(p.dK + (bh * rows + r0 + row) * p.dk, c0, p.dk, v2);
+    }
   }
   um::fence_before();
   __syncthreads();
   if (tid < Mc) {  // dbeta = row sums of U * dbU + column sums of the masked products
-    const int g4 = (tid >> 4) * 4, cl = tid & 15;
-    const float d = (rpart[tid] + rpart[64 + tid]) + (rpart[128 + tid] + rpart[192 + tid]) +
-                    (cpart[g4 * 16 + cl] + cpart[(g4 + 1) * 16 + cl]) +
-                    (cpart[(g4 + 2) * 16 + cl] + cpart[(g4 + 3) * 16 + cl]);
+    const int h2 = tid >> 5, cl = tid & 31;
+    const float d = (rpart[tid] + rpart[64 + tid]) +
+                    (cpart[(4 * h2) * 32 + cl] + cpart[(4 * h2 + 1) * 32 + cl]) +
+                    (cpart[(4 * h2 + 2) * 32 + cl] + cpart[(4 * h2 + 3) * 32 + cl]);
     p.dbeta[bh * rows + r0 + tid] = __float2bfloat16_rn(d);
   }
   if (warp == 0) {
@@ -641,6 +668,7 @@ __global__ void __launch_bounds__(kGradThreads, 1) bwd_grads_kernel(const TcArgs
 // Yp (fp32) go to the workspace for the forward chain. Two CTAs per SM.
 // smem: K | Q | V | beta | Td | T h/l (-> bW h/l) | Ti h/l | Y h/l (-> bU' h/l) | P~ h/l
 constexpr size_t kPrepSmem = 11 * (size_t)kTileBytes + 256 + kTdBytes;
+constexpr int kPrepThreads = 512;  // 16 warps: warp (mt, q) = (w & 3, w >> 2)
 
 // 16 x 8*NT fragment tile -> split bf16 saved tiles (hi, lo; padded layout),
 // f(row, col, x) applied first.
@@ -659,7 +687,7 @@ __device__ __forceinline__ void frag_to_global_split(const float (&c)[NT][4], bf
     }
 }
 
-__global__ void __launch_bounds__(kGradThreads, 2) prep_kernel(const TcArgs p) {
+__global__ void __launch_bounds__(kPrepThreads, 2) prep_kernel(const TcArgs p) {
   extern __shared__ __align__(128) unsigned char smem[];
   bf16* K = reinterpret_cast<bf16*>(smem);
   bf16* Q = K + kTile;
@@ -676,7 +704,7 @@ __global__ void __launch_bounds__(kGradThreads, 2) prep_kernel(const TcArgs p) {
   bf16* PL = PH + kTile;
   bf16 *BWH = TH, *BWL = TL, *BUH = YH, *BUL = YL;  // reused once the inverse is done
 
-  constexpr int NTH = kGradThreads;
+  constexpr int NTH = kPrepThreads;
   const int tid = threadIdx.x, warp = tid >> 5, mt = warp & 3, q = warp >> 2;
   const int m0 = 16 * mt, n0 = 16 * q, hf = q & 1, mat = q >> 1;
   const int c = blockIdx.x % p.nchunks;
@@ -1075,7 +1103,7 @@ int run_tc(bool fwd, const Args<__nv_bfloat16>& p, long long B, int H, long long
     }
     a.Bc = static_cast<float*>(ws);
     a.Yp = a.Bc + ncs * 4096;
-    const int rc = launch_tc(prep_kernel, (long long)ncs, kPrepSmem, st, a, kGradThreads);
+    const int rc = launch_tc(prep_kernel, (long long)ncs, kPrepSmem, st, a, kPrepThreads);
     if (rc != MGS_OK) return rc;
     return narrow ? launch_tc(chain_fwd_kernel<32>, BH * a.S, kChainFwdSmem, st, a, kSerialThreads)
                   : launch_tc(chain_fwd_kernel<64>, BH * a.S, kChainFwdSmem, st, a, kSerialThreads);
