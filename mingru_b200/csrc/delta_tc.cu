@@ -581,21 +581,32 @@ __global__ void __launch_bounds__(kGradThreads, 2) bwd_grads_kernel(const TcArgs
       um::ld_bind(r2, dk);
       um::ld_bind(r3, kk);
       um::ld_bind(r4, qk);
+      float e[16];  // this row's dbeta column terms
 #pragma unroll
       for (int i = 0; i < 16; ++i) {
         const int cl = c0 + i;
         const float x = (rv && cl < (row + 1) * p.nh && cl < Mc) ? ds[i] : 0.f;
         const float y = (rv && cl < row && cl < Mc) ? dk[i] : 0.f;
-        float s = rv ? x * qk[i] + y * kk[i] : 0.f;
-        s += __shfl_xor_sync(0xffffffffu, s, 1);
-        s += __shfl_xor_sync(0xffffffffu, s, 2);
-        s += __shfl_xor_sync(0xffffffffu, s, 4);
-        s += __shfl_xor_sync(0xffffffffu, s, 8);
-        s += __shfl_xor_sync(0xffffffffu, s, 16);  // lanes 16-31 hold no rows: every lane gets the sum
-        if (lane == 16 * half + i) cs = s;
+        e[i] = rv ? x * qk[i] + y * kk[i] : 0.f;
         ds[i] = x * bs[cl];
         dk[i] = y * bs[cl];
       }
+      // column sums over the 16 rows of each half-warp by a transposing
+      // butterfly: at distance d a lane keeps the half of its values selected
+      // by lane bit d and adds its partner's copy of that half, so lane i ends
+      // with column i (15 shuffles for 16 columns).
+#pragma unroll
+      for (int d = 8, n = 16; d >= 1; d >>= 1, n >>= 1) {
+        const bool upper = (lane & d) != 0;
+#pragma unroll
+        for (int j = 0; j < n / 2; ++j) {
+          const float keep = upper ? e[j + n / 2] : e[j];
+          const float send = upper ? e[j] : e[j + n / 2];
+          e[j] = keep + __shfl_xor_sync(0xffffffffu, send, d);
+        }
+      }
+      const float colsum = __shfl_sync(0xffffffffu, e[0], lane & 15);  // from the row lanes 0-15
+      if ((lane >> 4) == half) cs = colsum;
       if (rv) {
         um::store_split16(dSH, dSL, row, c0, ds);
         um::store_split16(dKH, dKL, row, c0, dk);
