@@ -569,6 +569,15 @@ __device__ __forceinline__ void tma_store_3d(const CUtensorMap* map, int x, int 
       : "memory");
 }
 
+// One bulk copy of `bytes` (multiple of 16, both addresses 16-byte aligned)
+// from this CTA's shared memory to global memory, in the current bulk group
+// (bulk_commit / bulk_wait_read; shared writes fenced with fence_proxy_async_smem).
+__device__ __forceinline__ void bulk_s2g(void* dst, const void* src, unsigned bytes) {
+  asm volatile("cp.async.bulk.global.shared::cta.bulk_group [%0], [%1], %2;" ::"l"(dst),
+               "r"(smem_u32(src)), "r"(bytes)
+               : "memory");
+}
+
 __device__ __forceinline__ void bulk_commit() {
   asm volatile("cp.async.bulk.commit_group;" ::: "memory");
 }

@@ -222,34 +222,6 @@ __device__ __forceinline__ void frag_from_global(float (&c)[NT][4], const float*
     }
 }
 
-// ---- chunk matrices from K K^T and Q K^T (exact bf16 products, fp32 sums).
-// Warp w: row tile w & 3; warps 0-3 one product, warps 4-7 the other.
-
-// P = (Q K^T) diag(beta) * read  as split tiles (NT n-tiles at columns n0..)
-template <int NT>
-__device__ __forceinline__ void store_P(const float (&acc)[NT][4], const float* bs, int nh, int Mc,
-                                        int m0, int n0, bf16* PH, bf16* PL) {
-  tc::store_split(acc, PH, PL, m0, n0, [&](int r, int cl, float x) {
-    return (cl < (r + 1) * nh && cl < Mc) ? x * bs[cl] : 0.f;
-  });
-}
-
-// T's strict lower part (K K^T diag(beta)) as fp32 (diagonal blocks, Td) and split tiles.
-template <int NT>
-__device__ __forceinline__ void store_T(const float (&acc)[NT][4], const float* bs, int m0, int n0,
-                                        float* Td, bf16* TH, bf16* TL) {
-#pragma unroll
-  for (int j = 0; j < NT; ++j)
-#pragma unroll
-    for (int v = 0; v < 4; ++v) {
-      const int row = tc::frag_row(m0, v), col = tc::frag_col(n0, j, v);
-      if ((col >> 4) == (row >> 4))
-        Td[(row >> 4) * 272 + (row & 15) * 17 + (col & 15)] = col < row ? acc[j][v] * bs[col] : 0.f;
-    }
-  tc::store_split(acc, TH, TL, m0, n0,
-                  [&](int r, int cl, float x) { return cl < r ? x * bs[cl] : 0.f; });
-}
-
 struct TcArgs {
   const bf16* Q;
   const bf16* K;
@@ -670,131 +642,242 @@ __global__ void __launch_bounds__(kGradThreads, 2) bwd_grads_kernel(const TcArgs
 }
 
 // ------------------------------------------------------- forward: prep --
-// One CTA per (b, h, chunk), independent of the state: T, T^{-1} (saved for
-// the backward), and the chunk's affine state map and readout
+// One CTA per (b, h, chunk), independent of the state, two CTAs per SM: T,
+// T^{-1} (saved for the backward), and the chunk's affine state map and readout
 //   S' = S + Xn S + Bc,   Xn = -K^T (beta W),  Bc = K^T (beta U')
 //   y  = Qt S + Yp,       Qt = Q - P~ (beta W), Yp = P~ (beta U')
 // with W = Ti K, U' = Ti V, P~ = (Q K^T) * read_mask (P = P~ diag(beta)).
-// Xn and Qt (split bf16 tiles) go to `saved` (both chains read them); Bc and
-// Yp (fp32) go to the workspace for the forward chain. Two CTAs per SM.
-// smem: K | Q | V | beta | Td | T h/l (-> bW h/l) | Ti h/l | Y h/l (-> bU' h/l) | P~ h/l
-constexpr size_t kPrepSmem = 11 * (size_t)kTileBytes + 256 + kTdBytes;
-constexpr int kPrepThreads = 512;  // 16 warps: warp (mt, q) = (w & 3, w >> 2)
+// The products run on the tcgen05 tensor cores (umma.cuh):
+//   1. [K; Q] K^T as one M = 128 product          -> T (strict lower, beta), P~
+//   2. (T^{-1} by blocked substitution on mma.sync, tri_inv_tc)
+//   3. Ti K, Ti V                                   -> beta W, beta U'
+//   4. K^T (beta W), P~ (beta W), K^T (beta U'), P~ (beta U')
+// Xn and Qt (split bf16, padded layout) go to `saved`, Bc and Yp (fp32) to the
+// forward workspace, T^{-1} (split, blocked layout) to `saved` for the grads,
+// all staged in shared memory and written by bulk copies.
+// smem: header | K | Q | V | P~ h/l (blocked) | beta | Td | region R of six
+// padded tiles: T h/l, X h/l, Y h/l for the inverse; afterwards beta W (over T),
+// beta U' (over X) and the blocked T^{-1} (over Y).
+constexpr int kPrepThreads = 256;
+constexpr size_t kPrepSmem =
+    1024 + 5 * (size_t)umma::kTileBytes + 256 + kTdBytes + 6 * (size_t)kTileBytes;
 
-// 16 x 8*NT fragment tile -> split bf16 saved tiles (hi, lo; padded layout),
-// f(row, col, x) applied first.
-template <int NT, class F>
-__device__ __forceinline__ void frag_to_global_split(const float (&c)[NT][4], bf16* hi, bf16* lo,
-                                                     int m0, int n0, F f) {
+// 16 values of row r (columns c0..c0+15) -> split bf16 tiles in the padded layout.
+__device__ __forceinline__ void store_split16_padded(bf16* hi, bf16* lo, int r, int c0,
+                                                     const float (&v)[16]) {
 #pragma unroll
-  for (int j = 0; j < NT; ++j)
+  for (int h = 0; h < 2; ++h) {
+    uint32_t ph[4], pl[4];
 #pragma unroll
-    for (int h = 0; h < 2; ++h) {
-      const int row = tc::frag_row(m0, 2 * h), col = tc::frag_col(n0, j, 0);
-      uint32_t ph, pl;
-      tc::split_pack(f(row, col, c[j][2 * h]), f(row, col + 1, c[j][2 * h + 1]), ph, pl);
-      *reinterpret_cast<uint32_t*>(hi + row * kLd + col) = ph;
-      *reinterpret_cast<uint32_t*>(lo + row * kLd + col) = pl;
-    }
+    for (int i = 0; i < 4; ++i) tc::split_pack(v[8 * h + 2 * i], v[8 * h + 2 * i + 1], ph[i], pl[i]);
+    *reinterpret_cast<uint4*>(hi + r * kLd + c0 + 8 * h) = make_uint4(ph[0], ph[1], ph[2], ph[3]);
+    *reinterpret_cast<uint4*>(lo + r * kLd + c0 + 8 * h) = make_uint4(pl[0], pl[1], pl[2], pl[3]);
+  }
+}
+
+// 16 fp32 values of row r (columns c0..) -> global row (columns < ncols).
+__device__ __forceinline__ void row16_f32_to_global(float* g, int c0, int ncols, const float (&v)[16]) {
+#pragma unroll
+  for (int k = 0; k < 4; ++k)
+    if (c0 + 4 * k < ncols)
+      *reinterpret_cast<float4*>(g + c0 + 4 * k) = make_float4(v[4 * k], v[4 * k + 1], v[4 * k + 2], v[4 * k + 3]);
 }
 
 __global__ void __launch_bounds__(kPrepThreads, 2) prep_kernel(const TcArgs p) {
-  extern __shared__ __align__(128) unsigned char smem[];
-  bf16* K = reinterpret_cast<bf16*>(smem);
-  bf16* Q = K + kTile;
-  bf16* V = Q + kTile;
-  float* bs = reinterpret_cast<float*>(V + kTile);
+  namespace um = umma;
+  extern __shared__ __align__(1024) unsigned char psmem[];
+  uint64_t* bar = reinterpret_cast<uint64_t*>(psmem);  // [0] level 1, [1] levels 3-4 (two issuers)
+  uint32_t* tbase_s = reinterpret_cast<uint32_t*>(psmem + 64);
+  bf16* bt = reinterpret_cast<bf16*>(psmem + 1024);
+  bf16 *K = bt, *Q = bt + 4096, *V = bt + 2 * 4096, *PH = bt + 3 * 4096, *PL = bt + 4 * 4096;
+  float* bs = reinterpret_cast<float*>(bt + 5 * 4096);
   float* Td = bs + 64;
-  bf16* TH = reinterpret_cast<bf16*>(reinterpret_cast<unsigned char*>(Td) + kTdBytes);
-  bf16* TL = TH + kTile;
-  bf16* TiH = TL + kTile;
-  bf16* TiL = TiH + kTile;
-  bf16* YH = TiL + kTile;
-  bf16* YL = YH + kTile;
-  bf16* PH = YL + kTile;
-  bf16* PL = PH + kTile;
-  bf16 *BWH = TH, *BWL = TL, *BUH = YH, *BUL = YL;  // reused once the inverse is done
+  bf16* R = reinterpret_cast<bf16*>(reinterpret_cast<unsigned char*>(Td) + kTdBytes);
+  bf16 *TH = R, *TL = R + kTile, *XH = R + 2 * kTile, *XL = R + 3 * kTile, *YH = R + 4 * kTile,
+       *YL = R + 5 * kTile;
+  bf16 *BWH = TH, *BWL = TH + 4096, *BUH = XH, *BUL = XH + 4096, *TiH = YH, *TiL = YH + 4096;
 
   constexpr int NTH = kPrepThreads;
-  const int tid = threadIdx.x, warp = tid >> 5, mt = warp & 3, q = warp >> 2;
-  const int m0 = 16 * mt, n0 = 16 * q, hf = q & 1, mat = q >> 1;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int q = warp & 3, hh = warp >> 2;
   const int c = blockIdx.x % p.nchunks;
   const long long bh = blockIdx.x / p.nchunks;
   const long long t0 = (long long)c * p.C;
   const int Cc = (int)min((long long)p.C, p.T - t0), Mc = Cc * p.nh;
-  const int kd = up16(p.dk);
   const long long r0 = t0 * p.nh, rows = p.T * p.nh;
   const long long blk = bh * p.nchunks + c;
 
-  zero_upper_blocks<NTH>(TiH, TiL);
-  stage_rows<8, NTH>(K, p.K + (bh * rows + r0) * p.dk, p.dk, Mc, p.dk >> 3);
-  stage_rows<8, NTH>(Q, p.Q + (bh * p.T + t0) * p.dk, p.dk, Cc, p.dk >> 3);
-  stage_rows<8, NTH>(V, p.V + (bh * rows + r0) * p.dv, p.dv, Mc, p.dv >> 3);
+  if (warp == 0) um::alloc(tbase_s, 256);
+  if (tid == 0) {
+    mbar_init(bar, 1);
+    mbar_init(bar + 1, 2);
+    mbar_fence_init();
+  }
+  zero_upper_blocks<NTH>(XH, XL);
+  stage_blocked<NTH>(K, p.K + (bh * rows + r0) * p.dk, p.dk, Mc, p.dk >> 3);
+  stage_blocked<NTH>(Q, p.Q + (bh * p.T + t0) * p.dk, p.dk, Cc, p.dk >> 3);
+  stage_blocked<NTH>(V, p.V + (bh * rows + r0) * p.dv, p.dv, Mc, p.dv >> 3);
   cp_async_commit();
   if (tid < 64) bs[tid] = tid < Mc ? __bfloat162float(p.beta[bh * rows + r0 + tid]) : 0.f;
   cp_async_wait_all();
-  __syncthreads();
+  auto to_mma = [&]() {
+    fence_proxy_async_smem();
+    um::fence_before();
+    __syncthreads();
+    um::fence_after();
+  };
+  to_mma();
+  const uint32_t tb = *tbase_s;
+  const uint32_t tA = tb, tB = tb + 64, tC = tb + 128, tD = tb + 192;
+  auto S_ = [](const bf16* t) { return um::saddr(t); };
 
-  // K K^T -> T (warps mat 0), Q K^T -> P~ (mat 1): row tile m0, columns 32*hf..
-  {
-    float acc[4][4];
-    tc::zero(acc);
-    const int ncol = mat == 0 ? m0 + 16 : min(64, (m0 + 16) * p.nh);
-    const int np = min(2, max(0, (ncol - 32 * hf + 15) / 16));
-    tc::gemm<4, false, false>(acc, Op{mat == 0 ? K : Q, nullptr}, m0, Op{K, nullptr}, 32 * hf, 0,
-                              kd, np);
-    if (mat == 0)
-      store_T(acc, bs, m0, 32 * hf, Td, TH, TL);
-    else
-      tc::store_split(acc, PH, PL, m0, 32 * hf, [&](int r, int cl, float x) {
-        return (cl < (r + 1) * p.nh && cl < Mc) ? x : 0.f;
-      });
+  // level 1: [K; Q] K^T (K and Q are consecutive blocked tiles: one M = 128 operand)
+  if (tid == 0) {
+    const um::Prod ps[1] = {{tA, um::opnd(S_(K), 0, false), um::opnd(S_(K), 0, false), false, true}};
+    um::products(ps);
+    um::commit(bar);
   }
+  mbar_wait(bar, 0, &g_sticky_err);
+  um::fence_after();
+  {  // row r = 32 q + lane of the M = 128 accumulator: T row r (r < 64) or P~ row r - 64
+    const int r = 32 * q + lane;
+    const uint32_t lb = tb + ((uint32_t)(32 * q) << 16) + 32 * hh;
+#pragma unroll
+    for (int half = 0; half < 2; ++half) {
+      const int c0 = 32 * hh + 16 * half;
+      float v[16];
+      um::ld16(lb + 16 * half, v);
+      if (r < 64) {
+#pragma unroll
+        for (int i = 0; i < 16; ++i) v[i] = c0 + i < r ? v[i] * bs[c0 + i] : 0.f;
+        if ((c0 >> 4) == (r >> 4))
+#pragma unroll
+          for (int i = 0; i < 16; ++i) Td[(r >> 4) * 272 + (r & 15) * 17 + i] = v[i];
+        store_split16_padded(TH, TL, r, c0, v);
+      } else {
+        const int ti = r - 64;
+#pragma unroll
+        for (int i = 0; i < 16; ++i) v[i] = (c0 + i < (ti + 1) * p.nh && c0 + i < Mc) ? v[i] : 0.f;
+        um::store_split16(PH, PL, ti, c0, v);
+      }
+    }
+  }
+  um::fence_before();
   __syncthreads();
-  tri_inv_tc(Td, Op{TH, TL}, TiH, TiL, YH, YL);
-  tile_to_global_blocked<NTH>(TiH, p.Ti + blk * kSavedPair);  // read by the tcgen05 grads kernel
-  tile_to_global_blocked<NTH>(TiL, p.Ti + blk * kSavedPair + 4096);
-
-  // beta W = diag(beta) Ti K (rows m0, d_k columns n0..), beta U' = diag(beta) Ti V
-  {
-    auto bscale = [&](int r, int, float x) { return x * bs[r]; };
-    float w[2][4];
-    tc::zero(w);
-    tc::gemm<2, false, true>(w, Op{TiH, TiL}, m0, Op{K, nullptr}, n0, 0, m0 + 16);
-    tc::store_split(w, BWH, BWL, m0, n0, bscale);
-    float u[2][4];
-    tc::zero(u);
-    tc::gemm<2, false, true>(u, Op{TiH, TiL}, m0, Op{V, nullptr}, n0, 0, m0 + 16);
-    tc::store_split(u, BUH, BUL, m0, n0, bscale);
+  tri_inv_tc(Td, Op{TH, TL}, XH, XL, YH, YL);  // ends with __syncthreads
+  for (int i = tid; i < 64 * 8; i += NTH) {  // padded X -> blocked T^{-1} (over Y)
+    const int row = i >> 3, ch = i & 7;
+    *reinterpret_cast<uint4*>(TiH + um::boff(row, ch * 8)) =
+        *reinterpret_cast<const uint4*>(XH + row * kLd + ch * 8);
+    *reinterpret_cast<uint4*>(TiL + um::boff(row, ch * 8)) =
+        *reinterpret_cast<const uint4*>(XL + row * kLd + ch * 8);
   }
+  to_mma();
+  if (tid == 64) {  // T^{-1} (blocked) to `saved` by bulk copies; Y is not reused until the end
+    bulk_s2g(p.Ti + blk * kSavedPair, TiH, um::kTileBytes);
+    bulk_s2g(p.Ti + blk * kSavedPair + 4096, TiL, um::kTileBytes);
+    bulk_commit();
+  }
+  // level 3: W = Ti K (B), U' = Ti V (C)
+  if (tid == 0 || tid == 32) {
+    const um::Prod ps[1] = {{tid == 0 ? tB : tC, um::opnd(S_(TiH), S_(TiL), false),
+                             um::opnd(S_(tid == 0 ? K : V), 0, true), false}};
+    um::products(ps);
+    um::commit(bar + 1);
+  }
+  mbar_wait(bar + 1, 0, &g_sticky_err);
+  um::fence_after();
+  const int row = 16 * q + lane;  // M = 64 accumulators: lanes 0-15 hold rows
+  const bool rv = lane < 16;
+  const uint32_t lb = tb + ((uint32_t)(32 * q) << 16) + 32 * hh;
+#pragma unroll
+  for (int half = 0; half < 2; ++half) {  // beta W (over T), beta U' (over X)
+    const int c0 = 32 * hh + 16 * half;
+    uint32_t r1[16], r2[16];
+    float w[16], u[16];
+    um::ld16_async(lb + 64 + 16 * half, r1);
+    um::ld16_async(lb + 128 + 16 * half, r2);
+    um::ld_wait();
+    um::ld_bind(r1, w);
+    um::ld_bind(r2, u);
+    if (rv) {
+      const float b = bs[row];
+#pragma unroll
+      for (int i = 0; i < 16; ++i) {
+        w[i] *= b;
+        u[i] *= b;
+      }
+      um::store_split16(BWH, BWL, row, c0, w);
+      um::store_split16(BUH, BUL, row, c0, u);
+    }
+  }
+  to_mma();
+  // level 4: K^T (beta W) (A), P~ (beta W) (B), K^T (beta U') (C), P~ (beta U') (D)
+  if (tid == 0) {
+    const um::Opnd oBW = um::opnd(S_(BWH), S_(BWL), true);
+    const um::Prod ps[2] = {{tA, um::opnd(S_(K), 0, true), oBW, false},
+                            {tB, um::opnd(S_(PH), S_(PL), false), oBW, false}};
+    um::products(ps);
+    um::commit(bar + 1);
+  } else if (tid == 32) {
+    const um::Opnd oBU = um::opnd(S_(BUH), S_(BUL), true);
+    const um::Prod ps[2] = {{tC, um::opnd(S_(K), 0, true), oBU, false},
+                            {tD, um::opnd(S_(PH), S_(PL), false), oBU, false}};
+    um::products(ps);
+    um::commit(bar + 1);
+  }
+  mbar_wait(bar + 1, 1, &g_sticky_err);
+  um::fence_after();
+  // Outputs are staged in shared memory no longer read by the MMAs and leave
+  // by bulk copies: Xn h/l over T, Qt h/l over X (both padded layout, as the
+  // chains read them), Bc [dk][dv] fp32 over Y, Yp [C][dv] fp32 over V and P~.
+  if (tid == 64) bulk_wait_read();  // the T^{-1} copies out of Y have read it
   __syncthreads();
-  const int kp = min(64, up16((m0 + 16) * p.nh));  // causal extent of P~'s row tile
-  bf16* Xg = p.Xn + blk * kSavedPair;
-  bf16* Qg = p.Qt + blk * kSavedPair;
-  {  // Xn = -K^T (beta W): d_k rows m0, d_k columns n0
-    float x[2][4];
-    tc::zero(x);
-    tc::gemm<2, true, true>(x, Op{K, nullptr}, m0, Op{BWH, BWL}, n0, 0, up16(Mc));
-    frag_to_global_split(x, Xg, Xg + kSavedTile, m0, n0, Neg());
+  bf16 *XsH = TH, *XsL = TL, *QsH = XH, *QsL = XL;
+  float* Bcs = reinterpret_cast<float*>(YH);
+  float* Yps = reinterpret_cast<float*>(V);
+#pragma unroll
+  for (int half = 0; half < 2; ++half) {  // Xn, Qt (saved, padded), Bc, Yp (workspace, fp32)
+    const int c0 = 32 * hh + 16 * half;
+    uint32_t r1[16], r2[16], r3[16], r4[16];
+    float x[16], qt[16], bc[16], yp[16];
+    um::ld16_async(lb + 0 + 16 * half, r1);
+    um::ld16_async(lb + 64 + 16 * half, r2);
+    um::ld16_async(lb + 128 + 16 * half, r3);
+    um::ld16_async(lb + 192 + 16 * half, r4);
+    um::ld_wait();
+    um::ld_bind(r1, x);
+    um::ld_bind(r2, qt);
+    um::ld_bind(r3, bc);
+    um::ld_bind(r4, yp);
+    if (rv) {
+#pragma unroll
+      for (int i = 0; i < 16; ++i) {
+        x[i] = -x[i];
+        qt[i] = __bfloat162float(Q[um::boff(row, c0 + i)]) - qt[i];
+      }
+      store_split16_padded(XsH, XsL, row, c0, x);
+      store_split16_padded(QsH, QsL, row, c0, qt);
+      if (row < p.dk) row16_f32_to_global(Bcs + row * p.dv, c0, p.dv, bc);
+      if (row < Cc) row16_f32_to_global(Yps + row * p.dv, c0, p.dv, yp);
+    }
   }
-  {  // Bc = K^T (beta U'): d_k rows m0, d_v columns n0
-    float b[2][4];
-    tc::zero(b);
-    tc::gemm<2, true, true>(b, Op{K, nullptr}, m0, Op{BUH, BUL}, n0, 0, up16(Mc));
-    frag_to_global(b, p.Bc + blk * 4096, p.dv, m0, n0, p.dk, p.dv);
+  fence_proxy_async_smem();
+  um::fence_before();
+  __syncthreads();
+  if (tid == 0) {
+    bulk_s2g(p.Xn + blk * kSavedPair, XsH, kTileBytes);
+    bulk_s2g(p.Xn + blk * kSavedPair + kSavedTile, XsL, kTileBytes);
+    bulk_s2g(p.Qt + blk * kSavedPair, QsH, kTileBytes);
+    bulk_s2g(p.Qt + blk * kSavedPair + kSavedTile, QsL, kTileBytes);
+    bulk_s2g(p.Bc + blk * 4096, Bcs, (unsigned)(p.dk * p.dv * 4));
+    bulk_s2g(p.Yp + blk * 4096, Yps, (unsigned)(Cc * p.dv * 4));
+    bulk_commit();
+    bulk_wait_read();  // shared memory stays valid until the copies have read it
   }
-  {  // Qt = Q - P~ (beta W): token rows m0, d_k columns n0
-    float a[2][4];
-    tc::zero(a);
-    tc::gemm<2, false, true>(a, Op{PH, PL}, m0, Op{BWH, BWL}, n0, 0, kp);
-    frag_to_global_split(a, Qg, Qg + kSavedTile, m0, n0,
-                         [&](int r, int cl, float v) { return __bfloat162float(Q[r * kLd + cl]) - v; });
-  }
-  {  // Yp = P~ (beta U'): token rows m0, d_v columns n0
-    float a[2][4];
-    tc::zero(a);
-    tc::gemm<2, false, true>(a, Op{PH, PL}, m0, Op{BUH, BUL}, n0, 0, kp);
-    frag_to_global(a, p.Yp + blk * 4096, p.dv, m0, n0, Cc, p.dv);
+  if (warp == 0) {
+    um::fence_after();
+    um::dealloc(tb, 256);
   }
 }
 

@@ -43,10 +43,12 @@ __device__ __forceinline__ uint64_t desc_mn(uint32_t tile, int kk) {
   return desc(tile + kk * 2048, 1024, 128);
 }
 
-// Instruction descriptor: bf16 x bf16 -> fp32, M = N = 64, operand majors.
-__host__ __device__ constexpr uint32_t idesc64(bool a_mn, bool b_mn) {
+// Instruction descriptor: bf16 x bf16 -> fp32, N = 64, M = 64 (or 128: two
+// blocked tiles stacked in consecutive memory, row m of D in TMEM lane m),
+// operand majors.
+__host__ __device__ constexpr uint32_t idesc64(bool a_mn, bool b_mn, bool m128 = false) {
   return (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)a_mn << 15) | ((uint32_t)b_mn << 16) |
-         ((64u >> 3) << 17) | ((64u >> 4) << 24);
+         ((64u >> 3) << 17) | ((m128 ? 128u >> 4 : 64u >> 4) << 24);
 }
 
 __device__ __forceinline__ void mma(uint32_t d, uint64_t a, uint64_t b, uint32_t idesc, bool acc) {
@@ -83,6 +85,7 @@ struct Prod {
   uint32_t d;
   Opnd A, B;
   bool accumulate;
+  bool m128 = false;
 };
 
 // Issue a batch of independent products (one thread) k-step by k-step,
@@ -97,7 +100,7 @@ __device__ __forceinline__ void products(const Prod (&ps)[N]) {
 #pragma unroll
     for (int i = 0; i < N; ++i) {
       const Prod& p = ps[i];
-      const uint32_t id = idesc64(p.A.mn, p.B.mn);
+      const uint32_t id = idesc64(p.A.mn, p.B.mn, p.m128);
       const uint64_t oa = (uint64_t)(kk * p.A.step), ob = (uint64_t)(kk * p.B.step);
       mma(p.d, p.A.hi + oa, p.B.hi + ob, id, kk > 0 || p.accumulate);
       if (p.B.lo) mma(p.d, p.A.hi + oa, p.B.lo + ob, id, true);
