@@ -652,9 +652,9 @@ __global__ void __launch_bounds__(kGradThreads, 2) bwd_grads_kernel(const TcArgs
 //   2. (T^{-1} by blocked substitution on mma.sync, tri_inv_tc)
 //   3. Ti K, Ti V                                   -> beta W, beta U'
 //   4. K^T (beta W), P~ (beta W), K^T (beta U'), P~ (beta U')
-// Xn and Qt (split bf16, padded layout) go to `saved`, Bc and Yp (fp32) to the
-// forward workspace, T^{-1} (split, blocked layout) to `saved` for the grads,
-// all staged in shared memory and written by bulk copies.
+// Xn, Qt (split bf16) and T^{-1} (for the grads) go to `saved` in the blocked
+// layout, Bc and Yp (fp32) to the forward workspace, all staged in shared
+// memory and written by bulk copies.
 // smem: header | K | Q | V | P~ h/l (blocked) | beta | Td | region R of six
 // padded tiles: T h/l, X h/l, Y h/l for the inverse; afterwards beta W (over T),
 // beta U' (over X) and the blocked T^{-1} (over Y).
@@ -829,11 +829,11 @@ __global__ void __launch_bounds__(kPrepThreads, 2) prep_kernel(const TcArgs p) {
   mbar_wait(bar + 1, 1, &g_sticky_err);
   um::fence_after();
   // Outputs are staged in shared memory no longer read by the MMAs and leave
-  // by bulk copies: Xn h/l over T, Qt h/l over X (both padded layout, as the
-  // chains read them), Bc [dk][dv] fp32 over Y, Yp [C][dv] fp32 over V and P~.
+  // by bulk copies: Xn h/l over T, Qt h/l over X (blocked, as the chains'
+  // MMAs read them), Bc [dk][dv] fp32 over Y, Yp [C][dv] fp32 over V and P~.
   if (tid == 64) bulk_wait_read();  // the T^{-1} copies out of Y have read it
   __syncthreads();
-  bf16 *XsH = TH, *XsL = TL, *QsH = XH, *QsL = XL;
+  bf16 *XsH = TH, *XsL = TH + 4096, *QsH = XH, *QsL = XH + 4096;  // blocked
   float* Bcs = reinterpret_cast<float*>(YH);
   float* Yps = reinterpret_cast<float*>(V);
 #pragma unroll
@@ -856,8 +856,8 @@ __global__ void __launch_bounds__(kPrepThreads, 2) prep_kernel(const TcArgs p) {
         x[i] = -x[i];
         qt[i] = __bfloat162float(Q[um::boff(row, c0 + i)]) - qt[i];
       }
-      store_split16_padded(XsH, XsL, row, c0, x);
-      store_split16_padded(QsH, QsL, row, c0, qt);
+      um::store_split16(XsH, XsL, row, c0, x);
+      um::store_split16(QsH, QsL, row, c0, qt);
       if (row < p.dk) row16_f32_to_global(Bcs + row * p.dv, c0, p.dv, bc);
       if (row < Cc) row16_f32_to_global(Yps + row * p.dv, c0, p.dv, yp);
     }
@@ -866,10 +866,8 @@ __global__ void __launch_bounds__(kPrepThreads, 2) prep_kernel(const TcArgs p) {
   um::fence_before();
   __syncthreads();
   if (tid == 0) {
-    bulk_s2g(p.Xn + blk * kSavedPair, XsH, kTileBytes);
-    bulk_s2g(p.Xn + blk * kSavedPair + kSavedTile, XsL, kTileBytes);
-    bulk_s2g(p.Qt + blk * kSavedPair, QsH, kTileBytes);
-    bulk_s2g(p.Qt + blk * kSavedPair + kSavedTile, QsL, kTileBytes);
+    bulk_s2g(p.Xn + blk * kSavedPair, XsH, 2 * um::kTileBytes);  // hi, lo contiguous
+    bulk_s2g(p.Qt + blk * kSavedPair, QsH, 2 * um::kTileBytes);
     bulk_s2g(p.Bc + blk * 4096, Bcs, (unsigned)(p.dk * p.dv * 4));
     bulk_s2g(p.Yp + blk * 4096, Yps, (unsigned)(Cc * p.dv * 4));
     bulk_commit();
@@ -881,154 +879,211 @@ __global__ void __launch_bounds__(kPrepThreads, 2) prep_kernel(const TcArgs p) {
   }
 }
 
-// Thread 0: stage the saved tile pairs Xn and Qt of one chunk with bulk copies
-// completing on `bar` (X receives Xn hi, Xn lo, Qt hi, Qt lo).
+// Thread 0: stage the saved tile pairs Xn and Qt of one chunk (blocked, hi and
+// lo contiguous) with bulk copies completing on `bar`: X receives Xn hi, Xn lo,
+// Qt hi, Qt lo.
 __device__ __forceinline__ void stage_xq(bf16* X, const TcArgs& p, long long blk, uint64_t* bar) {
-  mbar_arrive_expect_tx(bar, 4 * kTileBytes);
-  bulk_g2s(X, p.Xn + blk * kSavedPair, kTileBytes, bar);
-  bulk_g2s(X + kTile, p.Xn + blk * kSavedPair + kSavedTile, kTileBytes, bar);
-  bulk_g2s(X + 2 * kTile, p.Qt + blk * kSavedPair, kTileBytes, bar);
-  bulk_g2s(X + 3 * kTile, p.Qt + blk * kSavedPair + kSavedTile, kTileBytes, bar);
+  mbar_arrive_expect_tx(bar, 4 * umma::kTileBytes);
+  bulk_g2s(X, p.Xn + blk * kSavedPair, 2 * umma::kTileBytes, bar);
+  bulk_g2s(X + 8192, p.Qt + blk * kSavedPair, 2 * umma::kTileBytes, bar);
+}
+
+// The chunk-serial kernels: one CTA per (b, h, 32 value columns), 8 warps.
+// Thread (warp w, lane l < 16) owns row 16*(w%4) + l and columns 16*(w/4)..+15
+// of the CTA's state slice, in fp32 registers; the slice is also kept as a
+// split blocked tile (64 x 32) in shared memory, the B operand of the chunk's
+// MMAs. Per chunk, thread 0 issues the state product and thread 32 the other
+// product (12 and 8-12 tcgen05 MMAs, N = 32) into TMEM; all threads then add
+// them to the state and write the new split tile. The Xn, Qt tiles of the next
+// kRing - 1 chunks are staged by bulk copies.
+constexpr int kChainThreads = 256;
+constexpr int kChainCols = 32;
+constexpr int kSTile = 64 * kChainCols * 2;  // one split half of a 64 x 32 slice, bytes
+
+// 16 fp32 values at g[0..15] -> v (chunks of 8 starting below `valid`; others 0).
+__device__ __forceinline__ void load16_f32(const float* g, int c0, int valid, bool ok, float (&v)[16]) {
+#pragma unroll
+  for (int h = 0; h < 2; ++h) {
+    float4 a = make_float4(0.f, 0.f, 0.f, 0.f), b = a;
+    if (ok && c0 + 8 * h < valid) {
+      a = *reinterpret_cast<const float4*>(g + 8 * h);
+      b = *reinterpret_cast<const float4*>(g + 8 * h + 4);
+    }
+    v[8 * h] = a.x; v[8 * h + 1] = a.y; v[8 * h + 2] = a.z; v[8 * h + 3] = a.w;
+    v[8 * h + 4] = b.x; v[8 * h + 5] = b.y; v[8 * h + 6] = b.z; v[8 * h + 7] = b.w;
+  }
+}
+__device__ __forceinline__ void store16_f32(float* g, int c0, int valid, const float (&v)[16]) {
+#pragma unroll
+  for (int h = 0; h < 2; ++h)
+    if (c0 + 8 * h < valid) {
+      *reinterpret_cast<float4*>(g + 8 * h) = make_float4(v[8 * h], v[8 * h + 1], v[8 * h + 2], v[8 * h + 3]);
+      *reinterpret_cast<float4*>(g + 8 * h + 4) = make_float4(v[8 * h + 4], v[8 * h + 5], v[8 * h + 6], v[8 * h + 7]);
+    }
 }
 
 // ------------------------------------------------------ forward: chain --
-// One CTA per (b, h, value-column split) walks the chunks in order:
 //   S_c saved;  y_c = Qt S_c + Yp;  S_{c+1} = S_c + Xn S_c + Bc
-// State warps (0-7) own 16 x DVS/2 tiles of S in fp32 registers; output warps
-// (8-15) the matching tiles of y. Xn, Qt tiles are staged kRing - 1 chunks
-// ahead by bulk copies; Bc / Yp fragments are loaded into registers a chunk ahead.
-constexpr int kCfStage = 4 * kTileBytes;  // Xn h/l, Qt h/l
-constexpr size_t kChainFwdSmem = 128 + kRing * (size_t)kCfStage + 2 * (size_t)kTileBytes;
+// Both products share the state operand, so [Xn; Qt] is staged as one
+// M = 128 operand (Xn hi, Qt hi, Xn lo, Qt lo) and one thread issues 12 MMAs
+// per chunk. Accumulator row r sits in TMEM lane r: warps 0, 1, 4, 5 (rows
+// 0-63) own the state S, warps 2, 3, 6, 7 (rows 64-127) the output y; lane l of
+// warp w has row 32*(w%4) + l, columns 16*(w/4)..+15.
+// stage: [Xn; Qt] hi and lo (bulk copies) and every thread's 16 additive terms
+// (Bc or Yp; cp.async) as float4 [4][thread]
+constexpr int kCfAddend = 4 * kChainThreads * 16;
+constexpr int kCfStage = 4 * umma::kTileBytes + kCfAddend;
+constexpr size_t kChainFwdSmem = 1024 + kRing * (size_t)kCfStage + 2 * (size_t)kSTile;
 
-template <int DVS>
-__global__ void __launch_bounds__(kSerialThreads, 1) chain_fwd_kernel(const TcArgs p) {
-  constexpr int NT = DVS / 16;
-  extern __shared__ __align__(128) unsigned char smem[];
-  uint64_t* full = reinterpret_cast<uint64_t*>(smem);
-  unsigned char* ring = smem + 128;
+__global__ void __launch_bounds__(kChainThreads, 1) chain_fwd_kernel(const TcArgs p) {
+  namespace um = umma;
+  extern __shared__ __align__(1024) unsigned char csmem[];
+  uint64_t* full = reinterpret_cast<uint64_t*>(csmem);
+  uint64_t* mbar = full + kRing;  // MMA completion
+  uint32_t* tbase_s = reinterpret_cast<uint32_t*>(csmem + 64);
+  unsigned char* ring = csmem + 1024;
   bf16* SH = reinterpret_cast<bf16*>(ring + kRing * kCfStage);
-  bf16* SL = SH + kTile;
+  bf16* SL = SH + 64 * kChainCols;
   auto Xt = [&](int s) { return reinterpret_cast<bf16*>(ring + s * kCfStage); };
 
-  const int tid = threadIdx.x, warp = tid >> 5, mt = warp & 3;
-  const bool state = warp < 8;
-  const int m0 = 16 * mt, n0 = ((warp >> 2) & 1) * (DVS / 2);
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, q = warp & 3;
+  const int cb = 16 * (warp >> 2);
+  const bool st = q < 2;                 // state thread (row r of S) or output thread (row r of y)
+  const int r = 32 * (q & 1) + lane;     // row within S (state) or within the chunk's tokens (y)
   const int split = blockIdx.x % p.S;
   const long long bh = blockIdx.x / p.S;
-  const int c0 = split * p.dvs, ncols = min(p.dvs, p.dv - c0);
-  const int kd = up16(p.dk);
+  const int c0 = split * kChainCols, ncols = min(kChainCols, p.dv - c0);
   const long long blk0 = bh * p.nchunks;
-  bf16* yg = p.y + bh * p.T * p.dv + c0;
-  float* Hsg = p.Hs + blk0 * p.dk * p.dv + c0;
+  bf16* yg = p.y + bh * p.T * p.dv + c0 + cb;
+  float* Hsg = p.Hs + blk0 * p.dk * p.dv + r * p.dv + c0 + cb;
+  const bool srow = st && r < p.dk;
 
-  // this warp's fragment of chunk c's additive term (Bc for state warps, Yp otherwise)
-  auto addend = [&](int c, float (&a)[NT][4]) {
+  auto stage = [&](int c) {
+    bf16* X = Xt(c % kRing);
     const long long t0 = (long long)c * p.C;
-    if (state)
-      frag_from_global(a, p.Bc + (blk0 + c) * 4096 + c0, p.dv, m0, n0, p.dk, ncols);
-    else
-      frag_from_global(a, p.Yp + (blk0 + c) * 4096 + c0, p.dv, m0, n0,
-                       (int)min((long long)p.C, p.T - t0), ncols);
+    const int Cc = (int)min((long long)p.C, p.T - t0);
+    if (tid == 0) {
+      uint64_t* bar = full + c % kRing;
+      const long long blk = blk0 + c;
+      mbar_arrive_expect_tx(bar, 4 * umma::kTileBytes);
+      bulk_g2s(X, p.Xn + blk * kSavedPair, umma::kTileBytes, bar);
+      bulk_g2s(X + 4096, p.Qt + blk * kSavedPair, umma::kTileBytes, bar);
+      bulk_g2s(X + 8192, p.Xn + blk * kSavedPair + 4096, umma::kTileBytes, bar);
+      bulk_g2s(X + 12288, p.Qt + blk * kSavedPair + 4096, umma::kTileBytes, bar);
+    }
+    float4* ad = reinterpret_cast<float4*>(X + 16384);
+    const bool ok = st ? srow : r < Cc;
+    const float* g = (st ? p.Bc : p.Yp) + (blk0 + c) * 4096 + r * p.dv + c0 + cb;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const bool v = ok && cb + 4 * j < ncols;
+      cp_async16(ad + j * kChainThreads + tid, v ? g + 4 * j : p.Bc, v ? 16 : 0);
+    }
+    cp_async_commit();
   };
 
+  if (warp == 0) um::alloc(tbase_s, 32);
   if (tid == 0) {
     for (int s = 0; s < kRing; ++s) mbar_init(full + s, 1);
+    mbar_init(mbar, 1);
     mbar_fence_init();
   }
-  float hs[NT][4];
-  if (state) {
-    if (p.H0)
-      frag_from_global(hs, p.H0 + bh * p.dk * p.dv + c0, p.dv, m0, n0, p.dk, ncols);
-    else
-      tc::zero(hs);
-    tc::store_split(hs, SH, SL, m0, n0, Ident());
-  }
+  float hs[16];  // state threads: S row r, columns cb..cb+15 of the slice
+  load16_f32(p.H0 + bh * p.dk * p.dv + r * p.dv + c0 + cb, cb, ncols, p.H0 != nullptr && srow, hs);
+  if (st) um::store_split16_n(SH, SL, r, cb, kChainCols, kChainCols, hs);
+  um::fence_before();
   __syncthreads();
-  if (tid == 0)
-    for (int c = 0; c < kRing - 1 && c < p.nchunks; ++c) stage_xq(Xt(c), p, blk0 + c, full + c);
-  if (state) frag_to_global(hs, Hsg, p.dv, m0, n0, p.dk, ncols);
-  // additive terms of the next two chunks, loaded two chunks ahead
-  float nxt[NT][4], nxt2[NT][4];
-  addend(0, nxt);
-  if (p.nchunks > 1) addend(1, nxt2);
+  um::fence_after();
+  const uint32_t tb = *tbase_s;
+  const uint32_t lb = tb + ((uint32_t)(32 * q) << 16) + cb;
+  const um::Opnd oS = um::opnd_mn(um::saddr(SH), um::saddr(SL), kChainCols);
+  for (int c = 0; c < kRing - 1 && c < p.nchunks; ++c) stage(c);
+  if (srow) store16_f32(Hsg, cb, ncols, hs);
 
   for (int c = 0; c < p.nchunks; ++c) {
     const int s = c % kRing;
     const long long t0 = (long long)c * p.C;
     const int Cc = (int)min((long long)p.C, p.T - t0);
+    if (c + 1 < p.nchunks)  // the group of chunk c + 1 may still be in flight
+      asm volatile("cp.async.wait_group 1;\n" ::: "memory");
+    else
+      cp_async_wait_all();
     mbar_wait(full + s, (unsigned)(c / kRing) & 1u, &g_sticky_err);
+    fence_proxy_async_smem();  // the split state written below in the previous chunk
+    um::fence_before();
     __syncthreads();  // every thread is past chunk c - 1: its stage may be refilled
-    if (tid == 0 && c + kRing - 1 < p.nchunks) {
-      const int cn = c + kRing - 1;
-      stage_xq(Xt(cn % kRing), p, blk0 + cn, full + cn % kRing);
+    um::fence_after();
+    if (c + kRing - 1 < p.nchunks) stage(c + kRing - 1);
+    const float4* ad = reinterpret_cast<const float4*>(Xt(s) + 16384);
+    if (tid == 0) {  // [Xn; Qt] S, M = 128
+      const uint32_t X = um::saddr(Xt(s));
+      const um::Prod ps[1] = {{tb, um::opnd(X, X + 16384, false), oS, false, true, kChainCols}};
+      um::products(ps);
+      um::commit(mbar);
     }
-    float acc[NT][4];
+    mbar_wait(mbar, (unsigned)c & 1u, &g_sticky_err);
+    um::fence_after();
+    float v[16];
+    um::ld16(lb, v);
 #pragma unroll
-    for (int j = 0; j < NT; ++j)
-#pragma unroll
-      for (int v = 0; v < 4; ++v) {
-        acc[j][v] = nxt[j][v];
-        nxt[j][v] = nxt2[j][v];
-      }
-    if (c + 2 < p.nchunks) addend(c + 2, nxt2);
-    const bf16* X = Xt(s);
-    if (state) {
-#pragma unroll
-      for (int j = 0; j < NT; ++j)
-#pragma unroll
-        for (int v = 0; v < 4; ++v) acc[j][v] += hs[j][v];
-      tc::gemm_k64<NT, false, true>(acc, Op{X, X + kTile}, m0, Op{SH, SL}, n0);
-#pragma unroll
-      for (int j = 0; j < NT; ++j)
-#pragma unroll
-        for (int v = 0; v < 4; ++v) hs[j][v] = acc[j][v];
-    } else {
-      tc::gemm_k64<NT, false, true>(acc, Op{X + 2 * kTile, X + 3 * kTile}, m0, Op{SH, SL}, n0);
-      frag_to_global_bf16(acc, yg + t0 * p.dv, p.dv, m0, n0, Cc, ncols);
+    for (int j = 0; j < 4; ++j) {
+      const float4 a4 = ad[j * kChainThreads + tid];
+      v[4 * j] += a4.x;
+      v[4 * j + 1] += a4.y;
+      v[4 * j + 2] += a4.z;
+      v[4 * j + 3] += a4.w;
     }
-    __syncthreads();
-    if (state) {
-      tc::store_split(hs, SH, SL, m0, n0, Ident());
-      if (c + 1 < p.nchunks)  // S_{c+1}, off the critical path
-        frag_to_global(hs, Hsg + (long long)(c + 1) * p.dk * p.dv, p.dv, m0, n0, p.dk, ncols);
+    if (st) {
+#pragma unroll
+      for (int i = 0; i < 16; ++i) hs[i] += v[i];
+      um::store_split16_n(SH, SL, r, cb, kChainCols, kChainCols, hs);
+      if (srow && c + 1 < p.nchunks) store16_f32(Hsg + (long long)(c + 1) * p.dk * p.dv, cb, ncols, hs);
+    } else if (r < Cc) {
+#pragma unroll
+      for (int h = 0; h < 2; ++h)
+        if (cb + 8 * h < ncols) {
+          uint32_t w[4];
+#pragma unroll
+          for (int i = 0; i < 4; ++i) w[i] = tc::pack_bf16(v[8 * h + 2 * i], v[8 * h + 2 * i + 1]);
+          *reinterpret_cast<uint4*>(yg + (t0 + r) * p.dv + 8 * h) = make_uint4(w[0], w[1], w[2], w[3]);
+        }
     }
   }
-  if (state) frag_to_global(hs, p.HT + bh * p.dk * p.dv + c0, p.dv, m0, n0, p.dk, ncols);
+  if (srow) store16_f32(p.HT + bh * p.dk * p.dv + r * p.dv + c0 + cb, cb, ncols, hs);
+  um::fence_before();
+  __syncthreads();
+  if (warp == 0) {
+    um::fence_after();
+    um::dealloc(tb, 32);
+  }
 }
 
 // ----------------------------------------------------- backward: chain --
-// One CTA per (b, h, split) walks the chunks in reverse carrying dS:
-//   dS'_c (= dS entering from chunk c + 1) saved;
-//   dS_c = dS'_c + Xn^T dS'_c + Qt^T dy_c
-// State warps (0-7) own dS tiles in fp32 registers; warps 8-15 form Qt^T dy
-// (independent of dS) into shared memory in the same step. Xn, Qt by bulk
-// copies and dy by cp.async, kRing - 1 chunks ahead.
-constexpr int kCbStage = 5 * kTileBytes;  // Xn h/l, Qt h/l, dy
-constexpr size_t kChainBwdSmem =
-    128 + kRing * (size_t)kCbStage + 2 * (size_t)kTileBytes + kF32Bytes;
+//   dS'_c (= dS entering from chunk c + 1) saved;  dS_c = dS'_c + Xn^T dS'_c + Qt^T dy_c
+constexpr int kCbStage = 4 * umma::kTileBytes + kSTile;  // Xn h/l, Qt h/l, dy (64 x 32)
+constexpr size_t kChainBwdSmem = 1024 + kRing * (size_t)kCbStage + 2 * (size_t)kSTile;
 
-template <int DVS>
-__global__ void __launch_bounds__(kSerialThreads, 1) chain_bwd_kernel(const TcArgs p) {
-  constexpr int NT = DVS / 16;
-  constexpr int NTH = kSerialThreads;
-  extern __shared__ __align__(128) unsigned char smem[];
-  uint64_t* full = reinterpret_cast<uint64_t*>(smem);
-  unsigned char* ring = smem + 128;
+__global__ void __launch_bounds__(kChainThreads, 1) chain_bwd_kernel(const TcArgs p) {
+  namespace um = umma;
+  extern __shared__ __align__(1024) unsigned char csmem[];
+  uint64_t* full = reinterpret_cast<uint64_t*>(csmem);
+  uint64_t* mbar = full + kRing;
+  uint32_t* tbase_s = reinterpret_cast<uint32_t*>(csmem + 64);
+  unsigned char* ring = csmem + 1024;
   bf16* DH = reinterpret_cast<bf16*>(ring + kRing * kCbStage);
-  bf16* DL = DH + kTile;
-  float* Gf = reinterpret_cast<float*>(DL + kTile);  // Qt^T dy, [64][kTld]
+  bf16* DL = DH + 64 * kChainCols;
   auto Xt = [&](int s) { return reinterpret_cast<bf16*>(ring + s * kCbStage); };
 
-  const int tid = threadIdx.x, warp = tid >> 5, mt = warp & 3;
-  const bool state = warp < 8;
-  const int m0 = 16 * mt, n0 = ((warp >> 2) & 1) * (DVS / 2);
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, q = warp & 3;
+  const int row = 16 * q + lane, cb = 16 * (warp >> 2);
+  const bool rv = lane < 16;
   const int split = blockIdx.x % p.S;
   const long long bh = blockIdx.x / p.S;
-  const int c0 = split * p.dvs, ncols = min(p.dvs, p.dv - c0);
-  const int kd = up16(p.dk);
+  const int c0 = split * kChainCols, ncols = min(kChainCols, p.dv - c0);
   const long long blk0 = bh * p.nchunks;
   const bf16* dyg = p.dy + bh * p.T * p.dv + c0;
-  float* dHsg = p.dHs + blk0 * p.dk * p.dv + c0;
+  float* dHsg = p.dHs + blk0 * p.dk * p.dv + row * p.dv + c0 + cb;
+  const bool srow = rv && row < p.dk;
   const int last = p.nchunks - 1;
 
   // step qq handles chunk last - qq in ring slot qq % kRing
@@ -1037,69 +1092,79 @@ __global__ void __launch_bounds__(kSerialThreads, 1) chain_bwd_kernel(const TcAr
     bf16* X = Xt(qq % kRing);
     if (tid == 0) stage_xq(X, p, blk0 + c, full + qq % kRing);
     const long long t0 = (long long)c * p.C;
-    stage_rows<DVS / 8, NTH>(X + 4 * kTile, dyg + t0 * p.dv, p.dv,
-                             (int)min((long long)p.C, p.T - t0), ncols >> 3);
+    const int Cc = (int)min((long long)p.C, p.T - t0);
+    bf16* dY = X + 16384;
+    const int r = tid >> 2, ch = tid & 3;  // 64 rows x 4 chunks of 8 columns
+    const bool ok = r < Cc && 8 * ch < ncols;
+    const bf16* src = dyg + (t0 + r) * p.dv + 8 * ch;
+    cp_async16(dY + um::boff_n(r, 8 * ch, kChainCols), ok ? src : dyg, ok ? 16 : 0);
     cp_async_commit();
   };
 
+  if (warp == 0) um::alloc(tbase_s, 64);
   if (tid == 0) {
     for (int s = 0; s < kRing; ++s) mbar_init(full + s, 1);
+    mbar_init(mbar, 2);
     mbar_fence_init();
   }
-  float ds[NT][4];
-  if (state) {
-    if (p.dHT)
-      frag_from_global(ds, p.dHT + bh * p.dk * p.dv + c0, p.dv, m0, n0, p.dk, ncols);
-    else
-      tc::zero(ds);
-    tc::store_split(ds, DH, DL, m0, n0, Ident());
-  }
+  float ds[16];
+  load16_f32(p.dHT + bh * p.dk * p.dv + row * p.dv + c0 + cb, cb, ncols, p.dHT != nullptr && srow, ds);
+  if (rv) um::store_split16_n(DH, DL, row, cb, kChainCols, kChainCols, ds);
+  um::fence_before();
   __syncthreads();
+  um::fence_after();
+  const uint32_t tb = *tbase_s, tX = tb, tY = tb + 32;
+  const uint32_t lb = tb + ((uint32_t)(32 * q) << 16) + cb;
   for (int qq = 0; qq < kRing - 1 && qq <= last; ++qq) stage(qq);
-  if (state) frag_to_global(ds, dHsg + (long long)last * p.dk * p.dv, p.dv, m0, n0, p.dk, ncols);
+  if (srow) store16_f32(dHsg + (long long)last * p.dk * p.dv, cb, ncols, ds);
+  const um::Opnd oD = um::opnd_mn(um::saddr(DH), um::saddr(DL), kChainCols);
 
   for (int qq = 0; qq <= last; ++qq) {
     const int c = last - qq, s = qq % kRing;
-    const long long t0 = (long long)c * p.C;
-    const int Cc = (int)min((long long)p.C, p.T - t0);
     if (qq < last)  // the group of step qq + 1 may still be in flight
       asm volatile("cp.async.wait_group 1;\n" ::: "memory");
     else
       cp_async_wait_all();
     mbar_wait(full + s, (unsigned)(qq / kRing) & 1u, &g_sticky_err);
+    fence_proxy_async_smem();  // dy (cp.async) and the split dS written in the previous step
+    um::fence_before();
     __syncthreads();
+    um::fence_after();
     if (qq + kRing - 1 <= last) stage(qq + kRing - 1);
-    const bf16* X = Xt(s);
-    float acc[NT][4];
-    if (state) {
-#pragma unroll
-      for (int j = 0; j < NT; ++j)
-#pragma unroll
-        for (int v = 0; v < 4; ++v) acc[j][v] = ds[j][v];
-      tc::gemm_k64<NT, true, true>(acc, Op{X, X + kTile}, m0, Op{DH, DL}, n0);
-    } else {
-      tc::zero(acc);
-      tc::gemm_k64<NT, true, true>(acc, Op{X + 2 * kTile, X + 3 * kTile}, m0,
-                                   Op{X + 4 * kTile, nullptr}, n0);
-#pragma unroll
-      for (int j = 0; j < NT; ++j)
-#pragma unroll
-        for (int v = 0; v < 4; ++v)
-          Gf[tc::frag_row(m0, v) * kTld + tc::frag_col(n0, j, v)] = acc[j][v];
+    const uint32_t X = um::saddr(Xt(s));
+    if (tid == 0) {  // Xn^T dS'
+      const um::Prod ps[1] = {{tX, um::opnd(X, X + 8192, true), oD, false, false, kChainCols}};
+      um::products(ps);
+      um::commit(mbar);
+    } else if (tid == 32) {  // Qt^T dy
+      const um::Prod ps[1] = {{tY, um::opnd(X + 16384, X + 24576, true),
+                               um::opnd_mn(X + 32768, 0, kChainCols), false, false, kChainCols}};
+      um::products(ps);
+      um::commit(mbar);
     }
-    __syncthreads();
-    if (state) {
+    mbar_wait(mbar, (unsigned)qq & 1u, &g_sticky_err);
+    um::fence_after();
+    uint32_t rx[16], ry[16];
+    float xs[16], ys[16];
+    um::ld16_async(lb, rx);
+    um::ld16_async(lb + 32, ry);
+    um::ld_wait();
+    um::ld_bind(rx, xs);
+    um::ld_bind(ry, ys);
+    if (rv) {
 #pragma unroll
-      for (int j = 0; j < NT; ++j)
-#pragma unroll
-        for (int v = 0; v < 4; ++v)
-          ds[j][v] = acc[j][v] + Gf[tc::frag_row(m0, v) * kTld + tc::frag_col(n0, j, v)];
-      tc::store_split(ds, DH, DL, m0, n0, Ident());
-      if (c > 0)  // dS'_{c-1}, off the critical path
-        frag_to_global(ds, dHsg + (long long)(c - 1) * p.dk * p.dv, p.dv, m0, n0, p.dk, ncols);
+      for (int i = 0; i < 16; ++i) ds[i] += xs[i] + ys[i];
+      um::store_split16_n(DH, DL, row, cb, kChainCols, kChainCols, ds);
     }
+    if (srow && c > 0) store16_f32(dHsg + (long long)(c - 1) * p.dk * p.dv, cb, ncols, ds);
   }
-  if (state) frag_to_global(ds, p.dH0 + bh * p.dk * p.dv + c0, p.dv, m0, n0, p.dk, ncols);
+  if (srow) store16_f32(p.dH0 + bh * p.dk * p.dv + row * p.dv + c0 + cb, cb, ncols, ds);
+  um::fence_before();
+  __syncthreads();
+  if (warp == 0) {
+    um::fence_after();
+    um::dealloc(tb, 64);
+  }
 }
 
 // ---------------------------------------------------------------- host --
@@ -1174,9 +1239,8 @@ int run_tc(bool fwd, const Args<__nv_bfloat16>& p, long long B, int H, long long
   a.dv = dv;
   a.C = C;
   a.nchunks = (int)((T + C - 1) / C);
-  a.S = splits_for(BH, dv);
-  a.dvs = ((dv + a.S - 1) / a.S + 7) & ~7;
-  const bool narrow = a.dvs <= 32;
+  a.S = (dv + kChainCols - 1) / kChainCols;  // chain kernels: 32 value columns per CTA
+  a.dvs = kChainCols;
   if (BH == 0) return MGS_OK;
   if (saved == nullptr) return MGS_BAD_SHAPE;
   const size_t ncs = (size_t)BH * a.nchunks;
@@ -1199,8 +1263,7 @@ int run_tc(bool fwd, const Args<__nv_bfloat16>& p, long long B, int H, long long
     a.Yp = a.Bc + ncs * 4096;
     const int rc = launch_tc(prep_kernel, (long long)ncs, kPrepSmem, st, a, kPrepThreads);
     if (rc != MGS_OK) return rc;
-    return narrow ? launch_tc(chain_fwd_kernel<32>, BH * a.S, kChainFwdSmem, st, a, kSerialThreads)
-                  : launch_tc(chain_fwd_kernel<64>, BH * a.S, kChainFwdSmem, st, a, kSerialThreads);
+    return launch_tc(chain_fwd_kernel, BH * a.S, kChainFwdSmem, st, a, kChainThreads);
   }
   if (T == 0) {
     if (p.dHT)
@@ -1211,8 +1274,7 @@ int run_tc(bool fwd, const Args<__nv_bfloat16>& p, long long B, int H, long long
     return MGS_OK;
   }
   a.dHs = static_cast<float*>(ws);
-  int rc = narrow ? launch_tc(chain_bwd_kernel<32>, BH * a.S, kChainBwdSmem, st, a, kSerialThreads)
-                  : launch_tc(chain_bwd_kernel<64>, BH * a.S, kChainBwdSmem, st, a, kSerialThreads);
+  int rc = launch_tc(chain_bwd_kernel, BH * a.S, kChainBwdSmem, st, a, kChainThreads);
   if (rc != MGS_OK) return rc;
   return launch_tc(bwd_grads_kernel, BH * a.nchunks, kGradSmem, st, a, kGradThreads);
 }

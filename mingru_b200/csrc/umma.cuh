@@ -43,12 +43,13 @@ __device__ __forceinline__ uint64_t desc_mn(uint32_t tile, int kk) {
   return desc(tile + kk * 2048, 1024, 128);
 }
 
-// Instruction descriptor: bf16 x bf16 -> fp32, N = 64, M = 64 (or 128: two
-// blocked tiles stacked in consecutive memory, row m of D in TMEM lane m),
-// operand majors.
-__host__ __device__ constexpr uint32_t idesc64(bool a_mn, bool b_mn, bool m128 = false) {
+// Instruction descriptor: bf16 x bf16 -> fp32, N columns (a multiple of 16,
+// default 64), M = 64 (or 128: two blocked tiles stacked in consecutive
+// memory, row m of D in TMEM lane m), operand majors.
+__host__ __device__ constexpr uint32_t idesc64(bool a_mn, bool b_mn, bool m128 = false,
+                                               uint32_t n = 64) {
   return (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)a_mn << 15) | ((uint32_t)b_mn << 16) |
-         ((64u >> 3) << 17) | ((m128 ? 128u >> 4 : 64u >> 4) << 24);
+         ((n >> 3) << 17) | ((m128 ? 128u >> 4 : 64u >> 4) << 24);
 }
 
 __device__ __forceinline__ void mma(uint32_t d, uint64_t a, uint64_t b, uint32_t idesc, bool acc) {
@@ -69,6 +70,23 @@ struct Opnd {
   bool mn;
 };
 
+// MN-major operand from a blocked tile of `cols` columns (a multiple of 8;
+// rows are the contraction dimension, 64 of them): row-block stride cols*16 B.
+__device__ __forceinline__ Opnd opnd_mn(uint32_t hi_addr, uint32_t lo_addr, int cols) {
+  Opnd o;
+  o.mn = true;
+  const uint32_t rb = (uint32_t)cols * 16;
+  o.step = 2 * rb / 16;
+  o.hi = desc(hi_addr, rb, 128);
+  o.lo = lo_addr == 0 ? 0 : desc(lo_addr, rb, 128);
+  return o;
+}
+
+// Element offset of (r, c) in a blocked tile of `cols` columns.
+__device__ __forceinline__ int boff_n(int r, int c, int cols) {
+  return (r >> 3) * (cols * 8) + (c >> 3) * 64 + (r & 7) * 8 + (c & 7);
+}
+
 // Operand from tile addresses (lo_addr == 0: no lo term).
 __device__ __forceinline__ Opnd opnd(uint32_t hi_addr, uint32_t lo_addr, bool mn) {
   Opnd o;
@@ -86,6 +104,7 @@ struct Prod {
   Opnd A, B;
   bool accumulate;
   bool m128 = false;
+  uint32_t n = 64;  // columns of D (B's MN extent)
 };
 
 // Issue a batch of independent products (one thread) k-step by k-step,
@@ -100,7 +119,7 @@ __device__ __forceinline__ void products(const Prod (&ps)[N]) {
 #pragma unroll
     for (int i = 0; i < N; ++i) {
       const Prod& p = ps[i];
-      const uint32_t id = idesc64(p.A.mn, p.B.mn, p.m128);
+      const uint32_t id = idesc64(p.A.mn, p.B.mn, p.m128, p.n);
       const uint64_t oa = (uint64_t)(kk * p.A.step), ob = (uint64_t)(kk * p.B.step);
       mma(p.d, p.A.hi + oa, p.B.hi + ob, id, kk > 0 || p.accumulate);
       if (p.B.lo) mma(p.d, p.A.hi + oa, p.B.lo + ob, id, true);
@@ -200,6 +219,29 @@ __device__ __forceinline__ void store_split16(__nv_bfloat16* hi, __nv_bfloat16* 
     const int o = boff(r, c0 + 8 * h);
     *reinterpret_cast<uint4*>(hi + o) = make_uint4(ph[0], ph[1], ph[2], ph[3]);
     if (lo) *reinterpret_cast<uint4*>(lo + o) = make_uint4(pl[0], pl[1], pl[2], pl[3]);
+  }
+}
+
+// store_split16 for a blocked tile of `cols` columns (chunks of 8 columns
+// at c0 and c0 + 8; a chunk is written only if it starts below `valid`).
+__device__ __forceinline__ void store_split16_n(__nv_bfloat16* hi, __nv_bfloat16* lo, int r, int c0,
+                                                int cols, int valid, const float (&v)[16]) {
+#pragma unroll
+  for (int h = 0; h < 2; ++h) {
+    if (c0 + 8 * h >= valid) continue;
+    uint32_t ph[4], pl[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const float x0 = v[8 * h + 2 * i], x1 = v[8 * h + 2 * i + 1];
+      __nv_bfloat162 b = __floats2bfloat162_rn(x0, x1);
+      const float2 f = __bfloat1622float2(b);
+      __nv_bfloat162 l = __floats2bfloat162_rn(x0 - f.x, x1 - f.y);
+      ph[i] = *reinterpret_cast<uint32_t*>(&b);
+      pl[i] = *reinterpret_cast<uint32_t*>(&l);
+    }
+    const int o = boff_n(r, c0 + 8 * h, cols);
+    *reinterpret_cast<uint4*>(hi + o) = make_uint4(ph[0], ph[1], ph[2], ph[3]);
+    *reinterpret_cast<uint4*>(lo + o) = make_uint4(pl[0], pl[1], pl[2], pl[3]);
   }
 }
 
