@@ -53,8 +53,6 @@ using tc::Op;
 constexpr int kTcThreads = 256;
 constexpr int kTile = 64 * kLd;            // bf16 elements of one 64 x 64 tile
 constexpr int kTileBytes = kTile * 2;      // 9216
-constexpr int kTld = 66;                   // fp32 leading dimension of T / T^{-1}
-constexpr int kF32Bytes = 64 * kTld * 4;   // 16896
 constexpr int kTdBytes = 4 * 16 * 17 * 4;  // T's four diagonal 16 x 16 blocks, fp32, padded rows
 // Tiles kept in `saved` (T^{-1}, Xn, Qt) use the shared-memory layout (64 rows
 // of kLd elements), so one contiguous bulk copy stages a tile.
@@ -72,20 +70,6 @@ __device__ __forceinline__ void cp_async_commit() {
 }
 __device__ __forceinline__ void cp_async_wait_all() {
   asm volatile("cp.async.wait_group 0;\n" ::: "memory");
-}
-
-__device__ __forceinline__ int up16(int x) { return (x + 15) & ~15; }
-
-// 64 rows x (NCH * 8 columns) bf16 block of a row-major global matrix (leading
-// dimension ld elements) into a tile; rows >= nrows / chunks >= ncols8 zero.
-template <int NCH, int NTHR = kTcThreads>
-__device__ __forceinline__ void stage_rows(bf16* tile, const bf16* g, long long ld, int nrows,
-                                           int valid_ch) {
-  for (int i = threadIdx.x; i < 64 * NCH; i += NTHR) {
-    const int row = i / NCH, ch = i - row * NCH;
-    const bool ok = row < nrows && ch < valid_ch;
-    cp_async16(tile + row * kLd + ch * 8, ok ? g + row * ld + ch * 8 : g, ok ? 16 : 0);
-  }
 }
 
 struct Ident {
@@ -167,61 +151,6 @@ __device__ void zero_upper_blocks(bf16* H, bf16* L) {
   }
 }
 
-// Shared tile <-> saved global tile (same padded layout; 16-byte vectors, all threads).
-template <int NTHR = kTcThreads>
-__device__ __forceinline__ void tile_to_global(const bf16* t, bf16* g) {
-  for (int i = threadIdx.x; i < kTileBytes / 16; i += NTHR)
-    reinterpret_cast<uint4*>(g)[i] = reinterpret_cast<const uint4*>(t)[i];
-}
-template <int NTHR = kTcThreads>
-__device__ __forceinline__ void tile_from_global_async(bf16* t, const bf16* g) {
-  for (int i = threadIdx.x; i < kTileBytes / 16; i += NTHR) cp_async16(t + i * 8, g + i * 8, 16);
-}
-
-
-// c[nt] tile rows m0, cols n0 (fragment layout) -> fp32 global matrix (ld),
-// rows < nrows, cols < ncols.
-template <int NT>
-__device__ __forceinline__ void frag_to_global(const float (&c)[NT][4], float* g, long long ld,
-                                               int m0, int n0, int nrows, int ncols) {
-#pragma unroll
-  for (int j = 0; j < NT; ++j)
-#pragma unroll
-    for (int h = 0; h < 2; ++h) {
-      const int row = tc::frag_row(m0, 2 * h), col = tc::frag_col(n0, j, 0);
-      if (row < nrows && col < ncols)
-        *reinterpret_cast<float2*>(g + row * ld + col) = make_float2(c[j][2 * h], c[j][2 * h + 1]);
-    }
-}
-
-template <int NT>
-__device__ __forceinline__ void frag_to_global_bf16(const float (&c)[NT][4], bf16* g, long long ld,
-                                                    int m0, int n0, int nrows, int ncols) {
-#pragma unroll
-  for (int j = 0; j < NT; ++j)
-#pragma unroll
-    for (int h = 0; h < 2; ++h) {
-      const int row = tc::frag_row(m0, 2 * h), col = tc::frag_col(n0, j, 0);
-      if (row < nrows && col < ncols)
-        *reinterpret_cast<uint32_t*>(g + row * ld + col) = tc::pack_bf16(c[j][2 * h], c[j][2 * h + 1]);
-    }
-}
-
-template <int NT>
-__device__ __forceinline__ void frag_from_global(float (&c)[NT][4], const float* g, long long ld,
-                                                 int m0, int n0, int nrows, int ncols) {
-#pragma unroll
-  for (int j = 0; j < NT; ++j)
-#pragma unroll
-    for (int h = 0; h < 2; ++h) {
-      const int row = tc::frag_row(m0, 2 * h), col = tc::frag_col(n0, j, 0);
-      float2 v = make_float2(0.f, 0.f);
-      if (row < nrows && col < ncols) v = *reinterpret_cast<const float2*>(g + row * ld + col);
-      c[j][2 * h] = v.x;
-      c[j][2 * h + 1] = v.y;
-    }
-}
-
 struct TcArgs {
   const bf16* Q;
   const bf16* K;
@@ -247,8 +176,6 @@ struct TcArgs {
   long long T;
   int nh, dk, dv, C, nchunks, S, dvs;
 };
-
-constexpr int kSerialThreads = 512;  // 16 warps in the chunk-serial kernels
 
 // ----------------------------------------------------- backward: grads --
 // One CTA per (b, h, chunk), two CTAs per SM: every gradient of the chunk from
@@ -1169,19 +1096,6 @@ __global__ void __launch_bounds__(kChainThreads, 1) chain_bwd_kernel(const TcArg
 
 // ---------------------------------------------------------------- host --
 
-int sm_count() {
-  int dev = 0, n = 0;
-  if (cudaGetDevice(&dev) != cudaSuccess) return 148;
-  if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0)
-    return 148;
-  return n;
-}
-
-// Value-column splits per (b, h) for the chunk-serial kernels: two when that
-// still fits one wave of SMs (halves each CTA's serial work), else one.
-int splits_for(long long BH, int dv) {
-  return (dv > 32 && 2 * BH <= (long long)sm_count()) ? 2 : 1;
-}
 
 template <class K>
 int launch_tc(K kernel, long long grid, size_t smem, cudaStream_t st, const TcArgs& a,

@@ -178,50 +178,6 @@ __device__ __forceinline__ void gemm(float (&c)[NT][4], Op A, int m0, Op B, int 
   }
 }
 
-// c += A(m0.., 0:64) * B(0:64, n0..): the 64-deep product of gemm with the
-// 16-wide k-steps spread over KP = 4 (NT <= 2) or 2 separate accumulators, so a
-// warp issues independent mma chains per n-tile instead of one chain of
-// 4 x (terms) dependent mma; used on the latency-bound chunk-serial paths.
-template <int NT, bool ACOL, bool BKN>
-__device__ __forceinline__ void gemm_k64(float (&c)[NT][4], Op A, int m0, Op B, int n0) {
-  static_assert(NT % 2 == 0, "n-tiles come in pairs");
-  constexpr int KP = NT <= 2 ? 4 : 2;
-  float part[KP][NT][4];
-#pragma unroll
-  for (int kp = 0; kp < KP; ++kp)
-#pragma unroll
-    for (int j = 0; j < NT; ++j) part[kp][j][0] = part[kp][j][1] = part[kp][j][2] = part[kp][j][3] = 0.f;
-#pragma unroll
-  for (int kk = 0; kk < 4; ++kk) {
-    float (&pk)[NT][4] = part[kk % KP];
-    uint32_t ah[4], al[4];
-    load_a<ACOL>(A.hi, m0, 16 * kk, ah);
-    if (A.lo) load_a<ACOL>(A.lo, m0, 16 * kk, al);
-#pragma unroll
-    for (int j = 0; j < NT; j += 2) {
-      uint32_t bh[4], bl[4];
-      load_b<BKN>(B.hi, 16 * kk, n0 + 8 * j, bh);
-      mma(pk[j], ah, bh[0], bh[1]);
-      mma(pk[j + 1], ah, bh[2], bh[3]);
-      if (B.lo) {
-        load_b<BKN>(B.lo, 16 * kk, n0 + 8 * j, bl);
-        mma(pk[j], ah, bl[0], bl[1]);
-        mma(pk[j + 1], ah, bl[2], bl[3]);
-      }
-      if (A.lo) {
-        mma(pk[j], al, bh[0], bh[1]);
-        mma(pk[j + 1], al, bh[2], bh[3]);
-      }
-    }
-  }
-#pragma unroll
-  for (int kp = 0; kp < KP; ++kp)
-#pragma unroll
-    for (int j = 0; j < NT; ++j)
-#pragma unroll
-      for (int v = 0; v < 4; ++v) c[j][v] += part[kp][j][v];
-}
-
 template <int NT>
 __device__ __forceinline__ void zero(float (&c)[NT][4]) {
 #pragma unroll
