@@ -11,12 +11,14 @@
 // Three algorithms, chosen per shape (the same choice for forward and
 // backward, since the forward's carries feed the backward):
 //  * strip (wide problems, B*ceil(D/32) >= 2 x #SMs, rows 16-byte aligned):
-//    every CTA owns 32-channel strips and walks them through all of T. A
-//    producer warp streams 32-step chunks of the strip into a shared-memory
-//    ring with cp.async.bulk (mbarrier completion); four consumer warps scan
-//    a chunk (8 steps each, serial in registers), compose the per-warp
-//    aggregates through shared memory and carry the strip state on-chip from
-//    chunk to chunk. No global synchronisation at all.
+//    32-channel strips walk all of T, their 32-step chunks streamed by TMA
+//    into shared-memory rings (mbarrier completion); no global
+//    synchronisation. fp32: one warp per strip runs the recurrence itself
+//    (lane = channel, one FMA per step) and writes each chunk's results back
+//    by TMA box stores -- HBM-bound. 16-bit: the per-step latency of that
+//    walk, not HBM, would bound it, so four consumer warps split each chunk
+//    (8 steps each), compose their aggregates through shared memory and carry
+//    the strip state from chunk to chunk, fed by a producer warp.
 //  * direct-vec (narrow problems, rows 16-byte aligned): one tile (64 steps x
 //    128 channels, 4 channels per lane, 16-byte accesses) per CTA, chunk
 //    carries across CTAs by windowed decoupled look-back.
@@ -32,6 +34,9 @@ namespace mgs {
 namespace linear {
 
 constexpr int kLc = 32;  // carry-chunk length = backward tile length (all algorithms)
+constexpr int kStripNW = 4;                      // consumer warps per strip (16-bit path)
+constexpr int kStripS = kLc / kStripNW;          // steps per consumer warp and chunk
+constexpr int kRingBytes = 50 * 1024;            // shared-memory ring per CTA (4 CTAs per SM)
 
 // direct paths
 constexpr int kVecCpt = 4;                       // channels per lane, direct-vec
@@ -43,9 +48,6 @@ static_assert((kVecFwdS * kVecFwdNW) % kLc == 0 && kLc % kVecFwdS == 0, "vec car
 static_assert((kSclFwdS * kSclFwdNW) % kLc == 0 && kLc % kSclFwdS == 0, "scalar carry grid");
 
 // strip path
-constexpr int kStripNW = 4;                      // consumer warps
-constexpr int kStripS = kLc / kStripNW;          // steps per consumer warp and chunk
-constexpr int kRingBytes = 50 * 1024;            // shared-memory ring per CTA (4 CTAs per SM)
 
 enum Algo { kStrip = 0, kDirectVec = 1, kDirectScalar = 2 };
 
@@ -152,6 +154,7 @@ struct Args {
 // 32 channels x kLc steps (forward: a, b; backward: a, b, gA, gBc).
 struct StripMaps {
   CUtensorMap m[4];
+  CUtensorMap out[2];  // strip path: the two results (A, Bc or da, db), same boxes
 };
 
 // ------------------------------------------------------ shared step maths --
@@ -417,7 +420,241 @@ __global__ void __launch_bounds__(NW * 32) bwd_direct_kernel(Args<E> p) {
 
 // ------------------------------------------------------------- strip path --
 //
-// One CTA = kStripNW consumer warps + 1 producer warp, persistent over
+// One warp per 32-channel strip walks all of T with the recurrence itself
+// (lane = channel): no aggregates and no exchange between warps. Each warp
+// streams its strip's kLc-step chunks (TMA boxes of 32 channels x kLc steps;
+// backward: plus the chunk's forward carry) through a private ring of NST
+// stages in shared memory; lane 0 refills a stage with the chunk NST ahead as
+// soon as the warp has read it. Strips are dealt to warps CTA-first (strip =
+// warp * gridDim.x + blockIdx.x, then + kWsWarps * gridDim.x), so the SMs'
+// strip counts differ by at most one. The forward writes the strip state at
+// every chunk start (the carries); the backward recomputes each chunk's states
+// from them in registers and carries the adjoint in reverse.
+
+constexpr int kWsWarps = 4;
+constexpr size_t kWsRingPerWarp = 50 * 1024;
+
+// Per warp: NST input stages and two output buffers (the chunk's two result
+// arrays, written back by TMA box stores while the next chunk is computed).
+template <typename E, int NIN, bool WITH_CARRY>
+struct WsStage {
+  static constexpr size_t kArrayBytes = (size_t)kLc * 32 * sizeof(E);
+  static constexpr size_t kCarryBytes = WITH_CARRY ? 2 * 32 * sizeof(float) : 0;
+  static constexpr size_t kBytes = (NIN * kArrayBytes + kCarryBytes + 127) / 128 * 128;
+  static constexpr size_t kOutBytes = 2 * kArrayBytes;  // one output buffer (two arrays)
+  static constexpr int kFit = (int)((kWsRingPerWarp - 2 * kOutBytes) / kBytes);
+  static constexpr int kStages = kFit > 8 ? 8 : kFit;
+  static constexpr size_t kWarpBytes = kStages * kBytes + 2 * kOutBytes;
+  static constexpr size_t kSmem = (size_t)kWsWarps * kWarpBytes;
+};
+
+// Per-warp ring bookkeeping (lane 0 issues, every lane waits): chunk j of the
+// warp's whole sequence uses slot j % NST with phase (j / NST) & 1.
+template <int NST>
+struct WsRing {
+  uint64_t* full;
+  unsigned pending = 0u, pend_ph = 0u;  // slots issued and not yet waited for
+  __device__ void issued(int s, unsigned ph) {
+    pending |= 1u << s;
+    pend_ph = (pend_ph & ~(1u << s)) | (ph << s);
+  }
+  __device__ bool wait(int s, unsigned ph, unsigned* err) {
+    pending &= ~(1u << s);
+    return mbar_wait(&full[s], ph, err);
+  }
+  // After a failed wait: let every copy still in flight land before exiting.
+  __device__ void drain(unsigned* err) {
+    for (int i = 0; i < NST; ++i)
+      if (pending & (1u << i)) mbar_wait(&full[i], (pend_ph >> i) & 1u, err);
+  }
+};
+
+template <typename E>
+__global__ void __launch_bounds__(kWsWarps * 32, 1)
+    fwd_strip_kernel(Args<E> p, const __grid_constant__ StripMaps maps) {
+  using SS = WsStage<E, 2, false>;
+  constexpr int NST = SS::kStages;
+  extern __shared__ __align__(128) unsigned char ring[];
+  __shared__ __align__(8) uint64_t full[kWsWarps][NST];
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  if (lane == 0) {
+    for (int i = 0; i < NST; ++i) mbar_init(&full[warp][i], 1);
+    mbar_fence_init();
+    tma_prefetch_desc(&maps.m[0]);
+    tma_prefetch_desc(&maps.m[1]);
+  }
+  __syncwarp();
+  unsigned char* wring = ring + (size_t)warp * SS::kWarpBytes;
+  unsigned char* wout = wring + (size_t)NST * SS::kBytes;  // two output buffers
+  WsRing<NST> rg;
+  rg.full = full[warp];
+  long long j0 = 0;  // chunks of earlier strips taken by this warp
+  for (long long strip = (long long)warp * gridDim.x + blockIdx.x; strip < p.nstrips;
+       strip += (long long)kWsWarps * gridDim.x) {
+    const long long bi = strip / p.sper;
+    const int d0 = (int)((strip - bi * p.sper) * 32);
+    auto issue = [&](long long c) {  // lane 0: chunk c of this strip
+      const long long j = j0 + c;
+      const int s = (int)(j % NST);
+      unsigned char* st = wring + (size_t)s * SS::kBytes;
+      mbar_arrive_expect_tx(&rg.full[s], (unsigned)(2 * SS::kArrayBytes));
+      tma_load_3d(st, &maps.m[0], d0, (int)(c * kLc), (int)bi, &rg.full[s]);
+      tma_load_3d(st + SS::kArrayBytes, &maps.m[1], d0, (int)(c * kLc), (int)bi, &rg.full[s]);
+      rg.issued(s, (unsigned)(j / NST) & 1u);
+    };
+    if (lane == 0)
+      for (long long c = 0; c < NST && c < p.nchunks; ++c) issue(c);
+    float A = 1.f, Bv = 0.f;
+    for (long long c = 0; c < p.nchunks; ++c) {
+      const long long j = j0 + c;
+      const int s = (int)(j % NST);
+      if (!rg.wait(s, (unsigned)(j / NST) & 1u, p.lb.err)) {
+        if (lane == 0) {
+          rg.drain(p.lb.err);
+          bulk_wait_read();
+        }
+        return;
+      }
+      if (p.carries != nullptr) {
+        float* dst = p.carries + (size_t)(c * p.nstrips + strip) * 2 * 32;
+        __stcs(dst + lane, A);
+        __stcs(dst + 32 + lane, Bv);
+      }
+      const E* sa = reinterpret_cast<const E*>(wring + (size_t)s * SS::kBytes) + lane;
+      const E* sb = sa + SS::kArrayBytes / sizeof(E);
+      unsigned char* ob = wout + (size_t)(j & 1) * SS::kOutBytes;
+      if (lane == 0) bulk_wait_read_1();  // the stores of chunk j - 2 have read this buffer
+      __syncwarp();
+      E* oA = reinterpret_cast<E*>(ob) + lane;
+      E* oB = oA + SS::kArrayBytes / sizeof(E);
+      const long long t0 = c * kLc;
+#pragma unroll 8
+      for (int i = 0; i < kLc; ++i) {
+        const bool tv = t0 + i < p.T_;
+        const float a = tv ? to_f32<E>(sa[i * 32]) : 1.f, b = tv ? to_f32<E>(sb[i * 32]) : 0.f;
+        Bv = fmaf(a, Bv, b);
+        A *= a;
+        oA[i * 32] = from_f32<E>(A);
+        oB[i * 32] = from_f32<E>(Bv);
+      }
+      fence_proxy_async_smem();
+      __syncwarp();
+      if (lane == 0) {
+        if (c + NST < p.nchunks) issue(c + NST);
+        tma_store_3d(&maps.out[0], d0, (int)t0, (int)bi, ob);
+        tma_store_3d(&maps.out[1], d0, (int)t0, (int)bi, ob + SS::kArrayBytes);
+        bulk_commit();
+      }
+    }
+    j0 += p.nchunks;
+  }
+  if (lane == 0) bulk_wait_read();
+}
+
+template <typename E>
+__global__ void __launch_bounds__(kWsWarps * 32, 1)
+    bwd_strip_kernel(Args<E> p, const __grid_constant__ StripMaps maps) {
+  using SS = WsStage<E, 4, true>;
+  constexpr int NST = SS::kStages;
+  extern __shared__ __align__(128) unsigned char ring[];
+  __shared__ __align__(8) uint64_t full[kWsWarps][NST];
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  if (lane == 0) {
+    for (int i = 0; i < NST; ++i) mbar_init(&full[warp][i], 1);
+    mbar_fence_init();
+    for (int i = 0; i < 4; ++i) tma_prefetch_desc(&maps.m[i]);
+  }
+  __syncwarp();
+  unsigned char* wring = ring + (size_t)warp * SS::kWarpBytes;
+  unsigned char* wout = wring + (size_t)NST * SS::kBytes;  // two output buffers
+  WsRing<NST> rg;
+  rg.full = full[warp];
+  long long j0 = 0;
+  for (long long strip = (long long)warp * gridDim.x + blockIdx.x; strip < p.nstrips;
+       strip += (long long)kWsWarps * gridDim.x) {
+    const long long bi = strip / p.sper;
+    const int d0 = (int)((strip - bi * p.sper) * 32);
+    auto issue = [&](long long c) {  // lane 0: step c handles chunk nchunks - 1 - c
+      const long long chunk = p.nchunks - 1 - c;
+      const long long j = j0 + c;
+      const int s = (int)(j % NST);
+      unsigned char* st = wring + (size_t)s * SS::kBytes;
+      mbar_arrive_expect_tx(&rg.full[s], (unsigned)(4 * SS::kArrayBytes + SS::kCarryBytes));
+#pragma unroll
+      for (int arr = 0; arr < 4; ++arr)
+        tma_load_3d(st + arr * SS::kArrayBytes, &maps.m[arr], d0, (int)(chunk * kLc), (int)bi,
+                    &rg.full[s]);
+      bulk_g2s(st + 4 * SS::kArrayBytes, p.carries + (size_t)(chunk * p.nstrips + strip) * 2 * 32,
+               (unsigned)SS::kCarryBytes, &rg.full[s]);
+      rg.issued(s, (unsigned)(j / NST) & 1u);
+    };
+    if (lane == 0)
+      for (long long c = 0; c < NST && c < p.nchunks; ++c) issue(c);
+    float ya = 0.f, yb = 0.f;  // adjoints entering from later steps
+    for (long long c = 0; c < p.nchunks; ++c) {
+      const long long chunk = p.nchunks - 1 - c;
+      const long long j = j0 + c;
+      const int s = (int)(j % NST);
+      if (!rg.wait(s, (unsigned)(j / NST) & 1u, p.lb.err)) {
+        if (lane == 0) {
+          rg.drain(p.lb.err);
+          bulk_wait_read();
+        }
+        return;
+      }
+      const unsigned char* st = wring + (size_t)s * SS::kBytes;
+      const E* sa = reinterpret_cast<const E*>(st) + lane;
+      const E* sb = sa + SS::kArrayBytes / sizeof(E);
+      const E* sga = sb + SS::kArrayBytes / sizeof(E);
+      const E* sgb = sga + SS::kArrayBytes / sizeof(E);
+      const float* fc = reinterpret_cast<const float*>(st + 4 * SS::kArrayBytes);
+      float fA = fc[lane], fB = fc[32 + lane];
+      const long long t0 = chunk * kLc;
+      unsigned char* ob = wout + (size_t)(j & 1) * SS::kOutBytes;
+      if (lane == 0) bulk_wait_read_1();  // the stores of step j - 2 have read this buffer
+      __syncwarp();
+      E* oA = reinterpret_cast<E*>(ob) + lane;
+      E* oB = oA + SS::kArrayBytes / sizeof(E);
+      float ap[kLc], bp[kLc];  // states before each step of the chunk
+#pragma unroll
+      for (int i = 0; i < kLc; ++i) {
+        const bool tv = t0 + i < p.T_;
+        const float a = tv ? to_f32<E>(sa[i * 32]) : 1.f, b = tv ? to_f32<E>(sb[i * 32]) : 0.f;
+        ap[i] = fA;
+        bp[i] = fB;
+        fB = fmaf(a, fB, b);
+        fA *= a;
+      }
+#pragma unroll
+      for (int i = kLc - 1; i >= 0; --i) {
+        const bool tv = t0 + i < p.T_;
+        const float a = tv ? to_f32<E>(sa[i * 32]) : 1.f;
+        const float GA = (tv ? to_f32<E>(sga[i * 32]) : 0.f) + ya;
+        const float GB = (tv ? to_f32<E>(sgb[i * 32]) : 0.f) + yb;
+        ya = a * GA;
+        yb = a * GB;
+        oA[i * 32] = from_f32<E>(fmaf(GA, ap[i], GB * bp[i]));
+        oB[i * 32] = from_f32<E>(GB);
+      }
+      fence_proxy_async_smem();
+      __syncwarp();
+      if (lane == 0) {
+        if (c + NST < p.nchunks) issue(c + NST);
+        tma_store_3d(&maps.out[0], d0, (int)t0, (int)bi, ob);
+        tma_store_3d(&maps.out[1], d0, (int)t0, (int)bi, ob + SS::kArrayBytes);
+        bulk_commit();
+      }
+    }
+    j0 += p.nchunks;
+  }
+  if (lane == 0) bulk_wait_read();
+}
+
+// ------------------------------------------------- strip path, 16-bit --
+//
+// For 16-bit inputs the per-step latency of one warp per strip, not HBM,
+// bounds the strip walk (few strips per SM), so each strip is split over
+// kStripNW warps instead. One CTA = kStripNW consumer warps + 1 producer warp, persistent over
 // strips (strip = blockIdx.x, blockIdx.x + gridDim.x, ...). For each strip
 // the producer streams the kLc-step chunks, in time order (forward) or
 // reverse time order (backward), into an NSTAGE-deep ring: one bulk copy
@@ -490,7 +727,7 @@ __device__ __forceinline__ void strip_rows(const unsigned char* arr_base, int ro
 
 template <typename E>
 __global__ void __launch_bounds__((kStripNW + 1) * 32)
-    fwd_strip_kernel(Args<E> p, const __grid_constant__ StripMaps maps) {
+    fwd_split_kernel(Args<E> p, const __grid_constant__ StripMaps maps) {
   using SS = StripStage<E, 2, false>;
   constexpr int NSTAGE = SS::kStages;
   constexpr int NW = kStripNW, S = kStripS, NF = 2;
@@ -563,7 +800,7 @@ __global__ void __launch_bounds__((kStripNW + 1) * 32)
 
 template <typename E>
 __global__ void __launch_bounds__((kStripNW + 1) * 32)
-    bwd_strip_kernel(Args<E> p, const __grid_constant__ StripMaps maps) {
+    bwd_split_kernel(Args<E> p, const __grid_constant__ StripMaps maps) {
   using SS = StripStage<E, 4, true>;
   constexpr int NSTAGE = SS::kStages;
   constexpr int NW = kStripNW, S = kStripS;
@@ -708,14 +945,26 @@ int run(bool fwd, const void* a, const void* b, void* A, void* Bc, const void* g
     const void* src[4] = {a, b, gA, gB};
     for (int i = 0; i < (fwd ? 2 : 4); ++i)
       if (!make_tmap_3d<E>(&maps.m[i], src[i], D, T, B, 32u, (unsigned)kLc)) return MGS_LAUNCH_FAILED;
+    void* dst[2] = {fwd ? A : da, fwd ? Bc : db};
+    for (int i = 0; i < 2; ++i)
+      if (!make_tmap_3d<E>(&maps.out[i], dst[i], D, T, B, 32u, (unsigned)kLc)) return MGS_LAUNCH_FAILED;
     void* kargs[] = {&p, &maps};
-    if (fwd)
-      return launch_persistent(fwd_strip_kernel<E>, (kStripNW + 1) * 32,
-                               StripStage<E, 2, false>::kStages * StripStage<E, 2, false>::kBytes,
+    if (sizeof(E) == 2) {  // four warps per strip (see the 16-bit strip path)
+      if (fwd)
+        return launch_persistent(fwd_split_kernel<E>, (kStripNW + 1) * 32,
+                                 StripStage<E, 2, false>::kStages * StripStage<E, 2, false>::kBytes,
+                                 g.nstrips, kargs, st);
+      return launch_persistent(bwd_split_kernel<E>, (kStripNW + 1) * 32,
+                               StripStage<E, 4, true>::kStages * StripStage<E, 4, true>::kBytes,
                                g.nstrips, kargs, st);
-    return launch_persistent(bwd_strip_kernel<E>, (kStripNW + 1) * 32,
-                             StripStage<E, 4, true>::kStages * StripStage<E, 4, true>::kBytes,
-                             g.nstrips, kargs, st);
+    }
+    // strips are dealt CTA-first, so one CTA per SM keeps the SMs within one strip
+    const long long units = (g.nstrips + kWsWarps - 1) / kWsWarps;
+    if (fwd)
+      return launch_persistent(fwd_strip_kernel<E>, kWsWarps * 32, WsStage<E, 2, false>::kSmem,
+                               units < sm_count() ? units : sm_count(), kargs, st);
+    return launch_persistent(bwd_strip_kernel<E>, kWsWarps * 32, WsStage<E, 4, true>::kSmem,
+                             units < sm_count() ? units : sm_count(), kargs, st);
   }
   const long long lbt = g.ntiles > g.ftiles ? g.ntiles : g.ftiles;
   MGS_CUDA_OK(cudaMemsetAsync(ws, 0, lookback_zero_bytes(lbt), st));
