@@ -11,14 +11,11 @@
 // Three algorithms, chosen per shape (the same choice for forward and
 // backward, since the forward's carries feed the backward):
 //  * strip (wide problems, B*ceil(D/32) >= 2 x #SMs, rows 16-byte aligned):
-//    32-channel strips walk all of T, their 32-step chunks streamed by TMA
-//    into shared-memory rings (mbarrier completion); no global
-//    synchronisation. fp32: one warp per strip runs the recurrence itself
-//    (lane = channel, one FMA per step) and writes each chunk's results back
-//    by TMA box stores -- HBM-bound. 16-bit: the per-step latency of that
-//    walk, not HBM, would bound it, so four consumer warps split each chunk
-//    (8 steps each), compose their aggregates through shared memory and carry
-//    the strip state from chunk to chunk, fed by a producer warp.
+//    32-channel strips walk all of T, one warp per strip running the
+//    recurrence itself (one FMA per channel and step), their 32-step chunks
+//    streamed by TMA into per-warp shared-memory rings (mbarrier completion)
+//    and each chunk's results written back by TMA box stores; no global
+//    synchronisation.
 //  * direct-vec (narrow problems, rows 16-byte aligned): one tile (64 steps x
 //    128 channels, 4 channels per lane, 16-byte accesses) per CTA, chunk
 //    carries across CTAs by windowed decoupled look-back.
@@ -34,9 +31,6 @@ namespace mgs {
 namespace linear {
 
 constexpr int kLc = 32;  // carry-chunk length = backward tile length (all algorithms)
-constexpr int kStripNW = 4;                      // consumer warps per strip (16-bit path)
-constexpr int kStripS = kLc / kStripNW;          // steps per consumer warp and chunk
-constexpr int kRingBytes = 50 * 1024;            // shared-memory ring per CTA (4 CTAs per SM)
 
 // direct paths
 constexpr int kVecCpt = 4;                       // channels per lane, direct-vec
@@ -425,18 +419,32 @@ __global__ void __launch_bounds__(NW * 32) bwd_direct_kernel(Args<E> p) {
 // streams its strip's kLc-step chunks (TMA boxes of 32 channels x kLc steps;
 // backward: plus the chunk's forward carry) through a private ring of NST
 // stages in shared memory; lane 0 refills a stage with the chunk NST ahead as
-// soon as the warp has read it. Strips are dealt to warps CTA-first (strip =
-// warp * gridDim.x + blockIdx.x, then + kWsWarps * gridDim.x), so the SMs'
-// strip counts differ by at most one. The forward writes the strip state at
-// every chunk start (the carries); the backward recomputes each chunk's states
-// from them in registers and carries the adjoint in reverse.
+// soon as the warp has read it, and writes the chunk's results back by TMA box
+// stores from two output buffers. Strips are dealt to warps CTA-first (strip =
+// warp * gridDim.x + blockIdx.x, then + NW * gridDim.x), so the SMs' strip
+// counts differ by at most one. The forward writes the strip state at every
+// chunk start (the carries); the backward recomputes each chunk's states from
+// them in registers and carries the adjoint in reverse.
+//
+// The walk is bound by one warp's serial path per chunk (ring wait, shared
+// loads, 32 dependent steps, TMA issue) more than by the SM: 16-bit inputs,
+// with half the bytes per chunk, stay below HBM bandwidth, fp32 reaches it.
+//
+// Each chunk's inputs are read into registers before any result is written:
+// the stage and the output buffers are one shared array, so the compiler
+// keeps every shared load behind the stores written before it, and a walk
+// interleaving them would pay a load latency per step.
+//
+// Rows past T arrive zero-filled (TMA out-of-bounds fill). They come after
+// every valid step of the strip, their results are clipped by the box stores,
+// and a zero row passes a zero adjoint, so they need no masking.
 
-constexpr int kWsWarps = 4;
-constexpr size_t kWsRingPerWarp = 50 * 1024;
+constexpr int kWsWarps = 4;                  // warps (strips in flight) per CTA
+constexpr size_t kWsRingPerWarp = 50 * 1024; // shared memory per warp: ring + output buffers
 
 // Per warp: NST input stages and two output buffers (the chunk's two result
 // arrays, written back by TMA box stores while the next chunk is computed).
-template <typename E, int NIN, bool WITH_CARRY>
+template <typename E, int NIN, bool WITH_CARRY, int NW>
 struct WsStage {
   static constexpr size_t kArrayBytes = (size_t)kLc * 32 * sizeof(E);
   static constexpr size_t kCarryBytes = WITH_CARRY ? 2 * 32 * sizeof(float) : 0;
@@ -445,7 +453,8 @@ struct WsStage {
   static constexpr int kFit = (int)((kWsRingPerWarp - 2 * kOutBytes) / kBytes);
   static constexpr int kStages = kFit > 8 ? 8 : kFit;
   static constexpr size_t kWarpBytes = kStages * kBytes + 2 * kOutBytes;
-  static constexpr size_t kSmem = (size_t)kWsWarps * kWarpBytes;
+  static constexpr size_t kSmem = (size_t)NW * kWarpBytes;
+  static_assert(kStages >= 2, "ring too shallow");
 };
 
 // Per-warp ring bookkeeping (lane 0 issues, every lane waits): chunk j of the
@@ -469,13 +478,13 @@ struct WsRing {
   }
 };
 
-template <typename E>
-__global__ void __launch_bounds__(kWsWarps * 32, 1)
+template <typename E, int NW>
+__global__ void __launch_bounds__(NW * 32, 1)
     fwd_strip_kernel(Args<E> p, const __grid_constant__ StripMaps maps) {
-  using SS = WsStage<E, 2, false>;
+  using SS = WsStage<E, 2, false, NW>;
   constexpr int NST = SS::kStages;
   extern __shared__ __align__(128) unsigned char ring[];
-  __shared__ __align__(8) uint64_t full[kWsWarps][NST];
+  __shared__ __align__(8) uint64_t full[NW][NST];
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   if (lane == 0) {
     for (int i = 0; i < NST; ++i) mbar_init(&full[warp][i], 1);
@@ -490,7 +499,7 @@ __global__ void __launch_bounds__(kWsWarps * 32, 1)
   rg.full = full[warp];
   long long j0 = 0;  // chunks of earlier strips taken by this warp
   for (long long strip = (long long)warp * gridDim.x + blockIdx.x; strip < p.nstrips;
-       strip += (long long)kWsWarps * gridDim.x) {
+       strip += (long long)NW * gridDim.x) {
     const long long bi = strip / p.sper;
     const int d0 = (int)((strip - bi * p.sper) * 32);
     auto issue = [&](long long c) {  // lane 0: chunk c of this strip
@@ -522,17 +531,22 @@ __global__ void __launch_bounds__(kWsWarps * 32, 1)
       }
       const E* sa = reinterpret_cast<const E*>(wring + (size_t)s * SS::kBytes) + lane;
       const E* sb = sa + SS::kArrayBytes / sizeof(E);
+      E va[kLc], vb[kLc];
+#pragma unroll
+      for (int i = 0; i < kLc; ++i) {
+        va[i] = sa[i * 32];
+        vb[i] = sb[i * 32];
+      }
       unsigned char* ob = wout + (size_t)(j & 1) * SS::kOutBytes;
       if (lane == 0) bulk_wait_read_1();  // the stores of chunk j - 2 have read this buffer
       __syncwarp();
       E* oA = reinterpret_cast<E*>(ob) + lane;
       E* oB = oA + SS::kArrayBytes / sizeof(E);
       const long long t0 = c * kLc;
-#pragma unroll 8
+#pragma unroll
       for (int i = 0; i < kLc; ++i) {
-        const bool tv = t0 + i < p.T_;
-        const float a = tv ? to_f32<E>(sa[i * 32]) : 1.f, b = tv ? to_f32<E>(sb[i * 32]) : 0.f;
-        Bv = fmaf(a, Bv, b);
+        const float a = to_f32<E>(va[i]);
+        Bv = fmaf(a, Bv, to_f32<E>(vb[i]));
         A *= a;
         oA[i * 32] = from_f32<E>(A);
         oB[i * 32] = from_f32<E>(Bv);
@@ -551,13 +565,13 @@ __global__ void __launch_bounds__(kWsWarps * 32, 1)
   if (lane == 0) bulk_wait_read();
 }
 
-template <typename E>
-__global__ void __launch_bounds__(kWsWarps * 32, 1)
+template <typename E, int NW>
+__global__ void __launch_bounds__(NW * 32, 1)
     bwd_strip_kernel(Args<E> p, const __grid_constant__ StripMaps maps) {
-  using SS = WsStage<E, 4, true>;
+  using SS = WsStage<E, 4, true, NW>;
   constexpr int NST = SS::kStages;
   extern __shared__ __align__(128) unsigned char ring[];
-  __shared__ __align__(8) uint64_t full[kWsWarps][NST];
+  __shared__ __align__(8) uint64_t full[NW][NST];
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   if (lane == 0) {
     for (int i = 0; i < NST; ++i) mbar_init(&full[warp][i], 1);
@@ -571,7 +585,7 @@ __global__ void __launch_bounds__(kWsWarps * 32, 1)
   rg.full = full[warp];
   long long j0 = 0;
   for (long long strip = (long long)warp * gridDim.x + blockIdx.x; strip < p.nstrips;
-       strip += (long long)kWsWarps * gridDim.x) {
+       strip += (long long)NW * gridDim.x) {
     const long long bi = strip / p.sper;
     const int d0 = (int)((strip - bi * p.sper) * 32);
     auto issue = [&](long long c) {  // lane 0: step c handles chunk nchunks - 1 - c
@@ -618,23 +632,33 @@ __global__ void __launch_bounds__(kWsWarps * 32, 1)
       float ap[kLc], bp[kLc];  // states before each step of the chunk
 #pragma unroll
       for (int i = 0; i < kLc; ++i) {
-        const bool tv = t0 + i < p.T_;
-        const float a = tv ? to_f32<E>(sa[i * 32]) : 1.f, b = tv ? to_f32<E>(sb[i * 32]) : 0.f;
+        const float a = to_f32<E>(sa[i * 32]);
         ap[i] = fA;
         bp[i] = fB;
-        fB = fmaf(a, fB, b);
+        fB = fmaf(a, fB, to_f32<E>(sb[i * 32]));
         fA *= a;
       }
+      // Reverse walk in groups of kGrp steps, each group's inputs read first.
+      constexpr int kGrp = 8;
 #pragma unroll
-      for (int i = kLc - 1; i >= 0; --i) {
-        const bool tv = t0 + i < p.T_;
-        const float a = tv ? to_f32<E>(sa[i * 32]) : 1.f;
-        const float GA = (tv ? to_f32<E>(sga[i * 32]) : 0.f) + ya;
-        const float GB = (tv ? to_f32<E>(sgb[i * 32]) : 0.f) + yb;
-        ya = a * GA;
-        yb = a * GB;
-        oA[i * 32] = from_f32<E>(fmaf(GA, ap[i], GB * bp[i]));
-        oB[i * 32] = from_f32<E>(GB);
+      for (int g = kLc / kGrp - 1; g >= 0; --g) {
+        E va[kGrp], vga[kGrp], vgb[kGrp];
+#pragma unroll
+        for (int k = 0; k < kGrp; ++k) {
+          va[k] = sa[(g * kGrp + k) * 32];
+          vga[k] = sga[(g * kGrp + k) * 32];
+          vgb[k] = sgb[(g * kGrp + k) * 32];
+        }
+#pragma unroll
+        for (int k = kGrp - 1; k >= 0; --k) {
+          const int i = g * kGrp + k;
+          const float a = to_f32<E>(va[k]);
+          const float GA = to_f32<E>(vga[k]) + ya, GB = to_f32<E>(vgb[k]) + yb;
+          ya = a * GA;
+          yb = a * GB;
+          oA[i * 32] = from_f32<E>(fmaf(GA, ap[i], GB * bp[i]));
+          oB[i * 32] = from_f32<E>(GB);
+        }
       }
       fence_proxy_async_smem();
       __syncwarp();
@@ -648,238 +672,6 @@ __global__ void __launch_bounds__(kWsWarps * 32, 1)
     j0 += p.nchunks;
   }
   if (lane == 0) bulk_wait_read();
-}
-
-// ------------------------------------------------- strip path, 16-bit --
-//
-// For 16-bit inputs the per-step latency of one warp per strip, not HBM,
-// bounds the strip walk (few strips per SM), so each strip is split over
-// kStripNW warps instead. One CTA = kStripNW consumer warps + 1 producer warp, persistent over
-// strips (strip = blockIdx.x, blockIdx.x + gridDim.x, ...). For each strip
-// the producer streams the kLc-step chunks, in time order (forward) or
-// reverse time order (backward), into an NSTAGE-deep ring: one bulk copy
-// per (array, time row) of 32 channels, plus (backward) the chunk's forward
-// carry. Consumers and producer walk the same (strip, chunk) sequence, so no
-// per-stage metadata is needed.
-
-template <typename E, int NIN, bool WITH_CARRY>
-struct StripStage {
-  static constexpr int kRowElems = 32;
-  static constexpr size_t kArrayBytes = (size_t)kLc * kRowElems * sizeof(E);
-  static constexpr size_t kCarryBytes = WITH_CARRY ? 2 * 32 * sizeof(float) : 0;
-  static constexpr size_t kBytes = (NIN * kArrayBytes + kCarryBytes + 127) / 128 * 128;
-  static constexpr int kStages = (int)(kRingBytes / kBytes);
-};
-
-template <typename E, int NIN, bool WITH_CARRY, bool REVERSE>
-__device__ __forceinline__ void strip_produce(const Args<E>& p, const StripMaps& maps,
-                                              unsigned char* ring, uint64_t* full,
-                                              uint64_t* empty) {
-  using SS = StripStage<E, NIN, WITH_CARRY>;
-  constexpr int NSTAGE = SS::kStages;
-  const int lane = threadIdx.x & 31;
-  if (lane == 0)
-    for (int i = 0; i < NIN; ++i) tma_prefetch_desc(&maps.m[i]);
-  int s = 0;
-  unsigned ph = 0, pending = 0u, pend_ph = 0u;
-  for (long long strip = blockIdx.x; strip < p.nstrips; strip += gridDim.x) {
-    const long long bi = strip / p.sper;
-    const int d0 = (int)((strip - bi * p.sper) * 32);
-    for (long long q = 0; q < p.nchunks; ++q) {
-      const long long chunk = REVERSE ? p.nchunks - 1 - q : q;
-      if (!mbar_wait(&empty[s], ph ^ 1u, p.lb.err)) goto drain;
-      pending &= ~(1u << s);
-      if (lane == 0) {
-        unsigned char* stage = ring + (size_t)s * SS::kBytes;
-        mbar_arrive_expect_tx(&full[s], (unsigned)(NIN * SS::kArrayBytes + SS::kCarryBytes));
-#pragma unroll
-        for (int arr = 0; arr < NIN; ++arr)
-          tma_load_3d(stage + arr * SS::kArrayBytes, &maps.m[arr], d0, (int)(chunk * kLc), (int)bi,
-                      &full[s]);
-        if (WITH_CARRY)
-          bulk_g2s(stage + NIN * SS::kArrayBytes,
-                   p.carries + (size_t)(chunk * p.nstrips + strip) * 2 * 32,
-                   (unsigned)SS::kCarryBytes, &full[s]);
-      }
-      __syncwarp();
-      pending |= 1u << s;
-      pend_ph = (pend_ph & ~(1u << s)) | (ph << s);
-      if (++s == NSTAGE) {
-        s = 0;
-        ph ^= 1u;
-      }
-    }
-  }
-drain:
-  for (int i = 0; i < NSTAGE; ++i)
-    if (pending & (1u << i)) mbar_wait(&full[i], (pend_ph >> i) & 1u, p.lb.err);
-}
-
-template <typename E, int S>
-__device__ __forceinline__ void strip_rows(const unsigned char* arr_base, int row0, long long t0,
-                                           long long T, bool dok, float fill, float (&out)[S][1]) {
-  const int lane = threadIdx.x & 31;
-  const E* base = reinterpret_cast<const E*>(arr_base) + lane;
-#pragma unroll
-  for (int s = 0; s < S; ++s)
-    out[s][0] = (dok && t0 + s < T) ? to_f32<E>(base[(row0 + s) * 32]) : fill;
-}
-
-template <typename E>
-__global__ void __launch_bounds__((kStripNW + 1) * 32)
-    fwd_split_kernel(Args<E> p, const __grid_constant__ StripMaps maps) {
-  using SS = StripStage<E, 2, false>;
-  constexpr int NSTAGE = SS::kStages;
-  constexpr int NW = kStripNW, S = kStripS, NF = 2;
-  using M = FwdMonoid<1>;
-  extern __shared__ __align__(128) unsigned char ring[];
-  __shared__ __align__(8) uint64_t full[NSTAGE], empty[NSTAGE];
-  __shared__ float s_agg[2][NW][NF][32];
-  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  if (threadIdx.x == 0) {
-    for (int i = 0; i < NSTAGE; ++i) {
-      mbar_init(&full[i], 1);
-      mbar_init(&empty[i], NW);
-    }
-    mbar_fence_init();
-  }
-  __syncthreads();
-  if (warp == NW) {
-    strip_produce<E, 2, false, false>(p, maps, ring, full, empty);
-    return;
-  }
-  int s = 0, buf = 0;
-  unsigned ph = 0;
-  for (long long strip = blockIdx.x; strip < p.nstrips; strip += gridDim.x) {
-    const long long bi = strip / p.sper;
-    const long long d = (strip - bi * p.sper) * 32 + lane;
-    const bool dok = d < p.D;
-    const size_t base = (size_t)bi * p.T_ * p.D + d;
-    float carry[NF];
-    M::identity(carry);
-    for (long long chunk = 0; chunk < p.nchunks; ++chunk) {
-      const bool ok = mbar_wait(&full[s], ph, p.lb.err);
-      if (bar_any(1, NW * 32, !ok)) return;
-      const unsigned char* stage = ring + (size_t)s * SS::kBytes;
-      const long long t0 = chunk * kLc + (long long)warp * S;
-      float av[S][1], bv[S][1];
-      strip_rows<E, S>(stage, warp * S, t0, p.T_, dok, 1.f, av);
-      strip_rows<E, S>(stage + SS::kArrayBytes, warp * S, t0, p.T_, dok, 0.f, bv);
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&empty[s]);
-      if (++s == NSTAGE) {
-        s = 0;
-        ph ^= 1u;
-      }
-      float agg[NF];
-      fwd_agg<1, S>(av, bv, agg);
-      s_agg[buf][warp][0][lane] = agg[0];
-      s_agg[buf][warp][1][lane] = agg[1];
-      named_bar(2, NW * 32);
-      if (warp == 0 && p.carries != nullptr) {
-        float* dst = p.carries + (size_t)(chunk * p.nstrips + strip) * NF * 32;
-        __stcs(dst + lane, carry[0]);
-        __stcs(dst + 32 + lane, carry[1]);
-      }
-      float cur[NF] = {carry[0], carry[1]};
-#pragma unroll
-      for (int w = 0; w < NW; ++w) {
-        const float e[NF] = {s_agg[buf][w][0][lane], s_agg[buf][w][1][lane]};
-        if (w == warp) {
-          cur[0] = carry[0];
-          cur[1] = carry[1];
-        }
-        combine_into<M, NF>(carry, e);
-      }
-      // cur currently = prefix before warp `warp` (captured above)
-      fwd_emit<E, 1, S>(p, av, bv, cur, dok, t0, base);
-      buf ^= 1;
-    }
-  }
-}
-
-template <typename E>
-__global__ void __launch_bounds__((kStripNW + 1) * 32)
-    bwd_split_kernel(Args<E> p, const __grid_constant__ StripMaps maps) {
-  using SS = StripStage<E, 4, true>;
-  constexpr int NSTAGE = SS::kStages;
-  constexpr int NW = kStripNW, S = kStripS;
-  using FM = FwdMonoid<1>;
-  using RM = RevMonoid<1>;
-  extern __shared__ __align__(128) unsigned char ring[];
-  __shared__ __align__(8) uint64_t full[NSTAGE], empty[NSTAGE];
-  __shared__ float s_fagg[2][NW][2][32];
-  __shared__ float s_ragg[2][NW][3][32];
-  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  if (threadIdx.x == 0) {
-    for (int i = 0; i < NSTAGE; ++i) {
-      mbar_init(&full[i], 1);
-      mbar_init(&empty[i], NW);
-    }
-    mbar_fence_init();
-  }
-  __syncthreads();
-  if (warp == NW) {
-    strip_produce<E, 4, true, true>(p, maps, ring, full, empty);
-    return;
-  }
-  int s = 0, buf = 0;
-  unsigned ph = 0;
-  for (long long strip = blockIdx.x; strip < p.nstrips; strip += gridDim.x) {
-    const long long bi = strip / p.sper;
-    const long long d = (strip - bi * p.sper) * 32 + lane;
-    const bool dok = d < p.D;
-    const size_t base = (size_t)bi * p.T_ * p.D + d;
-    float rcarry[3];
-    RM::identity(rcarry);
-    for (long long q = 0; q < p.nchunks; ++q) {
-      const long long chunk = p.nchunks - 1 - q;
-      const bool ok = mbar_wait(&full[s], ph, p.lb.err);
-      if (bar_any(1, NW * 32, !ok)) return;
-      const unsigned char* stage = ring + (size_t)s * SS::kBytes;
-      const long long t0 = chunk * kLc + (long long)warp * S;
-      float av[S][1], bv[S][1], ga[S][1], gb[S][1];
-      strip_rows<E, S>(stage, warp * S, t0, p.T_, dok, 1.f, av);
-      strip_rows<E, S>(stage + SS::kArrayBytes, warp * S, t0, p.T_, dok, 0.f, bv);
-      strip_rows<E, S>(stage + 2 * SS::kArrayBytes, warp * S, t0, p.T_, dok, 0.f, ga);
-      strip_rows<E, S>(stage + 3 * SS::kArrayBytes, warp * S, t0, p.T_, dok, 0.f, gb);
-      const float* fc = reinterpret_cast<const float*>(stage + 4 * SS::kArrayBytes);
-      float fcur[2] = {fc[lane], fc[32 + lane]};
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&empty[s]);
-      if (++s == NSTAGE) {
-        s = 0;
-        ph ^= 1u;
-      }
-      float fagg[2], ragg[3];
-      fwd_agg<1, S>(av, bv, fagg);
-      rev_agg<1, S>(av, ga, gb, ragg);
-      s_fagg[buf][warp][0][lane] = fagg[0];
-      s_fagg[buf][warp][1][lane] = fagg[1];
-      s_ragg[buf][warp][0][lane] = ragg[0];
-      s_ragg[buf][warp][1][lane] = ragg[1];
-      s_ragg[buf][warp][2][lane] = ragg[2];
-      named_bar(2, NW * 32);
-      for (int w = 0; w < warp; ++w) {
-        const float e[2] = {s_fagg[buf][w][0][lane], s_fagg[buf][w][1][lane]};
-        combine_into<FM, 2>(fcur, e);
-      }
-      float rcur[3] = {rcarry[0], rcarry[1], rcarry[2]};
-#pragma unroll
-      for (int w = NW - 1; w >= 0; --w) {
-        if (w == warp) {
-          rcur[0] = rcarry[0];
-          rcur[1] = rcarry[1];
-          rcur[2] = rcarry[2];
-        }
-        const float e[3] = {s_ragg[buf][w][0][lane], s_ragg[buf][w][1][lane], s_ragg[buf][w][2][lane]};
-        combine_into<RM, 3>(rcarry, e);
-      }
-      float ya[1] = {rcur[1]}, yb[1] = {rcur[2]};
-      bwd_emit<E, 1, S>(p, av, bv, ga, gb, fcur, ya, yb, dok, t0, base);
-      buf ^= 1;
-    }
-  }
 }
 
 // ---------------------------------------------------------------- launch --
@@ -949,22 +741,13 @@ int run(bool fwd, const void* a, const void* b, void* A, void* Bc, const void* g
     for (int i = 0; i < 2; ++i)
       if (!make_tmap_3d<E>(&maps.out[i], dst[i], D, T, B, 32u, (unsigned)kLc)) return MGS_LAUNCH_FAILED;
     void* kargs[] = {&p, &maps};
-    if (sizeof(E) == 2) {  // four warps per strip (see the 16-bit strip path)
-      if (fwd)
-        return launch_persistent(fwd_split_kernel<E>, (kStripNW + 1) * 32,
-                                 StripStage<E, 2, false>::kStages * StripStage<E, 2, false>::kBytes,
-                                 g.nstrips, kargs, st);
-      return launch_persistent(bwd_split_kernel<E>, (kStripNW + 1) * 32,
-                               StripStage<E, 4, true>::kStages * StripStage<E, 4, true>::kBytes,
-                               g.nstrips, kargs, st);
-    }
-    // strips are dealt CTA-first, so one CTA per SM keeps the SMs within one strip
+    // one CTA of kWsWarps warps per SM (the rings fill its shared memory)
     const long long units = (g.nstrips + kWsWarps - 1) / kWsWarps;
     if (fwd)
-      return launch_persistent(fwd_strip_kernel<E>, kWsWarps * 32, WsStage<E, 2, false>::kSmem,
-                               units < sm_count() ? units : sm_count(), kargs, st);
-    return launch_persistent(bwd_strip_kernel<E>, kWsWarps * 32, WsStage<E, 4, true>::kSmem,
-                             units < sm_count() ? units : sm_count(), kargs, st);
+      return launch_persistent(fwd_strip_kernel<E, kWsWarps>, kWsWarps * 32,
+                               WsStage<E, 2, false, kWsWarps>::kSmem, units, kargs, st);
+    return launch_persistent(bwd_strip_kernel<E, kWsWarps>, kWsWarps * 32,
+                             WsStage<E, 4, true, kWsWarps>::kSmem, units, kargs, st);
   }
   const long long lbt = g.ntiles > g.ftiles ? g.ntiles : g.ftiles;
   MGS_CUDA_OK(cudaMemsetAsync(ws, 0, lookback_zero_bytes(lbt), st));

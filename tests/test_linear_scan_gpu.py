@@ -46,7 +46,9 @@ def test_golden(cuda, name):
 # Strip path (B*ceil(D/32) >= 296 on 148 SMs): (10, 100, 1000) and (3, 70, 3200)
 # with ragged T and a partial last strip, (19, 1100, 520) with a long ragged
 # walk, (20, 300, 1000) with more strips (640) than warps in flight, so warps
-# walk a second strip on the same ring.
+# walk a second strip on the same ring. 16-bit inputs take the same strip path:
+# (10, 45, 1000) and (15, 70, 1048) end in partial strips (8 and 24 channels),
+# (20, 300, 1000) has 640 strips for 592 warps.
 SHAPES = [(1, 1, 1), (2, 13, 3), (3, 31, 4), (2, 32, 128), (2, 33, 129), (1, 64, 256),
           (3, 100, 1000), (2, 1000, 36), (1, 777, 8), (4, 257, 512), (2, 50, 40), (1, 3000, 132),
           (10, 100, 1000), (3, 70, 3200), (19, 1100, 520), (20, 300, 1000)]
@@ -76,7 +78,7 @@ def test_vs_oracle_fp32(cuda, shape):
 
 @pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
 @pytest.mark.parametrize("shape", [(2, 13, 3), (2, 300, 256), (3, 100, 1000), (2, 77, 40), (1, 500, 36), (10, 45, 1000),
-                                   (20, 300, 1000)])
+                                   (20, 300, 1000), (15, 70, 1048)])
 def test_half_inputs_fp32_state(cuda, shape, dtype):
     a, b, gA, gB = inputs(*shape, seed=7)
     rnd = lambda x: torch.as_tensor(x, dtype=torch.float32).to(dtype).double().numpy()
