@@ -515,7 +515,7 @@ __global__ void __launch_bounds__(Shape<K, V>::NW * 32, 1) bwd_kernel(Args<E> p)
 // kStripNW consumer warps + 1 producer warp, each CTA walking 32-block strips
 // through all of T. The producer streams 32-step chunks of A and Bm (backward:
 // also gA, gB and the chunk's forward carry) into a shared-memory ring with
-// TMA; consumer warp w takes steps w*8 .. w*8+7 of each chunk with its lane's
+// TMA; consumer warp w takes steps w*S .. w*S+S-1 (S = 4) of each chunk with its lane's
 // inputs in registers, warp aggregates combine through shared memory and the
 // strip state is carried on chip from chunk to chunk: no look-back, every
 // input read once. The forward writes each chunk's start state (the carries);
@@ -523,7 +523,7 @@ __global__ void __launch_bounds__(Shape<K, V>::NW * 32, 1) bwd_kernel(Args<E> p)
 // carries the adjoint like the register kernels.
 
 constexpr int kLc = 32;          // steps per chunk (= carry granularity of the strip path)
-constexpr int kStripNW = 4;      // consumer warps
+constexpr int kStripNW = 8;      // consumer warps
 constexpr int kStripS = kLc / kStripNW;
 constexpr int kMaxStages = 16;
 
@@ -603,16 +603,26 @@ drain:
     if (pending & (1u << i)) mbar_wait(&full[i], (pend_ph >> i) & 1u, a.err);
 }
 
-// Lane `lane`'s N elements of time row `row` of a staged (rows x 32 N) block.
+// Lane `lane`'s N elements of time row `row` of a staged (rows x 32 N) block,
+// read as the widest vectors their alignment allows (N is a power of two, the
+// block 128-byte aligned).
 template <typename E, int N>
 __device__ __forceinline__ void stage_get(const unsigned char* base, int row, float (&o)[N]) {
+  constexpr int kBytes = N * (int)sizeof(E) < 16 ? N * (int)sizeof(E) : 16;
+  constexpr int kPer = kBytes / (int)sizeof(E);
+  using Vt = typename VecOf<kBytes>::type;
   const E* p = reinterpret_cast<const E*>(base) + (size_t)row * 32 * N + (threadIdx.x & 31) * N;
 #pragma unroll
-  for (int i = 0; i < N; ++i) o[i] = to_f32<E>(p[i]);
+  for (int c = 0; c < N / kPer; ++c) {
+    const Vt w = reinterpret_cast<const Vt*>(p)[c];
+    const E* e = reinterpret_cast<const E*>(&w);
+#pragma unroll
+    for (int i = 0; i < kPer; ++i) o[c * kPer + i] = to_f32<E>(e[i]);
+  }
 }
 
 template <typename E, int K, int V>
-__global__ void __launch_bounds__((kStripNW + 1) * 32)
+__global__ void __launch_bounds__((kStripNW + 1) * 32, 1)
     fwd_strip_kernel(Args<E> p, StripArgs a, const __grid_constant__ AStripMaps maps) {
   using SS = AStage<E, K, V, false>;
   using M = FwdMonoid<K, V>;
@@ -709,7 +719,7 @@ __global__ void __launch_bounds__((kStripNW + 1) * 32)
 }
 
 template <typename E, int K, int V>
-__global__ void __launch_bounds__((kStripNW + 1) * 32)
+__global__ void __launch_bounds__((kStripNW + 1) * 32, 1)
     bwd_strip_kernel(Args<E> p, StripArgs a, const __grid_constant__ AStripMaps maps) {
   using SS = AStage<E, K, V, true>;
   using FM = FwdMonoid<K, V>;
@@ -1047,20 +1057,28 @@ int launch_strip(bool fwd, Args<E>& p, const Geometry& g, void* ws, long long B,
     if (!fwd && (!make_tmap_3d<E>(&maps.m[2], p.gA, n * K * K, T, B, 32u * K * K, (unsigned)kLc) ||
                  !make_tmap_3d<E>(&maps.m[3], p.gB, n * K * V, T, B, 32u * K * V, (unsigned)kLc)))
       return MGS_LAUNCH_FAILED;
-    // One CTA per SM gets a deep ring; two share an SM when strips outnumber SMs.
+    // One CTA per SM gets a deep ring; two share an SM when strips outnumber SMs
+    // (228 KB of shared memory per SM, 1 KB of it reserved per CTA).
+    const void* fn = fwd ? (const void*)fwd_strip_kernel<E, K, V> : (const void*)bwd_strip_kernel<E, K, V>;
+    cudaFuncAttributes fa;
+    MGS_CUDA_OK(cudaFuncGetAttributes(&fa, fn));
     const int sms = sm_count();
-    const int per_sm = g.nstrips > sms ? 2 : 1;
-    const size_t ring_budget = per_sm == 1 ? 180 * 1024 : 88 * 1024;
     const size_t sbytes = fwd ? AStage<E, K, V, false>::kBytes : AStage<E, K, V, true>::kBytes;
-    int nst = (int)(ring_budget / sbytes);
-    if (nst > kMaxStages) nst = kMaxStages;
-    if (nst < 2) nst = 2;
+    auto stages = [&](int ctas_per_sm) {
+      const size_t per_cta = ctas_per_sm == 1 ? 227 * 1024 : 113 * 1024;
+      const size_t budget = per_cta > fa.sharedSizeBytes ? per_cta - fa.sharedSizeBytes : 0;
+      const int n = (int)(budget / sbytes);
+      return n > kMaxStages ? kMaxStages : n;
+    };
+    int per_sm = g.nstrips > sms ? 2 : 1;
+    int nst = stages(per_sm);
+    if (nst < 2 && per_sm == 2) nst = stages(per_sm = 1);
+    if (nst < 2) return MGS_UNSUPPORTED;
     a.nstage = nst;
     const size_t smem = (size_t)nst * sbytes;
     long long grid = (long long)per_sm * sms;
     if (grid > g.nstrips) grid = g.nstrips;
     void* kargs[] = {&p, &a, &maps};
-    const void* fn = fwd ? (const void*)fwd_strip_kernel<E, K, V> : (const void*)bwd_strip_kernel<E, K, V>;
     MGS_CUDA_OK(cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
     MGS_CUDA_OK(cudaLaunchKernel(fn, dim3((unsigned)grid), dim3((kStripNW + 1) * 32), kargs, smem, st));
     return MGS_OK;
