@@ -23,8 +23,9 @@
 // state runs in parallel over all chunks, and the two chunk-serial kernels do
 // one state product per chunk.
 //
-// Kernels (all 64 x 64 chunk products are bf16 mma.sync with split hi/lo
-// operands, mma_bf16.cuh; T^{-1} by blocked substitution in fp32):
+// Kernels (the 64 x 64 chunk products run on the tcgen05 tensor cores with
+// split hi/lo bf16 operands, umma.cuh; T^{-1} by blocked substitution, its
+// 16 x 16 blocks on mma.sync, mma_bf16.cuh):
 //   prep_kernel       one CTA per (b, h, chunk): T^{-1} (saved), Xn, Qt
 //                     (saved), Bc, Yp (forward workspace).
 //   chain_fwd_kernel  one CTA per (b, h, value-column split): S in registers,
@@ -1116,7 +1117,7 @@ bool tc_eligible(int dtype, int nh, int dk, int dv, int C) {
 }
 
 // saved: chunk-start states (fp32), then every chunk's T^{-1}, Xn and Qt
-// (split bf16 tile pairs in the padded shared-memory layout)
+// (split bf16 tile pairs, hi then lo, in the tcgen05 blocked layout)
 size_t tc_saved_floats(long long BH, long long T, int dk, int dv, int C) {
   const size_t nc = (size_t)BH * (size_t)((T + C - 1) / C);
   return nc * dk * dv + 3 * nc * (size_t)kSavedPair / 2;
