@@ -116,13 +116,18 @@ class ScanWorkload:
         pins = [x.pin_memory() for x in ins]
         pcots = [c.pin_memory() for c in cots]
         outs = [torch.empty_like(c).pin_memory() for c in cots] + [torch.empty_like(x).pin_memory() for x in ins]
-        return {"ins": pins, "cots": pcots, "out": outs, "dev": dev}
+        # two device copies of a step's inputs, filled alternately (no allocation per step)
+        slots = [([torch.empty_like(x, device=dev).requires_grad_(True) for x in ins],
+                  [torch.empty_like(c, device=dev) for c in cots]) for _ in range(2)]
+        return {"ins": pins, "cots": pcots, "out": outs, "dev": dev, "slots": slots}
 
-    def e2e_h2d(self, st):
-        """One step's inputs and cotangents, copied from the pinned host buffers."""
-        dev = st["dev"]
-        ins = [x.to(dev, non_blocking=True).requires_grad_(True) for x in st["ins"]]
-        cots = [c.to(dev, non_blocking=True) for c in st["cots"]]
+    def e2e_h2d(self, st, slot):
+        """One step's inputs and cotangents, copied from the pinned host buffers
+        into device slot `slot`."""
+        ins, cots = st["slots"][slot]
+        with torch.no_grad():
+            for d, h in zip(ins + cots, st["ins"] + st["cots"]):
+                d.copy_(h, non_blocking=True)
         return ins, cots
 
     def e2e_compute(self, st, ins, cots):
@@ -838,9 +843,10 @@ def e2e_pipeline(w, est, steps: int, dev) -> float:
     backward on the current stream once they have landed, and copies its
     results out to the pinned host buffers on a third stream once they are
     computed. PCIe carries both directions at once, so step k+1's inputs
-    travel while step k computes and step k-1's results come back; at most
-    two steps' inputs are on the device ahead of the compute. The events
-    bracket all three streams."""
+    travel while step k computes and step k-1's results come back. Inputs
+    land in two preallocated device slots, used alternately: slot k % 2 is
+    refilled once step k - 2's compute is done with it. The events bracket
+    all three streams."""
     cs = torch.cuda.current_stream(dev)
     s_in, s_out = torch.cuda.Stream(dev), torch.cuda.Stream(dev)
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
@@ -852,10 +858,8 @@ def e2e_pipeline(w, est, steps: int, dev) -> float:
         if k >= 2:
             s_in.wait_event(done[k - 2])
         with torch.cuda.stream(s_in):
-            ins, cots = w.e2e_h2d(est)
+            ins, cots = w.e2e_h2d(est, k % 2)
         cs.wait_stream(s_in)
-        for t in ins + cots:
-            t.record_stream(cs)
         res = w.e2e_compute(est, ins, cots)
         ev = torch.cuda.Event()
         ev.record(cs)
