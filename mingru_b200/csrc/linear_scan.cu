@@ -416,11 +416,11 @@ __global__ void __launch_bounds__(NW * 32) bwd_direct_kernel(Args<E> p) {
 //
 // One warp per 32-channel strip walks all of T with the recurrence itself
 // (lane = channel): no aggregates and no exchange between warps. Each warp
-// streams its strip's kLc-step chunks (TMA boxes of 32 channels x kLc steps;
-// backward: plus the chunk's forward carry) through a private ring of NST
-// stages in shared memory; lane 0 refills a stage with the chunk NST ahead as
-// soon as the warp has read it, and writes the chunk's results back by TMA box
-// stores from two output buffers. Strips are dealt to warps CTA-first (strip =
+// streams its strip in IO chunks (TMA boxes of 32 channels x 32 or 64 steps;
+// backward: plus the forward carry of each 32-step chunk inside) through a
+// private ring of NST stages in shared memory; lane 0 refills a stage with
+// the IO chunk NST ahead as soon as the warp has read it, and writes the
+// chunk's results back by TMA box stores from two output buffers. Strips are dealt to warps CTA-first (strip =
 // warp * gridDim.x + blockIdx.x, then + NW * gridDim.x), so the SMs' strip
 // counts differ by at most one. The forward writes the strip state at every
 // chunk start (the carries); the backward recomputes each chunk's states from
@@ -442,13 +442,22 @@ __global__ void __launch_bounds__(NW * 32) bwd_direct_kernel(Args<E> p) {
 constexpr int kWsWarps = 4;                  // warps (strips in flight) per CTA
 constexpr size_t kWsRingPerWarp = 50 * 1024; // shared memory per warp: ring + output buffers
 
-// Per warp: NST input stages and two output buffers (the chunk's two result
-// arrays, written back by TMA box stores while the next chunk is computed).
+// Rows per TMA box ("IO chunk"). The 16-bit backward takes two 32-step carry
+// chunks per box, so a chunk's fixed costs (ring wait, five copies, proxy
+// fence, buffer turnaround) are paid every 64 steps (measured 152 -> 131 us
+// at config 2); its forward measured no better that way, and an fp32 ring of
+// 64-row boxes would not fit beside its output buffers.
+template <typename E, bool BWD>
+constexpr int ws_io() { return BWD && sizeof(E) == 2 ? 2 * kLc : kLc; }
+
+// Per warp: NST input stages and two output buffers (an IO chunk's two result
+// arrays, written back by TMA box stores while the next one is computed).
 template <typename E, int NIN, bool WITH_CARRY, int NW>
 struct WsStage {
-  static constexpr size_t kArrayBytes = (size_t)kLc * 32 * sizeof(E);
-  static constexpr size_t kCarryBytes = WITH_CARRY ? 2 * 32 * sizeof(float) : 0;
-  static constexpr size_t kBytes = (NIN * kArrayBytes + kCarryBytes + 127) / 128 * 128;
+  static constexpr int IO = ws_io<E, WITH_CARRY>(), NH = IO / kLc;  // rows per box, carry chunks per box
+  static constexpr size_t kArrayBytes = (size_t)IO * 32 * sizeof(E);
+  static constexpr size_t kCarryBytes = WITH_CARRY ? 2 * 32 * sizeof(float) : 0;  // per carry chunk
+  static constexpr size_t kBytes = (NIN * kArrayBytes + NH * kCarryBytes + 127) / 128 * 128;
   static constexpr size_t kOutBytes = 2 * kArrayBytes;  // one output buffer (two arrays)
   static constexpr int kFit = (int)((kWsRingPerWarp - 2 * kOutBytes) / kBytes);
   static constexpr int kStages = kFit > 8 ? 8 : kFit;
@@ -457,8 +466,8 @@ struct WsStage {
   static_assert(kStages >= 2, "ring too shallow");
 };
 
-// Per-warp ring bookkeeping (lane 0 issues, every lane waits): chunk j of the
-// warp's whole sequence uses slot j % NST with phase (j / NST) & 1.
+// Per-warp ring bookkeeping (lane 0 issues, every lane waits): IO chunk j of
+// the warp's whole sequence uses slot j % NST with phase (j / NST) & 1.
 template <int NST>
 struct WsRing {
   uint64_t* full;
@@ -482,7 +491,7 @@ template <typename E, int NW>
 __global__ void __launch_bounds__(NW * 32, 1)
     fwd_strip_kernel(Args<E> p, const __grid_constant__ StripMaps maps) {
   using SS = WsStage<E, 2, false, NW>;
-  constexpr int NST = SS::kStages;
+  constexpr int NST = SS::kStages, IO = SS::IO, NH = SS::NH;
   extern __shared__ __align__(128) unsigned char ring[];
   __shared__ __align__(8) uint64_t full[NW][NST];
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
@@ -497,24 +506,25 @@ __global__ void __launch_bounds__(NW * 32, 1)
   unsigned char* wout = wring + (size_t)NST * SS::kBytes;  // two output buffers
   WsRing<NST> rg;
   rg.full = full[warp];
-  long long j0 = 0;  // chunks of earlier strips taken by this warp
+  const long long nio = (p.nchunks + NH - 1) / NH;  // IO chunks per strip
+  long long j0 = 0;  // IO chunks of earlier strips taken by this warp
   for (long long strip = (long long)warp * gridDim.x + blockIdx.x; strip < p.nstrips;
        strip += (long long)NW * gridDim.x) {
     const long long bi = strip / p.sper;
     const int d0 = (int)((strip - bi * p.sper) * 32);
-    auto issue = [&](long long c) {  // lane 0: chunk c of this strip
+    auto issue = [&](long long c) {  // lane 0: IO chunk c of this strip
       const long long j = j0 + c;
       const int s = (int)(j % NST);
       unsigned char* st = wring + (size_t)s * SS::kBytes;
       mbar_arrive_expect_tx(&rg.full[s], (unsigned)(2 * SS::kArrayBytes));
-      tma_load_3d(st, &maps.m[0], d0, (int)(c * kLc), (int)bi, &rg.full[s]);
-      tma_load_3d(st + SS::kArrayBytes, &maps.m[1], d0, (int)(c * kLc), (int)bi, &rg.full[s]);
+      tma_load_3d(st, &maps.m[0], d0, (int)(c * IO), (int)bi, &rg.full[s]);
+      tma_load_3d(st + SS::kArrayBytes, &maps.m[1], d0, (int)(c * IO), (int)bi, &rg.full[s]);
       rg.issued(s, (unsigned)(j / NST) & 1u);
     };
     if (lane == 0)
-      for (long long c = 0; c < NST && c < p.nchunks; ++c) issue(c);
+      for (long long c = 0; c < NST && c < nio; ++c) issue(c);
     float A = 1.f, Bv = 0.f;
-    for (long long c = 0; c < p.nchunks; ++c) {
+    for (long long c = 0; c < nio; ++c) {
       const long long j = j0 + c;
       const int s = (int)(j % NST);
       if (!rg.wait(s, (unsigned)(j / NST) & 1u, p.lb.err)) {
@@ -524,43 +534,48 @@ __global__ void __launch_bounds__(NW * 32, 1)
         }
         return;
       }
-      if (p.carries != nullptr) {
-        float* dst = p.carries + (size_t)(c * p.nstrips + strip) * 2 * 32;
-        __stcs(dst + lane, A);
-        __stcs(dst + 32 + lane, Bv);
-      }
-      const E* sa = reinterpret_cast<const E*>(wring + (size_t)s * SS::kBytes) + lane;
-      const E* sb = sa + SS::kArrayBytes / sizeof(E);
-      E va[kLc], vb[kLc];
-#pragma unroll
-      for (int i = 0; i < kLc; ++i) {
-        va[i] = sa[i * 32];
-        vb[i] = sb[i * 32];
-      }
       unsigned char* ob = wout + (size_t)(j & 1) * SS::kOutBytes;
-      if (lane == 0) bulk_wait_read_1();  // the stores of chunk j - 2 have read this buffer
-      __syncwarp();
-      E* oA = reinterpret_cast<E*>(ob) + lane;
-      E* oB = oA + SS::kArrayBytes / sizeof(E);
-      const long long t0 = c * kLc;
+#pragma unroll 1
+      for (int h = 0; h < NH; ++h) {  // carry chunks of this IO chunk
+        const long long cc = c * NH + h;
+        if (p.carries != nullptr && cc < p.nchunks) {
+          float* dst = p.carries + (size_t)(cc * p.nstrips + strip) * 2 * 32;
+          __stcs(dst + lane, A);
+          __stcs(dst + 32 + lane, Bv);
+        }
+        const E* sa = reinterpret_cast<const E*>(wring + (size_t)s * SS::kBytes) + h * kLc * 32 + lane;
+        const E* sb = sa + SS::kArrayBytes / sizeof(E);
+        E va[kLc], vb[kLc];
 #pragma unroll
-      for (int i = 0; i < kLc; ++i) {
-        const float a = to_f32<E>(va[i]);
-        Bv = fmaf(a, Bv, to_f32<E>(vb[i]));
-        A *= a;
-        oA[i * 32] = from_f32<E>(A);
-        oB[i * 32] = from_f32<E>(Bv);
+        for (int i = 0; i < kLc; ++i) {
+          va[i] = sa[i * 32];
+          vb[i] = sb[i * 32];
+        }
+        if (h == 0) {
+          if (lane == 0) bulk_wait_read_1();  // the stores of IO chunk j - 2 have read this buffer
+          __syncwarp();
+        }
+        E* oA = reinterpret_cast<E*>(ob) + h * kLc * 32 + lane;
+        E* oB = oA + SS::kArrayBytes / sizeof(E);
+#pragma unroll
+        for (int i = 0; i < kLc; ++i) {
+          const float a = to_f32<E>(va[i]);
+          Bv = fmaf(a, Bv, to_f32<E>(vb[i]));
+          A *= a;
+          oA[i * 32] = from_f32<E>(A);
+          oB[i * 32] = from_f32<E>(Bv);
+        }
       }
       fence_proxy_async_smem();
       __syncwarp();
       if (lane == 0) {
-        if (c + NST < p.nchunks) issue(c + NST);
-        tma_store_3d(&maps.out[0], d0, (int)t0, (int)bi, ob);
-        tma_store_3d(&maps.out[1], d0, (int)t0, (int)bi, ob + SS::kArrayBytes);
+        if (c + NST < nio) issue(c + NST);
+        tma_store_3d(&maps.out[0], d0, (int)(c * IO), (int)bi, ob);
+        tma_store_3d(&maps.out[1], d0, (int)(c * IO), (int)bi, ob + SS::kArrayBytes);
         bulk_commit();
       }
     }
-    j0 += p.nchunks;
+    j0 += nio;
   }
   if (lane == 0) bulk_wait_read();
 }
@@ -569,7 +584,7 @@ template <typename E, int NW>
 __global__ void __launch_bounds__(NW * 32, 1)
     bwd_strip_kernel(Args<E> p, const __grid_constant__ StripMaps maps) {
   using SS = WsStage<E, 4, true, NW>;
-  constexpr int NST = SS::kStages;
+  constexpr int NST = SS::kStages, IO = SS::IO, NH = SS::NH;
   extern __shared__ __align__(128) unsigned char ring[];
   __shared__ __align__(8) uint64_t full[NW][NST];
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
@@ -583,30 +598,34 @@ __global__ void __launch_bounds__(NW * 32, 1)
   unsigned char* wout = wring + (size_t)NST * SS::kBytes;  // two output buffers
   WsRing<NST> rg;
   rg.full = full[warp];
+  const long long nio = (p.nchunks + NH - 1) / NH;
   long long j0 = 0;
   for (long long strip = (long long)warp * gridDim.x + blockIdx.x; strip < p.nstrips;
        strip += (long long)NW * gridDim.x) {
     const long long bi = strip / p.sper;
     const int d0 = (int)((strip - bi * p.sper) * 32);
-    auto issue = [&](long long c) {  // lane 0: step c handles chunk nchunks - 1 - c
-      const long long chunk = p.nchunks - 1 - c;
+    auto issue = [&](long long c) {  // lane 0: step c handles IO chunk nio - 1 - c
+      const long long io = nio - 1 - c;
       const long long j = j0 + c;
       const int s = (int)(j % NST);
       unsigned char* st = wring + (size_t)s * SS::kBytes;
-      mbar_arrive_expect_tx(&rg.full[s], (unsigned)(4 * SS::kArrayBytes + SS::kCarryBytes));
+      const int nc = (int)min((long long)NH, p.nchunks - io * NH);  // carry chunks inside T
+      mbar_arrive_expect_tx(&rg.full[s], (unsigned)(4 * SS::kArrayBytes + nc * SS::kCarryBytes));
 #pragma unroll
       for (int arr = 0; arr < 4; ++arr)
-        tma_load_3d(st + arr * SS::kArrayBytes, &maps.m[arr], d0, (int)(chunk * kLc), (int)bi,
+        tma_load_3d(st + arr * SS::kArrayBytes, &maps.m[arr], d0, (int)(io * IO), (int)bi,
                     &rg.full[s]);
-      bulk_g2s(st + 4 * SS::kArrayBytes, p.carries + (size_t)(chunk * p.nstrips + strip) * 2 * 32,
-               (unsigned)SS::kCarryBytes, &rg.full[s]);
+      for (int h = 0; h < nc; ++h)
+        bulk_g2s(st + 4 * SS::kArrayBytes + h * SS::kCarryBytes,
+                 p.carries + (size_t)((io * NH + h) * p.nstrips + strip) * 2 * 32,
+                 (unsigned)SS::kCarryBytes, &rg.full[s]);
       rg.issued(s, (unsigned)(j / NST) & 1u);
     };
     if (lane == 0)
-      for (long long c = 0; c < NST && c < p.nchunks; ++c) issue(c);
+      for (long long c = 0; c < NST && c < nio; ++c) issue(c);
     float ya = 0.f, yb = 0.f;  // adjoints entering from later steps
-    for (long long c = 0; c < p.nchunks; ++c) {
-      const long long chunk = p.nchunks - 1 - c;
+    for (long long c = 0; c < nio; ++c) {
+      const long long io = nio - 1 - c;
       const long long j = j0 + c;
       const int s = (int)(j % NST);
       if (!rg.wait(s, (unsigned)(j / NST) & 1u, p.lb.err)) {
@@ -617,59 +636,62 @@ __global__ void __launch_bounds__(NW * 32, 1)
         return;
       }
       const unsigned char* st = wring + (size_t)s * SS::kBytes;
-      const E* sa = reinterpret_cast<const E*>(st) + lane;
-      const E* sb = sa + SS::kArrayBytes / sizeof(E);
-      const E* sga = sb + SS::kArrayBytes / sizeof(E);
-      const E* sgb = sga + SS::kArrayBytes / sizeof(E);
-      const float* fc = reinterpret_cast<const float*>(st + 4 * SS::kArrayBytes);
-      float fA = fc[lane], fB = fc[32 + lane];
-      const long long t0 = chunk * kLc;
       unsigned char* ob = wout + (size_t)(j & 1) * SS::kOutBytes;
       if (lane == 0) bulk_wait_read_1();  // the stores of step j - 2 have read this buffer
       __syncwarp();
-      E* oA = reinterpret_cast<E*>(ob) + lane;
-      E* oB = oA + SS::kArrayBytes / sizeof(E);
-      float ap[kLc], bp[kLc];  // states before each step of the chunk
+#pragma unroll 1
+      for (int h = NH - 1; h >= 0; --h) {  // carry chunks of this IO chunk, in reverse
+        if (io * NH + h >= p.nchunks) continue;  // past T: its rows are clipped by the stores
+        const E* sa = reinterpret_cast<const E*>(st) + h * kLc * 32 + lane;
+        const E* sb = sa + SS::kArrayBytes / sizeof(E);
+        const E* sga = sb + SS::kArrayBytes / sizeof(E);
+        const E* sgb = sga + SS::kArrayBytes / sizeof(E);
+        const float* fc = reinterpret_cast<const float*>(st + 4 * SS::kArrayBytes + h * SS::kCarryBytes);
+        float fA = fc[lane], fB = fc[32 + lane];
+        E* oA = reinterpret_cast<E*>(ob) + h * kLc * 32 + lane;
+        E* oB = oA + SS::kArrayBytes / sizeof(E);
+        float ap[kLc], bp[kLc];  // states before each step of the carry chunk
 #pragma unroll
-      for (int i = 0; i < kLc; ++i) {
-        const float a = to_f32<E>(sa[i * 32]);
-        ap[i] = fA;
-        bp[i] = fB;
-        fB = fmaf(a, fB, to_f32<E>(sb[i * 32]));
-        fA *= a;
-      }
-      // Reverse walk in groups of kGrp steps, each group's inputs read first.
-      constexpr int kGrp = 8;
-#pragma unroll
-      for (int g = kLc / kGrp - 1; g >= 0; --g) {
-        E va[kGrp], vga[kGrp], vgb[kGrp];
-#pragma unroll
-        for (int k = 0; k < kGrp; ++k) {
-          va[k] = sa[(g * kGrp + k) * 32];
-          vga[k] = sga[(g * kGrp + k) * 32];
-          vgb[k] = sgb[(g * kGrp + k) * 32];
+        for (int i = 0; i < kLc; ++i) {
+          const float a = to_f32<E>(sa[i * 32]);
+          ap[i] = fA;
+          bp[i] = fB;
+          fB = fmaf(a, fB, to_f32<E>(sb[i * 32]));
+          fA *= a;
         }
+        // Reverse walk in groups of kGrp steps, each group's inputs read first.
+        constexpr int kGrp = 8;
 #pragma unroll
-        for (int k = kGrp - 1; k >= 0; --k) {
-          const int i = g * kGrp + k;
-          const float a = to_f32<E>(va[k]);
-          const float GA = to_f32<E>(vga[k]) + ya, GB = to_f32<E>(vgb[k]) + yb;
-          ya = a * GA;
-          yb = a * GB;
-          oA[i * 32] = from_f32<E>(fmaf(GA, ap[i], GB * bp[i]));
-          oB[i * 32] = from_f32<E>(GB);
+        for (int g = kLc / kGrp - 1; g >= 0; --g) {
+          E va[kGrp], vga[kGrp], vgb[kGrp];
+#pragma unroll
+          for (int k = 0; k < kGrp; ++k) {
+            va[k] = sa[(g * kGrp + k) * 32];
+            vga[k] = sga[(g * kGrp + k) * 32];
+            vgb[k] = sgb[(g * kGrp + k) * 32];
+          }
+#pragma unroll
+          for (int k = kGrp - 1; k >= 0; --k) {
+            const int i = g * kGrp + k;
+            const float a = to_f32<E>(va[k]);
+            const float GA = to_f32<E>(vga[k]) + ya, GB = to_f32<E>(vgb[k]) + yb;
+            ya = a * GA;
+            yb = a * GB;
+            oA[i * 32] = from_f32<E>(fmaf(GA, ap[i], GB * bp[i]));
+            oB[i * 32] = from_f32<E>(GB);
+          }
         }
       }
       fence_proxy_async_smem();
       __syncwarp();
       if (lane == 0) {
-        if (c + NST < p.nchunks) issue(c + NST);
-        tma_store_3d(&maps.out[0], d0, (int)t0, (int)bi, ob);
-        tma_store_3d(&maps.out[1], d0, (int)t0, (int)bi, ob + SS::kArrayBytes);
+        if (c + NST < nio) issue(c + NST);
+        tma_store_3d(&maps.out[0], d0, (int)(io * IO), (int)bi, ob);
+        tma_store_3d(&maps.out[1], d0, (int)(io * IO), (int)bi, ob + SS::kArrayBytes);
         bulk_commit();
       }
     }
-    j0 += p.nchunks;
+    j0 += nio;
   }
   if (lane == 0) bulk_wait_read();
 }
@@ -734,12 +756,13 @@ int run(bool fwd, const void* a, const void* b, void* A, void* Bc, const void* g
     MGS_CUDA_OK(cudaMemsetAsync(ws, 0, 256, st));  // error word
     p.lb = lookback_view(ws, 0, 0);
     StripMaps maps;
+    const unsigned io = fwd ? (unsigned)ws_io<E, false>() : (unsigned)ws_io<E, true>();
     const void* src[4] = {a, b, gA, gB};
     for (int i = 0; i < (fwd ? 2 : 4); ++i)
-      if (!make_tmap_3d<E>(&maps.m[i], src[i], D, T, B, 32u, (unsigned)kLc)) return MGS_LAUNCH_FAILED;
+      if (!make_tmap_3d<E>(&maps.m[i], src[i], D, T, B, 32u, io)) return MGS_LAUNCH_FAILED;
     void* dst[2] = {fwd ? A : da, fwd ? Bc : db};
     for (int i = 0; i < 2; ++i)
-      if (!make_tmap_3d<E>(&maps.out[i], dst[i], D, T, B, 32u, (unsigned)kLc)) return MGS_LAUNCH_FAILED;
+      if (!make_tmap_3d<E>(&maps.out[i], dst[i], D, T, B, 32u, io)) return MGS_LAUNCH_FAILED;
     void* kargs[] = {&p, &maps};
     // one CTA of kWsWarps warps per SM (the rings fill its shared memory)
     const long long units = (g.nstrips + kWsWarps - 1) / kWsWarps;
