@@ -170,31 +170,35 @@ __device__ __forceinline__ void apply_Mt(float (&a)[K], const StepCoef<K, R>& cf
   if (hs) a[1] *= cf.scale;
 }
 
-// X <- M X + [0 | bvec] on all K+1 columns of the aggregate.
+// X <- M X + [0 | bvec] on all K+1 columns of the aggregate. Without a scale
+// M = gamma R (R a product of rotations), so the P columns can take R alone
+// (pd = false) and the caller multiplies them by the product of the gammas
+// once per tile: the decay then costs K multiplies per step instead of K^2 + K.
 template <int K, int R>
 __device__ __forceinline__ void agg_step(float (&X)[K * (K + 1)], const StepCoef<K, R>& cf,
-                                         const float (&bv)[K], bool hs, bool hd) {
+                                         const float (&bv)[K], bool hs, bool hd, bool pd) {
 #pragma unroll
   for (int j = 0; j <= K; ++j) {
     float col[K];
 #pragma unroll
     for (int i = 0; i < K; ++i) col[i] = X[i * (K + 1) + j];
-    apply_M<K, R>(col, cf, hs, hd);
+    apply_M<K, R>(col, cf, hs, j == K ? hd : pd);
 #pragma unroll
     for (int i = 0; i < K; ++i) X[i * (K + 1) + j] = col[i] + (j == K ? bv[i] : 0.f);
   }
 }
 
-// Reverse aggregate step: Q <- M^T (g + Q), P <- M^T P (columns 0..K-1 = P, K = Q).
+// Reverse aggregate step: Q <- M^T (g + Q), P <- M^T P (columns 0..K-1 = P,
+// K = Q); pd as in agg_step.
 template <int K, int R>
 __device__ __forceinline__ void ragg_step(float (&X)[K * (K + 1)], const StepCoef<K, R>& cf,
-                                          const float (&g)[K], bool hs, bool hd) {
+                                          const float (&g)[K], bool hs, bool hd, bool pd) {
 #pragma unroll
   for (int j = 0; j <= K; ++j) {
     float col[K];
 #pragma unroll
     for (int i = 0; i < K; ++i) col[i] = X[i * (K + 1) + j] + (j == K ? g[i] : 0.f);
-    apply_Mt<K, R>(col, cf, hs, hd);
+    apply_Mt<K, R>(col, cf, hs, j == K ? hd : pd);
 #pragma unroll
     for (int i = 0; i < K; ++i) X[i * (K + 1) + j] = col[i];
   }
@@ -481,13 +485,21 @@ __global__ void __launch_bounds__(kLanes) fwd_tile_kernel(Args<E> p) {
   };
   float X[NF];
   AffMonoid<K>::identity(X);
+  const bool pd = hd && hs;  // decay inside the P columns only when a scale is present
+  float gprod = 1.f;
   stream_steps<1, SI>(t0, t1 - t0, 1, load, [&](const SI& q, long long) {
     StepCoef<K, R> cf;
     q.coef(cf, hs, hd);
     float bv[K];
     q.x.get(bv);
-    agg_step<K, R>(X, cf, bv, hs, hd);
+    agg_step<K, R>(X, cf, bv, hs, hd, pd);
+    gprod *= cf.gamma;
   });
+  if (hd && !pd)
+#pragma unroll
+    for (int i = 0; i < K; ++i)
+#pragma unroll
+      for (int j = 0; j < K; ++j) X[i * (K + 1) + j] *= gprod;
   float v[K];
   if (tile == 0) {
     Vec<E, K>::load(p.h0 + ((size_t)bi * p.n + blk) * K, v);
@@ -540,13 +552,21 @@ __global__ void __launch_bounds__(kLanes) bwd_tile_kernel(Args<E> p) {
   };
   float X[NF];
   AffMonoid<K>::identity(X);
+  const bool pd = hd && hs;  // decay inside the P columns only when a scale is present
+  float gprod = 1.f;
   stream_steps<1, SA>(t1 - 1, t1 - t0, -1, load_a, [&](const SA& q, long long) {
     StepCoef<K, R> cf;
     q.coef(cf, hs, hd);
     float g[K];
     q.x.get(g);
-    ragg_step<K, R>(X, cf, g, hs, hd);
+    ragg_step<K, R>(X, cf, g, hs, hd, pd);
+    gprod *= cf.gamma;
   });
+  if (hd && !pd)
+#pragma unroll
+    for (int i = 0; i < K; ++i)
+#pragma unroll
+      for (int j = 0; j < K; ++j) X[i * (K + 1) + j] *= gprod;
   float y[K];
   if (rtile == 0) {
 #pragma unroll
