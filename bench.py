@@ -398,8 +398,12 @@ class DeltaWorkload(ScanWorkload):
         # bwd reads Q, K, V, beta, dy and writes dQ, dK, dV, dbeta.
         self.fwd_bytes = (4 * d + 1) * e / d
         self.bwd_bytes = (7 * d + 2) * e / d
-        # FLOPs of the reference chunked-WY algorithm per (b, h, chunk): fwd 3.40 M, bwd 8.90 M
-        self.flops = (3.40e6 + 8.90e6) * B * H * (T // chunk)
+
+    @property
+    def flops(self) -> float:
+        """FLOPs of the reference chunked-WY algorithm per step: fwd 3.40 M and bwd
+        8.90 M per (b, h, chunk)."""
+        return (3.40e6 + 8.90e6) * self.B * self.H * (self.T // self.chunk)
 
     def make_host(self, rows, seed):
         g = torch.Generator().manual_seed(seed)
@@ -474,6 +478,9 @@ WORKLOADS = {
     "cfg3": lambda: MatrixScanWorkload(),
     "cfg4": lambda: AngleScanWorkload(),
     "cfg5": lambda: DeltaWorkload(),
+    # BASELINE config 5's multi-GPU case: global batch 64 (with --scaling strong,
+    # split 32 / 16 / 8 per GPU over 2 / 4 / 8 GPUs)
+    "cfg5-b64": lambda: DeltaWorkload(B=64, name="cfg5-b64"),
 }
 
 
@@ -606,28 +613,28 @@ def host_threads() -> int:
     return n
 
 
-def time_cpu_baseline(w, target_s: float = 12.0) -> dict:
+def cpu_rows(w, requested: int) -> int:
+    """Batch rows of one CPU sample; the same rule for the `cpu_baseline` leg
+    and the `--impl reference` arm, so both time the same rows."""
+    return max(1, min(w.B, requested))
+
+
+def time_cpu_baseline(w, rows: int, reps: int = 3) -> dict:
     threads = host_threads()
-    rows = 1
+    rows = cpu_rows(w, rows)
     sample = w.cpu_sample(rows)
-    w.cpu_step(sample)  # first call also loads the oracle library
-    t0 = time.perf_counter()
-    w.cpu_step(sample)
-    one = time.perf_counter() - t0
-    rows = int(max(1, min(w.B, target_s / max(one, 1e-3) / 2)))
-    sample = w.cpu_sample(rows)
-    w.cpu_step(sample)  # warm-up
+    w.cpu_step(sample)  # warm-up (the first call also loads the oracle library)
     times = []
-    for _ in range(2):
+    for _ in range(reps):
         t0 = time.perf_counter()
         w.cpu_step(sample)
         times.append(time.perf_counter() - t0)
-    dt = min(times)
+    dt = statistics.median(times)
     elems = w.sample_elems(rows)
     return {"value": elems / dt / 1e9, "unit": "Gelem/s", "cores": threads, "kind": "port",
             "sample": f"{w.sample_desc(rows)} fwd+bwd through the CPU oracle "
                       f"(restatement of the reference algorithm, {threads} threads), "
-                      "best of 2 after 1 warm-up"}
+                      f"median of {reps} after 1 warm-up"}
 
 
 
@@ -636,7 +643,7 @@ def run_reference(args, w) -> None:
     if rank != 0:
         return
     threads = host_threads()
-    rows = max(1, min(w.B, args.ref_rows))
+    rows = cpu_rows(w, args.ref_rows)
     sample = w.cpu_sample(rows)
     for _ in range(args.warmup):
         w.cpu_step(sample)
@@ -649,7 +656,7 @@ def run_reference(args, w) -> None:
     line = {
         "impl": "reference", "metric": "scan fwd+bwd Gelem/s", "value": val, "unit": "Gelem/s",
         "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
-        "ms_per_step": dt * 1e3, "higher_is_better": True, "scaling": "weak",
+        "ms_per_step": dt * 1e3, "higher_is_better": True, "scaling": args.scaling,
         "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded, BASELINE shapes)",
         "config": w.config(args.gpus),
         "cpu_baseline": {"value": val, "unit": "Gelem/s", "cores": threads, "kind": "port",
@@ -699,82 +706,148 @@ def time_graph(g, reps: int, dev, flush=None) -> float:
     return e0.elapsed_time(e1) / reps
 
 
+def gpu_numa_cpus(dev) -> tuple[int | None, set[int] | None]:
+    """NUMA node of the GPU's PCIe device and that node's CPUs (None if unknown)."""
+    try:
+        pr = torch.cuda.get_device_properties(dev)
+        bus = f"{pr.pci_domain_id:04x}:{pr.pci_bus_id:02x}:{pr.pci_device_id:02x}.0"
+    except AttributeError:
+        return None, None
+    try:
+        node = int(Path(f"/sys/bus/pci/devices/{bus}/numa_node").read_text())
+        if node < 0:
+            return None, None
+        cpus: set[int] = set()
+        for part in Path(f"/sys/devices/system/node/node{node}/cpulist").read_text().split(","):
+            lo, _, hi = part.strip().partition("-")
+            cpus.update(range(int(lo), int(hi or lo) + 1))
+        return node, cpus & os.sched_getaffinity(0)
+    except (OSError, ValueError):
+        return None, None
+
+
+class NumaLocal:
+    """Run a block on the CPUs of the GPU's NUMA node, so the pinned host buffers
+    it allocates (first touch) are local to the GPU's PCIe root; the previous
+    affinity is restored afterwards."""
+
+    def __init__(self, dev):
+        self.node, self.cpus = gpu_numa_cpus(dev)
+        self.saved = None
+
+    def __enter__(self):
+        if self.cpus:
+            self.saved = os.sched_getaffinity(0)
+            os.sched_setaffinity(0, self.cpus)
+        return self
+
+    def __exit__(self, *exc):
+        if self.saved is not None:
+            os.sched_setaffinity(0, self.saved)
+
+
 def run_ours(args, w) -> None:
     rank, world, local = dist_setup(args.gpus)
     dev = torch.device("cuda", local)
     torch.cuda.set_device(dev)
     import mingru_b200 as mb
 
+    if args.scaling == "strong":  # the configuration's batch is the global batch
+        if w.B % world:
+            raise SystemExit(f"--scaling strong: global batch {w.B} does not split over {world} GPUs")
+        w.global_B = w.B
+        w.B //= world
     host = w.host_inputs(rank)
-    st = w.device_setup(host, dev)
-    for _ in range(args.warmup):
-        w.step(st)
-    torch.cuda.synchronize(dev)
-    mb.raise_device_error(dev)
-
-    # One step = forward + backward of the op, replayed as a CUDA graph so the
-    # device, not Python dispatch, sets the pace (every kernel of the step runs
-    # on every replay; inputs stay resident in HBM).
-    graph = None
-    if not args.no_graph:
-        graph, _keep = capture(lambda: w.step(st), dev)
-
-    # Inputs smaller than L2 would be served from cache on back-to-back steps:
-    # then every step is timed alone, after writing a buffer larger than L2.
-    flush = None
-    if w.footprint_bytes < L2_FLUSH_THRESHOLD:
-        flush = torch.empty(FLUSH_BYTES, dtype=torch.uint8, device=dev)
-    run_step = (graph.replay if graph is not None else (lambda: w.step(st)))
-    start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
-           for _ in range(args.steps)] if flush is not None else []
-    barrier(world, dev)
-    torch.cuda.synchronize(dev)
-    with ClockSampler(dev.index) as clk:
-        clk.mark_start()
-        start.record()
-        for i in range(args.steps):
-            if flush is not None:
-                flush.fill_(i & 255)
-                evs[i][0].record()
-            run_step()
-            if flush is not None:
-                evs[i][1].record()
-        stop.record()
+    # Every kernel of the run is issued on one stream: warm-up, graph capture,
+    # the per-kernel graphs and the e2e compute (so each autograd leaf sees its
+    # forward and backward on the same stream).
+    work = torch.cuda.Stream(dev)
+    with torch.cuda.stream(work):
+        st = w.device_setup(host, dev)
+        for _ in range(args.warmup):
+            w.step(st)
         torch.cuda.synchronize(dev)
-        clk.mark_stop()
-    barrier(world, dev)
-    local_ms = (sum(a.elapsed_time(b) for a, b in evs) if flush is not None
-                else start.elapsed_time(stop))
-    ms = max_over_ranks(local_ms, world, dev)
-    mb.raise_device_error(dev)
+        mb.raise_device_error(dev)
 
-    # Per-kernel device time: each op captured alone and replayed.
-    ins, cots = st["ins"], st["cots"]
-    with torch.no_grad():
-        gf, _kf = capture(lambda: w.forward(*ins), dev)
-    bstream = torch.cuda.Stream(dev)
-    bstream.wait_stream(torch.cuda.current_stream(dev))
-    with torch.cuda.stream(bstream):  # backward nodes replay on the forward's stream
+        # One step = forward + backward of the op, replayed as a CUDA graph so
+        # the device, not Python dispatch, sets the pace (every kernel of the
+        # step runs on every replay; inputs stay resident in HBM).
+        graph = None
+        if not args.no_graph:
+            graph, _keep = capture(lambda: w.step(st), dev, stream=work)
+
+        # Inputs smaller than L2 would be served from cache on back-to-back
+        # steps: then every step is timed alone, after writing a buffer larger
+        # than L2.
+        flush = None
+        if w.footprint_bytes < L2_FLUSH_THRESHOLD:
+            flush = torch.empty(FLUSH_BYTES, dtype=torch.uint8, device=dev)
+        run_step = (graph.replay if graph is not None else (lambda: w.step(st)))
+
+        def window() -> float:
+            """Exactly `steps` steps bracketed by a barrier and a synchronize on
+            both sides; device ms (max over ranks)."""
+            start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+                   for _ in range(args.steps)] if flush is not None else []
+            barrier(world, dev)
+            torch.cuda.synchronize(dev)
+            start.record()
+            for i in range(args.steps):
+                if flush is not None:
+                    flush.fill_(i & 255)
+                    evs[i][0].record()
+                run_step()
+                if flush is not None:
+                    evs[i][1].record()
+            stop.record()
+            torch.cuda.synchronize(dev)
+            barrier(world, dev)
+            local_ms = (sum(a.elapsed_time(b) for a, b in evs) if flush is not None
+                        else start.elapsed_time(stop))
+            return max_over_ranks(local_ms, world, dev)
+
+        # Several windows of K steps each (enough for a few clock samples), the
+        # median reported; every rank runs the same number of windows.
+        with ClockSampler(dev.index) as clk:
+            clk.mark_start()
+            t0 = time.perf_counter()
+            wins = [window()]
+            first_s = time.perf_counter() - t0
+            n_win = int(max_over_ranks(
+                float(max(1, min(args.max_windows, math.ceil(args.min_seconds / max(first_s, 1e-4))))),
+                world, dev))
+            for _ in range(n_win - 1):
+                wins.append(window())
+            clk.mark_stop()
+        ms = statistics.median(wins)
+        mb.raise_device_error(dev)
+
+        # Per-kernel device time: each op captured alone and replayed.
+        ins, cots = st["ins"], st["cots"]
+        with torch.no_grad():
+            gf, _kf = capture(lambda: w.forward(*ins), dev, stream=work)
         outs = w.forward(*ins)
-    gb, _kb = capture(lambda: torch.autograd.grad(outs, ins, cots, retain_graph=True), dev,
-                      stream=bstream)
-    reps = max(10, min(200, args.steps))
-    fwd_ms = time_graph(gf, reps, dev, flush)
-    bwd_ms = time_graph(gb, reps, dev, flush)
-    del gf, gb, _kf, _kb, outs, graph
+        gb, _kb = capture(lambda: torch.autograd.grad(outs, ins, cots, retain_graph=True), dev,
+                          stream=work)
+        reps = max(10, min(200, args.steps))
+        fwd_ms = time_graph(gf, reps, dev, flush)
+        bwd_ms = time_graph(gb, reps, dev, flush)
+        del gf, gb, _kf, _kb, outs, graph
 
-    # ---- e2e: public API with pinned host buffers, copies inside the timed region
-    est = w.e2e_setup(host, dev)
-    e2e_pipeline(w, est, max(1, min(args.warmup, 3)), dev)
-    torch.cuda.synchronize(dev)
-    e_steps = max(1, min(args.steps, args.e2e_steps))
-    barrier(world, dev)
-    torch.cuda.synchronize(dev)
-    e_ms = max_over_ranks(e2e_pipeline(w, est, e_steps, dev), world, dev)
-    barrier(world, dev)
+        # ---- e2e: public API with pinned host buffers, copies inside the timed region
+        with NumaLocal(dev) as numa:
+            est = w.e2e_setup(host, dev)
+        e2e_pipeline(w, est, max(1, min(args.warmup, 3)), dev)
+        torch.cuda.synchronize(dev)
+        e_steps = max(1, min(args.steps, args.e2e_steps))
+        barrier(world, dev)
+        torch.cuda.synchronize(dev)
+        e_ms = max_over_ranks(e2e_pipeline(w, est, e_steps, dev), world, dev)
+        barrier(world, dev)
 
-    cpu = time_cpu_baseline(w) if (rank == 0 and world == 1 and not args.no_cpu) else None
+    cpu = (time_cpu_baseline(w, args.ref_rows)
+           if (rank == 0 and world == 1 and not args.no_cpu) else None)
     if world > 1:
         import torch.distributed as dist
 
@@ -791,6 +864,14 @@ def run_ours(args, w) -> None:
     dom_bytes = (w.bwd_bytes if dom == "bwd" else w.fwd_bytes) * w.elems
     achieved = dom_bytes / (dom_ms * 1e-3) / 1e9
     key = f"{w.kernels[dom]}:{w.name}"
+    cfg = dict(w.config(world), step="cuda-graph replay" if not args.no_graph else "eager",
+               windows=f"median of {len(wins)} windows of {args.steps} steps "
+                       f"(window ms min/median/max {min(wins):.3f}/{ms:.3f}/{max(wins):.3f})",
+               host_numa_node=numa.node)
+    if args.scaling == "strong":
+        cfg.update(global_batch=w.global_B, B_per_gpu=w.B,
+                   parallelism=f"batch-sharded x{world} (global batch {w.global_B} split "
+                               f"{w.B} per GPU), no collective")
     line = {
         "metric": "scan fwd+bwd Gelem/s",
         "value": total_elems * args.steps / (ms * 1e-3) / 1e9,
@@ -800,11 +881,11 @@ def run_ours(args, w) -> None:
         "warmup": args.warmup,
         "ms_per_step": per_step_ms,
         "higher_is_better": True,
-        "scaling": "weak",
+        "scaling": args.scaling,
         "vs_baseline": None,
         "dtype": w.compute_dtype,
         "data": "synthetic (seeded, BASELINE shapes)",
-        "config": dict(w.config(world), step="cuda-graph replay" if not args.no_graph else "eager"),
+        "config": cfg,
         "tflops": (w.flops / (per_step_ms * 1e-3) / 1e12) if hasattr(w, "flops") else None,
         "kernel_ms": {"fwd": fwd_ms, "bwd": bwd_ms},
         "roofline": {
@@ -826,9 +907,10 @@ def run_ours(args, w) -> None:
             "unit": "Gelem/s",
             "h2d_bytes_per_step": w.h2d_bytes,
             "d2h_bytes_per_step": w.d2h_bytes,
-            "path": "public op + autograd (C ABI) from pinned host buffers, eager; each step's "
-                    "host-to-device copy, compute and device-to-host copy on three streams, so one "
-                    "step's inputs cross PCIe while the previous step's results come back",
+            "path": "public op + autograd (C ABI) from pinned host buffers (allocated on the "
+                    "GPU's NUMA node), eager; each step's host-to-device copy, compute and "
+                    "device-to-host copy on three streams, so one step's inputs cross PCIe while "
+                    "the previous step's results come back",
         },
         "gpu_launches": w.launches_per_step * args.steps,
         "clocks": clk.summary(),
@@ -886,7 +968,14 @@ def main() -> None:
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--config", choices=sorted(WORKLOADS), default="cfg2")
     ap.add_argument("--e2e-steps", type=int, default=5)
-    ap.add_argument("--ref-rows", type=int, default=2, help="batch rows per reference step")
+    ap.add_argument("--ref-rows", type=int, default=2,
+                    help="batch rows of each CPU sample (reference arm and cpu_baseline)")
+    ap.add_argument("--scaling", choices=["weak", "strong"], default="weak",
+                    help="weak: the configuration's batch on every GPU; strong: it is the global "
+                         "batch, split over the GPUs")
+    ap.add_argument("--min-seconds", type=float, default=0.5,
+                    help="time windows of --steps steps until about this long has run")
+    ap.add_argument("--max-windows", type=int, default=50)
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
     ap.add_argument("--no-graph", action="store_true", help="time eager steps instead of graph replay")
     ap.add_argument("--batch", type=int, default=None,

@@ -108,6 +108,27 @@ int mgs_linear_scan_fwd_noalloc(const void* a, const void* b, void* A, void* Bc,
                                 int64_t B, int64_t T, int64_t D, int dtype, void* stream);
 
 /* ------------------------------------------------------------------------ */
+/* Time-out test hooks. No counterpart in the reference (its Triton kernels
+ * have no cross-CTA waits). Each makes one bounded device-side wait run out
+ * on purpose, with a poll bound of `spin_limit`, so that a test can check the
+ * time-out path end to end: the launch completes, the error words carry
+ * MGS_LOOKBACK_TIMEOUT, mgs_take_device_error reports it and the context
+ * stays usable. Nothing here can hang: every wait involved is bounded.
+ *
+ * mgs_test_lookback_timeout: the fp32 linear_scan forward on its look-back
+ * path (shapes too narrow for the strip path, T > 64) with the tile counter
+ * started at 1, so the look-back behind tile 0 waits on a flag that nothing
+ * sets; the workspace header's error word (offset 4) receives the bit.
+ * Returns MGS_UNSUPPORTED for shapes that do not take that path. Outputs of
+ * the first tile are left unwritten.
+ * mgs_test_mbarrier_timeout: one CTA waits on an mbarrier nothing arrives on;
+ * `err_word` (device u32) receives the bit.                                   */
+int mgs_test_lookback_timeout(const void* a, const void* b, void* A, void* Bc, int64_t B,
+                              int64_t T, int64_t D, void* workspace, size_t workspace_bytes,
+                              int64_t spin_limit, void* stream);
+int mgs_test_mbarrier_timeout(void* err_word, int64_t spin_limit, void* stream);
+
+/* ------------------------------------------------------------------------ */
 /* parallel_scan_log: h_t = a_t h_{t-1} + b_t in log space, a_t =
  * exp(log_coeffs[:, t-1]), b_t = exp(log_values[:, t]), h_0 =
  * exp(log_values[:, 0]); returns h_1..h_T.

@@ -37,6 +37,9 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "mgs_linear_scan_fwd": (_int, [_p, _p, _p, _p, _p, _i64, _i64, _i64, _int, _p, _sz, _p]),
     "mgs_linear_scan_bwd": (_int, [_p, _p, _p, _p, _p, _p, _p, _i64, _i64, _i64, _int, _p, _sz, _p]),
     "mgs_linear_scan_fwd_noalloc": (_int, [_p, _p, _p, _p, _p, _i64, _i64, _i64, _int, _p]),
+    "mgs_test_lookback_timeout": (
+        _int, [_p, _p, _p, _p, _i64, _i64, _i64, _p, _sz, _i64, _p]),
+    "mgs_test_mbarrier_timeout": (_int, [_p, _i64, _p]),
     "mgs_log_scan_workspace_size": (_sz, [_i64, _i64, _i64, _int]),
     "mgs_log_scan_carry_size": (_sz, [_i64, _i64, _i64, _int]),
     "mgs_log_scan_fwd": (_int, [_p, _p, _p, _p, _i64, _i64, _i64, _int, _p, _sz, _p]),

@@ -10,6 +10,7 @@ unsigned take_error_linear(cudaStream_t s);
 unsigned take_error_log(cudaStream_t s);
 unsigned take_error_affine(cudaStream_t s);
 unsigned take_error_angle(cudaStream_t s);
+unsigned take_error_delta_tc(cudaStream_t s);
 }  // namespace mgs
 
 extern "C" {
@@ -37,6 +38,7 @@ int mgs_take_device_error(void* stream) {
   bits |= mgs::take_error_log(s);
   bits |= mgs::take_error_affine(s);
   bits |= mgs::take_error_angle(s);
+  bits |= mgs::take_error_delta_tc(s);
   return (int)bits;
 }
 

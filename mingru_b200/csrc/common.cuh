@@ -126,6 +126,7 @@ struct Lookback {
   unsigned* flags;
   float* agg;
   float* incl;
+  long long spin;  // poll bound of each wait (kSpinLimit; tests pass a small one)
 };
 
 // Sticky error word of this translation unit (each .cu file that includes
@@ -165,6 +166,7 @@ inline Lookback lookback_view(void* ws, long long ntiles, int nf) {
   size_t flags = align_up((size_t)ntiles * 4, 256);
   lb.agg = reinterpret_cast<float*>(base + 256 + flags);
   lb.incl = lb.agg + (size_t)ntiles * nf * 32;
+  lb.spin = kSpinLimit;
   return lb;
 }
 
@@ -188,7 +190,7 @@ __device__ __forceinline__ unsigned lb_wait(const Lookback& lb, long long tile) 
   unsigned f = ld_acquire_u32(lb.flags + tile);
   long long it = 0;
   while (f == kFlagEmpty) {
-    if (++it > kSpinLimit) {
+    if (++it > lb.spin) {
       atomicOr(lb.err, kErrTimeout);
       atomicOr(&g_sticky_err, kErrTimeout);
       f = kFlagIncl;  // proceed with whatever is there; the host raises
@@ -278,7 +280,7 @@ __device__ __forceinline__ void warp_lookback_win(const Lookback& lb, long long 
       const bool need = lane <= last;
       const unsigned em = __ballot_sync(0xffffffffu, need && f == kFlagEmpty);
       if (em == 0u) break;
-      if (++it > kSpinLimit) {
+      if (++it > lb.spin) {
         if (lane == 0) {
           atomicOr(lb.err, kErrTimeout);
           atomicOr(&g_sticky_err, kErrTimeout);
@@ -368,7 +370,7 @@ __device__ __forceinline__ void warp_lookback_win_smem(const Lookback& lb, long 
       const bool need = lane <= last;
       const unsigned em = __ballot_sync(0xffffffffu, need && f == kFlagEmpty);
       if (em == 0u) break;
-      if (++it > kSpinLimit) {
+      if (++it > lb.spin) {
         if (lane == 0) {
           atomicOr(lb.err, kErrTimeout);
           atomicOr(&g_sticky_err, kErrTimeout);
@@ -452,11 +454,12 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, unsigned parity) {
 }
 
 // Bounded wait for an mbarrier phase; returns false (after recording a
-// timeout) if the phase never completes.
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, unsigned parity, unsigned* err) {
+// timeout) if the phase never completes within `limit` polls.
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, unsigned parity, unsigned* err,
+                                          long long limit = kSpinLimit) {
   long long it = 0;
   while (!mbar_try_wait(bar, parity)) {
-    if (++it > kSpinLimit) {
+    if (++it > limit) {
       atomicOr(err, kErrTimeout);
       atomicOr(&g_sticky_err, kErrTimeout);
       return false;

@@ -317,7 +317,10 @@ __global__ void __launch_bounds__(kGradThreads, 2) bwd_grads_kernel(const TcArgs
   }
   if (tid < 64) bs[tid] = tid < Mc ? __bfloat162float(p.beta[bh * rows + r0 + tid]) : 0.f;
   cp_async_wait_all();
-  mbar_wait(bar + 1, 0, &g_sticky_err);
+  // okw: every wait so far completed. A wait that runs out records the time-out
+  // (sticky word) and from then on this CTA issues no MMA, waits on nothing and
+  // writes no output; to_mma makes the flag the same in every thread.
+  bool okw = mbar_wait(bar + 1, 0, &g_sticky_err);
   const uint32_t tb = *tbase_s;
   const uint32_t tA = tb, tB = tb + 64, tC = tb + 128, tD = tb + 192;
   const uint32_t lb = tb + ((uint32_t)(32 * q) << 16) + 32 * hh;  // this warp's accumulator window
@@ -328,11 +331,11 @@ __global__ void __launch_bounds__(kGradThreads, 2) bwd_grads_kernel(const TcArgs
   auto to_mma = [&]() {
     fence_proxy_async_smem();
     um::fence_before();
-    __syncthreads();
+    okw = !__syncthreads_or(!okw);
     um::fence_after();
   };
   auto wait_mma = [&]() {
-    mbar_wait(bar, phase, &g_sticky_err);
+    if (okw) okw = mbar_wait(bar, phase, &g_sticky_err);
     phase ^= 1u;
     um::fence_after();
   };
@@ -342,13 +345,13 @@ __global__ void __launch_bounds__(kGradThreads, 2) bwd_grads_kernel(const TcArgs
 
   // level 1
   to_mma();
-  if (tid == 0) {
+  if (okw && tid == 0) {
     const um::Opnd oTi = um::opnd(S_(TiH), S_(TiL), false);
     const um::Prod ps[2] = {{tA, oTi, um::opnd(S_(K), 0, true), false},
                             {tB, oTi, um::opnd(S_(V), 0, true), false}};
     um::products(ps);
     um::commit(bar);
-  } else if (tid == 32) {
+  } else if (okw && tid == 32) {
     const um::Prod ps[2] = {{tC, um::opnd(S_(K), 0, false), um::opnd(S_(DH), S_(DL), true), false},
                             {tD, um::opnd(S_(Q), 0, false), um::opnd(S_(K), 0, false), false}};
     um::products(ps);
@@ -378,11 +381,11 @@ __global__ void __launch_bounds__(kGradThreads, 2) bwd_grads_kernel(const TcArgs
   }
   // level 2
   to_mma();
-  if (tid == 0) {
+  if (okw && tid == 0) {
     const um::Prod ps[1] = {{tB, um::opnd(S_(WH), S_(WL), false), um::opnd(S_(SH), S_(SL), true), true}};
     um::products(ps);
     um::commit(bar);
-  } else if (tid == 32) {
+  } else if (okw && tid == 32) {
     const um::Prod ps[1] = {{tA, um::opnd(S_(PH), S_(PL), true), um::opnd(S_(dY), 0, true), false}};
     um::products(ps);
     um::commit(bar);
@@ -417,13 +420,13 @@ __global__ void __launch_bounds__(kGradThreads, 2) bwd_grads_kernel(const TcArgs
   }
   // level 3
   to_mma();
-  if (tid == 0) {  // G = Ti^T dU as (Ti^T dU_hi) + (Ti_hi^T dU_lo) in C and D
+  if (okw && tid == 0) {  // G = Ti^T dU as (Ti^T dU_hi) + (Ti_hi^T dU_lo) in C and D
     const um::Prod ps[2] = {
         {tC, um::opnd(S_(TiH), S_(TiL), true), um::opnd(S_(dUH), 0, true), false},
         {tD, um::opnd(S_(TiH), 0, true), um::opnd(S_(dUL), 0, true), false}};
     um::products(ps);
     um::commit(bar);
-  } else if (tid == 32) {  // U dS'^T in A
+  } else if (okw && tid == 32) {  // U dS'^T in A
     const um::Prod ps[1] = {{tA, um::opnd(S_(UH), S_(UL), false), um::opnd(S_(DH), S_(DL), false), false}};
     um::products(ps);
     um::commit(bar);
@@ -445,7 +448,7 @@ __global__ void __launch_bounds__(kGradThreads, 2) bwd_grads_kernel(const TcArgs
     if (rv) {
 #pragma unroll
       for (int i = 0; i < 16; ++i) g[i] += g2[i];
-      if (row < Mc) row16_to_global(p.dV + (bh * rows + r0 + row) * p.dv, c0, p.dv, g);
+      if (okw && row < Mc) row16_to_global(p.dV + (bh * rows + r0 + row) * p.dv, c0, p.dv, g);
 #pragma unroll
       for (int i = 0; i < 16; ++i) g[i] = -g[i];
       um::store_split16(GH, GL, row, c0, g);
@@ -453,12 +456,12 @@ __global__ void __launch_bounds__(kGradThreads, 2) bwd_grads_kernel(const TcArgs
   }
   // level 4
   to_mma();
-  if (tid == 0) {  // Gn U^T in B, K K^T in C
+  if (okw && tid == 0) {  // Gn U^T in B, K K^T in C
     const um::Prod ps[2] = {{tB, um::opnd(S_(GH), S_(GL), false), um::opnd(S_(UH), S_(UL), false), false},
                             {tC, um::opnd(S_(K), 0, false), um::opnd(S_(K), 0, false), false}};
     um::products(ps);
     um::commit(bar);
-  } else if (tid == 32) {  // dy U^T in A, Q K^T in D
+  } else if (okw && tid == 32) {  // dy U^T in A, Q K^T in D
     const um::Prod ps[2] = {{tA, um::opnd(S_(dY), 0, false), um::opnd(S_(UH), S_(UL), false), false},
                             {tD, um::opnd(S_(Q), 0, false), um::opnd(S_(K), 0, false), false}};
     um::products(ps);
@@ -516,14 +519,14 @@ __global__ void __launch_bounds__(kGradThreads, 2) bwd_grads_kernel(const TcArgs
   }
   // level 5
   to_mma();
-  if (tid == 0) {  // dQ in A, Gn S^T in C
+  if (okw && tid == 0) {  // dQ in A, Gn S^T in C
     const um::Opnd oS = um::opnd(S_(SH), S_(SL), false);
     const um::Prod ps[3] = {{tA, um::opnd(S_(dY), 0, false), oS, false},
                             {tC, um::opnd(S_(GH), S_(GL), false), oS, false},
                             {tA, um::opnd(S_(dSH), S_(dSL), false), um::opnd(S_(K), 0, true), true}};
     um::products(ps);
     um::commit(bar);
-  } else if (tid == 32) {  // dS_^T Q + dKK K in B, dKK^T K in D
+  } else if (okw && tid == 32) {  // dS_^T Q + dKK K in B, dKK^T K in D
     const um::Opnd oKmn = um::opnd(S_(K), 0, true);
     const um::Prod ps[3] = {{tB, um::opnd(S_(dSH), S_(dSL), true), um::opnd(S_(Q), 0, true), false},
                             {tD, um::opnd(S_(dKH), S_(dKL), true), oKmn, false},
@@ -546,8 +549,8 @@ __global__ void __launch_bounds__(kGradThreads, 2) bwd_grads_kernel(const TcArgs
     um::ld_bind(r2, v2);
     um::ld_bind(r3, v3);
     um::ld_bind(r4, v4);
-    if (rv && row < Cc) row16_to_global(p.dQ + (bh * p.T + t0 + row) * p.dk, c0, p.dk, v);
-    if (rv && row < Mc) {
+    if (okw && rv && row < Cc) row16_to_global(p.dQ + (bh * p.T + t0 + row) * p.dk, c0, p.dk, v);
+    if (okw && rv && row < Mc) {
       const float b = bs[row];
 #pragma unroll
       for (int i = 0; i < 16; ++i) v2[i] += v3[i] + v4[i] + b * uds[half][i];
@@ -556,7 +559,7 @@ __global__ void __launch_bounds__(kGradThreads, 2) bwd_grads_kernel(const TcArgs
   }
   um::fence_before();
   __syncthreads();
-  if (tid < Mc) {  // dbeta = row sums of U * dbU + column sums of the masked products
+  if (okw && tid < Mc) {  // dbeta = row sums of U * dbU + column sums of the masked products
     const int h2 = tid >> 5, cl = tid & 31;
     const float d = (rpart[tid] + rpart[64 + tid]) +
                     (cpart[(4 * h2) * 32 + cl] + cpart[(4 * h2 + 1) * 32 + cl]) +
@@ -648,10 +651,14 @@ __global__ void __launch_bounds__(kPrepThreads, 2) prep_kernel(const TcArgs p) {
   cp_async_commit();
   if (tid < 64) bs[tid] = tid < Mc ? __bfloat162float(p.beta[bh * rows + r0 + tid]) : 0.f;
   cp_async_wait_all();
+  // okw: every wait so far completed. After a wait that runs out (recorded in
+  // the sticky word) the CTA issues no MMA, waits on nothing and writes no
+  // output; to_mma makes the flag the same in every thread.
+  bool okw = true;
   auto to_mma = [&]() {
     fence_proxy_async_smem();
     um::fence_before();
-    __syncthreads();
+    okw = !__syncthreads_or(!okw);
     um::fence_after();
   };
   to_mma();
@@ -665,7 +672,7 @@ __global__ void __launch_bounds__(kPrepThreads, 2) prep_kernel(const TcArgs p) {
     um::products(ps);
     um::commit(bar);
   }
-  mbar_wait(bar, 0, &g_sticky_err);
+  okw = mbar_wait(bar, 0, &g_sticky_err);
   um::fence_after();
   {  // row r = 32 q + lane of the M = 128 accumulator: T row r (r < 64) or P~ row r - 64
     const int r = 32 * q + lane;
@@ -691,7 +698,7 @@ __global__ void __launch_bounds__(kPrepThreads, 2) prep_kernel(const TcArgs p) {
     }
   }
   um::fence_before();
-  __syncthreads();
+  okw = !__syncthreads_or(!okw);
   tri_inv_tc(Td, Op{TH, TL}, XH, XL, YH, YL);  // ends with __syncthreads
   for (int i = tid; i < 64 * 8; i += NTH) {  // padded X -> blocked T^{-1} (over Y)
     const int row = i >> 3, ch = i & 7;
@@ -701,19 +708,19 @@ __global__ void __launch_bounds__(kPrepThreads, 2) prep_kernel(const TcArgs p) {
         *reinterpret_cast<const uint4*>(XL + row * kLd + ch * 8);
   }
   to_mma();
-  if (tid == 64) {  // T^{-1} (blocked) to `saved` by bulk copies; Y is not reused until the end
+  if (okw && tid == 64) {  // T^{-1} (blocked) to `saved` by bulk copies; Y is not reused until the end
     bulk_s2g(p.Ti + blk * kSavedPair, TiH, um::kTileBytes);
     bulk_s2g(p.Ti + blk * kSavedPair + 4096, TiL, um::kTileBytes);
     bulk_commit();
   }
   // level 3: W = Ti K (B), U' = Ti V (C)
-  if (tid == 0 || tid == 32) {
+  if (okw && (tid == 0 || tid == 32)) {
     const um::Prod ps[1] = {{tid == 0 ? tB : tC, um::opnd(S_(TiH), S_(TiL), false),
                              um::opnd(S_(tid == 0 ? K : V), 0, true), false}};
     um::products(ps);
     um::commit(bar + 1);
   }
-  mbar_wait(bar + 1, 0, &g_sticky_err);
+  if (okw) okw = mbar_wait(bar + 1, 0, &g_sticky_err);
   um::fence_after();
   const int row = 16 * q + lane;  // M = 64 accumulators: lanes 0-15 hold rows
   const bool rv = lane < 16;
@@ -741,26 +748,26 @@ __global__ void __launch_bounds__(kPrepThreads, 2) prep_kernel(const TcArgs p) {
   }
   to_mma();
   // level 4: K^T (beta W) (A), P~ (beta W) (B), K^T (beta U') (C), P~ (beta U') (D)
-  if (tid == 0) {
+  if (okw && tid == 0) {
     const um::Opnd oBW = um::opnd(S_(BWH), S_(BWL), true);
     const um::Prod ps[2] = {{tA, um::opnd(S_(K), 0, true), oBW, false},
                             {tB, um::opnd(S_(PH), S_(PL), false), oBW, false}};
     um::products(ps);
     um::commit(bar + 1);
-  } else if (tid == 32) {
+  } else if (okw && tid == 32) {
     const um::Opnd oBU = um::opnd(S_(BUH), S_(BUL), true);
     const um::Prod ps[2] = {{tC, um::opnd(S_(K), 0, true), oBU, false},
                             {tD, um::opnd(S_(PH), S_(PL), false), oBU, false}};
     um::products(ps);
     um::commit(bar + 1);
   }
-  mbar_wait(bar + 1, 1, &g_sticky_err);
+  if (okw) okw = mbar_wait(bar + 1, 1, &g_sticky_err);
   um::fence_after();
   // Outputs are staged in shared memory no longer read by the MMAs and leave
   // by bulk copies: Xn h/l over T, Qt h/l over X (blocked, as the chains'
   // MMAs read them), Bc [dk][dv] fp32 over Y, Yp [C][dv] fp32 over V and P~.
   if (tid == 64) bulk_wait_read();  // the T^{-1} copies out of Y have read it
-  __syncthreads();
+  okw = !__syncthreads_or(!okw);
   bf16 *XsH = TH, *XsL = TH + 4096, *QsH = XH, *QsL = XH + 4096;  // blocked
   float* Bcs = reinterpret_cast<float*>(YH);
   float* Yps = reinterpret_cast<float*>(V);
@@ -793,7 +800,7 @@ __global__ void __launch_bounds__(kPrepThreads, 2) prep_kernel(const TcArgs p) {
   fence_proxy_async_smem();
   um::fence_before();
   __syncthreads();
-  if (tid == 0) {
+  if (okw && tid == 0) {
     bulk_s2g(p.Xn + blk * kSavedPair, XsH, 2 * um::kTileBytes);  // hi, lo contiguous
     bulk_s2g(p.Qt + blk * kSavedPair, QsH, 2 * um::kTileBytes);
     bulk_s2g(p.Bc + blk * 4096, Bcs, (unsigned)(p.dk * p.dv * 4));
@@ -928,7 +935,12 @@ __global__ void __launch_bounds__(kChainThreads, 1) chain_fwd_kernel(const TcArg
   for (int c = 0; c < kRing - 1 && c < p.nchunks; ++c) stage(c);
   if (srow) store16_f32(Hsg, cb, ncols, hs);
 
-  for (int c = 0; c < p.nchunks; ++c) {
+  // okw: every wait so far completed. A wait that runs out (recorded in the
+  // sticky word) ends the chunk loop in every thread at the next barrier; the
+  // CTA then drains the copies it has in flight and writes nothing more.
+  bool okw = true;
+  int c = 0;
+  for (; c < p.nchunks; ++c) {
     const int s = c % kRing;
     const long long t0 = (long long)c * p.C;
     const int Cc = (int)min((long long)p.C, p.T - t0);
@@ -936,10 +948,14 @@ __global__ void __launch_bounds__(kChainThreads, 1) chain_fwd_kernel(const TcArg
       asm volatile("cp.async.wait_group 1;\n" ::: "memory");
     else
       cp_async_wait_all();
-    mbar_wait(full + s, (unsigned)(c / kRing) & 1u, &g_sticky_err);
+    if (okw) okw = mbar_wait(full + s, (unsigned)(c / kRing) & 1u, &g_sticky_err);
     fence_proxy_async_smem();  // the split state written below in the previous chunk
     um::fence_before();
-    __syncthreads();  // every thread is past chunk c - 1: its stage may be refilled
+    // every thread is past chunk c - 1: its stage may be refilled
+    if (__syncthreads_or(!okw)) {
+      okw = false;
+      break;
+    }
     um::fence_after();
     if (c + kRing - 1 < p.nchunks) stage(c + kRing - 1);
     const float4* ad = reinterpret_cast<const float4*>(Xt(s) + 16384);
@@ -949,8 +965,9 @@ __global__ void __launch_bounds__(kChainThreads, 1) chain_fwd_kernel(const TcArg
       um::products(ps);
       um::commit(mbar);
     }
-    mbar_wait(mbar, (unsigned)c & 1u, &g_sticky_err);
+    okw = mbar_wait(mbar, (unsigned)c & 1u, &g_sticky_err);
     um::fence_after();
+    if (!okw) continue;  // the loop ends at the next chunk's barrier
     float v[16];
     um::ld16(lb, v);
 #pragma unroll
@@ -977,7 +994,14 @@ __global__ void __launch_bounds__(kChainThreads, 1) chain_fwd_kernel(const TcArg
         }
     }
   }
-  if (srow) store16_f32(p.HT + bh * p.dk * p.dv + r * p.dv + c0 + cb, cb, ncols, hs);
+  if (!okw) {  // drain: the stages of chunks c .. c + kRing - 2 may still be in flight
+    cp_async_wait_all();
+    if (tid == 0)
+      for (int j = c; j < c + kRing - 1 && j < p.nchunks; ++j)
+        (void)mbar_wait(full + j % kRing, (unsigned)(j / kRing) & 1u, &g_sticky_err);
+  } else if (srow) {
+    store16_f32(p.HT + bh * p.dk * p.dv + r * p.dv + c0 + cb, cb, ncols, hs);
+  }
   um::fence_before();
   __syncthreads();
   if (warp == 0) {
@@ -1047,16 +1071,23 @@ __global__ void __launch_bounds__(kChainThreads, 1) chain_bwd_kernel(const TcArg
   if (srow) store16_f32(dHsg + (long long)last * p.dk * p.dv, cb, ncols, ds);
   const um::Opnd oD = um::opnd_mn(um::saddr(DH), um::saddr(DL), kChainCols);
 
-  for (int qq = 0; qq <= last; ++qq) {
+  // okw: as in chain_fwd_kernel (a wait that runs out ends the loop in every
+  // thread at the next barrier, then the CTA drains its copies and stops).
+  bool okw = true;
+  int qq = 0;
+  for (; qq <= last; ++qq) {
     const int c = last - qq, s = qq % kRing;
     if (qq < last)  // the group of step qq + 1 may still be in flight
       asm volatile("cp.async.wait_group 1;\n" ::: "memory");
     else
       cp_async_wait_all();
-    mbar_wait(full + s, (unsigned)(qq / kRing) & 1u, &g_sticky_err);
+    if (okw) okw = mbar_wait(full + s, (unsigned)(qq / kRing) & 1u, &g_sticky_err);
     fence_proxy_async_smem();  // dy (cp.async) and the split dS written in the previous step
     um::fence_before();
-    __syncthreads();
+    if (__syncthreads_or(!okw)) {
+      okw = false;
+      break;
+    }
     um::fence_after();
     if (qq + kRing - 1 <= last) stage(qq + kRing - 1);
     const uint32_t X = um::saddr(Xt(s));
@@ -1070,8 +1101,9 @@ __global__ void __launch_bounds__(kChainThreads, 1) chain_bwd_kernel(const TcArg
       um::products(ps);
       um::commit(mbar);
     }
-    mbar_wait(mbar, (unsigned)qq & 1u, &g_sticky_err);
+    okw = mbar_wait(mbar, (unsigned)qq & 1u, &g_sticky_err);
     um::fence_after();
+    if (!okw) continue;  // the loop ends at the next step's barrier
     uint32_t rx[16], ry[16];
     float xs[16], ys[16];
     um::ld16_async(lb, rx);
@@ -1086,7 +1118,14 @@ __global__ void __launch_bounds__(kChainThreads, 1) chain_bwd_kernel(const TcArg
     }
     if (srow && c > 0) store16_f32(dHsg + (long long)(c - 1) * p.dk * p.dv, cb, ncols, ds);
   }
-  if (srow) store16_f32(p.dH0 + bh * p.dk * p.dv + row * p.dv + c0 + cb, cb, ncols, ds);
+  if (!okw) {  // drain: the stages of steps qq .. qq + kRing - 2 may still be in flight
+    cp_async_wait_all();
+    if (tid == 0)
+      for (int j = qq; j < qq + kRing - 1 && j <= last; ++j)
+        (void)mbar_wait(full + j % kRing, (unsigned)(j / kRing) & 1u, &g_sticky_err);
+  } else if (srow) {
+    store16_f32(p.dH0 + bh * p.dk * p.dv + row * p.dv + c0 + cb, cb, ncols, ds);
+  }
   um::fence_before();
   __syncthreads();
   if (warp == 0) {
@@ -1195,4 +1234,9 @@ int run_tc(bool fwd, const Args<__nv_bfloat16>& p, long long B, int H, long long
 }
 
 }  // namespace delta
+
+// The tensor-core kernels' sticky error word (bounded mbarrier waits that ran
+// out); read and cleared through mgs_take_device_error.
+unsigned take_error_delta_tc(cudaStream_t s) { return take_sticky_error(s); }
+
 }  // namespace mgs

@@ -27,6 +27,8 @@
 // minimum -- and carries the adjoint G in reverse time order.
 #include "common.cuh"
 
+#include <mutex>
+
 namespace mgs {
 namespace linear {
 
@@ -256,6 +258,7 @@ __global__ void __launch_bounds__(NW * 32) fwd_direct_kernel(Args<E> p) {
   if (threadIdx.x == 0) s_tile = atomicAdd(p.lb.counter, 1u);
   __syncthreads();
   const long long tile = s_tile;
+  if (tile >= p.ntiles) return;  // only when a test starts the counter past 0
   const long long chunk = tile / p.nstrips;
   const long long strip = tile - chunk * p.nstrips;
   const long long bi = strip / p.sper;
@@ -331,6 +334,7 @@ __global__ void __launch_bounds__(NW * 32) bwd_direct_kernel(Args<E> p) {
   if (threadIdx.x == 0) s_tile = atomicAdd(p.lb.counter, 1u);
   __syncthreads();
   const long long tile = s_tile;                   // position in reverse processing order
+  if (tile >= p.ntiles) return;  // only when a test starts the counter past 0
   const long long rchunk = tile / p.nstrips;
   const long long strip = tile - rchunk * p.nstrips;
   const long long chunk = p.nchunks - 1 - rchunk;  // time chunk
@@ -816,6 +820,65 @@ int dispatch(bool fwd, const void* a, const void* b, void* A, void* Bc, const vo
 
 unsigned take_error_linear(cudaStream_t s) { return take_sticky_error(s); }
 
+// ------------------------------------------------------ time-out test hooks --
+//
+// Both hooks make a bounded wait run out on purpose, with a small poll bound,
+// so a test can check the whole time-out path (error words set, launch
+// completes, the host sees MGS_LOOKBACK_TIMEOUT, the context stays usable)
+// without anything that could hang: every wait involved is bounded.
+
+namespace linear {
+
+// The forward direct path with the tile counter started at 1: no CTA takes
+// tile 0, so the look-back of the tile after it in strip 0 waits on a flag
+// that nothing sets. The tickets run 1..ntiles; the CTA that draws ntiles
+// returns at once.
+int run_lookback_stall(const float* a, const float* b, float* A, float* Bc, long long B,
+                       long long T, long long D, void* ws, size_t ws_bytes, long long spin,
+                       cudaStream_t st) {
+  const Geometry g = geometry(B, T, D, MGS_F32);
+  if (g.algo != kDirectVec || g.fchunks < 2) return MGS_UNSUPPORTED;  // needs a look-back
+  if (spin < 1) return MGS_BAD_SHAPE;
+  if (ws == nullptr || ws_bytes < workspace_bytes(g)) return MGS_WORKSPACE_TOO_SMALL;
+  const void* ptrs[4] = {a, b, A, Bc};
+  for (const void* q : ptrs)
+    if (q == nullptr || !aligned(q, 16)) return MGS_BAD_ALIGNMENT;
+  if (!aligned(ws, 256)) return MGS_BAD_ALIGNMENT;
+  Args<float> p{};
+  p.a = a;
+  p.b = b;
+  p.A = A;
+  p.Bc = Bc;
+  p.carries = nullptr;
+  p.T_ = T;
+  p.D = D;
+  p.sper = g.sper;
+  p.nstrips = g.nstrips;
+  p.nchunks = g.fchunks;
+  p.ntiles = g.ftiles;
+  const long long lbt = g.ntiles > g.ftiles ? g.ntiles : g.ftiles;
+  MGS_CUDA_OK(cudaMemsetAsync(ws, 0, lookback_zero_bytes(lbt), st));
+  MGS_CUDA_OK(cudaMemsetAsync(ws, 1, 1, st));  // counter = 1 (little-endian u32)
+  p.lb = lookback_view(ws, lbt, nf_max(g));
+  p.lb.spin = spin;
+  fwd_direct_kernel<float, kVecCpt, kVecFwdS, kVecFwdNW>
+      <<<(unsigned)g.ftiles, kVecFwdNW * 32, 0, st>>>(p);
+  return cudaGetLastError() == cudaSuccess ? MGS_OK : MGS_LAUNCH_FAILED;
+}
+
+// One CTA waits on an mbarrier that nothing arrives on.
+__global__ void mbarrier_stall_kernel(unsigned* err, long long spin) {
+  __shared__ uint64_t bar;
+  if (threadIdx.x == 0) {
+    mbar_init(&bar, 1);
+    mbar_fence_init();
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) (void)mbar_wait(&bar, 0u, err, spin);
+}
+
+}  // namespace linear
+
 // ------------------------------------------------ allocation-free variant --
 //
 // Scratch for mgs_linear_scan_fwd_noalloc: one fixed array per device, part
@@ -827,7 +890,33 @@ static __device__ __align__(256) unsigned char g_noalloc_scratch[MGS_NOALLOC_SCR
 
 namespace {
 constexpr int kMaxDevices = 64;
-void* g_scratch_addr[kMaxDevices] = {};
+
+// The array's address is resolved once per device and remembered together
+// with the CUDA context it was resolved in: a device whose primary context
+// was torn down and created again (cudaDeviceReset) gets a fresh address
+// instead of a stale one.
+struct ScratchSlot {
+  CUcontext ctx;
+  void* addr;
+};
+ScratchSlot g_scratch_slot[kMaxDevices] = {};
+std::mutex g_scratch_mu;
+
+using CtxGetCurrentFn = CUresult (*)(CUcontext*);
+
+CUcontext current_context() {
+  static CtxGetCurrentFn fn = [] {
+    void* ptr = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &ptr, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      return reinterpret_cast<CtxGetCurrentFn>(ptr);
+    return static_cast<CtxGetCurrentFn>(nullptr);
+  }();
+  CUcontext ctx = nullptr;
+  if (fn == nullptr || fn(&ctx) != CUDA_SUCCESS) return nullptr;
+  return ctx;
+}
 
 void* noalloc_scratch_address() {
   int dev = 0;
@@ -835,14 +924,20 @@ void* noalloc_scratch_address() {
     (void)cudaGetLastError();
     return nullptr;
   }
-  void* addr = __atomic_load_n(&g_scratch_addr[dev], __ATOMIC_ACQUIRE);
-  if (addr == nullptr) {
-    if (cudaGetSymbolAddress(&addr, g_noalloc_scratch) != cudaSuccess) {
-      (void)cudaGetLastError();
-      return nullptr;
-    }
-    __atomic_store_n(&g_scratch_addr[dev], addr, __ATOMIC_RELEASE);
+  std::lock_guard<std::mutex> lock(g_scratch_mu);
+  ScratchSlot& slot = g_scratch_slot[dev];
+  const CUcontext ctx = current_context();
+  if (slot.addr != nullptr && ctx != nullptr && slot.ctx == ctx) return slot.addr;
+  // first call on this device, or its context changed: resolve the address
+  // (this also makes the device's primary context current) and remember the
+  // context it belongs to
+  void* addr = nullptr;
+  if (cudaGetSymbolAddress(&addr, g_noalloc_scratch) != cudaSuccess) {
+    (void)cudaGetLastError();
+    return nullptr;
   }
+  slot.ctx = current_context();
+  slot.addr = addr;
   return addr;
 }
 }  // namespace
@@ -877,6 +972,24 @@ int mgs_linear_scan_bwd(const void* a, const void* b, const void* gA, const void
   return mgs::linear::dispatch(false, a, b, nullptr, nullptr, gA, gBc, da, db,
                                const_cast<void*>(carries), B, T, D, dtype, workspace,
                                workspace_bytes, static_cast<cudaStream_t>(stream));
+}
+
+int mgs_test_lookback_timeout(const void* a, const void* b, void* A, void* Bc, int64_t B,
+                              int64_t T, int64_t D, void* workspace, size_t workspace_bytes,
+                              int64_t spin_limit, void* stream) {
+  if (B < 0 || T < 0 || D < 0) return MGS_BAD_SHAPE;
+  return mgs::linear::run_lookback_stall(
+      static_cast<const float*>(a), static_cast<const float*>(b), static_cast<float*>(A),
+      static_cast<float*>(Bc), B, T, D, workspace, workspace_bytes, spin_limit,
+      static_cast<cudaStream_t>(stream));
+}
+
+int mgs_test_mbarrier_timeout(void* err_word, int64_t spin_limit, void* stream) {
+  if (err_word == nullptr || !mgs::aligned(err_word, 4)) return MGS_BAD_ALIGNMENT;
+  if (spin_limit < 1) return MGS_BAD_SHAPE;
+  mgs::linear::mbarrier_stall_kernel<<<1, 32, 0, static_cast<cudaStream_t>(stream)>>>(
+      static_cast<unsigned*>(err_word), spin_limit);
+  return cudaGetLastError() == cudaSuccess ? MGS_OK : MGS_LAUNCH_FAILED;
 }
 
 int mgs_linear_scan_fwd_noalloc(const void* a, const void* b, void* A, void* Bc, void* carries,

@@ -96,20 +96,20 @@ def _linear_scan_fwd(
     a: torch.Tensor, b: torch.Tensor, save_carries: bool
 ) -> tuple[torch.Tensor, torch.Tensor, torch.Tensor]:
     lib = _lib.load()
-    a, b = _dense(a), _dense(b)
-    Bn, T, D = a.shape
-    code = _dtype_code("linear_scan", a)
-    A, Bc = torch.empty_like(a), torch.empty_like(b)
-    csz = lib.mgs_linear_scan_carry_size(Bn, T, D, code) if save_carries else 0
-    carries = torch.empty(csz // 4, dtype=torch.float32, device=a.device)
-    ws = _workspace(lib.mgs_linear_scan_workspace_size(Bn, T, D, code), a.device)
-    with torch.cuda.device(a.device):
+    with torch.cuda.device(a.device):  # sizes are queried on the launch device
+        a, b = _dense(a), _dense(b)
+        Bn, T, D = a.shape
+        code = _dtype_code("linear_scan", a)
+        A, Bc = torch.empty_like(a), torch.empty_like(b)
+        csz = lib.mgs_linear_scan_carry_size(Bn, T, D, code) if save_carries else 0
+        carries = torch.empty(csz // 4, dtype=torch.float32, device=a.device)
+        ws = _workspace(lib.mgs_linear_scan_workspace_size(Bn, T, D, code), a.device)
         st = lib.mgs_linear_scan_fwd(
             _ptr(a), _ptr(b), _ptr(A), _ptr(Bc), _ptr(carries) if save_carries else None,
             Bn, T, D, code, _ptr(ws), ws.numel(), _stream(a),
         )
-    _lib.check(st, "linear_scan forward")
-    return A, Bc, carries
+        _lib.check(st, "linear_scan forward")
+        return A, Bc, carries
 
 
 @_linear_scan_fwd.register_fake
@@ -125,20 +125,20 @@ def _linear_scan_bwd(
     a: torch.Tensor, b: torch.Tensor, gA: torch.Tensor, gBc: torch.Tensor, carries: torch.Tensor
 ) -> tuple[torch.Tensor, torch.Tensor]:
     lib = _lib.load()
-    a, b, gA, gBc = (_dense(x) for x in (a, b, gA.to(a.dtype), gBc.to(a.dtype)))
-    Bn, T, D = a.shape
-    code = _dtype_code("linear_scan", a)
-    if carries.numel() * 4 < lib.mgs_linear_scan_carry_size(Bn, T, D, code):
-        raise RuntimeError("linear_scan backward: forward carries were not saved")
-    da, db = torch.empty_like(a), torch.empty_like(b)
-    ws = _workspace(lib.mgs_linear_scan_workspace_size(Bn, T, D, code), a.device)
-    with torch.cuda.device(a.device):
+    with torch.cuda.device(a.device):  # sizes are queried on the launch device
+        a, b, gA, gBc = (_dense(x) for x in (a, b, gA.to(a.dtype), gBc.to(a.dtype)))
+        Bn, T, D = a.shape
+        code = _dtype_code("linear_scan", a)
+        if carries.numel() * 4 < lib.mgs_linear_scan_carry_size(Bn, T, D, code):
+            raise RuntimeError("linear_scan backward: forward carries were not saved")
+        da, db = torch.empty_like(a), torch.empty_like(b)
+        ws = _workspace(lib.mgs_linear_scan_workspace_size(Bn, T, D, code), a.device)
         st = lib.mgs_linear_scan_bwd(
             _ptr(a), _ptr(b), _ptr(gA), _ptr(gBc), _ptr(carries), _ptr(da), _ptr(db),
             Bn, T, D, code, _ptr(ws), ws.numel(), _stream(a),
         )
-    _lib.check(st, "linear_scan backward")
-    return da, db
+        _lib.check(st, "linear_scan backward")
+        return da, db
 
 
 @_linear_scan_bwd.register_fake
@@ -201,20 +201,20 @@ def _log_scan_fwd(
     log_coeffs: torch.Tensor, log_values: torch.Tensor, save_carries: bool
 ) -> tuple[torch.Tensor, torch.Tensor]:
     lib = _lib.load()
-    lc, lv = _dense(log_coeffs), _dense(log_values)
-    Bn, T, D = lc.shape
-    code = _dtype_code("parallel_scan_log", lc)
-    h = torch.empty_like(lc)
-    csz = lib.mgs_log_scan_carry_size(Bn, T, D, code) if save_carries else 0
-    carries = torch.empty(csz // 4, dtype=torch.float32, device=lc.device)
-    ws = _workspace(lib.mgs_log_scan_workspace_size(Bn, T, D, code), lc.device)
-    with torch.cuda.device(lc.device):
+    with torch.cuda.device(log_coeffs.device):  # sizes are queried on the launch device
+        lc, lv = _dense(log_coeffs), _dense(log_values)
+        Bn, T, D = lc.shape
+        code = _dtype_code("parallel_scan_log", lc)
+        h = torch.empty_like(lc)
+        csz = lib.mgs_log_scan_carry_size(Bn, T, D, code) if save_carries else 0
+        carries = torch.empty(csz // 4, dtype=torch.float32, device=lc.device)
+        ws = _workspace(lib.mgs_log_scan_workspace_size(Bn, T, D, code), lc.device)
         st = lib.mgs_log_scan_fwd(
             _ptr(lc), _ptr(lv), _ptr(h), _ptr(carries) if save_carries else None,
             Bn, T, D, code, _ptr(ws), ws.numel(), _stream(lc),
         )
-    _lib.check(st, "parallel_scan_log forward")
-    return h, carries
+        _lib.check(st, "parallel_scan_log forward")
+        return h, carries
 
 
 @_log_scan_fwd.register_fake
@@ -230,21 +230,21 @@ def _log_scan_bwd(
     log_coeffs: torch.Tensor, log_values: torch.Tensor, grad_h: torch.Tensor, carries: torch.Tensor
 ) -> tuple[torch.Tensor, torch.Tensor]:
     lib = _lib.load()
-    lc, lv = _dense(log_coeffs), _dense(log_values)
-    gh = _dense(grad_h.to(lc.dtype))
-    Bn, T, D = lc.shape
-    code = _dtype_code("parallel_scan_log", lc)
-    if carries.numel() * 4 < lib.mgs_log_scan_carry_size(Bn, T, D, code):
-        raise RuntimeError("parallel_scan_log backward: forward carries were not saved")
-    dlc, dlv = torch.empty_like(lc), torch.empty_like(lv)
-    ws = _workspace(lib.mgs_log_scan_workspace_size(Bn, T, D, code), lc.device)
-    with torch.cuda.device(lc.device):
+    with torch.cuda.device(log_coeffs.device):  # sizes are queried on the launch device
+        lc, lv = _dense(log_coeffs), _dense(log_values)
+        gh = _dense(grad_h.to(lc.dtype))
+        Bn, T, D = lc.shape
+        code = _dtype_code("parallel_scan_log", lc)
+        if carries.numel() * 4 < lib.mgs_log_scan_carry_size(Bn, T, D, code):
+            raise RuntimeError("parallel_scan_log backward: forward carries were not saved")
+        dlc, dlv = torch.empty_like(lc), torch.empty_like(lv)
+        ws = _workspace(lib.mgs_log_scan_workspace_size(Bn, T, D, code), lc.device)
         st = lib.mgs_log_scan_bwd(
             _ptr(lc), _ptr(lv), _ptr(gh), _ptr(carries), _ptr(dlc), _ptr(dlv),
             Bn, T, D, code, _ptr(ws), ws.numel(), _stream(lc),
         )
-    _lib.check(st, "parallel_scan_log backward")
-    return dlc, dlv
+        _lib.check(st, "parallel_scan_log backward")
+        return dlc, dlv
 
 
 @_log_scan_bwd.register_fake
@@ -307,21 +307,21 @@ def _affine_scan_fwd(
     A: torch.Tensor, Bm: torch.Tensor, save_carries: bool
 ) -> tuple[torch.Tensor, torch.Tensor, torch.Tensor]:
     lib = _lib.load()
-    A, Bm = _dense(A), _dense(Bm)
-    Bn, T, n, k, _ = A.shape
-    v = Bm.shape[-1]
-    code = _dtype_code("matrix_affine_scan", A)
-    Abar, Bbar = torch.empty_like(A), torch.empty_like(Bm)
-    csz = lib.mgs_affine_scan_carry_size(Bn, T, n, k, v, code) if save_carries else 0
-    carries = torch.empty(csz // 4, dtype=torch.float32, device=A.device)
-    ws = _workspace(lib.mgs_affine_scan_workspace_size(Bn, T, n, k, v, code), A.device)
-    with torch.cuda.device(A.device):
+    with torch.cuda.device(A.device):  # sizes are queried on the launch device
+        A, Bm = _dense(A), _dense(Bm)
+        Bn, T, n, k, _ = A.shape
+        v = Bm.shape[-1]
+        code = _dtype_code("matrix_affine_scan", A)
+        Abar, Bbar = torch.empty_like(A), torch.empty_like(Bm)
+        csz = lib.mgs_affine_scan_carry_size(Bn, T, n, k, v, code) if save_carries else 0
+        carries = torch.empty(csz // 4, dtype=torch.float32, device=A.device)
+        ws = _workspace(lib.mgs_affine_scan_workspace_size(Bn, T, n, k, v, code), A.device)
         st = lib.mgs_affine_scan_fwd(
             _ptr(A), _ptr(Bm), _ptr(Abar), _ptr(Bbar), _ptr(carries) if csz else None,
             Bn, T, n, k, v, code, _ptr(ws), ws.numel(), _stream(A),
         )
-    _lib.check(st, "matrix_affine_scan forward")
-    return Abar, Bbar, carries
+        _lib.check(st, "matrix_affine_scan forward")
+        return Abar, Bbar, carries
 
 
 @_affine_scan_fwd.register_fake
@@ -339,24 +339,24 @@ def _affine_scan_bwd(
     gAbar: torch.Tensor, gBbar: torch.Tensor, carries: torch.Tensor,
 ) -> tuple[torch.Tensor, torch.Tensor]:
     lib = _lib.load()
-    A, Bm, Abar, Bbar = (_dense(x) for x in (A, Bm, Abar, Bbar))
-    gA, gB = _dense(gAbar.to(A.dtype)), _dense(gBbar.to(A.dtype))
-    Bn, T, n, k, _ = A.shape
-    v = Bm.shape[-1]
-    code = _dtype_code("matrix_affine_scan", A)
-    csz = lib.mgs_affine_scan_carry_size(Bn, T, n, k, v, code)
-    if carries.numel() * 4 < csz:
-        raise RuntimeError("matrix_affine_scan backward: forward carries were not saved")
-    dA, dB = torch.empty_like(A), torch.empty_like(Bm)
-    ws = _workspace(lib.mgs_affine_scan_workspace_size(Bn, T, n, k, v, code), A.device)
-    with torch.cuda.device(A.device):
+    with torch.cuda.device(A.device):  # sizes are queried on the launch device
+        A, Bm, Abar, Bbar = (_dense(x) for x in (A, Bm, Abar, Bbar))
+        gA, gB = _dense(gAbar.to(A.dtype)), _dense(gBbar.to(A.dtype))
+        Bn, T, n, k, _ = A.shape
+        v = Bm.shape[-1]
+        code = _dtype_code("matrix_affine_scan", A)
+        csz = lib.mgs_affine_scan_carry_size(Bn, T, n, k, v, code)
+        if carries.numel() * 4 < csz:
+            raise RuntimeError("matrix_affine_scan backward: forward carries were not saved")
+        dA, dB = torch.empty_like(A), torch.empty_like(Bm)
+        ws = _workspace(lib.mgs_affine_scan_workspace_size(Bn, T, n, k, v, code), A.device)
         st = lib.mgs_affine_scan_bwd(
             _ptr(A), _ptr(Bm), _ptr(Abar), _ptr(Bbar), _ptr(gA), _ptr(gB),
             _ptr(carries) if csz else None, _ptr(dA), _ptr(dB),
             Bn, T, n, k, v, code, _ptr(ws), ws.numel(), _stream(A),
         )
-    _lib.check(st, "matrix_affine_scan backward")
-    return dA, dB
+        _lib.check(st, "matrix_affine_scan backward")
+        return dA, dB
 
 
 @_affine_scan_bwd.register_fake
@@ -494,23 +494,23 @@ def _angle_scan_fwd(
     has_scale: int, has_decay: int, brickwall: int, save_carries: bool,
 ) -> tuple[torch.Tensor, torch.Tensor]:
     lib = _lib.load()
-    theta, scale, gamma, b, h0 = (_dense(x) for x in (theta, scale, gamma, b, h0))
-    Bn, T, n, R, half = theta.shape
-    k = b.shape[-1]
-    code = _dtype_code("angle_scan", b)
-    h = torch.empty_like(b)
-    csz = lib.mgs_angle_scan_carry_size(Bn, T, n, R, k, brickwall, code) if save_carries else 0
-    carries = torch.empty(csz // 4, dtype=torch.float32, device=b.device)
-    ws = _workspace(lib.mgs_angle_scan_workspace_size(Bn, T, n, R, k, brickwall, code), b.device)
-    with torch.cuda.device(b.device):
+    with torch.cuda.device(theta.device):  # sizes are queried on the launch device
+        theta, scale, gamma, b, h0 = (_dense(x) for x in (theta, scale, gamma, b, h0))
+        Bn, T, n, R, half = theta.shape
+        k = b.shape[-1]
+        code = _dtype_code("angle_scan", b)
+        h = torch.empty_like(b)
+        csz = lib.mgs_angle_scan_carry_size(Bn, T, n, R, k, brickwall, code) if save_carries else 0
+        carries = torch.empty(csz // 4, dtype=torch.float32, device=b.device)
+        ws = _workspace(lib.mgs_angle_scan_workspace_size(Bn, T, n, R, k, brickwall, code), b.device)
         st = lib.mgs_angle_scan_fwd(
             _ptr(theta), _ptr(scale), _ptr(gamma), _ptr(b), _ptr(h0),
             _ptr(perm), _ptr(sgn), _ptr(p2p), _ptr(h), _ptr(carries) if csz else None,
             Bn, T, n, R, k, int(has_scale), int(has_decay), int(brickwall), code,
             _ptr(ws), ws.numel(), _stream(b),
         )
-    _lib.check(st, "angle_scan forward")
-    return h, carries
+        _lib.check(st, "angle_scan forward")
+        return h, carries
 
 
 @_angle_scan_fwd.register_fake
@@ -529,19 +529,19 @@ def _angle_scan_bwd(
     has_scale: int, has_decay: int, brickwall: int,
 ) -> tuple[torch.Tensor, torch.Tensor, torch.Tensor, torch.Tensor, torch.Tensor]:
     lib = _lib.load()
-    theta, scale, gamma, b, h0, h = (_dense(x) for x in (theta, scale, gamma, b, h0, h))
-    gh = _dense(grad_h.to(b.dtype))
-    Bn, T, n, R, half = theta.shape
-    k = b.shape[-1]
-    code = _dtype_code("angle_scan", b)
-    csz = lib.mgs_angle_scan_carry_size(Bn, T, n, R, k, brickwall, code)
-    if carries.numel() * 4 < csz:
-        raise RuntimeError("angle_scan backward: forward carries were not saved")
-    dtheta, db, dh0 = torch.empty_like(theta), torch.empty_like(b), torch.empty_like(h0)
-    dscale = torch.empty_like(scale) if has_scale else torch.zeros_like(scale)
-    dgamma = torch.empty_like(gamma) if has_decay else torch.zeros_like(gamma)
-    ws = _workspace(lib.mgs_angle_scan_workspace_size(Bn, T, n, R, k, brickwall, code), b.device)
-    with torch.cuda.device(b.device):
+    with torch.cuda.device(theta.device):  # sizes are queried on the launch device
+        theta, scale, gamma, b, h0, h = (_dense(x) for x in (theta, scale, gamma, b, h0, h))
+        gh = _dense(grad_h.to(b.dtype))
+        Bn, T, n, R, half = theta.shape
+        k = b.shape[-1]
+        code = _dtype_code("angle_scan", b)
+        csz = lib.mgs_angle_scan_carry_size(Bn, T, n, R, k, brickwall, code)
+        if carries.numel() * 4 < csz:
+            raise RuntimeError("angle_scan backward: forward carries were not saved")
+        dtheta, db, dh0 = torch.empty_like(theta), torch.empty_like(b), torch.empty_like(h0)
+        dscale = torch.empty_like(scale) if has_scale else torch.zeros_like(scale)
+        dgamma = torch.empty_like(gamma) if has_decay else torch.zeros_like(gamma)
+        ws = _workspace(lib.mgs_angle_scan_workspace_size(Bn, T, n, R, k, brickwall, code), b.device)
         st = lib.mgs_angle_scan_bwd(
             _ptr(theta), _ptr(scale), _ptr(gamma), _ptr(b), _ptr(h0),
             _ptr(perm), _ptr(sgn), _ptr(p2p), _ptr(h), _ptr(gh), _ptr(carries) if csz else None,
@@ -549,8 +549,8 @@ def _angle_scan_bwd(
             Bn, T, n, R, k, int(has_scale), int(has_decay), int(brickwall), code,
             _ptr(ws), ws.numel(), _stream(b),
         )
-    _lib.check(st, "angle_scan backward")
-    return dtheta, dscale, dgamma, db, dh0
+        _lib.check(st, "angle_scan backward")
+        return dtheta, dscale, dgamma, db, dh0
 
 
 @_angle_scan_bwd.register_fake
@@ -651,22 +651,22 @@ def _delta_fwd(
     chunk_size: int,
 ) -> tuple[torch.Tensor, torch.Tensor, torch.Tensor]:
     lib = _lib.load()
-    Q, K, V, beta = (_dense(x) for x in (Q, K, V, beta))
-    H0 = _dense(H0.float())
-    Bn, H, T, nh, dk, dv = _delta_dims(Q, K, V)
-    code = _dtype_code("delta_scan", Q)
-    y = torch.empty(Bn, H, T, dv, dtype=Q.dtype, device=Q.device)
-    HT = torch.empty(Bn, H, dk, dv, dtype=torch.float32, device=Q.device)
-    saved = torch.empty(lib.mgs_delta_saved_size(Bn, H, T, nh, dk, dv, chunk_size, code) // 4,
-                        dtype=torch.float32, device=Q.device)
-    ws = _workspace(lib.mgs_delta_workspace_size(Bn, H, T, nh, dk, dv, chunk_size, code), Q.device)
-    with torch.cuda.device(Q.device):
+    with torch.cuda.device(Q.device):  # sizes are queried on the launch device
+        Q, K, V, beta = (_dense(x) for x in (Q, K, V, beta))
+        H0 = _dense(H0.float())
+        Bn, H, T, nh, dk, dv = _delta_dims(Q, K, V)
+        code = _dtype_code("delta_scan", Q)
+        y = torch.empty(Bn, H, T, dv, dtype=Q.dtype, device=Q.device)
+        HT = torch.empty(Bn, H, dk, dv, dtype=torch.float32, device=Q.device)
+        saved = torch.empty(lib.mgs_delta_saved_size(Bn, H, T, nh, dk, dv, chunk_size, code) // 4,
+                            dtype=torch.float32, device=Q.device)
+        ws = _workspace(lib.mgs_delta_workspace_size(Bn, H, T, nh, dk, dv, chunk_size, code), Q.device)
         st = lib.mgs_delta_fwd(
             _ptr(Q), _ptr(K), _ptr(V), _ptr(beta), _ptr(H0), _ptr(y), _ptr(HT), _ptr(saved),
             Bn, H, T, nh, dk, dv, chunk_size, code, _ptr(ws), ws.numel(), _stream(Q),
         )
-    _lib.check(st, "delta_scan forward")
-    return y, HT, saved
+        _lib.check(st, "delta_scan forward")
+        return y, HT, saved
 
 
 @_delta_fwd.register_fake
@@ -684,22 +684,22 @@ def _delta_bwd(
     dy: torch.Tensor, dHT: torch.Tensor, chunk_size: int,
 ) -> tuple[torch.Tensor, torch.Tensor, torch.Tensor, torch.Tensor, torch.Tensor]:
     lib = _lib.load()
-    Q, K, V, beta = (_dense(x) for x in (Q, K, V, beta))
-    dy = _dense(dy.to(Q.dtype))
-    dHT = _dense(dHT.float())
-    Bn, H, T, nh, dk, dv = _delta_dims(Q, K, V)
-    code = _dtype_code("delta_scan", Q)
-    dQ, dK, dV, db = (torch.empty_like(x) for x in (Q, K, V, beta))
-    dH0 = torch.empty(Bn, H, dk, dv, dtype=torch.float32, device=Q.device)
-    ws = _workspace(lib.mgs_delta_workspace_size(Bn, H, T, nh, dk, dv, chunk_size, code), Q.device)
-    with torch.cuda.device(Q.device):
+    with torch.cuda.device(Q.device):  # sizes are queried on the launch device
+        Q, K, V, beta = (_dense(x) for x in (Q, K, V, beta))
+        dy = _dense(dy.to(Q.dtype))
+        dHT = _dense(dHT.float())
+        Bn, H, T, nh, dk, dv = _delta_dims(Q, K, V)
+        code = _dtype_code("delta_scan", Q)
+        dQ, dK, dV, db = (torch.empty_like(x) for x in (Q, K, V, beta))
+        dH0 = torch.empty(Bn, H, dk, dv, dtype=torch.float32, device=Q.device)
+        ws = _workspace(lib.mgs_delta_workspace_size(Bn, H, T, nh, dk, dv, chunk_size, code), Q.device)
         st = lib.mgs_delta_bwd(
             _ptr(Q), _ptr(K), _ptr(V), _ptr(beta), _ptr(saved), _ptr(dy), _ptr(dHT),
             _ptr(dQ), _ptr(dK), _ptr(dV), _ptr(db), _ptr(dH0),
             Bn, H, T, nh, dk, dv, chunk_size, code, _ptr(ws), ws.numel(), _stream(Q),
         )
-    _lib.check(st, "delta_scan backward")
-    return dQ, dK, dV, db, dH0
+        _lib.check(st, "delta_scan backward")
+        return dQ, dK, dV, db, dH0
 
 
 @_delta_bwd.register_fake

@@ -25,6 +25,18 @@ Cases and the reference code each one exercises:
              and the gradients w.r.t. the input and every parameter
 Every case stores the inputs, the outputs and the gradients of
 ``sum(out * cotangent)`` w.r.t. every input, with a seeded cotangent.
+
+``--eager-dev`` instead writes ``eager_dev.json``: for the delta and angle
+test cases (inputs from ``tests/cases.py``, the same functions the GPU tests
+call) and their golden fixtures, the largest |eager fp32 - eager fp64|
+deviation of every output and gradient of the reference's own eager path.
+The GPU tests widen a tolerance's absolute part to 10x that deviation where
+it exceeds the parity bar -- the reference parity runner's rule
+(triton_scans.py:3303-3330). The delta path runs DeltaMinGRU._forward_chunked
+(min_gru.py:3152-3255); the angle path builds each step's k x k matrix from
+the plane angles (the product of the rounds' rotations, times gamma, times
+diag(1, scale) for k = 2: GivensMinGRU._coeffs / RotationMinGRU._coeffs,
+min_gru.py:2552-2602, 2137-2155) and scans it with matrix_affine_scan.
 """
 
 from __future__ import annotations
@@ -48,7 +60,12 @@ def _np(t):
 def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("--ref", required=True, help="path to the reference's src/ directory")
+    ap.add_argument("--eager-dev", action="store_true",
+                    help="write eager_dev.json only (the golden .npz files are left as they are)")
     args = ap.parse_args()
+    if args.eager_dev:
+        eager_dev(args.ref)
+        return
     os.environ["MINGRU_SCAN"] = "eager"
     sys.path.insert(0, args.ref)
     import torch
@@ -257,6 +274,116 @@ def main() -> None:
                             **{k: _np(v) for k, v in arrays.items()})
 
     print(f"wrote {len(list(HERE.glob('*.npz')))} fixtures to {HERE}")
+
+
+def eager_dev(ref: str) -> None:
+    import json
+
+    os.environ["MINGRU_SCAN"] = "eager"
+    sys.path.insert(0, ref)
+    sys.path.insert(0, str(HERE.parent))
+    import torch
+    from mingru import min_gru as mg
+
+    import cases as C
+
+    torch.set_num_threads(os.cpu_count() or 1)
+
+    def t(x, dtype, grad=False):
+        r = torch.as_tensor(np.asarray(x), dtype=dtype)
+        return r.requires_grad_(True) if grad else r
+
+    # ---- delta: DeltaMinGRU._forward_chunked through the raw-tensor shim
+    def delta_eager(d, chunk, dtype):
+        Q, K, V, beta = (t(d[k], dtype, True) for k in ("Q", "K", "V", "beta"))
+        H0 = t(d["H0"], dtype, True)
+        Bq, nH, Tq, dk = Q.shape
+        nh, dv = K.shape[3], V.shape[4]
+        q = Q.permute(0, 2, 1, 3)
+        ks = list(K.permute(0, 2, 3, 1, 4).unbind(2))
+        vs = list(V.permute(0, 2, 3, 1, 4).unbind(2))
+        bs = list(beta.permute(0, 2, 3, 1).unbind(2))
+        shim = types.SimpleNamespace(nh=nh, n_heads=nH, d_k=dk, d_v=dv, chunk_size=chunk,
+                                     _coeffs=lambda x: (q, ks, vs, bs))
+        y, HT = mg.DeltaMinGRU._forward_chunked(shim, Q.new_empty(Bq, Tq, 1), H0)
+        y = y.permute(0, 2, 1, 3)
+        gs = torch.autograd.grad((y * t(d["grad_y"], dtype)).sum() + (HT * t(d["grad_H_T"], dtype)).sum(),
+                                 [Q, K, V, beta, H0])
+        out = {"y": y, "H_T": HT}
+        out.update(zip(C.DELTA_NAMES, gs))
+        return {k: v.detach().double().numpy() for k, v in out.items()}
+
+    def dev_of(f32, f64):
+        return {k: float(np.max(np.abs(f32[k] - f64[k]))) if f64[k].size else 0.0 for k in f64}
+
+    res: dict[str, dict[str, float]] = {}
+
+    def delta_case(key, d, chunk):
+        res[key] = dev_of(delta_eager(d, chunk, torch.float32), delta_eager(d, chunk, torch.float64))
+        print(key, {k: f"{v:.2e}" for k, v in res[key].items()}, flush=True)
+
+    for case in C.DELTA_CASES:
+        delta_case(C.case_key("delta_fp32", case), C.delta_case_inputs("fp32", case), case[-1])
+    for case in C.DELTA_TC_CASES:
+        delta_case(C.case_key("delta_bf16", case), C.delta_case_inputs("bf16", case), case[-1])
+    delta_case("delta_full_fp32", C.delta_full_inputs(False), C.DELTA_FULL[-1])
+    delta_case("delta_full_bf16", C.delta_full_inputs(True), C.DELTA_FULL[-1])
+    for f in sorted(HERE.glob("delta_*.npz")):
+        with np.load(f) as z:
+            g = {k: z[k] for k in z.files}
+        e32 = delta_eager(g, int(g["chunk"]), torch.float32)
+        res["golden:" + f.stem] = {k: float(np.max(np.abs(e32[k] - g[k]))) for k in e32}
+
+    # ---- angle: per-step matrices from the plane angles, matrix_affine_scan
+    def angle_eager(d, hs, hd, dtype):
+        th, sc, ga, bb, h0 = (t(d[k], dtype, True) for k in ("theta", "scale", "gamma", "b", "h0"))
+        perm, sgn, p2p = (torch.as_tensor(np.asarray(d[k])) for k in ("perm", "sgn", "p2p"))
+        B, T, n, R, half = th.shape
+        k = bb.shape[-1]
+        eye = torch.eye(k, dtype=dtype)
+        M = eye.expand(B, T, n, k, k)
+        if hs and k == 2:
+            S = torch.stack([torch.stack([torch.ones_like(sc), torch.zeros_like(sc)], -1),
+                             torch.stack([torch.zeros_like(sc), sc], -1)], -2)
+            M = S
+        for r in range(R):
+            ang = th[:, :, :, r, :][..., p2p[r].long()]  # (B, T, n, k): angle of row p's plane
+            P = torch.nn.functional.one_hot(perm[r].long(), k).to(dtype)  # P[p, perm[p]] = 1
+            # row p of the round: cos(a_p) e_p + sgn_p sin(a_p) e_perm(p)
+            Rm = torch.diag_embed(torch.cos(ang)) + (sgn[r].to(dtype) * torch.sin(ang))[..., None] * P
+            M = Rm @ M
+        if hd:
+            M = ga[..., None, None] * M
+        Ab, Bb = mg.matrix_affine_scan(M, bb.unsqueeze(-1))
+        h = torch.einsum("btnij,bnj->btni", Ab, h0) + Bb.squeeze(-1)
+        gs = torch.autograd.grad((h * t(d["grad_h"], dtype)).sum(), [th, sc, ga, bb, h0],
+                                 allow_unused=True)
+        out = {"h": h}
+        for name, gg, x in zip(["dtheta", "dscale", "dgamma", "db", "dh0"], gs, [th, sc, ga, bb, h0]):
+            out[name] = torch.zeros_like(x) if gg is None else gg
+        return {k2: v.detach().double().numpy() for k2, v in out.items()}
+
+    def angle_case(key, d, hs, hd):
+        res[key] = dev_of(angle_eager(d, hs, hd, torch.float32), angle_eager(d, hs, hd, torch.float64))
+        print(key, {k: f"{v:.2e}" for k, v in res[key].items()}, flush=True)
+
+    for case in C.ANGLE_CASES:
+        angle_case(C.case_key("angle", case), C.angle_case_inputs(case), case[5], case[6])
+    # config 4: the deviation of the first batch row stands for all eight
+    # (the rows are i.i.d.; eager fp64 of all eight would need ~80 GB of host memory)
+    angle_case("angle_full_config4", C.angle_full_config4(rows=1), 0, 1)
+    for f in sorted(list(HERE.glob("givens_*.npz")) + list(HERE.glob("rotation*.npz"))):
+        with np.load(f) as z:
+            g = {k: z[k] for k in z.files}
+        hs, hd = (int(x) for x in g["flags"])
+        e32 = angle_eager(g, hs, hd, torch.float32)
+        ref = {"h": g["h"], "dtheta": g["dtheta"], "dgamma": g["dgamma"], "db": g["db"],
+               "dh0": g["dh0"], "dscale": g.get("dscale", np.zeros_like(e32["dscale"]))}
+        res["golden:" + f.stem] = {k: float(np.max(np.abs(e32[k] - ref[k]))) for k in ref}
+
+    out = HERE / "eager_dev.json"
+    out.write_text(json.dumps(res, indent=1, sort_keys=True) + "\n")
+    print(f"wrote {out} ({len(res)} cases)")
 
 
 if __name__ == "__main__":

@@ -127,3 +127,24 @@ def test_full_config2_fp32(cuda):
     np.testing.assert_allclose(A, rA, **FWD)
     np.testing.assert_allclose(db, rdb, **BWD)
     np.testing.assert_allclose(da, rda, **BWD)
+
+
+def test_full_config2_bf16(cuda):
+    """BASELINE config 2 at full size with bf16 inputs and fp32 state (B=16,
+    T=4096, D=1024): the 16-bit strip kernels against the fp64 oracle on the
+    bf16-rounded inputs, at the bf16 bar (rtol 2e-2 / atol 2e-2)."""
+    B, T, D = 16, 4096, 1024
+    g = torch.Generator().manual_seed(0)
+    a = torch.tanh(torch.randn(B, T, D, generator=g)).to(torch.bfloat16)
+    b = torch.randn(B, T, D, generator=g).to(torch.bfloat16)
+    gB = torch.randn(B, T, D, generator=torch.Generator().manual_seed(1234)).to(torch.bfloat16)
+    gA = torch.zeros(B, T, D, dtype=torch.bfloat16)
+    a64, b64, gA64, gB64 = (x.double().numpy() for x in (a, b, gA, gB))
+    rA, rB = oracle.linear_scan(a64, b64)
+    rda, rdb = oracle.linear_scan_bwd(a64, rA, rB, gA64, gB64)
+    A, Bc, da, db = run(a, b, gA, gB, cuda, torch.bfloat16)
+    tol = dict(rtol=2e-2, atol=2e-2)
+    np.testing.assert_allclose(Bc, rB, **tol)
+    np.testing.assert_allclose(A, rA, **tol)
+    np.testing.assert_allclose(db, rdb, **tol)
+    np.testing.assert_allclose(da, rda, **tol)

@@ -11,6 +11,7 @@ run the same kernels and agree exactly."""
 
 from __future__ import annotations
 
+import numpy as np
 import pytest
 import torch
 
@@ -60,6 +61,12 @@ def test_noalloc_matches_allocating_entry_point(cuda, shape):
         torch.testing.assert_close(A_na, A_ref, rtol=1e-5, atol=1e-6)
         torch.testing.assert_close(B_na, B_ref, rtol=1e-5, atol=1e-6)
         torch.testing.assert_close(car_na, car_ref, rtol=1e-5, atol=1e-6)
+        if a.numel() <= 1 << 20:  # and directly against the fp64 oracle
+            from oracle import oracle
+
+            rA, rB = oracle.linear_scan(a.double().cpu().numpy(), b.double().cpu().numpy())
+            np.testing.assert_allclose(A_na.double().cpu().numpy(), rA, rtol=1e-5, atol=1e-6)
+            np.testing.assert_allclose(B_na.double().cpu().numpy(), rB, rtol=1e-5, atol=1e-6)
 
 
 def test_noalloc_rejects_shapes_beyond_its_scratch(cuda):
