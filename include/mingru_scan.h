@@ -234,7 +234,12 @@ int mgs_angle_scan_bwd(const void* theta, const void* scale, const void* gamma, 
  * and the torch backward _delta_backward_torch (triton_scans.py:473-605) --
  * called from DeltaMinGRU._delta_fused_forward (min_gru.py:3565-3609); eager
  * oracle DeltaMinGRU._forward_chunked (min_gru.py:3152-3255).
- * Envelope: nh * chunk <= 64, dk <= 64, dv <= 64.
+ * Envelope: dk <= 128, dv <= 64 (wider d_v runs as independent column blocks,
+ * one call each), any chunk >= 1 and nh whose one-token chunk fits shared
+ * memory. The chunked form is exact for any chunk length, so the kernels may
+ * run shorter chunks than `chunk` (whole tokens; nh * chunk <= 64 on the bf16
+ * tensor-core kernels): results differ only by rounding. The size queries
+ * return 0 outside the envelope and the entry points MGS_UNSUPPORTED.
  * `saved` (mgs_delta_saved_size bytes) is written by the forward and read by
  * the backward (chunk transitions and chunk-start states, fp32).          */
 

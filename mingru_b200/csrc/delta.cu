@@ -175,13 +175,13 @@ template <typename E>
 __global__ void __launch_bounds__(kThreads) fwd_prepass_kernel(Args<E> p) {
   extern __shared__ __align__(16) float sm[];
   const Chunk ck = chunk_of(p.T_, p.C, p.nh, blockIdx.x, blockIdx.y);
-  const int M = ck.M, dk = p.dk, dv = p.dv, W = dk + dv;
-  float* sK = sm;                   // M x dk
-  float* sb = sK + kMaxM * kMaxD;   // M
-  float* sL = sb + kMaxM;           // M x M
-  float* sX = sL + kMaxM * kMaxM;   // M x (dk + dv): [W | Ut]
-  float* sA = sX + kMaxM * 2 * kMaxD;  // dk x dk
-  float* sB = sA + kMaxD * kMaxD;      // dk x dv
+  const int M = ck.M, dk = p.dk, dv = p.dv, W = dk + dv, Mx = p.nh * p.C;
+  float* sK = sm;              // M x dk
+  float* sb = sK + Mx * dk;    // M
+  float* sL = sb + Mx;         // M x M
+  float* sX = sL + Mx * Mx;    // M x (dk + dv): [W | Ut]
+  float* sA = sX + Mx * W;     // dk x dk
+  float* sB = sA + dk * dk;    // dk x dv
   load_chunk<E>(p, ck, sK, nullptr, sb, nullptr);
   {
     const size_t tok0 = (size_t)ck.bh * p.T_ + ck.t0;
@@ -213,9 +213,9 @@ __global__ void __launch_bounds__(kThreads) state_pass_kernel(const float* Ac, c
                                                              const float* H0, float* Hb, float* HT,
                                                              int nchunks, int dk, int dv) {
   extern __shared__ __align__(16) float sm[];
-  float* sS = sm;                  // dk x dv
-  float* sA = sS + kMaxD * kMaxD;  // dk x dk
-  float* sN = sA + kMaxD * kMaxD;  // dk x dv (new state)
+  float* sS = sm;           // dk x dv
+  float* sA = sS + dk * dv; // dk x dk
+  float* sN = sA + dk * dk; // dk x dv (new state)
   const long long bh = blockIdx.x;
   for (int i = threadIdx.x; i < dk * dv; i += blockDim.x) sS[i] = H0[(size_t)bh * dk * dv + i];
   __syncthreads();
@@ -240,14 +240,15 @@ __global__ void __launch_bounds__(kThreads) fwd_readout_kernel(Args<E> p) {
   extern __shared__ __align__(16) float sm[];
   const Chunk ck = chunk_of(p.T_, p.C, p.nh, blockIdx.x, blockIdx.y);
   const int M = ck.M, Ct = ck.Ct, dk = p.dk, dv = p.dv, nh = p.nh;
-  float* sK = sm;                     // M x dk
-  float* sV = sK + kMaxM * kMaxD;     // M x dv -> U
-  float* sb = sV + kMaxM * kMaxD;     // M
-  float* sQ = sb + kMaxM;             // Ct x dk
-  float* sS = sQ + kMaxM * kMaxD;     // dk x dv
-  float* sL = sS + kMaxD * kMaxD;     // M x M
-  float* sP = sL + kMaxM * kMaxM;     // Ct x M
-  float* sY = sP + kMaxM * kMaxM;     // Ct x dv
+  const int Mx = nh * p.C, Cx = p.C;
+  float* sK = sm;              // M x dk
+  float* sV = sK + Mx * dk;    // M x dv -> U
+  float* sb = sV + Mx * dv;    // M
+  float* sQ = sb + Mx;         // Ct x dk
+  float* sS = sQ + Cx * dk;    // dk x dv
+  float* sL = sS + dk * dv;    // M x M
+  float* sP = sL + Mx * Mx;    // Ct x M
+  float* sY = sP + Cx * Mx;    // Ct x dv
   load_chunk<E>(p, ck, sK, sV, sb, sQ);
   const size_t o = (size_t)ck.bh * p.nchunks + ck.c;
   for (int i = threadIdx.x; i < dk * dv; i += blockDim.x) sS[i] = p.Hb[o * dk * dv + i];
@@ -269,14 +270,15 @@ __global__ void __launch_bounds__(kThreads) bwd_e_kernel(Args<E> p) {
   extern __shared__ __align__(16) float sm[];
   const Chunk ck = chunk_of(p.T_, p.C, p.nh, blockIdx.x, blockIdx.y);
   const int M = ck.M, Ct = ck.Ct, dk = p.dk, dv = p.dv, nh = p.nh;
-  float* sK = sm;
-  float* sb = sK + kMaxM * kMaxD;
-  float* sQ = sb + kMaxM;
-  float* sdy = sQ + kMaxM * kMaxD;   // Ct x dv
-  float* sL = sdy + kMaxM * kMaxD;   // M x M
-  float* sP = sL + kMaxM * kMaxM;    // Ct x M
-  float* sZ = sP + kMaxM * kMaxM;    // M x dv
-  float* sE = sZ + kMaxM * kMaxD;    // dk x dv
+  const int Mx = nh * p.C, Cx = p.C;
+  float* sK = sm;              // M x dk
+  float* sb = sK + Mx * dk;    // M
+  float* sQ = sb + Mx;         // Ct x dk
+  float* sdy = sQ + Cx * dk;   // Ct x dv
+  float* sL = sdy + Cx * dv;   // M x M
+  float* sP = sL + Mx * Mx;    // Ct x M
+  float* sZ = sP + Cx * Mx;    // M x dv
+  float* sE = sZ + Mx * dv;    // dk x dv
   load_chunk<E>(p, ck, sK, nullptr, sb, sQ);
   {
     const E* dy = p.dy + ((size_t)ck.bh * p.T_ + ck.t0) * dv;
@@ -299,9 +301,9 @@ __global__ void __launch_bounds__(kThreads) adj_pass_kernel(const float* Ac, con
                                                            const float* dHT, float* dSo, float* dH0,
                                                            int nchunks, int dk, int dv) {
   extern __shared__ __align__(16) float sm[];
-  float* sS = sm;
-  float* sA = sS + kMaxD * kMaxD;
-  float* sN = sA + kMaxD * kMaxD;
+  float* sS = sm;           // dk x dv
+  float* sA = sS + dk * dv; // dk x dk
+  float* sN = sA + dk * dk; // dk x dv
   const long long bh = blockIdx.x;
   for (int i = threadIdx.x; i < dk * dv; i += blockDim.x) sS[i] = dHT[(size_t)bh * dk * dv + i];
   __syncthreads();
@@ -327,22 +329,22 @@ __global__ void __launch_bounds__(kThreads) bwd_grads_kernel(Args<E> p) {
   extern __shared__ __align__(16) float sm[];
   const Chunk ck = chunk_of(p.T_, p.C, p.nh, blockIdx.x, blockIdx.y);
   const int M = ck.M, Ct = ck.Ct, dk = p.dk, dv = p.dv, nh = p.nh;
-  const int MD = kMaxM * kMaxD, MM = kMaxM * kMaxM, DD = kMaxD * kMaxD;
-  float* sK = sm;            // M x dk
-  float* sU = sK + MD;       // M x dv: V, then U
-  float* sb = sU + MD;       // M
-  float* sQ = sb + kMaxM;    // Ct x dk
-  float* sS = sQ + MD;       // dk x dv   (chunk-start state)
-  float* sdS = sS + DD;      // dk x dv   (grad of the chunk's output state)
-  float* sdy = sdS + DD;     // Ct x dv   (dy; after its last use: dbU = K dSo, M x dv)
-  float* sL = sdy + MD;      // M x M
-  float* sSm = sL + MM;      // Ct x M
-  float* sP = sSm + MM;      // Ct x M  (later dSm)
-  float* sdP = sP + MM;      // Ct x M  (later dT / dKK, M x M)
-  float* sdU = sdP + MM;     // M x dv  (dU, then G)
-  float* sdK = sdU + MD;     // M x dk
-  float* sdQ = sdK + MD;     // Ct x dk
-  float* sdb = sdQ + MD;     // M
+  const int Mx = nh * p.C, Cx = p.C;
+  float* sK = sm;              // M x dk
+  float* sU = sK + Mx * dk;    // M x dv: V, then U
+  float* sb = sU + Mx * dv;    // M
+  float* sQ = sb + Mx;         // Ct x dk
+  float* sS = sQ + Cx * dk;    // dk x dv   (chunk-start state)
+  float* sdS = sS + dk * dv;   // dk x dv   (grad of the chunk's output state)
+  float* sdy = sdS + dk * dv;  // Ct x dv   (dy; after its last use: dbU = K dSo, M x dv)
+  float* sL = sdy + Mx * dv;   // M x M
+  float* sSm = sL + Mx * Mx;   // Ct x M
+  float* sP = sSm + Cx * Mx;   // Ct x M  (later dSm)
+  float* sdP = sP + Cx * Mx;   // Ct x M  (later dT / dKK, M x M)
+  float* sdU = sdP + Mx * Mx;  // M x dv  (dU, then G)
+  float* sdK = sdU + Mx * dv;  // M x dk
+  float* sdQ = sdK + Mx * dk;  // Ct x dk
+  float* sdb = sdQ + Cx * dk;  // M
   float* sdbU = sdy;
   load_chunk<E>(p, ck, sK, sU, sb, sQ);
   {
@@ -431,26 +433,67 @@ __global__ void __launch_bounds__(kThreads) bwd_grads_kernel(Args<E> p) {
 
 // ---------------------------------------------------------------- launch --
 
-constexpr size_t kPrepassSmem =
-    (kMaxM * kMaxD + kMaxM + kMaxM * kMaxM + kMaxM * 2 * kMaxD + 2 * kMaxD * kMaxD) * 4;
-constexpr size_t kReadoutSmem =
-    (3 * kMaxM * kMaxD + kMaxM + kMaxD * kMaxD + 2 * kMaxM * kMaxM + kMaxM * kMaxD) * 4;
-constexpr size_t kStateSmem = 3 * kMaxD * kMaxD * 4;
-constexpr size_t kBwdESmem =
-    (3 * kMaxM * kMaxD + kMaxM + 2 * kMaxM * kMaxM + kMaxM * kMaxD + kMaxD * kMaxD) * 4;
-constexpr size_t kBwdGSmem =
-    (7 * kMaxM * kMaxD + 2 * kMaxM + 2 * kMaxD * kMaxD + 4 * kMaxM * kMaxM) * 4;
-static_assert(kBwdGSmem <= 227 * 1024, "backward-grads tiles exceed shared memory");
+// Shared-memory floats of each kernel for chunks of at most C tokens and
+// M = nh * C micro-steps (the carve-ups in the kernels above).
+struct SmemPlan {
+  size_t prepass, readout, state, bwd_e, bwd_grads;
+  size_t max() const {
+    size_t m = prepass;
+    for (size_t x : {readout, state, bwd_e, bwd_grads}) m = x > m ? x : m;
+    return m;
+  }
+};
+
+inline SmemPlan smem_plan(int nh, int C, int dk, int dv) {
+  const size_t M = (size_t)nh * C, c = (size_t)C, k = (size_t)dk, v = (size_t)dv;
+  SmemPlan s;
+  s.prepass = (M * k + M + M * M + M * (k + v) + k * k + k * v) * 4;
+  s.readout = (M * k + M * v + M + c * k + k * v + M * M + c * M + c * v) * 4;
+  s.state = (2 * k * v + k * k) * 4;
+  s.bwd_e = (M * k + M + c * k + c * v + M * M + c * M + M * v + k * v) * 4;
+  s.bwd_grads = (M * k + M * v + M + c * k + 2 * k * v + M * v + M * M + 2 * c * M + M * M +
+                 M * v + M * k + c * k + M) * 4;
+  return s;
+}
+
+constexpr size_t kSmemLimit = 227 * 1024;
+constexpr int kMaxDk = 128;  // d_k bound (the state has d_k rows)
+constexpr int kMaxDvBlock = 64;  // value columns per call (wider d_v is split by the caller)
+
+// Tokens per chunk the CUDA-core kernels use: the requested chunk length,
+// shortened (to whole tokens) until every kernel's tiles fit in shared
+// memory. The chunked form is exact for any chunk length, so this changes
+// only the rounding, not the result. 0 if even one-token chunks do not fit.
+inline int ffma_chunk(int nh, int dk, int dv, int C, long long T) {
+  long long c = C;
+  if (T >= 1 && c > T) c = T;
+  for (; c >= 1; --c)
+    if (smem_plan(nh, (int)c, dk, dv).max() <= kSmemLimit) return (int)c;
+  return 0;
+}
+
+// Tokens per chunk of the tensor-core kernels (bf16 inputs): nh * C <= 64.
+inline int tc_chunk(int nh, int C) {
+  const int cap = kMaxM / nh;
+  return C < cap ? C : cap;
+}
 
 struct Geometry {
+  bool tc;      // tensor-core kernels
+  int C;        // tokens per chunk actually used
   int nchunks;
   size_t ac, hb;  // floats per (b, h) of A_c and of Hbound / B_c / E_c / dSo
 };
 
-inline bool geometry(long long B, int H, long long T, int nh, int dk, int dv, int C, Geometry* g) {
+inline bool geometry(long long B, int H, long long T, int nh, int dk, int dv, int C, int dtype,
+                     Geometry* g) {
   if (B < 0 || H < 0 || T < 0 || nh < 1 || C < 1 || dk < 1 || dv < 1) return false;
-  if (nh * C > kMaxM || dk > kMaxD || dv > kMaxD) return false;
-  g->nchunks = (int)((T + C - 1) / C);
+  if (dk > kMaxDk || dv > kMaxDvBlock) return false;
+  const int ct = nh <= kMaxM ? tc_chunk(nh, C) : 0;
+  g->tc = ct >= 1 && tc_eligible(dtype, nh, dk, dv, ct);
+  g->C = g->tc ? ct : ffma_chunk(nh, dk, dv, C, T);
+  if (g->C < 1) return false;
+  g->nchunks = (int)((T + g->C - 1) / g->C);
   g->ac = (size_t)g->nchunks * dk * dk;
   g->hb = (size_t)g->nchunks * dk * dv;
   return true;
@@ -466,12 +509,15 @@ int launch(K kernel, dim3 grid, size_t smem, cudaStream_t st, void** args) {
 template <typename E>
 int run(bool fwd, Args<E> p, long long B, int H, long long T, int nh, int dk, int dv, int C,
         float* saved, void* ws, size_t ws_bytes, cudaStream_t st) {
+  constexpr int dtype = std::is_same_v<E, float> ? MGS_F32
+                        : std::is_same_v<E, __nv_bfloat16> ? MGS_BF16 : MGS_F16;
   Geometry g;
-  if (!geometry(B, H, T, nh, dk, dv, C, &g)) return MGS_UNSUPPORTED;
+  if (!geometry(B, H, T, nh, dk, dv, C, dtype, &g)) return MGS_UNSUPPORTED;
   if constexpr (std::is_same_v<E, __nv_bfloat16>) {
-    if (tc_eligible(MGS_BF16, nh, dk, dv, C))
-      return run_tc(fwd, p, B, H, T, nh, dk, dv, C, saved, ws, ws_bytes, st);
+    if (g.tc) return run_tc(fwd, p, B, H, T, nh, dk, dv, g.C, saved, ws, ws_bytes, st);
   }
+  C = g.C;
+  const SmemPlan sp = smem_plan(nh, C, dk, dv);
   const long long BH = B * (long long)H;
   p.T_ = T;
   p.H = H;
@@ -495,7 +541,7 @@ int run(bool fwd, Args<E> p, long long B, int H, long long T, int nh, int dk, in
       return MGS_OK;
     }
     void* a1[] = {&p};
-    int rc = launch(fwd_prepass_kernel<E>, dim3(g.nchunks, (unsigned)BH), kPrepassSmem, st, a1);
+    int rc = launch(fwd_prepass_kernel<E>, dim3(g.nchunks, (unsigned)BH), sp.prepass, st, a1);
     if (rc != MGS_OK) return rc;
     const float* Ac = p.Ac;
     const float* Bc = p.Bc;
@@ -504,9 +550,9 @@ int run(bool fwd, Args<E> p, long long B, int H, long long T, int nh, int dk, in
     float* HT = p.HT;
     int nc = g.nchunks;
     void* a2[] = {&Ac, &Bc, &H0, &Hb, &HT, &nc, &dk, &dv};
-    rc = launch(state_pass_kernel, dim3((unsigned)BH), kStateSmem, st, a2);
+    rc = launch(state_pass_kernel, dim3((unsigned)BH), sp.state, st, a2);
     if (rc != MGS_OK) return rc;
-    return launch(fwd_readout_kernel<E>, dim3(g.nchunks, (unsigned)BH), kReadoutSmem, st, a1);
+    return launch(fwd_readout_kernel<E>, dim3(g.nchunks, (unsigned)BH), sp.readout, st, a1);
   }
   p.Ec = scratch;
   p.dSo = scratch + BH * g.hb;
@@ -516,7 +562,7 @@ int run(bool fwd, Args<E> p, long long B, int H, long long T, int nh, int dk, in
     return MGS_OK;
   }
   void* a1[] = {&p};
-  int rc = launch(bwd_e_kernel<E>, dim3(g.nchunks, (unsigned)BH), kBwdESmem, st, a1);
+  int rc = launch(bwd_e_kernel<E>, dim3(g.nchunks, (unsigned)BH), sp.bwd_e, st, a1);
   if (rc != MGS_OK) return rc;
   const float* Ac = p.Ac;
   const float* Ec = p.Ec;
@@ -525,9 +571,9 @@ int run(bool fwd, Args<E> p, long long B, int H, long long T, int nh, int dk, in
   float* dH0 = p.dH0;
   int nc = g.nchunks;
   void* a2[] = {&Ac, &Ec, &dHT, &dSo, &dH0, &nc, &dk, &dv};
-  rc = launch(adj_pass_kernel, dim3((unsigned)BH), kStateSmem, st, a2);
+  rc = launch(adj_pass_kernel, dim3((unsigned)BH), sp.state, st, a2);
   if (rc != MGS_OK) return rc;
-  return launch(bwd_grads_kernel<E>, dim3(g.nchunks, (unsigned)BH), kBwdGSmem, st, a1);
+  return launch(bwd_grads_kernel<E>, dim3(g.nchunks, (unsigned)BH), sp.bwd_grads, st, a1);
 }
 
 }  // namespace delta
@@ -538,19 +584,17 @@ extern "C" {
 size_t mgs_delta_saved_size(int64_t B, int H, int64_t T, int nh, int dk, int dv, int chunk,
                             int dtype) {
   mgs::delta::Geometry g;
-  if (!mgs::delta::geometry(B, H, T, nh, dk, dv, chunk, &g)) return 0;
-  if (mgs::delta::tc_eligible(dtype, nh, dk, dv, chunk))
-    return mgs::delta::tc_saved_floats(B * (int64_t)H, T, dk, dv, chunk) * sizeof(float);
+  if (!mgs::delta::geometry(B, H, T, nh, dk, dv, chunk, dtype, &g)) return 0;
+  if (g.tc) return mgs::delta::tc_saved_floats(B * (int64_t)H, T, dk, dv, g.C) * sizeof(float);
   return (size_t)B * H * (g.ac + g.hb) * sizeof(float);
 }
 
 size_t mgs_delta_workspace_size(int64_t B, int H, int64_t T, int nh, int dk, int dv, int chunk,
                                 int dtype) {
   mgs::delta::Geometry g;
-  if (!mgs::delta::geometry(B, H, T, nh, dk, dv, chunk, &g)) return 0;
+  if (!mgs::delta::geometry(B, H, T, nh, dk, dv, chunk, dtype, &g)) return 0;
   size_t n = (size_t)B * H * 2 * g.hb * sizeof(float);
-  if (mgs::delta::tc_eligible(dtype, nh, dk, dv, chunk))
-    n = mgs::delta::tc_workspace_floats(B * (int64_t)H, T, dk, dv, chunk) * sizeof(float);
+  if (g.tc) n = mgs::delta::tc_workspace_floats(B * (int64_t)H, T, dk, dv, g.C) * sizeof(float);
   return n < 256 ? 256 : n;
 }
 

@@ -8,8 +8,7 @@
 namespace mgs {
 namespace delta {
 
-constexpr int kMaxM = 64;   // nh * chunk micro-steps per chunk
-constexpr int kMaxD = 64;   // d_k, d_v
+constexpr int kMaxM = 64;   // nh * chunk micro-steps per chunk on the tensor-core kernels
 
 template <typename E>
 struct Args {

@@ -736,8 +736,8 @@ def _delta_backward(ctx, dy, dHT, _gsaved):
 
 torch.library.register_autograd("mingru_b200::delta_fwd", _delta_backward, setup_context=_delta_setup)
 
-_DELTA_MAX_MICROSTEPS = 64
-_DELTA_MAX_D = 64
+_DELTA_MAX_DK = 128
+_DELTA_DV_BLOCK = 64  # value columns per kernel call: wider d_v runs as column blocks
 
 
 def delta_scan_impl(
@@ -752,8 +752,15 @@ def delta_scan_impl(
     ``(B, n_heads, T, nh, d_v)``, ``beta`` ``(B, n_heads, T, nh)``, ``H0``
     ``(B, n_heads, d_k, d_v)``. ``y`` ``(B, n_heads, T, d_v)`` has the inputs'
     dtype; the state ``H_T`` is fp32 (``H0``'s dtype if that is wider).
-    Differentiable w.r.t. all five tensors. Envelope: ``nh * chunk_size <= 64``,
-    ``d_k, d_v <= 64``; fp32, bf16 or fp16 inputs (fp32 arithmetic).
+    Differentiable w.r.t. all five tensors; fp32, bf16 or fp16 inputs (fp32
+    arithmetic). Envelope: ``d_k <= 128``, any ``d_v``, ``nh`` and
+    ``chunk_size`` whose one-token chunk fits the kernels' shared memory
+    (``nh`` up to 96 at ``d_k = d_v = 64``). The chunked form is exact for any
+    chunk length, so the kernels may use shorter chunks than ``chunk_size``
+    (whole tokens, at most ``64 / nh`` on the bf16 tensor-core kernels) -- the
+    result differs only by rounding. The state's value columns evolve
+    independently, so ``d_v > 64`` runs as blocks of 64 columns whose
+    gradients w.r.t. Q, K and beta add up.
     """
     op = "delta_scan"
     if Q.ndim != 4 or K.ndim != 5 or V.ndim != 5 or beta.ndim != 4 or H0.ndim != 4:
@@ -772,17 +779,32 @@ def delta_scan_impl(
             f"V={(Bn, H, T, nh, dv)}, beta={(Bn, H, T, nh)}, H0={(Bn, H, dk, dv)}; got "
             f"K={tuple(K.shape)}, V={tuple(V.shape)}, beta={tuple(beta.shape)}, H0={tuple(H0.shape)}"
         )
-    if chunk_size < 1 or nh * chunk_size > _DELTA_MAX_MICROSTEPS or dk > _DELTA_MAX_D \
-            or dv > _DELTA_MAX_D:
+    if chunk_size < 1 or dk > _DELTA_MAX_DK:
         raise ValueError(
-            f"{op}: outside the kernel envelope: need nh * chunk_size <= {_DELTA_MAX_MICROSTEPS} and "
-            f"d_k, d_v <= {_DELTA_MAX_D} (got nh={nh}, chunk_size={chunk_size}, d_k={dk}, d_v={dv})"
+            f"{op}: outside the kernel envelope: need chunk_size >= 1 and d_k <= {_DELTA_MAX_DK} "
+            f"(got nh={nh}, chunk_size={chunk_size}, d_k={dk}, d_v={dv})"
         )
     _require_cuda(op, Q, K, V, beta, H0)
     if any(x.dtype != Q.dtype for x in (K, V, beta)):
         raise ValueError(f"{op}: Q, K, V and beta must share a dtype")
-    _dtype_code(op, Q)
-    y, HT, _ = _delta_fwd(Q, K, V, beta, H0, int(chunk_size))
+    code = _dtype_code(op, Q)
+    lib = _lib.load()
+    if lib.mgs_delta_saved_size(Bn, H, T, nh, dk, min(dv, _DELTA_DV_BLOCK), int(chunk_size), code) == 0 \
+            and Bn * H * T > 0:
+        raise ValueError(
+            f"{op}: outside the kernel envelope: nh={nh} micro-steps of one token do not fit the "
+            f"kernels' shared memory at d_k={dk} (chunk_size={chunk_size}, d_v={dv})"
+        )
+    if dv <= _DELTA_DV_BLOCK:
+        y, HT, _ = _delta_fwd(Q, K, V, beta, H0, int(chunk_size))
+    else:  # independent value-column blocks; autograd adds their Q, K, beta gradients
+        ys, hts = [], []
+        for j0 in range(0, dv, _DELTA_DV_BLOCK):
+            j1 = min(dv, j0 + _DELTA_DV_BLOCK)
+            yj, hj, _ = _delta_fwd(Q, K, V[..., j0:j1], beta, H0[..., j0:j1], int(chunk_size))
+            ys.append(yj)
+            hts.append(hj)
+        y, HT = torch.cat(ys, -1), torch.cat(hts, -1)
     if H0.dtype == torch.float64:
         HT = HT.double()
     return y, HT

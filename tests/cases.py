@@ -33,6 +33,10 @@ DELTA_CASES = [
     (1, 2, 100, 1, 64, 64, 64), (2, 1, 77, 2, 32, 32, 32), (1, 2, 130, 1, 16, 16, 16),
     (2, 2, 19, 1, 8, 8, 8), (1, 1, 65, 1, 64, 32, 64), (1, 3, 40, 4, 8, 16, 16),
     (1, 1, 1, 1, 4, 4, 4),
+    # wider than the 64-micro-step tiles: nh * chunk = 128 (the kernels run
+    # shorter chunks), d_k = d_v = 128 (d_v in two column blocks), an odd chunk
+    (1, 2, 150, 2, 16, 16, 64), (1, 2, 100, 2, 64, 64, 64), (1, 1, 70, 1, 128, 128, 64),
+    (1, 1, 30, 3, 8, 8, 50),
 ]
 # bf16 inputs on the tensor-core kernels: value-column splits of 2 (d_v > 32,
 # few heads) and 1 (many heads, or d_v <= 32), padded d_k / d_v / chunk rows,
@@ -41,6 +45,9 @@ DELTA_TC_CASES = [
     (1, 2, 100, 1, 64, 64, 64), (2, 1, 77, 2, 32, 32, 32), (1, 2, 130, 1, 16, 16, 16),
     (2, 2, 19, 1, 8, 8, 8), (1, 1, 65, 1, 64, 32, 64), (1, 3, 40, 4, 8, 16, 16),
     (1, 2, 90, 1, 48, 40, 64), (10, 8, 70, 1, 64, 64, 64), (1, 1, 1, 1, 8, 8, 64),
+    # nh * chunk = 128 (tensor cores with 32-token chunks) and d_k = d_v = 128
+    # (CUDA-core kernels on bf16 inputs, d_v in two column blocks)
+    (1, 2, 150, 2, 64, 64, 64), (1, 1, 70, 1, 128, 128, 64),
 ]
 # BASELINE config 5 at full size: B=8, H=8, T=8192, d_k=d_v=64, chunk=64
 DELTA_FULL = (8, 8, 8192, 1, 64, 64, 64)

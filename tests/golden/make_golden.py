@@ -62,7 +62,10 @@ def main() -> None:
     ap.add_argument("--ref", required=True, help="path to the reference's src/ directory")
     ap.add_argument("--eager-dev", action="store_true",
                     help="write eager_dev.json only (the golden .npz files are left as they are)")
+    ap.add_argument("--only", default=None,
+                    help="comma-separated fixture names: write only these (others are left as they are)")
     args = ap.parse_args()
+    only = None if args.only is None else set(args.only.split(","))
     if args.eager_dev:
         eager_dev(args.ref)
         return
@@ -77,7 +80,8 @@ def main() -> None:
     dt = torch.float64
 
     def save(name, **arrays):
-        np.savez_compressed(HERE / f"{name}.npz", **{k: _np(v) for k, v in arrays.items()})
+        if only is None or name in only:
+            np.savez_compressed(HERE / f"{name}.npz", **{k: _np(v) for k, v in arrays.items()})
 
     def grads(outs, ins, seed):
         g = torch.Generator().manual_seed(seed)
@@ -244,11 +248,19 @@ def main() -> None:
                                                    mixer=["delta", "rotation"],
                                                    mixer_kwargs={"delta": {"n_heads": 2,
                                                                            "chunk_size": 16}}), False),
+        # two micro-steps per token at the default chunk_size=64 (nh * chunk = 128)
+        "module_delta_nh2": ("DeltaMinGRU", dict(input_size=8, hidden_size=32, n_heads=2, nh=2), False),
+        # d_k = d_v = 128 per head (hidden 256 over 2 heads; d_model=512 over 4 heads
+        # runs the same kernels per head)
+        "module_delta_d128": ("DeltaMinGRU", dict(input_size=16, hidden_size=256, n_heads=2), False),
     }
+    long_t = {"module_delta_nh2": 150, "module_delta_d128": 70}  # several chunks
     for name, (cls_name, kwargs, use_dt) in module_cases.items():
+        if only is not None and name not in only:
+            continue
         torch.manual_seed(101)
         mod = getattr(mg, cls_name)(**kwargs).double()
-        B, T = 3, 37
+        B, T = 3, long_t.get(name, 37)
         g = torch.Generator().manual_seed(102)
         x = torch.randn(B, T, kwargs["input_size"], generator=g, dtype=dt).requires_grad_(True)
         dtv = (torch.rand(B, T, generator=g, dtype=dt) * 2) if use_dt else None
@@ -273,7 +285,32 @@ def main() -> None:
                             meta=np.array(json.dumps({"cls": cls_name, "kwargs": kwargs})),
                             **{k: _np(v) for k, v in arrays.items()})
 
-    print(f"wrote {len(list(HERE.glob('*.npz')))} fixtures to {HERE}")
+    if only is None or "module_delta_ref_fixture" in only:
+        ref_fixture(Path(args.ref).parent / "tests" / "fixtures" / "delta_mingru_decay_none_golden.json")
+    print(f"wrote fixtures to {HERE}")
+
+
+def ref_fixture(src: Path) -> None:
+    """The reference's own DeltaMinGRU golden (tests/fixtures/
+    delta_mingru_decay_none_golden.json, checked by tests/test_mixers.py:403-437:
+    DeltaMinGRU(8, 6, n_heads=2, nh=2) from seed 42, its state_dict, input,
+    output and the gradients of output.sum()) in this directory's module-fixture
+    layout, so the module tests gate against it too."""
+    import json
+
+    f = json.loads(src.read_text())
+    arrays = {"x": np.array(f["x"], np.float32), "out": np.array(f["output"], np.float32),
+              "dx": np.array(f["x_grad"], np.float32)}
+    arrays["cot"] = np.ones_like(arrays["out"])
+    for k in f["state_dict_keys"]:
+        arrays["sd." + k] = np.array(f["state_dict"][k], np.float32)
+    for k, v in f["param_grads"].items():
+        arrays["grad." + k] = np.array(v, np.float32)
+    meta = {"cls": "DeltaMinGRU", "kwargs": {"input_size": f["D_IN"], "hidden_size": f["D_H"],
+                                             "n_heads": f["n_heads"], "nh": f["nh"]},
+            "source": "reference tests/fixtures/delta_mingru_decay_none_golden.json"}
+    np.savez_compressed(HERE / "module_delta_ref_fixture.npz", meta=np.array(json.dumps(meta)),
+                        **arrays)
 
 
 def eager_dev(ref: str) -> None:

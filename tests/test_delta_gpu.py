@@ -123,12 +123,15 @@ def test_full_length_config5_fp32(cuda):
 def test_envelope_errors(cuda):
     import mingru_b200 as mb
 
-    Q = torch.randn(1, 1, 10, 8, device=cuda)
-    K = torch.randn(1, 1, 10, 2, 8, device=cuda)
-    V = torch.randn(1, 1, 10, 2, 8, device=cuda)
-    b = torch.rand(1, 1, 10, 2, device=cuda)
-    H0 = torch.zeros(1, 1, 8, 8, device=cuda)
-    with pytest.raises(ValueError, match="envelope"):
-        mb.delta_scan_impl(Q, K, V, b, H0, chunk_size=65)
+    def args(T, nh, dk, dv):
+        return (torch.randn(1, 1, T, dk, device=cuda), torch.randn(1, 1, T, nh, dk, device=cuda),
+                torch.randn(1, 1, T, nh, dv, device=cuda), torch.rand(1, 1, T, nh, device=cuda),
+                torch.zeros(1, 1, dk, dv, device=cuda))
+
+    with pytest.raises(ValueError, match="envelope"):  # d_k above 128
+        mb.delta_scan_impl(*args(10, 1, 136, 8), chunk_size=16)
+    with pytest.raises(ValueError, match="envelope"):  # one token's micro-steps do not fit
+        mb.delta_scan_impl(*args(10, 200, 64, 64), chunk_size=1)
+    Q, K, V, b, H0 = args(10, 2, 8, 8)
     with pytest.raises(ValueError, match="disagree"):
         mb.delta_scan_impl(Q, K, V[..., :4], b, H0, chunk_size=4)
