@@ -308,6 +308,7 @@ def ref_fixture(src: Path) -> None:
         arrays["grad." + k] = np.array(v, np.float32)
     meta = {"cls": "DeltaMinGRU", "kwargs": {"input_size": f["D_IN"], "hidden_size": f["D_H"],
                                              "n_heads": f["n_heads"], "nh": f["nh"]},
+            "seed": f["seed"], "dtype": "float32",
             "source": "reference tests/fixtures/delta_mingru_decay_none_golden.json"}
     np.savez_compressed(HERE / "module_delta_ref_fixture.npz", meta=np.array(json.dumps(meta)),
                         **arrays)

@@ -36,9 +36,11 @@ def test_same_seed_same_init(name):
     g = load_golden(name)
     meta = json.loads(str(g["meta"]))
     prev = torch.get_default_dtype()
-    torch.set_default_dtype(torch.float64)  # the fixtures were built with fp64 as default
+    # the generated fixtures were built with fp64 as default and seed 101; the
+    # reference's own fixture records its seed and dtype
+    torch.set_default_dtype(getattr(torch, meta.get("dtype", "float64")))
     try:
-        torch.manual_seed(101)
+        torch.manual_seed(meta.get("seed", 101))
         mod = build(meta)
     finally:
         torch.set_default_dtype(prev)
