@@ -154,6 +154,30 @@ int mgs_log_scan_bwd(const void* log_coeffs, const void* log_values, const void*
                      void* stream);
 
 /* ------------------------------------------------------------------------ */
+/* MinGRU gate scan: parallel_scan_log fed straight from MinGRU's
+ * pre-activations. Replaces the coefficient prologue of MinGRU.forward
+ * (min_gru.py:1383-1397: log_coeffs = -softplus(k), log_values =
+ * cat[log h_0, -softplus(-k) + log_g(x~)], log_g at min_gru.py:751-752)
+ * followed by parallel_scan_log (min_gru.py:1394). k = linear_z(x),
+ * x~ = linear_h(x), h, dk, dx~ are (B, T, D); log_h0, dlog_h0 are (B, D).
+ * fp32 shapes on the parallel_scan_log column path form the log
+ * coefficients in shared memory (they never exist in HBM); other shapes and
+ * 16-bit storage form them in the workspace with one elementwise kernel.
+ * The backward returns dk, dx~ and dlog_h0 directly.                       */
+
+size_t mgs_log_gate_scan_workspace_size(int64_t B, int64_t T, int64_t D, int dtype);
+size_t mgs_log_gate_scan_carry_size(int64_t B, int64_t T, int64_t D, int dtype);
+
+int mgs_log_gate_scan_fwd(const void* k, const void* x, const void* log_h0, void* h, void* carries,
+                          int64_t B, int64_t T, int64_t D, int dtype, void* workspace,
+                          size_t workspace_bytes, void* stream);
+
+int mgs_log_gate_scan_bwd(const void* k, const void* x, const void* log_h0, const void* grad_h,
+                          const void* carries, void* dk, void* dx, void* dlog_h0, int64_t B,
+                          int64_t T, int64_t D, int dtype, void* workspace, size_t workspace_bytes,
+                          void* stream);
+
+/* ------------------------------------------------------------------------ */
 /* matrix_affine_scan / matrix_scan: H_t = A_t H_{t-1} + B_t per block,
  * A (B, T, n, k, k), Bm (B, T, n, k, v); returns Abar_t (running product,
  * Abar_0 = I) and Bbar_t (the H_0 = 0 solution). matrix_scan is k = 2, v = 1

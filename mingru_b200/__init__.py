@@ -25,6 +25,7 @@ from .scan_ops import (
     linear_scan,
     matrix_affine_scan,
     matrix_scan,
+    mingru_gate_scan,
     parallel_scan_log,
     raise_device_error,
     take_device_error,
@@ -46,6 +47,7 @@ __all__ = [
     "linear_scan",
     "matrix_affine_scan",
     "matrix_scan",
+    "mingru_gate_scan",
     "parallel_scan_log",
     "raise_device_error",
     "take_device_error",

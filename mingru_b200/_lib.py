@@ -44,6 +44,11 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "mgs_log_scan_carry_size": (_sz, [_i64, _i64, _i64, _int]),
     "mgs_log_scan_fwd": (_int, [_p, _p, _p, _p, _i64, _i64, _i64, _int, _p, _sz, _p]),
     "mgs_log_scan_bwd": (_int, [_p, _p, _p, _p, _p, _p, _i64, _i64, _i64, _int, _p, _sz, _p]),
+    "mgs_log_gate_scan_workspace_size": (_sz, [_i64, _i64, _i64, _int]),
+    "mgs_log_gate_scan_carry_size": (_sz, [_i64, _i64, _i64, _int]),
+    "mgs_log_gate_scan_fwd": (_int, [_p, _p, _p, _p, _p, _i64, _i64, _i64, _int, _p, _sz, _p]),
+    "mgs_log_gate_scan_bwd": (
+        _int, [_p, _p, _p, _p, _p, _p, _p, _p, _i64, _i64, _i64, _int, _p, _sz, _p]),
     "mgs_affine_scan_workspace_size": (_sz, [_i64, _i64, _i64, _int, _int, _int]),
     "mgs_affine_scan_carry_size": (_sz, [_i64, _i64, _i64, _int, _int, _int]),
     "mgs_affine_scan_fwd": (

@@ -145,6 +145,8 @@ struct Args {
   const E* gh;   // (B, T, D)
   E* dlc;        // (B, T, D)
   E* dlv;        // (B, T+1, D)
+  const E* lh0;  // gate-fused column kernels: log h_0 (B, D) (lc, lv then hold k, x~)
+  E* dlh0;       // gate-fused column kernels: gradient of log h_0 (B, D)
   float* carries;
   long long T_, D, sper, nstrips;
   long long nchunks, ntiles;
@@ -521,7 +523,7 @@ __device__ __forceinline__ float col_exp(float x) {
 
 // Thread 0: issue the TMA boxes of NT tensors in time order (lv skips its h_0
 // row), box b of every tensor completing on barrier b.
-template <typename E, int W, int NT>
+template <typename E, int W, int NT, int LVOFF = 1>
 __device__ __forceinline__ void col_fetch(const ColMaps& maps, const ColSmem<E, W>& sm,
                                           long long T, int d0, int bi) {
   const int nb = col_boxes(T);
@@ -532,7 +534,7 @@ __device__ __forceinline__ void col_fetch(const ColMaps& maps, const ColSmem<E, 
       mbar_arrive_expect_tx(sm.bar + b, (unsigned)(NT * kColBox * W * sizeof(E)));
       for (int k = 0; k < NT; ++k)
         tma_load_3d(sm.t[k] + (size_t)b * kColBox * W, &maps.m[k], d0,
-                    b * kColBox + (k == 1 ? 1 : 0), bi, sm.bar + b);
+                    b * kColBox + (k == 1 ? LVOFF : 0), bi, sm.bar + b);
     }
   }
   __syncthreads();
@@ -558,6 +560,55 @@ __device__ __forceinline__ void col_put(const CUtensorMap* m, const E* src, long
       tma_store_3d(m, d0, y0 + b * kColBox, bi, src + (size_t)b * kColBox * W);
     bulk_commit();
   }
+}
+
+// ------------------------------------------------- MinGRU gate prologue --
+// MinGRU.forward (min_gru.py:1383-1397) builds the scan inputs from the gate
+// pre-activation k = linear_z(x) and the candidate pre-activation
+// x~ = linear_h(x):  log a = -softplus(k),  log b = log sigmoid(k) + log_g(x~),
+// log_g(x) = log(x + 1/2) for x >= 0, -softplus(-x) otherwise
+// (min_gru.py:751-752). The gate-fused kernels read k and x~ and form these in
+// shared memory. Derivatives: d log a / dk = -sigmoid(k), d log b / dk =
+// sigmoid(-k) = a, d log b / dx~ = 1 / (x~ + 1/2) (x~ >= 0) or 1 - g(x~)
+// (x~ < 0), the branch at x~ = 0 taken as in the reference (x~ >= 0).
+
+// softplus(x) = max(x, 0) + log1p(exp(-|x|)), without overflow.
+__device__ __forceinline__ float softplus_f(float x) {
+  return fmaxf(x, 0.f) + log1pf(expf(-fabsf(x)));
+}
+
+__device__ __forceinline__ void gate_logs(float k, float x, float& lc, float& lv) {
+  const float e = log1pf(expf(-fabsf(k)));
+  lc = -(fmaxf(k, 0.f) + e);                 // log(1 - sigmoid(k))
+  const float lz = -(fmaxf(-k, 0.f) + e);    // log sigmoid(k)
+  lv = lz + (x >= 0.f ? logf(x + 0.5f) : -softplus_f(-x));
+}
+
+// (dk, dx~) from (dlc, dlv) given k and x~.
+__device__ __forceinline__ void gate_grads(float k, float x, float dlc, float dlv, float& dk,
+                                           float& dx) {
+  const float sk = 1.f / (1.f + expf(-k));   // sigmoid(k)
+  dk = fmaf(-sk, dlc, (1.f - sk) * dlv);
+  const float fx = x >= 0.f ? 1.f / (x + 0.5f) : 1.f / (1.f + expf(x));  // 1 - sigmoid(x) = sigmoid(-x)
+  dx = fx * dlv;
+}
+
+// In place over this lane's segment: (k, x~) -> (log a, log b); bit i of the
+// returned mask is set where x~ < 0 (the branch of log_g, kept for the backward).
+template <typename E, int W>
+__device__ __forceinline__ unsigned long long col_gate_prologue(E* lc, E* lv, int n) {
+  unsigned long long neg = 0ull;
+#pragma unroll
+  for (int i = 0; i < kColMaxLen; ++i)
+    if (i < n) {
+      const float k = cld<E, W>(lc, i), x = cld<E, W>(lv, i);
+      float a, b;
+      gate_logs(k, x, a, b);
+      cst<E, W>(lc, i, a);
+      cst<E, W>(lv, i, b);
+      neg |= (unsigned long long)(x < 0.f) << i;
+    }
+  return neg;
 }
 
 // Does this lane's segment allow the linear-domain recurrence?
@@ -591,7 +642,7 @@ struct ColLog {
 };
 
 // Forward aggregate of one segment (linear: caches a, b over lc, lv for fp32).
-template <typename E, int W, bool LIN>
+template <typename E, int W, bool LIN, bool CACHE = true>
 __device__ __forceinline__ void col_fwd_agg(E* lc, E* lv, int n, bool first, float s0, float& A,
                                             float& B) {
   if (LIN) {
@@ -601,7 +652,7 @@ __device__ __forceinline__ void col_fwd_agg(E* lc, E* lv, int n, bool first, flo
     for (int i = 0; i < kColMaxLen; ++i)
       if (i < n) {
         const float a = col_exp(cld<E, W>(lc, i)), b = col_exp(cld<E, W>(lv, i));
-        if constexpr (std::is_same<E, float>::value) {
+        if constexpr (CACHE && std::is_same<E, float>::value) {
           lc[i * W] = a;
           lv[i * W] = b;
         }
@@ -620,9 +671,9 @@ __device__ __forceinline__ void col_fwd_agg(E* lc, E* lv, int n, bool first, flo
 }
 
 // a_t, b_t of step i on the linear path (cached for fp32, recomputed otherwise).
-template <typename E, int W>
+template <typename E, int W, bool CACHE = true>
 __device__ __forceinline__ void col_ab(const E* lc, const E* lv, int i, float& a, float& b) {
-  if constexpr (std::is_same<E, float>::value) {
+  if constexpr (CACHE && std::is_same<E, float>::value) {
     a = lc[i * W];
     b = lv[i * W];
   } else {
@@ -662,7 +713,9 @@ __device__ __forceinline__ float col_scan_fwd(float A, float B, float s0, float*
   return (w == 0 && j == 0) ? s0 : Be;  // segments after 0 carry the h_0 reset: state = B
 }
 
-template <typename E, int W>
+// GATE: the MinGRU gate-fused form (maps 0, 1 = k, x~ (B, T, D); log h_0 from
+// p.lh0): each lane turns its segment's k, x~ into log a, log b in place first.
+template <typename E, int W, bool GATE = false>
 __global__ void __launch_bounds__(32 * W, 16 / W)
     fwd_col_kernel(Args<E> p, const __grid_constant__ ColMaps maps) {
   extern __shared__ __align__(128) unsigned char col_raw[];
@@ -671,13 +724,16 @@ __global__ void __launch_bounds__(32 * W, 16 / W)
   const int d0 = (int)(blockIdx.x - (long long)bi * p.sper) * W;
   const int lane = threadIdx.x & 31, c = lane % W, s = (threadIdx.x >> 5) * (32 / W) + lane / W;
   const bool cok = d0 + c < p.D;
-  const float lv0 = cok ? to_f32<E>(p.lv[(size_t)bi * (p.T_ + 1) * p.D + d0 + c]) : 0.f;
-  col_fetch<E, W, 2>(maps, sm, p.T_, d0, bi);
+  const float lv0 = !cok ? 0.f
+                    : GATE ? to_f32<E>(p.lh0[(size_t)bi * p.D + d0 + c])
+                           : to_f32<E>(p.lv[(size_t)bi * (p.T_ + 1) * p.D + d0 + c]);
+  col_fetch<E, W, 2, GATE ? 0 : 1>(maps, sm, p.T_, d0, bi);
   int start, n;
   col_segment<W>(p.T_, s, start, n);
   col_wait_rows(sm, start, n);
   E* lc = sm.t[0] + (size_t)start * W + c;
   E* lv = sm.t[1] + (size_t)start * W + c;
+  if constexpr (GATE) (void)col_gate_prologue<E, W>(lc, lv, n);
   const bool lin = __syncthreads_and(col_linear_ok<E, W>(lc, lv, n) && !(lv0 > kColLinHi)) != 0;
   float A, B;
   if (lin) {
@@ -704,11 +760,14 @@ __global__ void __launch_bounds__(32 * W, 16 / W)
   if (threadIdx.x == 0) bulk_wait_read();
 }
 
-template <typename E, int W, bool LIN>
+// GATE: lc, lv hold log a, log b formed from k, x~ (never replaced by cached
+// a, b, so the chain rule can read them); `neg` marks the x~ < 0 steps.
+template <typename E, int W, bool LIN, bool GATE = false>
 __device__ __forceinline__ void col_bwd_body(const Args<E>& p, const ColSmem<E, W>& sm,
                                              int start, int n, int s, float lv0, bool cok,
-                                             size_t row0) {
+                                             size_t row0, unsigned long long neg = 0ull) {
   using M = typename std::conditional<LIN, ColLin, ColLog>::type;
+  constexpr bool CACHE = !GATE;
   constexpr int SPW = 32 / W;
   const int lane = threadIdx.x & 31, w = threadIdx.x >> 5, c = lane % W, j = lane / W;
   E* lc = sm.t[0] + (size_t)start * W + c;
@@ -716,7 +775,7 @@ __device__ __forceinline__ void col_bwd_body(const Args<E>& p, const ColSmem<E, 
   const E* g = sm.t[2] + (size_t)start * W + c;
   const float s0 = LIN ? expf(lv0) : lv0;
   float A, B;
-  col_fwd_agg<E, W, LIN>(lc, lv, n, s == 0, s0, A, B);
+  col_fwd_agg<E, W, LIN, CACHE>(lc, lv, n, s == 0, s0, A, B);
   // Reverse adjoint Y_t = a_t (g_t + Y_{t+1}) per segment: Y_start = P Y_after + Q.
   float P = 1.f, Q = 0.f;
 #pragma unroll
@@ -724,7 +783,7 @@ __device__ __forceinline__ void col_bwd_body(const Args<E>& p, const ColSmem<E, 
     if (i < n) {
       float a, b;
       if (LIN)
-        col_ab<E, W>(lc, lv, i, a, b);
+        col_ab<E, W, CACHE>(lc, lv, i, a, b);
       else
         a = __expf(cld<E, W>(lc, i));
       Q = a * (cld<E, W>(g, i) + Q);
@@ -759,7 +818,7 @@ __device__ __forceinline__ void col_bwd_body(const Args<E>& p, const ColSmem<E, 
       xp[i] = x;
       if (LIN) {
         float a, b;
-        col_ab<E, W>(lc, lv, i, a, b);
+        col_ab<E, W, CACHE>(lc, lv, i, a, b);
         x = fmaf(a, x, b);
       } else {
         x = logaddexp(x + cld<E, W>(lc, i), cld<E, W>(lv, i));
@@ -772,7 +831,7 @@ __device__ __forceinline__ void col_bwd_body(const Args<E>& p, const ColSmem<E, 
       float a, dc, dv;
       if (LIN) {
         float b;
-        col_ab<E, W>(lc, lv, i, a, b);
+        col_ab<E, W, CACHE>(lc, lv, i, a, b);
         dc = G * a * xp[i];
         dv = G * b;
       } else {
@@ -782,13 +841,33 @@ __device__ __forceinline__ void col_bwd_body(const Args<E>& p, const ColSmem<E, 
         dv = G * __expf(cld<E, W>(lv, i));
       }
       y = a * G;
-      cst<E, W>(lc, i, dc);  // dlc_t over lc_t, dlv_{t+1} over lv_t
-      cst<E, W>(lv, i, dv);
+      if constexpr (GATE) {
+        // chain rule through the prologue: sigmoid(k) = 1 - e^{log a} (by expm1,
+        // exact for k << 0), sigmoid(-k) = e^{log a}, g(x~) = e^{log b} / sigmoid(k)
+        const float lci = cld<E, W>(lc, i), lvi = cld<E, W>(lv, i);
+        const float ea = expf(lci), sk = -expm1f(lci);
+        const float dk = fmaf(-sk, dc, ea * dv);
+        const float gx = sk > 0.f ? expf(lvi - logf(sk)) : 1.f;  // sk == 0 only where dv == 0
+        const float fx = ((neg >> i) & 1ull) ? 1.f - gx : 1.f / gx;
+        cst<E, W>(lc, i, dk);  // dk_t over k_t, dx~_t over x~_t
+        cst<E, W>(lv, i, fx * dv);
+      } else {
+        cst<E, W>(lc, i, dc);  // dlc_t over lc_t, dlv_{t+1} over lv_t
+        cst<E, W>(lv, i, dv);
+      }
     }
-  if (s == 0 && cok) p.dlv[row0] = from_f32<E>(y * (LIN ? s0 : expf(lv0)));
+  if (s == 0 && cok) {
+    const float d0v = y * (LIN ? s0 : expf(lv0));
+    if constexpr (GATE)
+      p.dlh0[row0] = from_f32<E>(d0v);
+    else
+      p.dlv[row0] = from_f32<E>(d0v);
+  }
 }
 
-template <typename E, int W>
+// GATE: maps 0, 1 = k, x~; 3, 4 = dk, dx~ (all (B, T, D)); log h_0 and its
+// gradient in p.lh0 / p.dlh0.
+template <typename E, int W, bool GATE = false>
 __global__ void __launch_bounds__(32 * W, 16 / W)
     bwd_col_kernel(Args<E> p, const __grid_constant__ ColMaps maps) {
   extern __shared__ __align__(128) unsigned char col_raw[];
@@ -797,21 +876,25 @@ __global__ void __launch_bounds__(32 * W, 16 / W)
   const int d0 = (int)(blockIdx.x - (long long)bi * p.sper) * W;
   const int lane = threadIdx.x & 31, c = lane % W, s = (threadIdx.x >> 5) * (32 / W) + lane / W;
   const bool cok = d0 + c < p.D;
-  const size_t row0 = (size_t)bi * (p.T_ + 1) * p.D + d0 + c;
-  const float lv0 = cok ? to_f32<E>(p.lv[row0]) : 0.f;
-  col_fetch<E, W, 3>(maps, sm, p.T_, d0, bi);
+  const size_t row0 = GATE ? (size_t)bi * p.D + d0 + c : (size_t)bi * (p.T_ + 1) * p.D + d0 + c;
+  const float lv0 = cok ? to_f32<E>(GATE ? p.lh0[row0] : p.lv[row0]) : 0.f;
+  col_fetch<E, W, 3, GATE ? 0 : 1>(maps, sm, p.T_, d0, bi);
   int start, n;
   col_segment<W>(p.T_, s, start, n);
   col_wait_rows(sm, start, n);
+  unsigned long long neg = 0ull;
+  if constexpr (GATE)
+    neg = col_gate_prologue<E, W>(sm.t[0] + (size_t)start * W + c, sm.t[1] + (size_t)start * W + c,
+                                  n);
   const bool lin = __syncthreads_and(col_linear_ok<E, W>(sm.t[0] + (size_t)start * W + c,
                                                          sm.t[1] + (size_t)start * W + c, n) &&
                                      !(lv0 > kColLinHi)) != 0;
   if (lin)
-    col_bwd_body<E, W, true>(p, sm, start, n, s, lv0, cok, row0);
+    col_bwd_body<E, W, true, GATE>(p, sm, start, n, s, lv0, cok, row0, neg);
   else
-    col_bwd_body<E, W, false>(p, sm, start, n, s, lv0, cok, row0);
+    col_bwd_body<E, W, false, GATE>(p, sm, start, n, s, lv0, cok, row0, neg);
   col_put<E, W>(&maps.m[3], sm.t[0], p.T_, d0, 0, bi);
-  col_put<E, W>(&maps.m[4], sm.t[1], p.T_, d0, 1, bi);
+  col_put<E, W>(&maps.m[4], sm.t[1], p.T_, d0, GATE ? 0 : 1, bi);
   if (threadIdx.x == 0) bulk_wait_read();
 }
 
@@ -1172,6 +1255,169 @@ int dispatch(bool fwd, const void* lc, const void* lv, void* h, const void* gh, 
   }
 }
 
+// ------------------------------------------------------ MinGRU gate scan --
+//
+// parallel_scan_log fed straight from MinGRU's pre-activations k, x~ and
+// log h_0 (B, D). fp32 shapes on the column path run the gate-fused column
+// kernels (k, x~ in, h or dk, dx~ out: no log-coefficient tensors in HBM).
+// Other shapes and 16-bit storage form log a, log b with one elementwise
+// kernel into the workspace, run the scan above, and (backward) turn dlog a,
+// dlog b into dk, dx~ with one more.
+
+template <typename E>
+__global__ void __launch_bounds__(256) gate_prologue_kernel(const E* k, const E* x, const E* lh0,
+                                                            E* lc, E* lv, long long B, long long T,
+                                                            long long D) {
+  const long long n = B * T * D, stride = (long long)gridDim.x * blockDim.x;
+  for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += stride) {
+    const long long d = i % D, bt = i / D, b = bt / T, t = bt - b * T;
+    float a, v;
+    gate_logs(to_f32<E>(k[i]), to_f32<E>(x[i]), a, v);
+    lc[i] = from_f32<E>(a);
+    lv[(b * (T + 1) + t + 1) * D + d] = from_f32<E>(v);
+  }
+  for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < B * D; i += stride)
+    lv[(i / D) * (T + 1) * D + i % D] = lh0[i];
+}
+
+template <typename E>
+__global__ void __launch_bounds__(256) gate_epilogue_kernel(const E* k, const E* x, const E* dlc,
+                                                            const E* dlv, E* dk, E* dx, E* dlh0,
+                                                            long long B, long long T, long long D) {
+  const long long n = B * T * D, stride = (long long)gridDim.x * blockDim.x;
+  for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += stride) {
+    const long long d = i % D, bt = i / D, b = bt / T, t = bt - b * T;
+    float gk, gx;
+    gate_grads(to_f32<E>(k[i]), to_f32<E>(x[i]), to_f32<E>(dlc[i]),
+               to_f32<E>(dlv[(b * (T + 1) + t + 1) * D + d]), gk, gx);
+    dk[i] = from_f32<E>(gk);
+    dx[i] = from_f32<E>(gx);
+  }
+  for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < B * D; i += stride)
+    dlh0[i] = dlv[(i / D) * (T + 1) * D + i % D];
+}
+
+inline bool gate_fused(const Geometry& g, int dtype) { return g.algo == kColumn && dtype == MGS_F32; }
+
+// Workspace of the elementwise route: [scan workspace][lc][lv][dlc][dlv], 256-byte aligned.
+struct GateWs {
+  size_t scan, lc, lv, dlc, dlv, total;
+};
+
+inline GateWs gate_ws(const Geometry& g, long long B, long long T, long long D, int dtype) {
+  GateWs w{};
+  const size_t es = dtype_size(dtype);
+  w.scan = 0;
+  w.lc = align_up(workspace_bytes(g), 256);
+  w.lv = w.lc + align_up((size_t)(B * T * D) * es, 256);
+  w.dlc = w.lv + align_up((size_t)(B * (T + 1) * D) * es, 256);
+  w.dlv = w.dlc + align_up((size_t)(B * T * D) * es, 256);
+  w.total = w.dlv + align_up((size_t)(B * (T + 1) * D) * es, 256);
+  return w;
+}
+
+inline size_t gate_workspace_bytes(long long B, long long T, long long D, int dtype) {
+  const Geometry g = geometry(B, T, D, dtype);
+  if (gate_fused(g, dtype)) return 256;
+  return gate_ws(g, B, T, D, dtype).total;
+}
+
+inline unsigned elementwise_blocks(long long n) {
+  const long long cap = 8LL * sm_count();
+  long long b = (n + 255) / 256;
+  return (unsigned)(b < 1 ? 1 : (b > cap ? cap : b));
+}
+
+template <typename E>
+int gate_run(bool fwd, const void* k, const void* x, const void* lh0, void* h, const void* gh,
+             void* dk, void* dx, void* dlh0, void* carries, long long B, long long T, long long D,
+             int dtype, void* ws, size_t ws_bytes, cudaStream_t st) {
+  if (B == 0 || D == 0) return MGS_OK;
+  if (T == 0) {  // no output: the only gradient, d log h_0, is zero
+    if (!fwd) MGS_CUDA_OK(cudaMemsetAsync(dlh0, 0, (size_t)(B * D) * sizeof(E), st));
+    return MGS_OK;
+  }
+  const Geometry g = geometry(B, T, D, dtype);
+  if (ws == nullptr || ws_bytes < gate_workspace_bytes(B, T, D, dtype)) return MGS_WORKSPACE_TOO_SMALL;
+  if (!aligned(ws, 256)) return MGS_BAD_ALIGNMENT;
+  if (gate_fused(g, dtype)) {
+    const void* ptrs[7] = {k, x, lh0, fwd ? h : gh, fwd ? nullptr : dk, fwd ? nullptr : dx,
+                           fwd ? nullptr : dlh0};
+    for (const void* q : ptrs)
+      if (q != nullptr && !aligned(q, 16)) return MGS_BAD_ALIGNMENT;
+    if (g.nstrips > 0x7fffffffLL || B > 0x7fffffffLL) return MGS_UNSUPPORTED;
+    Args<E> p{};
+    p.lc = static_cast<const E*>(k);
+    p.lv = static_cast<const E*>(x);
+    p.lh0 = static_cast<const E*>(lh0);
+    p.h = static_cast<E*>(h);
+    p.gh = static_cast<const E*>(gh);
+    p.dlc = static_cast<E*>(dk);
+    p.dlv = static_cast<E*>(dx);
+    p.dlh0 = static_cast<E*>(dlh0);
+    p.T_ = T;
+    p.D = D;
+    p.sper = g.sper;
+    p.nstrips = g.nstrips;
+    ColMaps maps;
+    const unsigned bx = (unsigned)g.cpt, by = kColBox;
+    bool ok = make_tmap_3d<E>(&maps.m[0], k, D, T, B, bx, by) &&
+              make_tmap_3d<E>(&maps.m[1], x, D, T, B, bx, by);
+    if (fwd)
+      ok = ok && make_tmap_3d<E>(&maps.m[2], h, D, T, B, bx, by);
+    else
+      ok = ok && make_tmap_3d<E>(&maps.m[2], gh, D, T, B, bx, by) &&
+           make_tmap_3d<E>(&maps.m[3], dk, D, T, B, bx, by) &&
+           make_tmap_3d<E>(&maps.m[4], dx, D, T, B, bx, by);
+    if (!ok) return MGS_LAUNCH_FAILED;
+    const size_t smem = col_smem_bytes<E>(T, fwd ? 2 : 3, g.cpt);
+    void (*kern)(Args<E>, const ColMaps) =
+        g.cpt == 16 ? (fwd ? fwd_col_kernel<E, 16, true> : bwd_col_kernel<E, 16, true>)
+                    : (fwd ? fwd_col_kernel<E, 8, true> : bwd_col_kernel<E, 8, true>);
+    MGS_CUDA_OK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+    kern<<<(unsigned)g.nstrips, 32 * g.cpt, smem, st>>>(p, maps);
+    return cudaGetLastError() == cudaSuccess ? MGS_OK : MGS_LAUNCH_FAILED;
+  }
+  const GateWs w = gate_ws(g, B, T, D, dtype);
+  char* base = static_cast<char*>(ws);
+  E* lc = reinterpret_cast<E*>(base + w.lc);
+  E* lv = reinterpret_cast<E*>(base + w.lv);
+  const unsigned nb = elementwise_blocks(B * T * D);
+  gate_prologue_kernel<E><<<nb, 256, 0, st>>>(static_cast<const E*>(k), static_cast<const E*>(x),
+                                              static_cast<const E*>(lh0), lc, lv, B, T, D);
+  if (cudaGetLastError() != cudaSuccess) return MGS_LAUNCH_FAILED;
+  if (fwd)
+    return run<E>(true, lc, lv, h, nullptr, nullptr, nullptr, carries, B, T, D, dtype, ws,
+                  w.lc, st);
+  E* dlc = reinterpret_cast<E*>(base + w.dlc);
+  E* dlv = reinterpret_cast<E*>(base + w.dlv);
+  const int rc = run<E>(false, lc, lv, nullptr, gh, dlc, dlv, carries, B, T, D, dtype, ws, w.lc, st);
+  if (rc != MGS_OK) return rc;
+  gate_epilogue_kernel<E><<<nb, 256, 0, st>>>(static_cast<const E*>(k), static_cast<const E*>(x),
+                                              dlc, dlv, static_cast<E*>(dk), static_cast<E*>(dx),
+                                              static_cast<E*>(dlh0), B, T, D);
+  return cudaGetLastError() == cudaSuccess ? MGS_OK : MGS_LAUNCH_FAILED;
+}
+
+int gate_dispatch(bool fwd, const void* k, const void* x, const void* lh0, void* h, const void* gh,
+                  void* dk, void* dx, void* dlh0, void* carries, long long B, long long T,
+                  long long D, int dtype, void* ws, size_t ws_bytes, cudaStream_t st) {
+  if (B < 0 || T < 0 || D < 0) return MGS_BAD_SHAPE;
+  switch (dtype) {
+    case MGS_F32:
+      return gate_run<float>(fwd, k, x, lh0, h, gh, dk, dx, dlh0, carries, B, T, D, dtype, ws,
+                             ws_bytes, st);
+    case MGS_BF16:
+      return gate_run<__nv_bfloat16>(fwd, k, x, lh0, h, gh, dk, dx, dlh0, carries, B, T, D, dtype,
+                                     ws, ws_bytes, st);
+    case MGS_F16:
+      return gate_run<__half>(fwd, k, x, lh0, h, gh, dk, dx, dlh0, carries, B, T, D, dtype, ws,
+                              ws_bytes, st);
+    default:
+      return MGS_BAD_DTYPE;
+  }
+}
+
 }  // namespace logscan
 
 unsigned take_error_log(cudaStream_t s) { return take_sticky_error(s); }
@@ -1198,6 +1444,32 @@ int mgs_log_scan_fwd(const void* log_coeffs, const void* log_values, void* h, vo
   return mgs::logscan::dispatch(true, log_coeffs, log_values, h, nullptr, nullptr, nullptr,
                                 carries, B, T, D, dtype, workspace, workspace_bytes,
                                 static_cast<cudaStream_t>(stream));
+}
+
+size_t mgs_log_gate_scan_workspace_size(int64_t B, int64_t T, int64_t D, int dtype) {
+  if (mgs::dtype_size(dtype) == 0 || B < 0 || T < 0 || D < 0) return 0;
+  return mgs::logscan::gate_workspace_bytes(B, T, D, dtype);
+}
+
+size_t mgs_log_gate_scan_carry_size(int64_t B, int64_t T, int64_t D, int dtype) {
+  return mgs_log_scan_carry_size(B, T, D, dtype);  // same scan geometry
+}
+
+int mgs_log_gate_scan_fwd(const void* k, const void* x, const void* log_h0, void* h, void* carries,
+                          int64_t B, int64_t T, int64_t D, int dtype, void* workspace,
+                          size_t workspace_bytes, void* stream) {
+  return mgs::logscan::gate_dispatch(true, k, x, log_h0, h, nullptr, nullptr, nullptr, nullptr,
+                                     carries, B, T, D, dtype, workspace, workspace_bytes,
+                                     static_cast<cudaStream_t>(stream));
+}
+
+int mgs_log_gate_scan_bwd(const void* k, const void* x, const void* log_h0, const void* grad_h,
+                          const void* carries, void* dk, void* dx, void* dlog_h0, int64_t B,
+                          int64_t T, int64_t D, int dtype, void* workspace, size_t workspace_bytes,
+                          void* stream) {
+  return mgs::logscan::gate_dispatch(false, k, x, log_h0, nullptr, grad_h, dk, dx, dlog_h0,
+                                     const_cast<void*>(carries), B, T, D, dtype, workspace,
+                                     workspace_bytes, static_cast<cudaStream_t>(stream));
 }
 
 int mgs_log_scan_bwd(const void* log_coeffs, const void* log_values, const void* grad_h,

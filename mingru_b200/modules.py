@@ -42,6 +42,7 @@ from .scan_ops import (
     brickwall_meta,
     delta_scan_impl,
     linear_scan,
+    mingru_gate_scan,
     parallel_scan_log,
 )
 
@@ -184,11 +185,11 @@ class MinGRU(DecayMixin, nn.Module):
                                 "(an output of forward()/step()), not a pre-activation.")
             log_h0 = h_0.clamp_min(torch.finfo(h_0.dtype).tiny).log()
         k = self.linear_z(x)
-        log_z = -F.softplus(-k)
-        log_coeffs = -F.softplus(k)
         dt = self._prepare_decay(delta_t, canonical_ndim=2)
-        if dt is not None:
-            log_coeffs = log_coeffs - self._decay_lambda() * dt.unsqueeze(-1)
+        if dt is None:  # the coefficient prologue runs inside the scan kernels
+            return mingru_gate_scan(k, self.linear_h(x), log_h0.to(k.dtype))
+        log_z = -F.softplus(-k)
+        log_coeffs = -F.softplus(k) - self._decay_lambda() * dt.unsqueeze(-1)
         log_values = torch.cat([log_h0.to(log_z.dtype), log_z + log_g(self.linear_h(x))], dim=1)
         return parallel_scan_log(log_coeffs, log_values)
 

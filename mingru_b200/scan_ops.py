@@ -299,6 +299,118 @@ def parallel_scan_log(log_coeffs: torch.Tensor, log_values: torch.Tensor) -> tor
     return h
 
 
+# =================================================== MinGRU gate scan ==
+
+
+@torch.library.custom_op("mingru_b200::log_gate_scan_fwd", mutates_args=())
+def _log_gate_fwd(
+    k: torch.Tensor, x: torch.Tensor, log_h0: torch.Tensor, save_carries: bool
+) -> tuple[torch.Tensor, torch.Tensor]:
+    lib = _lib.load()
+    with torch.cuda.device(k.device):  # sizes are queried on the launch device
+        k, x, lh0 = _dense(k), _dense(x), _dense(log_h0)
+        Bn, T, D = k.shape
+        code = _dtype_code("mingru_gate_scan", k)
+        h = torch.empty_like(k)
+        csz = lib.mgs_log_gate_scan_carry_size(Bn, T, D, code) if save_carries else 0
+        carries = torch.empty(csz // 4, dtype=torch.float32, device=k.device)
+        ws = _workspace(lib.mgs_log_gate_scan_workspace_size(Bn, T, D, code), k.device)
+        st = lib.mgs_log_gate_scan_fwd(
+            _ptr(k), _ptr(x), _ptr(lh0), _ptr(h), _ptr(carries) if save_carries else None,
+            Bn, T, D, code, _ptr(ws), ws.numel(), _stream(k),
+        )
+        _lib.check(st, "mingru_gate_scan forward")
+        return h, carries
+
+
+@_log_gate_fwd.register_fake
+def _(k, x, log_h0, save_carries):
+    Bn, T, D = k.shape
+    csz = _lib.load().mgs_log_gate_scan_carry_size(Bn, T, D, _dtype_code("mingru_gate_scan", k))
+    return torch.empty_like(k), k.new_empty((csz // 4 if save_carries else 0,), dtype=torch.float32)
+
+
+@torch.library.custom_op("mingru_b200::log_gate_scan_bwd", mutates_args=())
+def _log_gate_bwd(
+    k: torch.Tensor, x: torch.Tensor, log_h0: torch.Tensor, grad_h: torch.Tensor,
+    carries: torch.Tensor,
+) -> tuple[torch.Tensor, torch.Tensor, torch.Tensor]:
+    lib = _lib.load()
+    with torch.cuda.device(k.device):  # sizes are queried on the launch device
+        k, x, lh0 = _dense(k), _dense(x), _dense(log_h0)
+        gh = _dense(grad_h.to(k.dtype))
+        Bn, T, D = k.shape
+        code = _dtype_code("mingru_gate_scan", k)
+        if carries.numel() * 4 < lib.mgs_log_gate_scan_carry_size(Bn, T, D, code):
+            raise RuntimeError("mingru_gate_scan backward: forward carries were not saved")
+        dk, dx, dlh0 = torch.empty_like(k), torch.empty_like(x), torch.empty_like(lh0)
+        ws = _workspace(lib.mgs_log_gate_scan_workspace_size(Bn, T, D, code), k.device)
+        st = lib.mgs_log_gate_scan_bwd(
+            _ptr(k), _ptr(x), _ptr(lh0), _ptr(gh), _ptr(carries), _ptr(dk), _ptr(dx), _ptr(dlh0),
+            Bn, T, D, code, _ptr(ws), ws.numel(), _stream(k),
+        )
+        _lib.check(st, "mingru_gate_scan backward")
+        return dk, dx, dlh0
+
+
+@_log_gate_bwd.register_fake
+def _(k, x, log_h0, grad_h, carries):
+    return torch.empty_like(k), torch.empty_like(x), torch.empty_like(log_h0)
+
+
+def _log_gate_setup(ctx, inputs, output):
+    k, x, lh0, _ = inputs
+    ctx.save_for_backward(k, x, lh0, output[1])
+    ctx.mark_non_differentiable(output[1])
+    ctx.set_materialize_grads(False)
+
+
+def _log_gate_backward(ctx, grad_h, _gcarries):
+    if torch.is_grad_enabled():
+        raise RuntimeError(
+            "mingru_gate_scan does not support second-order autograd (create_graph=True)"
+        )
+    k, x, lh0, carries = ctx.saved_tensors
+    if grad_h is None:
+        return None, None, None, None
+    dk, dx, dlh0 = _log_gate_bwd(k, x, lh0, grad_h, carries)
+    return dk, dx, dlh0, None
+
+
+torch.library.register_autograd(
+    "mingru_b200::log_gate_scan_fwd", _log_gate_backward, setup_context=_log_gate_setup
+)
+
+
+def mingru_gate_scan(k: torch.Tensor, x: torch.Tensor, log_h0: torch.Tensor) -> torch.Tensor:
+    """MinGRU's scan straight from its pre-activations: returns ``h_1..h_T``.
+
+    ``k`` = ``linear_z(x)`` and ``x`` = ``linear_h(x)`` (the candidate
+    pre-activation), both ``(B, T, D)``; ``log_h0`` ``(B, D)`` or ``(B, 1, D)``.
+    Equal to ``parallel_scan_log(-softplus(k), cat([log_h0, -softplus(-k) +
+    log_g(x)], 1))`` -- what MinGRU.forward builds without decay (reference
+    ``min_gru.py:1383-1397``) -- with the prologue fused into the scan kernels:
+    the log coefficients never exist in HBM on the column path (fp32,
+    T <= 1024), and the backward returns ``dk``, ``dx`` and ``dlog_h0``
+    directly. Differentiable w.r.t. all three inputs.
+    """
+    op = "mingru_gate_scan"
+    if k.ndim != 3 or x.shape != k.shape:
+        raise ValueError(f"{op}: need matching (B, T, D) k and x (got k={tuple(k.shape)}, "
+                         f"x={tuple(x.shape)})")
+    Bn, T, D = k.shape
+    lh0 = log_h0.reshape(Bn, D) if log_h0.ndim == 3 and log_h0.shape[1] == 1 else log_h0
+    if tuple(lh0.shape) != (Bn, D):
+        raise ValueError(f"{op}: log_h0 must be (B, D) or (B, 1, D) (got {tuple(log_h0.shape)})")
+    _require_cuda(op, k, x, lh0)
+    if x.dtype != k.dtype or lh0.dtype != k.dtype:
+        raise ValueError(f"{op}: k, x and log_h0 must share a dtype")
+    _dtype_code(op, k)
+    need = torch.is_grad_enabled() and (k.requires_grad or x.requires_grad or lh0.requires_grad)
+    h, _ = _log_gate_fwd(k, x, lh0, need)
+    return h
+
+
 # ================================================ matrix(_affine)_scan ==
 
 
@@ -760,7 +872,8 @@ def delta_scan_impl(
     (whole tokens, at most ``64 / nh`` on the bf16 tensor-core kernels) -- the
     result differs only by rounding. The state's value columns evolve
     independently, so ``d_v > 64`` runs as blocks of 64 columns whose
-    gradients w.r.t. Q, K and beta add up.
+    gradients w.r.t. Q, K and beta add up (in fp32: 16-bit inputs run those
+    blocks on fp32 copies).
     """
     op = "delta_scan"
     if Q.ndim != 4 or K.ndim != 5 or V.ndim != 5 or beta.ndim != 4 or H0.ndim != 4:
@@ -797,14 +910,19 @@ def delta_scan_impl(
         )
     if dv <= _DELTA_DV_BLOCK:
         y, HT, _ = _delta_fwd(Q, K, V, beta, H0, int(chunk_size))
-    else:  # independent value-column blocks; autograd adds their Q, K, beta gradients
+    else:
+        # Independent value-column blocks; autograd adds their Q, K, beta
+        # gradients. Blocks of 16-bit inputs run in fp32 so the partial
+        # gradients are summed before the one rounding to the input dtype.
+        wide = (lambda t: t.float()) if Q.dtype != torch.float32 else (lambda t: t)
+        Qw, Kw, bw = wide(Q), wide(K), wide(beta)
         ys, hts = [], []
         for j0 in range(0, dv, _DELTA_DV_BLOCK):
             j1 = min(dv, j0 + _DELTA_DV_BLOCK)
-            yj, hj, _ = _delta_fwd(Q, K, V[..., j0:j1], beta, H0[..., j0:j1], int(chunk_size))
+            yj, hj, _ = _delta_fwd(Qw, Kw, wide(V[..., j0:j1]), bw, H0[..., j0:j1], int(chunk_size))
             ys.append(yj)
             hts.append(hj)
-        y, HT = torch.cat(ys, -1), torch.cat(hts, -1)
+        y, HT = torch.cat(ys, -1).to(Q.dtype), torch.cat(hts, -1)
     if H0.dtype == torch.float64:
         HT = HT.double()
     return y, HT

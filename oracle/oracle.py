@@ -85,6 +85,41 @@ def parallel_scan_log_bwd(log_coeffs, log_values, grad_h, dtype=np.float64):
     return dlc, dlv
 
 
+def _softplus(x):
+    return np.maximum(x, 0) + np.log1p(np.exp(-np.abs(x)))
+
+
+def mingru_gate_logs(k, x, log_h0):
+    """(log_coeffs, log_values) MinGRU.forward builds from the gate and
+    candidate pre-activations k = linear_z(x), x~ = linear_h(x) and log h_0
+    (B, D) (reference min_gru.py:1383-1397, log_g at min_gru.py:751-752):
+    log a = -softplus(k), log b = -softplus(-k) + log_g(x~)."""
+    k, x, lh0 = (np.asarray(t, dtype=np.float64) for t in (k, x, log_h0))
+    log_g = np.where(x >= 0, np.log(np.maximum(x, 0) + 0.5), -_softplus(-x))
+    lc = -_softplus(k)
+    lv = np.concatenate([lh0[:, None, :], -_softplus(-k) + log_g], axis=1)
+    return lc, lv
+
+
+def mingru_gate_scan(k, x, log_h0):
+    """h of parallel_scan_log over MinGRU's gate prologue (fp64)."""
+    return parallel_scan_log(*mingru_gate_logs(k, x, log_h0))
+
+
+def mingru_gate_scan_bwd(k, x, log_h0, grad_h):
+    """(dk, dx~, dlog_h0): the log-scan adjoint chained through the prologue
+    (d log a/dk = -sigmoid(k), d log b/dk = sigmoid(-k), d log_g/dx~ =
+    1/(x~ + 1/2) for x~ >= 0 else sigmoid(-x~))."""
+    k, x = np.asarray(k, dtype=np.float64), np.asarray(x, dtype=np.float64)
+    lc, lv = mingru_gate_logs(k, x, log_h0)
+    dlc, dlv = parallel_scan_log_bwd(lc, lv, grad_h)
+    with np.errstate(over="ignore"):
+        sk = 1.0 / (1.0 + np.exp(-k))
+        fx = np.where(x >= 0, 1.0 / (np.maximum(x, 0) + 0.5), 1.0 / (1.0 + np.exp(x)))
+    dk = -sk * dlc + (1.0 - sk) * dlv[:, 1:]
+    return dk, fx * dlv[:, 1:], dlv[:, 0]
+
+
 def linear_scan(a, b, dtype=np.float64):
     """(A, Bc) of min_gru.linear_scan."""
     a, b = _arr(a, dtype), _arr(b, dtype)
