@@ -268,6 +268,48 @@ class LogScanWorkload(ScanWorkload):
         oracle.parallel_scan_log_bwd(lc, lv, gh, dtype=np.float32)
 
 
+class GateScanWorkload(LogScanWorkload):
+    """BASELINE config 1's MinGRU scan fed from the pre-activations: the gate
+    scan (coefficient prologue fused into the scan kernels) on k, x~ ~ N(0,1)
+    and log h0 = log(float32 tiny), B=8, T=1024, D=256. Same algorithmic bytes
+    as config 1 (fwd reads k, x~ and writes h; bwd reads k, x~, grad_h and writes
+    dk, dx~). The unfused path -- softplus / log_g / cat in torch, then
+    parallel_scan_log -- is timed in the same run for comparison."""
+
+    kernels = {"fwd": "log_gate_scan_fwd", "bwd": "log_gate_scan_bwd"}
+    workload = ("MinGRU gate scan fwd+bwd from pre-activations (BASELINE config 1 shape, "
+                "prologue fused)")
+
+    def make_host(self, rows, seed):
+        g = torch.Generator().manual_seed(seed)
+        k = torch.randn(rows, self.T, self.D, generator=g)
+        x = torch.randn(rows, self.T, self.D, generator=g)
+        lh0 = torch.full((rows, self.D), math.log(torch.finfo(torch.float32).tiny))
+        gh = torch.randn(rows, self.T, self.D, generator=torch.Generator().manual_seed(1234 + seed))
+        return [k, x, lh0], [gh]
+
+    def forward(self, k, x, lh0):
+        import mingru_b200 as mb
+
+        return (mb.mingru_gate_scan(k, x, lh0),)
+
+    def unfused_forward(self, k, x, lh0):
+        import mingru_b200 as mb
+
+        F = torch.nn.functional
+        lc = -F.softplus(k)
+        lv = torch.cat([lh0[:, None], -F.softplus(-k) + mb.log_g(x)], 1)
+        return (mb.parallel_scan_log(lc, lv),)
+
+    def cpu_step(self, sample):
+        from oracle import oracle
+
+        (k, x, lh0), (gh,) = sample
+        lc, lv = oracle.mingru_gate_logs(k, x, lh0)
+        oracle.parallel_scan_log(lc, lv, dtype=np.float32)
+        oracle.parallel_scan_log_bwd(lc, lv, gh, dtype=np.float32)
+
+
 class MatrixScanWorkload(ScanWorkload):
     """RotationMinGRU matrix_scan (2x2 blocks) fwd+bwd,
     B=16, T=2048, D=512 (n=256 blocks): M = sigmoid(N(0,1)) * R(theta),
@@ -473,6 +515,7 @@ class DeltaWorkload(ScanWorkload):
 
 WORKLOADS = {
     "cfg1": lambda: LogScanWorkload(),
+    "cfg1-gate": lambda: GateScanWorkload(name="cfg1-gate"),
     "cfg2": lambda: LinearScanWorkload(),
     "cfg2-bf16": lambda: LinearScanWorkload(dtype=torch.bfloat16, name="cfg2-bf16"),
     "cfg3": lambda: MatrixScanWorkload(),
@@ -834,6 +877,14 @@ def run_ours(args, w) -> None:
         fwd_ms = time_graph(gf, reps, dev, flush)
         bwd_ms = time_graph(gb, reps, dev, flush)
         del gf, gb, _kf, _kb, outs, graph
+        unfused_ms = None
+        if hasattr(w, "unfused_forward"):  # the same step through the unfused path
+            def unfused_step():
+                o = w.unfused_forward(*ins)
+                return o, torch.autograd.grad(o, ins, cots)
+            gu, _ku = capture(unfused_step, dev, stream=work)
+            unfused_ms = time_graph(gu, reps, dev, flush)
+            del gu, _ku
 
         # ---- e2e: public API with pinned host buffers, copies inside the timed region
         with NumaLocal(dev) as numa:
@@ -888,6 +939,7 @@ def run_ours(args, w) -> None:
         "config": cfg,
         "tflops": (w.flops / (per_step_ms * 1e-3) / 1e12) if hasattr(w, "flops") else None,
         "kernel_ms": {"fwd": fwd_ms, "bwd": bwd_ms},
+        "unfused_ms_per_step": unfused_ms,
         "roofline": {
             "bound": "hbm",
             "kernel": w.kernels[dom],
@@ -913,6 +965,145 @@ def run_ours(args, w) -> None:
                     "the previous step's results come back",
         },
         "gpu_launches": w.launches_per_step * args.steps,
+        "clocks": clk.summary(),
+    }
+    print(json.dumps(line), flush=True)
+
+
+def run_stack(args) -> None:
+    """MinGRUStack training step (forward, backward, AdamW) under a CUDA graph.
+
+    Not a BASELINE configuration: it measures whether the scan kernels still
+    dominate a whole training step once they are fast (the stack's LayerNorms,
+    projections, MLPs and the optimizer around them). Synthetic input and a
+    mean-square loss on the output; the step is captured once and replayed.
+    Reports tokens/s of the graph replay, the eager step for comparison, and the
+    share of the step's device time spent in this library's scan kernels
+    (torch.profiler over replays, kernels named mgs::...)."""
+    rank, world, local = dist_setup(args.gpus)
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    import mingru_b200 as mb
+
+    B, T, D, L = args.stack_batch, args.stack_t, args.stack_d, args.stack_layers
+    mixers = args.stack_mixers.split(",")
+    mixers = (mixers * L)[:L]
+    torch.manual_seed(0)
+    model = mb.MinGRUStack(D, D, L, mixer=mixers).to(dev)
+    opt = torch.optim.AdamW(model.parameters(), lr=1e-4, capturable=True, foreach=True)
+    g = torch.Generator(device=dev).manual_seed(rank)
+    x = torch.randn(B, T, D, device=dev, generator=g)
+
+    def step():
+        opt.zero_grad(set_to_none=True)
+        out, _ = model(x)
+        loss = out.float().pow(2).mean()
+        loss.backward()
+        opt.step()
+        return loss
+
+    work = torch.cuda.Stream(dev)
+    work.wait_stream(torch.cuda.current_stream(dev))
+    with torch.cuda.stream(work):
+        for _ in range(args.warmup):
+            step()
+        torch.cuda.synchronize(dev)
+        mb.raise_device_error(dev)
+        # eager step time (for the graph's launch-overhead saving)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(args.steps):
+            step()
+        e1.record()
+        torch.cuda.synchronize(dev)
+        eager_ms = e0.elapsed_time(e1) / args.steps
+        graph = torch.cuda.CUDAGraph()
+        opt.zero_grad(set_to_none=True)
+        with torch.cuda.graph(graph, stream=work):
+            static_loss = step()
+        for _ in range(3):
+            graph.replay()
+        torch.cuda.synchronize(dev)
+
+        def window() -> float:
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            barrier(world, dev)
+            torch.cuda.synchronize(dev)
+            a.record()
+            for _ in range(args.steps):
+                graph.replay()
+            b.record()
+            torch.cuda.synchronize(dev)
+            barrier(world, dev)
+            return max_over_ranks(a.elapsed_time(b), world, dev)
+
+        with ClockSampler(dev.index) as clk:
+            clk.mark_start()
+            t0 = time.perf_counter()
+            wins = [window()]
+            n_win = int(max_over_ranks(float(max(1, min(args.max_windows, math.ceil(
+                args.min_seconds / max(time.perf_counter() - t0, 1e-4))))), world, dev))
+            for _ in range(n_win - 1):
+                wins.append(window())
+            clk.mark_stop()
+        ms = statistics.median(wins)
+        mb.raise_device_error(dev)
+        loss_val = float(static_loss.item())
+
+        # device-time share of the scan kernels over a few replays
+        share, scan_ms, kernels = None, None, {}
+        try:
+            from torch.profiler import ProfilerActivity, profile
+
+            reps = 5
+            with profile(activities=[ProfilerActivity.CUDA]) as prof:
+                for _ in range(reps):
+                    graph.replay()
+                torch.cuda.synchronize(dev)
+            tot = scan = 0.0
+            for ev in prof.events():
+                if ev.device_type is None or "cuda" not in str(ev.device_type).lower():
+                    continue
+                t = ev.device_time_total if hasattr(ev, "device_time_total") else ev.cuda_time_total
+                tot += t
+                if "mgs::" in ev.name:
+                    scan += t
+                    short = ev.name.split("(")[0].replace("void ", "")
+                    kernels[short] = kernels.get(short, 0.0) + t / reps / 1e3
+            if tot > 0:
+                share, scan_ms = scan / tot, scan / reps / 1e3
+        except Exception as exc:  # profiler unavailable: report without the share
+            kernels = {"profiler_error": str(exc)[:200]}
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.destroy_process_group()
+    if rank != 0:
+        return
+    per_step = ms / args.steps
+    line = {
+        "metric": "MinGRUStack training step tokens/s",
+        "value": B * T * world * args.steps / (ms * 1e-3),
+        "unit": "tokens/s",
+        "n_gpus": world,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": per_step,
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": "f32",
+        "data": "synthetic (seeded), random-init weights",
+        "config": {"workload": "MinGRUStack fwd+bwd+AdamW step (CUDA graph)", "B_per_gpu": B,
+                   "T": T, "d_model": D, "n_layers": L, "mixers": mixers,
+                   "windows": f"median of {len(wins)} windows of {args.steps} steps"},
+        "eager_ms_per_step": eager_ms,
+        "graph_speedup": eager_ms / per_step,
+        "scan_share": share,
+        "scan_ms_per_step": scan_ms,
+        "scan_kernels_ms": kernels,
+        "loss": loss_val,
+        "gpu_launches": None,
         "clocks": clk.summary(),
     }
     print(json.dumps(line), flush=True)
@@ -966,7 +1157,13 @@ def main() -> None:
     ap.add_argument("--steps", type=int, default=1000)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--config", choices=sorted(WORKLOADS), default="cfg2")
+    ap.add_argument("--config", choices=sorted(WORKLOADS) + ["stack"], default="cfg2")
+    ap.add_argument("--stack-batch", type=int, default=8)
+    ap.add_argument("--stack-t", type=int, default=1024)
+    ap.add_argument("--stack-d", type=int, default=512)
+    ap.add_argument("--stack-layers", type=int, default=4)
+    ap.add_argument("--stack-mixers", default="log,signed,rotation,givens",
+                    help="comma-separated mixers, cycled over the layers")
     ap.add_argument("--e2e-steps", type=int, default=5)
     ap.add_argument("--ref-rows", type=int, default=2,
                     help="batch rows of each CPU sample (reference arm and cpu_baseline)")
@@ -982,6 +1179,13 @@ def main() -> None:
                     help="override the per-GPU batch (small ncu captures only; not a bench line)")
     args = ap.parse_args()
     args.warmup = max(3, args.warmup)  # timing rule: at least 3 untimed warm-up steps
+    if args.config == "stack":
+        if args.impl == "reference":
+            print(json.dumps({"impl": "reference", "unavailable": "the stack training step has "
+                              "no reference CPU arm (the reference arm times the scan path)"}))
+            return
+        run_stack(args)
+        return
     w = WORKLOADS[args.config]()
     if args.batch is not None:
         w.B = args.batch
