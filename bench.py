@@ -1109,6 +1109,92 @@ def run_stack(args) -> None:
     print(json.dumps(line), flush=True)
 
 
+def run_stack_step(args) -> None:
+    """MinGRUStack.step (the streaming / decoding path, one token per call for
+    a batch of streams): tokens/s of the eager step loop and of the step
+    captured once as a CUDA graph and replayed (state carried in static
+    buffers). The mixers' recurrence updates are the fused step kernels."""
+    rank, world, local = dist_setup(args.gpus)
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    import mingru_b200 as mb
+
+    B, D, L = args.stack_batch, args.stack_d, args.stack_layers
+    mixers = (args.stack_mixers.split(",") * L)[:L]
+    torch.manual_seed(0)
+    model = mb.MinGRUStack(D, D, L, mixer=mixers).to(dev).eval()
+    g = torch.Generator(device=dev).manual_seed(rank)
+    x = torch.randn(B, D, device=dev, generator=g)
+    work = torch.cuda.Stream(dev)
+    work.wait_stream(torch.cuda.current_stream(dev))
+    with torch.cuda.stream(work), torch.no_grad():
+        _, state = model.step(x, model.init_state())  # materialise every layer's state
+        for _ in range(args.warmup):
+            _, state = model.step(x, state)
+        torch.cuda.synchronize(dev)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(args.steps):
+            _, state = model.step(x, state)
+        e1.record()
+        torch.cuda.synchronize(dev)
+        eager_ms = e0.elapsed_time(e1) / args.steps
+        static = [s_.clone() for s_ in state]
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph, stream=work):
+            out, new = model.step(x, static)
+            for dst, src in zip(static, new):
+                dst.copy_(src)
+        for _ in range(3):
+            graph.replay()
+        torch.cuda.synchronize(dev)
+        with ClockSampler(dev.index) as clk:
+            clk.mark_start()
+            wins = []
+            for _ in range(max(1, args.max_windows // 5)):
+                a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                barrier(world, dev)
+                torch.cuda.synchronize(dev)
+                a.record()
+                for _ in range(args.steps):
+                    graph.replay()
+                b.record()
+                torch.cuda.synchronize(dev)
+                wins.append(max_over_ranks(a.elapsed_time(b), world, dev))
+            clk.mark_stop()
+        ms = statistics.median(wins)
+        mb.raise_device_error(dev)
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.destroy_process_group()
+    if rank != 0:
+        return
+    per_tok = ms / args.steps
+    line = {
+        "metric": "MinGRUStack.step tokens/s (streaming decode)",
+        "value": B * world * args.steps / (ms * 1e-3),
+        "unit": "tokens/s",
+        "n_gpus": world,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": per_tok,
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": "f32",
+        "data": "synthetic (seeded), random-init weights",
+        "config": {"workload": "MinGRUStack.step, one token per stream (CUDA graph)",
+                   "streams_per_gpu": B, "d_model": D, "n_layers": L, "mixers": mixers,
+                   "windows": f"median of {len(wins)} windows of {args.steps} steps"},
+        "eager_ms_per_step": eager_ms,
+        "graph_speedup": eager_ms / per_tok,
+        "gpu_launches": None,
+        "clocks": clk.summary(),
+    }
+    print(json.dumps(line), flush=True)
+
+
 def e2e_pipeline(w, est, steps: int, dev) -> float:
     """Run `steps` end-to-end steps and return their device time in ms.
 
@@ -1157,7 +1243,8 @@ def main() -> None:
     ap.add_argument("--steps", type=int, default=1000)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--config", choices=sorted(WORKLOADS) + ["stack"], default="cfg2")
+    ap.add_argument("--config", choices=sorted(WORKLOADS) + ["stack", "stack-step"],
+                    default="cfg2")
     ap.add_argument("--stack-batch", type=int, default=8)
     ap.add_argument("--stack-t", type=int, default=1024)
     ap.add_argument("--stack-d", type=int, default=512)
@@ -1179,12 +1266,12 @@ def main() -> None:
                     help="override the per-GPU batch (small ncu captures only; not a bench line)")
     args = ap.parse_args()
     args.warmup = max(3, args.warmup)  # timing rule: at least 3 untimed warm-up steps
-    if args.config == "stack":
+    if args.config in ("stack", "stack-step"):
         if args.impl == "reference":
-            print(json.dumps({"impl": "reference", "unavailable": "the stack training step has "
-                              "no reference CPU arm (the reference arm times the scan path)"}))
+            print(json.dumps({"impl": "reference", "unavailable": "the stack benches have no "
+                              "reference CPU arm (the reference arm times the scan path)"}))
             return
-        run_stack(args)
+        (run_stack if args.config == "stack" else run_stack_step)(args)
         return
     w = WORKLOADS[args.config]()
     if args.batch is not None:

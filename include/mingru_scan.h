@@ -283,6 +283,43 @@ int mgs_delta_bwd(const void* Q, const void* K, const void* V, const void* beta,
                   float* dH0, int64_t B, int H, int64_t T, int nh, int dk, int dv, int chunk,
                   int dtype, void* workspace, size_t workspace_bytes, void* stream);
 
+/* ------------------------------------------------------------------------ */
+/* Streaming step: one token's recurrence update per mixer, one kernel each.
+ * Replaces the per-token torch op chains of MinGRU.step (min_gru.py:1399-1448),
+ * SignedMinGRU.step (min_gru.py:1858-1901), RotationMinGRU.step
+ * (min_gru.py:2316-2359), GivensMinGRU.step (min_gru.py:2776-2818) and
+ * DeltaMinGRU.step (min_gru.py:3611-3688), which MinGRUStack.step
+ * (min_gru.py:4289-4336) calls per layer. Inputs are the outputs of the
+ * mixers' linear projections (pre-activations) and the previous state, all in
+ * the op dtype, C-contiguous; `gamma` (the decay factor exp(-lambda dt) at the
+ * state's granularity) may be NULL (no decay). The new state may overwrite
+ * the previous one (same pointer). fp32 arithmetic.
+ *   mingru:   k, xh, h_prev, gamma, h (B, D):
+ *             h = gamma (1 - sigmoid(k)) h_prev + sigmoid(k) g(xh)
+ *   signed:   z, s, xh, h_prev, gamma, h (B, D):
+ *             h = gamma tanh(s) [(1 - sigmoid(z)) if coupled] h_prev + sigmoid(z) xh
+ *   rotation: theta, u, gamma (B, n); z, xh, h_prev, h (B, 2n):
+ *             per block h = gamma R(theta) diag(1, tanh u) h_prev + sigmoid(z) xh
+ *   givens:   theta (B, n, R, k/2); gamma (B, n); z, xh, h_prev, h (B, n*k),
+ *             k in {2, 4, 8, 16, 32, 64}: R brick-wall rounds, gamma, + sigmoid(z) xh
+ *   delta:    q (B, H, dk), k (B, H, nh, dk), v (B, H, nh, dv), beta (B, H, nh),
+ *             gamma (B, H), H_prev, H (B, H, dk, dv), y (B, H, dv):
+ *             H = gamma H_prev; per micro-step H += beta k (v - k^T H)^T; y = H^T q */
+int mgs_mingru_step(const void* k, const void* xh, const void* h_prev, const void* gamma, void* h,
+                    int64_t B, int64_t D, int dtype, void* stream);
+int mgs_signed_step(const void* z, const void* s, const void* xh, const void* h_prev,
+                    const void* gamma, int coupled, void* h, int64_t B, int64_t D, int dtype,
+                    void* stream);
+int mgs_rotation_step(const void* theta, const void* u, const void* z, const void* xh,
+                      const void* h_prev, const void* gamma, void* h, int64_t B, int64_t n,
+                      int dtype, void* stream);
+int mgs_givens_step(const void* theta, const void* z, const void* xh, const void* h_prev,
+                    const void* gamma, void* h, int64_t B, int64_t n, int R, int k, int dtype,
+                    void* stream);
+int mgs_delta_step(const void* q, const void* k, const void* v, const void* beta, const void* gamma,
+                   const void* H_prev, void* y, void* H, int64_t B, int heads, int nh, int dk,
+                   int dv, int dtype, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

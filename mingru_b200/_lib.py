@@ -75,6 +75,12 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
         _int,
         [_p, _p, _p, _p, _p, _p, _p, _p, _p, _p, _p, _p, _i64, _int, _i64, _int, _int, _int, _int,
          _int, _p, _sz, _p]),
+    "mgs_mingru_step": (_int, [_p, _p, _p, _p, _p, _i64, _i64, _int, _p]),
+    "mgs_signed_step": (_int, [_p, _p, _p, _p, _p, _int, _p, _i64, _i64, _int, _p]),
+    "mgs_rotation_step": (_int, [_p, _p, _p, _p, _p, _p, _p, _i64, _i64, _int, _p]),
+    "mgs_givens_step": (_int, [_p, _p, _p, _p, _p, _p, _i64, _i64, _int, _int, _int, _p]),
+    "mgs_delta_step": (
+        _int, [_p, _p, _p, _p, _p, _p, _p, _p, _i64, _int, _int, _int, _int, _int, _p]),
 }
 
 _lock = threading.Lock()

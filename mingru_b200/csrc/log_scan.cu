@@ -572,16 +572,24 @@ __device__ __forceinline__ void col_put(const CUtensorMap* m, const E* src, long
 // sigmoid(-k) = a, d log b / dx~ = 1 / (x~ + 1/2) (x~ >= 0) or 1 - g(x~)
 // (x~ < 0), the branch at x~ = 0 taken as in the reference (x~ >= 0).
 
+// log1p(e^{-|x|}) on the hardware exp2 / log2 approximations: the argument
+// 1 + e^{-|x|} lies in (1, 2], where __logf's absolute error is ~4e-7, and
+// where 1 + e^{-|x|} rounds to 1 the true value is below 6e-8. So each log
+// coefficient carries ~5e-7 absolute error, i.e. ~5e-7 relative on h.
+__device__ __forceinline__ float log1p_exp_neg_abs(float x) {
+  return __logf(1.f + __expf(-fabsf(x)));
+}
+
 // softplus(x) = max(x, 0) + log1p(exp(-|x|)), without overflow.
 __device__ __forceinline__ float softplus_f(float x) {
-  return fmaxf(x, 0.f) + log1pf(expf(-fabsf(x)));
+  return fmaxf(x, 0.f) + log1p_exp_neg_abs(x);
 }
 
 __device__ __forceinline__ void gate_logs(float k, float x, float& lc, float& lv) {
-  const float e = log1pf(expf(-fabsf(k)));
+  const float e = log1p_exp_neg_abs(k);
   lc = -(fmaxf(k, 0.f) + e);                 // log(1 - sigmoid(k))
   const float lz = -(fmaxf(-k, 0.f) + e);    // log sigmoid(k)
-  lv = lz + (x >= 0.f ? logf(x + 0.5f) : -softplus_f(-x));
+  lv = lz + (x >= 0.f ? __logf(x + 0.5f) : -softplus_f(-x));
 }
 
 // (dk, dx~) from (dlc, dlv) given k and x~.
@@ -845,9 +853,9 @@ __device__ __forceinline__ void col_bwd_body(const Args<E>& p, const ColSmem<E, 
         // chain rule through the prologue: sigmoid(k) = 1 - e^{log a} (by expm1,
         // exact for k << 0), sigmoid(-k) = e^{log a}, g(x~) = e^{log b} / sigmoid(k)
         const float lci = cld<E, W>(lc, i), lvi = cld<E, W>(lv, i);
-        const float ea = expf(lci), sk = -expm1f(lci);
+        const float ea = __expf(lci), sk = -expm1f(lci);
         const float dk = fmaf(-sk, dc, ea * dv);
-        const float gx = sk > 0.f ? expf(lvi - logf(sk)) : 1.f;  // sk == 0 only where dv == 0
+        const float gx = sk > 0.f ? __expf(lvi - __logf(sk)) : 1.f;  // sk == 0 only where dv == 0
         const float fx = ((neg >> i) & 1ull) ? 1.f - gx : 1.f / gx;
         cst<E, W>(lc, i, dk);  // dk_t over k_t, dx~_t over x~_t
         cst<E, W>(lv, i, fx * dv);

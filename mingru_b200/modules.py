@@ -37,6 +37,7 @@ import torch
 import torch.nn as nn
 import torch.nn.functional as F
 
+from . import step_ops
 from .scan_ops import (
     angle_scan_impl,
     brickwall_meta,
@@ -199,12 +200,10 @@ class MinGRU(DecayMixin, nn.Module):
             h_prev = (g(self.h0_pre)[:, 0].expand(x_t.size(0), self.hidden_size)
                       if self.h0_pre is not None
                       else x_t.new_full((x_t.size(0), self.hidden_size), 0.5))
-        z = torch.sigmoid(self.linear_z(x_t))
-        a = 1 - z
         dt = self._prepare_decay(delta_t, canonical_ndim=1)
-        if dt is not None:
-            a = self._decay_gamma(dt) * a
-        return a * h_prev + z * g(self.linear_h(x_t))
+        gamma = self._decay_gamma(dt).to(x_t.dtype) if dt is not None else None
+        return step_ops.mingru_step(self.linear_z(x_t), self.linear_h(x_t), h_prev.to(x_t.dtype),
+                                    None if gamma is None else gamma.expand(h_prev.shape))
 
     def extra_repr(self):
         return f"input_size={self.input_size}, hidden_size={self.hidden_size}"
@@ -246,8 +245,10 @@ class SignedMinGRU(DecayMixin, nn.Module):
         if h_prev is None:
             h_prev = (self.h0[:, 0].expand(x_t.size(0), self.hidden_size) if self.h0 is not None
                       else x_t.new_zeros(x_t.size(0), self.hidden_size))
-        a, b = self._coeffs(x_t, self._prepare_decay(delta_t, canonical_ndim=1))
-        return a * h_prev + b
+        dt = self._prepare_decay(delta_t, canonical_ndim=1)
+        gamma = self._decay_gamma(dt).to(x_t.dtype).expand(h_prev.shape) if dt is not None else None
+        return step_ops.signed_step(self.linear_z(x_t), self.linear_s(x_t), self.linear_h(x_t),
+                                    h_prev.to(x_t.dtype), gamma, self.coupled)
 
     def extra_repr(self):
         return f"input_size={self.input_size}, hidden_size={self.hidden_size}, coupled={self.coupled}"
@@ -317,17 +318,11 @@ class RotationMinGRU(DecayMixin, nn.Module):
         B = x_t.size(0)
         if h_prev is None:
             h_prev = self.h0.expand(B, 1, self.hidden_size)[:, 0]
-        v = h_prev.reshape(B, self.n_blocks, 2)
-        theta = self._theta(x_t)
-        c, s = torch.cos(theta), torch.sin(theta)
-        d = torch.tanh(self.linear_u(x_t))
-        v1 = d * v[..., 1]
-        out = torch.stack([c * v[..., 0] - s * v1, s * v[..., 0] + c * v1], dim=-1)
         dt = self._prepare_decay(delta_t, canonical_ndim=1)
-        if dt is not None:
-            out = self._decay_gamma(dt).unsqueeze(-1) * out
-        b = (torch.sigmoid(self.linear_z(x_t)) * self.linear_h(x_t)).reshape(B, self.n_blocks, 2)
-        return (out + b).reshape(B, self.hidden_size)
+        gamma = (self._decay_gamma(dt).to(x_t.dtype).expand(B, self.n_blocks) if dt is not None
+                 else None)
+        return step_ops.rotation_step(self._theta(x_t), self.linear_u(x_t), self.linear_z(x_t),
+                                      self.linear_h(x_t), h_prev.to(x_t.dtype), gamma)
 
     def extra_repr(self):
         return f"input_size={self.input_size}, hidden_size={self.hidden_size}, snap={self.snap}"
@@ -398,20 +393,11 @@ class GivensMinGRU(DecayMixin, nn.Module):
         n, k, R = self.n_blocks, self.k, self.rounds
         if h_prev is None:
             h_prev = self.h0.expand(B, 1, self.hidden_size)[:, 0]
-        v = h_prev.reshape(B, n, k)
-        theta = self.linear_theta(x_t).view(B, n, R, k // 2)
-        for r in range(R):
-            i_idx, j_idx = getattr(self, f"_pi{r}"), getattr(self, f"_pj{r}")
-            c, s = torch.cos(theta[:, :, r]), torch.sin(theta[:, :, r])
-            vi, vj = v[..., i_idx], v[..., j_idx]
-            v = v.clone()
-            v[..., i_idx] = c * vi - s * vj
-            v[..., j_idx] = s * vi + c * vj
         dt = self._prepare_decay(delta_t, canonical_ndim=1)
-        if dt is not None:
-            v = self._decay_gamma(dt).unsqueeze(-1) * v
-        b = (torch.sigmoid(self.linear_z(x_t)) * self.linear_h(x_t)).reshape(B, n, k)
-        return (v + b).reshape(B, self.hidden_size)
+        gamma = self._decay_gamma(dt).to(x_t.dtype).expand(B, n) if dt is not None else None
+        theta = self.linear_theta(x_t).view(B, n, R, k // 2)
+        return step_ops.givens_step(theta, self.linear_z(x_t), self.linear_h(x_t),
+                                    h_prev.to(x_t.dtype), gamma)
 
     def extra_repr(self):
         return (f"input_size={self.input_size}, hidden_size={self.hidden_size}, "
@@ -509,14 +495,12 @@ class DeltaMinGRU(DecayMixin, nn.Module):
             if tuple(h_prev.shape) != expected:
                 raise ValueError(f"h_prev must have shape {expected} (got {tuple(h_prev.shape)})")
             H = h_prev.reshape(B, self.n_heads, self.d_k, self.d_v)
-        if dt is not None:
-            H = self._decay_gamma(dt).unsqueeze(-1).unsqueeze(-1) * H
+        gamma = (self._decay_gamma(dt).to(x_t.dtype).expand(B, self.n_heads) if dt is not None
+                 else None)
         q, ks, vs, betas = self._coeffs(x_t)
-        for k, v, bt in zip(ks, vs, betas):  # H <- H + beta k (v - k^T H)^T
-            kH = torch.einsum("bhk,bhkv->bhv", k, H)
-            H = H + bt[..., None, None] * torch.einsum("bhk,bhv->bhkv", k, v - kH)
-        y = torch.einsum("bhk,bhkv->bhv", q, H).reshape(B, self.n_heads * self.d_v)
-        return self.out_proj(y), H.reshape(*expected)
+        y, H = step_ops.delta_step(q, torch.stack(ks, 2), torch.stack(vs, 2), torch.stack(betas, 2),
+                                   H.to(x_t.dtype), gamma)
+        return self.out_proj(y.reshape(B, self.n_heads * self.d_v)), H.reshape(*expected)
 
     def extra_repr(self):
         return (f"input_size={self.input_size}, hidden_size={self.hidden_size}, "

@@ -285,6 +285,55 @@ def main() -> None:
                             meta=np.array(json.dumps({"cls": cls_name, "kwargs": kwargs})),
                             **{k: _np(v) for k, v in arrays.items()})
 
+    # -------------------------------------------------------------- steps
+    # Each mixer's step() over a few tokens (the streaming path), from a
+    # seeded module; with decay the time gaps are passed per token.
+    step_cases = {
+        "step_mingru": ("MinGRU", dict(input_size=6, hidden_size=16, learnable_h0=True), False),
+        "step_mingru_decay": ("MinGRU", dict(input_size=6, hidden_size=16, decay="learnable"), True),
+        "step_signed": ("SignedMinGRU", dict(input_size=6, hidden_size=16, coupled=True,
+                                             learnable_h0=True), False),
+        "step_signed_decay": ("SignedMinGRU", dict(input_size=6, hidden_size=16,
+                                                   decay="fixed"), True),
+        "step_rotation": ("RotationMinGRU", dict(input_size=6, hidden_size=16, snap=None), False),
+        "step_rotation_decay": ("RotationMinGRU", dict(input_size=6, hidden_size=12,
+                                                       decay="learnable"), True),
+        "step_givens": ("GivensMinGRU", dict(input_size=6, hidden_size=32, block_size=8,
+                                             rounds=3), False),
+        "step_givens_decay": ("GivensMinGRU", dict(input_size=6, hidden_size=16, block_size=4,
+                                                   rounds=2, decay="fixed"), True),
+        "step_delta": ("DeltaMinGRU", dict(input_size=6, hidden_size=16, n_heads=2, nh=2), False),
+        "step_delta_decay": ("DeltaMinGRU", dict(input_size=6, hidden_size=16, n_heads=2,
+                                                 decay="learnable"), True),
+    }
+    for name, (cls_name, kwargs, use_dt) in step_cases.items():
+        if only is not None and name not in only:
+            continue
+        torch.manual_seed(201)
+        mod = getattr(mg, cls_name)(**kwargs).double()
+        B, T = 3, 6
+        g = torch.Generator().manual_seed(202)
+        xs = torch.randn(B, T, kwargs["input_size"], generator=g, dtype=dt)
+        dts = torch.rand(B, T, generator=g, dtype=dt) * 2 if use_dt else None
+        h, ys, hs = None, [], []
+        with torch.no_grad():
+            for t in range(T):
+                r = mod.step(xs[:, t], h, None if dts is None else dts[:, t])
+                if cls_name == "DeltaMinGRU":
+                    y, h = r
+                else:
+                    y = h = r
+                ys.append(y)
+                hs.append(h)
+        arrays = {"x": xs, "y": torch.stack(ys, 1), "h": torch.stack(hs, 1)}
+        if dts is not None:
+            arrays["delta_t"] = dts
+        for k2, v in mod.state_dict().items():
+            arrays["sd." + k2] = v
+        np.savez_compressed(HERE / f"{name}.npz",
+                            meta=np.array(json.dumps({"cls": cls_name, "kwargs": kwargs})),
+                            **{k2: _np(v) for k2, v in arrays.items()})
+
     if only is None or "module_delta_ref_fixture" in only:
         ref_fixture(Path(args.ref).parent / "tests" / "fixtures" / "delta_mingru_decay_none_golden.json")
     print(f"wrote fixtures to {HERE}")

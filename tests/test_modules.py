@@ -67,10 +67,13 @@ def test_validation_errors():
         mb.MinGRU(4, 8, decay="fixed").step(torch.randn(2, 4))
 
 
-def test_step_runs_on_cpu_forward_does_not():
+def test_cpu_tensors_raise_in_forward_and_step():
+    """No CPU path: both the parallel forward and the per-token step run the
+    CUDA kernels only."""
     import mingru_b200 as mb
 
     m = mb.MinGRU(4, 8)
-    assert m.step(torch.randn(2, 4)).shape == (2, 8)
+    with pytest.raises(ValueError, match="CUDA"):
+        m.step(torch.randn(2, 4))
     with pytest.raises(ValueError, match="CUDA"):
         m(torch.randn(2, 5, 4))
