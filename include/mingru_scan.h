@@ -283,6 +283,32 @@ int mgs_delta_bwd(const void* Q, const void* K, const void* V, const void* beta,
                   float* dH0, int64_t B, int H, int64_t T, int nh, int dk, int dv, int chunk,
                   int dtype, void* workspace, size_t workspace_bytes, void* stream);
 
+/* DeltaMinGRU with per-token time decay (decay active). Same layouts as
+ * mgs_delta_*, plus log_gamma (B, H, T) fp32: the per-token log decay
+ * -lambda * dt (<= 0) of each head; the backward also writes dlog_gamma
+ * (B, H, T) fp32. Replaces DeltaMinGRU._forward_chunked_gated
+ * (min_gru.py:3290-3448) and its span sums _span_log_decay
+ * (min_gru.py:3257-3288), which the reference runs eagerly only (its Triton
+ * path declines decay). The incoming state of each token decays by
+ * gamma_t = exp(log_gamma_t) before the token's nh micro-steps; every decay
+ * factor is exp of a chunk-relative span sum of log_gamma (no division, no
+ * difference of running sums). CUDA-core kernels (fp32 arithmetic) for every
+ * dtype; envelope as mgs_delta_* (the shared-memory budget picks the chunk). */
+size_t mgs_delta_gated_saved_size(int64_t B, int H, int64_t T, int nh, int dk, int dv, int chunk,
+                                  int dtype);
+size_t mgs_delta_gated_workspace_size(int64_t B, int H, int64_t T, int nh, int dk, int dv,
+                                      int chunk, int dtype);
+int mgs_delta_gated_fwd(const void* Q, const void* K, const void* V, const void* beta,
+                        const float* H0, const float* log_gamma, void* y, float* H_T, void* saved,
+                        int64_t B, int H, int64_t T, int nh, int dk, int dv, int chunk, int dtype,
+                        void* workspace, size_t workspace_bytes, void* stream);
+int mgs_delta_gated_bwd(const void* Q, const void* K, const void* V, const void* beta,
+                        const float* log_gamma, const void* saved, const void* dy,
+                        const float* dH_T, void* dQ, void* dK, void* dV, void* dbeta, float* dH0,
+                        float* dlog_gamma, int64_t B, int H, int64_t T, int nh, int dk, int dv,
+                        int chunk, int dtype, void* workspace, size_t workspace_bytes,
+                        void* stream);
+
 /* ------------------------------------------------------------------------ */
 /* Streaming step: one token's recurrence update per mixer, one kernel each.
  * Replaces the per-token torch op chains of MinGRU.step (min_gru.py:1399-1448),

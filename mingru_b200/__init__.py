@@ -19,6 +19,7 @@ from .modules import (
     log_g,
 )
 from .scan_ops import (
+    delta_gated_scan_impl,
     delta_scan_impl,
     angle_scan_impl,
     brickwall_meta,
@@ -42,6 +43,7 @@ __all__ = [
     "MinGRUBlock",
     "MinGRUStack",
     "delta_scan_impl",
+    "delta_gated_scan_impl",
     "angle_scan_impl",
     "brickwall_meta",
     "linear_scan",

@@ -75,6 +75,16 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
         _int,
         [_p, _p, _p, _p, _p, _p, _p, _p, _p, _p, _p, _p, _i64, _int, _i64, _int, _int, _int, _int,
          _int, _p, _sz, _p]),
+    "mgs_delta_gated_saved_size": (_sz, [_i64, _int, _i64, _int, _int, _int, _int, _int]),
+    "mgs_delta_gated_workspace_size": (_sz, [_i64, _int, _i64, _int, _int, _int, _int, _int]),
+    "mgs_delta_gated_fwd": (
+        _int,
+        [_p, _p, _p, _p, _p, _p, _p, _p, _p, _i64, _int, _i64, _int, _int, _int, _int, _int, _p,
+         _sz, _p]),
+    "mgs_delta_gated_bwd": (
+        _int,
+        [_p, _p, _p, _p, _p, _p, _p, _p, _p, _p, _p, _p, _p, _p, _i64, _int, _i64, _int, _int,
+         _int, _int, _int, _p, _sz, _p]),
     "mgs_mingru_step": (_int, [_p, _p, _p, _p, _p, _i64, _i64, _int, _p]),
     "mgs_signed_step": (_int, [_p, _p, _p, _p, _p, _int, _p, _i64, _i64, _int, _p]),
     "mgs_rotation_step": (_int, [_p, _p, _p, _p, _p, _p, _p, _i64, _i64, _int, _p]),

@@ -146,64 +146,112 @@ __device__ void load_chunk(const Args<E>& p, const Chunk& ck, float* sK, float* 
   __syncthreads();
 }
 
-// L = strict_lower(K K^T) * beta[col]; also keeps KK (unmasked) when wanted.
-__device__ void build_L(int M, int dk, const float* sK, const float* sb, float* sL, float* sKK) {
-  float* dst = sKK ? sKK : sL;
-  bgemm<false, true>(M, M, dk, sK, dk, sK, dk, dst, M, false);
-  for (int i = threadIdx.x; i < M * M; i += blockDim.x) {
-    const int r = i / M, c = i - r * M;
-    sL[i] = c < r ? dst[i] * sb[c] : 0.f;
+// Per-token time decay (DeltaMinGRU._forward_chunked_gated, min_gru.py:
+// 3290-3448; span sums _span_log_decay, min_gru.py:3257-3288). With l_s the
+// chunk's per-token log-decay, every decay factor is exp of a span sum
+// span[t][t'] = sum_{s=t'+1}^{t} l_s (t >= t'), each accumulated from its own
+// span's terms (never a difference of running sums, so one huge saturated
+// term zeroes exactly the spans that contain it), and lam[t] = sum_{s<=t} l_s
+// (P_t = exp(lam[t])). Sums run from s = t down, as the reference's flipped
+// cumulative sum does.
+__device__ void build_spans(const float* lg, int Ct, float* sSpan, float* sLam) {
+  for (int i = threadIdx.x; i < Ct * Ct; i += blockDim.x) {
+    const int t = i / Ct, u = i - t * Ct;
+    if (u <= t) {
+      float s = 0.f;
+      for (int w = t; w > u; --w) s += lg[w];
+      sSpan[i] = s;
+    }
+  }
+  for (int t = threadIdx.x; t < Ct; t += blockDim.x) {
+    float s = 0.f;
+    for (int w = t; w >= 0; --w) s += lg[w];
+    sLam[t] = s;
   }
   __syncthreads();
 }
 
-// P = (Q K^T) * beta[col] * read_mask  (Ct x M); keeps Sm = Q K^T when wanted.
+// Decay factor between micro-steps i >= l (tokens i / nh >= l / nh).
+__device__ __forceinline__ float span_factor(const float* sSpan, int Ct, int nh, int ti, int l) {
+  return expf(sSpan[ti * Ct + l / nh]);
+}
+
+// L = strict_lower(K K^T) * beta[col] [* exp(span[tau(row)][tau(col)])]; also
+// keeps KK (unmasked) when wanted.
+__device__ void build_L(int M, int dk, const float* sK, const float* sb, float* sL, float* sKK,
+                        const float* sSpan = nullptr, int Ct = 0, int nh = 1) {
+  float* dst = sKK ? sKK : sL;
+  bgemm<false, true>(M, M, dk, sK, dk, sK, dk, dst, M, false);
+  for (int i = threadIdx.x; i < M * M; i += blockDim.x) {
+    const int r = i / M, c = i - r * M;
+    float v = c < r ? dst[i] * sb[c] : 0.f;
+    if (sSpan && c < r) v *= span_factor(sSpan, Ct, nh, r / nh, c);
+    sL[i] = v;
+  }
+  __syncthreads();
+}
+
+// P = (Q K^T) * beta[col] * read_mask [* exp(span[t][tau(col)])]  (Ct x M);
+// keeps Sm = Q K^T when wanted.
 __device__ void build_P(int Ct, int M, int nh, int dk, const float* sQ, const float* sK,
-                        const float* sb, float* sP, float* sSm) {
+                        const float* sb, float* sP, float* sSm, const float* sSpan = nullptr) {
   float* dst = sSm ? sSm : sP;
   bgemm<false, true>(Ct, M, dk, sQ, dk, sK, dk, dst, M, false);
   for (int i = threadIdx.x; i < Ct * M; i += blockDim.x) {
     const int t = i / M, m = i - t * M;
-    sP[i] = (m / nh) <= t ? dst[i] * sb[m] : 0.f;
+    float v = (m / nh) <= t ? dst[i] * sb[m] : 0.f;
+    if (sSpan && (m / nh) <= t) v *= span_factor(sSpan, Ct, nh, t, m);
+    sP[i] = v;
   }
   __syncthreads();
 }
 
 // ------------------------------------------------------------ forward (1) --
 // A_c = I - K^T diag(beta) W, B_c = K^T diag(beta) Ut with [W | Ut] = T^{-1} [K | V].
+// With decay (P_t, c_m = exp(span[C-1][tau(m)]), P^ = P per micro-step):
+// A_c = P_{C-1} I - K^T diag(c beta) T^{-1} diag(P^) K, B_c = K^T diag(c beta) T^{-1} V.
 template <typename E>
 __global__ void __launch_bounds__(kThreads) fwd_prepass_kernel(Args<E> p) {
   extern __shared__ __align__(16) float sm[];
   const Chunk ck = chunk_of(p.T_, p.C, p.nh, blockIdx.x, blockIdx.y);
-  const int M = ck.M, dk = p.dk, dv = p.dv, W = dk + dv, Mx = p.nh * p.C;
+  const int M = ck.M, dk = p.dk, dv = p.dv, W = dk + dv, Mx = p.nh * p.C, nh = p.nh;
   float* sK = sm;              // M x dk
   float* sb = sK + Mx * dk;    // M
   float* sL = sb + Mx;         // M x M
   float* sX = sL + Mx * Mx;    // M x (dk + dv): [W | Ut]
   float* sA = sX + Mx * W;     // dk x dk
   float* sB = sA + dk * dk;    // dk x dv
+  float* sSpan = sB + dk * dv;         // decay only: C x C
+  float* sLam = sSpan + p.C * p.C;     // decay only: C
+  const bool dec = p.lg != nullptr;
   load_chunk<E>(p, ck, sK, nullptr, sb, nullptr);
+  if (dec) build_spans(p.lg + ck.bh * p.T_ + ck.t0, ck.Ct, sSpan, sLam);
   {
     const size_t tok0 = (size_t)ck.bh * p.T_ + ck.t0;
     const E* V = p.V + tok0 * p.nh * dv;
     for (int i = threadIdx.x; i < M * W; i += blockDim.x) {
       const int r = i / W, c = i - r * W;
-      sX[i] = c < dk ? sK[r * dk + c] : to_f32<E>(V[r * dv + c - dk]);
+      sX[i] = c < dk ? (dec ? expf(sLam[r / nh]) : 1.f) * sK[r * dk + c]
+                     : to_f32<E>(V[r * dv + c - dk]);
     }
   }
-  build_L(M, dk, sK, sb, sL, nullptr);
+  build_L(M, dk, sK, sb, sL, nullptr, dec ? sSpan : nullptr, ck.Ct, nh);
   solve_lower_unit(M, W, sL, M, sX, W);
-  // scale rows of [W | Ut] by beta
-  for (int i = threadIdx.x; i < M * W; i += blockDim.x) sX[i] *= sb[i / W];
+  // scale rows of [W | Ut] by beta (times the carry factor c with decay)
+  for (int i = threadIdx.x; i < M * W; i += blockDim.x) {
+    const int r = i / W;
+    sX[i] *= dec ? sb[r] * span_factor(sSpan, ck.Ct, nh, ck.Ct - 1, r) : sb[r];
+  }
   __syncthreads();
-  // A = I - K^T (beta W), B = K^T (beta Ut)
+  // A = P I - K^T (beta W), B = K^T (beta Ut)
   bgemm<true, false>(dk, dk, M, sK, dk, sX, W, sA, dk, false, -1.f);
   bgemm<true, false>(dk, dv, M, sK, dk, sX + dk, W, sB, dv, false);
   const size_t o = ((size_t)ck.bh * p.nchunks + ck.c);
   float* Ag = p.Ac + o * dk * dk;
   float* Bg = p.Bc + o * dk * dv;
+  const float pc = dec ? expf(sLam[ck.Ct - 1]) : 1.f;
   for (int i = threadIdx.x; i < dk * dk; i += blockDim.x)
-    Ag[i] = sA[i] + ((i / dk) == (i % dk) ? 1.f : 0.f);
+    Ag[i] = sA[i] + ((i / dk) == (i % dk) ? pc : 0.f);
   for (int i = threadIdx.x; i < dk * dv; i += blockDim.x) Bg[i] = sB[i];
 }
 
@@ -249,15 +297,27 @@ __global__ void __launch_bounds__(kThreads) fwd_readout_kernel(Args<E> p) {
   float* sL = sS + dk * dv;    // M x M
   float* sP = sL + Mx * Mx;    // Ct x M
   float* sY = sP + Cx * Mx;    // Ct x dv
+  float* sSpan = sY + Cx * dv;     // decay only: C x C
+  float* sLam = sSpan + Cx * Cx;   // decay only: C
+  float* sKp = sLam + Cx;          // decay only: M x dk, diag(P^) K
+  const bool dec = p.lg != nullptr;
   load_chunk<E>(p, ck, sK, sV, sb, sQ);
   const size_t o = (size_t)ck.bh * p.nchunks + ck.c;
   for (int i = threadIdx.x; i < dk * dv; i += blockDim.x) sS[i] = p.Hb[o * dk * dv + i];
+  if (dec) {
+    build_spans(p.lg + ck.bh * p.T_ + ck.t0, Ct, sSpan, sLam);  // ends with a barrier
+    for (int i = threadIdx.x; i < M * dk; i += blockDim.x) sKp[i] = expf(sLam[(i / dk) / nh]) * sK[i];
+  }
   __syncthreads();
-  build_L(M, dk, sK, sb, sL, nullptr);
-  bgemm<false, false>(M, dv, dk, sK, dk, sS, dv, sV, dv, true, -1.f);  // V - K S
+  build_L(M, dk, sK, sb, sL, nullptr, dec ? sSpan : nullptr, Ct, nh);
+  bgemm<false, false>(M, dv, dk, dec ? sKp : sK, dk, sS, dv, sV, dv, true, -1.f);  // V - P^ K S
   solve_lower_unit(M, dv, sL, M, sV, dv);                              // U
-  build_P(Ct, M, nh, dk, sQ, sK, sb, sP, nullptr);
+  build_P(Ct, M, nh, dk, sQ, sK, sb, sP, nullptr, dec ? sSpan : nullptr);
   bgemm<false, false>(Ct, dv, dk, sQ, dk, sS, dv, sY, dv, false);      // Q S
+  if (dec) {  // P_t Q S
+    for (int i = threadIdx.x; i < Ct * dv; i += blockDim.x) sY[i] *= expf(sLam[i / dv]);
+    __syncthreads();
+  }
   bgemm<false, false>(Ct, dv, M, sP, M, sV, dv, sY, dv, true);         // + P U
   E* y = p.y + ((size_t)ck.bh * p.T_ + ck.t0) * dv;
   for (int i = threadIdx.x; i < Ct * dv; i += blockDim.x) y[i] = from_f32<E>(sY[i]);
@@ -279,16 +339,25 @@ __global__ void __launch_bounds__(kThreads) bwd_e_kernel(Args<E> p) {
   float* sP = sL + Mx * Mx;    // Ct x M
   float* sZ = sP + Cx * Mx;    // M x dv
   float* sE = sZ + Mx * dv;    // dk x dv
+  float* sSpan = sE + dk * dv;     // decay only: C x C
+  float* sLam = sSpan + Cx * Cx;   // decay only: C
+  const bool dec = p.lg != nullptr;
   load_chunk<E>(p, ck, sK, nullptr, sb, sQ);
   {
     const E* dy = p.dy + ((size_t)ck.bh * p.T_ + ck.t0) * dv;
     for (int i = threadIdx.x; i < Ct * dv; i += blockDim.x) sdy[i] = to_f32<E>(dy[i]);
   }
+  if (dec) build_spans(p.lg + ck.bh * p.T_ + ck.t0, Ct, sSpan, sLam);
   __syncthreads();
-  build_L(M, dk, sK, sb, sL, nullptr);
-  build_P(Ct, M, nh, dk, sQ, sK, sb, sP, nullptr);
+  build_L(M, dk, sK, sb, sL, nullptr, dec ? sSpan : nullptr, Ct, nh);
+  build_P(Ct, M, nh, dk, sQ, sK, sb, sP, nullptr, dec ? sSpan : nullptr);
   bgemm<true, false>(M, dv, Ct, sP, M, sdy, dv, sZ, dv, false);   // P^T dy
   solve_lower_unit_t(M, dv, sL, M, sZ, dv);                       // T^{-T} P^T dy
+  if (dec) {  // diag(P^) T^{-T} P^T dy and diag(P) dy
+    for (int i = threadIdx.x; i < M * dv; i += blockDim.x) sZ[i] *= expf(sLam[(i / dv) / nh]);
+    for (int i = threadIdx.x; i < Ct * dv; i += blockDim.x) sdy[i] *= expf(sLam[i / dv]);
+    __syncthreads();
+  }
   bgemm<true, false>(dk, dv, Ct, sQ, dk, sdy, dv, sE, dv, false);  // Q^T dy
   bgemm<true, false>(dk, dv, M, sK, dk, sZ, dv, sE, dv, true, -1.f);
   float* Eg = p.Ec + ((size_t)ck.bh * p.nchunks + ck.c) * dk * dv;
@@ -323,7 +392,14 @@ __global__ void __launch_bounds__(kThreads) adj_pass_kernel(const float* Ac, con
 }
 
 // ----------------------------------------------------------- backward (3) --
-// Per-chunk adjoint (the reference's _delta_backward_torch body, restated).
+// Per-chunk adjoint (the reference's _delta_backward_torch body, restated),
+// with decay extended by the factors' own gradients: every factor is exp of a
+// difference of chunk prefix sums lam[t] = sum_{s<=t} l_s, so its gradient is
+// gathered per token as dlam[t] (+ for the later token of a span, - for the
+// earlier one) and d l_s = sum_{t >= s} dlam[t]:
+//   y_t = P_t q_t S + sum_l R~[t,l] u_l   R~ = (Q K^T) beta[col] D, D = exp(span[t][tau(l)])
+//   rhs = V - diag(P^) K S,  T = I + strict(K K^T) beta[col] E,  E = exp(span[tau(i)][tau(l)])
+//   S' = P_{C-1} S + K^T diag(c beta) U,  c = exp(span[C-1][tau(l)])
 template <typename E>
 __global__ void __launch_bounds__(kThreads) bwd_grads_kernel(Args<E> p) {
   extern __shared__ __align__(16) float sm[];
@@ -345,7 +421,17 @@ __global__ void __launch_bounds__(kThreads) bwd_grads_kernel(Args<E> p) {
   float* sdK = sdU + Mx * dv;  // M x dk
   float* sdQ = sdK + Mx * dk;  // Ct x dk
   float* sdb = sdQ + Cx * dk;  // M
+  // decay only:
+  float* sSpan = sdb + Mx;         // C x C
+  float* sLam = sSpan + Cx * Cx;   // C
+  float* sdL = sLam + Cx;          // C   d lam
+  float* sKS = sdL + Cx;           // M x dv  (K S, later diag(P^) G)
+  float* sQS = sKS + Mx * dv;      // C x dv  (Q S)
+  float* sc = sQS + Cx * dv;       // M   carry factors c
+  float* sw = sc + Mx;             // M   dc_m c_m
+  float* sKK = sw + Mx;            // M x M  K K^T
   float* sdbU = sdy;
+  const bool dec = p.lg != nullptr;
   load_chunk<E>(p, ck, sK, sU, sb, sQ);
   {
     const size_t o = (size_t)ck.bh * p.nchunks + ck.c;
@@ -356,66 +442,148 @@ __global__ void __launch_bounds__(kThreads) bwd_grads_kernel(Args<E> p) {
     const E* dy = p.dy + ((size_t)ck.bh * p.T_ + ck.t0) * dv;
     for (int i = threadIdx.x; i < Ct * dv; i += blockDim.x) sdy[i] = to_f32<E>(dy[i]);
   }
+  if (dec) {
+    build_spans(p.lg + ck.bh * p.T_ + ck.t0, Ct, sSpan, sLam);
+    for (int t = threadIdx.x; t < Ct; t += blockDim.x) sdL[t] = 0.f;
+    for (int m = threadIdx.x; m < M; m += blockDim.x)
+      sc[m] = span_factor(sSpan, Ct, nh, Ct - 1, m);
+  }
   __syncthreads();
-  build_L(M, dk, sK, sb, sL, nullptr);
-  bgemm<false, false>(M, dv, dk, sK, dk, sS, dv, sU, dv, true, -1.f);  // V - K S
+  build_L(M, dk, sK, sb, sL, dec ? sKK : nullptr, dec ? sSpan : nullptr, Ct, nh);
+  if (dec) {  // U = T^{-1} (V - diag(P^) K S)
+    bgemm<false, false>(M, dv, dk, sK, dk, sS, dv, sKS, dv, false);
+    for (int i = threadIdx.x; i < M * dv; i += blockDim.x) sU[i] -= expf(sLam[(i / dv) / nh]) * sKS[i];
+    __syncthreads();
+  } else {
+    bgemm<false, false>(M, dv, dk, sK, dk, sS, dv, sU, dv, true, -1.f);  // V - K S
+  }
   solve_lower_unit(M, dv, sL, M, sU, dv);                              // U
-  build_P(Ct, M, nh, dk, sQ, sK, sb, sP, sSm);
+  build_P(Ct, M, nh, dk, sQ, sK, sb, sP, sSm, dec ? sSpan : nullptr);
   bgemm<false, true>(Ct, dk, dv, sdy, dv, sS, dv, sdQ, dk, false);     // dQ = dy S^T
+  if (dec) {
+    // dP_t = q_t^T S dy_t -> dlam[t] += dP_t P_t;  dQ = diag(P) dy S^T
+    bgemm<false, false>(Ct, dv, dk, sQ, dk, sS, dv, sQS, dv, false);
+    for (int t = threadIdx.x; t < Ct; t += blockDim.x) {
+      float d = 0.f;
+      for (int v = 0; v < dv; ++v) d = fmaf(sQS[t * dv + v], sdy[t * dv + v], d);
+      sdL[t] += d * expf(sLam[t]);
+    }
+    for (int i = threadIdx.x; i < Ct * dk; i += blockDim.x) sdQ[i] *= expf(sLam[i / dk]);
+    __syncthreads();
+  }
   bgemm<false, true>(Ct, M, dv, sdy, dv, sU, dv, sdP, M, false);       // dP = dy U^T
   bgemm<true, false>(M, dv, Ct, sP, M, sdy, dv, sdU, dv, false);       // dU = P^T dy
   bgemm<false, false>(M, dv, dk, sK, dk, sdS, dv, sdbU, dv, false);    // dbU = K dSo
   for (int i = threadIdx.x; i < M * dk; i += blockDim.x) sdK[i] = 0.f;
   __syncthreads();
-  // dK = (beta U) dSo^T
-  for (int i = threadIdx.x; i < M * dv; i += blockDim.x) sdU[i] += sb[i / dv] * sdbU[i];
+  // dU += (c) beta dbU
+  for (int i = threadIdx.x; i < M * dv; i += blockDim.x)
+    sdU[i] += sb[i / dv] * (dec ? sc[i / dv] : 1.f) * sdbU[i];
   __syncthreads();
   {
-    // beta-scaled U into sdbU's slot would clobber dbU; compute dK directly.
+    // dK = ((c) beta U) dSo^T; dbeta = (c) rowsum(U * dbU); with decay dc c -> sw
     for (int i = threadIdx.x; i < M * dk; i += blockDim.x) {
       const int m = i / dk, k = i - m * dk;
       float s = 0.f;
       for (int v = 0; v < dv; ++v) s = fmaf(sU[m * dv + v], sdS[k * dv + v], s);
-      sdK[i] = sb[m] * s;
+      sdK[i] = sb[m] * (dec ? sc[m] : 1.f) * s;
     }
     for (int m = threadIdx.x; m < M; m += blockDim.x) {
       float s = 0.f;
       for (int v = 0; v < dv; ++v) s = fmaf(sU[m * dv + v], sdbU[m * dv + v], s);
-      sdb[m] = s;
+      sdb[m] = (dec ? sc[m] : 1.f) * s;
+      if (dec) sw[m] = sb[m] * s * sc[m];
     }
     __syncthreads();
   }
-  // dSm = dP * beta[col] * read (into sP); dbeta += sum_t dP * Sm * read
+  // dSm = dP * beta[col] * read (* D) (into sP); dbeta += sum_t dP * Sm * read (* D)
   for (int m = threadIdx.x; m < M; m += blockDim.x) {
     float s = 0.f;
-    for (int t = m / nh; t < Ct; ++t) s = fmaf(sdP[t * M + m], sSm[t * M + m], s);
+    for (int t = m / nh; t < Ct; ++t) {
+      const float f = dec ? span_factor(sSpan, Ct, nh, t, m) : 1.f;
+      s = fmaf(sdP[t * M + m] * f, sSm[t * M + m], s);
+    }
     sdb[m] += s;
+  }
+  if (dec) {
+    // D pairs: a[t,l] = dP Sm beta D; dlam[t] += sum_l a[t,l], dlam[tau(l)] -= sum_t a[t,l]
+    for (int u = threadIdx.x; u < Ct; u += blockDim.x) {
+      float plus = 0.f, minus = 0.f;
+      for (int l = 0; l < M && l / nh <= u; ++l)
+        plus += sdP[u * M + l] * sSm[u * M + l] * sb[l] * span_factor(sSpan, Ct, nh, u, l);
+      for (int l = u * nh; l < (u + 1) * nh; ++l)
+        for (int t = u; t < Ct; ++t)
+          minus += sdP[t * M + l] * sSm[t * M + l] * sb[l] * span_factor(sSpan, Ct, nh, t, l);
+      sdL[u] += plus - minus;
+    }
   }
   __syncthreads();
   for (int i = threadIdx.x; i < Ct * M; i += blockDim.x) {
     const int t = i / M, m = i - t * M;
-    sP[i] = (m / nh) <= t ? sdP[i] * sb[m] : 0.f;
+    sP[i] = (m / nh) <= t ? sdP[i] * sb[m] * (dec ? span_factor(sSpan, Ct, nh, t, m) : 1.f) : 0.f;
   }
   __syncthreads();
   bgemm<false, false>(Ct, dk, M, sP, M, sK, dk, sdQ, dk, true);   // dQ += dSm K
   bgemm<true, false>(M, dk, Ct, sP, M, sQ, dk, sdK, dk, true);    // dK += dSm^T Q
   solve_lower_unit_t(M, dv, sL, M, sdU, dv);                      // G = T^{-T} dU
   bgemm<false, true>(M, M, dv, sdU, dv, sU, dv, sdP, M, false, -1.f);  // dT = -G U^T
-  bgemm<false, true>(M, dk, dv, sdU, dv, sS, dv, sdK, dk, true, -1.f); // dK -= G S^T
-  // dKK = dT * beta[col] * strict; dbeta += sum_i dT * KK * strict (KK[i][l] = k_i . k_l)
+  if (dec) {
+    // dP^_m = -(K S)_m . G_m -> dlam[tau(m)] += dP^_m P^_m; then K S <- diag(P^) G
+    for (int u = threadIdx.x; u < Ct; u += blockDim.x) {
+      float d = 0.f;
+      for (int m = u * nh; m < (u + 1) * nh; ++m)
+        for (int v = 0; v < dv; ++v) d -= sKS[m * dv + v] * sdU[m * dv + v];
+      sdL[u] += d * expf(sLam[u]);
+    }
+    __syncthreads();
+    for (int i = threadIdx.x; i < M * dv; i += blockDim.x) sKS[i] = expf(sLam[(i / dv) / nh]) * sdU[i];
+    __syncthreads();
+    bgemm<false, true>(M, dk, dv, sKS, dv, sS, dv, sdK, dk, true, -1.f);  // dK -= diag(P^) G S^T
+  } else {
+    bgemm<false, true>(M, dk, dv, sdU, dv, sS, dv, sdK, dk, true, -1.f);  // dK -= G S^T
+  }
+  // dKK = dT * beta[col] * strict (* E); dbeta += sum_i dT * KK * strict (* E)
   for (int l = threadIdx.x; l < M; l += blockDim.x) {
     float s = 0.f;
     for (int i = l + 1; i < M; ++i) {
-      float kk = 0.f;
-      for (int q = 0; q < dk; ++q) kk = fmaf(sK[i * dk + q], sK[l * dk + q], kk);
+      float kk;
+      if (dec) {
+        kk = sKK[i * M + l] * span_factor(sSpan, Ct, nh, i / nh, l);
+      } else {
+        kk = 0.f;
+        for (int q = 0; q < dk; ++q) kk = fmaf(sK[i * dk + q], sK[l * dk + q], kk);
+      }
       s = fmaf(sdP[i * M + l], kk, s);
     }
     sdb[l] += s;
   }
+  if (dec) {
+    // E pairs: e[i,l] = dT KK beta E (i > l): dlam[tau(i)] += e, dlam[tau(l)] -= e;
+    // carry factors: dlam[C-1] += sum_m dc_m c_m, dlam[tau(m)] -= dc_m c_m;
+    // S' = P_{C-1} S: dlam[C-1] += <S, dSo> P_{C-1}
+    for (int u = threadIdx.x; u < Ct; u += blockDim.x) {
+      float plus = 0.f, minus = 0.f;
+      for (int i = u * nh; i < (u + 1) * nh; ++i)
+        for (int l = 0; l < i; ++l)
+          plus += sdP[i * M + l] * sKK[i * M + l] * sb[l] * span_factor(sSpan, Ct, nh, u, l);
+      for (int l = u * nh; l < (u + 1) * nh; ++l) {
+        for (int i = l + 1; i < M; ++i)
+          minus += sdP[i * M + l] * sKK[i * M + l] * sb[l] * span_factor(sSpan, Ct, nh, i / nh, l);
+        minus += sw[l];
+      }
+      if (u == Ct - 1) {
+        for (int m = 0; m < M; ++m) plus += sw[m];
+        float sd = 0.f;
+        for (int i = 0; i < dk * dv; ++i) sd = fmaf(sS[i], sdS[i], sd);
+        plus += sd * expf(sLam[u]);
+      }
+      sdL[u] += plus - minus;
+    }
+  }
   __syncthreads();
   for (int i = threadIdx.x; i < M * M; i += blockDim.x) {
     const int r = i / M, c = i - r * M;
-    sdP[i] = c < r ? sdP[i] * sb[c] : 0.f;
+    sdP[i] = c < r ? sdP[i] * sb[c] * (dec ? span_factor(sSpan, Ct, nh, r / nh, c) : 1.f) : 0.f;
   }
   __syncthreads();
   bgemm<false, false>(M, dk, M, sdP, M, sK, dk, sdK, dk, true);   // dK += dKK K
@@ -429,6 +597,13 @@ __global__ void __launch_bounds__(kThreads) bwd_grads_kernel(Args<E> p) {
   for (int i = threadIdx.x; i < M * dk; i += blockDim.x) dK[i] = from_f32<E>(sdK[i]);
   for (int i = threadIdx.x; i < M * dv; i += blockDim.x) dV[i] = from_f32<E>(sdU[i]);
   for (int i = threadIdx.x; i < M; i += blockDim.x) db[i] = from_f32<E>(sdb[i]);
+  if (dec && threadIdx.x == 0) {  // d l_s = sum_{t >= s} dlam[t]
+    float acc = 0.f;
+    for (int t = Ct - 1; t >= 0; --t) {
+      acc += sdL[t];
+      p.dlg[tok0 + t] = acc;
+    }
+  }
 }
 
 // ---------------------------------------------------------------- launch --
@@ -444,15 +619,18 @@ struct SmemPlan {
   }
 };
 
-inline SmemPlan smem_plan(int nh, int C, int dk, int dv) {
+inline SmemPlan smem_plan(int nh, int C, int dk, int dv, bool decay = false) {
   const size_t M = (size_t)nh * C, c = (size_t)C, k = (size_t)dk, v = (size_t)dv;
+  const size_t spans = decay ? c * c + c : 0;  // span table and prefix sums
   SmemPlan s;
-  s.prepass = (M * k + M + M * M + M * (k + v) + k * k + k * v) * 4;
-  s.readout = (M * k + M * v + M + c * k + k * v + M * M + c * M + c * v) * 4;
+  s.prepass = (M * k + M + M * M + M * (k + v) + k * k + k * v + spans) * 4;
+  s.readout = (M * k + M * v + M + c * k + k * v + M * M + c * M + c * v + spans +
+               (decay ? M * k : 0)) * 4;
   s.state = (2 * k * v + k * k) * 4;
-  s.bwd_e = (M * k + M + c * k + c * v + M * M + c * M + M * v + k * v) * 4;
+  s.bwd_e = (M * k + M + c * k + c * v + M * M + c * M + M * v + k * v + spans) * 4;
   s.bwd_grads = (M * k + M * v + M + c * k + 2 * k * v + M * v + M * M + 2 * c * M + M * M +
-                 M * v + M * k + c * k + M) * 4;
+                 M * v + M * k + c * k + M +
+                 (decay ? spans + c + M * v + c * v + 2 * M + M * M : 0)) * 4;
   return s;
 }
 
@@ -464,11 +642,11 @@ constexpr int kMaxDvBlock = 64;  // value columns per call (wider d_v is split b
 // shortened (to whole tokens) until every kernel's tiles fit in shared
 // memory. The chunked form is exact for any chunk length, so this changes
 // only the rounding, not the result. 0 if even one-token chunks do not fit.
-inline int ffma_chunk(int nh, int dk, int dv, int C, long long T) {
+inline int ffma_chunk(int nh, int dk, int dv, int C, long long T, bool decay = false) {
   long long c = C;
   if (T >= 1 && c > T) c = T;
   for (; c >= 1; --c)
-    if (smem_plan(nh, (int)c, dk, dv).max() <= kSmemLimit) return (int)c;
+    if (smem_plan(nh, (int)c, dk, dv, decay).max() <= kSmemLimit) return (int)c;
   return 0;
 }
 
@@ -485,13 +663,14 @@ struct Geometry {
   size_t ac, hb;  // floats per (b, h) of A_c and of Hbound / B_c / E_c / dSo
 };
 
+// decay: per-token time decay (only the CUDA-core kernels implement it).
 inline bool geometry(long long B, int H, long long T, int nh, int dk, int dv, int C, int dtype,
-                     Geometry* g) {
+                     Geometry* g, bool decay = false) {
   if (B < 0 || H < 0 || T < 0 || nh < 1 || C < 1 || dk < 1 || dv < 1) return false;
   if (dk > kMaxDk || dv > kMaxDvBlock) return false;
   const int ct = nh <= kMaxM ? tc_chunk(nh, C) : 0;
-  g->tc = ct >= 1 && tc_eligible(dtype, nh, dk, dv, ct);
-  g->C = g->tc ? ct : ffma_chunk(nh, dk, dv, C, T);
+  g->tc = !decay && ct >= 1 && tc_eligible(dtype, nh, dk, dv, ct);
+  g->C = g->tc ? ct : ffma_chunk(nh, dk, dv, C, T, decay);
   if (g->C < 1) return false;
   g->nchunks = (int)((T + g->C - 1) / g->C);
   g->ac = (size_t)g->nchunks * dk * dk;
@@ -511,13 +690,15 @@ int run(bool fwd, Args<E> p, long long B, int H, long long T, int nh, int dk, in
         float* saved, void* ws, size_t ws_bytes, cudaStream_t st) {
   constexpr int dtype = std::is_same_v<E, float> ? MGS_F32
                         : std::is_same_v<E, __nv_bfloat16> ? MGS_BF16 : MGS_F16;
+  const bool decay = p.lg != nullptr;
+  if (decay && !fwd && p.dlg == nullptr) return MGS_BAD_SHAPE;
   Geometry g;
-  if (!geometry(B, H, T, nh, dk, dv, C, dtype, &g)) return MGS_UNSUPPORTED;
+  if (!geometry(B, H, T, nh, dk, dv, C, dtype, &g, decay)) return MGS_UNSUPPORTED;
   if constexpr (std::is_same_v<E, __nv_bfloat16>) {
     if (g.tc) return run_tc(fwd, p, B, H, T, nh, dk, dv, g.C, saved, ws, ws_bytes, st);
   }
   C = g.C;
-  const SmemPlan sp = smem_plan(nh, C, dk, dv);
+  const SmemPlan sp = smem_plan(nh, C, dk, dv, decay);
   const long long BH = B * (long long)H;
   p.T_ = T;
   p.H = H;
@@ -581,27 +762,28 @@ int run(bool fwd, Args<E> p, long long B, int H, long long T, int nh, int dk, in
 
 extern "C" {
 
-size_t mgs_delta_saved_size(int64_t B, int H, int64_t T, int nh, int dk, int dv, int chunk,
-                            int dtype) {
+namespace {
+size_t delta_saved_size(int64_t B, int H, int64_t T, int nh, int dk, int dv, int chunk, int dtype,
+                        bool decay) {
   mgs::delta::Geometry g;
-  if (!mgs::delta::geometry(B, H, T, nh, dk, dv, chunk, dtype, &g)) return 0;
+  if (!mgs::delta::geometry(B, H, T, nh, dk, dv, chunk, dtype, &g, decay)) return 0;
   if (g.tc) return mgs::delta::tc_saved_floats(B * (int64_t)H, T, dk, dv, g.C) * sizeof(float);
   return (size_t)B * H * (g.ac + g.hb) * sizeof(float);
 }
 
-size_t mgs_delta_workspace_size(int64_t B, int H, int64_t T, int nh, int dk, int dv, int chunk,
-                                int dtype) {
+size_t delta_workspace_size(int64_t B, int H, int64_t T, int nh, int dk, int dv, int chunk,
+                            int dtype, bool decay) {
   mgs::delta::Geometry g;
-  if (!mgs::delta::geometry(B, H, T, nh, dk, dv, chunk, dtype, &g)) return 0;
+  if (!mgs::delta::geometry(B, H, T, nh, dk, dv, chunk, dtype, &g, decay)) return 0;
   size_t n = (size_t)B * H * 2 * g.hb * sizeof(float);
   if (g.tc) n = mgs::delta::tc_workspace_floats(B * (int64_t)H, T, dk, dv, g.C) * sizeof(float);
   return n < 256 ? 256 : n;
 }
 
-int mgs_delta_fwd(const void* Q, const void* K, const void* V, const void* beta, const float* H0,
-                  void* y, float* H_T, void* saved, int64_t B, int H, int64_t T, int nh, int dk,
-                  int dv, int chunk, int dtype, void* workspace, size_t workspace_bytes,
-                  void* stream) {
+int delta_fwd(const void* Q, const void* K, const void* V, const void* beta, const float* H0,
+              const float* log_gamma, void* y, float* H_T, void* saved, int64_t B, int H,
+              int64_t T, int nh, int dk, int dv, int chunk, int dtype, void* workspace,
+              size_t workspace_bytes, void* stream) {
   auto st = static_cast<cudaStream_t>(stream);
 #define MGS_DELTA_FWD(E)                                                                        \
   {                                                                                             \
@@ -613,6 +795,7 @@ int mgs_delta_fwd(const void* Q, const void* K, const void* V, const void* beta,
     p.H0 = H0;                                                                                  \
     p.y = static_cast<E*>(y);                                                                   \
     p.HT = H_T;                                                                                 \
+    p.lg = log_gamma;                                                                           \
     return mgs::delta::run<E>(true, p, B, H, T, nh, dk, dv, chunk, static_cast<float*>(saved), \
                               workspace, workspace_bytes, st);                                  \
   }
@@ -625,10 +808,11 @@ int mgs_delta_fwd(const void* Q, const void* K, const void* V, const void* beta,
 #undef MGS_DELTA_FWD
 }
 
-int mgs_delta_bwd(const void* Q, const void* K, const void* V, const void* beta, const void* saved,
-                  const void* dy, const float* dH_T, void* dQ, void* dK, void* dV, void* dbeta,
-                  float* dH0, int64_t B, int H, int64_t T, int nh, int dk, int dv, int chunk,
-                  int dtype, void* workspace, size_t workspace_bytes, void* stream) {
+int delta_bwd(const void* Q, const void* K, const void* V, const void* beta, const float* log_gamma,
+              const void* saved, const void* dy, const float* dH_T, void* dQ, void* dK, void* dV,
+              void* dbeta, float* dH0, float* dlog_gamma, int64_t B, int H, int64_t T, int nh,
+              int dk, int dv, int chunk, int dtype, void* workspace, size_t workspace_bytes,
+              void* stream) {
   auto st = static_cast<cudaStream_t>(stream);
 #define MGS_DELTA_BWD(E)                                                                        \
   {                                                                                             \
@@ -644,6 +828,8 @@ int mgs_delta_bwd(const void* Q, const void* K, const void* V, const void* beta,
     p.dV = static_cast<E*>(dV);                                                                 \
     p.dbeta = static_cast<E*>(dbeta);                                                           \
     p.dH0 = dH0;                                                                                \
+    p.lg = log_gamma;                                                                           \
+    p.dlg = dlog_gamma;                                                                         \
     return mgs::delta::run<E>(false, p, B, H, T, nh, dk, dv, chunk,                            \
                               static_cast<float*>(const_cast<void*>(saved)), workspace,         \
                               workspace_bytes, st);                                             \
@@ -655,6 +841,63 @@ int mgs_delta_bwd(const void* Q, const void* K, const void* V, const void* beta,
     default: return MGS_BAD_DTYPE;
   }
 #undef MGS_DELTA_BWD
+}
+}  // namespace
+
+size_t mgs_delta_saved_size(int64_t B, int H, int64_t T, int nh, int dk, int dv, int chunk,
+                            int dtype) {
+  return delta_saved_size(B, H, T, nh, dk, dv, chunk, dtype, false);
+}
+
+size_t mgs_delta_workspace_size(int64_t B, int H, int64_t T, int nh, int dk, int dv, int chunk,
+                                int dtype) {
+  return delta_workspace_size(B, H, T, nh, dk, dv, chunk, dtype, false);
+}
+
+int mgs_delta_fwd(const void* Q, const void* K, const void* V, const void* beta, const float* H0,
+                  void* y, float* H_T, void* saved, int64_t B, int H, int64_t T, int nh, int dk,
+                  int dv, int chunk, int dtype, void* workspace, size_t workspace_bytes,
+                  void* stream) {
+  return delta_fwd(Q, K, V, beta, H0, nullptr, y, H_T, saved, B, H, T, nh, dk, dv, chunk, dtype,
+                   workspace, workspace_bytes, stream);
+}
+
+int mgs_delta_bwd(const void* Q, const void* K, const void* V, const void* beta, const void* saved,
+                  const void* dy, const float* dH_T, void* dQ, void* dK, void* dV, void* dbeta,
+                  float* dH0, int64_t B, int H, int64_t T, int nh, int dk, int dv, int chunk,
+                  int dtype, void* workspace, size_t workspace_bytes, void* stream) {
+  return delta_bwd(Q, K, V, beta, nullptr, saved, dy, dH_T, dQ, dK, dV, dbeta, dH0, nullptr, B, H,
+                   T, nh, dk, dv, chunk, dtype, workspace, workspace_bytes, stream);
+}
+
+size_t mgs_delta_gated_saved_size(int64_t B, int H, int64_t T, int nh, int dk, int dv, int chunk,
+                                  int dtype) {
+  return delta_saved_size(B, H, T, nh, dk, dv, chunk, dtype, true);
+}
+
+size_t mgs_delta_gated_workspace_size(int64_t B, int H, int64_t T, int nh, int dk, int dv,
+                                      int chunk, int dtype) {
+  return delta_workspace_size(B, H, T, nh, dk, dv, chunk, dtype, true);
+}
+
+int mgs_delta_gated_fwd(const void* Q, const void* K, const void* V, const void* beta,
+                        const float* H0, const float* log_gamma, void* y, float* H_T, void* saved,
+                        int64_t B, int H, int64_t T, int nh, int dk, int dv, int chunk, int dtype,
+                        void* workspace, size_t workspace_bytes, void* stream) {
+  if (log_gamma == nullptr) return MGS_BAD_SHAPE;
+  return delta_fwd(Q, K, V, beta, H0, log_gamma, y, H_T, saved, B, H, T, nh, dk, dv, chunk, dtype,
+                   workspace, workspace_bytes, stream);
+}
+
+int mgs_delta_gated_bwd(const void* Q, const void* K, const void* V, const void* beta,
+                        const float* log_gamma, const void* saved, const void* dy,
+                        const float* dH_T, void* dQ, void* dK, void* dV, void* dbeta, float* dH0,
+                        float* dlog_gamma, int64_t B, int H, int64_t T, int nh, int dk, int dv,
+                        int chunk, int dtype, void* workspace, size_t workspace_bytes,
+                        void* stream) {
+  if (log_gamma == nullptr || dlog_gamma == nullptr) return MGS_BAD_SHAPE;
+  return delta_bwd(Q, K, V, beta, log_gamma, saved, dy, dH_T, dQ, dK, dV, dbeta, dH0, dlog_gamma,
+                   B, H, T, nh, dk, dv, chunk, dtype, workspace, workspace_bytes, stream);
 }
 
 }  // extern "C"

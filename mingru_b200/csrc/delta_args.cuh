@@ -31,6 +31,8 @@ struct Args {
   float* Hb;      // (BH, nchunks, dk, dv)  chunk-start states, saved for the backward
   float* Ec;      // (BH, nchunks, dk, dv)  backward scratch
   float* dSo;     // (BH, nchunks, dk, dv)  gradient w.r.t. each chunk's output state
+  const float* lg;  // (BH, T) per-token log decay (<= 0), or null: no decay
+  float* dlg;       // (BH, T) its gradient (backward with decay)
   long long T_;
   int H, nh, dk, dv, C, nchunks;
 };

@@ -12,19 +12,18 @@ MinGRU             min_gru.py:1213-1451        ``parallel_scan_log``
 SignedMinGRU       min_gru.py:1658-1906        ``linear_scan``
 RotationMinGRU     min_gru.py:1909-2362        ``angle_scan_impl`` (k = 2, scale channel)
 GivensMinGRU       min_gru.py:2365-2824        ``angle_scan_impl`` (k = block_size)
-DeltaMinGRU        min_gru.py:2827-3695        ``delta_scan_impl``
+DeltaMinGRU        min_gru.py:2827-3695        ``delta_scan_impl`` (with decay:
+                                               ``delta_gated_scan_impl``)
 MinGRUBlock        min_gru.py:3698-3922        (pre-norm residual wrapper)
 MinGRUStack        min_gru.py:4019-4336        (stack of blocks)
 =================  ==========================  =====================================
 
 The coefficient heads (``nn.Linear`` + elementwise activations) are plain
-torch; the recurrences run only on the CUDA kernels (no eager or CPU path:
-``forward`` on CPU tensors raises ``ValueError``). ``step()`` is the O(1)
-per-token recurrence in torch and works on any device. Not implemented
-here: the decay-active ``DeltaMinGRU`` forward (the reference's eager
-``_forward_chunked_gated``, min_gru.py:3257-3448) -- constructing the module
-with decay works, its ``forward`` with ``delta_t`` raises
-``NotImplementedError``; ``step()`` with decay works.
+torch, except MinGRU's without decay, whose softplus / log_g prologue runs
+inside the scan kernels (``mingru_gate_scan``). The recurrences run only on
+the CUDA kernels (no eager or CPU path: CPU tensors raise ``ValueError``):
+``forward`` on the scans above, ``step()`` -- the O(1) per-token recurrence
+-- on the fused step kernels of ``step_ops``.
 """
 
 from __future__ import annotations
@@ -41,6 +40,7 @@ from . import step_ops
 from .scan_ops import (
     angle_scan_impl,
     brickwall_meta,
+    delta_gated_scan_impl,
     delta_scan_impl,
     linear_scan,
     mingru_gate_scan,
@@ -461,11 +461,6 @@ class DeltaMinGRU(DecayMixin, nn.Module):
             if tuple(h_0.shape) != expected:
                 raise ValueError(f"h_0 must have shape {expected} (got {tuple(h_0.shape)})")
             H = h_0.reshape(B, self.n_heads, self.d_k, self.d_v)
-        if dt is not None:
-            raise NotImplementedError(
-                "DeltaMinGRU forward with decay (delta_t) has no kernel in this library yet; "
-                "step() supports decay"
-            )
         if T == 0:
             y = x.new_zeros(B, 0, self.n_heads * self.d_v)
             H = H.clone()
@@ -475,7 +470,15 @@ class DeltaMinGRU(DecayMixin, nn.Module):
             V = torch.stack(vs, dim=2).permute(0, 3, 1, 2, 4)
             beta = torch.stack(betas, dim=2).permute(0, 3, 1, 2)
             Q = q.permute(0, 2, 1, 3)
-            y, H_T = delta_scan_impl(Q, K, V, beta, H.to(torch.float32), chunk_size=self.chunk_size)
+            if dt is None:
+                y, H_T = delta_scan_impl(Q, K, V, beta, H.to(torch.float32),
+                                         chunk_size=self.chunk_size)
+            else:  # per-token log decay -lambda dt per head (min_gru.py:3379-3386)
+                lam = self._decay_lambda()
+                log_gamma = -lam.reshape(1, -1, 1) * dt.unsqueeze(1)
+                y, H_T = delta_gated_scan_impl(Q, K, V, beta, H.to(torch.float32),
+                                               log_gamma.expand(B, self.n_heads, T),
+                                               chunk_size=self.chunk_size)
             H = H_T.to(x.dtype)
             y = y.permute(0, 2, 1, 3).reshape(B, T, self.n_heads * self.d_v).to(x.dtype)
         y = self.out_proj(y)

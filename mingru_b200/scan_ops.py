@@ -848,6 +848,130 @@ def _delta_backward(ctx, dy, dHT, _gsaved):
 
 torch.library.register_autograd("mingru_b200::delta_fwd", _delta_backward, setup_context=_delta_setup)
 
+@torch.library.custom_op("mingru_b200::delta_gated_fwd", mutates_args=())
+def _delta_gated_fwd(
+    Q: torch.Tensor, K: torch.Tensor, V: torch.Tensor, beta: torch.Tensor, H0: torch.Tensor,
+    log_gamma: torch.Tensor, chunk_size: int,
+) -> tuple[torch.Tensor, torch.Tensor, torch.Tensor]:
+    lib = _lib.load()
+    with torch.cuda.device(Q.device):  # sizes are queried on the launch device
+        Q, K, V, beta = (_dense(x) for x in (Q, K, V, beta))
+        H0 = _dense(H0.float())
+        lg = _dense(log_gamma.float())
+        Bn, H, T, nh, dk, dv = _delta_dims(Q, K, V)
+        code = _dtype_code("delta_scan", Q)
+        y = torch.empty(Bn, H, T, dv, dtype=Q.dtype, device=Q.device)
+        HT = torch.empty(Bn, H, dk, dv, dtype=torch.float32, device=Q.device)
+        n = lib.mgs_delta_gated_saved_size(Bn, H, T, nh, dk, dv, chunk_size, code)
+        saved = torch.empty(n // 4, dtype=torch.float32, device=Q.device)
+        ws = _workspace(lib.mgs_delta_gated_workspace_size(Bn, H, T, nh, dk, dv, chunk_size, code),
+                        Q.device)
+        st = lib.mgs_delta_gated_fwd(
+            _ptr(Q), _ptr(K), _ptr(V), _ptr(beta), _ptr(H0), _ptr(lg), _ptr(y), _ptr(HT),
+            _ptr(saved), Bn, H, T, nh, dk, dv, chunk_size, code, _ptr(ws), ws.numel(), _stream(Q),
+        )
+        _lib.check(st, "delta_scan (decay) forward")
+        return y, HT, saved
+
+
+@_delta_gated_fwd.register_fake
+def _(Q, K, V, beta, H0, log_gamma, chunk_size):
+    Bn, H, T, nh, dk, dv = _delta_dims(Q, K, V)
+    n = _lib.load().mgs_delta_gated_saved_size(Bn, H, T, nh, dk, dv, chunk_size,
+                                               _dtype_code("delta_scan", Q)) // 4
+    return (Q.new_empty((Bn, H, T, dv)), Q.new_empty((Bn, H, dk, dv), dtype=torch.float32),
+            Q.new_empty((n,), dtype=torch.float32))
+
+
+@torch.library.custom_op("mingru_b200::delta_gated_bwd", mutates_args=())
+def _delta_gated_bwd(
+    Q: torch.Tensor, K: torch.Tensor, V: torch.Tensor, beta: torch.Tensor, log_gamma: torch.Tensor,
+    saved: torch.Tensor, dy: torch.Tensor, dHT: torch.Tensor, chunk_size: int,
+) -> tuple[torch.Tensor, torch.Tensor, torch.Tensor, torch.Tensor, torch.Tensor, torch.Tensor]:
+    lib = _lib.load()
+    with torch.cuda.device(Q.device):  # sizes are queried on the launch device
+        Q, K, V, beta = (_dense(x) for x in (Q, K, V, beta))
+        lg = _dense(log_gamma.float())
+        dy = _dense(dy.to(Q.dtype))
+        dHT = _dense(dHT.float())
+        Bn, H, T, nh, dk, dv = _delta_dims(Q, K, V)
+        code = _dtype_code("delta_scan", Q)
+        dQ, dK, dV, db = (torch.empty_like(x) for x in (Q, K, V, beta))
+        dH0 = torch.empty(Bn, H, dk, dv, dtype=torch.float32, device=Q.device)
+        dlg = torch.empty(Bn, H, T, dtype=torch.float32, device=Q.device)
+        ws = _workspace(lib.mgs_delta_gated_workspace_size(Bn, H, T, nh, dk, dv, chunk_size, code),
+                        Q.device)
+        st = lib.mgs_delta_gated_bwd(
+            _ptr(Q), _ptr(K), _ptr(V), _ptr(beta), _ptr(lg), _ptr(saved), _ptr(dy), _ptr(dHT),
+            _ptr(dQ), _ptr(dK), _ptr(dV), _ptr(db), _ptr(dH0), _ptr(dlg),
+            Bn, H, T, nh, dk, dv, chunk_size, code, _ptr(ws), ws.numel(), _stream(Q),
+        )
+        _lib.check(st, "delta_scan (decay) backward")
+        return dQ, dK, dV, db, dH0, dlg
+
+
+@_delta_gated_bwd.register_fake
+def _(Q, K, V, beta, log_gamma, saved, dy, dHT, chunk_size):
+    Bn, H, T, nh, dk, dv = _delta_dims(Q, K, V)
+    return (torch.empty_like(Q), torch.empty_like(K), torch.empty_like(V), torch.empty_like(beta),
+            Q.new_empty((Bn, H, dk, dv), dtype=torch.float32),
+            Q.new_empty((Bn, H, T), dtype=torch.float32))
+
+
+def _delta_gated_setup(ctx, inputs, output):
+    Q, K, V, beta, H0, lg, chunk_size = inputs
+    ctx.save_for_backward(Q, K, V, beta, lg, output[2])
+    ctx.chunk_size = chunk_size
+    ctx.h0_dtype = H0.dtype
+    ctx.lg_dtype = lg.dtype
+    ctx.mark_non_differentiable(output[2])
+    ctx.set_materialize_grads(False)
+
+
+def _delta_gated_backward(ctx, dy, dHT, _gsaved):
+    if torch.is_grad_enabled():
+        raise RuntimeError("delta_scan does not support second-order autograd (create_graph=True)")
+    Q, K, V, beta, lg, saved = ctx.saved_tensors
+    if dy is None and dHT is None:
+        return (None,) * 7
+    Bn, H, T, nh, dk, dv = _delta_dims(Q, K, V)
+    if dy is None:
+        dy = torch.zeros(Bn, H, T, dv, dtype=Q.dtype, device=Q.device)
+    if dHT is None:
+        dHT = torch.zeros(Bn, H, dk, dv, dtype=torch.float32, device=Q.device)
+    dQ, dK, dV, db, dH0, dlg = _delta_gated_bwd(Q, K, V, beta, lg, saved, dy, dHT, ctx.chunk_size)
+    return dQ, dK, dV, db, dH0.to(ctx.h0_dtype), dlg.to(ctx.lg_dtype), None
+
+
+torch.library.register_autograd(
+    "mingru_b200::delta_gated_fwd", _delta_gated_backward, setup_context=_delta_gated_setup
+)
+
+
+def delta_gated_scan_impl(
+    Q: torch.Tensor, K: torch.Tensor, V: torch.Tensor, beta: torch.Tensor, H0: torch.Tensor,
+    log_gamma: torch.Tensor, *, chunk_size: int,
+) -> tuple[torch.Tensor, torch.Tensor]:
+    """The delta rule with per-token time decay; returns ``(y, H_T)``.
+
+    Arguments as :func:`delta_scan_impl`, plus ``log_gamma`` ``(B, n_heads, T)``
+    (or broadcastable to it): the per-token log decay ``-lambda * dt <= 0`` of
+    each head. The state entering token t decays by ``exp(log_gamma_t)``
+    before the token's ``nh`` micro-steps -- the decay-active
+    ``DeltaMinGRU._forward_chunked_gated`` (reference ``min_gru.py:3290-3448``),
+    which the reference runs in eager torch only. Every decay factor is exp of
+    a chunk-relative span sum (no division, no difference of running sums), so
+    a saturated gap wipes the memory exactly. Differentiable w.r.t. all six
+    tensors (``log_gamma`` included, so lambda and dt get gradients through it).
+    """
+    op = "delta_scan"
+    if Q.ndim != 4:
+        raise ValueError(f"{op}: need 4-D Q (B, n_heads, T, d_k) (got {tuple(Q.shape)})")
+    Bn, H, T, dk = Q.shape
+    lg = torch.broadcast_to(log_gamma, (Bn, H, T))
+    return _delta_checked(Q, K, V, beta, H0, chunk_size, gated=True, log_gamma=lg)
+
+
 _DELTA_MAX_DK = 128
 _DELTA_DV_BLOCK = 64  # value columns per kernel call: wider d_v runs as column blocks
 
@@ -855,6 +979,13 @@ _DELTA_DV_BLOCK = 64  # value columns per kernel call: wider d_v runs as column 
 def delta_scan_impl(
     Q: torch.Tensor, K: torch.Tensor, V: torch.Tensor, beta: torch.Tensor, H0: torch.Tensor,
     *, chunk_size: int,
+) -> tuple[torch.Tensor, torch.Tensor]:
+    return _delta_checked(Q, K, V, beta, H0, chunk_size)
+
+
+def _delta_checked(
+    Q: torch.Tensor, K: torch.Tensor, V: torch.Tensor, beta: torch.Tensor, H0: torch.Tensor,
+    chunk_size: int, gated: bool = False, log_gamma: torch.Tensor | None = None,
 ) -> tuple[torch.Tensor, torch.Tensor]:
     """DeltaMinGRU chunked-WY delta rule; returns ``(y, H_T)``.
 
@@ -902,14 +1033,20 @@ def delta_scan_impl(
         raise ValueError(f"{op}: Q, K, V and beta must share a dtype")
     code = _dtype_code(op, Q)
     lib = _lib.load()
-    if lib.mgs_delta_saved_size(Bn, H, T, nh, dk, min(dv, _DELTA_DV_BLOCK), int(chunk_size), code) == 0 \
+    size_fn = lib.mgs_delta_gated_saved_size if gated else lib.mgs_delta_saved_size
+    if size_fn(Bn, H, T, nh, dk, min(dv, _DELTA_DV_BLOCK), int(chunk_size), code) == 0 \
             and Bn * H * T > 0:
         raise ValueError(
             f"{op}: outside the kernel envelope: nh={nh} micro-steps of one token do not fit the "
             f"kernels' shared memory at d_k={dk} (chunk_size={chunk_size}, d_v={dv})"
         )
+    if gated:
+        _require_cuda(op, log_gamma)
+        fwd = lambda q, k, v, b, h0: _delta_gated_fwd(q, k, v, b, h0, log_gamma, int(chunk_size))
+    else:
+        fwd = lambda q, k, v, b, h0: _delta_fwd(q, k, v, b, h0, int(chunk_size))
     if dv <= _DELTA_DV_BLOCK:
-        y, HT, _ = _delta_fwd(Q, K, V, beta, H0, int(chunk_size))
+        y, HT, _ = fwd(Q, K, V, beta, H0)
     else:
         # Independent value-column blocks; autograd adds their Q, K, beta
         # gradients. Blocks of 16-bit inputs run in fp32 so the partial
@@ -919,7 +1056,7 @@ def delta_scan_impl(
         ys, hts = [], []
         for j0 in range(0, dv, _DELTA_DV_BLOCK):
             j1 = min(dv, j0 + _DELTA_DV_BLOCK)
-            yj, hj, _ = _delta_fwd(Qw, Kw, wide(V[..., j0:j1]), bw, H0[..., j0:j1], int(chunk_size))
+            yj, hj, _ = fwd(Qw, Kw, wide(V[..., j0:j1]), bw, H0[..., j0:j1])
             ys.append(yj)
             hts.append(hj)
         y, HT = torch.cat(ys, -1).to(Q.dtype), torch.cat(hts, -1)

@@ -143,3 +143,40 @@ def delta_backward(Q, K, V, beta, H0, dy, dHT, chunk_size):
                 dH = dHc
             dH0[b, h] = dH
     return dQ, dK, dV, dbeta, dH0
+
+
+def gated_sequential_torch(Q, K, V, beta, H0, log_gamma, grad_y=None, grad_HT=None):
+    """The decay-active delta rule as its sequential recurrence, in float64
+    torch on the CPU, with autograd for the gradients. TEST INFRASTRUCTURE.
+
+    Per token t (``DeltaMinGRU.step`` with decay, reference min_gru.py:
+    3611-3688): the incoming state decays once, H <- exp(log_gamma_t) H, then
+    the token's nh micro-steps H <- H + beta k (v - k^T H)^T run undecayed,
+    and y_t = q_t^T H. ``_forward_chunked_gated`` (min_gru.py:3290-3448) is the
+    chunked form of exactly this recurrence. Inputs as ``delta_forward`` plus
+    ``log_gamma`` (B, H, T). Returns (y, H_T) and, when ``grad_y`` is given,
+    the gradients (dQ, dK, dV, dbeta, dH0, dlog_gamma) of
+    sum(y * grad_y) + sum(H_T * grad_HT)."""
+    import torch
+
+    ts = [torch.as_tensor(np.asarray(x), dtype=torch.float64).requires_grad_(grad_y is not None)
+          for x in (Q, K, V, beta, H0, log_gamma)]
+    q, k, v, b, H, lg = ts
+    Bn, nH, T, dk = q.shape
+    nh = k.shape[3]
+    ys = []
+    for t in range(T):
+        H = torch.exp(lg[:, :, t])[..., None, None] * H
+        for m in range(nh):
+            km, vm = k[:, :, t, m], v[:, :, t, m]
+            kH = torch.einsum("bhk,bhkv->bhv", km, H)
+            H = H + b[:, :, t, m][..., None, None] * torch.einsum("bhk,bhv->bhkv", km, vm - kH)
+        ys.append(torch.einsum("bhk,bhkv->bhv", q[:, :, t], H))
+    y = torch.stack(ys, 2) if ys else q.new_zeros(Bn, nH, 0, v.shape[-1])
+    if grad_y is None:
+        return y.detach().numpy(), H.detach().numpy()
+    gy = torch.as_tensor(np.asarray(grad_y), dtype=torch.float64)
+    gH = torch.as_tensor(np.asarray(grad_HT), dtype=torch.float64)
+    grads = torch.autograd.grad((y * gy).sum() + (H * gH).sum(), ts, allow_unused=True)
+    grads = [torch.zeros_like(x) if g is None else g for x, g in zip(ts, grads)]
+    return y.detach().numpy(), H.detach().numpy(), [g.numpy() for g in grads]

@@ -224,6 +224,50 @@ def main() -> None:
         save(name, Q=Q, K=K, V=V, beta=beta, H0=H0, y=y, H_T=HT, grad_y=gy, grad_H_T=gHT,
              dQ=dQ, dK=dK, dV=dV, dbeta=dbeta, dH0=dH0, chunk=torch.tensor(chunk))
 
+    # ------------------------------------------------------- delta, decay
+    # DeltaMinGRU._forward_chunked_gated (min_gru.py:3290-3448) through the same
+    # raw-tensor shim, with lambda and dt as inputs (log gamma = -lambda dt).
+    def delta_gated_ref(Q, K, V, beta, H0, lam, dtt, chunk):
+        Bq, nH, Tq, dk = Q.shape
+        nh, dv = K.shape[3], V.shape[4]
+        q = Q.permute(0, 2, 1, 3)
+        ks = list(K.permute(0, 2, 3, 1, 4).unbind(2))
+        vs = list(V.permute(0, 2, 3, 1, 4).unbind(2))
+        bs = list(beta.permute(0, 2, 3, 1).unbind(2))
+        shim = types.SimpleNamespace(nh=nh, n_heads=nH, d_k=dk, d_v=dv, chunk_size=chunk,
+                                     _coeffs=lambda x: (q, ks, vs, bs), _decay_lambda=lambda: lam,
+                                     _span_log_decay=mg.DeltaMinGRU._span_log_decay,
+                                     _warned_fp32_decay_saturation=True)
+        y, HT = mg.DeltaMinGRU._forward_chunked_gated(shim, Q.new_empty(Bq, Tq, 1), H0, dtt)
+        return y.permute(0, 2, 1, 3), HT
+
+    for name, (B, H, T, nh, dk, dv, chunk, big) in {
+        "deltagated_small": (2, 2, 11, 1, 8, 8, 4, False),
+        "deltagated_nh2": (1, 2, 13, 2, 4, 4, 5, False),
+        "deltagated_c16": (1, 2, 40, 1, 16, 16, 16, False),
+        "deltagated_saturated": (1, 2, 30, 1, 8, 8, 8, True),
+    }.items():
+        if only is not None and name not in only:
+            continue
+        g = torch.Generator().manual_seed(41)
+        Q = torch.randn(B, H, T, dk, generator=g, dtype=dt).requires_grad_(True)
+        K = F.normalize(torch.randn(B, H, T, nh, dk, generator=g, dtype=dt), dim=-1).requires_grad_(True)
+        V = torch.randn(B, H, T, nh, dv, generator=g, dtype=dt).requires_grad_(True)
+        beta = (2 * torch.sigmoid(torch.randn(B, H, T, nh, generator=g, dtype=dt))).requires_grad_(True)
+        H0 = (torch.randn(B, H, dk, dv, generator=g, dtype=dt) * 0.1).requires_grad_(True)
+        lam = (torch.rand(H, generator=g, dtype=dt) + 0.1).requires_grad_(True)
+        dtt = torch.rand(B, T, generator=g, dtype=dt) * 2
+        if big:  # a few gaps large enough to wipe the memory
+            dtt[:, 7] = 1e4
+            dtt[:, 19] = 80.0
+        dtt.requires_grad_(True)
+        y, HT = delta_gated_ref(Q, K, V, beta, H0, lam, dtt, chunk)
+        (gy, gHT), gs = grads([y, HT], [Q, K, V, beta, H0, lam, dtt], 1234)
+        dQ, dK, dV, dbeta, dH0, dlam, ddt = gs
+        save(name, Q=Q, K=K, V=V, beta=beta, H0=H0, lam=lam, dt=dtt, y=y, H_T=HT, grad_y=gy,
+             grad_H_T=gHT, dQ=dQ, dK=dK, dV=dV, dbeta=dbeta, dH0=dH0, dlam=dlam, ddt=ddt,
+             chunk=torch.tensor(chunk))
+
     # ------------------------------------------------------------ modules
     import json
 
@@ -253,8 +297,14 @@ def main() -> None:
         # d_k = d_v = 128 per head (hidden 256 over 2 heads; d_model=512 over 4 heads
         # runs the same kernels per head)
         "module_delta_d128": ("DeltaMinGRU", dict(input_size=16, hidden_size=256, n_heads=2), False),
+        # decay active: the reference's eager _forward_chunked_gated
+        "module_delta_decay": ("DeltaMinGRU", dict(input_size=8, hidden_size=32, n_heads=2,
+                                                   chunk_size=16, decay="learnable"), True),
+        "module_delta_decay_fixed": ("DeltaMinGRU", dict(input_size=8, hidden_size=16, n_heads=2,
+                                                         nh=2, decay="fixed", decay_rate=0.3), True),
     }
-    long_t = {"module_delta_nh2": 150, "module_delta_d128": 70}  # several chunks
+    long_t = {"module_delta_nh2": 150, "module_delta_d128": 70,  # several chunks
+              "module_delta_decay": 50, "module_delta_decay_fixed": 40}
     for name, (cls_name, kwargs, use_dt) in module_cases.items():
         if only is not None and name not in only:
             continue
@@ -267,7 +317,7 @@ def main() -> None:
         if cls_name == "MinGRUStack":
             out, _ = mod(x)
         elif cls_name == "DeltaMinGRU":
-            out = mod(x)
+            out = mod(x) if dtv is None else mod(x, None, dtv)
         else:
             out = mod(x, None, dtv)
         cot = torch.randn(out.shape, generator=torch.Generator().manual_seed(1234), dtype=dt)

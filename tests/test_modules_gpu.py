@@ -31,7 +31,7 @@ def test_module_matches_reference(cuda, name):
     x = torch.as_tensor(g["x"], dtype=torch.float32, device=cuda).requires_grad_(True)
     if meta["cls"] == "MinGRUStack":
         out, _ = mod(x)
-    elif meta["cls"] == "DeltaMinGRU":
+    elif meta["cls"] == "DeltaMinGRU" and "delta_t" not in g:
         out = mod(x)
     else:
         dt = torch.as_tensor(g["delta_t"], dtype=torch.float32, device=cuda) if "delta_t" in g else None

@@ -103,3 +103,25 @@ def test_float32_oracle_tracks_float64():
     A32, B32 = oracle.linear_scan(a, b, dtype=np.float32)
     np.testing.assert_allclose(B32, B64, rtol=1e-4, atol=1e-5)
     np.testing.assert_allclose(A32, A64, rtol=1e-4, atol=1e-30)
+
+
+@pytest.mark.parametrize("name", golden_names("deltagated_"))
+def test_gated_delta_oracle_vs_reference(name):
+    """The sequential gated recurrence (oracle.delta_oracle.gated_sequential_torch)
+    reproduces the reference's chunked _forward_chunked_gated and its autograd
+    gradients, including those w.r.t. lambda and dt (log gamma = -lambda dt)."""
+    from oracle import delta_oracle
+
+    g = load_golden(name)
+    lam, dtt = g["lam"], g["dt"]
+    lg = -lam[None, :, None] * dtt[:, None, :]
+    y, HT, grads = delta_oracle.gated_sequential_torch(
+        g["Q"], g["K"], g["V"], g["beta"], g["H0"], lg, g["grad_y"], g["grad_H_T"])
+    tol = dict(rtol=1e-9, atol=1e-10)
+    np.testing.assert_allclose(y, g["y"], **tol)
+    np.testing.assert_allclose(HT, g["H_T"], **tol)
+    for got, key in zip(grads[:5], ["dQ", "dK", "dV", "dbeta", "dH0"]):
+        np.testing.assert_allclose(got, g[key], **tol, err_msg=key)
+    dlg = grads[5]
+    np.testing.assert_allclose(-(dlg * dtt[:, None, :]).sum((0, 2)), g["dlam"], **tol)
+    np.testing.assert_allclose(-(dlg * lam[None, :, None]).sum(1), g["ddt"], **tol)
