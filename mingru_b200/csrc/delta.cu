@@ -393,10 +393,13 @@ __global__ void __launch_bounds__(kThreads) adj_pass_kernel(const float* Ac, con
 
 // ----------------------------------------------------------- backward (3) --
 // Per-chunk adjoint (the reference's _delta_backward_torch body, restated),
-// with decay extended by the factors' own gradients: every factor is exp of a
-// difference of chunk prefix sums lam[t] = sum_{s<=t} l_s, so its gradient is
-// gathered per token as dlam[t] (+ for the later token of a span, - for the
-// earlier one) and d l_s = sum_{t >= s} dlam[t]:
+// with decay extended by the factors' own gradients. Every factor is exp of
+// the span sum over tokens (t', t] for a token pair t > t' (P_t is the span
+// (-1, t]), so the gradients are gathered per token pair, G2[t][t'] (both
+// tokens' micro-steps summed), and d l_s = sum of G2 over the spans that
+// contain s: t >= s > t'. Nothing cancels (a span not containing s never
+// enters d l_s), so a saturated token whose factors are all 0 gets exactly 0,
+// as autograd through the reference's span sums gives:
 //   y_t = P_t q_t S + sum_l R~[t,l] u_l   R~ = (Q K^T) beta[col] D, D = exp(span[t][tau(l)])
 //   rhs = V - diag(P^) K S,  T = I + strict(K K^T) beta[col] E,  E = exp(span[tau(i)][tau(l)])
 //   S' = P_{C-1} S + K^T diag(c beta) U,  c = exp(span[C-1][tau(l)])
@@ -424,8 +427,8 @@ __global__ void __launch_bounds__(kThreads) bwd_grads_kernel(Args<E> p) {
   // decay only:
   float* sSpan = sdb + Mx;         // C x C
   float* sLam = sSpan + Cx * Cx;   // C
-  float* sdL = sLam + Cx;          // C   d lam
-  float* sKS = sdL + Cx;           // M x dv  (K S, later diag(P^) G)
+  float* sG2 = sLam + Cx;          // C x (C + 1)  span gradients, column t' + 1
+  float* sKS = sG2 + Cx * (Cx + 1);  // M x dv  (K S, later diag(P^) G)
   float* sQS = sKS + Mx * dv;      // C x dv  (Q S)
   float* sc = sQS + Cx * dv;       // M   carry factors c
   float* sw = sc + Mx;             // M   dc_m c_m
@@ -442,9 +445,10 @@ __global__ void __launch_bounds__(kThreads) bwd_grads_kernel(Args<E> p) {
     const E* dy = p.dy + ((size_t)ck.bh * p.T_ + ck.t0) * dv;
     for (int i = threadIdx.x; i < Ct * dv; i += blockDim.x) sdy[i] = to_f32<E>(dy[i]);
   }
+  auto G2 = [&](int t, int t2) -> float& { return sG2[t * (Cx + 1) + t2 + 1]; };
   if (dec) {
     build_spans(p.lg + ck.bh * p.T_ + ck.t0, Ct, sSpan, sLam);
-    for (int t = threadIdx.x; t < Ct; t += blockDim.x) sdL[t] = 0.f;
+    for (int i = threadIdx.x; i < Cx * (Cx + 1); i += blockDim.x) sG2[i] = 0.f;
     for (int m = threadIdx.x; m < M; m += blockDim.x)
       sc[m] = span_factor(sSpan, Ct, nh, Ct - 1, m);
   }
@@ -461,12 +465,12 @@ __global__ void __launch_bounds__(kThreads) bwd_grads_kernel(Args<E> p) {
   build_P(Ct, M, nh, dk, sQ, sK, sb, sP, sSm, dec ? sSpan : nullptr);
   bgemm<false, true>(Ct, dk, dv, sdy, dv, sS, dv, sdQ, dk, false);     // dQ = dy S^T
   if (dec) {
-    // dP_t = q_t^T S dy_t -> dlam[t] += dP_t P_t;  dQ = diag(P) dy S^T
+    // dP_t = q_t^T S dy_t -> span (-1, t]: G2[t][-1] += dP_t P_t;  dQ = diag(P) dy S^T
     bgemm<false, false>(Ct, dv, dk, sQ, dk, sS, dv, sQS, dv, false);
     for (int t = threadIdx.x; t < Ct; t += blockDim.x) {
       float d = 0.f;
       for (int v = 0; v < dv; ++v) d = fmaf(sQS[t * dv + v], sdy[t * dv + v], d);
-      sdL[t] += d * expf(sLam[t]);
+      G2(t, -1) += d * expf(sLam[t]);
     }
     for (int i = threadIdx.x; i < Ct * dk; i += blockDim.x) sdQ[i] *= expf(sLam[i / dk]);
     __syncthreads();
@@ -506,16 +510,10 @@ __global__ void __launch_bounds__(kThreads) bwd_grads_kernel(Args<E> p) {
     sdb[m] += s;
   }
   if (dec) {
-    // D pairs: a[t,l] = dP Sm beta D; dlam[t] += sum_l a[t,l], dlam[tau(l)] -= sum_t a[t,l]
-    for (int u = threadIdx.x; u < Ct; u += blockDim.x) {
-      float plus = 0.f, minus = 0.f;
-      for (int l = 0; l < M && l / nh <= u; ++l)
-        plus += sdP[u * M + l] * sSm[u * M + l] * sb[l] * span_factor(sSpan, Ct, nh, u, l);
-      for (int l = u * nh; l < (u + 1) * nh; ++l)
-        for (int t = u; t < Ct; ++t)
-          minus += sdP[t * M + l] * sSm[t * M + l] * sb[l] * span_factor(sSpan, Ct, nh, t, l);
-      sdL[u] += plus - minus;
-    }
+    // read factors D[t][l] = exp(span (tau(l), t]): G2[t][tau(l)] += dP Sm beta D
+    for (int u = threadIdx.x; u < Ct; u += blockDim.x)
+      for (int l = 0; l < u * nh; ++l)
+        G2(u, l / nh) += sdP[u * M + l] * sSm[u * M + l] * sb[l] * span_factor(sSpan, Ct, nh, u, l);
   }
   __syncthreads();
   for (int i = threadIdx.x; i < Ct * M; i += blockDim.x) {
@@ -528,12 +526,12 @@ __global__ void __launch_bounds__(kThreads) bwd_grads_kernel(Args<E> p) {
   solve_lower_unit_t(M, dv, sL, M, sdU, dv);                      // G = T^{-T} dU
   bgemm<false, true>(M, M, dv, sdU, dv, sU, dv, sdP, M, false, -1.f);  // dT = -G U^T
   if (dec) {
-    // dP^_m = -(K S)_m . G_m -> dlam[tau(m)] += dP^_m P^_m; then K S <- diag(P^) G
+    // dP^_m = -(K S)_m . G_m -> G2[tau(m)][-1] += dP^_m P^_m; then K S <- diag(P^) G
     for (int u = threadIdx.x; u < Ct; u += blockDim.x) {
       float d = 0.f;
       for (int m = u * nh; m < (u + 1) * nh; ++m)
         for (int v = 0; v < dv; ++v) d -= sKS[m * dv + v] * sdU[m * dv + v];
-      sdL[u] += d * expf(sLam[u]);
+      G2(u, -1) += d * expf(sLam[u]);
     }
     __syncthreads();
     for (int i = threadIdx.x; i < M * dv; i += blockDim.x) sKS[i] = expf(sLam[(i / dv) / nh]) * sdU[i];
@@ -558,26 +556,19 @@ __global__ void __launch_bounds__(kThreads) bwd_grads_kernel(Args<E> p) {
     sdb[l] += s;
   }
   if (dec) {
-    // E pairs: e[i,l] = dT KK beta E (i > l): dlam[tau(i)] += e, dlam[tau(l)] -= e;
-    // carry factors: dlam[C-1] += sum_m dc_m c_m, dlam[tau(m)] -= dc_m c_m;
-    // S' = P_{C-1} S: dlam[C-1] += <S, dSo> P_{C-1}
+    // T factors E[i][l] = exp(span (tau(l), tau(i)]): G2[tau(i)][tau(l)] += dT KK beta E;
+    // carry factors c_m = exp(span (tau(m), C-1]): G2[C-1][tau(m)] += dc_m c_m;
+    // S' = P_{C-1} S: G2[C-1][-1] += <S, dSo> P_{C-1}
     for (int u = threadIdx.x; u < Ct; u += blockDim.x) {
-      float plus = 0.f, minus = 0.f;
       for (int i = u * nh; i < (u + 1) * nh; ++i)
-        for (int l = 0; l < i; ++l)
-          plus += sdP[i * M + l] * sKK[i * M + l] * sb[l] * span_factor(sSpan, Ct, nh, u, l);
-      for (int l = u * nh; l < (u + 1) * nh; ++l) {
-        for (int i = l + 1; i < M; ++i)
-          minus += sdP[i * M + l] * sKK[i * M + l] * sb[l] * span_factor(sSpan, Ct, nh, i / nh, l);
-        minus += sw[l];
-      }
+        for (int l = 0; l < u * nh; ++l)
+          G2(u, l / nh) += sdP[i * M + l] * sKK[i * M + l] * sb[l] * span_factor(sSpan, Ct, nh, u, l);
       if (u == Ct - 1) {
-        for (int m = 0; m < M; ++m) plus += sw[m];
+        for (int m = 0; m < u * nh; ++m) G2(u, m / nh) += sw[m];
         float sd = 0.f;
         for (int i = 0; i < dk * dv; ++i) sd = fmaf(sS[i], sdS[i], sd);
-        plus += sd * expf(sLam[u]);
+        G2(u, -1) += sd * expf(sLam[u]);
       }
-      sdL[u] += plus - minus;
     }
   }
   __syncthreads();
@@ -597,13 +588,13 @@ __global__ void __launch_bounds__(kThreads) bwd_grads_kernel(Args<E> p) {
   for (int i = threadIdx.x; i < M * dk; i += blockDim.x) dK[i] = from_f32<E>(sdK[i]);
   for (int i = threadIdx.x; i < M * dv; i += blockDim.x) dV[i] = from_f32<E>(sdU[i]);
   for (int i = threadIdx.x; i < M; i += blockDim.x) db[i] = from_f32<E>(sdb[i]);
-  if (dec && threadIdx.x == 0) {  // d l_s = sum_{t >= s} dlam[t]
-    float acc = 0.f;
-    for (int t = Ct - 1; t >= 0; --t) {
-      acc += sdL[t];
-      p.dlg[tok0 + t] = acc;
+  if (dec)  // d l_s = sum of G2 over the spans (t', t] that contain s: t >= s > t'
+    for (int s0 = threadIdx.x; s0 < Ct; s0 += blockDim.x) {
+      float acc = 0.f;
+      for (int t = s0; t < Ct; ++t)
+        for (int t2 = -1; t2 < s0; ++t2) acc += G2(t, t2);
+      p.dlg[tok0 + s0] = acc;
     }
-  }
 }
 
 // ---------------------------------------------------------------- launch --
@@ -630,7 +621,7 @@ inline SmemPlan smem_plan(int nh, int C, int dk, int dv, bool decay = false) {
   s.bwd_e = (M * k + M + c * k + c * v + M * M + c * M + M * v + k * v + spans) * 4;
   s.bwd_grads = (M * k + M * v + M + c * k + 2 * k * v + M * v + M * M + 2 * c * M + M * M +
                  M * v + M * k + c * k + M +
-                 (decay ? spans + c + M * v + c * v + 2 * M + M * M : 0)) * 4;
+                 (decay ? spans + c * (c + 1) + M * v + c * v + 2 * M + M * M : 0)) * 4;
   return s;
 }
 

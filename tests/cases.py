@@ -95,6 +95,36 @@ def delta_case_inputs(kind: str, case):
     return delta_bf16_inputs(case, seed=sum(case) + 1)
 
 
+# decay-active delta: (B, H, T, nh, dk, dv, chunk)
+DELTA_GATED_CASES = [
+    (2, 2, 100, 1, 32, 32, 32), (1, 2, 150, 2, 16, 16, 64), (1, 1, 70, 1, 64, 64, 64),
+    (2, 3, 45, 3, 8, 16, 10), (1, 2, 90, 1, 16, 80, 64),
+]
+
+
+def delta_gated_inputs(case, seed):
+    """Inputs of a decay-active case: the delta inputs (beta = 2 sigmoid, as
+    DeltaMinGRU builds it), per-head lambda and per-token gaps dt, one gap
+    large enough to wipe the memory."""
+    B, H, T, nh, dk, dv, chunk = case
+    rng = np.random.default_rng(seed)
+    K = rng.standard_normal((B, H, T, nh, dk))
+    K /= np.linalg.norm(K, axis=-1, keepdims=True)
+    d = {
+        "Q": rng.standard_normal((B, H, T, dk)),
+        "K": K,
+        "V": rng.standard_normal((B, H, T, nh, dv)),
+        "beta": 2 / (1 + np.exp(-rng.standard_normal((B, H, T, nh)))),
+        "H0": rng.standard_normal((B, H, dk, dv)) * 0.1,
+        "grad_y": rng.standard_normal((B, H, T, dv)),
+        "grad_H_T": rng.standard_normal((B, H, dk, dv)),
+    }
+    lam = rng.random(H) * 0.5 + 0.05
+    dtt = rng.random((B, T)) * 2
+    dtt[:, T // 3] = 1e3
+    return {k: _f32(v) for k, v in d.items()}, _f32(lam), _f32(dtt)
+
+
 def case_key(prefix: str, case) -> str:
     return prefix + ":" + ",".join(str(x) for x in case)
 

@@ -463,6 +463,33 @@ def eager_dev(ref: str) -> None:
         delta_case(C.case_key("delta_fp32", case), C.delta_case_inputs("fp32", case), case[-1])
     for case in C.DELTA_TC_CASES:
         delta_case(C.case_key("delta_bf16", case), C.delta_case_inputs("bf16", case), case[-1])
+    def delta_gated_eager(d, lam, dtt, chunk, dtype):
+        Q, K, V, beta, H0 = (t(d[k], dtype, True) for k in ("Q", "K", "V", "beta", "H0"))
+        lm, dd = t(lam, dtype, True), t(dtt, dtype, True)
+        Bq, nH, Tq, dk = Q.shape
+        nh, dv = K.shape[3], V.shape[4]
+        q = Q.permute(0, 2, 1, 3)
+        ks = list(K.permute(0, 2, 3, 1, 4).unbind(2))
+        vs = list(V.permute(0, 2, 3, 1, 4).unbind(2))
+        bs = list(beta.permute(0, 2, 3, 1).unbind(2))
+        shim = types.SimpleNamespace(nh=nh, n_heads=nH, d_k=dk, d_v=dv, chunk_size=chunk,
+                                     _coeffs=lambda x: (q, ks, vs, bs), _decay_lambda=lambda: lm,
+                                     _span_log_decay=mg.DeltaMinGRU._span_log_decay,
+                                     _warned_fp32_decay_saturation=True)
+        y, HT = mg.DeltaMinGRU._forward_chunked_gated(shim, Q.new_empty(Bq, Tq, 1), H0, dd)
+        y = y.permute(0, 2, 1, 3)
+        gs = torch.autograd.grad((y * t(d["grad_y"], dtype)).sum() + (HT * t(d["grad_H_T"], dtype)).sum(),
+                                 [Q, K, V, beta, H0, lm, dd])
+        out = {"y": y, "H_T": HT}
+        out.update(zip(C.DELTA_NAMES + ["dlam", "ddt"], gs))
+        return {k: v.detach().double().numpy() for k, v in out.items()}
+
+    for case in C.DELTA_GATED_CASES:
+        d, lam, dtt = C.delta_gated_inputs(case, seed=sum(case))
+        key = C.case_key("delta_gated", case)
+        res[key] = dev_of(delta_gated_eager(d, lam, dtt, case[-1], torch.float32),
+                          delta_gated_eager(d, lam, dtt, case[-1], torch.float64))
+        print(key, {k: f"{v:.2e}" for k, v in res[key].items()}, flush=True)
     delta_case("delta_full_fp32", C.delta_full_inputs(False), C.DELTA_FULL[-1])
     delta_case("delta_full_bf16", C.delta_full_inputs(True), C.DELTA_FULL[-1])
     for f in sorted(HERE.glob("delta_*.npz")):
