@@ -108,6 +108,52 @@ int mgs_linear_scan_fwd_noalloc(const void* a, const void* b, void* A, void* Bc,
                                 int64_t B, int64_t T, int64_t D, int dtype, void* stream);
 
 /* ------------------------------------------------------------------------ */
+/* Sequence-parallel helpers (the sequence split over ranks in time order).
+ * No counterpart in the reference (single-device); they replace the
+ * full-tensor fix-up a sharded scan would otherwise need.
+ *  - *_carry_fwd: one read-only pass over a slice; writes per channel the
+ *    slice's composed forward element, fp32 (NF, B, D): linear (A, B) with
+ *    x -> A x + B; log (alpha, nu) with x -> logaddexp(x + alpha, nu) over
+ *    rows 1..T of log_values.
+ *  - *_carry_bwd: the slice's composed reverse adjoint element, fp32: linear
+ *    (P, Q_A, Q_B), log (P, Q), with Y -> P Y + Q the adjoint the slice passes
+ *    to its left given the one entering from its right.
+ *  - *_fwd_fixup / *_bwd_fixup: the scans of mgs_linear_scan_* and
+ *    mgs_log_scan_* started from a carried-in state (linear: carry_in
+ *    (2, B, D) = (A_in, B_in); log: log_h_in (B, D) in place of
+ *    log_values[:, 0]) and, backward, from the adjoints entering from the
+ *    right (linear (2, B, D), log (B, D)): every output is the full-length
+ *    scan's, with no separate fix-up pass.
+ * Workspace of the *_carry_* calls: mgs_scan_carry_workspace_size bytes.   */
+size_t mgs_scan_carry_workspace_size(int64_t B, int64_t T, int64_t D);
+int mgs_linear_scan_carry_fwd(const void* a, const void* b, float* carry, int64_t B, int64_t T,
+                              int64_t D, int dtype, void* workspace, size_t workspace_bytes,
+                              void* stream);
+int mgs_linear_scan_carry_bwd(const void* a, const void* gA, const void* gBc, float* carry,
+                              int64_t B, int64_t T, int64_t D, int dtype, void* workspace,
+                              size_t workspace_bytes, void* stream);
+int mgs_linear_scan_fwd_fixup(const void* a, const void* b, const float* carry_in, void* A,
+                              void* Bc, void* carries, int64_t B, int64_t T, int64_t D, int dtype,
+                              void* workspace, size_t workspace_bytes, void* stream);
+int mgs_linear_scan_bwd_fixup(const void* a, const void* b, const void* gA, const void* gBc,
+                              const void* carries, const float* adjoint_in, void* da, void* db,
+                              int64_t B, int64_t T, int64_t D, int dtype, void* workspace,
+                              size_t workspace_bytes, void* stream);
+int mgs_log_scan_carry_fwd(const void* log_coeffs, const void* log_values, float* carry, int64_t B,
+                           int64_t T, int64_t D, int dtype, void* workspace,
+                           size_t workspace_bytes, void* stream);
+int mgs_log_scan_carry_bwd(const void* log_coeffs, const void* grad_h, float* carry, int64_t B,
+                           int64_t T, int64_t D, int dtype, void* workspace,
+                           size_t workspace_bytes, void* stream);
+int mgs_log_scan_fwd_fixup(const void* log_coeffs, const void* log_values, const float* log_h_in,
+                           void* h, void* carries, int64_t B, int64_t T, int64_t D, int dtype,
+                           void* workspace, size_t workspace_bytes, void* stream);
+int mgs_log_scan_bwd_fixup(const void* log_coeffs, const void* log_values, const float* log_h_in,
+                           const void* grad_h, const void* carries, const float* adjoint_in,
+                           void* dlog_coeffs, void* dlog_values, int64_t B, int64_t T, int64_t D,
+                           int dtype, void* workspace, size_t workspace_bytes, void* stream);
+
+/* ------------------------------------------------------------------------ */
 /* Time-out test hooks. No counterpart in the reference (its Triton kernels
  * have no cross-CTA waits). Each makes one bounded device-side wait run out
  * on purpose, with a poll bound of `spin_limit`, so that a test can check the

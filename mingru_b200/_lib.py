@@ -37,6 +37,19 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "mgs_linear_scan_fwd": (_int, [_p, _p, _p, _p, _p, _i64, _i64, _i64, _int, _p, _sz, _p]),
     "mgs_linear_scan_bwd": (_int, [_p, _p, _p, _p, _p, _p, _p, _i64, _i64, _i64, _int, _p, _sz, _p]),
     "mgs_linear_scan_fwd_noalloc": (_int, [_p, _p, _p, _p, _p, _i64, _i64, _i64, _int, _p]),
+    "mgs_scan_carry_workspace_size": (_sz, [_i64, _i64, _i64]),
+    "mgs_linear_scan_carry_fwd": (_int, [_p, _p, _p, _i64, _i64, _i64, _int, _p, _sz, _p]),
+    "mgs_linear_scan_carry_bwd": (_int, [_p, _p, _p, _p, _i64, _i64, _i64, _int, _p, _sz, _p]),
+    "mgs_linear_scan_fwd_fixup": (
+        _int, [_p, _p, _p, _p, _p, _p, _i64, _i64, _i64, _int, _p, _sz, _p]),
+    "mgs_linear_scan_bwd_fixup": (
+        _int, [_p, _p, _p, _p, _p, _p, _p, _p, _i64, _i64, _i64, _int, _p, _sz, _p]),
+    "mgs_log_scan_carry_fwd": (_int, [_p, _p, _p, _i64, _i64, _i64, _int, _p, _sz, _p]),
+    "mgs_log_scan_carry_bwd": (_int, [_p, _p, _p, _i64, _i64, _i64, _int, _p, _sz, _p]),
+    "mgs_log_scan_fwd_fixup": (
+        _int, [_p, _p, _p, _p, _p, _i64, _i64, _i64, _int, _p, _sz, _p]),
+    "mgs_log_scan_bwd_fixup": (
+        _int, [_p, _p, _p, _p, _p, _p, _p, _p, _i64, _i64, _i64, _int, _p, _sz, _p]),
     "mgs_test_lookback_timeout": (
         _int, [_p, _p, _p, _p, _i64, _i64, _i64, _p, _sz, _i64, _p]),
     "mgs_test_mbarrier_timeout": (_int, [_p, _i64, _p]),

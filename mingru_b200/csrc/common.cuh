@@ -252,14 +252,26 @@ __device__ __forceinline__ void warp_lookback(const Lookback& lb, long long tile
 // (lane i looks at predecessor i+1 of the strip), so the walk back to the
 // nearest inclusive prefix costs one L2 round trip per 32 predecessors
 // instead of one per predecessor. Same contract as warp_lookback.
+// `seed` (optional, NF floats of this lane) is the element before the first
+// segment of the strip (a carried-in state); the first segment's exclusive
+// prefix is then the seed instead of the identity.
 template <class Monoid, int NF>
 __device__ __forceinline__ void warp_lookback_win(const Lookback& lb, long long tile,
                                                   long long stride, long long pos,
-                                                  const float (&agg)[NF], float (&excl)[NF]) {
+                                                  const float (&agg)[NF], float (&excl)[NF],
+                                                  const float* seed = nullptr) {
   const int lane = threadIdx.x & 31;
   if (pos == 0) {
-    Monoid::identity(excl);
-    lb_publish<NF>(lb, tile, kFlagIncl, agg);
+    if (seed == nullptr) {
+      Monoid::identity(excl);
+      lb_publish<NF>(lb, tile, kFlagIncl, agg);
+    } else {
+      float inc[NF];
+#pragma unroll
+      for (int i = 0; i < NF; ++i) excl[i] = seed[i];
+      Monoid::combine(excl, agg, inc);
+      lb_publish<NF>(lb, tile, kFlagIncl, inc);
+    }
     return;
   }
   lb_publish<NF>(lb, tile, kFlagAgg, agg);

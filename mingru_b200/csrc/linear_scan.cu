@@ -140,6 +140,10 @@ struct Args {
   E* da;
   E* db;
   float* carries;  // forward: written (may be null); backward: read
+  // Sequence-parallel carry-in (null = none), fp32 [2][B][D]: forward, the
+  // state (A, B) the slice starts from; backward, the adjoints (Y_A, Y_B)
+  // entering the slice from the later slices.
+  const float* cin;
   long long T_, D, sper, nstrips;
   long long nchunks;  // tiles (direct) or chunks (strip) per strip for this launch
   long long ntiles;
@@ -295,8 +299,18 @@ __global__ void __launch_bounds__(NW * 32) fwd_direct_kernel(Args<E> p) {
       for (int f = 0; f < NF; ++f) w_[f] = s_agg[w][f][lane];
       combine_into<M, NF>(tot, w_);
     }
-    float ex[NF];
-    warp_lookback_win<M, NF>(p.lb, tile, p.nstrips, chunk, tot, ex);
+    float ex[NF], seed[NF];
+    const bool seeded = p.cin != nullptr && chunk == 0;
+    if (seeded) {  // the carried-in state (A_in, B_in) starts strip position 0
+      const size_t bd = (size_t)(p.nstrips / p.sper) * p.D, o = (size_t)bi * p.D + d0;
+#pragma unroll
+      for (int c = 0; c < C; ++c) {
+        const bool ok = dok && d0 + c < p.D;
+        seed[c] = ok ? p.cin[o + c] : 1.f;
+        seed[C + c] = ok ? p.cin[bd + o + c] : 0.f;
+      }
+    }
+    warp_lookback_win<M, NF>(p.lb, tile, p.nstrips, chunk, tot, ex, seeded ? seed : nullptr);
 #pragma unroll
     for (int f = 0; f < NF; ++f) s_ex[f][lane] = ex[f];
   }
@@ -378,8 +392,19 @@ __global__ void __launch_bounds__(NW * 32) bwd_direct_kernel(Args<E> p) {
       for (int f = 0; f < NFR; ++f) w_[f] = s_ragg[w][f][lane];
       combine_into<RM, NFR>(tot, w_);
     }
-    float ex[NFR];
-    warp_lookback_win<RM, NFR>(p.lb, tile, p.nstrips, rchunk, tot, ex);
+    float ex[NFR], seed[NFR];
+    const bool seeded = p.cin != nullptr && rchunk == 0;
+    if (seeded) {  // the adjoints (Y_A, Y_B) entering from later slices
+      const size_t bd = (size_t)(p.nstrips / p.sper) * p.D, o = (size_t)bi * p.D + d0;
+#pragma unroll
+      for (int c = 0; c < C; ++c) {
+        const bool ok = dok && d0 + c < p.D;
+        seed[c] = 1.f;
+        seed[C + c] = ok ? p.cin[o + c] : 0.f;
+        seed[2 * C + c] = ok ? p.cin[bd + o + c] : 0.f;
+      }
+    }
+    warp_lookback_win<RM, NFR>(p.lb, tile, p.nstrips, rchunk, tot, ex, seeded ? seed : nullptr);
 #pragma unroll
     for (int f = 0; f < NFR; ++f) s_rex[f][lane] = ex[f];
   } else if (warp == 1) {
@@ -528,6 +553,11 @@ __global__ void __launch_bounds__(NW * 32, 1)
     if (lane == 0)
       for (long long c = 0; c < NST && c < nio; ++c) issue(c);
     float A = 1.f, Bv = 0.f;
+    if (p.cin != nullptr && d0 + lane < p.D) {  // carried-in state of the slice
+      const size_t o = (size_t)bi * p.D + d0 + lane;
+      A = p.cin[o];
+      Bv = p.cin[(size_t)(p.nstrips / p.sper) * p.D + o];
+    }
     for (long long c = 0; c < nio; ++c) {
       const long long j = j0 + c;
       const int s = (int)(j % NST);
@@ -628,6 +658,11 @@ __global__ void __launch_bounds__(NW * 32, 1)
     if (lane == 0)
       for (long long c = 0; c < NST && c < nio; ++c) issue(c);
     float ya = 0.f, yb = 0.f;  // adjoints entering from later steps
+    if (p.cin != nullptr && d0 + lane < p.D) {  // ... and from later slices
+      const size_t o = (size_t)bi * p.D + d0 + lane;
+      ya = p.cin[o];
+      yb = p.cin[(size_t)(p.nstrips / p.sper) * p.D + o];
+    }
     for (long long c = 0; c < nio; ++c) {
       const long long io = nio - 1 - c;
       const long long j = j0 + c;
@@ -728,7 +763,8 @@ inline size_t workspace_bytes(const Geometry& g) {
 template <typename E>
 int run(bool fwd, const void* a, const void* b, void* A, void* Bc, const void* gA,
         const void* gB, void* da, void* db, void* carries, long long B, long long T,
-        long long D, int dtype, void* ws, size_t ws_bytes, cudaStream_t st) {
+        long long D, int dtype, void* ws, size_t ws_bytes, cudaStream_t st,
+        const float* cin = nullptr) {
   const Geometry g = geometry(B, T, D, dtype);
   if (g.ntiles == 0) return MGS_OK;
   if (g.ntiles > 0x7fffffffLL) return MGS_UNSUPPORTED;
@@ -740,7 +776,8 @@ int run(bool fwd, const void* a, const void* b, void* A, void* Bc, const void* g
     if (q != nullptr && !aligned(q, va)) return MGS_BAD_ALIGNMENT;
   if (!aligned(ws, 256) || (carries != nullptr && !aligned(carries, 16))) return MGS_BAD_ALIGNMENT;
   if (!fwd && carries == nullptr) return MGS_BAD_SHAPE;
-  Args<E> p;
+  Args<E> p{};
+  p.cin = cin;
   p.a = static_cast<const E*>(a);
   p.b = static_cast<const E*>(b);
   p.A = static_cast<E*>(A);
@@ -800,17 +837,20 @@ int run(bool fwd, const void* a, const void* b, void* A, void* Bc, const void* g
 
 int dispatch(bool fwd, const void* a, const void* b, void* A, void* Bc, const void* gA,
              const void* gB, void* da, void* db, void* carries, long long B, long long T,
-             long long D, int dtype, void* ws, size_t ws_bytes, cudaStream_t st) {
+             long long D, int dtype, void* ws, size_t ws_bytes, cudaStream_t st,
+             const float* cin = nullptr) {
   if (B < 0 || T < 0 || D < 0) return MGS_BAD_SHAPE;
+  if (cin != nullptr && !aligned(cin, 4)) return MGS_BAD_ALIGNMENT;
   switch (dtype) {
     case MGS_F32:
-      return run<float>(fwd, a, b, A, Bc, gA, gB, da, db, carries, B, T, D, dtype, ws, ws_bytes, st);
+      return run<float>(fwd, a, b, A, Bc, gA, gB, da, db, carries, B, T, D, dtype, ws, ws_bytes, st,
+                        cin);
     case MGS_BF16:
       return run<__nv_bfloat16>(fwd, a, b, A, Bc, gA, gB, da, db, carries, B, T, D, dtype, ws,
-                                ws_bytes, st);
+                                ws_bytes, st, cin);
     case MGS_F16:
       return run<__half>(fwd, a, b, A, Bc, gA, gB, da, db, carries, B, T, D, dtype, ws, ws_bytes,
-                         st);
+                         st, cin);
     default:
       return MGS_BAD_DTYPE;
   }
@@ -972,6 +1012,25 @@ int mgs_linear_scan_bwd(const void* a, const void* b, const void* gA, const void
   return mgs::linear::dispatch(false, a, b, nullptr, nullptr, gA, gBc, da, db,
                                const_cast<void*>(carries), B, T, D, dtype, workspace,
                                workspace_bytes, static_cast<cudaStream_t>(stream));
+}
+
+int mgs_linear_scan_fwd_fixup(const void* a, const void* b, const float* carry_in, void* A,
+                              void* Bc, void* carries, int64_t B, int64_t T, int64_t D, int dtype,
+                              void* workspace, size_t workspace_bytes, void* stream) {
+  if (carry_in == nullptr) return MGS_BAD_SHAPE;
+  return mgs::linear::dispatch(true, a, b, A, Bc, nullptr, nullptr, nullptr, nullptr, carries, B, T,
+                               D, dtype, workspace, workspace_bytes,
+                               static_cast<cudaStream_t>(stream), carry_in);
+}
+
+int mgs_linear_scan_bwd_fixup(const void* a, const void* b, const void* gA, const void* gBc,
+                              const void* carries, const float* adjoint_in, void* da, void* db,
+                              int64_t B, int64_t T, int64_t D, int dtype, void* workspace,
+                              size_t workspace_bytes, void* stream) {
+  if (adjoint_in == nullptr) return MGS_BAD_SHAPE;
+  return mgs::linear::dispatch(false, a, b, nullptr, nullptr, gA, gBc, da, db,
+                               const_cast<void*>(carries), B, T, D, dtype, workspace,
+                               workspace_bytes, static_cast<cudaStream_t>(stream), adjoint_in);
 }
 
 int mgs_test_lookback_timeout(const void* a, const void* b, void* A, void* Bc, int64_t B,

@@ -147,6 +147,11 @@ struct Args {
   E* dlv;        // (B, T+1, D)
   const E* lh0;  // gate-fused column kernels: log h_0 (B, D) (lc, lv then hold k, x~)
   E* dlh0;       // gate-fused column kernels: gradient of log h_0 (B, D)
+  // Sequence-parallel carry-in (null = none), fp32 (B, D): lh_in replaces
+  // log_values[:, 0] (the log state the slice starts from); y_in is the
+  // adjoint Y entering the slice from the later slices (backward).
+  const float* lh_in;
+  const float* y_in;
   float* carries;
   long long T_, D, sper, nstrips;
   long long nchunks, ntiles;
@@ -292,9 +297,17 @@ __global__ void __launch_bounds__(NW * 32, 2) fwd_direct_kernel(Args<E> p) {
   const size_t base1 = (size_t)bi * (p.T_ + 1) * p.D + d0;
 
   float lc[S][C], lv[S][C], lv0[C];
+  const size_t bd0 = (size_t)bi * p.D + d0;  // (B, D) index of this lane's first channel
   load_steps<E, C, S>(p.lc, base, t0, p.T_, p.D, dok, 0.f, lc);
   load_steps<E, C, S>(p.lv, base1 + p.D, t0, p.T_, p.D, dok, -INFINITY, lv);
-  if (t0 == 0 && dok) load_vec<E, C>(p.lv + base1, lv0);
+  if (t0 == 0 && dok) {
+    if (p.lh_in != nullptr) {
+#pragma unroll
+      for (int c = 0; c < C; ++c) lv0[c] = p.lh_in[bd0 + c];
+    } else {
+      load_vec<E, C>(p.lv + base1, lv0);
+    }
+  }
   float agg[NF];
   M::identity(agg);
   if (t0 == 0 && dok) fold_h0<C>(agg, lv0);
@@ -364,10 +377,18 @@ __global__ void __launch_bounds__(NW * 32, 2) bwd_direct_kernel(Args<E> p) {
   const size_t base1 = (size_t)bi * (p.T_ + 1) * p.D + d0;
 
   float lc[S][C], lv[S][C], g[S][C], lv0[C];
+  const size_t bd0 = (size_t)bi * p.D + d0;  // (B, D) index of this lane's first channel
   load_steps<E, C, S>(p.lc, base, t0, p.T_, p.D, dok, 0.f, lc);
   load_steps<E, C, S>(p.lv, base1 + p.D, t0, p.T_, p.D, dok, -INFINITY, lv);
   load_steps<E, C, S>(p.gh, base, t0, p.T_, p.D, dok, 0.f, g);
-  if (t0 == 0 && dok) load_vec<E, C>(p.lv + base1, lv0);
+  if (t0 == 0 && dok) {
+    if (p.lh_in != nullptr) {
+#pragma unroll
+      for (int c = 0; c < C; ++c) lv0[c] = p.lh_in[bd0 + c];
+    } else {
+      load_vec<E, C>(p.lv + base1, lv0);
+    }
+  }
   float fagg[NFF], ragg[NFR];
   FM::identity(fagg);
   if (t0 == 0 && dok) fold_h0<C>(fagg, lv0);
@@ -389,8 +410,16 @@ __global__ void __launch_bounds__(NW * 32, 2) bwd_direct_kernel(Args<E> p) {
       for (int f = 0; f < NFR; ++f) w_[f] = s_ragg[w][f][lane];
       combine_into<RM, NFR>(tot, w_);
     }
-    float ex[NFR];
-    warp_lookback_win<RM, NFR>(p.lb, tile, p.nstrips, rchunk, tot, ex);
+    float ex[NFR], seed[NFR];
+    const bool seeded = p.y_in != nullptr && rchunk == 0;
+    if (seeded) {  // the adjoint Y entering from later slices
+#pragma unroll
+      for (int c = 0; c < C; ++c) {
+        seed[c] = 1.f;
+        seed[C + c] = dok ? p.y_in[bd0 + c] : 0.f;
+      }
+    }
+    warp_lookback_win<RM, NFR>(p.lb, tile, p.nstrips, rchunk, tot, ex, seeded ? seed : nullptr);
 #pragma unroll
     for (int f = 0; f < NFR; ++f) s_rex[f][lane] = ex[f];
   } else if (warp == 1) {
@@ -734,7 +763,8 @@ __global__ void __launch_bounds__(32 * W, 16 / W)
   const bool cok = d0 + c < p.D;
   const float lv0 = !cok ? 0.f
                     : GATE ? to_f32<E>(p.lh0[(size_t)bi * p.D + d0 + c])
-                           : to_f32<E>(p.lv[(size_t)bi * (p.T_ + 1) * p.D + d0 + c]);
+                    : p.lh_in != nullptr ? p.lh_in[(size_t)bi * p.D + d0 + c]
+                                         : to_f32<E>(p.lv[(size_t)bi * (p.T_ + 1) * p.D + d0 + c]);
   col_fetch<E, W, 2, GATE ? 0 : 1>(maps, sm, p.T_, d0, bi);
   int start, n;
   col_segment<W>(p.T_, s, start, n);
@@ -814,7 +844,8 @@ __device__ __forceinline__ void col_bwd_body(const Args<E>& p, const ColSmem<E, 
   float Pe = __shfl_down_sync(0xffffffffu, P, W), Qe = __shfl_down_sync(0xffffffffu, Q, W);
   if (j == SPW - 1) { Pe = 1.f; Qe = 0.f; }
   const float xin = col_scan_fwd<M, W>(A, B, s0, sm.tot);  // synchronises the CTA
-  float y = 0.f;
+  // adjoint entering from beyond T (another slice's, in sequence-parallel use)
+  float y = (!GATE && p.y_in != nullptr && cok) ? p.y_in[(size_t)(row0 / (p.T_ + 1) / p.D) * p.D + (row0 % p.D)] : 0.f;
   for (int v = W - 1; v > w; --v) y = fmaf(rtot[v * W + c], y, rtot[W * W + v * W + c]);
   y = fmaf(Pe, y, Qe);
 
@@ -885,7 +916,10 @@ __global__ void __launch_bounds__(32 * W, 16 / W)
   const int lane = threadIdx.x & 31, c = lane % W, s = (threadIdx.x >> 5) * (32 / W) + lane / W;
   const bool cok = d0 + c < p.D;
   const size_t row0 = GATE ? (size_t)bi * p.D + d0 + c : (size_t)bi * (p.T_ + 1) * p.D + d0 + c;
-  const float lv0 = cok ? to_f32<E>(GATE ? p.lh0[row0] : p.lv[row0]) : 0.f;
+  const float lv0 = !cok ? 0.f
+                    : GATE ? to_f32<E>(p.lh0[row0])
+                    : p.lh_in != nullptr ? p.lh_in[(size_t)bi * p.D + d0 + c]
+                                         : to_f32<E>(p.lv[row0]);
   col_fetch<E, W, 3, GATE ? 0 : 1>(maps, sm, p.T_, d0, bi);
   int start, n;
   col_segment<W>(p.T_, s, start, n);
@@ -1002,7 +1036,9 @@ __global__ void __launch_bounds__((kStripNW + 1) * 32)
     const bool dok = d < p.D;
     const size_t base = (size_t)bi * p.T_ * p.D + d;
     const size_t base1 = (size_t)bi * (p.T_ + 1) * p.D + d;
-    float carry[NF] = {-INFINITY, dok ? to_f32<E>(p.lv[base1]) : -INFINITY};
+    float carry[NF] = {-INFINITY,
+                       !dok ? -INFINITY
+                            : (p.lh_in != nullptr ? p.lh_in[(size_t)bi * p.D + d] : to_f32<E>(p.lv[base1]))};
     for (long long chunk = 0; chunk < p.nchunks; ++chunk) {
       const bool ok = mbar_wait(&full[s], ph, p.lb.err);
       if (bar_any(1, NW * 32, !ok)) return;
@@ -1077,9 +1113,11 @@ __global__ void __launch_bounds__((kStripNW + 1) * 32)
     const bool dok = d < p.D;
     const size_t base = (size_t)bi * p.T_ * p.D + d;
     const size_t base1 = (size_t)bi * (p.T_ + 1) * p.D + d;
-    float lv0[1] = {dok ? to_f32<E>(p.lv[base1]) : -INFINITY};
+    float lv0[1] = {!dok ? -INFINITY
+                         : (p.lh_in != nullptr ? p.lh_in[(size_t)bi * p.D + d] : to_f32<E>(p.lv[base1]))};
     float rcarry[2];
     RM::identity(rcarry);
+    if (p.y_in != nullptr && dok) rcarry[1] = p.y_in[(size_t)bi * p.D + d];  // from later slices
     for (long long q = 0; q < p.nchunks; ++q) {
       const long long chunk = p.nchunks - 1 - q;
       const bool ok = mbar_wait(&full[s], ph, p.lb.err);
@@ -1155,7 +1193,8 @@ inline size_t workspace_bytes(const Geometry& g) {
 template <typename E>
 int run(bool fwd, const void* lc, const void* lv, void* h, const void* gh, void* dlc, void* dlv,
         void* carries, long long B, long long T, long long D, int dtype, void* ws,
-        size_t ws_bytes, cudaStream_t st) {
+        size_t ws_bytes, cudaStream_t st, const float* lh_in = nullptr,
+        const float* y_in = nullptr) {
   const Geometry g = geometry(B, T, D, dtype);
   if (g.ntiles == 0) {
     // T == 0: the only gradient is dlv[:, 0] = 0 (h_0 feeds no output).
@@ -1171,7 +1210,9 @@ int run(bool fwd, const void* lc, const void* lv, void* h, const void* gh, void*
     if (q != nullptr && !aligned(q, va)) return MGS_BAD_ALIGNMENT;
   if (!aligned(ws, 256) || (carries != nullptr && !aligned(carries, 16))) return MGS_BAD_ALIGNMENT;
   if (!fwd && carries == nullptr && g.algo != kColumn) return MGS_BAD_SHAPE;
-  Args<E> p;
+  Args<E> p{};
+  p.lh_in = lh_in;
+  p.y_in = y_in;
   p.lc = static_cast<const E*>(lc);
   p.lv = static_cast<const E*>(lv);
   p.h = static_cast<E*>(h);
@@ -1248,16 +1289,21 @@ int run(bool fwd, const void* lc, const void* lv, void* h, const void* gh, void*
 
 int dispatch(bool fwd, const void* lc, const void* lv, void* h, const void* gh, void* dlc,
              void* dlv, void* carries, long long B, long long T, long long D, int dtype, void* ws,
-             size_t ws_bytes, cudaStream_t st) {
+             size_t ws_bytes, cudaStream_t st, const float* lh_in = nullptr,
+             const float* y_in = nullptr) {
   if (B < 0 || T < 0 || D < 0) return MGS_BAD_SHAPE;
+  if ((lh_in != nullptr && !aligned(lh_in, 4)) || (y_in != nullptr && !aligned(y_in, 4)))
+    return MGS_BAD_ALIGNMENT;
   switch (dtype) {
     case MGS_F32:
-      return run<float>(fwd, lc, lv, h, gh, dlc, dlv, carries, B, T, D, dtype, ws, ws_bytes, st);
+      return run<float>(fwd, lc, lv, h, gh, dlc, dlv, carries, B, T, D, dtype, ws, ws_bytes, st,
+                        lh_in, y_in);
     case MGS_BF16:
       return run<__nv_bfloat16>(fwd, lc, lv, h, gh, dlc, dlv, carries, B, T, D, dtype, ws,
-                                ws_bytes, st);
+                                ws_bytes, st, lh_in, y_in);
     case MGS_F16:
-      return run<__half>(fwd, lc, lv, h, gh, dlc, dlv, carries, B, T, D, dtype, ws, ws_bytes, st);
+      return run<__half>(fwd, lc, lv, h, gh, dlc, dlv, carries, B, T, D, dtype, ws, ws_bytes, st,
+                         lh_in, y_in);
     default:
       return MGS_BAD_DTYPE;
   }
@@ -1452,6 +1498,26 @@ int mgs_log_scan_fwd(const void* log_coeffs, const void* log_values, void* h, vo
   return mgs::logscan::dispatch(true, log_coeffs, log_values, h, nullptr, nullptr, nullptr,
                                 carries, B, T, D, dtype, workspace, workspace_bytes,
                                 static_cast<cudaStream_t>(stream));
+}
+
+int mgs_log_scan_fwd_fixup(const void* log_coeffs, const void* log_values, const float* log_h_in,
+                           void* h, void* carries, int64_t B, int64_t T, int64_t D, int dtype,
+                           void* workspace, size_t workspace_bytes, void* stream) {
+  if (log_h_in == nullptr) return MGS_BAD_SHAPE;
+  return mgs::logscan::dispatch(true, log_coeffs, log_values, h, nullptr, nullptr, nullptr,
+                                carries, B, T, D, dtype, workspace, workspace_bytes,
+                                static_cast<cudaStream_t>(stream), log_h_in, nullptr);
+}
+
+int mgs_log_scan_bwd_fixup(const void* log_coeffs, const void* log_values, const float* log_h_in,
+                           const void* grad_h, const void* carries, const float* adjoint_in,
+                           void* dlog_coeffs, void* dlog_values, int64_t B, int64_t T, int64_t D,
+                           int dtype, void* workspace, size_t workspace_bytes, void* stream) {
+  if (log_h_in == nullptr || adjoint_in == nullptr) return MGS_BAD_SHAPE;
+  return mgs::logscan::dispatch(false, log_coeffs, log_values, nullptr, grad_h, dlog_coeffs,
+                                dlog_values, const_cast<void*>(carries), B, T, D, dtype,
+                                workspace, workspace_bytes, static_cast<cudaStream_t>(stream),
+                                log_h_in, adjoint_in);
 }
 
 size_t mgs_log_gate_scan_workspace_size(int64_t B, int64_t T, int64_t D, int dtype) {

@@ -1,7 +1,10 @@
 """Multi-rank host logic on CPU (gloo, world_size 2 and 4): the
-sequence-parallel linear scan (carry all-gather + fix-up, and its backward
-through the differentiable all-gather) equals the single-device scan, batch
-sharding partitions rows, and failures surface as errors on every rank."""
+sequence-parallel linear and log scans (per-slice carries, all-gather,
+prefix / suffix composition, scans from the carried-in state, and the
+backward's reverse carries) equal the single-device scans, batch sharding
+partitions rows, and failures surface as errors on every rank. The
+per-slice operations are the torch restatements of tests/sp_torch_ops.py
+(the GPU tests run the kernels)."""
 
 from __future__ import annotations
 
@@ -12,6 +15,8 @@ import pytest
 import torch
 import torch.distributed as dist
 import torch.multiprocessing as mp
+
+from sp_torch_ops import TorchOps
 
 
 def _ref_scan(a, b):
@@ -57,7 +62,7 @@ def _sp_worker(rank, world, port, q):
         sl = slice(rank * per, (rank + 1) * per)
         a = a_full[:, sl].clone().requires_grad_(True)
         b = b_full[:, sl].clone().requires_grad_(True)
-        A, Bc = sp_linear_scan(a, b, scan_fn=_ref_scan)
+        A, Bc = sp_linear_scan(a, b, ops=TorchOps())
         torch.autograd.backward([A, Bc], [gA[:, sl], gB[:, sl]])
         # single-device reference
         af = a_full.clone().requires_grad_(True)
@@ -72,6 +77,53 @@ def _sp_worker(rank, world, port, q):
         q.put((rank, False, repr(e)))
 
 
+def _ref_log_scan(lc, lv):
+    x = lv[:, 0]
+    hs = []
+    for t in range(lc.shape[1]):
+        x = torch.logaddexp(x + lc[:, t], lv[:, t + 1])
+        hs.append(torch.exp(x))
+    return torch.stack(hs, 1)
+
+
+def _sp_log_worker(rank, world, port, q):
+    try:
+        _init(rank, world, port)
+        from mingru_b200.parallel import sp_parallel_scan_log
+
+        g = torch.Generator().manual_seed(1)
+        B, T, D = 2, 10 * world, 4
+        k = torch.randn(B, T, D, generator=g, dtype=torch.float64)
+        lc_full = -torch.nn.functional.softplus(k)
+        lv_full = torch.cat([torch.randn(B, 1, D, generator=g, dtype=torch.float64) * 0.1,
+                             -torch.nn.functional.softplus(-k)
+                             + torch.randn(B, T, D, generator=g, dtype=torch.float64) * 0.3], 1)
+        gh = torch.randn(B, T, D, generator=g, dtype=torch.float64)
+        per = T // world
+        sl = slice(rank * per, (rank + 1) * per)
+        lc = lc_full[:, sl].clone().requires_grad_(True)
+        lv_local = lv_full[:, rank * per:(rank + 1) * per + 1].clone()
+        if rank > 0:
+            lv_local[:, 0] = 123.0  # slot 0 is read on rank 0 only
+        lv = lv_local.requires_grad_(True)
+        h = sp_parallel_scan_log(lc, lv, ops=TorchOps())
+        h.backward(gh[:, sl])
+        lcf = lc_full.clone().requires_grad_(True)
+        lvf = lv_full.clone().requires_grad_(True)
+        hr = _ref_log_scan(lcf, lvf)
+        hr.backward(gh)
+        want_dlv = lvf.grad[:, rank * per:(rank + 1) * per + 1].clone()
+        if rank > 0:
+            want_dlv[:, 0] = 0.0
+        ok = (torch.allclose(h, hr[:, sl]) and torch.allclose(lc.grad, lcf.grad[:, sl])
+              and torch.allclose(lv.grad[:, 1:], want_dlv[:, 1:])
+              and torch.allclose(lv.grad[:, 0], want_dlv[:, 0]))
+        q.put((rank, ok, None))
+        dist.destroy_process_group()
+    except Exception as e:  # pragma: no cover - reported through the queue
+        q.put((rank, False, repr(e)))
+
+
 def _mismatch_worker(rank, world, port, q):
     try:
         _init(rank, world, port)
@@ -80,7 +132,7 @@ def _mismatch_worker(rank, world, port, q):
         T = 8 if rank == 0 else 9  # ranks disagree on the slice length
         a = torch.rand(2, T, 3)
         try:
-            sp_linear_scan(a, a, scan_fn=_ref_scan)
+            sp_linear_scan(a, a, ops=TorchOps())
             q.put((rank, False, "no error"))
         except ValueError as e:
             q.put((rank, "different shapes" in str(e), None))
@@ -100,7 +152,7 @@ def _dead_rank_worker(rank, world, port, q):
         if rank == 1:
             raise RuntimeError("injected failure on rank 1")
         try:
-            sp_linear_scan(a, a, scan_fn=_ref_scan)
+            sp_linear_scan(a, a, ops=TorchOps())
             q.put((rank, False, "collective completed without rank 1"))
         except Exception:  # gloo reports the lost peer / timeout
             q.put((rank, True, None))
@@ -126,6 +178,12 @@ def _run(fn, world):
 @pytest.mark.parametrize("world", [2, 4])
 def test_sequence_parallel_matches_single_device(world):
     res = _run(_sp_worker, world)
+    assert all(ok for _, ok, _ in res), res
+
+
+@pytest.mark.parametrize("world", [2, 4])
+def test_sequence_parallel_log_matches_single_device(world):
+    res = _run(_sp_log_worker, world)
     assert all(ok for _, ok, _ in res), res
 
 

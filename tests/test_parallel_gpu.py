@@ -1,6 +1,7 @@
-"""Sequence-parallel linear_scan with the CUDA kernel over NCCL (needs >= 2
-GPUs; skipped otherwise): every rank's slice of the forward outputs and of
-the input gradients equals the single-GPU full-length scan."""
+"""Sequence-parallel linear_scan and parallel_scan_log with the CUDA kernels
+over NCCL (needs >= 2 GPUs; skipped otherwise): every rank's slice of the
+forward outputs and of the input gradients equals the single-GPU
+full-length scan."""
 
 from __future__ import annotations
 
@@ -31,7 +32,7 @@ def _worker(rank, world, port, q):
         dist.init_process_group("nccl", rank=rank, world_size=world,
                                 timeout=datetime.timedelta(seconds=60), device_id=dev)
         import mingru_b200 as mb
-        from mingru_b200.parallel import sp_linear_scan
+        from mingru_b200.parallel import sp_linear_scan, sp_parallel_scan_log
 
         g = torch.Generator().manual_seed(0)
         B, T, D = 4, 512 * world, 256
@@ -52,6 +53,23 @@ def _worker(rank, world, port, q):
         ok = (torch.allclose(A, Ar[:, sl], **tol) and torch.allclose(Bc, Br[:, sl], **tol)
               and torch.allclose(al.grad, af.grad[:, sl], rtol=1e-4, atol=1e-4)
               and torch.allclose(bl.grad, bf.grad[:, sl], rtol=1e-4, atol=1e-4))
+        # parallel_scan_log: log h_0 in slot 0 of rank 0's log values
+        k = torch.randn(B, T, D, generator=g).to(dev)
+        lc = -torch.nn.functional.softplus(k)
+        lv = torch.cat([torch.full((B, 1, D), -0.7, device=dev),
+                        -torch.nn.functional.softplus(-k) + 0.3 * torch.randn(B, T, D, generator=g).to(dev)], 1)
+        gh = torch.randn(B, T, D, generator=g).to(dev)
+        lcl = lc[:, sl].clone().requires_grad_(True)
+        lvl = lv[:, sl.start:sl.stop + 1].clone().requires_grad_(True)
+        h = sp_parallel_scan_log(lcl, lvl)
+        h.backward(gh[:, sl])
+        lcf, lvf = lc.clone().requires_grad_(True), lv.clone().requires_grad_(True)
+        hr = mb.parallel_scan_log(lcf, lvf)
+        hr.backward(gh)
+        ok = ok and (torch.allclose(h, hr[:, sl], **tol)
+                     and torch.allclose(lcl.grad, lcf.grad[:, sl], rtol=1e-4, atol=1e-4)
+                     and torch.allclose(lvl.grad[:, 1:], lvf.grad[:, sl.start + 1:sl.stop + 1],
+                                        rtol=1e-4, atol=1e-4))
         dist.barrier(device_ids=[rank])
         dist.destroy_process_group()
         q.put((rank, ok, None))
