@@ -513,6 +513,65 @@ class DeltaWorkload(ScanWorkload):
         delta_oracle.delta_backward(Q, K, V, beta, H0, gy, gHT, self.chunk)
 
 
+class GatedDeltaWorkload(DeltaWorkload):
+    """Config 5's delta rule with per-token decay active (the reference runs
+    _forward_chunked_gated in eager torch only): log gamma = -lambda dt with
+    lambda = softplus(0) per head and dt ~ U(0, 2). Same tensors and bytes as
+    config 5 plus the (B, H, T) log decay read and its gradient written."""
+
+    kernels = {"fwd": "delta_gated_fwd", "bwd": "delta_gated_bwd"}
+    workload = "DeltaMinGRU chunked-WY with decay fwd+bwd (BASELINE config 5 shape, bf16 in)"
+    compute_dtype = "f32"  # CUDA-core kernels, fp32 arithmetic
+
+    def make_host(self, rows, seed):
+        ins, cots = super().make_host(rows, seed)
+        g = torch.Generator().manual_seed(100 + seed)
+        lg = -math.log(2.0) * torch.rand(rows, self.H, self.T, generator=g) * 2
+        return ins + [lg], cots
+
+    def device_setup(self, host, dev):
+        ins, cots = host
+        st = {"ins": [x.to(dev).requires_grad_(True) for x in ins[:4]] +
+                     [ins[4].to(dev, torch.float32).requires_grad_(True)],
+              "cots": [cots[0].to(dev), cots[1].to(dev, torch.float32)]}
+        self.H0 = torch.zeros(self.B, self.H, self.d, self.d, device=dev)
+        return st
+
+    def forward(self, Q, K, V, beta, lg):
+        import mingru_b200 as mb
+
+        H0 = self.H0 if self.H0.shape[0] == Q.shape[0] else torch.zeros(
+            Q.shape[0], self.H, self.d, self.d, device=Q.device)
+        return mb.delta_gated_scan_impl(Q, K, V, beta, H0, lg, chunk_size=self.chunk)
+
+    def e2e_setup(self, host, dev):
+        ins, cots = host
+        st = ScanWorkload.e2e_setup(self, (ins[:4], [cots[0]]), dev)
+        st["lg"] = ins[4].to(dev, torch.float32)
+        st["dHT"] = torch.zeros(self.B, self.H, self.d, self.d, device=dev)
+        return st
+
+    def e2e_compute(self, st, ins, cots):
+        y, HT = self.forward(*ins, st["lg"])
+        grads = torch.autograd.grad((y, HT), ins, (cots[0], st["dHT"]))
+        return [y] + list(grads)
+
+    cpu_heads = 1
+
+    def cpu_sample(self, rows: int):
+        (Q, K, V, beta, lg), (gy, gHT) = self.make_host(rows, seed=0)
+        h = self.cpu_heads
+        return ([Q[:, :h].numpy(), K[:, :h].numpy(), V[:, :h].numpy(), beta[:, :h].numpy(),
+                 lg[:, :h].numpy()], [gy[:, :h].numpy(), gHT[:, :h].numpy()])
+
+    def cpu_step(self, sample):
+        from oracle import delta_oracle
+
+        (Q, K, V, beta, lg), (gy, gHT) = sample
+        H0 = np.zeros((Q.shape[0], Q.shape[1], self.d, self.d))
+        delta_oracle.gated_sequential_torch(Q, K, V, beta, H0, lg, gy, gHT)
+
+
 WORKLOADS = {
     "cfg1": lambda: LogScanWorkload(),
     "cfg1-gate": lambda: GateScanWorkload(name="cfg1-gate"),
@@ -524,6 +583,7 @@ WORKLOADS = {
     # BASELINE config 5's multi-GPU case: global batch 64 (with --scaling strong,
     # split 32 / 16 / 8 per GPU over 2 / 4 / 8 GPUs)
     "cfg5-b64": lambda: DeltaWorkload(B=64, name="cfg5-b64"),
+    "cfg5-gated": lambda: GatedDeltaWorkload(name="cfg5-gated"),
 }
 
 
@@ -1109,6 +1169,113 @@ def run_stack(args) -> None:
     print(json.dumps(line), flush=True)
 
 
+def run_sp(args) -> None:
+    """Sequence-parallel scan on one GPU, the time axis cut into --sp-slices
+    slices and every slice's per-rank work run in turn (carry summaries, the
+    prefix / suffix composition of the gathered summaries, the scans from the
+    carried-in states), the all-gathers replaced by stacking. Reports the whole
+    sequence's fwd+bwd time through the sliced path next to the one-launch
+    scan, i.e. what sequence parallelism costs in kernel work before any
+    NCCL time (config 2 shape for linear_scan, config 1 for parallel_scan_log)."""
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    import mingru_b200 as mb
+    from mingru_b200.parallel import (KernelOps, linear_prefix, linear_suffix, log_prefix,
+                                      log_suffix)
+
+    n = args.sp_slices
+    ops = KernelOps()
+    g = torch.Generator(device=dev).manual_seed(0)
+    if args.config == "cfg2-sp":
+        B, T, D = 16, 4096, 1024
+        a = torch.tanh(torch.randn(B, T, D, device=dev, generator=g))
+        b = torch.randn(B, T, D, device=dev, generator=g)
+        gA = torch.zeros(B, T, D, device=dev)
+        gB = torch.randn(B, T, D, device=dev, generator=g)
+        per = T // n
+        sl = [slice(r * per, (r + 1) * per) for r in range(n)]
+        ta, tb = a.clone().requires_grad_(True), b.clone().requires_grad_(True)
+
+        def plain():
+            A, Bc = mb.linear_scan(ta, tb)
+            return torch.autograd.grad((A, Bc), (ta, tb), (gA, gB))
+
+        def sliced():
+            G = torch.stack([ops.linear_carry_fwd(a[:, s], b[:, s]) for s in sl])
+            outs = [ops.linear_fwd_fixup(a[:, s], b[:, s], linear_prefix(G, r)) for r, s in enumerate(sl)]
+            R = torch.stack([ops.linear_carry_bwd(a[:, s], gA[:, s], gB[:, s]) for s in sl])
+            return [ops.linear_bwd_fixup(a[:, s], b[:, s], outs[r][2], linear_suffix(R, r),
+                                         gA[:, s], gB[:, s]) for r, s in enumerate(sl)]
+        workload, nbytes = "linear_scan fwd+bwd, config 2 shape", 40 * B * T * D
+    else:
+        B, T, D = 8, 1024 * n, 256
+        k = torch.randn(B, T, D, device=dev, generator=g)
+        lc = -torch.nn.functional.softplus(k)
+        lv = torch.cat([torch.full((B, 1, D), -87.0, device=dev),
+                        -torch.nn.functional.softplus(-k) + mb.log_g(torch.randn(B, T, D, device=dev, generator=g))], 1)
+        gh = torch.randn(B, T, D, device=dev, generator=g)
+        per = T // n
+        sl = [slice(r * per, (r + 1) * per) for r in range(n)]
+        tlc, tlv = lc.clone().requires_grad_(True), lv.clone().requires_grad_(True)
+
+        def plain():
+            h = mb.parallel_scan_log(tlc, tlv)
+            return torch.autograd.grad(h, (tlc, tlv), gh)
+
+        def sliced():
+            lvs = [lv[:, s.start:s.stop + 1] for s in sl]
+            G = torch.stack([torch.cat([ops.log_carry_fwd(lc[:, s], lvs[r]), lvs[r][:, 0].float()[None]])
+                             for r, s in enumerate(sl)])
+            outs = []
+            for r, s in enumerate(sl):
+                lh = log_prefix(G, r)
+                outs.append((lh,) + tuple(ops.log_fwd_fixup(lc[:, s], lvs[r], lh)))
+            R = torch.stack([ops.log_carry_bwd(lc[:, s], gh[:, s]) for s in sl])
+            return [ops.log_bwd_fixup(lc[:, s], lvs[r], outs[r][0], outs[r][2], log_suffix(R, r),
+                                      gh[:, s]) for r, s in enumerate(sl)]
+        workload, nbytes = f"parallel_scan_log fwd+bwd, config 1 shape x{n} in T", 32 * B * T * D
+    work = torch.cuda.Stream(dev)
+    work.wait_stream(torch.cuda.current_stream(dev))
+    with torch.cuda.stream(work):
+        for _ in range(args.warmup):
+            plain()
+            sliced()
+        gp, _kp = capture(plain, dev, stream=work)
+        gs, _ks = capture(sliced, dev, stream=work)
+        reps = max(10, args.steps)
+        with ClockSampler(dev.index) as clk:
+            clk.mark_start()
+            plain_ms = time_graph(gp, reps, dev)
+            sliced_ms = time_graph(gs, reps, dev)
+            clk.mark_stop()
+        mb.raise_device_error(dev)
+    elems = B * T * D
+    peaks, peak_kind = load_peaks()
+    line = {
+        "metric": "scan fwd+bwd Gelem/s, sequence-parallel slices on one GPU",
+        "value": elems / (sliced_ms * 1e-3) / 1e9,
+        "unit": "Gelem/s",
+        "n_gpus": 1,
+        "steps": reps,
+        "warmup": args.warmup,
+        "ms_per_step": sliced_ms,
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": "f32",
+        "data": "synthetic (seeded)",
+        "config": {"workload": workload, "B": B, "T": T, "D": D, "slices": n,
+                   "collectives": "none (all-gathers replaced by stacking on one GPU)"},
+        "one_launch_ms_per_step": plain_ms,
+        "one_launch_value": elems / (plain_ms * 1e-3) / 1e9,
+        "sliced_over_one_launch": sliced_ms / plain_ms,
+        "step_hbm_frac_one_launch": nbytes / (plain_ms * 1e-3) / 1e9 / peaks["hbm_gbs"],
+        "gpu_launches": None,
+        "clocks": clk.summary(),
+    }
+    print(json.dumps(line), flush=True)
+
+
 def run_stack_step(args) -> None:
     """MinGRUStack.step (the streaming / decoding path, one token per call for
     a batch of streams): tokens/s of the eager step loop and of the step
@@ -1243,8 +1410,11 @@ def main() -> None:
     ap.add_argument("--steps", type=int, default=1000)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--config", choices=sorted(WORKLOADS) + ["stack", "stack-step"],
+    ap.add_argument("--config", choices=sorted(WORKLOADS) + ["stack", "stack-step", "cfg1-sp",
+                                                              "cfg2-sp"],
                     default="cfg2")
+    ap.add_argument("--sp-slices", type=int, default=4,
+                    help="cfg1-sp / cfg2-sp: time slices (emulated ranks) on one GPU")
     ap.add_argument("--stack-batch", type=int, default=8)
     ap.add_argument("--stack-t", type=int, default=1024)
     ap.add_argument("--stack-d", type=int, default=512)
@@ -1266,6 +1436,13 @@ def main() -> None:
                     help="override the per-GPU batch (small ncu captures only; not a bench line)")
     args = ap.parse_args()
     args.warmup = max(3, args.warmup)  # timing rule: at least 3 untimed warm-up steps
+    if args.config in ("cfg1-sp", "cfg2-sp"):
+        if args.impl == "reference":
+            print(json.dumps({"impl": "reference", "unavailable": "the sliced scan has no "
+                              "reference CPU arm (the reference arm times the scan path)"}))
+            return
+        run_sp(args)
+        return
     if args.config in ("stack", "stack-step"):
         if args.impl == "reference":
             print(json.dumps({"impl": "reference", "unavailable": "the stack benches have no "

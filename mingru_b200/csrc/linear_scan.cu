@@ -465,8 +465,9 @@ __global__ void __launch_bounds__(NW * 32) bwd_direct_kernel(Args<E> p) {
 // interleaving them would pay a load latency per step.
 //
 // Rows past T arrive zero-filled (TMA out-of-bounds fill). They come after
-// every valid step of the strip, their results are clipped by the box stores,
-// and a zero row passes a zero adjoint, so they need no masking.
+// every valid step of the strip and their results are clipped by the box
+// stores; the backward walks only the valid rows of the chunk holding T's
+// end, so an adjoint carried in from a later slice reaches step T - 1 intact.
 
 constexpr int kWsWarps = 4;                  // warps (strips in flight) per CTA
 constexpr size_t kWsRingPerWarp = 50 * 1024; // shared memory per warp: ring + output buffers
@@ -699,21 +700,36 @@ __global__ void __launch_bounds__(NW * 32, 1)
           fA *= a;
         }
         // Reverse walk in groups of kGrp steps, each group's inputs read first.
+        // In the chunk holding T's end, the zero-filled rows past T must not
+        // touch the adjoint (it may carry another slice's adjoint in).
         constexpr int kGrp = 8;
+        const long long nvalid = p.T_ - (io * NH + h) * kLc;
+        if (nvalid >= kLc) {
 #pragma unroll
-        for (int g = kLc / kGrp - 1; g >= 0; --g) {
-          E va[kGrp], vga[kGrp], vgb[kGrp];
+          for (int g = kLc / kGrp - 1; g >= 0; --g) {
+            E va[kGrp], vga[kGrp], vgb[kGrp];
 #pragma unroll
-          for (int k = 0; k < kGrp; ++k) {
-            va[k] = sa[(g * kGrp + k) * 32];
-            vga[k] = sga[(g * kGrp + k) * 32];
-            vgb[k] = sgb[(g * kGrp + k) * 32];
+            for (int k = 0; k < kGrp; ++k) {
+              va[k] = sa[(g * kGrp + k) * 32];
+              vga[k] = sga[(g * kGrp + k) * 32];
+              vgb[k] = sgb[(g * kGrp + k) * 32];
+            }
+#pragma unroll
+            for (int k = kGrp - 1; k >= 0; --k) {
+              const int i = g * kGrp + k;
+              const float a = to_f32<E>(va[k]);
+              const float GA = to_f32<E>(vga[k]) + ya, GB = to_f32<E>(vgb[k]) + yb;
+              ya = a * GA;
+              yb = a * GB;
+              oA[i * 32] = from_f32<E>(fmaf(GA, ap[i], GB * bp[i]));
+              oB[i * 32] = from_f32<E>(GB);
+            }
           }
-#pragma unroll
-          for (int k = kGrp - 1; k >= 0; --k) {
-            const int i = g * kGrp + k;
-            const float a = to_f32<E>(va[k]);
-            const float GA = to_f32<E>(vga[k]) + ya, GB = to_f32<E>(vgb[k]) + yb;
+        } else {
+#pragma unroll 1
+          for (int i = (int)nvalid - 1; i >= 0; --i) {
+            const float a = to_f32<E>(sa[i * 32]);
+            const float GA = to_f32<E>(sga[i * 32]) + ya, GB = to_f32<E>(sgb[i * 32]) + yb;
             ya = a * GA;
             yb = a * GB;
             oA[i * 32] = from_f32<E>(fmaf(GA, ap[i], GB * bp[i]));
