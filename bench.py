@@ -1200,12 +1200,15 @@ def run_sp(args) -> None:
             A, Bc = mb.linear_scan(ta, tb)
             return torch.autograd.grad((A, Bc), (ta, tb), (gA, gB))
 
+        # each emulated rank holds its slice contiguously, as a real rank would
+        al, bl, gAl, gBl = ([x[:, s].contiguous() for s in sl] for x in (a, b, gA, gB))
+
         def sliced():
-            G = torch.stack([ops.linear_carry_fwd(a[:, s], b[:, s]) for s in sl])
-            outs = [ops.linear_fwd_fixup(a[:, s], b[:, s], linear_prefix(G, r)) for r, s in enumerate(sl)]
-            R = torch.stack([ops.linear_carry_bwd(a[:, s], gA[:, s], gB[:, s]) for s in sl])
-            return [ops.linear_bwd_fixup(a[:, s], b[:, s], outs[r][2], linear_suffix(R, r),
-                                         gA[:, s], gB[:, s]) for r, s in enumerate(sl)]
+            G = torch.stack([ops.linear_carry_fwd(al[r], bl[r]) for r in range(n)])
+            outs = [ops.linear_fwd_fixup(al[r], bl[r], linear_prefix(G, r)) for r in range(n)]
+            R = torch.stack([ops.linear_carry_bwd(al[r], gAl[r], gBl[r]) for r in range(n)])
+            return [ops.linear_bwd_fixup(al[r], bl[r], outs[r][2], linear_suffix(R, r), gAl[r],
+                                         gBl[r]) for r in range(n)]
         workload, nbytes = "linear_scan fwd+bwd, config 2 shape", 40 * B * T * D
     else:
         B, T, D = 8, 1024 * n, 256
@@ -1222,17 +1225,21 @@ def run_sp(args) -> None:
             h = mb.parallel_scan_log(tlc, tlv)
             return torch.autograd.grad(h, (tlc, tlv), gh)
 
+        # each emulated rank holds its slice contiguously, as a real rank would
+        lcl = [lc[:, s].contiguous() for s in sl]
+        lvl = [lv[:, s.start:s.stop + 1].contiguous() for s in sl]
+        ghl = [gh[:, s].contiguous() for s in sl]
+
         def sliced():
-            lvs = [lv[:, s.start:s.stop + 1] for s in sl]
-            G = torch.stack([torch.cat([ops.log_carry_fwd(lc[:, s], lvs[r]), lvs[r][:, 0].float()[None]])
-                             for r, s in enumerate(sl)])
+            G = torch.stack([torch.cat([ops.log_carry_fwd(lcl[r], lvl[r]), lvl[r][:, 0].float()[None]])
+                             for r in range(n)])
             outs = []
-            for r, s in enumerate(sl):
+            for r in range(n):
                 lh = log_prefix(G, r)
-                outs.append((lh,) + tuple(ops.log_fwd_fixup(lc[:, s], lvs[r], lh)))
-            R = torch.stack([ops.log_carry_bwd(lc[:, s], gh[:, s]) for s in sl])
-            return [ops.log_bwd_fixup(lc[:, s], lvs[r], outs[r][0], outs[r][2], log_suffix(R, r),
-                                      gh[:, s]) for r, s in enumerate(sl)]
+                outs.append((lh,) + tuple(ops.log_fwd_fixup(lcl[r], lvl[r], lh)))
+            R = torch.stack([ops.log_carry_bwd(lcl[r], ghl[r]) for r in range(n)])
+            return [ops.log_bwd_fixup(lcl[r], lvl[r], outs[r][0], outs[r][2], log_suffix(R, r),
+                                      ghl[r]) for r in range(n)]
         workload, nbytes = f"parallel_scan_log fwd+bwd, config 1 shape x{n} in T", 32 * B * T * D
     work = torch.cuda.Stream(dev)
     work.wait_stream(torch.cuda.current_stream(dev))

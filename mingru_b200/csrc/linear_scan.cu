@@ -725,15 +725,17 @@ __global__ void __launch_bounds__(NW * 32, 1)
               oB[i * 32] = from_f32<E>(GB);
             }
           }
-        } else {
-#pragma unroll 1
-          for (int i = (int)nvalid - 1; i >= 0; --i) {
-            const float a = to_f32<E>(sa[i * 32]);
-            const float GA = to_f32<E>(sga[i * 32]) + ya, GB = to_f32<E>(sgb[i * 32]) + yb;
-            ya = a * GA;
-            yb = a * GB;
-            oA[i * 32] = from_f32<E>(fmaf(GA, ap[i], GB * bp[i]));
-            oB[i * 32] = from_f32<E>(GB);
+        } else {  // unrolled with a predicate, so ap / bp keep static indices (registers)
+#pragma unroll
+          for (int i = kLc - 1; i >= 0; --i) {
+            if (i < nvalid) {
+              const float a = to_f32<E>(sa[i * 32]);
+              const float GA = to_f32<E>(sga[i * 32]) + ya, GB = to_f32<E>(sgb[i * 32]) + yb;
+              ya = a * GA;
+              yb = a * GB;
+              oA[i * 32] = from_f32<E>(fmaf(GA, ap[i], GB * bp[i]));
+              oB[i * 32] = from_f32<E>(GB);
+            }
           }
         }
       }
