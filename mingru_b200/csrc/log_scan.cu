@@ -73,8 +73,10 @@ inline Geometry geometry(long long B, long long T, long long D, int dtype) {
   else
     g.algo = rows16 ? kDirectVec : kDirectScalar;
   g.cpt = g.algo == kDirectVec ? kVecCpt : 1;
-  if (g.algo == kColumn)  // 16-channel groups (64-byte fp32 rows) while they fill 3/4 of the SMs
-    g.cpt = 4 * B * ((D + 15) / 16) >= 3LL * sm_count() ? 16 : 8;
+  // Column path: 16-channel groups with 32 time segments each while those fill
+  // the SMs; otherwise 8-channel groups with 64 segments (twice the CTAs, half
+  // the serial chain per lane). Either way 512 threads per CTA.
+  if (g.algo == kColumn) g.cpt = B * ((D + 15) / 16) >= sm_count() ? 16 : 8;
   const long long w = g.algo == kColumn ? (long long)g.cpt : 32LL * g.cpt;
   g.sper = (D + w - 1) / w;
   g.nstrips = B * g.sper;
@@ -461,9 +463,9 @@ __global__ void __launch_bounds__(NW * 32, 2) bwd_direct_kernel(Args<E> p) {
 // One CTA per (batch row, W-channel group), W = 8 or 16, holds the whole time
 // axis (T <= 1024) in shared memory, brought in (and written back) by TMA
 // boxes of 256 rows x W channels; rows stay dense [t][channel]. The CTA has
-// 32 * W threads: lane (c = lane % W, j = lane / W) of warp w scans channel c
-// over segment s = w * SPW + j (SPW = 32 / W segments per warp, 32 segments per
-// channel). Segment starts are staggered (start = s*seg + s % SPW, seg a
+// NS * W threads: lane (c = lane % W, j = lane / W) of warp w scans channel c
+// over segment s = w * SPW + j (SPW = 32 / W segments per warp, NS segments per
+// channel: 32 for 16-channel groups, 64 for 8-channel groups). Segment starts are staggered (start = s*seg + s % SPW, seg a
 // multiple of 4), so at every step the lanes of a warp read distinct banks.
 // Segment aggregates combine by warp shuffles over j and through shared
 // memory over warps; each lane then replays its segment from the incoming
@@ -481,18 +483,25 @@ __global__ void __launch_bounds__(NW * 32, 2) bwd_direct_kernel(Args<E> p) {
 // product that underflows (< 2^-126) changes a result by < e^-30 relative.
 // Otherwise the CTA runs the log-space monoid (alpha, nu) of the other paths.
 
-constexpr int kColSegs = 32;    // segments per channel
+constexpr int kColSegs = 32;    // default segments per channel (NS)
 constexpr int kColBox = 256;    // rows per TMA box
 constexpr long long kColTmax = 1024;
-constexpr int kColMaxLen = (int)(kColTmax / kColSegs) + 1;
+// Longest segment of NS segments per channel (T <= kColTmax).
+template <int NS>
+constexpr int col_maxlen() { return (int)(kColTmax / NS) + 1; }
+constexpr int kColMaxLen = col_maxlen<kColSegs>();
 constexpr float kColLinLo = -30.f, kColLinHi = 20.f;  // linear-domain envelope of log values
+
+// Segments per channel of a W-channel group (see the geometry: 16 x 32 or 8 x 64).
+constexpr int col_segments(int W) { return W == 16 ? 32 : 64; }
 
 struct ColMaps {
   CUtensorMap m[5];  // fwd: lc, lv, h; bwd: lc, lv, gh, dlc, dlv
 };
 
+template <int NS = kColSegs>
 __host__ __device__ __forceinline__ int col_seg(long long T) {
-  int s = (int)((T + kColSegs - 1) / kColSegs);
+  int s = (int)((T + NS - 1) / NS);
   if (s < 4) s = 4;
   return (s + 3) & ~3;
 }
@@ -501,10 +510,12 @@ __host__ __device__ __forceinline__ int col_boxes(long long T) {
   return (int)((T + kColBox - 1) / kColBox);
 }
 
+// NS segments per channel: NS * W / 32 warps; the combine buffers hold
+// 4 x [warp][channel] floats.
 template <typename E>
-inline size_t col_smem_bytes(long long T, int ntensors, int W) {
+inline size_t col_smem_bytes(long long T, int ntensors, int W, int NS = kColSegs) {
   return 128 + (size_t)ntensors * col_boxes(T) * kColBox * W * sizeof(E) +
-         4 * (size_t)W * W * sizeof(float);
+         4 * (size_t)(NS * W / 32) * W * sizeof(float);
 }
 
 template <typename E, int W>
@@ -521,13 +532,13 @@ struct ColSmem {
   }
 };
 
-template <int W>
+template <int W, int NS = kColSegs>
 __device__ __forceinline__ void col_segment(long long T, int s, int& start, int& n) {
   constexpr int SPW = 32 / W;
-  const long long seg = col_seg(T);
+  const long long seg = col_seg<NS>(T);
   const long long a = min((long long)s * seg + (s % SPW), T);
   const long long b =
-      s == kColSegs - 1 ? T : min((long long)(s + 1) * seg + ((s + 1) % SPW), T);
+      s == NS - 1 ? T : min((long long)(s + 1) * seg + ((s + 1) % SPW), T);
   start = (int)a;
   n = (int)(b - a);
 }
@@ -632,11 +643,11 @@ __device__ __forceinline__ void gate_grads(float k, float x, float dlc, float dl
 
 // In place over this lane's segment: (k, x~) -> (log a, log b); bit i of the
 // returned mask is set where x~ < 0 (the branch of log_g, kept for the backward).
-template <typename E, int W>
+template <typename E, int W, int NS = kColSegs>
 __device__ __forceinline__ unsigned long long col_gate_prologue(E* lc, E* lv, int n) {
   unsigned long long neg = 0ull;
 #pragma unroll
-  for (int i = 0; i < kColMaxLen; ++i)
+  for (int i = 0; i < col_maxlen<NS>(); ++i)
     if (i < n) {
       const float k = cld<E, W>(lc, i), x = cld<E, W>(lv, i);
       float a, b;
@@ -649,11 +660,11 @@ __device__ __forceinline__ unsigned long long col_gate_prologue(E* lc, E* lv, in
 }
 
 // Does this lane's segment allow the linear-domain recurrence?
-template <typename E, int W>
+template <typename E, int W, int NS = kColSegs>
 __device__ __forceinline__ bool col_linear_ok(const E* lc, const E* lv, int n) {
   bool ok = true;
 #pragma unroll
-  for (int i = 0; i < kColMaxLen; ++i)
+  for (int i = 0; i < col_maxlen<NS>(); ++i)
     if (i < n) {
       const float c = cld<E, W>(lc, i), v = cld<E, W>(lv, i);
       ok &= (c <= 0.f) & (v >= kColLinLo) & (v <= kColLinHi);
@@ -679,14 +690,14 @@ struct ColLog {
 };
 
 // Forward aggregate of one segment (linear: caches a, b over lc, lv for fp32).
-template <typename E, int W, bool LIN, bool CACHE = true>
+template <typename E, int W, bool LIN, bool CACHE = true, int NS = kColSegs>
 __device__ __forceinline__ void col_fwd_agg(E* lc, E* lv, int n, bool first, float s0, float& A,
                                             float& B) {
   if (LIN) {
     A = first ? 0.f : 1.f;
     B = first ? s0 : 0.f;
 #pragma unroll
-    for (int i = 0; i < kColMaxLen; ++i)
+    for (int i = 0; i < col_maxlen<NS>(); ++i)
       if (i < n) {
         const float a = col_exp(cld<E, W>(lc, i)), b = col_exp(cld<E, W>(lv, i));
         if constexpr (CACHE && std::is_same<E, float>::value) {
@@ -721,9 +732,9 @@ __device__ __forceinline__ void col_ab(const E* lc, const E* lv, int i, float& a
 
 // Exclusive scan of segment elements over the CTA: returns the state entering
 // this lane's segment (s0 = state entering segment 0). `tot` holds 2 x [warp][channel].
-template <class M, int W>
+template <class M, int W, int NS = kColSegs>
 __device__ __forceinline__ float col_scan_fwd(float A, float B, float s0, float* tot) {
-  constexpr int SPW = 32 / W;
+  constexpr int SPW = 32 / W, NW = NS / SPW;  // segments per warp, warps
   const int lane = threadIdx.x & 31, w = threadIdx.x >> 5, c = lane % W, j = lane / W;
 #pragma unroll
   for (int off = W; off < 32; off <<= 1) {
@@ -733,7 +744,7 @@ __device__ __forceinline__ float col_scan_fwd(float A, float B, float s0, float*
   }
   if (j == SPW - 1) {
     tot[w * W + c] = A;
-    tot[W * W + w * W + c] = B;
+    tot[NW * W + w * W + c] = B;
   }
   float Ae = __shfl_up_sync(0xffffffffu, A, W), Be = __shfl_up_sync(0xffffffffu, B, W);
   if (j == 0) M::ident(Ae, Be);
@@ -741,7 +752,7 @@ __device__ __forceinline__ float col_scan_fwd(float A, float B, float s0, float*
   float Ap, Bp;
   M::ident(Ap, Bp);
   for (int v = 0; v < w; ++v) {  // prefix <- prefix then warp v
-    float tA = tot[v * W + c], tB = tot[W * W + v * W + c];
+    float tA = tot[v * W + c], tB = tot[NW * W + v * W + c];
     M::after(tA, tB, Ap, Bp);
     Ap = tA;
     Bp = tB;
@@ -752,8 +763,8 @@ __device__ __forceinline__ float col_scan_fwd(float A, float B, float s0, float*
 
 // GATE: the MinGRU gate-fused form (maps 0, 1 = k, x~ (B, T, D); log h_0 from
 // p.lh0): each lane turns its segment's k, x~ into log a, log b in place first.
-template <typename E, int W, bool GATE = false>
-__global__ void __launch_bounds__(32 * W, 16 / W)
+template <typename E, int W, bool GATE = false, int NS = kColSegs>
+__global__ void __launch_bounds__(NS * W, NS == kColSegs ? 16 / W : 1)
     fwd_col_kernel(Args<E> p, const __grid_constant__ ColMaps maps) {
   extern __shared__ __align__(128) unsigned char col_raw[];
   const ColSmem<E, W> sm(col_raw, p.T_, 2);
@@ -767,19 +778,19 @@ __global__ void __launch_bounds__(32 * W, 16 / W)
                                          : to_f32<E>(p.lv[(size_t)bi * (p.T_ + 1) * p.D + d0 + c]);
   col_fetch<E, W, 2, GATE ? 0 : 1>(maps, sm, p.T_, d0, bi);
   int start, n;
-  col_segment<W>(p.T_, s, start, n);
+  col_segment<W, NS>(p.T_, s, start, n);
   col_wait_rows(sm, start, n);
   E* lc = sm.t[0] + (size_t)start * W + c;
   E* lv = sm.t[1] + (size_t)start * W + c;
-  if constexpr (GATE) (void)col_gate_prologue<E, W>(lc, lv, n);
-  const bool lin = __syncthreads_and(col_linear_ok<E, W>(lc, lv, n) && !(lv0 > kColLinHi)) != 0;
+  if constexpr (GATE) (void)col_gate_prologue<E, W, NS>(lc, lv, n);
+  const bool lin = __syncthreads_and(col_linear_ok<E, W, NS>(lc, lv, n) && !(lv0 > kColLinHi)) != 0;
   float A, B;
   if (lin) {
     const float h0 = expf(lv0);
-    col_fwd_agg<E, W, true>(lc, lv, n, s == 0, h0, A, B);
-    float h = col_scan_fwd<ColLin, W>(A, B, h0, sm.tot);
+    col_fwd_agg<E, W, true, true, NS>(lc, lv, n, s == 0, h0, A, B);
+    float h = col_scan_fwd<ColLin, W, NS>(A, B, h0, sm.tot);
 #pragma unroll
-    for (int i = 0; i < kColMaxLen; ++i)
+    for (int i = 0; i < col_maxlen<NS>(); ++i)
       if (i < n) {
         float a, b;
         col_ab<E, W>(lc, lv, i, a, b);
@@ -787,8 +798,8 @@ __global__ void __launch_bounds__(32 * W, 16 / W)
         cst<E, W>(lc, i, h);
       }
   } else {
-    col_fwd_agg<E, W, false>(lc, lv, n, s == 0, lv0, A, B);
-    float x = col_scan_fwd<ColLog, W>(A, B, lv0, sm.tot);
+    col_fwd_agg<E, W, false, true, NS>(lc, lv, n, s == 0, lv0, A, B);
+    float x = col_scan_fwd<ColLog, W, NS>(A, B, lv0, sm.tot);
     for (int i = 0; i < n; ++i) {
       x = logaddexp(x + cld<E, W>(lc, i), cld<E, W>(lv, i));
       cst<E, W>(lc, i, expf(x));
@@ -800,24 +811,24 @@ __global__ void __launch_bounds__(32 * W, 16 / W)
 
 // GATE: lc, lv hold log a, log b formed from k, x~ (never replaced by cached
 // a, b, so the chain rule can read them); `neg` marks the x~ < 0 steps.
-template <typename E, int W, bool LIN, bool GATE = false>
+template <typename E, int W, bool LIN, bool GATE = false, int NS = kColSegs>
 __device__ __forceinline__ void col_bwd_body(const Args<E>& p, const ColSmem<E, W>& sm,
                                              int start, int n, int s, float lv0, bool cok,
                                              size_t row0, unsigned long long neg = 0ull) {
   using M = typename std::conditional<LIN, ColLin, ColLog>::type;
   constexpr bool CACHE = !GATE;
-  constexpr int SPW = 32 / W;
+  constexpr int SPW = 32 / W, NW = NS / SPW, ML = col_maxlen<NS>();
   const int lane = threadIdx.x & 31, w = threadIdx.x >> 5, c = lane % W, j = lane / W;
   E* lc = sm.t[0] + (size_t)start * W + c;
   E* lv = sm.t[1] + (size_t)start * W + c;
   const E* g = sm.t[2] + (size_t)start * W + c;
   const float s0 = LIN ? expf(lv0) : lv0;
   float A, B;
-  col_fwd_agg<E, W, LIN, CACHE>(lc, lv, n, s == 0, s0, A, B);
+  col_fwd_agg<E, W, LIN, CACHE, NS>(lc, lv, n, s == 0, s0, A, B);
   // Reverse adjoint Y_t = a_t (g_t + Y_{t+1}) per segment: Y_start = P Y_after + Q.
   float P = 1.f, Q = 0.f;
 #pragma unroll
-  for (int i = kColMaxLen - 1; i >= 0; --i)
+  for (int i = ML - 1; i >= 0; --i)
     if (i < n) {
       float a, b;
       if (LIN)
@@ -836,23 +847,23 @@ __device__ __forceinline__ void col_bwd_body(const Args<E>& p, const ColSmem<E, 
       P *= P2;
     }
   }
-  float* rtot = sm.tot + 2 * W * W;
+  float* rtot = sm.tot + 2 * NW * W;
   if (j == 0) {
     rtot[w * W + c] = P;
-    rtot[W * W + w * W + c] = Q;
+    rtot[NW * W + w * W + c] = Q;
   }
   float Pe = __shfl_down_sync(0xffffffffu, P, W), Qe = __shfl_down_sync(0xffffffffu, Q, W);
   if (j == SPW - 1) { Pe = 1.f; Qe = 0.f; }
-  const float xin = col_scan_fwd<M, W>(A, B, s0, sm.tot);  // synchronises the CTA
+  const float xin = col_scan_fwd<M, W, NS>(A, B, s0, sm.tot);  // synchronises the CTA
   // adjoint entering from beyond T (another slice's, in sequence-parallel use)
   float y = (!GATE && p.y_in != nullptr && cok) ? p.y_in[(size_t)(row0 / (p.T_ + 1) / p.D) * p.D + (row0 % p.D)] : 0.f;
-  for (int v = W - 1; v > w; --v) y = fmaf(rtot[v * W + c], y, rtot[W * W + v * W + c]);
+  for (int v = NW - 1; v > w; --v) y = fmaf(rtot[v * W + c], y, rtot[NW * W + v * W + c]);
   y = fmaf(Pe, y, Qe);
 
-  float xp[kColMaxLen];
+  float xp[ML];
   float x = xin;
 #pragma unroll
-  for (int i = 0; i < kColMaxLen; ++i)
+  for (int i = 0; i < ML; ++i)
     if (i < n) {
       xp[i] = x;
       if (LIN) {
@@ -864,7 +875,7 @@ __device__ __forceinline__ void col_bwd_body(const Args<E>& p, const ColSmem<E, 
       }
     }
 #pragma unroll
-  for (int i = kColMaxLen - 1; i >= 0; --i)
+  for (int i = ML - 1; i >= 0; --i)
     if (i < n) {
       const float G = cld<E, W>(g, i) + y;
       float a, dc, dv;
@@ -906,8 +917,8 @@ __device__ __forceinline__ void col_bwd_body(const Args<E>& p, const ColSmem<E, 
 
 // GATE: maps 0, 1 = k, x~; 3, 4 = dk, dx~ (all (B, T, D)); log h_0 and its
 // gradient in p.lh0 / p.dlh0.
-template <typename E, int W, bool GATE = false>
-__global__ void __launch_bounds__(32 * W, 16 / W)
+template <typename E, int W, bool GATE = false, int NS = kColSegs>
+__global__ void __launch_bounds__(NS * W, NS == kColSegs ? 16 / W : 1)
     bwd_col_kernel(Args<E> p, const __grid_constant__ ColMaps maps) {
   extern __shared__ __align__(128) unsigned char col_raw[];
   const ColSmem<E, W> sm(col_raw, p.T_, 3);
@@ -922,19 +933,19 @@ __global__ void __launch_bounds__(32 * W, 16 / W)
                                          : to_f32<E>(p.lv[row0]);
   col_fetch<E, W, 3, GATE ? 0 : 1>(maps, sm, p.T_, d0, bi);
   int start, n;
-  col_segment<W>(p.T_, s, start, n);
+  col_segment<W, NS>(p.T_, s, start, n);
   col_wait_rows(sm, start, n);
   unsigned long long neg = 0ull;
   if constexpr (GATE)
-    neg = col_gate_prologue<E, W>(sm.t[0] + (size_t)start * W + c, sm.t[1] + (size_t)start * W + c,
+    neg = col_gate_prologue<E, W, NS>(sm.t[0] + (size_t)start * W + c, sm.t[1] + (size_t)start * W + c,
                                   n);
-  const bool lin = __syncthreads_and(col_linear_ok<E, W>(sm.t[0] + (size_t)start * W + c,
+  const bool lin = __syncthreads_and(col_linear_ok<E, W, NS>(sm.t[0] + (size_t)start * W + c,
                                                          sm.t[1] + (size_t)start * W + c, n) &&
                                      !(lv0 > kColLinHi)) != 0;
   if (lin)
-    col_bwd_body<E, W, true, GATE>(p, sm, start, n, s, lv0, cok, row0, neg);
+    col_bwd_body<E, W, true, GATE, NS>(p, sm, start, n, s, lv0, cok, row0, neg);
   else
-    col_bwd_body<E, W, false, GATE>(p, sm, start, n, s, lv0, cok, row0, neg);
+    col_bwd_body<E, W, false, GATE, NS>(p, sm, start, n, s, lv0, cok, row0, neg);
   col_put<E, W>(&maps.m[3], sm.t[0], p.T_, d0, 0, bi);
   col_put<E, W>(&maps.m[4], sm.t[1], p.T_, d0, GATE ? 0 : 1, bi);
   if (threadIdx.x == 0) bulk_wait_read();
@@ -1238,12 +1249,13 @@ int run(bool fwd, const void* lc, const void* lv, void* h, const void* gh, void*
            make_tmap_3d<E>(&maps.m[3], dlc, D, T, B, bx, by) &&
            make_tmap_3d<E>(&maps.m[4], dlv, D, T + 1, B, bx, by);
     if (!ok) return MGS_LAUNCH_FAILED;
-    const size_t smem = col_smem_bytes<E>(T, fwd ? 2 : 3, g.cpt);
+    const int ns = col_segments(g.cpt);
+    const size_t smem = col_smem_bytes<E>(T, fwd ? 2 : 3, g.cpt, ns);
     void (*kern)(Args<E>, const ColMaps) =
-        g.cpt == 16 ? (fwd ? fwd_col_kernel<E, 16> : bwd_col_kernel<E, 16>)
-                    : (fwd ? fwd_col_kernel<E, 8> : bwd_col_kernel<E, 8>);
+        g.cpt == 16 ? (fwd ? fwd_col_kernel<E, 16, false, 32> : bwd_col_kernel<E, 16, false, 32>)
+                    : (fwd ? fwd_col_kernel<E, 8, false, 64> : bwd_col_kernel<E, 8, false, 64>);
     MGS_CUDA_OK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
-    kern<<<(unsigned)g.nstrips, 32 * g.cpt, smem, st>>>(p, maps);
+    kern<<<(unsigned)g.nstrips, ns * g.cpt, smem, st>>>(p, maps);
     return cudaGetLastError() == cudaSuccess ? MGS_OK : MGS_LAUNCH_FAILED;
   }
   if (g.algo == kStrip) {
@@ -1424,12 +1436,13 @@ int gate_run(bool fwd, const void* k, const void* x, const void* lh0, void* h, c
            make_tmap_3d<E>(&maps.m[3], dk, D, T, B, bx, by) &&
            make_tmap_3d<E>(&maps.m[4], dx, D, T, B, bx, by);
     if (!ok) return MGS_LAUNCH_FAILED;
-    const size_t smem = col_smem_bytes<E>(T, fwd ? 2 : 3, g.cpt);
+    const int ns = col_segments(g.cpt);
+    const size_t smem = col_smem_bytes<E>(T, fwd ? 2 : 3, g.cpt, ns);
     void (*kern)(Args<E>, const ColMaps) =
-        g.cpt == 16 ? (fwd ? fwd_col_kernel<E, 16, true> : bwd_col_kernel<E, 16, true>)
-                    : (fwd ? fwd_col_kernel<E, 8, true> : bwd_col_kernel<E, 8, true>);
+        g.cpt == 16 ? (fwd ? fwd_col_kernel<E, 16, true, 32> : bwd_col_kernel<E, 16, true, 32>)
+                    : (fwd ? fwd_col_kernel<E, 8, true, 64> : bwd_col_kernel<E, 8, true, 64>);
     MGS_CUDA_OK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
-    kern<<<(unsigned)g.nstrips, 32 * g.cpt, smem, st>>>(p, maps);
+    kern<<<(unsigned)g.nstrips, ns * g.cpt, smem, st>>>(p, maps);
     return cudaGetLastError() == cudaSuccess ? MGS_OK : MGS_LAUNCH_FAILED;
   }
   const GateWs w = gate_ws(g, B, T, D, dtype);
