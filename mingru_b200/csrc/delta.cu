@@ -256,30 +256,38 @@ __global__ void __launch_bounds__(kThreads) fwd_prepass_kernel(Args<E> p) {
 }
 
 // ------------------------------------------------------------ forward (2) --
-// One block per (b, h): S_{c+1} = A_c S_c + B_c; Hb[c] = S_c; HT = S_last.
+// One block per (b, h, block of value columns): S_{c+1} = A_c S_c + B_c;
+// Hb[c] = S_c; HT = S_last. The state's value columns evolve independently,
+// so the serial chain is split over column blocks (more CTAs in flight).
+constexpr int kChainCols = 16;  // value columns per chain block
+
 __global__ void __launch_bounds__(kThreads) state_pass_kernel(const float* Ac, const float* Bc,
                                                              const float* H0, float* Hb, float* HT,
                                                              int nchunks, int dk, int dv) {
   extern __shared__ __align__(16) float sm[];
-  float* sS = sm;           // dk x dv
-  float* sA = sS + dk * dv; // dk x dk
-  float* sN = sA + dk * dk; // dk x dv (new state)
+  const int j0 = blockIdx.y * kChainCols, nc = min(kChainCols, dv - j0);
+  float* sS = sm;            // dk x nc
+  float* sA = sS + dk * nc;  // dk x dk
+  float* sN = sA + dk * dk;  // dk x nc (new state)
   const long long bh = blockIdx.x;
-  for (int i = threadIdx.x; i < dk * dv; i += blockDim.x) sS[i] = H0[(size_t)bh * dk * dv + i];
+  for (int i = threadIdx.x; i < dk * nc; i += blockDim.x)
+    sS[i] = H0[(size_t)bh * dk * dv + (i / nc) * dv + j0 + i % nc];
   __syncthreads();
   for (int c = 0; c < nchunks; ++c) {
     const size_t o = (size_t)bh * nchunks + c;
     for (int i = threadIdx.x; i < dk * dk; i += blockDim.x) sA[i] = Ac[o * dk * dk + i];
-    for (int i = threadIdx.x; i < dk * dv; i += blockDim.x) {
-      Hb[o * dk * dv + i] = sS[i];
-      sN[i] = Bc[o * dk * dv + i];
+    for (int i = threadIdx.x; i < dk * nc; i += blockDim.x) {
+      const size_t g = o * dk * dv + (i / nc) * dv + j0 + i % nc;
+      Hb[g] = sS[i];
+      sN[i] = Bc[g];
     }
     __syncthreads();
-    bgemm<false, false>(dk, dv, dk, sA, dk, sS, dv, sN, dv, true);
-    for (int i = threadIdx.x; i < dk * dv; i += blockDim.x) sS[i] = sN[i];
+    bgemm<false, false>(dk, nc, dk, sA, dk, sS, nc, sN, nc, true);
+    for (int i = threadIdx.x; i < dk * nc; i += blockDim.x) sS[i] = sN[i];
     __syncthreads();
   }
-  for (int i = threadIdx.x; i < dk * dv; i += blockDim.x) HT[(size_t)bh * dk * dv + i] = sS[i];
+  for (int i = threadIdx.x; i < dk * nc; i += blockDim.x)
+    HT[(size_t)bh * dk * dv + (i / nc) * dv + j0 + i % nc] = sS[i];
 }
 
 // ------------------------------------------------------------ forward (3) --
@@ -365,30 +373,35 @@ __global__ void __launch_bounds__(kThreads) bwd_e_kernel(Args<E> p) {
 }
 
 // ----------------------------------------------------------- backward (2) --
-// dS_c = A_c^T dS_{c+1} + E_c in reverse; dSo[c] = dS_{c+1}; dH0 = dS_0.
+// dS_c = A_c^T dS_{c+1} + E_c in reverse; dSo[c] = dS_{c+1}; dH0 = dS_0. One
+// block per (b, h, block of value columns), as the forward chain.
 __global__ void __launch_bounds__(kThreads) adj_pass_kernel(const float* Ac, const float* Ec,
                                                            const float* dHT, float* dSo, float* dH0,
                                                            int nchunks, int dk, int dv) {
   extern __shared__ __align__(16) float sm[];
-  float* sS = sm;           // dk x dv
-  float* sA = sS + dk * dv; // dk x dk
-  float* sN = sA + dk * dk; // dk x dv
+  const int j0 = blockIdx.y * kChainCols, nc = min(kChainCols, dv - j0);
+  float* sS = sm;            // dk x nc
+  float* sA = sS + dk * nc;  // dk x dk
+  float* sN = sA + dk * dk;  // dk x nc
   const long long bh = blockIdx.x;
-  for (int i = threadIdx.x; i < dk * dv; i += blockDim.x) sS[i] = dHT[(size_t)bh * dk * dv + i];
+  for (int i = threadIdx.x; i < dk * nc; i += blockDim.x)
+    sS[i] = dHT[(size_t)bh * dk * dv + (i / nc) * dv + j0 + i % nc];
   __syncthreads();
   for (int c = nchunks - 1; c >= 0; --c) {
     const size_t o = (size_t)bh * nchunks + c;
     for (int i = threadIdx.x; i < dk * dk; i += blockDim.x) sA[i] = Ac[o * dk * dk + i];
-    for (int i = threadIdx.x; i < dk * dv; i += blockDim.x) {
-      dSo[o * dk * dv + i] = sS[i];
-      sN[i] = Ec[o * dk * dv + i];
+    for (int i = threadIdx.x; i < dk * nc; i += blockDim.x) {
+      const size_t g = o * dk * dv + (i / nc) * dv + j0 + i % nc;
+      dSo[g] = sS[i];
+      sN[i] = Ec[g];
     }
     __syncthreads();
-    bgemm<true, false>(dk, dv, dk, sA, dk, sS, dv, sN, dv, true);
-    for (int i = threadIdx.x; i < dk * dv; i += blockDim.x) sS[i] = sN[i];
+    bgemm<true, false>(dk, nc, dk, sA, dk, sS, nc, sN, nc, true);
+    for (int i = threadIdx.x; i < dk * nc; i += blockDim.x) sS[i] = sN[i];
     __syncthreads();
   }
-  for (int i = threadIdx.x; i < dk * dv; i += blockDim.x) dH0[(size_t)bh * dk * dv + i] = sS[i];
+  for (int i = threadIdx.x; i < dk * nc; i += blockDim.x)
+    dH0[(size_t)bh * dk * dv + (i / nc) * dv + j0 + i % nc] = sS[i];
 }
 
 // ----------------------------------------------------------- backward (3) --
@@ -617,7 +630,8 @@ inline SmemPlan smem_plan(int nh, int C, int dk, int dv, bool decay = false) {
   s.prepass = (M * k + M + M * M + M * (k + v) + k * k + k * v + spans) * 4;
   s.readout = (M * k + M * v + M + c * k + k * v + M * M + c * M + c * v + spans +
                (decay ? M * k : 0)) * 4;
-  s.state = (2 * k * v + k * k) * 4;
+  const size_t vc = v < (size_t)kChainCols ? v : (size_t)kChainCols;  // chain column block
+  s.state = (2 * k * vc + k * k) * 4;
   s.bwd_e = (M * k + M + c * k + c * v + M * M + c * M + M * v + k * v + spans) * 4;
   s.bwd_grads = (M * k + M * v + M + c * k + 2 * k * v + M * v + M * M + 2 * c * M + M * M +
                  M * v + M * k + c * k + M +
@@ -722,7 +736,8 @@ int run(bool fwd, Args<E> p, long long B, int H, long long T, int nh, int dk, in
     float* HT = p.HT;
     int nc = g.nchunks;
     void* a2[] = {&Ac, &Bc, &H0, &Hb, &HT, &nc, &dk, &dv};
-    rc = launch(state_pass_kernel, dim3((unsigned)BH), sp.state, st, a2);
+    rc = launch(state_pass_kernel, dim3((unsigned)BH, (unsigned)((dv + kChainCols - 1) / kChainCols)),
+                sp.state, st, a2);
     if (rc != MGS_OK) return rc;
     return launch(fwd_readout_kernel<E>, dim3(g.nchunks, (unsigned)BH), sp.readout, st, a1);
   }
@@ -743,7 +758,8 @@ int run(bool fwd, Args<E> p, long long B, int H, long long T, int nh, int dk, in
   float* dH0 = p.dH0;
   int nc = g.nchunks;
   void* a2[] = {&Ac, &Ec, &dHT, &dSo, &dH0, &nc, &dk, &dv};
-  rc = launch(adj_pass_kernel, dim3((unsigned)BH), sp.state, st, a2);
+  rc = launch(adj_pass_kernel, dim3((unsigned)BH, (unsigned)((dv + kChainCols - 1) / kChainCols)),
+              sp.state, st, a2);
   if (rc != MGS_OK) return rc;
   return launch(bwd_grads_kernel<E>, dim3(g.nchunks, (unsigned)BH), sp.bwd_grads, st, a1);
 }
