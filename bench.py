@@ -584,6 +584,8 @@ WORKLOADS = {
     # split 32 / 16 / 8 per GPU over 2 / 4 / 8 GPUs)
     "cfg5-b64": lambda: DeltaWorkload(B=64, name="cfg5-b64"),
     "cfg5-gated": lambda: GatedDeltaWorkload(name="cfg5-gated"),
+    # config 5 shape with fp32 inputs (the module's default dtype): CUDA-core kernels
+    "cfg5-fp32": lambda: DeltaWorkload(dtype=torch.float32, name="cfg5-fp32"),
 }
 
 
