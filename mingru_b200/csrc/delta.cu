@@ -655,7 +655,7 @@ inline int ffma_chunk(int nh, int dk, int dv, int C, long long T, bool decay = f
   return 0;
 }
 
-// Tokens per chunk of the tensor-core kernels (bf16 inputs): nh * C <= 64.
+// Tokens per chunk of the tensor-core kernels (bf16 / fp32 inputs): nh * C <= 64.
 inline int tc_chunk(int nh, int C) {
   const int cap = kMaxM / nh;
   return C < cap ? C : cap;
@@ -699,7 +699,7 @@ int run(bool fwd, Args<E> p, long long B, int H, long long T, int nh, int dk, in
   if (decay && !fwd && p.dlg == nullptr) return MGS_BAD_SHAPE;
   Geometry g;
   if (!geometry(B, H, T, nh, dk, dv, C, dtype, &g, decay)) return MGS_UNSUPPORTED;
-  if constexpr (std::is_same_v<E, __nv_bfloat16>) {
+  if constexpr (!std::is_same_v<E, __half>) {
     if (g.tc) return run_tc(fwd, p, B, H, T, nh, dk, dv, g.C, saved, ws, ws_bytes, st);
   }
   C = g.C;
@@ -774,7 +774,7 @@ size_t delta_saved_size(int64_t B, int H, int64_t T, int nh, int dk, int dv, int
                         bool decay) {
   mgs::delta::Geometry g;
   if (!mgs::delta::geometry(B, H, T, nh, dk, dv, chunk, dtype, &g, decay)) return 0;
-  if (g.tc) return mgs::delta::tc_saved_floats(B * (int64_t)H, T, dk, dv, g.C) * sizeof(float);
+  if (g.tc) return mgs::delta::tc_saved_floats(B * (int64_t)H, T, dk, dv, g.C, dtype) * sizeof(float);
   return (size_t)B * H * (g.ac + g.hb) * sizeof(float);
 }
 

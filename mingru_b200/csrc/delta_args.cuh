@@ -37,12 +37,14 @@ struct Args {
   int H, nh, dk, dv, C, nchunks;
 };
 
-// Tensor-core path (bf16 inputs): eligibility, buffer sizes and launch.
+// Tensor-core path (bf16 and fp32 inputs): eligibility, buffer sizes and launch.
 bool tc_eligible(int dtype, int nh, int dk, int dv, int C);
-size_t tc_saved_floats(long long BH, long long T, int dk, int dv, int C);
+size_t tc_saved_floats(long long BH, long long T, int dk, int dv, int C, int dtype);
 size_t tc_workspace_floats(long long BH, long long T, int dk, int dv, int C);
 int run_tc(bool fwd, const Args<__nv_bfloat16>& p, long long B, int H, long long T, int nh, int dk,
            int dv, int C, float* saved, void* ws, size_t ws_bytes, cudaStream_t st);
+int run_tc(bool fwd, const Args<float>& p, long long B, int H, long long T, int nh, int dk, int dv,
+           int C, float* saved, void* ws, size_t ws_bytes, cudaStream_t st);
 
 }  // namespace delta
 }  // namespace mgs

@@ -1,5 +1,5 @@
 // delta_tc.cu -- DeltaMinGRU chunked-WY delta rule on the tensor cores (bf16
-// inputs, fp32 state and accumulation).
+// or fp32 inputs, fp32 state and accumulation).
 //
 // Same mathematics as delta.cu (reference: DeltaMinGRU._forward_chunked,
 // min_gru.py:3152-3255; backward _delta_backward_torch, triton_scans.py:
@@ -23,11 +23,19 @@
 // state runs in parallel over all chunks, and the two chunk-serial kernels do
 // one state product per chunk.
 //
-// Kernels (the 64 x 64 chunk products run on the tcgen05 tensor cores with
-// split hi/lo bf16 operands, umma.cuh; T^{-1} by blocked substitution, its
-// 16 x 16 blocks on mma.sync, mma_bf16.cuh):
+// Operands. A bf16 input is exact in one bf16 tile. Every other operand (fp32
+// values computed here, and fp32 inputs) is held as bf16 levels: hi and lo
+// (x = hi + lo to 2^-16) when the inputs are bf16, hi, mid and lo (x = h + m
+// + l to 2^-24) when they are fp32. A product takes every term down to 2^-16
+// of its leading one -- three MMAs per k-step for two levels, six for three
+// (umma::products) -- so fp32 inputs get results within fp32 rounding of an
+// fp32 computation, at twice the MMA count of the bf16 path.
+//
+// Kernels (the 64 x 64 chunk products run on the tcgen05 tensor cores,
+// umma.cuh; for bf16 inputs T^{-1} by blocked substitution with its 16 x 16
+// blocks on mma.sync, mma_bf16.cuh, for fp32 inputs by substitution in fp32):
 //   prep_kernel       one CTA per (b, h, chunk): T^{-1} (saved), Xn, Qt
-//                     (saved), Bc, Yp (forward workspace).
+//   prep_f32_kernel   (saved), Bc, Yp (forward workspace).
 //   chain_fwd_kernel  one CTA per (b, h, value-column split): S in registers,
 //                     one chunk per step; writes y, H_T and every chunk-start
 //                     state (saved for the backward).
@@ -55,10 +63,6 @@ constexpr int kTcThreads = 256;
 constexpr int kTile = 64 * kLd;            // bf16 elements of one 64 x 64 tile
 constexpr int kTileBytes = kTile * 2;      // 9216
 constexpr int kTdBytes = 4 * 16 * 17 * 4;  // T's four diagonal 16 x 16 blocks, fp32, padded rows
-// Tiles kept in `saved` (T^{-1}, Xn, Qt) use the shared-memory layout (64 rows
-// of kLd elements), so one contiguous bulk copy stages a tile.
-constexpr int kSavedTile = 64 * kLd;
-constexpr long long kSavedPair = 2 * kSavedTile;
 constexpr int kRing = 3;  // staging depth of the chunk-serial kernels
 
 __device__ __forceinline__ void cp_async16(void* dst, const void* src, int src_bytes) {
@@ -152,25 +156,26 @@ __device__ void zero_upper_blocks(bf16* H, bf16* L) {
   }
 }
 
+template <typename E>
 struct TcArgs {
-  const bf16* Q;
-  const bf16* K;
-  const bf16* V;
-  const bf16* beta;
+  const E* Q;
+  const E* K;
+  const E* V;
+  const E* beta;
   const float* H0;
-  bf16* y;
+  E* y;
   float* HT;
-  const bf16* dy;
+  const E* dy;
   const float* dHT;
-  bf16* dQ;
-  bf16* dK;
-  bf16* dV;
-  bf16* dbeta;
+  E* dQ;
+  E* dK;
+  E* dV;
+  E* dbeta;
   float* dH0;
   float* Hs;    // (BH, nchunks, dk, dv) chunk-start states
-  bf16* Ti;     // (BH, nchunks, 2, 64, 64) T^{-1} of every chunk, split hi / lo
-  bf16* Xn;     // (BH, nchunks, 2, 64, 64) -K^T diag(beta) W, split
-  bf16* Qt;     // (BH, nchunks, 2, 64, 64) Q - P W, split
+  bf16* Ti;     // (BH, nchunks, L, 64, 64) T^{-1} of every chunk, L bf16 levels, blocked
+  bf16* Xn;     // (BH, nchunks, L, 64, 64) -K^T diag(beta) W
+  bf16* Qt;     // (BH, nchunks, L, 64, 64) Q - P W
   float* Bc;    // (BH, nchunks, 4096) K^T diag(beta) U' as [dk][dv] (forward workspace)
   float* Yp;    // (BH, nchunks, 4096) P U' as [C][dv] (forward workspace)
   float* dHs;   // (BH, nchunks, dk, dv) gradient of each chunk's output state
@@ -178,9 +183,82 @@ struct TcArgs {
   int nh, dk, dv, C, nchunks, S, dvs;
 };
 
+template <typename E>
+constexpr bool kF32 = std::is_same_v<E, float>;
+// bf16 levels of an fp32 operand: 2 for bf16 inputs, 3 for fp32 inputs
+template <typename E>
+constexpr int kLevels = kF32<E> ? 3 : 2;
+// bf16 elements of one saved matrix (T^{-1}, Xn, Qt): its levels, each a
+// blocked 64 x 64 tile, contiguous, so one bulk copy stages all of them
+template <typename E>
+constexpr long long kSavedSet = kLevels<E> * 4096LL;
+
+__device__ __forceinline__ float tof(float x) { return x; }
+__device__ __forceinline__ float tof(bf16 x) { return __bfloat162float(x); }
+template <typename E>
+__device__ __forceinline__ E fromf(float x) {
+  if constexpr (kF32<E>) return x; else return __float2bfloat16_rn(x);
+}
+
+// A matrix held as up to three bf16 levels, each a blocked 64-column tile in
+// shared memory (null: the level is absent; level 0 is always present).
+struct Lv {
+  bf16* t[3];
+};
+__device__ __forceinline__ Lv lv(bf16* a, bf16* b = nullptr, bf16* c = nullptr) {
+  return Lv{{a, b, c}};
+}
+// the first n levels of x
+__device__ __forceinline__ Lv lv_first(const Lv& x, int n) {
+  return Lv{{x.t[0], n > 1 ? x.t[1] : nullptr, n > 2 ? x.t[2] : nullptr}};
+}
+// levels 1.. of x, level 1 first
+__device__ __forceinline__ Lv lv_rest(const Lv& x) { return Lv{{x.t[1], x.t[2], nullptr}}; }
+__device__ __forceinline__ uint32_t lv_addr(const bf16* t) { return t ? umma::saddr(t) : 0u; }
+__device__ __forceinline__ umma::Opnd op(const Lv& x, bool mn) {
+  return umma::opnd3(lv_addr(x.t[0]), lv_addr(x.t[1]), lv_addr(x.t[2]), mn);
+}
+__device__ __forceinline__ umma::Opnd op_mn(const Lv& x, int cols) {
+  return umma::opnd_mn3(lv_addr(x.t[0]), lv_addr(x.t[1]), lv_addr(x.t[2]), cols);
+}
+// 8 consecutive values -> the levels of x at element offset o (of a blocked tile)
+__device__ __forceinline__ void store8(const Lv& x, int o, const float* v) {
+  if (x.t[2]) {
+    umma::store_split8_3(x.t[0], x.t[1], x.t[2], o, v);
+    return;
+  }
+  uint32_t ph[4], pl[4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) tc::split_pack(v[2 * i], v[2 * i + 1], ph[i], pl[i]);
+  *reinterpret_cast<uint4*>(x.t[0] + o) = make_uint4(ph[0], ph[1], ph[2], ph[3]);
+  if (x.t[1]) *reinterpret_cast<uint4*>(x.t[1] + o) = make_uint4(pl[0], pl[1], pl[2], pl[3]);
+}
+// 16 values of row r (columns c0.., c0 % 8 == 0) of a blocked 64-column matrix
+__device__ __forceinline__ void store16(const Lv& x, int r, int c0, const float (&v)[16]) {
+  store8(x, umma::boff(r, c0), v);
+  store8(x, umma::boff(r, c0 + 8), v + 8);
+}
+// as store16 for a blocked tile of `cols` columns (8-column chunks starting
+// below `valid` only)
+__device__ __forceinline__ void store16_n(const Lv& x, int r, int c0, int cols, int valid,
+                                          const float (&v)[16]) {
+#pragma unroll
+  for (int h = 0; h < 2; ++h)
+    if (c0 + 8 * h < valid) store8(x, umma::boff_n(r, c0 + 8 * h, cols), v + 8 * h);
+}
+
+// 16 fp32 values of row r (columns c0..) -> global row (columns < ncols).
+__device__ __forceinline__ void row16_f32_to_global(float* g, int c0, int ncols, const float (&v)[16]) {
+#pragma unroll
+  for (int k = 0; k < 4; ++k)
+    if (c0 + 4 * k < ncols)
+      *reinterpret_cast<float4*>(g + c0 + 4 * k) = make_float4(v[4 * k], v[4 * k + 1], v[4 * k + 2], v[4 * k + 3]);
+}
+
 // ----------------------------------------------------- backward: grads --
-// One CTA per (b, h, chunk), two CTAs per SM: every gradient of the chunk from
-// its saved S, T^{-1} and dS', on the tcgen05 tensor cores (umma.cuh). Two
+// One CTA per (b, h, chunk), two CTAs per SM for bf16 inputs (one for fp32):
+// every gradient of the chunk from its saved S, T^{-1} and dS', on the tcgen05
+// tensor cores (umma.cuh). Two
 // threads (lane 0 of warps 0 and 1) issue each level of products, split by
 // accumulator, as batches of 64 x 64 x 64 split MMAs into TMEM and commit to
 // one barrier of arrival count 2 (MMA issue, not the tensor pipe, bounds these
@@ -194,11 +272,16 @@ struct TcArgs {
 //   5. dQ = dy S^T + dS_ K;  dK = beta * (U dS'^T) + dS_^T Q + dKK K + Gn S^T + dKK^T K
 // TMEM: four 64-column accumulators A, B, C, D (256 columns per CTA), each
 // reused once its previous contents have been read.
-// Shared tiles (blocked, 8 KB): 0 K | 1 Q | 2 dY | 3, 4 S | 5, 6 dS' -> dKK |
-//   7, 8 Ti -> Gn | 9 V -> -W hi -> U hi | 10, 11 P -> dU -> dS_ | 12 -W lo -> U lo
+// Shared tiles (blocked, 8 KB), bf16 inputs: 0 K | 1 Q | 2 dY | 3, 4 S |
+//   5, 6 dS' -> dKK | 7, 8 Ti -> Gn | 9 V -> -W hi -> U hi | 10, 11 P -> dU ->
+//   dS_ | 12 -W lo -> U lo (two CTAs per SM); fp32 inputs, three levels each:
+//   0-2 K | 3-5 Q | 6-8 dY | 9-11 S | 12-14 dS' -> dKK | 15-17 Ti -> Gn |
+//   18-20 V -> -W -> U | 21-23 P -> dU -> dS_ (one CTA per SM).
 constexpr int kGradThreads = 256;
-constexpr int kGradTiles = 13;
-constexpr size_t kGradSmem = 1024 + kGradTiles * (size_t)umma::kTileBytes + 2048;
+template <typename E>
+constexpr int kGradTiles = kF32<E> ? 24 : 13;
+template <typename E>
+constexpr size_t kGradSmem = 1024 + kGradTiles<E> * (size_t)umma::kTileBytes + 2048;
 constexpr int kGradTmemCols = 256;
 
 // 64 rows x (8 * valid_ch) columns of a row-major global bf16 matrix into a
@@ -210,6 +293,29 @@ __device__ __forceinline__ void stage_blocked(bf16* tile, const bf16* g, long lo
     const int row = i >> 3, ch = i & 7;
     const bool ok = row < nrows && ch < valid_ch;
     cp_async16(tile + umma::boff(row, ch * 8), ok ? g + row * ld + ch * 8 : g, ok ? 16 : 0);
+  }
+}
+
+// An input matrix (64 rows x 8 * valid_ch columns of a row-major global
+// matrix; other rows and chunks zero) into its blocked levels: bf16 by
+// cp.async (the caller commits and waits), fp32 loaded and split into three
+// levels here.
+template <int NTHR, typename E>
+__device__ __forceinline__ void stage_in(const Lv& x, const E* g, long long ld, int nrows,
+                                         int valid_ch) {
+  if constexpr (kF32<E>) {
+    for (int i = threadIdx.x; i < 64 * 8; i += NTHR) {
+      const int row = i >> 3, ch = i & 7;
+      float4 a = make_float4(0.f, 0.f, 0.f, 0.f), b = a;
+      if (row < nrows && ch < valid_ch) {
+        a = __ldg(reinterpret_cast<const float4*>(g + row * ld + ch * 8));
+        b = __ldg(reinterpret_cast<const float4*>(g + row * ld + ch * 8 + 4));
+      }
+      const float v[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
+      store8(x, umma::boff(row, ch * 8), v);
+    }
+  } else {
+    stage_blocked<NTHR>(x.t[0], g, ld, nrows, valid_ch);
   }
 }
 
@@ -234,20 +340,31 @@ __device__ __forceinline__ void row16_to_global(bf16* g, int c0, int ncols, cons
       *reinterpret_cast<uint4*>(g + c0 + 8 * h) = make_uint4(w[0], w[1], w[2], w[3]);
     }
 }
+__device__ __forceinline__ void row16_to_global(float* g, int c0, int ncols, const float (&v)[16]) {
+  row16_f32_to_global(g, c0, ncols, v);
+}
 
-__global__ void __launch_bounds__(kGradThreads, 2) bwd_grads_kernel(const TcArgs p) {
+template <typename E>
+__global__ void __launch_bounds__(kGradThreads, kF32<E> ? 1 : 2) bwd_grads_kernel(const TcArgs<E> p) {
   namespace um = umma;
+  constexpr bool F = kF32<E>;
+  constexpr int L = kLevels<E>;
   extern __shared__ __align__(1024) unsigned char gsmem[];
   uint64_t* bar = reinterpret_cast<uint64_t*>(gsmem);  // [0] MMA batches, [1] T^{-1} copy
   uint32_t* tbase_s = reinterpret_cast<uint32_t*>(gsmem + 64);
   bf16* tiles = reinterpret_cast<bf16*>(gsmem + 1024);
   auto T = [&](int i) { return tiles + i * (um::kTileBytes / 2); };
-  bf16 *K = T(0), *Q = T(1), *dY = T(2), *SH = T(3), *SL = T(4), *DH = T(5), *DL = T(6),
-       *TiH = T(7), *TiL = T(8), *V = T(9);
-  bf16 *dKH = T(5), *dKL = T(6), *GH = T(7), *GL = T(8), *WH = T(9), *WL = T(12), *UH = T(9),
-       *UL = T(12), *PH = T(10), *PL = T(11), *dUH = T(10), *dUL = T(11), *dSH = T(10),
-       *dSL = T(11);
-  float* bs = reinterpret_cast<float*>(T(kGradTiles));
+  const Lv K = F ? lv(T(0), T(1), T(2)) : lv(T(0));
+  const Lv Q = F ? lv(T(3), T(4), T(5)) : lv(T(1));
+  const Lv dY = F ? lv(T(6), T(7), T(8)) : lv(T(2));
+  const Lv S = F ? lv(T(9), T(10), T(11)) : lv(T(3), T(4));
+  const Lv Dp = F ? lv(T(12), T(13), T(14)) : lv(T(5), T(6));  // dS' -> dKK
+  const Lv Ti = F ? lv(T(15), T(16), T(17)) : lv(T(7), T(8));  // T^{-1} -> Gn
+  const Lv V = F ? lv(T(18), T(19), T(20)) : lv(T(9));
+  const Lv W = F ? V : lv(T(9), T(12));                         // -W -> U
+  const Lv P = F ? lv(T(21), T(22), T(23)) : lv(T(10), T(11));  // P -> dU -> dS_
+  const Lv &dKK = Dp, &Gn = Ti, &U = W, &dU = P, &dS_ = P;
+  float* bs = reinterpret_cast<float*>(T(kGradTiles<E>));
   float* rpart = bs + 64;      // [2 column halves][64 rows]: sum_col U * dbU
   float* cpart = rpart + 128;  // [8 warps][32 columns]: masked-product column sums
 
@@ -269,19 +386,18 @@ __global__ void __launch_bounds__(kGradThreads, 2) bwd_grads_kernel(const TcArgs
     mbar_init(bar + 1, 1);
     mbar_fence_init();
   }
-  stage_blocked<NTH>(K, p.K + (bh * rows + r0) * p.dk, p.dk, Mc, p.dk >> 3);
-  stage_blocked<NTH>(Q, p.Q + (bh * p.T + t0) * p.dk, p.dk, Cc, p.dk >> 3);
-  stage_blocked<NTH>(dY, p.dy + (bh * p.T + t0) * p.dv, p.dv, Cc, p.dv >> 3);
-  stage_blocked<NTH>(V, p.V + (bh * rows + r0) * p.dv, p.dv, Mc, p.dv >> 3);
+  stage_in<NTH>(K, p.K + (bh * rows + r0) * p.dk, p.dk, Mc, p.dk >> 3);
+  stage_in<NTH>(Q, p.Q + (bh * p.T + t0) * p.dk, p.dk, Cc, p.dk >> 3);
+  stage_in<NTH>(dY, p.dy + (bh * p.T + t0) * p.dv, p.dv, Cc, p.dv >> 3);
+  stage_in<NTH>(V, p.V + (bh * rows + r0) * p.dv, p.dv, Mc, p.dv >> 3);
   cp_async_commit();
   um::fence_before();
   __syncthreads();  // barriers initialised, TMEM base written
-  if (tid == 0) {
-    mbar_arrive_expect_tx(bar + 1, 2 * um::kTileBytes);
-    bulk_g2s(TiH, p.Ti + blk * kSavedPair, um::kTileBytes, bar + 1);
-    bulk_g2s(TiL, p.Ti + blk * kSavedPair + 4096, um::kTileBytes, bar + 1);
+  if (tid == 0) {  // T^{-1}: its levels are contiguous in `saved` and in shared memory
+    mbar_arrive_expect_tx(bar + 1, L * um::kTileBytes);
+    bulk_g2s(Ti.t[0], p.Ti + blk * kSavedSet<E>, L * um::kTileBytes, bar + 1);
   }
-  {  // S (chunk-start state) and dS' (fp32 [dk][dv]) -> split blocked tiles
+  {  // S (chunk-start state) and dS' (fp32 [dk][dv]) -> blocked levels
     float4 a[2][2], b[2][2];
 #pragma unroll
     for (int k = 0; k < 2; ++k) {
@@ -302,20 +418,12 @@ __global__ void __launch_bounds__(kGradThreads, 2) bwd_grads_kernel(const TcArgs
                            a[k][1].x, a[k][1].y, a[k][1].z, a[k][1].w};
       const float bv[8] = {b[k][0].x, b[k][0].y, b[k][0].z, b[k][0].w,
                            b[k][1].x, b[k][1].y, b[k][1].z, b[k][1].w};
-      uint32_t ph[4], pl[4], qh[4], ql[4];
-#pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        tc::split_pack(av[2 * j], av[2 * j + 1], ph[j], pl[j]);
-        tc::split_pack(bv[2 * j], bv[2 * j + 1], qh[j], ql[j]);
-      }
       const int o = um::boff(r, cb * 8);
-      *reinterpret_cast<uint4*>(SH + o) = make_uint4(ph[0], ph[1], ph[2], ph[3]);
-      *reinterpret_cast<uint4*>(SL + o) = make_uint4(pl[0], pl[1], pl[2], pl[3]);
-      *reinterpret_cast<uint4*>(DH + o) = make_uint4(qh[0], qh[1], qh[2], qh[3]);
-      *reinterpret_cast<uint4*>(DL + o) = make_uint4(ql[0], ql[1], ql[2], ql[3]);
+      store8(S, o, av);
+      store8(Dp, o, bv);
     }
   }
-  if (tid < 64) bs[tid] = tid < Mc ? __bfloat162float(p.beta[bh * rows + r0 + tid]) : 0.f;
+  if (tid < 64) bs[tid] = tid < Mc ? tof(p.beta[bh * rows + r0 + tid]) : 0.f;
   cp_async_wait_all();
   // okw: every wait so far completed. A wait that runs out records the time-out
   // (sticky word) and from then on this CTA issues no MMA, waits on nothing and
@@ -339,21 +447,17 @@ __global__ void __launch_bounds__(kGradThreads, 2) bwd_grads_kernel(const TcArgs
     phase ^= 1u;
     um::fence_after();
   };
-  // load two 16-column halves of this thread's 32 columns from NA accumulators
-  // at column offsets off[] (one wait), as v[acc][half][16]
-  auto S_ = [](const bf16* t) { return um::saddr(t); };
 
   // level 1
   to_mma();
   if (okw && tid == 0) {
-    const um::Opnd oTi = um::opnd(S_(TiH), S_(TiL), false);
-    const um::Prod ps[2] = {{tA, oTi, um::opnd(S_(K), 0, true), false},
-                            {tB, oTi, um::opnd(S_(V), 0, true), false}};
+    const um::Opnd oTi = op(Ti, false);
+    const um::Prod ps[2] = {{tA, oTi, op(K, true), false}, {tB, oTi, op(V, true), false}};
     um::products(ps);
     um::commit(bar);
   } else if (okw && tid == 32) {
-    const um::Prod ps[2] = {{tC, um::opnd(S_(K), 0, false), um::opnd(S_(DH), S_(DL), true), false},
-                            {tD, um::opnd(S_(Q), 0, false), um::opnd(S_(K), 0, false), false}};
+    const um::Prod ps[2] = {{tC, op(K, false), op(Dp, true), false},
+                            {tD, op(Q, false), op(K, false), false}};
     um::products(ps);
     um::commit(bar);
   }
@@ -375,18 +479,18 @@ __global__ void __launch_bounds__(kGradThreads, 2) bwd_grads_kernel(const TcArgs
         v[i] = (cl < (row + 1) * p.nh && cl < Mc) ? v[i] * bs[cl] : 0.f;
         w[i] = -w[i];
       }
-      um::store_split16(PH, PL, row, c0, v);
-      um::store_split16(WH, WL, row, c0, w);
+      store16(P, row, c0, v);
+      store16(W, row, c0, w);
     }
   }
   // level 2
   to_mma();
   if (okw && tid == 0) {
-    const um::Prod ps[1] = {{tB, um::opnd(S_(WH), S_(WL), false), um::opnd(S_(SH), S_(SL), true), true}};
+    const um::Prod ps[1] = {{tB, op(W, false), op(S, true), true}};
     um::products(ps);
     um::commit(bar);
   } else if (okw && tid == 32) {
-    const um::Prod ps[1] = {{tA, um::opnd(S_(PH), S_(PL), true), um::opnd(S_(dY), 0, true), false}};
+    const um::Prod ps[1] = {{tA, op(P, true), op(dY, true), false}};
     um::products(ps);
     um::commit(bar);
   }
@@ -412,22 +516,22 @@ __global__ void __launch_bounds__(kGradThreads, 2) bwd_grads_kernel(const TcArgs
           rs += u[i] * db[i];
           pd[i] += b * db[i];
         }
-        um::store_split16(UH, UL, row, c0, u);
-        um::store_split16(dUH, dUL, row, c0, pd);
+        store16(U, row, c0, u);
+        store16(dU, row, c0, pd);
       }
     }
     if (rv) rpart[hh * 64 + row] = rs;
   }
   // level 3
   to_mma();
-  if (okw && tid == 0) {  // G = Ti^T dU as (Ti^T dU_hi) + (Ti_hi^T dU_lo) in C and D
+  if (okw && tid == 0) {  // G = Ti^T dU, its terms in two accumulators: Ti^T dU_hi (C), the rest (D)
     const um::Prod ps[2] = {
-        {tC, um::opnd(S_(TiH), S_(TiL), true), um::opnd(S_(dUH), 0, true), false},
-        {tD, um::opnd(S_(TiH), 0, true), um::opnd(S_(dUL), 0, true), false}};
+        {tC, op(Ti, true), op(lv_first(dU, 1), true), false},
+        {tD, op(lv_first(Ti, L - 1), true), op(lv_rest(dU), true), false}};
     um::products(ps);
     um::commit(bar);
   } else if (okw && tid == 32) {  // U dS'^T in A
-    const um::Prod ps[1] = {{tA, um::opnd(S_(UH), S_(UL), false), um::opnd(S_(DH), S_(DL), false), false}};
+    const um::Prod ps[1] = {{tA, op(U, false), op(Dp, false), false}};
     um::products(ps);
     um::commit(bar);
   }
@@ -451,19 +555,19 @@ __global__ void __launch_bounds__(kGradThreads, 2) bwd_grads_kernel(const TcArgs
       if (okw && row < Mc) row16_to_global(p.dV + (bh * rows + r0 + row) * p.dv, c0, p.dv, g);
 #pragma unroll
       for (int i = 0; i < 16; ++i) g[i] = -g[i];
-      um::store_split16(GH, GL, row, c0, g);
+      store16(Gn, row, c0, g);
     }
   }
   // level 4
   to_mma();
   if (okw && tid == 0) {  // Gn U^T in B, K K^T in C
-    const um::Prod ps[2] = {{tB, um::opnd(S_(GH), S_(GL), false), um::opnd(S_(UH), S_(UL), false), false},
-                            {tC, um::opnd(S_(K), 0, false), um::opnd(S_(K), 0, false), false}};
+    const um::Prod ps[2] = {{tB, op(Gn, false), op(U, false), false},
+                            {tC, op(K, false), op(K, false), false}};
     um::products(ps);
     um::commit(bar);
   } else if (okw && tid == 32) {  // dy U^T in A, Q K^T in D
-    const um::Prod ps[2] = {{tA, um::opnd(S_(dY), 0, false), um::opnd(S_(UH), S_(UL), false), false},
-                            {tD, um::opnd(S_(Q), 0, false), um::opnd(S_(K), 0, false), false}};
+    const um::Prod ps[2] = {{tA, op(dY, false), op(U, false), false},
+                            {tD, op(Q, false), op(K, false), false}};
     um::products(ps);
     um::commit(bar);
   }
@@ -511,8 +615,8 @@ __global__ void __launch_bounds__(kGradThreads, 2) bwd_grads_kernel(const TcArgs
       const float colsum = __shfl_sync(0xffffffffu, e[0], lane & 15);  // from the row lanes 0-15
       if ((lane >> 4) == half) cs = colsum;
       if (rv) {
-        um::store_split16(dSH, dSL, row, c0, ds);
-        um::store_split16(dKH, dKL, row, c0, dk);
+        store16(dS_, row, c0, ds);
+        store16(dKK, row, c0, dk);
       }
     }
     cpart[warp * 32 + lane] = cs;
@@ -520,17 +624,17 @@ __global__ void __launch_bounds__(kGradThreads, 2) bwd_grads_kernel(const TcArgs
   // level 5
   to_mma();
   if (okw && tid == 0) {  // dQ in A, Gn S^T in C
-    const um::Opnd oS = um::opnd(S_(SH), S_(SL), false);
-    const um::Prod ps[3] = {{tA, um::opnd(S_(dY), 0, false), oS, false},
-                            {tC, um::opnd(S_(GH), S_(GL), false), oS, false},
-                            {tA, um::opnd(S_(dSH), S_(dSL), false), um::opnd(S_(K), 0, true), true}};
+    const um::Opnd oS = op(S, false);
+    const um::Prod ps[3] = {{tA, op(dY, false), oS, false},
+                            {tC, op(Gn, false), oS, false},
+                            {tA, op(dS_, false), op(K, true), true}};
     um::products(ps);
     um::commit(bar);
   } else if (okw && tid == 32) {  // dS_^T Q + dKK K in B, dKK^T K in D
-    const um::Opnd oKmn = um::opnd(S_(K), 0, true);
-    const um::Prod ps[3] = {{tB, um::opnd(S_(dSH), S_(dSL), true), um::opnd(S_(Q), 0, true), false},
-                            {tD, um::opnd(S_(dKH), S_(dKL), true), oKmn, false},
-                            {tB, um::opnd(S_(dKH), S_(dKL), false), oKmn, true}};
+    const um::Opnd oKmn = op(K, true);
+    const um::Prod ps[3] = {{tB, op(dS_, true), op(Q, true), false},
+                            {tD, op(dKK, true), oKmn, false},
+                            {tB, op(dKK, false), oKmn, true}};
     um::products(ps);
     um::commit(bar);
   }
@@ -564,7 +668,7 @@ __global__ void __launch_bounds__(kGradThreads, 2) bwd_grads_kernel(const TcArgs
     const float d = (rpart[tid] + rpart[64 + tid]) +
                     (cpart[(4 * h2) * 32 + cl] + cpart[(4 * h2 + 1) * 32 + cl]) +
                     (cpart[(4 * h2 + 2) * 32 + cl] + cpart[(4 * h2 + 3) * 32 + cl]);
-    p.dbeta[bh * rows + r0 + tid] = __float2bfloat16_rn(d);
+    p.dbeta[bh * rows + r0 + tid] = fromf<E>(d);
   }
   if (warp == 0) {
     um::fence_after();
@@ -606,15 +710,7 @@ __device__ __forceinline__ void store_split16_padded(bf16* hi, bf16* lo, int r, 
   }
 }
 
-// 16 fp32 values of row r (columns c0..) -> global row (columns < ncols).
-__device__ __forceinline__ void row16_f32_to_global(float* g, int c0, int ncols, const float (&v)[16]) {
-#pragma unroll
-  for (int k = 0; k < 4; ++k)
-    if (c0 + 4 * k < ncols)
-      *reinterpret_cast<float4*>(g + c0 + 4 * k) = make_float4(v[4 * k], v[4 * k + 1], v[4 * k + 2], v[4 * k + 3]);
-}
-
-__global__ void __launch_bounds__(kPrepThreads, 2) prep_kernel(const TcArgs p) {
+__global__ void __launch_bounds__(kPrepThreads, 2) prep_kernel(const TcArgs<bf16> p) {
   namespace um = umma;
   extern __shared__ __align__(1024) unsigned char psmem[];
   uint64_t* bar = reinterpret_cast<uint64_t*>(psmem);  // [0] level 1, [1] levels 3-4 (two issuers)
@@ -709,8 +805,8 @@ __global__ void __launch_bounds__(kPrepThreads, 2) prep_kernel(const TcArgs p) {
   }
   to_mma();
   if (okw && tid == 64) {  // T^{-1} (blocked) to `saved` by bulk copies; Y is not reused until the end
-    bulk_s2g(p.Ti + blk * kSavedPair, TiH, um::kTileBytes);
-    bulk_s2g(p.Ti + blk * kSavedPair + 4096, TiL, um::kTileBytes);
+    bulk_s2g(p.Ti + blk * kSavedSet<bf16>, TiH, um::kTileBytes);
+    bulk_s2g(p.Ti + blk * kSavedSet<bf16> + 4096, TiL, um::kTileBytes);
     bulk_commit();
   }
   // level 3: W = Ti K (B), U' = Ti V (C)
@@ -801,8 +897,8 @@ __global__ void __launch_bounds__(kPrepThreads, 2) prep_kernel(const TcArgs p) {
   um::fence_before();
   __syncthreads();
   if (okw && tid == 0) {
-    bulk_s2g(p.Xn + blk * kSavedPair, XsH, 2 * um::kTileBytes);  // hi, lo contiguous
-    bulk_s2g(p.Qt + blk * kSavedPair, QsH, 2 * um::kTileBytes);
+    bulk_s2g(p.Xn + blk * kSavedSet<bf16>, XsH, 2 * um::kTileBytes);  // hi, lo contiguous
+    bulk_s2g(p.Qt + blk * kSavedSet<bf16>, QsH, 2 * um::kTileBytes);
     bulk_s2g(p.Bc + blk * 4096, Bcs, (unsigned)(p.dk * p.dv * 4));
     bulk_s2g(p.Yp + blk * 4096, Yps, (unsigned)(Cc * p.dv * 4));
     bulk_commit();
@@ -814,26 +910,266 @@ __global__ void __launch_bounds__(kPrepThreads, 2) prep_kernel(const TcArgs p) {
   }
 }
 
-// Thread 0: stage the saved tile pairs Xn and Qt of one chunk (blocked, hi and
-// lo contiguous) with bulk copies completing on `bar`: X receives Xn hi, Xn lo,
-// Qt hi, Qt lo.
-__device__ __forceinline__ void stage_xq(bf16* X, const TcArgs& p, long long blk, uint64_t* bar) {
-  mbar_arrive_expect_tx(bar, 4 * umma::kTileBytes);
-  bulk_g2s(X, p.Xn + blk * kSavedPair, 2 * umma::kTileBytes, bar);
-  bulk_g2s(X + 8192, p.Qt + blk * kSavedPair, 2 * umma::kTileBytes, bar);
+// ------------------------------------------------ forward: prep (fp32) --
+// prep_kernel for fp32 inputs: the same products with every operand in three
+// bf16 levels, and T^{-1} by substitution in fp32 on the CUDA cores
+// (tri_inv_f32). One CTA per SM.
+// smem: header | 15 blocked tiles: 0-5 the levels of [K; Q] interleaved
+// (Kh Qh Km Qm Kl Ql, so each level is one M = 128 operand) | 6-8 V | 9-11 P~ |
+// 12-14 T^{-1} | beta | Tf, Xf fp32 [64][65] | Ys fp32 [16][48].
+// beta W goes over Q's levels, beta U' over V's; the outputs Xn (0-2) and Qt
+// (3-5) over K and beta W, Bc and Yp (fp32) over Tf and Xf.
+constexpr int kF32Ld = 65;
+constexpr size_t kPrepF32Smem =
+    1024 + 15 * (size_t)umma::kTileBytes + 256 + 2 * 64 * kF32Ld * 4 + 16 * 48 * 4;
+
+// X = T^{-1} for the unit lower-triangular T = I + Tf (Tf strictly lower,
+// fp32 [64][kF32Ld]) in fp32: the four diagonal 16 x 16 blocks by forward
+// substitution (a thread per column), then block row i = 1..3 from the rows
+// above it, X_ij = -D_i^{-1} sum_{k=j}^{i-1} T_ik X_kj (Ys holds the sums).
+// Only the lower blocks of X are written (the diagonal blocks with zeros above
+// the diagonal). Ends with __syncthreads.
+__device__ void tri_inv_f32(const float* Tf, float* Xf, float* Ys) {
+  const int tid = threadIdx.x;
+  if (tid < 64) {
+    const int o = (tid >> 4) * 16, j = tid & 15;
+    float x[16];
+#pragma unroll
+    for (int i = 0; i < 16; ++i) {
+      float s = 0.f;
+#pragma unroll
+      for (int k = 0; k < i; ++k) s = fmaf(Tf[(o + i) * kF32Ld + o + k], x[k], s);
+      x[i] = i == j ? 1.f : (i > j ? -s : 0.f);
+    }
+#pragma unroll
+    for (int i = 0; i < 16; ++i) Xf[(o + i) * kF32Ld + o + j] = x[i];
+  }
+  __syncthreads();
+  for (int bi = 1; bi < 4; ++bi) {
+    const int r0 = 16 * bi, ncol = 16 * bi;
+    for (int e = tid; e < 16 * ncol; e += blockDim.x) {
+      const int r = e / ncol, cc = e - r * ncol;
+      float s = 0.f;
+      for (int k = cc & ~15; k < r0; ++k) s = fmaf(Tf[(r0 + r) * kF32Ld + k], Xf[k * kF32Ld + cc], s);
+      Ys[r * 48 + cc] = s;
+    }
+    __syncthreads();
+    for (int e = tid; e < 16 * ncol; e += blockDim.x) {
+      const int r = e / ncol, cc = e - r * ncol;
+      float s = 0.f;
+      for (int k = 0; k <= r; ++k) s = fmaf(Xf[(r0 + r) * kF32Ld + r0 + k], Ys[k * 48 + cc], s);
+      Xf[(r0 + r) * kF32Ld + cc] = -s;
+    }
+    __syncthreads();
+  }
+}
+
+__global__ void __launch_bounds__(kPrepThreads, 1) prep_f32_kernel(const TcArgs<float> p) {
+  namespace um = umma;
+  extern __shared__ __align__(1024) unsigned char psmem[];
+  uint64_t* bar = reinterpret_cast<uint64_t*>(psmem);  // [0] level 1, [1] levels 3-4 (two issuers)
+  uint32_t* tbase_s = reinterpret_cast<uint32_t*>(psmem + 64);
+  bf16* bt = reinterpret_cast<bf16*>(psmem + 1024);
+  auto T = [&](int i) { return bt + i * 4096; };
+  const Lv K = lv(T(0), T(2), T(4)), Q = lv(T(1), T(3), T(5)), V = lv(T(6), T(7), T(8));
+  const Lv P = lv(T(9), T(10), T(11)), Ti = lv(T(12), T(13), T(14));
+  const Lv &BW = Q, &BU = V;
+  const Lv Xs = lv(T(0), T(1), T(2)), Qs = lv(T(3), T(4), T(5));
+  float* bs = reinterpret_cast<float*>(T(15));
+  float* Tf = bs + 64;
+  float* Xf = Tf + 64 * kF32Ld;
+  float* Ys = Xf + 64 * kF32Ld;
+  float* Bcs = Tf;  // outputs, after the last products
+  float* Yps = Xf;
+
+  constexpr int NTH = kPrepThreads;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int q = warp & 3, hh = warp >> 2;
+  const int c = blockIdx.x % p.nchunks;
+  const long long bh = blockIdx.x / p.nchunks;
+  const long long t0 = (long long)c * p.C;
+  const int Cc = (int)min((long long)p.C, p.T - t0), Mc = Cc * p.nh;
+  const long long r0 = t0 * p.nh, rows = p.T * p.nh;
+  const long long blk = bh * p.nchunks + c;
+
+  if (warp == 0) um::alloc(tbase_s, 256);
+  if (tid == 0) {
+    mbar_init(bar, 1);
+    mbar_init(bar + 1, 2);
+    mbar_fence_init();
+  }
+  stage_in<NTH>(K, p.K + (bh * rows + r0) * p.dk, p.dk, Mc, p.dk >> 3);
+  stage_in<NTH>(Q, p.Q + (bh * p.T + t0) * p.dk, p.dk, Cc, p.dk >> 3);
+  stage_in<NTH>(V, p.V + (bh * rows + r0) * p.dv, p.dv, Mc, p.dv >> 3);
+  if (tid < 64) bs[tid] = tid < Mc ? p.beta[bh * rows + r0 + tid] : 0.f;
+  // okw: every wait so far completed (as in prep_kernel).
+  bool okw = true;
+  auto to_mma = [&]() {
+    fence_proxy_async_smem();
+    um::fence_before();
+    okw = !__syncthreads_or(!okw);
+    um::fence_after();
+  };
+  to_mma();
+  const uint32_t tb = *tbase_s;
+  const uint32_t tA = tb, tB = tb + 64, tC = tb + 128, tD = tb + 192;
+
+  // level 1: [K; Q] K^T, M = 128
+  if (tid == 0) {
+    const um::Prod ps[1] = {{tA, op(K, false), op(K, false), false, true}};
+    um::products(ps);
+    um::commit(bar);
+  }
+  okw = mbar_wait(bar, 0, &g_sticky_err);
+  um::fence_after();
+  {  // row r = 32 q + lane of the M = 128 accumulator: T row r (r < 64) or P~ row r - 64
+    const int r = 32 * q + lane;
+    const uint32_t lb = tb + ((uint32_t)(32 * q) << 16) + 32 * hh;
+#pragma unroll
+    for (int half = 0; half < 2; ++half) {
+      const int c0 = 32 * hh + 16 * half;
+      float v[16];
+      um::ld16(lb + 16 * half, v);
+      if (r < 64) {
+#pragma unroll
+        for (int i = 0; i < 16; ++i) Tf[r * kF32Ld + c0 + i] = c0 + i < r ? v[i] * bs[c0 + i] : 0.f;
+      } else {
+        const int ti = r - 64;
+#pragma unroll
+        for (int i = 0; i < 16; ++i) v[i] = (c0 + i < (ti + 1) * p.nh && c0 + i < Mc) ? v[i] : 0.f;
+        store16(P, ti, c0, v);
+      }
+    }
+  }
+  um::fence_before();
+  okw = !__syncthreads_or(!okw);
+  tri_inv_f32(Tf, Xf, Ys);  // ends with __syncthreads
+  for (int i = tid; i < 64 * 8; i += NTH) {  // X -> blocked levels of T^{-1}
+    const int row = i >> 3, ch = i & 7;
+    float v[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) v[j] = ch * 8 + j <= row ? Xf[row * kF32Ld + ch * 8 + j] : 0.f;
+    store8(Ti, um::boff(row, ch * 8), v);
+  }
+  to_mma();
+  if (okw && tid == 64) {  // T^{-1} (three contiguous levels) to `saved`; its tiles stay untouched
+    bulk_s2g(p.Ti + blk * kSavedSet<float>, Ti.t[0], 3 * um::kTileBytes);
+    bulk_commit();
+  }
+  // level 3: W = Ti K (B), U' = Ti V (C)
+  if (okw && (tid == 0 || tid == 32)) {
+    const um::Prod ps[1] = {{tid == 0 ? tB : tC, op(Ti, false), op(tid == 0 ? K : V, true), false}};
+    um::products(ps);
+    um::commit(bar + 1);
+  }
+  if (okw) okw = mbar_wait(bar + 1, 0, &g_sticky_err);
+  um::fence_after();
+  const int row = 16 * q + lane;  // M = 64 accumulators: lanes 0-15 hold rows
+  const bool rv = lane < 16;
+  const uint32_t lb = tb + ((uint32_t)(32 * q) << 16) + 32 * hh;
+#pragma unroll
+  for (int half = 0; half < 2; ++half) {  // beta W (over Q), beta U' (over V)
+    const int c0 = 32 * hh + 16 * half;
+    uint32_t r1[16], r2[16];
+    float w[16], u[16];
+    um::ld16_async(lb + 64 + 16 * half, r1);
+    um::ld16_async(lb + 128 + 16 * half, r2);
+    um::ld_wait();
+    um::ld_bind(r1, w);
+    um::ld_bind(r2, u);
+    if (rv) {
+      const float b = bs[row];
+#pragma unroll
+      for (int i = 0; i < 16; ++i) {
+        w[i] *= b;
+        u[i] *= b;
+      }
+      store16(BW, row, c0, w);
+      store16(BU, row, c0, u);
+    }
+  }
+  to_mma();
+  // level 4: K^T (beta W) (A), P~ (beta W) (B), K^T (beta U') (C), P~ (beta U') (D)
+  if (okw && tid == 0) {
+    const um::Opnd oBW = op(BW, true);
+    const um::Prod ps[2] = {{tA, op(K, true), oBW, false}, {tB, op(P, false), oBW, false}};
+    um::products(ps);
+    um::commit(bar + 1);
+  } else if (okw && tid == 32) {
+    const um::Opnd oBU = op(BU, true);
+    const um::Prod ps[2] = {{tC, op(K, true), oBU, false}, {tD, op(P, false), oBU, false}};
+    um::products(ps);
+    um::commit(bar + 1);
+  }
+  if (okw) okw = mbar_wait(bar + 1, 1, &g_sticky_err);
+  um::fence_after();
+  okw = !__syncthreads_or(!okw);
+#pragma unroll
+  for (int half = 0; half < 2; ++half) {  // Xn, Qt (saved), Bc, Yp (workspace, fp32)
+    const int c0 = 32 * hh + 16 * half;
+    uint32_t r1[16], r2[16], r3[16], r4[16];
+    float x[16], qt[16], bc[16], yp[16];
+    um::ld16_async(lb + 0 + 16 * half, r1);
+    um::ld16_async(lb + 64 + 16 * half, r2);
+    um::ld16_async(lb + 128 + 16 * half, r3);
+    um::ld16_async(lb + 192 + 16 * half, r4);
+    um::ld_wait();
+    um::ld_bind(r1, x);
+    um::ld_bind(r2, qt);
+    um::ld_bind(r3, bc);
+    um::ld_bind(r4, yp);
+    if (rv) {
+      float qv[16];  // Q row `row`, columns c0.. (fp32, from global: exact)
+      const float* qg = p.Q + (bh * p.T + t0 + row) * p.dk + c0;
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        const float4 a = row < Cc && c0 + 4 * k < p.dk ? __ldg(reinterpret_cast<const float4*>(qg + 4 * k))
+                                                       : make_float4(0.f, 0.f, 0.f, 0.f);
+        qv[4 * k] = a.x;
+        qv[4 * k + 1] = a.y;
+        qv[4 * k + 2] = a.z;
+        qv[4 * k + 3] = a.w;
+      }
+#pragma unroll
+      for (int i = 0; i < 16; ++i) {
+        x[i] = -x[i];
+        qt[i] = qv[i] - qt[i];
+      }
+      store16(Xs, row, c0, x);
+      store16(Qs, row, c0, qt);
+      if (row < p.dk) row16_f32_to_global(Bcs + row * p.dv, c0, p.dv, bc);
+      if (row < Cc) row16_f32_to_global(Yps + row * p.dv, c0, p.dv, yp);
+    }
+  }
+  fence_proxy_async_smem();
+  um::fence_before();
+  __syncthreads();
+  if (okw && tid == 0) {
+    bulk_s2g(p.Xn + blk * kSavedSet<float>, Xs.t[0], 3 * um::kTileBytes);  // levels contiguous
+    bulk_s2g(p.Qt + blk * kSavedSet<float>, Qs.t[0], 3 * um::kTileBytes);
+    bulk_s2g(p.Bc + blk * 4096, Bcs, (unsigned)(p.dk * p.dv * 4));
+    bulk_s2g(p.Yp + blk * 4096, Yps, (unsigned)(Cc * p.dv * 4));
+    bulk_commit();
+    bulk_wait_read();  // shared memory stays valid until the copies have read it
+  }
+  if (tid == 64) bulk_wait_read();  // the T^{-1} copy has read its tiles
+  if (warp == 0) {
+    um::fence_after();
+    um::dealloc(tb, 256);
+  }
 }
 
 // The chunk-serial kernels: one CTA per (b, h, 32 value columns), 8 warps.
 // Thread (warp w, lane l < 16) owns row 16*(w%4) + l and columns 16*(w/4)..+15
-// of the CTA's state slice, in fp32 registers; the slice is also kept as a
-// split blocked tile (64 x 32) in shared memory, the B operand of the chunk's
-// MMAs. Per chunk, thread 0 issues the state product and thread 32 the other
-// product (12 and 8-12 tcgen05 MMAs, N = 32) into TMEM; all threads then add
-// them to the state and write the new split tile. The Xn, Qt tiles of the next
-// kRing - 1 chunks are staged by bulk copies.
+// of the CTA's state slice, in fp32 registers; the slice is also kept in
+// shared memory as blocked bf16 levels (64 x 32 each), the B operand of the
+// chunk's MMAs. Per chunk, thread 0 issues the state product and thread 32
+// the other product (N = 32) into TMEM; all threads then add them to the state
+// and write its new levels. The Xn, Qt levels of the next kRing - 1 chunks are
+// staged by bulk copies.
 constexpr int kChainThreads = 256;
 constexpr int kChainCols = 32;
-constexpr int kSTile = 64 * kChainCols * 2;  // one split half of a 64 x 32 slice, bytes
+constexpr int kSTile = 64 * kChainCols * 2;  // one level of a 64 x 32 slice, bytes
 
 // 16 fp32 values at g[0..15] -> v (chunks of 8 starting below `valid`; others 0).
 __device__ __forceinline__ void load16_f32(const float* g, int c0, int valid, bool ok, float (&v)[16]) {
@@ -856,30 +1192,49 @@ __device__ __forceinline__ void store16_f32(float* g, int c0, int valid, const f
       *reinterpret_cast<float4*>(g + 8 * h + 4) = make_float4(v[8 * h + 4], v[8 * h + 5], v[8 * h + 6], v[8 * h + 7]);
     }
 }
+// 16 values -> the output row (bf16 or fp32; chunks of 8 starting below `valid`)
+__device__ __forceinline__ void store16_out(bf16* g, int c0, int valid, const float (&v)[16]) {
+#pragma unroll
+  for (int h = 0; h < 2; ++h)
+    if (c0 + 8 * h < valid) {
+      uint32_t w[4];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) w[i] = tc::pack_bf16(v[8 * h + 2 * i], v[8 * h + 2 * i + 1]);
+      *reinterpret_cast<uint4*>(g + 8 * h) = make_uint4(w[0], w[1], w[2], w[3]);
+    }
+}
+__device__ __forceinline__ void store16_out(float* g, int c0, int valid, const float (&v)[16]) {
+  store16_f32(g, c0, valid, v);
+}
 
 // ------------------------------------------------------ forward: chain --
 //   S_c saved;  y_c = Qt S_c + Yp;  S_{c+1} = S_c + Xn S_c + Bc
 // Both products share the state operand, so [Xn; Qt] is staged as one
-// M = 128 operand (Xn hi, Qt hi, Xn lo, Qt lo) and one thread issues 12 MMAs
-// per chunk. Accumulator row r sits in TMEM lane r: warps 0, 1, 4, 5 (rows
-// 0-63) own the state S, warps 2, 3, 6, 7 (rows 64-127) the output y; lane l of
-// warp w has row 32*(w%4) + l, columns 16*(w/4)..+15.
-// stage: [Xn; Qt] hi and lo (bulk copies) and every thread's 16 additive terms
-// (Bc or Yp; cp.async) as float4 [4][thread]
+// M = 128 operand per level (Xn hi, Qt hi, Xn lo, Qt lo[, Xn lo2, Qt lo2])
+// and one thread issues 12 (bf16 inputs) or 24 (fp32) MMAs per chunk.
+// Accumulator row r sits in TMEM lane r: warps 0, 1, 4, 5 (rows 0-63) own the
+// state S, warps 2, 3, 6, 7 (rows 64-127) the output y; lane l of warp w has
+// row 32*(w%4) + l, columns 16*(w/4)..+15.
+// stage: the levels of [Xn; Qt] (bulk copies) and every thread's 16 additive
+// terms (Bc or Yp; cp.async) as float4 [4][thread]
 constexpr int kCfAddend = 4 * kChainThreads * 16;
-constexpr int kCfStage = 4 * umma::kTileBytes + kCfAddend;
-constexpr size_t kChainFwdSmem = 1024 + kRing * (size_t)kCfStage + 2 * (size_t)kSTile;
+template <typename E>
+constexpr int kCfStage = 2 * kLevels<E> * umma::kTileBytes + kCfAddend;
+template <typename E>
+constexpr size_t kChainFwdSmem = 1024 + kRing * (size_t)kCfStage<E> + kLevels<E> * (size_t)kSTile;
 
-__global__ void __launch_bounds__(kChainThreads, 1) chain_fwd_kernel(const TcArgs p) {
+template <typename E>
+__global__ void __launch_bounds__(kChainThreads, 1) chain_fwd_kernel(const TcArgs<E> p) {
   namespace um = umma;
+  constexpr int L = kLevels<E>;
   extern __shared__ __align__(1024) unsigned char csmem[];
   uint64_t* full = reinterpret_cast<uint64_t*>(csmem);
   uint64_t* mbar = full + kRing;  // MMA completion
   uint32_t* tbase_s = reinterpret_cast<uint32_t*>(csmem + 64);
   unsigned char* ring = csmem + 1024;
-  bf16* SH = reinterpret_cast<bf16*>(ring + kRing * kCfStage);
-  bf16* SL = SH + 64 * kChainCols;
-  auto Xt = [&](int s) { return reinterpret_cast<bf16*>(ring + s * kCfStage); };
+  bf16* S0 = reinterpret_cast<bf16*>(ring + kRing * kCfStage<E>);
+  const Lv Sl = lv(S0, S0 + 64 * kChainCols, L > 2 ? S0 + 2 * 64 * kChainCols : nullptr);
+  auto Xt = [&](int s) { return reinterpret_cast<bf16*>(ring + s * kCfStage<E>); };
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, q = warp & 3;
   const int cb = 16 * (warp >> 2);
@@ -889,24 +1244,25 @@ __global__ void __launch_bounds__(kChainThreads, 1) chain_fwd_kernel(const TcArg
   const long long bh = blockIdx.x / p.S;
   const int c0 = split * kChainCols, ncols = min(kChainCols, p.dv - c0);
   const long long blk0 = bh * p.nchunks;
-  bf16* yg = p.y + bh * p.T * p.dv + c0 + cb;
+  E* yg = p.y + bh * p.T * p.dv + c0 + cb;
   float* Hsg = p.Hs + blk0 * p.dk * p.dv + r * p.dv + c0 + cb;
   const bool srow = st && r < p.dk;
 
   auto stage = [&](int c) {
     bf16* X = Xt(c % kRing);
-    const long long t0 = (long long)c * p.C;
-    const int Cc = (int)min((long long)p.C, p.T - t0);
     if (tid == 0) {
       uint64_t* bar = full + c % kRing;
       const long long blk = blk0 + c;
-      mbar_arrive_expect_tx(bar, 4 * umma::kTileBytes);
-      bulk_g2s(X, p.Xn + blk * kSavedPair, umma::kTileBytes, bar);
-      bulk_g2s(X + 4096, p.Qt + blk * kSavedPair, umma::kTileBytes, bar);
-      bulk_g2s(X + 8192, p.Xn + blk * kSavedPair + 4096, umma::kTileBytes, bar);
-      bulk_g2s(X + 12288, p.Qt + blk * kSavedPair + 4096, umma::kTileBytes, bar);
+      mbar_arrive_expect_tx(bar, 2 * L * umma::kTileBytes);
+#pragma unroll
+      for (int l = 0; l < L; ++l) {
+        bulk_g2s(X + 8192 * l, p.Xn + blk * kSavedSet<E> + 4096 * l, umma::kTileBytes, bar);
+        bulk_g2s(X + 8192 * l + 4096, p.Qt + blk * kSavedSet<E> + 4096 * l, umma::kTileBytes, bar);
+      }
     }
-    float4* ad = reinterpret_cast<float4*>(X + 16384);
+    const long long t0 = (long long)c * p.C;
+    const int Cc = (int)min((long long)p.C, p.T - t0);
+    float4* ad = reinterpret_cast<float4*>(X + 8192 * L);
     const bool ok = st ? srow : r < Cc;
     const float* g = (st ? p.Bc : p.Yp) + (blk0 + c) * 4096 + r * p.dv + c0 + cb;
 #pragma unroll
@@ -925,13 +1281,13 @@ __global__ void __launch_bounds__(kChainThreads, 1) chain_fwd_kernel(const TcArg
   }
   float hs[16];  // state threads: S row r, columns cb..cb+15 of the slice
   load16_f32(p.H0 + bh * p.dk * p.dv + r * p.dv + c0 + cb, cb, ncols, p.H0 != nullptr && srow, hs);
-  if (st) um::store_split16_n(SH, SL, r, cb, kChainCols, kChainCols, hs);
+  if (st) store16_n(Sl, r, cb, kChainCols, kChainCols, hs);
   um::fence_before();
   __syncthreads();
   um::fence_after();
   const uint32_t tb = *tbase_s;
   const uint32_t lb = tb + ((uint32_t)(32 * q) << 16) + cb;
-  const um::Opnd oS = um::opnd_mn(um::saddr(SH), um::saddr(SL), kChainCols);
+  const um::Opnd oS = op_mn(Sl, kChainCols);
   for (int c = 0; c < kRing - 1 && c < p.nchunks; ++c) stage(c);
   if (srow) store16_f32(Hsg, cb, ncols, hs);
 
@@ -949,7 +1305,7 @@ __global__ void __launch_bounds__(kChainThreads, 1) chain_fwd_kernel(const TcArg
     else
       cp_async_wait_all();
     if (okw) okw = mbar_wait(full + s, (unsigned)(c / kRing) & 1u, &g_sticky_err);
-    fence_proxy_async_smem();  // the split state written below in the previous chunk
+    fence_proxy_async_smem();  // the state levels written below in the previous chunk
     um::fence_before();
     // every thread is past chunk c - 1: its stage may be refilled
     if (__syncthreads_or(!okw)) {
@@ -958,10 +1314,11 @@ __global__ void __launch_bounds__(kChainThreads, 1) chain_fwd_kernel(const TcArg
     }
     um::fence_after();
     if (c + kRing - 1 < p.nchunks) stage(c + kRing - 1);
-    const float4* ad = reinterpret_cast<const float4*>(Xt(s) + 16384);
+    const float4* ad = reinterpret_cast<const float4*>(Xt(s) + 8192 * L);
     if (tid == 0) {  // [Xn; Qt] S, M = 128
       const uint32_t X = um::saddr(Xt(s));
-      const um::Prod ps[1] = {{tb, um::opnd(X, X + 16384, false), oS, false, true, kChainCols}};
+      const um::Prod ps[1] = {
+          {tb, um::opnd3(X, X + 16384, L > 2 ? X + 32768 : 0u, false), oS, false, true, kChainCols}};
       um::products(ps);
       um::commit(mbar);
     }
@@ -981,17 +1338,10 @@ __global__ void __launch_bounds__(kChainThreads, 1) chain_fwd_kernel(const TcArg
     if (st) {
 #pragma unroll
       for (int i = 0; i < 16; ++i) hs[i] += v[i];
-      um::store_split16_n(SH, SL, r, cb, kChainCols, kChainCols, hs);
+      store16_n(Sl, r, cb, kChainCols, kChainCols, hs);
       if (srow && c + 1 < p.nchunks) store16_f32(Hsg + (long long)(c + 1) * p.dk * p.dv, cb, ncols, hs);
     } else if (r < Cc) {
-#pragma unroll
-      for (int h = 0; h < 2; ++h)
-        if (cb + 8 * h < ncols) {
-          uint32_t w[4];
-#pragma unroll
-          for (int i = 0; i < 4; ++i) w[i] = tc::pack_bf16(v[8 * h + 2 * i], v[8 * h + 2 * i + 1]);
-          *reinterpret_cast<uint4*>(yg + (t0 + r) * p.dv + 8 * h) = make_uint4(w[0], w[1], w[2], w[3]);
-        }
+      store16_out(yg + (t0 + r) * p.dv, cb, ncols, v);
     }
   }
   if (!okw) {  // drain: the stages of chunks c .. c + kRing - 2 may still be in flight
@@ -1012,19 +1362,31 @@ __global__ void __launch_bounds__(kChainThreads, 1) chain_fwd_kernel(const TcArg
 
 // ----------------------------------------------------- backward: chain --
 //   dS'_c (= dS entering from chunk c + 1) saved;  dS_c = dS'_c + Xn^T dS'_c + Qt^T dy_c
-constexpr int kCbStage = 4 * umma::kTileBytes + kSTile;  // Xn h/l, Qt h/l, dy (64 x 32)
-constexpr size_t kChainBwdSmem = 1024 + kRing * (size_t)kCbStage + 2 * (size_t)kSTile;
+// stage: Xn levels, Qt levels (bulk copies), then dy: bf16 inputs as a blocked
+// 64 x 32 tile (cp.async); fp32 inputs as raw rows [64][32] (cp.async, 8
+// columns per thread), split into three levels by the thread that copied them
+// once its copies have landed.
+template <typename E>
+constexpr int kCbStage = 2 * kLevels<E> * umma::kTileBytes + (kF32<E> ? 64 * kChainCols * 4 : kSTile);
+template <typename E>
+constexpr size_t kChainBwdSmem = 1024 + kRing * (size_t)kCbStage<E> + kLevels<E> * (size_t)kSTile +
+                                 (kF32<E> ? 3 * (size_t)kSTile : 0);
 
-__global__ void __launch_bounds__(kChainThreads, 1) chain_bwd_kernel(const TcArgs p) {
+template <typename E>
+__global__ void __launch_bounds__(kChainThreads, 1) chain_bwd_kernel(const TcArgs<E> p) {
   namespace um = umma;
+  constexpr bool F = kF32<E>;
+  constexpr int L = kLevels<E>;
   extern __shared__ __align__(1024) unsigned char csmem[];
   uint64_t* full = reinterpret_cast<uint64_t*>(csmem);
   uint64_t* mbar = full + kRing;
   uint32_t* tbase_s = reinterpret_cast<uint32_t*>(csmem + 64);
   unsigned char* ring = csmem + 1024;
-  bf16* DH = reinterpret_cast<bf16*>(ring + kRing * kCbStage);
-  bf16* DL = DH + 64 * kChainCols;
-  auto Xt = [&](int s) { return reinterpret_cast<bf16*>(ring + s * kCbStage); };
+  bf16* D0 = reinterpret_cast<bf16*>(ring + kRing * kCbStage<E>);
+  const Lv Dl = lv(D0, D0 + 64 * kChainCols, L > 2 ? D0 + 2 * 64 * kChainCols : nullptr);
+  bf16* Y0 = D0 + L * 64 * kChainCols;  // fp32 inputs: dy levels of the current step
+  const Lv Yl = lv(Y0, Y0 + 64 * kChainCols, Y0 + 2 * 64 * kChainCols);
+  auto Xt = [&](int s) { return reinterpret_cast<bf16*>(ring + s * kCbStage<E>); };
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, q = warp & 3;
   const int row = 16 * q + lane, cb = 16 * (warp >> 2);
@@ -1033,23 +1395,35 @@ __global__ void __launch_bounds__(kChainThreads, 1) chain_bwd_kernel(const TcArg
   const long long bh = blockIdx.x / p.S;
   const int c0 = split * kChainCols, ncols = min(kChainCols, p.dv - c0);
   const long long blk0 = bh * p.nchunks;
-  const bf16* dyg = p.dy + bh * p.T * p.dv + c0;
+  const E* dyg = p.dy + bh * p.T * p.dv + c0;
   float* dHsg = p.dHs + blk0 * p.dk * p.dv + row * p.dv + c0 + cb;
   const bool srow = rv && row < p.dk;
   const int last = p.nchunks - 1;
+  const int yr = tid >> 2, ych = tid & 3;  // dy staging: 64 rows x 4 chunks of 8 columns
 
   // step qq handles chunk last - qq in ring slot qq % kRing
   auto stage = [&](int qq) {
     const int c = last - qq;
     bf16* X = Xt(qq % kRing);
-    if (tid == 0) stage_xq(X, p, blk0 + c, full + qq % kRing);
+    if (tid == 0) {
+      uint64_t* bar = full + qq % kRing;
+      const long long blk = blk0 + c;
+      mbar_arrive_expect_tx(bar, 2 * L * umma::kTileBytes);
+      bulk_g2s(X, p.Xn + blk * kSavedSet<E>, L * umma::kTileBytes, bar);
+      bulk_g2s(X + 4096 * L, p.Qt + blk * kSavedSet<E>, L * umma::kTileBytes, bar);
+    }
     const long long t0 = (long long)c * p.C;
     const int Cc = (int)min((long long)p.C, p.T - t0);
-    bf16* dY = X + 16384;
-    const int r = tid >> 2, ch = tid & 3;  // 64 rows x 4 chunks of 8 columns
-    const bool ok = r < Cc && 8 * ch < ncols;
-    const bf16* src = dyg + (t0 + r) * p.dv + 8 * ch;
-    cp_async16(dY + um::boff_n(r, 8 * ch, kChainCols), ok ? src : dyg, ok ? 16 : 0);
+    const bool ok = yr < Cc && 8 * ych < ncols;
+    const E* src = dyg + (t0 + yr) * p.dv + 8 * ych;
+    if constexpr (F) {
+      float* raw = reinterpret_cast<float*>(X + 8192 * L) + yr * kChainCols + 8 * ych;
+      cp_async16(raw, ok ? src : dyg, ok ? 16 : 0);
+      cp_async16(raw + 4, ok ? src + 4 : dyg, ok ? 16 : 0);
+    } else {
+      bf16* dY = X + 8192 * L;
+      cp_async16(dY + um::boff_n(yr, 8 * ych, kChainCols), ok ? src : dyg, ok ? 16 : 0);
+    }
     cp_async_commit();
   };
 
@@ -1061,7 +1435,7 @@ __global__ void __launch_bounds__(kChainThreads, 1) chain_bwd_kernel(const TcArg
   }
   float ds[16];
   load16_f32(p.dHT + bh * p.dk * p.dv + row * p.dv + c0 + cb, cb, ncols, p.dHT != nullptr && srow, ds);
-  if (rv) um::store_split16_n(DH, DL, row, cb, kChainCols, kChainCols, ds);
+  if (rv) store16_n(Dl, row, cb, kChainCols, kChainCols, ds);
   um::fence_before();
   __syncthreads();
   um::fence_after();
@@ -1069,7 +1443,7 @@ __global__ void __launch_bounds__(kChainThreads, 1) chain_bwd_kernel(const TcArg
   const uint32_t lb = tb + ((uint32_t)(32 * q) << 16) + cb;
   for (int qq = 0; qq < kRing - 1 && qq <= last; ++qq) stage(qq);
   if (srow) store16_f32(dHsg + (long long)last * p.dk * p.dv, cb, ncols, ds);
-  const um::Opnd oD = um::opnd_mn(um::saddr(DH), um::saddr(DL), kChainCols);
+  const um::Opnd oD = op_mn(Dl, kChainCols);
 
   // okw: as in chain_fwd_kernel (a wait that runs out ends the loop in every
   // thread at the next barrier, then the CTA drains its copies and stops).
@@ -1081,8 +1455,15 @@ __global__ void __launch_bounds__(kChainThreads, 1) chain_bwd_kernel(const TcArg
       asm volatile("cp.async.wait_group 1;\n" ::: "memory");
     else
       cp_async_wait_all();
+    if constexpr (F) {  // this thread's dy copies have landed: split them into levels
+      const float* raw = reinterpret_cast<const float*>(Xt(s) + 8192 * L) + yr * kChainCols + 8 * ych;
+      const float4 a = *reinterpret_cast<const float4*>(raw);
+      const float4 b = *reinterpret_cast<const float4*>(raw + 4);
+      const float v[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
+      store8(Yl, um::boff_n(yr, 8 * ych, kChainCols), v);
+    }
     if (okw) okw = mbar_wait(full + s, (unsigned)(qq / kRing) & 1u, &g_sticky_err);
-    fence_proxy_async_smem();  // dy (cp.async) and the split dS written in the previous step
+    fence_proxy_async_smem();  // dy and the dS levels written in the previous step
     um::fence_before();
     if (__syncthreads_or(!okw)) {
       okw = false;
@@ -1092,12 +1473,15 @@ __global__ void __launch_bounds__(kChainThreads, 1) chain_bwd_kernel(const TcArg
     if (qq + kRing - 1 <= last) stage(qq + kRing - 1);
     const uint32_t X = um::saddr(Xt(s));
     if (tid == 0) {  // Xn^T dS'
-      const um::Prod ps[1] = {{tX, um::opnd(X, X + 8192, true), oD, false, false, kChainCols}};
+      const um::Prod ps[1] = {{tX, um::opnd3(X, X + 8192, L > 2 ? X + 16384 : 0u, true), oD, false,
+                               false, kChainCols}};
       um::products(ps);
       um::commit(mbar);
     } else if (tid == 32) {  // Qt^T dy
-      const um::Prod ps[1] = {{tY, um::opnd(X + 16384, X + 24576, true),
-                               um::opnd_mn(X + 32768, 0, kChainCols), false, false, kChainCols}};
+      const uint32_t Qa = X + 8192 * L;
+      const um::Opnd oY = F ? op_mn(Yl, kChainCols) : um::opnd_mn(X + 16384 * L, 0, kChainCols);
+      const um::Prod ps[1] = {{tY, um::opnd3(Qa, Qa + 8192, L > 2 ? Qa + 16384 : 0u, true), oY,
+                               false, false, kChainCols}};
       um::products(ps);
       um::commit(mbar);
     }
@@ -1114,7 +1498,7 @@ __global__ void __launch_bounds__(kChainThreads, 1) chain_bwd_kernel(const TcArg
     if (rv) {
 #pragma unroll
       for (int i = 0; i < 16; ++i) ds[i] += xs[i] + ys[i];
-      um::store_split16_n(DH, DL, row, cb, kChainCols, kChainCols, ds);
+      store16_n(Dl, row, cb, kChainCols, kChainCols, ds);
     }
     if (srow && c > 0) store16_f32(dHsg + (long long)(c - 1) * p.dk * p.dv, cb, ncols, ds);
   }
@@ -1136,43 +1520,21 @@ __global__ void __launch_bounds__(kChainThreads, 1) chain_bwd_kernel(const TcArg
 
 // ---------------------------------------------------------------- host --
 
-
-template <class K>
-int launch_tc(K kernel, long long grid, size_t smem, cudaStream_t st, const TcArgs& a,
-              int threads = kTcThreads) {
+template <class K, class A>
+int launch_tc(K kernel, long long grid, size_t smem, cudaStream_t st, const A& a, int threads) {
   MGS_CUDA_OK(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
-  TcArgs args = a;
+  A args = a;
   void* kargs[] = {&args};
   MGS_CUDA_OK(cudaLaunchKernel((const void*)kernel, dim3((unsigned)grid), dim3(threads), kargs,
                                smem, st));
   return MGS_OK;
 }
 
-}  // namespace
-
-bool tc_eligible(int dtype, int nh, int dk, int dv, int C) {
-  return dtype == MGS_BF16 && nh >= 1 && C >= 1 && nh * C <= 64 && dk >= 8 && dk <= 64 &&
-         dv >= 8 && dv <= 64 && dk % 8 == 0 && dv % 8 == 0;
-}
-
-// saved: chunk-start states (fp32), then every chunk's T^{-1}, Xn and Qt
-// (split bf16 tile pairs, hi then lo, in the tcgen05 blocked layout)
-size_t tc_saved_floats(long long BH, long long T, int dk, int dv, int C) {
-  const size_t nc = (size_t)BH * (size_t)((T + C - 1) / C);
-  return nc * dk * dv + 3 * nc * (size_t)kSavedPair / 2;
-}
-
-// forward: Bc and Yp (4096 floats each per chunk); backward: dS' per chunk
-size_t tc_workspace_floats(long long BH, long long T, int dk, int dv, int C) {
-  const size_t nc = (size_t)BH * (size_t)((T + C - 1) / C);
-  const size_t bwd = nc * dk * dv, fwd = 2 * nc * 4096;
-  return fwd > bwd ? fwd : bwd;
-}
-
-int run_tc(bool fwd, const Args<__nv_bfloat16>& p, long long B, int H, long long T, int nh, int dk,
-           int dv, int C, float* saved, void* ws, size_t ws_bytes, cudaStream_t st) {
+template <typename E>
+int run_tc_impl(bool fwd, const Args<E>& p, long long B, int H, long long T, int nh, int dk, int dv,
+                int C, float* saved, void* ws, size_t ws_bytes, cudaStream_t st) {
   const long long BH = B * (long long)H;
-  TcArgs a{};
+  TcArgs<E> a{};
   a.Q = p.Q;
   a.K = p.K;
   a.V = p.V;
@@ -1200,8 +1562,8 @@ int run_tc(bool fwd, const Args<__nv_bfloat16>& p, long long B, int H, long long
   const size_t ncs = (size_t)BH * a.nchunks;
   a.Hs = saved;
   a.Ti = reinterpret_cast<bf16*>(saved + ncs * dk * dv);
-  a.Xn = a.Ti + ncs * kSavedPair;
-  a.Qt = a.Xn + ncs * kSavedPair;
+  a.Xn = a.Ti + ncs * kSavedSet<E>;
+  a.Qt = a.Xn + ncs * kSavedSet<E>;
   if (T > 0 && (ws == nullptr || ws_bytes < tc_workspace_floats(BH, T, dk, dv, C) * sizeof(float)))
     return MGS_WORKSPACE_TOO_SMALL;
   if (fwd) {
@@ -1215,9 +1577,13 @@ int run_tc(bool fwd, const Args<__nv_bfloat16>& p, long long B, int H, long long
     }
     a.Bc = static_cast<float*>(ws);
     a.Yp = a.Bc + ncs * 4096;
-    const int rc = launch_tc(prep_kernel, (long long)ncs, kPrepSmem, st, a, kPrepThreads);
+    int rc;
+    if constexpr (kF32<E>)
+      rc = launch_tc(prep_f32_kernel, (long long)ncs, kPrepF32Smem, st, a, kPrepThreads);
+    else
+      rc = launch_tc(prep_kernel, (long long)ncs, kPrepSmem, st, a, kPrepThreads);
     if (rc != MGS_OK) return rc;
-    return launch_tc(chain_fwd_kernel, BH * a.S, kChainFwdSmem, st, a, kChainThreads);
+    return launch_tc(chain_fwd_kernel<E>, BH * a.S, kChainFwdSmem<E>, st, a, kChainThreads);
   }
   if (T == 0) {
     if (p.dHT)
@@ -1228,9 +1594,41 @@ int run_tc(bool fwd, const Args<__nv_bfloat16>& p, long long B, int H, long long
     return MGS_OK;
   }
   a.dHs = static_cast<float*>(ws);
-  int rc = launch_tc(chain_bwd_kernel, BH * a.S, kChainBwdSmem, st, a, kChainThreads);
+  int rc = launch_tc(chain_bwd_kernel<E>, BH * a.S, kChainBwdSmem<E>, st, a, kChainThreads);
   if (rc != MGS_OK) return rc;
-  return launch_tc(bwd_grads_kernel, BH * a.nchunks, kGradSmem, st, a, kGradThreads);
+  return launch_tc(bwd_grads_kernel<E>, BH * a.nchunks, kGradSmem<E>, st, a, kGradThreads);
+}
+
+}  // namespace
+
+bool tc_eligible(int dtype, int nh, int dk, int dv, int C) {
+  return (dtype == MGS_BF16 || dtype == MGS_F32) && nh >= 1 && C >= 1 && nh * C <= 64 && dk >= 8 &&
+         dk <= 64 && dv >= 8 && dv <= 64 && dk % 8 == 0 && dv % 8 == 0;
+}
+
+// saved: chunk-start states (fp32), then every chunk's T^{-1}, Xn and Qt
+// (bf16 levels -- two for bf16 inputs, three for fp32 -- in the tcgen05
+// blocked layout)
+size_t tc_saved_floats(long long BH, long long T, int dk, int dv, int C, int dtype) {
+  const size_t nc = (size_t)BH * (size_t)((T + C - 1) / C);
+  const size_t set = dtype == MGS_F32 ? (size_t)kSavedSet<float> : (size_t)kSavedSet<bf16>;
+  return nc * dk * dv + 3 * nc * set / 2;
+}
+
+// forward: Bc and Yp (4096 floats each per chunk); backward: dS' per chunk
+size_t tc_workspace_floats(long long BH, long long T, int dk, int dv, int C) {
+  const size_t nc = (size_t)BH * (size_t)((T + C - 1) / C);
+  const size_t bwd = nc * dk * dv, fwd = 2 * nc * 4096;
+  return fwd > bwd ? fwd : bwd;
+}
+
+int run_tc(bool fwd, const Args<__nv_bfloat16>& p, long long B, int H, long long T, int nh, int dk,
+           int dv, int C, float* saved, void* ws, size_t ws_bytes, cudaStream_t st) {
+  return run_tc_impl(fwd, p, B, H, T, nh, dk, dv, C, saved, ws, ws_bytes, st);
+}
+int run_tc(bool fwd, const Args<float>& p, long long B, int H, long long T, int nh, int dk, int dv,
+           int C, float* saved, void* ws, size_t ws_bytes, cudaStream_t st) {
+  return run_tc_impl(fwd, p, B, H, T, nh, dk, dv, C, saved, ws, ws_bytes, st);
 }
 
 }  // namespace delta

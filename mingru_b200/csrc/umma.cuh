@@ -68,6 +68,7 @@ struct Opnd {
   uint64_t hi, lo;
   uint32_t step;
   bool mn;
+  uint64_t lo2 = 0;  // third level (0: none): x = hi + lo + lo2 for fp32-grade operands
 };
 
 // MN-major operand from a blocked tile of `cols` columns (a multiple of 8;
@@ -96,9 +97,24 @@ __device__ __forceinline__ Opnd opnd(uint32_t hi_addr, uint32_t lo_addr, bool mn
   o.lo = lo_addr == 0 ? 0 : (mn ? desc(lo_addr, 1024, 128) : desc(lo_addr, 128, 1024));
   return o;
 }
+// Three-level operand (64-column blocked tiles; a zero address drops a level).
+__device__ __forceinline__ Opnd opnd3(uint32_t hi_addr, uint32_t lo_addr, uint32_t lo2_addr, bool mn) {
+  Opnd o = opnd(hi_addr, lo_addr, mn);
+  o.lo2 = lo2_addr == 0 ? 0 : (mn ? desc(lo2_addr, 1024, 128) : desc(lo2_addr, 128, 1024));
+  return o;
+}
+// Three-level MN-major operand of a blocked tile of `cols` columns.
+__device__ __forceinline__ Opnd opnd_mn3(uint32_t hi_addr, uint32_t lo_addr, uint32_t lo2_addr,
+                                         int cols) {
+  Opnd o = opnd_mn(hi_addr, lo_addr, cols);
+  o.lo2 = lo2_addr == 0 ? 0 : desc(lo2_addr, (uint32_t)cols * 16, 128);
+  return o;
+}
 
 // One product of a batch: D (+)= A B^T over K = 64 with the hi*hi, hi*lo and
-// lo*hi terms.
+// lo*hi terms; where either operand has a third level, also hi*lo2, lo2*hi
+// and lo*lo (every term down to 2^-16 of the leading one: the dropped terms
+// are below 2^-24 relative, fp32 rounding).
 struct Prod {
   uint32_t d;
   Opnd A, B;
@@ -124,6 +140,9 @@ __device__ __forceinline__ void products(const Prod (&ps)[N]) {
       mma(p.d, p.A.hi + oa, p.B.hi + ob, id, kk > 0 || p.accumulate);
       if (p.B.lo) mma(p.d, p.A.hi + oa, p.B.lo + ob, id, true);
       if (p.A.lo) mma(p.d, p.A.lo + oa, p.B.hi + ob, id, true);
+      if (p.B.lo2) mma(p.d, p.A.hi + oa, p.B.lo2 + ob, id, true);
+      if (p.A.lo2) mma(p.d, p.A.lo2 + oa, p.B.hi + ob, id, true);
+      if ((p.A.lo2 || p.B.lo2) && p.A.lo && p.B.lo) mma(p.d, p.A.lo + oa, p.B.lo + ob, id, true);
     }
 }
 
@@ -243,6 +262,32 @@ __device__ __forceinline__ void store_split16_n(__nv_bfloat16* hi, __nv_bfloat16
     *reinterpret_cast<uint4*>(hi + o) = make_uint4(ph[0], ph[1], ph[2], ph[3]);
     *reinterpret_cast<uint4*>(lo + o) = make_uint4(pl[0], pl[1], pl[2], pl[3]);
   }
+}
+
+// x -> bf16 levels h, m, l with x = h + m + l to within 2^-24 relative
+// (each level is the bf16 rounding of what the previous ones leave; the
+// differences are exact in fp32), for two values packed per 32-bit word.
+__device__ __forceinline__ void split3_pack(float x0, float x1, uint32_t& h, uint32_t& m, uint32_t& l) {
+  __nv_bfloat162 bh = __floats2bfloat162_rn(x0, x1);
+  const float2 fh = __bfloat1622float2(bh);
+  const float r0 = x0 - fh.x, r1 = x1 - fh.y;
+  __nv_bfloat162 bm = __floats2bfloat162_rn(r0, r1);
+  const float2 fm = __bfloat1622float2(bm);
+  __nv_bfloat162 bl = __floats2bfloat162_rn(r0 - fm.x, r1 - fm.y);
+  h = *reinterpret_cast<uint32_t*>(&bh);
+  m = *reinterpret_cast<uint32_t*>(&bm);
+  l = *reinterpret_cast<uint32_t*>(&bl);
+}
+
+// 8 consecutive values -> three levels at element offset o of tiles h, m, l.
+__device__ __forceinline__ void store_split8_3(__nv_bfloat16* h, __nv_bfloat16* m, __nv_bfloat16* l,
+                                               int o, const float* v) {
+  uint32_t ph[4], pm[4], pl[4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) split3_pack(v[2 * i], v[2 * i + 1], ph[i], pm[i], pl[i]);
+  *reinterpret_cast<uint4*>(h + o) = make_uint4(ph[0], ph[1], ph[2], ph[3]);
+  *reinterpret_cast<uint4*>(m + o) = make_uint4(pm[0], pm[1], pm[2], pm[3]);
+  *reinterpret_cast<uint4*>(l + o) = make_uint4(pl[0], pl[1], pl[2], pl[3]);
 }
 
 }  // namespace umma

@@ -1000,7 +1000,8 @@ def _delta_checked(
     ``chunk_size`` whose one-token chunk fits the kernels' shared memory
     (``nh`` up to 96 at ``d_k = d_v = 64``). The chunked form is exact for any
     chunk length, so the kernels may use shorter chunks than ``chunk_size``
-    (whole tokens, at most ``64 / nh`` on the bf16 tensor-core kernels) -- the
+    (whole tokens, at most ``64 / nh`` on the tensor-core kernels that bf16
+    and fp32 inputs with ``d_k, d_v <= 64`` take) -- the
     result differs only by rounding. The state's value columns evolve
     independently, so ``d_v > 64`` runs as blocks of 64 columns whose
     gradients w.r.t. Q, K and beta add up (in fp32: 16-bit inputs run those
