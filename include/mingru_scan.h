@@ -307,11 +307,13 @@ int mgs_angle_scan_bwd(const void* theta, const void* scale, const void* gamma, 
  * Envelope: dk <= 128, dv <= 64 (wider d_v runs as independent column blocks,
  * one call each), any chunk >= 1 and nh whose one-token chunk fits shared
  * memory. The chunked form is exact for any chunk length, so the kernels may
- * run shorter chunks than `chunk` (whole tokens; nh * chunk <= 64 on the bf16
- * tensor-core kernels): results differ only by rounding. The size queries
- * return 0 outside the envelope and the entry points MGS_UNSUPPORTED.
+ * run shorter chunks than `chunk` (whole tokens; nh * chunk <= 64 on the
+ * tensor-core kernels, which bf16 and fp32 inputs with dk, dv <= 64, multiples
+ * of 8, take): results differ only by rounding. The size queries return 0
+ * outside the envelope and the entry points MGS_UNSUPPORTED.
  * `saved` (mgs_delta_saved_size bytes) is written by the forward and read by
- * the backward (chunk transitions and chunk-start states, fp32).          */
+ * the backward (chunk-start states and per-chunk maps; its layout depends on
+ * the path the size query picked for these arguments).                     */
 
 size_t mgs_delta_saved_size(int64_t B, int H, int64_t T, int nh, int dk, int dv, int chunk,
                             int dtype);

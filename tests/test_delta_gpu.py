@@ -104,6 +104,32 @@ def test_bf16_tensor_core_vs_oracle(cuda, case):
             EAGER_DEV[C.case_key("delta_bf16", case)])
 
 
+FP16 = dict(rtol=2e-3, atol=2e-3)
+
+
+@pytest.mark.parametrize("case", [(1, 2, 100, 1, 64, 64, 64), (2, 1, 77, 2, 32, 32, 32),
+                                  (1, 1, 70, 1, 128, 128, 64)])
+def test_fp16_inputs_vs_oracle(cuda, case):
+    """fp16 inputs: fp32 arithmetic (the fp32 kernels), outputs and input
+    gradients rounded once to fp16 (relative 2^-11), against the fp64 oracle on
+    the fp16-rounded inputs."""
+    d = C.delta_case_inputs("fp32", case)
+    for k in ("Q", "K", "V", "beta", "grad_y"):
+        d[k] = d[k].astype(np.float16).astype(np.float64)
+    got = run(d, case[-1], cuda, torch.float16)
+    ref = oracle_ref(d, case[-1])
+    bars = {"y": FP16, "H_T": FWD, "dQ": FP16, "dK": FP16, "dV": FP16, "dbeta": FP16,
+            "dH0": BWD}
+    dev = EAGER_DEV[C.case_key("delta_fp32", case)]  # the fp32 states: fp32 gates
+    for name in ["y", "H_T"] + C.DELTA_NAMES:
+        print(C.report(str(case), got[name], ref[name], dev, name))
+        if bars[name] is FP16:  # one fp16 rounding of values up to max|ref|
+            tol = dict(rtol=FP16["rtol"], atol=FP16["atol"] * max(1.0, float(np.max(np.abs(ref[name])))))
+        else:
+            tol = C.gate(bars[name], dev, name)
+        np.testing.assert_allclose(got[name], ref[name], **tol, err_msg=f"{case} {name}")
+
+
 def test_full_length_config5_bf16(cuda):
     """BASELINE config 5 at full size in its own dtype: bf16 Q/K/V/beta, fp32
     state, B=8, H=8, d_k=d_v=64, chunk=64, T=8192."""
