@@ -1287,6 +1287,107 @@ def run_sp(args) -> None:
     print(json.dumps(line), flush=True)
 
 
+def run_sp_dist(args) -> None:
+    """Sequence parallelism across GPUs (torchrun, one rank per GPU): rank r
+    holds time slice r of a sequence N times the configuration's length (the
+    config 2 shape per rank for cfg2-sp, config 1 for cfg1-sp: weak scaling in
+    T), and one step is the public sp_* op forward + backward with its NCCL
+    all-gathers. Timed eagerly with CUDA events, max over ranks; next to it each
+    rank's plain one-launch scan of its own slice (what the slice costs
+    without sequence parallelism)."""
+    import torch.distributed as dist
+
+    rank, world, local = dist_setup(args.gpus)
+    dev = torch.device("cuda", local)
+    import mingru_b200 as mb
+    from mingru_b200.parallel import sp_linear_scan, sp_parallel_scan_log
+
+    g = torch.Generator(device=dev).manual_seed(1000 + rank)
+    if args.config == "cfg2-sp":
+        B, Tl, D = 16, 4096, 1024
+        a = torch.tanh(torch.randn(B, Tl, D, device=dev, generator=g)).requires_grad_(True)
+        b = torch.randn(B, Tl, D, device=dev, generator=g).requires_grad_(True)
+        gA = torch.zeros(B, Tl, D, device=dev)
+        gB = torch.randn(B, Tl, D, device=dev, generator=g)
+
+        def sp_step():
+            A, Bc = sp_linear_scan(a, b)
+            return torch.autograd.grad((A, Bc), (a, b), (gA, gB))
+
+        def plain_step():
+            A, Bc = mb.linear_scan(a, b)
+            return torch.autograd.grad((A, Bc), (a, b), (gA, gB))
+        workload, per_elem = "linear_scan fwd+bwd, config 2 shape per rank, T split over ranks", 40
+    else:
+        B, Tl, D = 8, 1024, 256
+        k = torch.randn(B, Tl, D, device=dev, generator=g)
+        lc = (-torch.nn.functional.softplus(k)).requires_grad_(True)
+        lv = torch.cat([torch.full((B, 1, D), -87.0, device=dev),
+                        -torch.nn.functional.softplus(-k)
+                        + mb.log_g(torch.randn(B, Tl, D, device=dev, generator=g))], 1).requires_grad_(True)
+        gh = torch.randn(B, Tl, D, device=dev, generator=g)
+
+        def sp_step():
+            h = sp_parallel_scan_log(lc, lv)
+            return torch.autograd.grad(h, (lc, lv), gh)
+
+        def plain_step():
+            h = mb.parallel_scan_log(lc, lv)
+            return torch.autograd.grad(h, (lc, lv), gh)
+        workload, per_elem = "parallel_scan_log fwd+bwd, config 1 shape per rank, T split over ranks", 32
+
+    def timed(fn, steps):
+        barrier(world, dev)
+        torch.cuda.synchronize(dev)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(steps):
+            fn()
+        e1.record()
+        torch.cuda.synchronize(dev)
+        barrier(world, dev)
+        return max_over_ranks(e0.elapsed_time(e1) / steps, world, dev)
+
+    for _ in range(args.warmup):
+        sp_step()
+        plain_step()
+    steps = max(3, args.steps)
+    with ClockSampler(dev.index) as clk:
+        clk.mark_start()
+        sp_ms = timed(sp_step, steps)
+        clk.mark_stop()
+    plain_ms = timed(plain_step, steps)
+    mb.raise_device_error(dev)
+    elems = B * Tl * D * world
+    peaks, _ = load_peaks()
+    if rank == 0:
+        line = {
+            "metric": "scan fwd+bwd Gelem/s, sequence-parallel over GPUs",
+            "value": elems / (sp_ms * 1e-3) / 1e9,
+            "unit": "Gelem/s",
+            "n_gpus": world,
+            "steps": steps,
+            "warmup": args.warmup,
+            "ms_per_step": sp_ms,
+            "higher_is_better": True,
+            "scaling": "weak",
+            "vs_baseline": None,
+            "dtype": "f32",
+            "data": "synthetic (seeded per rank)",
+            "config": {"workload": workload, "B": B, "T_per_rank": Tl, "T_total": Tl * world,
+                       "D": D, "parallelism": f"sp{world}", "step": "eager, public sp_* op + autograd",
+                       "collectives": "NCCL all-gather of per-slice carries, forward and backward"},
+            "local_one_launch_ms_per_step": plain_ms,
+            "sp_over_local_one_launch": sp_ms / plain_ms,
+            "step_hbm_frac_per_gpu": per_elem * B * Tl * D / (sp_ms * 1e-3) / 1e9 / peaks["hbm_gbs"],
+            "gpu_launches": None,
+            "clocks": clk.summary(),
+        }
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.destroy_process_group()
+
+
 def run_stack_step(args) -> None:
     """MinGRUStack.step (the streaming / decoding path, one token per call for
     a batch of streams): tokens/s of the eager step loop and of the step
@@ -1452,7 +1553,10 @@ def main() -> None:
             print(json.dumps({"impl": "reference", "unavailable": "the sliced scan has no "
                               "reference CPU arm (the reference arm times the scan path)"}))
             return
-        run_sp(args)
+        if int(os.environ.get("WORLD_SIZE", "1")) > 1:
+            run_sp_dist(args)
+        else:
+            run_sp(args)
         return
     if args.config in ("stack", "stack-step"):
         if args.impl == "reference":

@@ -319,6 +319,40 @@ __device__ __forceinline__ void stage_in(const Lv& x, const E* g, long long ld, 
   }
 }
 
+// Several fp32 input matrices into their blocked levels with every load of
+// every matrix issued before the first split (one memory round trip, as the
+// bf16 path's cp.async copies are all in flight together).
+struct InSrc {
+  const float* g;
+  long long ld;
+  int nrows, valid_ch;
+};
+template <int NTHR, int N>
+__device__ __forceinline__ void stage_in_f32(const Lv (&x)[N], const InSrc (&src)[N]) {
+  constexpr int U = 64 * 8 / NTHR;  // 8-column units of a 64 x 64 matrix per thread
+  float4 a[N][U][2];
+#pragma unroll
+  for (int m = 0; m < N; ++m)
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      const int i = threadIdx.x + u * NTHR, row = i >> 3, ch = i & 7;
+      const float4 z = make_float4(0.f, 0.f, 0.f, 0.f);
+      const bool ok = row < src[m].nrows && ch < src[m].valid_ch;
+      const float4* q = reinterpret_cast<const float4*>(src[m].g + row * src[m].ld + ch * 8);
+      a[m][u][0] = ok ? __ldg(q) : z;
+      a[m][u][1] = ok ? __ldg(q + 1) : z;
+    }
+#pragma unroll
+  for (int m = 0; m < N; ++m)
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      const int i = threadIdx.x + u * NTHR, row = i >> 3, ch = i & 7;
+      const float v[8] = {a[m][u][0].x, a[m][u][0].y, a[m][u][0].z, a[m][u][0].w,
+                          a[m][u][1].x, a[m][u][1].y, a[m][u][1].z, a[m][u][1].w};
+      store8(x[m], umma::boff(row, ch * 8), v);
+    }
+}
+
 // Padded shared tile -> blocked global tile (16-byte chunks, all threads).
 template <int NTHR>
 __device__ __forceinline__ void tile_to_global_blocked(const bf16* t, bf16* g) {
@@ -386,10 +420,19 @@ __global__ void __launch_bounds__(kGradThreads, kF32<E> ? 1 : 2) bwd_grads_kerne
     mbar_init(bar + 1, 1);
     mbar_fence_init();
   }
-  stage_in<NTH>(K, p.K + (bh * rows + r0) * p.dk, p.dk, Mc, p.dk >> 3);
-  stage_in<NTH>(Q, p.Q + (bh * p.T + t0) * p.dk, p.dk, Cc, p.dk >> 3);
-  stage_in<NTH>(dY, p.dy + (bh * p.T + t0) * p.dv, p.dv, Cc, p.dv >> 3);
-  stage_in<NTH>(V, p.V + (bh * rows + r0) * p.dv, p.dv, Mc, p.dv >> 3);
+  if constexpr (F) {
+    const Lv xs[4] = {K, Q, dY, V};
+    const InSrc ss[4] = {{p.K + (bh * rows + r0) * p.dk, p.dk, Mc, p.dk >> 3},
+                         {p.Q + (bh * p.T + t0) * p.dk, p.dk, Cc, p.dk >> 3},
+                         {p.dy + (bh * p.T + t0) * p.dv, p.dv, Cc, p.dv >> 3},
+                         {p.V + (bh * rows + r0) * p.dv, p.dv, Mc, p.dv >> 3}};
+    stage_in_f32<NTH>(xs, ss);
+  } else {
+    stage_in<NTH>(K, p.K + (bh * rows + r0) * p.dk, p.dk, Mc, p.dk >> 3);
+    stage_in<NTH>(Q, p.Q + (bh * p.T + t0) * p.dk, p.dk, Cc, p.dk >> 3);
+    stage_in<NTH>(dY, p.dy + (bh * p.T + t0) * p.dv, p.dv, Cc, p.dv >> 3);
+    stage_in<NTH>(V, p.V + (bh * rows + r0) * p.dv, p.dv, Mc, p.dv >> 3);
+  }
   cp_async_commit();
   um::fence_before();
   __syncthreads();  // barriers initialised, TMEM base written
@@ -998,9 +1041,13 @@ __global__ void __launch_bounds__(kPrepThreads, 1) prep_f32_kernel(const TcArgs<
     mbar_init(bar + 1, 2);
     mbar_fence_init();
   }
-  stage_in<NTH>(K, p.K + (bh * rows + r0) * p.dk, p.dk, Mc, p.dk >> 3);
-  stage_in<NTH>(Q, p.Q + (bh * p.T + t0) * p.dk, p.dk, Cc, p.dk >> 3);
-  stage_in<NTH>(V, p.V + (bh * rows + r0) * p.dv, p.dv, Mc, p.dv >> 3);
+  {
+    const Lv xs[3] = {K, Q, V};
+    const InSrc ss[3] = {{p.K + (bh * rows + r0) * p.dk, p.dk, Mc, p.dk >> 3},
+                         {p.Q + (bh * p.T + t0) * p.dk, p.dk, Cc, p.dk >> 3},
+                         {p.V + (bh * rows + r0) * p.dv, p.dv, Mc, p.dv >> 3}};
+    stage_in_f32<NTH>(xs, ss);
+  }
   if (tid < 64) bs[tid] = tid < Mc ? p.beta[bh * rows + r0 + tid] : 0.f;
   // okw: every wait so far completed (as in prep_kernel).
   bool okw = true;
@@ -1101,6 +1148,22 @@ __global__ void __launch_bounds__(kPrepThreads, 1) prep_f32_kernel(const TcArgs<
     um::products(ps);
     um::commit(bar + 1);
   }
+  float qv[2][16];  // Q row `row`, columns 32*hh.. (fp32, exact), fetched while the products run
+#pragma unroll
+  for (int half = 0; half < 2; ++half) {
+    const int c0 = 32 * hh + 16 * half;
+    const float* qg = p.Q + (bh * p.T + t0 + row) * p.dk + c0;
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      const float4 a = rv && row < Cc && c0 + 4 * k < p.dk
+                           ? __ldg(reinterpret_cast<const float4*>(qg + 4 * k))
+                           : make_float4(0.f, 0.f, 0.f, 0.f);
+      qv[half][4 * k] = a.x;
+      qv[half][4 * k + 1] = a.y;
+      qv[half][4 * k + 2] = a.z;
+      qv[half][4 * k + 3] = a.w;
+    }
+  }
   if (okw) okw = mbar_wait(bar + 1, 1, &g_sticky_err);
   um::fence_after();
   okw = !__syncthreads_or(!okw);
@@ -1119,21 +1182,10 @@ __global__ void __launch_bounds__(kPrepThreads, 1) prep_f32_kernel(const TcArgs<
     um::ld_bind(r3, bc);
     um::ld_bind(r4, yp);
     if (rv) {
-      float qv[16];  // Q row `row`, columns c0.. (fp32, from global: exact)
-      const float* qg = p.Q + (bh * p.T + t0 + row) * p.dk + c0;
-#pragma unroll
-      for (int k = 0; k < 4; ++k) {
-        const float4 a = row < Cc && c0 + 4 * k < p.dk ? __ldg(reinterpret_cast<const float4*>(qg + 4 * k))
-                                                       : make_float4(0.f, 0.f, 0.f, 0.f);
-        qv[4 * k] = a.x;
-        qv[4 * k + 1] = a.y;
-        qv[4 * k + 2] = a.z;
-        qv[4 * k + 3] = a.w;
-      }
 #pragma unroll
       for (int i = 0; i < 16; ++i) {
         x[i] = -x[i];
-        qt[i] = qv[i] - qt[i];
+        qt[i] = qv[half][i] - qt[i];
       }
       store16(Xs, row, c0, x);
       store16(Qs, row, c0, qt);
