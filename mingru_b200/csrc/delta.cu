@@ -668,13 +668,13 @@ struct Geometry {
   size_t ac, hb;  // floats per (b, h) of A_c and of Hbound / B_c / E_c / dSo
 };
 
-// decay: per-token time decay (only the CUDA-core kernels implement it).
+// decay: per-token time decay (the tensor-core kernels take it with fp32 inputs).
 inline bool geometry(long long B, int H, long long T, int nh, int dk, int dv, int C, int dtype,
                      Geometry* g, bool decay = false) {
   if (B < 0 || H < 0 || T < 0 || nh < 1 || C < 1 || dk < 1 || dv < 1) return false;
   if (dk > kMaxDk || dv > kMaxDvBlock) return false;
   const int ct = nh <= kMaxM ? tc_chunk(nh, C) : 0;
-  g->tc = !decay && ct >= 1 && tc_eligible(dtype, nh, dk, dv, ct);
+  g->tc = (!decay || dtype == MGS_F32) && ct >= 1 && tc_eligible(dtype, nh, dk, dv, ct);
   g->C = g->tc ? ct : ffma_chunk(nh, dk, dv, C, T, decay);
   if (g->C < 1) return false;
   g->nchunks = (int)((T + g->C - 1) / g->C);

@@ -179,6 +179,8 @@ struct TcArgs {
   float* Bc;    // (BH, nchunks, 4096) K^T diag(beta) U' as [dk][dv] (forward workspace)
   float* Yp;    // (BH, nchunks, 4096) P U' as [C][dv] (forward workspace)
   float* dHs;   // (BH, nchunks, dk, dv) gradient of each chunk's output state
+  const float* lg;  // (BH, T) per-token log decay <= 0 (fp32 inputs only), or null
+  float* dlg;       // (BH, T) its gradient (backward with decay)
   long long T;
   int nh, dk, dv, C, nchunks, S, dvs;
 };
@@ -255,6 +257,58 @@ __device__ __forceinline__ void row16_f32_to_global(float* g, int c0, int ncols,
       *reinterpret_cast<float4*>(g + c0 + 4 * k) = make_float4(v[4 * k], v[4 * k + 1], v[4 * k + 2], v[4 * k + 3]);
 }
 
+// Per-token time decay (DeltaMinGRU._forward_chunked_gated, min_gru.py:
+// 3290-3448; span sums min_gru.py:3257-3288). With l_s the chunk's per-token
+// log decay, every factor is exp of a span sum span[t][t'] = sum_{s=t'+1}^{t}
+// l_s, accumulated from s = t down (as the reference's flipped cumulative sum),
+// each span from its own terms -- never a difference of running sums, so a
+// saturated gap zeroes exactly the spans that contain it:
+//   F[t][t'] = exp(span[t][t']) (t' <= t; 64 x 64 table), P_t = exp(span[t][-1]),
+//   c_m = F[Ct-1][tau(m)] (tau(m) = m / nh, the token of micro-step m).
+// The chunk's maps with decay:
+//   T = I + strict(K K^T * E) diag(beta),  E[i][l] = F[tau(i)][tau(l)]
+//   R = (Q K^T * D * read) diag(beta),     D[t][l] = F[t][tau(l)]
+//   W' = T^{-1} diag(P^) K,  U' = T^{-1} V  (P^_m = P_{tau(m)})
+//   S' = P_{C-1} S + K^T diag(c beta) (U' - W' S),  y = diag(P) Q S + R (U' - W' S)
+// One thread per token row; ends with a barrier.
+__device__ void decay_tables(const float* lg, int Ct, int nh, float* F, float* Pt, float* cm) {
+  for (int i = threadIdx.x; i < 64 * 64; i += blockDim.x) F[i] = 0.f;  // padding factors are 0
+  for (int i = threadIdx.x; i < 64; i += blockDim.x) Pt[i] = 0.f;
+  __syncthreads();
+  const int t = threadIdx.x;
+  if (t < Ct) {
+    float s = 0.f;
+    F[t * 64 + t] = 1.f;
+    for (int u = t - 1; u >= 0; --u) {
+      s += lg[u + 1];
+      F[t * 64 + u] = expf(s);
+    }
+    Pt[t] = expf(s + lg[0]);
+  }
+  __syncthreads();
+  for (int m = threadIdx.x; m < 64; m += blockDim.x)
+    cm[m] = m < Ct * nh ? F[(Ct - 1) * 64 + m / nh] : 0.f;
+  __syncthreads();
+}
+
+// 64 rows of a row-major fp32 global matrix, each scaled by f[row / nh], into
+// three blocked levels (rows >= nrows and chunks >= valid_ch zero).
+template <int NTHR>
+__device__ __forceinline__ void stage_scaled_f32(const Lv& x, const float* g, long long ld, int nrows,
+                                                 int valid_ch, const float* f, int nh) {
+  for (int i = threadIdx.x; i < 64 * 8; i += NTHR) {
+    const int row = i >> 3, ch = i & 7;
+    float4 a = make_float4(0.f, 0.f, 0.f, 0.f), b = a;
+    if (row < nrows && ch < valid_ch) {
+      a = __ldg(reinterpret_cast<const float4*>(g + row * ld + ch * 8));
+      b = __ldg(reinterpret_cast<const float4*>(g + row * ld + ch * 8 + 4));
+    }
+    const float sc = row < nrows ? f[row / nh] : 0.f;
+    const float v[8] = {sc * a.x, sc * a.y, sc * a.z, sc * a.w, sc * b.x, sc * b.y, sc * b.z, sc * b.w};
+    store8(x, umma::boff(row, ch * 8), v);
+  }
+}
+
 // ----------------------------------------------------- backward: grads --
 // One CTA per (b, h, chunk), two CTAs per SM for bf16 inputs (one for fp32):
 // every gradient of the chunk from its saved S, T^{-1} and dS', on the tcgen05
@@ -282,6 +336,8 @@ template <typename E>
 constexpr int kGradTiles = kF32<E> ? 24 : 13;
 template <typename E>
 constexpr size_t kGradSmem = 1024 + kGradTiles<E> * (size_t)umma::kTileBytes + 2048;
+// decay: span factor table [64][64], P_t [64], c_m [64], d l accumulator (fp64) [80]
+constexpr size_t kGradDecaySmem = 64 * 64 * 4 + (64 + 64) * 4 + 80 * 8;
 constexpr int kGradTmemCols = 256;
 
 // 64 rows x (8 * valid_ch) columns of a row-major global bf16 matrix into a
@@ -353,15 +409,6 @@ __device__ __forceinline__ void stage_in_f32(const Lv (&x)[N], const InSrc (&src
     }
 }
 
-// Padded shared tile -> blocked global tile (16-byte chunks, all threads).
-template <int NTHR>
-__device__ __forceinline__ void tile_to_global_blocked(const bf16* t, bf16* g) {
-  for (int i = threadIdx.x; i < 64 * 8; i += NTHR) {
-    const int row = i >> 3, ch = i & 7;
-    *reinterpret_cast<uint4*>(g + umma::boff(row, ch * 8)) =
-        *reinterpret_cast<const uint4*>(t + row * kLd + ch * 8);
-  }
-}
 
 // Columns c0..c0+15 of an accumulator row -> bf16 global row (columns < ncols).
 __device__ __forceinline__ void row16_to_global(bf16* g, int c0, int ncols, const float (&v)[16]) {
@@ -378,7 +425,15 @@ __device__ __forceinline__ void row16_to_global(float* g, int c0, int ncols, con
   row16_f32_to_global(g, c0, ncols, v);
 }
 
-template <typename E>
+// DEC (fp32 inputs, per-token decay p.lg; the maps of decay_tables): level 1
+// takes K S instead of T^{-1} K and level 2 forms U = U' + T^{-1} (-P^ K S);
+// level 3 adds dy S^T (diag(P) dy S^T is dQ's first term, kept in registers);
+// the masks of levels 1 and 4 carry the span factors; dK's -G S^T rows take
+// P^, its U dS'^T rows c; and every factor's gradient is gathered per token
+// span (t', t] into `dl` as a difference array (+w at t' + 1, -w at t + 1:
+// d l_s is the sum over the spans containing s, a prefix sum at the end), the
+// entries of span-free factors (same token, factor 1) left out.
+template <typename E, bool DEC = false>
 __global__ void __launch_bounds__(kGradThreads, kF32<E> ? 1 : 2) bwd_grads_kernel(const TcArgs<E> p) {
   namespace um = umma;
   constexpr bool F = kF32<E>;
@@ -401,6 +456,13 @@ __global__ void __launch_bounds__(kGradThreads, kF32<E> ? 1 : 2) bwd_grads_kerne
   float* bs = reinterpret_cast<float*>(T(kGradTiles<E>));
   float* rpart = bs + 64;      // [2 column halves][64 rows]: sum_col U * dbU
   float* cpart = rpart + 128;  // [8 warps][32 columns]: masked-product column sums
+  float* Ft = bs + 512;        // decay: factor table [64][64]
+  float* Pt = Ft + 64 * 64;    // decay: P_t
+  float* cm = Pt + 64;         // decay: c_m
+  // decay: d l difference array [Cc + 1], then <S, dS'> at [72], in fp64: its prefix sums
+  // carry every entry's rounding into all later tokens, and with fp32 entries that
+  // shared error adds up coherently in sums over tokens (the gradient of lambda)
+  double* dl = reinterpret_cast<double*>(cm + 64);
 
   constexpr int NTH = kGradThreads;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -420,6 +482,8 @@ __global__ void __launch_bounds__(kGradThreads, kF32<E> ? 1 : 2) bwd_grads_kerne
     mbar_init(bar + 1, 1);
     mbar_fence_init();
   }
+  if constexpr (DEC)
+    if (tid < 80) dl[tid] = 0.0;  // before the barrier below: the S . dS' sums start right after it
   if constexpr (F) {
     const Lv xs[4] = {K, Q, dY, V};
     const InSrc ss[4] = {{p.K + (bh * rows + r0) * p.dk, p.dk, Mc, p.dk >> 3},
@@ -464,9 +528,16 @@ __global__ void __launch_bounds__(kGradThreads, kF32<E> ? 1 : 2) bwd_grads_kerne
       const int o = um::boff(r, cb * 8);
       store8(S, o, av);
       store8(Dp, o, bv);
+      if constexpr (DEC) {  // <S, dS'>: the gradient of P_{C-1} S
+        float d = 0.f;
+#pragma unroll
+        for (int j = 0; j < 8; ++j) d = fmaf(av[j], bv[j], d);
+        atomicAdd(dl + 72, (double)(d));
+      }
     }
   }
   if (tid < 64) bs[tid] = tid < Mc ? tof(p.beta[bh * rows + r0 + tid]) : 0.f;
+  if constexpr (DEC) decay_tables(p.lg + bh * p.T + t0, Cc, p.nh, Ft, Pt, cm);  // barriers inside
   cp_async_wait_all();
   // okw: every wait so far completed. A wait that runs out records the time-out
   // (sticky word) and from then on this CTA issues no MMA, waits on nothing and
@@ -495,7 +566,8 @@ __global__ void __launch_bounds__(kGradThreads, kF32<E> ? 1 : 2) bwd_grads_kerne
   to_mma();
   if (okw && tid == 0) {
     const um::Opnd oTi = op(Ti, false);
-    const um::Prod ps[2] = {{tA, oTi, op(K, true), false}, {tB, oTi, op(V, true), false}};
+    const um::Prod ps[2] = {{tA, DEC ? op(K, false) : oTi, op(DEC ? S : K, true), false},
+                            {tB, oTi, op(V, true), false}};
     um::products(ps);
     um::commit(bar);
   } else if (okw && tid == 32) {
@@ -516,11 +588,15 @@ __global__ void __launch_bounds__(kGradThreads, kF32<E> ? 1 : 2) bwd_grads_kerne
     um::ld_bind(r1, v);
     um::ld_bind(r2, w);
     if (rv) {
+      // decay: -W <- -P^ (K S) (rhs of U = T^{-1} (V - P^ K S)), P's read factors D
+      const float ph = DEC ? (row < Mc ? Pt[row / p.nh] : 0.f) : 1.f;
 #pragma unroll
       for (int i = 0; i < 16; ++i) {
         const int cl = c0 + i;
-        v[i] = (cl < (row + 1) * p.nh && cl < Mc) ? v[i] * bs[cl] : 0.f;
-        w[i] = -w[i];
+        const bool rd = cl < (row + 1) * p.nh && cl < Mc;
+        v[i] = rd ? v[i] * bs[cl] : 0.f;
+        if constexpr (DEC) v[i] *= rd && row < Cc ? Ft[row * 64 + cl / p.nh] : 0.f;
+        w[i] = -ph * w[i];
       }
       store16(P, row, c0, v);
       store16(W, row, c0, w);
@@ -528,8 +604,8 @@ __global__ void __launch_bounds__(kGradThreads, kF32<E> ? 1 : 2) bwd_grads_kerne
   }
   // level 2
   to_mma();
-  if (okw && tid == 0) {
-    const um::Prod ps[1] = {{tB, op(W, false), op(S, true), true}};
+  if (okw && tid == 0) {  // U = U' + (-W) S, decay U' + T^{-1} (-P^ K S)
+    const um::Prod ps[1] = {{tB, op(DEC ? Ti : W, false), op(DEC ? W : S, true), true}};
     um::products(ps);
     um::commit(bar);
   } else if (okw && tid == 32) {
@@ -553,7 +629,7 @@ __global__ void __launch_bounds__(kGradThreads, kF32<E> ? 1 : 2) bwd_grads_kerne
       um::ld_bind(r2, db);
       um::ld_bind(r3, pd);
       if (rv) {
-        const float b = bs[row];
+        const float b = DEC ? bs[row] * cm[row] : bs[row];  // decay: carry factor c
 #pragma unroll
         for (int i = 0; i < 16; ++i) {
           rs += u[i] * db[i];
@@ -573,13 +649,44 @@ __global__ void __launch_bounds__(kGradThreads, kF32<E> ? 1 : 2) bwd_grads_kerne
         {tD, op(lv_first(Ti, L - 1), true), op(lv_rest(dU), true), false}};
     um::products(ps);
     um::commit(bar);
-  } else if (okw && tid == 32) {  // U dS'^T in A
-    const um::Prod ps[1] = {{tA, op(U, false), op(Dp, false), false}};
-    um::products(ps);
+  } else if (okw && tid == 32) {  // U dS'^T in A (decay: dy S^T in B)
+    if constexpr (DEC) {
+      const um::Prod ps[2] = {{tA, op(U, false), op(Dp, false), false},
+                              {tB, op(dY, false), op(S, false), false}};
+      um::products(ps);
+    } else {
+      const um::Prod ps[1] = {{tA, op(U, false), op(Dp, false), false}};
+      um::products(ps);
+    }
     um::commit(bar);
   }
   wait_mma();
   float uds[2][16];  // U dS'^T of this thread's row, held until the last epilogue
+  float dqs[2][16];  // decay: P_t (dy S^T) of this thread's row (dQ's first term)
+  if constexpr (DEC) {
+#pragma unroll
+    for (int half = 0; half < 2; ++half) {
+      const int c0 = 32 * hh + 16 * half;
+      uint32_t r1[16];
+      um::ld16_async(lb + 64 + 16 * half, r1);
+      um::ld_wait();
+      um::ld_bind(r1, dqs[half]);
+      const float pt = rv && row < Cc ? Pt[row] : 0.f;
+      float d = 0.f;  // q_t . (dy S^T)_t over these columns: the gradient of P_t
+#pragma unroll
+      for (int i = 0; i < 16; ++i) {
+        const int o = um::boff(row, c0 + i);
+        const float qv = __bfloat162float(Q.t[0][o]) + __bfloat162float(Q.t[1][o]) +
+                         __bfloat162float(Q.t[2][o]);
+        d = fmaf(qv, dqs[half][i], d);
+        dqs[half][i] *= pt;
+      }
+      if (rv && row < Cc) {  // G2[t][-1] += P_t dP_t
+        atomicAdd(dl + 0, (double)(pt * d));
+        atomicAdd(dl + row + 1, (double)(-pt * d));
+      }
+    }
+  }
 #pragma unroll
   for (int half = 0; half < 2; ++half) {  // dV = G; Gn = -G
     const int c0 = 32 * hh + 16 * half;
@@ -632,14 +739,51 @@ __global__ void __launch_bounds__(kGradThreads, kF32<E> ? 1 : 2) bwd_grads_kerne
       um::ld_bind(r3, kk);
       um::ld_bind(r4, qk);
       float e[16];  // this row's dbeta column terms
+      // decay: the factor gradients of span-carrying entries (x beta), summed by
+      // row and by column in fp64 so that the +w / -w entries they make in the
+      // difference array cancel exactly outside each span
+      double eg[16];
+      double rsR = 0.0, rsT = 0.0;
 #pragma unroll
       for (int i = 0; i < 16; ++i) {
         const int cl = c0 + i;
         const float x = (rv && cl < (row + 1) * p.nh && cl < Mc) ? ds[i] : 0.f;
         const float y = (rv && cl < row && cl < Mc) ? dk[i] : 0.f;
-        e[i] = rv ? x * qk[i] + y * kk[i] : 0.f;
-        ds[i] = x * bs[cl];
-        dk[i] = y * bs[cl];
+        if constexpr (DEC) {
+          const float fd = rv && row < Cc ? Ft[row * 64 + cl / p.nh] : 0.f;           // D[t][l]
+          const float fe = rv && row < Mc ? Ft[(row / p.nh) * 64 + cl / p.nh] : 0.f;  // E[i][l]
+          const float xr = x * qk[i] * fd, yt = y * kk[i] * fe;
+          e[i] = xr + yt;
+          const double wr = cl / p.nh < row ? (double)(xr * bs[cl]) : 0.0;         // span (tau(l), t]
+          const double wt = cl / p.nh < row / p.nh ? (double)(yt * bs[cl]) : 0.0;  // span (tau(l), tau(i)]
+          rsR += wr;
+          rsT += wt;
+          eg[i] = wr + wt;
+          ds[i] = x * bs[cl] * fd;
+          dk[i] = y * bs[cl] * fe;
+        } else {
+          e[i] = rv ? x * qk[i] + y * kk[i] : 0.f;
+          ds[i] = x * bs[cl];
+          dk[i] = y * bs[cl];
+        }
+      }
+      if constexpr (DEC) {
+        if (rv && row < Cc) atomicAdd(dl + row + 1, (double)(-rsR));
+        if (rv && row < Mc) atomicAdd(dl + row / p.nh + 1, (double)(-rsT));
+        // column sums of eg (as for e below): + at tau(l) + 1
+#pragma unroll
+        for (int d = 8, n = 16; d >= 1; d >>= 1, n >>= 1) {
+          const bool upper = (lane & d) != 0;
+#pragma unroll
+          for (int j = 0; j < n / 2; ++j) {
+            const double keep = upper ? eg[j + n / 2] : eg[j];
+            const double send = upper ? eg[j] : eg[j + n / 2];
+            eg[j] = keep + __shfl_xor_sync(0xffffffffu, send, d);
+          }
+        }
+        const double colg = __shfl_sync(0xffffffffu, eg[0], lane & 15);
+        const int cg = c0 + (lane & 15);
+        if (lane < 16 && cg < Mc) atomicAdd(dl + cg / p.nh + 1, (double)(colg));
       }
       // column sums over the 16 rows of each half-warp by a transposing
       // butterfly: at distance d a lane keeps the half of its values selected
@@ -666,12 +810,17 @@ __global__ void __launch_bounds__(kGradThreads, kF32<E> ? 1 : 2) bwd_grads_kerne
   }
   // level 5
   to_mma();
-  if (okw && tid == 0) {  // dQ in A, Gn S^T in C
+  if (okw && tid == 0) {  // dQ in A (decay: its dy S^T term is in registers), Gn S^T in C
     const um::Opnd oS = op(S, false);
-    const um::Prod ps[3] = {{tA, op(dY, false), oS, false},
-                            {tC, op(Gn, false), oS, false},
-                            {tA, op(dS_, false), op(K, true), true}};
-    um::products(ps);
+    if constexpr (DEC) {
+      const um::Prod ps[2] = {{tC, op(Gn, false), oS, false}, {tA, op(dS_, false), op(K, true), false}};
+      um::products(ps);
+    } else {
+      const um::Prod ps[3] = {{tA, op(dY, false), oS, false},
+                              {tC, op(Gn, false), oS, false},
+                              {tA, op(dS_, false), op(K, true), true}};
+      um::products(ps);
+    }
     um::commit(bar);
   } else if (okw && tid == 32) {  // dS_^T Q + dKK K in B, dKK^T K in D
     const um::Opnd oKmn = op(K, true);
@@ -696,9 +845,27 @@ __global__ void __launch_bounds__(kGradThreads, kF32<E> ? 1 : 2) bwd_grads_kerne
     um::ld_bind(r2, v2);
     um::ld_bind(r3, v3);
     um::ld_bind(r4, v4);
+    if constexpr (DEC) {
+#pragma unroll
+      for (int i = 0; i < 16; ++i) v[i] += dqs[half][i];
+    }
     if (okw && rv && row < Cc) row16_to_global(p.dQ + (bh * p.T + t0 + row) * p.dk, c0, p.dk, v);
     if (okw && rv && row < Mc) {
-      const float b = bs[row];
+      const float b = DEC ? bs[row] * cm[row] : bs[row];
+      if constexpr (DEC) {  // -G S^T rows take P^; its K-weighted sum is the gradient of P^
+        const float ph = Pt[row / p.nh];
+        float d = 0.f;
+#pragma unroll
+        for (int i = 0; i < 16; ++i) {
+          const int o = um::boff(row, c0 + i);
+          const float kv = __bfloat162float(K.t[0][o]) + __bfloat162float(K.t[1][o]) +
+                           __bfloat162float(K.t[2][o]);
+          d = fmaf(kv, v3[i], d);
+          v3[i] *= ph;
+        }
+        atomicAdd(dl + 0, (double)(ph * d));  // G2[tau(m)][-1] += P^_m dP^_m
+        atomicAdd(dl + row / p.nh + 1, (double)(-ph * d));
+      }
 #pragma unroll
       for (int i = 0; i < 16; ++i) v2[i] += v3[i] + v4[i] + b * uds[half][i];
       row16_to_global(p.dK + (bh * rows + r0 + row) * p.dk, c0, p.dk, v2);
@@ -708,10 +875,33 @@ __global__ void __launch_bounds__(kGradThreads, kF32<E> ? 1 : 2) bwd_grads_kerne
   __syncthreads();
   if (okw && tid < Mc) {  // dbeta = row sums of U * dbU + column sums of the masked products
     const int h2 = tid >> 5, cl = tid & 31;
-    const float d = (rpart[tid] + rpart[64 + tid]) +
+    const float ru = rpart[tid] + rpart[64 + tid];
+    const float d = (DEC ? cm[tid] * ru : ru) +
                     (cpart[(4 * h2) * 32 + cl] + cpart[(4 * h2 + 1) * 32 + cl]) +
                     (cpart[(4 * h2 + 2) * 32 + cl] + cpart[(4 * h2 + 3) * 32 + cl]);
     p.dbeta[bh * rows + r0 + tid] = fromf<E>(d);
+    if constexpr (DEC) {  // carry factor c_m: span (tau(m), Ct - 1]
+      if (tid / p.nh < Cc - 1) {
+        const float w = bs[tid] * cm[tid] * ru;
+        atomicAdd(dl + tid / p.nh + 1, (double)(w));
+        atomicAdd(dl + Cc, (double)(-w));
+      }
+    }
+  }
+  if constexpr (DEC) {
+    if (tid == 0) {  // P_{C-1} S: span (-1, Ct - 1]
+      const double w = (double)Pt[Cc - 1] * dl[72];
+      atomicAdd(dl + 0, (double)(w));
+      atomicAdd(dl + Cc, (double)(-w));
+    }
+    __syncthreads();
+    if (okw && tid == 0) {  // d l_s = prefix sums of the difference array
+      double acc = 0.0;
+      for (int t = 0; t < Cc; ++t) {
+        acc += dl[t];
+        p.dlg[bh * p.T + t0 + t] = (float)acc;
+      }
+    }
   }
   if (warp == 0) {
     um::fence_after();
@@ -719,6 +909,53 @@ __global__ void __launch_bounds__(kGradThreads, kF32<E> ? 1 : 2) bwd_grads_kerne
   }
 }
 
+constexpr int kF32Ld = 65;  // row stride of the fp32 64 x 64 matrices of the inverse
+
+// X = T^{-1} for the unit lower-triangular T = I + Tf (Tf strictly lower,
+// fp32 [64][kF32Ld]) in fp32: the four diagonal 16 x 16 blocks by forward
+// substitution (a thread per column), then block row i = 1..3 from the rows
+// above it, X_ij = -D_i^{-1} sum_{k=j}^{i-1} T_ik X_kj (Ys holds the sums).
+// Only the lower blocks of X are written (the diagonal blocks with zeros above
+// the diagonal). Ends with __syncthreads.
+__device__ void tri_inv_f32(const float* Tf, float* Xf, float* Ys) {
+  const int tid = threadIdx.x;
+  if (tid < 64) {
+    const int o = (tid >> 4) * 16, j = tid & 15;
+    float x[16];
+#pragma unroll
+    for (int i = 0; i < 16; ++i) {
+      float s = 0.f;
+#pragma unroll
+      for (int k = 0; k < i; ++k) s = fmaf(Tf[(o + i) * kF32Ld + o + k], x[k], s);
+      x[i] = i == j ? 1.f : (i > j ? -s : 0.f);
+    }
+#pragma unroll
+    for (int i = 0; i < 16; ++i) Xf[(o + i) * kF32Ld + o + j] = x[i];
+  }
+  __syncthreads();
+  for (int bi = 1; bi < 4; ++bi) {
+    const int r0 = 16 * bi, ncol = 16 * bi;
+    for (int e = tid; e < 16 * ncol; e += blockDim.x) {
+      const int r = e / ncol, cc = e - r * ncol;
+      float s = 0.f;
+      for (int k = cc & ~15; k < r0; ++k) s = fmaf(Tf[(r0 + r) * kF32Ld + k], Xf[k * kF32Ld + cc], s);
+      Ys[r * 48 + cc] = s;
+    }
+    __syncthreads();
+    for (int e = tid; e < 16 * ncol; e += blockDim.x) {
+      const int r = e / ncol, cc = e - r * ncol;
+      float s = 0.f;
+      for (int k = 0; k <= r; ++k) s = fmaf(Xf[(r0 + r) * kF32Ld + r0 + k], Ys[k * 48 + cc], s);
+      Xf[(r0 + r) * kF32Ld + cc] = -s;
+    }
+    __syncthreads();
+  }
+}
+
+// DEC: per-token time decay (p.lg): the span factors enter T and P~ (level-1
+// epilogue), W' is T^{-1} (P^ K) and the K^T products take c K (levels 3, 4),
+// and Xn, Qt take P_{C-1} and P (last epilogue) -- the maps above. The tables
+// live in Xf until the inverse, P^ K and then c K over Tf / Xf.
 // ------------------------------------------------------- forward: prep --
 // One CTA per (b, h, chunk), independent of the state, two CTAs per SM: T,
 // T^{-1} (saved for the backward), and the chunk's affine state map and readout
@@ -962,51 +1199,10 @@ __global__ void __launch_bounds__(kPrepThreads, 2) prep_kernel(const TcArgs<bf16
 // 12-14 T^{-1} | beta | Tf, Xf fp32 [64][65] | Ys fp32 [16][48].
 // beta W goes over Q's levels, beta U' over V's; the outputs Xn (0-2) and Qt
 // (3-5) over K and beta W, Bc and Yp (fp32) over Tf and Xf.
-constexpr int kF32Ld = 65;
 constexpr size_t kPrepF32Smem =
-    1024 + 15 * (size_t)umma::kTileBytes + 256 + 2 * 64 * kF32Ld * 4 + 16 * 48 * 4;
+    1024 + 15 * (size_t)umma::kTileBytes + 256 + 2 * 64 * kF32Ld * 4 + 16 * 48 * 4 + 512;
 
-// X = T^{-1} for the unit lower-triangular T = I + Tf (Tf strictly lower,
-// fp32 [64][kF32Ld]) in fp32: the four diagonal 16 x 16 blocks by forward
-// substitution (a thread per column), then block row i = 1..3 from the rows
-// above it, X_ij = -D_i^{-1} sum_{k=j}^{i-1} T_ik X_kj (Ys holds the sums).
-// Only the lower blocks of X are written (the diagonal blocks with zeros above
-// the diagonal). Ends with __syncthreads.
-__device__ void tri_inv_f32(const float* Tf, float* Xf, float* Ys) {
-  const int tid = threadIdx.x;
-  if (tid < 64) {
-    const int o = (tid >> 4) * 16, j = tid & 15;
-    float x[16];
-#pragma unroll
-    for (int i = 0; i < 16; ++i) {
-      float s = 0.f;
-#pragma unroll
-      for (int k = 0; k < i; ++k) s = fmaf(Tf[(o + i) * kF32Ld + o + k], x[k], s);
-      x[i] = i == j ? 1.f : (i > j ? -s : 0.f);
-    }
-#pragma unroll
-    for (int i = 0; i < 16; ++i) Xf[(o + i) * kF32Ld + o + j] = x[i];
-  }
-  __syncthreads();
-  for (int bi = 1; bi < 4; ++bi) {
-    const int r0 = 16 * bi, ncol = 16 * bi;
-    for (int e = tid; e < 16 * ncol; e += blockDim.x) {
-      const int r = e / ncol, cc = e - r * ncol;
-      float s = 0.f;
-      for (int k = cc & ~15; k < r0; ++k) s = fmaf(Tf[(r0 + r) * kF32Ld + k], Xf[k * kF32Ld + cc], s);
-      Ys[r * 48 + cc] = s;
-    }
-    __syncthreads();
-    for (int e = tid; e < 16 * ncol; e += blockDim.x) {
-      const int r = e / ncol, cc = e - r * ncol;
-      float s = 0.f;
-      for (int k = 0; k <= r; ++k) s = fmaf(Xf[(r0 + r) * kF32Ld + r0 + k], Ys[k * 48 + cc], s);
-      Xf[(r0 + r) * kF32Ld + cc] = -s;
-    }
-    __syncthreads();
-  }
-}
-
+template <bool DEC>
 __global__ void __launch_bounds__(kPrepThreads, 1) prep_f32_kernel(const TcArgs<float> p) {
   namespace um = umma;
   extern __shared__ __align__(1024) unsigned char psmem[];
@@ -1022,6 +1218,11 @@ __global__ void __launch_bounds__(kPrepThreads, 1) prep_f32_kernel(const TcArgs<
   float* Tf = bs + 64;
   float* Xf = Tf + 64 * kF32Ld;
   float* Ys = Xf + 64 * kF32Ld;
+  float* Pt = Ys + 16 * 48;  // decay: P_t (64), c_m (64)
+  float* cm = Pt + 64;
+  float* Ft = Xf;            // decay: span factor table, until the inverse
+  const Lv Ks = lv(reinterpret_cast<bf16*>(Tf), reinterpret_cast<bf16*>(Tf) + 4096,
+                   reinterpret_cast<bf16*>(Tf) + 8192);  // decay: P^ K (level 3), c K (level 4)
   float* Bcs = Tf;  // outputs, after the last products
   float* Yps = Xf;
 
@@ -1049,6 +1250,7 @@ __global__ void __launch_bounds__(kPrepThreads, 1) prep_f32_kernel(const TcArgs<
     stage_in_f32<NTH>(xs, ss);
   }
   if (tid < 64) bs[tid] = tid < Mc ? p.beta[bh * rows + r0 + tid] : 0.f;
+  if constexpr (DEC) decay_tables(p.lg + bh * p.T + t0, Cc, p.nh, Ft, Pt, cm);
   // okw: every wait so far completed (as in prep_kernel).
   bool okw = true;
   auto to_mma = [&]() {
@@ -1079,11 +1281,19 @@ __global__ void __launch_bounds__(kPrepThreads, 1) prep_f32_kernel(const TcArgs<
       um::ld16(lb + 16 * half, v);
       if (r < 64) {
 #pragma unroll
-        for (int i = 0; i < 16; ++i) Tf[r * kF32Ld + c0 + i] = c0 + i < r ? v[i] * bs[c0 + i] : 0.f;
+        for (int i = 0; i < 16; ++i) {
+          float x = c0 + i < r ? v[i] * bs[c0 + i] : 0.f;
+          if constexpr (DEC) x *= c0 + i < r ? Ft[(r / p.nh) * 64 + (c0 + i) / p.nh] : 0.f;
+          Tf[r * kF32Ld + c0 + i] = x;
+        }
       } else {
         const int ti = r - 64;
 #pragma unroll
-        for (int i = 0; i < 16; ++i) v[i] = (c0 + i < (ti + 1) * p.nh && c0 + i < Mc) ? v[i] : 0.f;
+        for (int i = 0; i < 16; ++i) {
+          const bool rd = c0 + i < (ti + 1) * p.nh && c0 + i < Mc;
+          v[i] = rd ? v[i] : 0.f;
+          if constexpr (DEC) v[i] *= rd ? Ft[ti * 64 + (c0 + i) / p.nh] : 0.f;
+        }
         store16(P, ti, c0, v);
       }
     }
@@ -1098,14 +1308,19 @@ __global__ void __launch_bounds__(kPrepThreads, 1) prep_f32_kernel(const TcArgs<
     for (int j = 0; j < 8; ++j) v[j] = ch * 8 + j <= row ? Xf[row * kF32Ld + ch * 8 + j] : 0.f;
     store8(Ti, um::boff(row, ch * 8), v);
   }
+  if constexpr (DEC) {  // P^ K over Tf / Xf (the inverse is done with them)
+    __syncthreads();
+    stage_scaled_f32<NTH>(Ks, p.K + (bh * rows + r0) * p.dk, p.dk, Mc, p.dk >> 3, Pt, p.nh);
+  }
   to_mma();
   if (okw && tid == 64) {  // T^{-1} (three contiguous levels) to `saved`; its tiles stay untouched
     bulk_s2g(p.Ti + blk * kSavedSet<float>, Ti.t[0], 3 * um::kTileBytes);
     bulk_commit();
   }
-  // level 3: W = Ti K (B), U' = Ti V (C)
+  // level 3: W = Ti K (B) (decay: Ti (P^ K)), U' = Ti V (C)
   if (okw && (tid == 0 || tid == 32)) {
-    const um::Prod ps[1] = {{tid == 0 ? tB : tC, op(Ti, false), op(tid == 0 ? K : V, true), false}};
+    const Lv& Kw = DEC ? Ks : K;
+    const um::Prod ps[1] = {{tid == 0 ? tB : tC, op(Ti, false), op(tid == 0 ? Kw : V, true), false}};
     um::products(ps);
     um::commit(bar + 1);
   }
@@ -1114,6 +1329,8 @@ __global__ void __launch_bounds__(kPrepThreads, 1) prep_f32_kernel(const TcArgs<
   const int row = 16 * q + lane;  // M = 64 accumulators: lanes 0-15 hold rows
   const bool rv = lane < 16;
   const uint32_t lb = tb + ((uint32_t)(32 * q) << 16) + 32 * hh;
+  if constexpr (DEC)  // c K over P^ K (level 3 has read it)
+    stage_scaled_f32<NTH>(Ks, p.K + (bh * rows + r0) * p.dk, p.dk, Mc, p.dk >> 3, cm, 1);
 #pragma unroll
   for (int half = 0; half < 2; ++half) {  // beta W (over Q), beta U' (over V)
     const int c0 = 32 * hh + 16 * half;
@@ -1139,12 +1356,12 @@ __global__ void __launch_bounds__(kPrepThreads, 1) prep_f32_kernel(const TcArgs<
   // level 4: K^T (beta W) (A), P~ (beta W) (B), K^T (beta U') (C), P~ (beta U') (D)
   if (okw && tid == 0) {
     const um::Opnd oBW = op(BW, true);
-    const um::Prod ps[2] = {{tA, op(K, true), oBW, false}, {tB, op(P, false), oBW, false}};
+    const um::Prod ps[2] = {{tA, op(DEC ? Ks : K, true), oBW, false}, {tB, op(P, false), oBW, false}};
     um::products(ps);
     um::commit(bar + 1);
   } else if (okw && tid == 32) {
     const um::Opnd oBU = op(BU, true);
-    const um::Prod ps[2] = {{tC, op(K, true), oBU, false}, {tD, op(P, false), oBU, false}};
+    const um::Prod ps[2] = {{tC, op(DEC ? Ks : K, true), oBU, false}, {tD, op(P, false), oBU, false}};
     um::products(ps);
     um::commit(bar + 1);
   }
@@ -1182,10 +1399,12 @@ __global__ void __launch_bounds__(kPrepThreads, 1) prep_f32_kernel(const TcArgs<
     um::ld_bind(r3, bc);
     um::ld_bind(r4, yp);
     if (rv) {
+      const float pr = DEC ? (row < Cc ? Pt[row] : 0.f) : 1.f;  // P_t of token `row`
+      const float pe = DEC ? Pt[Cc - 1] - 1.f : 0.f;             // P_{C-1} - 1 on Xn's diagonal
 #pragma unroll
       for (int i = 0; i < 16; ++i) {
-        x[i] = -x[i];
-        qt[i] = qv[half][i] - qt[i];
+        x[i] = -x[i] + (DEC && row == c0 + i && row < p.dk ? pe : 0.f);
+        qt[i] = pr * qv[half][i] - qt[i];
       }
       store16(Xs, row, c0, x);
       store16(Qs, row, c0, qt);
@@ -1601,6 +1820,9 @@ int run_tc_impl(bool fwd, const Args<E>& p, long long B, int H, long long T, int
   a.dV = p.dV;
   a.dbeta = p.dbeta;
   a.dH0 = p.dH0;
+  a.lg = p.lg;
+  a.dlg = p.dlg;
+  if (a.lg != nullptr && (!kF32<E> || (!fwd && a.dlg == nullptr))) return MGS_UNSUPPORTED;
   a.T = T;
   a.nh = nh;
   a.dk = dk;
@@ -1631,7 +1853,8 @@ int run_tc_impl(bool fwd, const Args<E>& p, long long B, int H, long long T, int
     a.Yp = a.Bc + ncs * 4096;
     int rc;
     if constexpr (kF32<E>)
-      rc = launch_tc(prep_f32_kernel, (long long)ncs, kPrepF32Smem, st, a, kPrepThreads);
+      rc = a.lg ? launch_tc(prep_f32_kernel<true>, (long long)ncs, kPrepF32Smem, st, a, kPrepThreads)
+                : launch_tc(prep_f32_kernel<false>, (long long)ncs, kPrepF32Smem, st, a, kPrepThreads);
     else
       rc = launch_tc(prep_kernel, (long long)ncs, kPrepSmem, st, a, kPrepThreads);
     if (rc != MGS_OK) return rc;
@@ -1648,6 +1871,10 @@ int run_tc_impl(bool fwd, const Args<E>& p, long long B, int H, long long T, int
   a.dHs = static_cast<float*>(ws);
   int rc = launch_tc(chain_bwd_kernel<E>, BH * a.S, kChainBwdSmem<E>, st, a, kChainThreads);
   if (rc != MGS_OK) return rc;
+  if constexpr (kF32<E>)
+    if (a.lg)
+      return launch_tc(bwd_grads_kernel<E, true>, BH * a.nchunks, kGradSmem<E> + kGradDecaySmem, st,
+                       a, kGradThreads);
   return launch_tc(bwd_grads_kernel<E>, BH * a.nchunks, kGradSmem<E>, st, a, kGradThreads);
 }
 

@@ -1046,10 +1046,12 @@ def _delta_checked(
         fwd = lambda q, k, v, b, h0: _delta_gated_fwd(q, k, v, b, h0, log_gamma, int(chunk_size))
     else:
         fwd = lambda q, k, v, b, h0: _delta_fwd(q, k, v, b, h0, int(chunk_size))
-    if Q.dtype == torch.float16 and not gated:
-        # fp16 inputs take the fp32 kernels (tensor cores where the shape
-        # allows): fp32 arithmetic either way, rounded once to fp16 on output.
-        y, HT = _delta_checked(Q.float(), K.float(), V.float(), beta.float(), H0, chunk_size)
+    if Q.dtype == torch.float16 or (gated and Q.dtype != torch.float32):
+        # fp16 inputs, and 16-bit inputs with decay, take the fp32 kernels
+        # (tensor cores where the shape allows): fp32 arithmetic either way,
+        # rounded once to the input dtype on output.
+        y, HT = _delta_checked(Q.float(), K.float(), V.float(), beta.float(), H0, chunk_size,
+                               gated, log_gamma)
         return y.to(Q.dtype), HT
     if dv <= _DELTA_DV_BLOCK:
         y, HT, _ = fwd(Q, K, V, beta, H0)
