@@ -276,7 +276,7 @@ __device__ void decay_tables(const float* lg, int Ct, int nh, float* F, float* P
   for (int i = threadIdx.x; i < 64; i += blockDim.x) Pt[i] = 0.f;
   __syncthreads();
   const int t = threadIdx.x;
-  if (t < Ct) {
+  if (t < Ct) {  // row t: the spans (u, t] for u = t-1 .. 0, summed from s = t down
     float s = 0.f;
     F[t * 64 + t] = 1.f;
     for (int u = t - 1; u >= 0; --u) {
@@ -476,7 +476,10 @@ __global__ void __launch_bounds__(kGradThreads, kF32<E> ? 1 : 2) bwd_grads_kerne
   const long long blk = bh * p.nchunks + c;
   const long long sofs = blk * (long long)p.dk * p.dv;
 
-  if (warp == 0) um::alloc(tbase_s, kGradTmemCols);
+  // decay: two more accumulators (E, F: U dS'^T and dy S^T, read at the last
+  // epilogue) -- one CTA per SM, so all 512 columns are free
+  constexpr int kCols = DEC ? 2 * kGradTmemCols : kGradTmemCols;
+  if (warp == 0) um::alloc(tbase_s, kCols);
   if (tid == 0) {
     mbar_init(bar, 2);  // MMA batches: one commit from each issuing thread
     mbar_init(bar + 1, 1);
@@ -649,10 +652,10 @@ __global__ void __launch_bounds__(kGradThreads, kF32<E> ? 1 : 2) bwd_grads_kerne
         {tD, op(lv_first(Ti, L - 1), true), op(lv_rest(dU), true), false}};
     um::products(ps);
     um::commit(bar);
-  } else if (okw && tid == 32) {  // U dS'^T in A (decay: dy S^T in B)
+  } else if (okw && tid == 32) {  // U dS'^T in A (decay: in E, and dy S^T in F)
     if constexpr (DEC) {
-      const um::Prod ps[2] = {{tA, op(U, false), op(Dp, false), false},
-                              {tB, op(dY, false), op(S, false), false}};
+      const um::Prod ps[2] = {{tb + 256, op(U, false), op(Dp, false), false},
+                              {tb + 320, op(dY, false), op(S, false), false}};
       um::products(ps);
     } else {
       const um::Prod ps[1] = {{tA, op(U, false), op(Dp, false), false}};
@@ -661,32 +664,7 @@ __global__ void __launch_bounds__(kGradThreads, kF32<E> ? 1 : 2) bwd_grads_kerne
     um::commit(bar);
   }
   wait_mma();
-  float uds[2][16];  // U dS'^T of this thread's row, held until the last epilogue
-  float dqs[2][16];  // decay: P_t (dy S^T) of this thread's row (dQ's first term)
-  if constexpr (DEC) {
-#pragma unroll
-    for (int half = 0; half < 2; ++half) {
-      const int c0 = 32 * hh + 16 * half;
-      uint32_t r1[16];
-      um::ld16_async(lb + 64 + 16 * half, r1);
-      um::ld_wait();
-      um::ld_bind(r1, dqs[half]);
-      const float pt = rv && row < Cc ? Pt[row] : 0.f;
-      float d = 0.f;  // q_t . (dy S^T)_t over these columns: the gradient of P_t
-#pragma unroll
-      for (int i = 0; i < 16; ++i) {
-        const int o = um::boff(row, c0 + i);
-        const float qv = __bfloat162float(Q.t[0][o]) + __bfloat162float(Q.t[1][o]) +
-                         __bfloat162float(Q.t[2][o]);
-        d = fmaf(qv, dqs[half][i], d);
-        dqs[half][i] *= pt;
-      }
-      if (rv && row < Cc) {  // G2[t][-1] += P_t dP_t
-        atomicAdd(dl + 0, (double)(pt * d));
-        atomicAdd(dl + row + 1, (double)(-pt * d));
-      }
-    }
-  }
+  float uds[2][16];  // U dS'^T of this thread's row, held until the last epilogue (no decay)
 #pragma unroll
   for (int half = 0; half < 2; ++half) {  // dV = G; Gn = -G
     const int c0 = 32 * hh + 16 * half;
@@ -694,11 +672,11 @@ __global__ void __launch_bounds__(kGradThreads, kF32<E> ? 1 : 2) bwd_grads_kerne
     float g[16], g2[16];
     um::ld16_async(lb + 128 + 16 * half, r1);
     um::ld16_async(lb + 192 + 16 * half, r2);
-    um::ld16_async(lb + 0 + 16 * half, r3);
+    if constexpr (!DEC) um::ld16_async(lb + 0 + 16 * half, r3);
     um::ld_wait();
     um::ld_bind(r1, g);
     um::ld_bind(r2, g2);
-    um::ld_bind(r3, uds[half]);
+    if constexpr (!DEC) um::ld_bind(r3, uds[half]);
     if (rv) {
 #pragma unroll
       for (int i = 0; i < 16; ++i) g[i] += g2[i];
@@ -845,9 +823,28 @@ __global__ void __launch_bounds__(kGradThreads, kF32<E> ? 1 : 2) bwd_grads_kerne
     um::ld_bind(r2, v2);
     um::ld_bind(r3, v3);
     um::ld_bind(r4, v4);
-    if constexpr (DEC) {
+    if constexpr (DEC) {  // U dS'^T (E); dQ += P_t (dy S^T) (F), whose Q-weighted sum is dP_t
+      uint32_t r5[16], r6[16];
+      float dys[16];
+      um::ld16_async(lb + 256 + 16 * half, r5);
+      um::ld16_async(lb + 320 + 16 * half, r6);
+      um::ld_wait();
+      um::ld_bind(r5, uds[half]);
+      um::ld_bind(r6, dys);
+      const float pt = rv && row < Cc ? Pt[row] : 0.f;
+      float d = 0.f;
 #pragma unroll
-      for (int i = 0; i < 16; ++i) v[i] += dqs[half][i];
+      for (int i = 0; i < 16; ++i) {
+        const int o = um::boff(row, c0 + i);
+        const float qv = __bfloat162float(Q.t[0][o]) + __bfloat162float(Q.t[1][o]) +
+                         __bfloat162float(Q.t[2][o]);
+        d = fmaf(qv, dys[i], d);
+        v[i] += pt * dys[i];
+      }
+      if (rv && row < Cc) {  // G2[t][-1] += P_t dP_t
+        atomicAdd(dl + 0, (double)(pt * d));
+        atomicAdd(dl + row + 1, (double)(-pt * d));
+      }
     }
     if (okw && rv && row < Cc) row16_to_global(p.dQ + (bh * p.T + t0 + row) * p.dk, c0, p.dk, v);
     if (okw && rv && row < Mc) {
@@ -905,7 +902,7 @@ __global__ void __launch_bounds__(kGradThreads, kF32<E> ? 1 : 2) bwd_grads_kerne
   }
   if (warp == 0) {
     um::fence_after();
-    um::dealloc(tb, kGradTmemCols);
+    um::dealloc(tb, kCols);
   }
 }
 
@@ -915,10 +912,15 @@ constexpr int kF32Ld = 65;  // row stride of the fp32 64 x 64 matrices of the in
 // fp32 [64][kF32Ld]) in fp32: the four diagonal 16 x 16 blocks by forward
 // substitution (a thread per column), then block row i = 1..3 from the rows
 // above it, X_ij = -D_i^{-1} sum_{k=j}^{i-1} T_ik X_kj (Ys holds the sums).
-// Only the lower blocks of X are written (the diagonal blocks with zeros above
-// the diagonal). Ends with __syncthreads.
+// X's strictly-upper blocks are zeroed first, so every sum runs over a fixed
+// range (unrolled; each thread carries 1-3 independent sums). 256 threads;
+// ends with __syncthreads.
 __device__ void tri_inv_f32(const float* Tf, float* Xf, float* Ys) {
   const int tid = threadIdx.x;
+  for (int i = tid; i < 64 * 64; i += 256) {
+    const int r = i >> 6, c = i & 63;
+    if ((c >> 4) > (r >> 4)) Xf[r * kF32Ld + c] = 0.f;
+  }
   if (tid < 64) {
     const int o = (tid >> 4) * 16, j = tid & 15;
     float x[16];
@@ -933,20 +935,36 @@ __device__ void tri_inv_f32(const float* Tf, float* Xf, float* Ys) {
     for (int i = 0; i < 16; ++i) Xf[(o + i) * kF32Ld + o + j] = x[i];
   }
   __syncthreads();
+#pragma unroll
   for (int bi = 1; bi < 4; ++bi) {
-    const int r0 = 16 * bi, ncol = 16 * bi;
-    for (int e = tid; e < 16 * ncol; e += blockDim.x) {
-      const int r = e / ncol, cc = e - r * ncol;
-      float s = 0.f;
-      for (int k = cc & ~15; k < r0; ++k) s = fmaf(Tf[(r0 + r) * kF32Ld + k], Xf[k * kF32Ld + cc], s);
-      Ys[r * 48 + cc] = s;
+    const int r0 = 16 * bi, ncol = 16 * bi;  // 16 x ncol outputs: bi per thread
+    float y[3];
+#pragma unroll
+    for (int u = 0; u < bi; ++u) {
+      const int e = tid + 256 * u, r = e / ncol, cc = e - r * ncol;
+      float acc = 0.f;
+#pragma unroll
+      for (int k = 0; k < r0; ++k) acc = fmaf(Tf[(r0 + r) * kF32Ld + k], Xf[k * kF32Ld + cc], acc);
+      y[u] = acc;
+    }
+#pragma unroll
+    for (int u = 0; u < bi; ++u) {
+      const int e = tid + 256 * u, r = e / ncol, cc = e - r * ncol;
+      Ys[r * 48 + cc] = y[u];
     }
     __syncthreads();
-    for (int e = tid; e < 16 * ncol; e += blockDim.x) {
-      const int r = e / ncol, cc = e - r * ncol;
-      float s = 0.f;
-      for (int k = 0; k <= r; ++k) s = fmaf(Xf[(r0 + r) * kF32Ld + r0 + k], Ys[k * 48 + cc], s);
-      Xf[(r0 + r) * kF32Ld + cc] = -s;
+#pragma unroll
+    for (int u = 0; u < bi; ++u) {
+      const int e = tid + 256 * u, r = e / ncol, cc = e - r * ncol;
+      float acc = 0.f;
+#pragma unroll
+      for (int k = 0; k < 16; ++k) acc = fmaf(Xf[(r0 + r) * kF32Ld + r0 + k], Ys[k * 48 + cc], acc);
+      y[u] = -acc;
+    }
+#pragma unroll
+    for (int u = 0; u < bi; ++u) {
+      const int e = tid + 256 * u, r = e / ncol, cc = e - r * ncol;
+      Xf[(r0 + r) * kF32Ld + cc] = y[u];
     }
     __syncthreads();
   }
@@ -1197,8 +1215,8 @@ __global__ void __launch_bounds__(kPrepThreads, 2) prep_kernel(const TcArgs<bf16
 // smem: header | 15 blocked tiles: 0-5 the levels of [K; Q] interleaved
 // (Kh Qh Km Qm Kl Ql, so each level is one M = 128 operand) | 6-8 V | 9-11 P~ |
 // 12-14 T^{-1} | beta | Tf, Xf fp32 [64][65] | Ys fp32 [16][48].
-// beta W goes over Q's levels, beta U' over V's; the outputs Xn (0-2) and Qt
-// (3-5) over K and beta W, Bc and Yp (fp32) over Tf and Xf.
+// beta W goes over Q's levels, beta U' over V's; the outputs (Xn, Qt as
+// blocked levels, Bc, Yp fp32) go from registers straight to global memory.
 constexpr size_t kPrepF32Smem =
     1024 + 15 * (size_t)umma::kTileBytes + 256 + 2 * 64 * kF32Ld * 4 + 16 * 48 * 4 + 512;
 
@@ -1213,7 +1231,6 @@ __global__ void __launch_bounds__(kPrepThreads, 1) prep_f32_kernel(const TcArgs<
   const Lv K = lv(T(0), T(2), T(4)), Q = lv(T(1), T(3), T(5)), V = lv(T(6), T(7), T(8));
   const Lv P = lv(T(9), T(10), T(11)), Ti = lv(T(12), T(13), T(14));
   const Lv &BW = Q, &BU = V;
-  const Lv Xs = lv(T(0), T(1), T(2)), Qs = lv(T(3), T(4), T(5));
   float* bs = reinterpret_cast<float*>(T(15));
   float* Tf = bs + 64;
   float* Xf = Tf + 64 * kF32Ld;
@@ -1223,8 +1240,6 @@ __global__ void __launch_bounds__(kPrepThreads, 1) prep_f32_kernel(const TcArgs<
   float* Ft = Xf;            // decay: span factor table, until the inverse
   const Lv Ks = lv(reinterpret_cast<bf16*>(Tf), reinterpret_cast<bf16*>(Tf) + 4096,
                    reinterpret_cast<bf16*>(Tf) + 8192);  // decay: P^ K (level 3), c K (level 4)
-  float* Bcs = Tf;  // outputs, after the last products
-  float* Yps = Xf;
 
   constexpr int NTH = kPrepThreads;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -1406,23 +1421,24 @@ __global__ void __launch_bounds__(kPrepThreads, 1) prep_f32_kernel(const TcArgs<
         x[i] = -x[i] + (DEC && row == c0 + i && row < p.dk ? pe : 0.f);
         qt[i] = pr * qv[half][i] - qt[i];
       }
-      store16(Xs, row, c0, x);
-      store16(Qs, row, c0, qt);
-      if (row < p.dk) row16_f32_to_global(Bcs + row * p.dv, c0, p.dv, bc);
-      if (row < Cc) row16_f32_to_global(Yps + row * p.dv, c0, p.dv, yp);
+      // straight from registers to global memory (one CTA per SM: a bulk-copy
+      // drain at the end would hold the SM): Xn, Qt as blocked levels
+      if (okw) {
+        bf16* xg = p.Xn + blk * kSavedSet<float>;
+        bf16* qg = p.Qt + blk * kSavedSet<float>;
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+          const int o = um::boff(row, c0 + 8 * h);
+          um::store_split8_3(xg, xg + 4096, xg + 8192, o, x + 8 * h);
+          um::store_split8_3(qg, qg + 4096, qg + 8192, o, qt + 8 * h);
+        }
+        if (row < p.dk) row16_f32_to_global(p.Bc + blk * 4096 + row * p.dv, c0, p.dv, bc);
+        if (row < Cc) row16_f32_to_global(p.Yp + blk * 4096 + row * p.dv, c0, p.dv, yp);
+      }
     }
   }
-  fence_proxy_async_smem();
   um::fence_before();
   __syncthreads();
-  if (okw && tid == 0) {
-    bulk_s2g(p.Xn + blk * kSavedSet<float>, Xs.t[0], 3 * um::kTileBytes);  // levels contiguous
-    bulk_s2g(p.Qt + blk * kSavedSet<float>, Qs.t[0], 3 * um::kTileBytes);
-    bulk_s2g(p.Bc + blk * 4096, Bcs, (unsigned)(p.dk * p.dv * 4));
-    bulk_s2g(p.Yp + blk * 4096, Yps, (unsigned)(Cc * p.dv * 4));
-    bulk_commit();
-    bulk_wait_read();  // shared memory stays valid until the copies have read it
-  }
   if (tid == 64) bulk_wait_read();  // the T^{-1} copy has read its tiles
   if (warp == 0) {
     um::fence_after();
