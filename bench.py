@@ -707,6 +707,23 @@ def max_over_ranks(x: float, world: int, dev) -> float:
     return float(t.item())
 
 
+def count_mgs_launches(fn, dev) -> int | None:
+    """Kernel launches of this library (kernels in namespace mgs) in one call
+    of fn, from the CUDA activity of torch.profiler; None if it is unavailable."""
+    try:
+        from torch.profiler import ProfilerActivity, profile
+
+        torch.cuda.synchronize(dev)
+        with profile(activities=[ProfilerActivity.CUDA]) as prof:
+            fn()
+            torch.cuda.synchronize(dev)
+        return sum(1 for ev in prof.events()
+                   if ev.device_type is not None and "cuda" in str(ev.device_type).lower()
+                   and "mgs::" in ev.name)
+    except Exception:  # profiler unavailable
+        return None
+
+
 def host_threads() -> int:
     """All host cores this process may run on; also applied to the oracle and torch."""
     try:
@@ -1115,11 +1132,11 @@ def run_stack(args) -> None:
         loss_val = float(static_loss.item())
 
         # device-time share of the scan kernels over a few replays
-        share, scan_ms, kernels = None, None, {}
+        share, scan_ms, kernels, n_mgs = None, None, {}, 0
+        reps = 5
         try:
             from torch.profiler import ProfilerActivity, profile
 
-            reps = 5
             with profile(activities=[ProfilerActivity.CUDA]) as prof:
                 for _ in range(reps):
                     graph.replay()
@@ -1131,6 +1148,7 @@ def run_stack(args) -> None:
                 t = ev.device_time_total if hasattr(ev, "device_time_total") else ev.cuda_time_total
                 tot += t
                 if "mgs::" in ev.name:
+                    n_mgs += 1
                     scan += t
                     short = ev.name.split("(")[0].replace("void ", "")
                     kernels[short] = kernels.get(short, 0.0) + t / reps / 1e3
@@ -1167,7 +1185,7 @@ def run_stack(args) -> None:
         "scan_ms_per_step": scan_ms,
         "scan_kernels_ms": kernels,
         "loss": loss_val,
-        "gpu_launches": None,
+        "gpu_launches": (n_mgs // reps) * args.steps if n_mgs else None,  # one timed window
         "clocks": clk.summary(),
     }
     print(json.dumps(line), flush=True)
@@ -1254,6 +1272,7 @@ def run_sp(args) -> None:
         gp, _kp = capture(plain, dev, stream=work)
         gs, _ks = capture(sliced, dev, stream=work)
         reps = max(10, args.steps)
+        per_sliced = count_mgs_launches(gs.replay, dev)
         with ClockSampler(dev.index) as clk:
             clk.mark_start()
             plain_ms = time_graph(gp, reps, dev)
@@ -1281,7 +1300,7 @@ def run_sp(args) -> None:
         "one_launch_value": elems / (plain_ms * 1e-3) / 1e9,
         "sliced_over_one_launch": sliced_ms / plain_ms,
         "step_hbm_frac_one_launch": nbytes / (plain_ms * 1e-3) / 1e9 / peaks["hbm_gbs"],
-        "gpu_launches": None,
+        "gpu_launches": per_sliced * reps if per_sliced else None,
         "clocks": clk.summary(),
     }
     print(json.dumps(line), flush=True)
@@ -1351,6 +1370,7 @@ def run_sp_dist(args) -> None:
     for _ in range(args.warmup):
         sp_step()
         plain_step()
+    per_sp = count_mgs_launches(sp_step, dev)
     steps = max(3, args.steps)
     with ClockSampler(dev.index) as clk:
         clk.mark_start()
@@ -1380,7 +1400,7 @@ def run_sp_dist(args) -> None:
             "local_one_launch_ms_per_step": plain_ms,
             "sp_over_local_one_launch": sp_ms / plain_ms,
             "step_hbm_frac_per_gpu": per_elem * B * Tl * D / (sp_ms * 1e-3) / 1e9 / peaks["hbm_gbs"],
-            "gpu_launches": None,
+            "gpu_launches": per_sp * steps if per_sp else None,
             "clocks": clk.summary(),
         }
         print(json.dumps(line), flush=True)
@@ -1427,6 +1447,7 @@ def run_stack_step(args) -> None:
         for _ in range(3):
             graph.replay()
         torch.cuda.synchronize(dev)
+        per_token = count_mgs_launches(graph.replay, dev)
         with ClockSampler(dev.index) as clk:
             clk.mark_start()
             wins = []
@@ -1468,7 +1489,7 @@ def run_stack_step(args) -> None:
                    "windows": f"median of {len(wins)} windows of {args.steps} steps"},
         "eager_ms_per_step": eager_ms,
         "graph_speedup": eager_ms / per_tok,
-        "gpu_launches": None,
+        "gpu_launches": per_token * args.steps if per_token else None,  # one timed window
         "clocks": clk.summary(),
     }
     print(json.dumps(line), flush=True)

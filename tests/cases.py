@@ -99,6 +99,8 @@ def delta_case_inputs(kind: str, case):
 DELTA_GATED_CASES = [
     (2, 2, 100, 1, 32, 32, 32), (1, 2, 150, 2, 16, 16, 64), (1, 1, 70, 1, 64, 64, 64),
     (2, 3, 45, 3, 8, 16, 10), (1, 2, 90, 1, 16, 80, 64),
+    # d_k = 96 (the CUDA-core kernels with decay) and one token with nh = 2
+    (1, 2, 60, 1, 96, 32, 16), (2, 1, 1, 2, 16, 16, 8),
 ]
 
 
