@@ -263,7 +263,7 @@ __device__ __forceinline__ void row16_f32_to_global(float* g, int c0, int ncols,
 // l_s, accumulated from s = t down (as the reference's flipped cumulative sum),
 // each span from its own terms -- never a difference of running sums, so a
 // saturated gap zeroes exactly the spans that contain it:
-//   F[t][t'] = exp(span[t][t']) (t' <= t; 64 x 64 table), P_t = exp(span[t][-1]),
+//   F[t][t'] = exp(span[t][t']) (t' <= t; 64 x 64 table, rows kFLd apart), P_t = exp(span[t][-1]),
 //   c_m = F[Ct-1][tau(m)] (tau(m) = m / nh, the token of micro-step m).
 // The chunk's maps with decay:
 //   T = I + strict(K K^T * E) diag(beta),  E[i][l] = F[tau(i)][tau(l)]
@@ -271,23 +271,24 @@ __device__ __forceinline__ void row16_f32_to_global(float* g, int c0, int ncols,
 //   W' = T^{-1} diag(P^) K,  U' = T^{-1} V  (P^_m = P_{tau(m)})
 //   S' = P_{C-1} S + K^T diag(c beta) (U' - W' S),  y = diag(P) Q S + R (U' - W' S)
 // One thread per token row; ends with a barrier.
+constexpr int kFLd = 65;  // row stride of the factor table: lanes reading one column of many rows hit distinct banks
 __device__ void decay_tables(const float* lg, int Ct, int nh, float* F, float* Pt, float* cm) {
-  for (int i = threadIdx.x; i < 64 * 64; i += blockDim.x) F[i] = 0.f;  // padding factors are 0
+  for (int i = threadIdx.x; i < 64 * kFLd; i += blockDim.x) F[i] = 0.f;  // padding factors are 0
   for (int i = threadIdx.x; i < 64; i += blockDim.x) Pt[i] = 0.f;
   __syncthreads();
   const int t = threadIdx.x;
   if (t < Ct) {  // row t: the spans (u, t] for u = t-1 .. 0, summed from s = t down
     float s = 0.f;
-    F[t * 64 + t] = 1.f;
+    F[t * kFLd + t] = 1.f;
     for (int u = t - 1; u >= 0; --u) {
       s += lg[u + 1];
-      F[t * 64 + u] = expf(s);
+      F[t * kFLd + u] = expf(s);
     }
     Pt[t] = expf(s + lg[0]);
   }
   __syncthreads();
   for (int m = threadIdx.x; m < 64; m += blockDim.x)
-    cm[m] = m < Ct * nh ? F[(Ct - 1) * 64 + m / nh] : 0.f;
+    cm[m] = m < Ct * nh ? F[(Ct - 1) * kFLd + m / nh] : 0.f;
   __syncthreads();
 }
 
@@ -336,8 +337,9 @@ template <typename E>
 constexpr int kGradTiles = kF32<E> ? 24 : 13;
 template <typename E>
 constexpr size_t kGradSmem = 1024 + kGradTiles<E> * (size_t)umma::kTileBytes + 2048;
-// decay: span factor table [64][64], P_t [64], c_m [64], d l accumulator (fp64) [80]
-constexpr size_t kGradDecaySmem = 64 * 64 * 4 + (64 + 64) * 4 + 80 * 8;
+// decay: span factor table [64][65], P_t [64], c_m [64]; fp64: the d l difference
+// array [80], column sums [4][2][32], row sums [2][64] x 2, carry terms [64], warp sums [16]
+constexpr size_t kGradDecaySmem = 64 * 65 * 4 + (64 + 64) * 4 + (80 + 256 + 128 + 128 + 64 + 16) * 8;
 constexpr int kGradTmemCols = 256;
 
 // 64 rows x (8 * valid_ch) columns of a row-major global bf16 matrix into a
@@ -456,13 +458,20 @@ __global__ void __launch_bounds__(kGradThreads, kF32<E> ? 1 : 2) bwd_grads_kerne
   float* bs = reinterpret_cast<float*>(T(kGradTiles<E>));
   float* rpart = bs + 64;      // [2 column halves][64 rows]: sum_col U * dbU
   float* cpart = rpart + 128;  // [8 warps][32 columns]: masked-product column sums
-  float* Ft = bs + 512;        // decay: factor table [64][64]
-  float* Pt = Ft + 64 * 64;    // decay: P_t
+  float* Ft = bs + 512;        // decay: factor table [64][kFLd]
+  float* Pt = Ft + 64 * kFLd;  // decay: P_t
   float* cm = Pt + 64;         // decay: c_m
-  // decay: d l difference array [Cc + 1], then <S, dS'> at [72], in fp64: its prefix sums
-  // carry every entry's rounding into all later tokens, and with fp32 entries that
-  // shared error adds up coherently in sums over tokens (the gradient of lambda)
+  // decay: the d l difference array [Cc + 1] and the partial sums it is built
+  // from, in fp64 (a prefix sum carries every entry's rounding into all later
+  // tokens, and in fp32 that shared error adds up coherently in sums over tokens,
+  // the gradient of lambda). Every partial has one writer: no atomics.
   double* dl = reinterpret_cast<double*>(cm + 64);
+  double* colb = dl + 80;     // [q][hh][32]: column sums of the level-4 span terms (+ at tau(l) + 1)
+  double* rowT = colb + 256;  // [hh][64]: token-row terms, negated (at t + 1)
+  double* rowM = rowT + 128;  // [hh][64]: micro-step-row terms, negated (at tau(i) + 1)
+  double* carS = rowM + 128;  // [64]: carry terms (+ at tau(m) + 1, - at Ct)
+  double* wred = carS + 64;   // [2][8]: per-warp sums of the (-1, .] terms and of <S, dS'>
+  double accT = 0.0, accM = 0.0, acc0 = 0.0, accS = 0.0;  // this thread's partials
 
   constexpr int NTH = kGradThreads;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -485,8 +494,6 @@ __global__ void __launch_bounds__(kGradThreads, kF32<E> ? 1 : 2) bwd_grads_kerne
     mbar_init(bar + 1, 1);
     mbar_fence_init();
   }
-  if constexpr (DEC)
-    if (tid < 80) dl[tid] = 0.0;  // before the barrier below: the S . dS' sums start right after it
   if constexpr (F) {
     const Lv xs[4] = {K, Q, dY, V};
     const InSrc ss[4] = {{p.K + (bh * rows + r0) * p.dk, p.dk, Mc, p.dk >> 3},
@@ -535,7 +542,7 @@ __global__ void __launch_bounds__(kGradThreads, kF32<E> ? 1 : 2) bwd_grads_kerne
         float d = 0.f;
 #pragma unroll
         for (int j = 0; j < 8; ++j) d = fmaf(av[j], bv[j], d);
-        atomicAdd(dl + 72, (double)(d));
+        accS += d;
       }
     }
   }
@@ -598,7 +605,7 @@ __global__ void __launch_bounds__(kGradThreads, kF32<E> ? 1 : 2) bwd_grads_kerne
         const int cl = c0 + i;
         const bool rd = cl < (row + 1) * p.nh && cl < Mc;
         v[i] = rd ? v[i] * bs[cl] : 0.f;
-        if constexpr (DEC) v[i] *= rd && row < Cc ? Ft[row * 64 + cl / p.nh] : 0.f;
+        if constexpr (DEC) v[i] *= rd && row < Cc ? Ft[row * kFLd + cl / p.nh] : 0.f;
         w[i] = -ph * w[i];
       }
       store16(P, row, c0, v);
@@ -728,8 +735,8 @@ __global__ void __launch_bounds__(kGradThreads, kF32<E> ? 1 : 2) bwd_grads_kerne
         const float x = (rv && cl < (row + 1) * p.nh && cl < Mc) ? ds[i] : 0.f;
         const float y = (rv && cl < row && cl < Mc) ? dk[i] : 0.f;
         if constexpr (DEC) {
-          const float fd = rv && row < Cc ? Ft[row * 64 + cl / p.nh] : 0.f;           // D[t][l]
-          const float fe = rv && row < Mc ? Ft[(row / p.nh) * 64 + cl / p.nh] : 0.f;  // E[i][l]
+          const float fd = rv && row < Cc ? Ft[row * kFLd + cl / p.nh] : 0.f;           // D[t][l]
+          const float fe = rv && row < Mc ? Ft[(row / p.nh) * kFLd + cl / p.nh] : 0.f;  // E[i][l]
           const float xr = x * qk[i] * fd, yt = y * kk[i] * fe;
           e[i] = xr + yt;
           const double wr = cl / p.nh < row ? (double)(xr * bs[cl]) : 0.0;         // span (tau(l), t]
@@ -746,8 +753,8 @@ __global__ void __launch_bounds__(kGradThreads, kF32<E> ? 1 : 2) bwd_grads_kerne
         }
       }
       if constexpr (DEC) {
-        if (rv && row < Cc) atomicAdd(dl + row + 1, (double)(-rsR));
-        if (rv && row < Mc) atomicAdd(dl + row / p.nh + 1, (double)(-rsT));
+        accT -= rsR;  // zero on padded rows (their factors are 0)
+        accM -= rsT;
         // column sums of eg (as for e below): + at tau(l) + 1
 #pragma unroll
         for (int d = 8, n = 16; d >= 1; d >>= 1, n >>= 1) {
@@ -760,8 +767,7 @@ __global__ void __launch_bounds__(kGradThreads, kF32<E> ? 1 : 2) bwd_grads_kerne
           }
         }
         const double colg = __shfl_sync(0xffffffffu, eg[0], lane & 15);
-        const int cg = c0 + (lane & 15);
-        if (lane < 16 && cg < Mc) atomicAdd(dl + cg / p.nh + 1, (double)(colg));
+        if (lane < 16) colb[(q * 2 + hh) * 32 + 16 * half + lane] = colg;
       }
       // column sums over the 16 rows of each half-warp by a transposing
       // butterfly: at distance d a lane keeps the half of its values selected
@@ -842,8 +848,8 @@ __global__ void __launch_bounds__(kGradThreads, kF32<E> ? 1 : 2) bwd_grads_kerne
         v[i] += pt * dys[i];
       }
       if (rv && row < Cc) {  // G2[t][-1] += P_t dP_t
-        atomicAdd(dl + 0, (double)(pt * d));
-        atomicAdd(dl + row + 1, (double)(-pt * d));
+        acc0 += (double)(pt * d);
+        accT -= (double)(pt * d);
       }
     }
     if (okw && rv && row < Cc) row16_to_global(p.dQ + (bh * p.T + t0 + row) * p.dk, c0, p.dk, v);
@@ -860,8 +866,8 @@ __global__ void __launch_bounds__(kGradThreads, kF32<E> ? 1 : 2) bwd_grads_kerne
           d = fmaf(kv, v3[i], d);
           v3[i] *= ph;
         }
-        atomicAdd(dl + 0, (double)(ph * d));  // G2[tau(m)][-1] += P^_m dP^_m
-        atomicAdd(dl + row / p.nh + 1, (double)(-ph * d));
+        acc0 += (double)(ph * d);  // G2[tau(m)][-1] += P^_m dP^_m
+        accM -= (double)(ph * d);
       }
 #pragma unroll
       for (int i = 0; i < 16; ++i) v2[i] += v3[i] + v4[i] + b * uds[half][i];
@@ -877,19 +883,51 @@ __global__ void __launch_bounds__(kGradThreads, kF32<E> ? 1 : 2) bwd_grads_kerne
                     (cpart[(4 * h2) * 32 + cl] + cpart[(4 * h2 + 1) * 32 + cl]) +
                     (cpart[(4 * h2 + 2) * 32 + cl] + cpart[(4 * h2 + 3) * 32 + cl]);
     p.dbeta[bh * rows + r0 + tid] = fromf<E>(d);
-    if constexpr (DEC) {  // carry factor c_m: span (tau(m), Ct - 1]
-      if (tid / p.nh < Cc - 1) {
-        const float w = bs[tid] * cm[tid] * ru;
-        atomicAdd(dl + tid / p.nh + 1, (double)(w));
-        atomicAdd(dl + Cc, (double)(-w));
-      }
-    }
+    if constexpr (DEC)  // carry factor c_m: span (tau(m), Ct - 1]
+      carS[tid] = tid / p.nh < Cc - 1 ? (double)(bs[tid] * cm[tid] * ru) : 0.0;
   }
   if constexpr (DEC) {
-    if (tid == 0) {  // P_{C-1} S: span (-1, Ct - 1]
-      const double w = (double)Pt[Cc - 1] * dl[72];
-      atomicAdd(dl + 0, (double)(w));
-      atomicAdd(dl + Cc, (double)(-w));
+    if (tid >= Mc && tid < 64) carS[tid] = 0.0;
+    if (rv) {
+      rowT[hh * 64 + row] = accT;
+      rowM[hh * 64 + row] = accM;
+    }
+#pragma unroll
+    for (int o = 16; o >= 1; o >>= 1) {
+      acc0 += __shfl_xor_sync(0xffffffffu, acc0, o);
+      accS += __shfl_xor_sync(0xffffffffu, accS, o);
+    }
+    if (lane == 0) {
+      wred[warp] = acc0;
+      wred[8 + warp] = accS;
+    }
+    __syncthreads();
+    if (tid <= Cc) {  // difference-array entry u = tid: + terms starting at u, - terms ending at u
+      const int u = tid;
+      double sum = 0.0, car = 0.0;
+      for (int m = 0; m < Mc; ++m) car += carS[m];
+      if (u == 0) {
+        double z = 0.0, sd = 0.0;
+        for (int w = 0; w < 8; ++w) {
+          z += wred[w];
+          sd += wred[8 + w];
+        }
+        sum = z + (double)Pt[Cc - 1] * sd;  // (-1, t] terms and P_{C-1} S: span (-1, Ct - 1]
+      }
+      if (u >= 1) {
+        for (int l = (u - 1) * p.nh; l < u * p.nh && l < Mc; ++l) {  // columns of token u - 1
+          for (int qq = 0; qq < 4; ++qq) sum += colb[(qq * 2 + (l >> 5)) * 32 + (l & 31)];
+          sum += carS[l];
+          sum += rowM[l] + rowM[64 + l];  // micro-step rows of token u - 1 (hold -w)
+        }
+        if (u - 1 < Cc) sum += rowT[u - 1] + rowT[64 + u - 1];  // token row u - 1 (holds -w)
+      }
+      if (u == Cc) sum -= car + (double)Pt[Cc - 1] * [&] {
+        double sd = 0.0;
+        for (int w = 0; w < 8; ++w) sd += wred[8 + w];
+        return sd;
+      }();
+      dl[u] = sum;
     }
     __syncthreads();
     if (okw && tid == 0) {  // d l_s = prefix sums of the difference array
@@ -1298,7 +1336,7 @@ __global__ void __launch_bounds__(kPrepThreads, 1) prep_f32_kernel(const TcArgs<
 #pragma unroll
         for (int i = 0; i < 16; ++i) {
           float x = c0 + i < r ? v[i] * bs[c0 + i] : 0.f;
-          if constexpr (DEC) x *= c0 + i < r ? Ft[(r / p.nh) * 64 + (c0 + i) / p.nh] : 0.f;
+          if constexpr (DEC) x *= c0 + i < r ? Ft[(r / p.nh) * kFLd + (c0 + i) / p.nh] : 0.f;
           Tf[r * kF32Ld + c0 + i] = x;
         }
       } else {
@@ -1307,7 +1345,7 @@ __global__ void __launch_bounds__(kPrepThreads, 1) prep_f32_kernel(const TcArgs<
         for (int i = 0; i < 16; ++i) {
           const bool rd = c0 + i < (ti + 1) * p.nh && c0 + i < Mc;
           v[i] = rd ? v[i] : 0.f;
-          if constexpr (DEC) v[i] *= rd ? Ft[ti * 64 + (c0 + i) / p.nh] : 0.f;
+          if constexpr (DEC) v[i] *= rd ? Ft[ti * kFLd + (c0 + i) / p.nh] : 0.f;
         }
         store16(P, ti, c0, v);
       }
