@@ -270,43 +270,73 @@ __device__ __forceinline__ void row16_f32_to_global(float* g, int c0, int ncols,
 //   R = (Q K^T * D * read) diag(beta),     D[t][l] = F[t][tau(l)]
 //   W' = T^{-1} diag(P^) K,  U' = T^{-1} V  (P^_m = P_{tau(m)})
 //   S' = P_{C-1} S + K^T diag(c beta) (U' - W' S),  y = diag(P) Q S + R (U' - W' S)
-// One thread per token row; ends with a barrier.
 constexpr int kFLd = 65;  // row stride of the factor table: lanes reading one column of many rows hit distinct banks
+
+// tau(m) = m / nh (the token of micro-step m) for 0 <= m < 128 without an
+// integer division: (m + 1/2) / nh lies at least 1 / (2 nh) >= 1/128 from an
+// integer, far beyond the rounding of m * (1 / nh) in fp32.
+__device__ __forceinline__ int tok_of(int m, float inv_nh) {
+  return __float2int_rz(((float)m + 0.5f) * inv_nh);
+}
+
+// The factor table F, P_t and c_m of a chunk. Row t, one warp:
+// span[t][t-1-j] = a_0 + ... + a_j with a_j = l_{t-j}, an inclusive warp scan
+// per 32 terms plus the running total. Every l <= 0, so any summation order
+// is well conditioned; each partial sum holds only its own span's terms (no
+// differences). Ends with a barrier.
 __device__ void decay_tables(const float* lg, int Ct, int nh, float* F, float* Pt, float* cm) {
   for (int i = threadIdx.x; i < 64 * kFLd; i += blockDim.x) F[i] = 0.f;  // padding factors are 0
   for (int i = threadIdx.x; i < 64; i += blockDim.x) Pt[i] = 0.f;
   __syncthreads();
-  const int t = threadIdx.x;
-  if (t < Ct) {  // row t: the spans (u, t] for u = t-1 .. 0, summed from s = t down
-    float s = 0.f;
-    F[t * kFLd + t] = 1.f;
-    for (int u = t - 1; u >= 0; --u) {
-      s += lg[u + 1];
-      F[t * kFLd + u] = expf(s);
+  const int lane = threadIdx.x & 31, nw = blockDim.x >> 5;
+  for (int t = threadIdx.x >> 5; t < Ct; t += nw) {
+    float carry = 0.f;
+    for (int j0 = 0; j0 < t; j0 += 32) {
+      const int j = j0 + lane;
+      float v = j < t ? lg[t - j] : 0.f;
+#pragma unroll
+      for (int d = 1; d < 32; d <<= 1) {
+        const float n = __shfl_up_sync(0xffffffffu, v, d);
+        if (lane >= d) v += n;
+      }
+      v += carry;
+      if (j < t) F[t * kFLd + t - 1 - j] = expf(v);
+      carry = __shfl_sync(0xffffffffu, v, 31);
     }
-    Pt[t] = expf(s + lg[0]);
+    if (lane == 0) {
+      F[t * kFLd + t] = 1.f;
+      Pt[t] = expf(carry + lg[0]);
+    }
   }
   __syncthreads();
+  const float inh = 1.f / (float)nh;
   for (int m = threadIdx.x; m < 64; m += blockDim.x)
-    cm[m] = m < Ct * nh ? F[(Ct - 1) * kFLd + m / nh] : 0.f;
+    cm[m] = m < Ct * nh ? F[(Ct - 1) * kFLd + tok_of(m, inh)] : 0.f;
   __syncthreads();
 }
 
-// 64 rows of a row-major fp32 global matrix, each scaled by f[row / nh], into
-// three blocked levels (rows >= nrows and chunks >= valid_ch zero).
+// dst = diag(f[tau(row)]) x, x given by its three blocked levels in shared
+// memory (rows >= nrows zero), re-split into three levels.
 template <int NTHR>
-__device__ __forceinline__ void stage_scaled_f32(const Lv& x, const float* g, long long ld, int nrows,
-                                                 int valid_ch, const float* f, int nh) {
+__device__ __forceinline__ void scale_rows_levels(const Lv& dst, const Lv& x, int nrows, const float* f,
+                                                  float inh) {
   for (int i = threadIdx.x; i < 64 * 8; i += NTHR) {
-    const int row = i >> 3, ch = i & 7;
-    float4 a = make_float4(0.f, 0.f, 0.f, 0.f), b = a;
-    if (row < nrows && ch < valid_ch) {
-      a = __ldg(reinterpret_cast<const float4*>(g + row * ld + ch * 8));
-      b = __ldg(reinterpret_cast<const float4*>(g + row * ld + ch * 8 + 4));
+    const int row = i >> 3, ch = i & 7, o = umma::boff(row, ch * 8);
+    const float sc = row < nrows ? f[tok_of(row, inh)] : 0.f;
+    const uint4 h = *reinterpret_cast<const uint4*>(x.t[0] + o);
+    const uint4 m = *reinterpret_cast<const uint4*>(x.t[1] + o);
+    const uint4 l = *reinterpret_cast<const uint4*>(x.t[2] + o);
+    const uint32_t hw[4] = {h.x, h.y, h.z, h.w}, mw[4] = {m.x, m.y, m.z, m.w}, lw[4] = {l.x, l.y, l.z, l.w};
+    float v[8];
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      const float2 a = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&hw[k]));
+      const float2 b = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&mw[k]));
+      const float2 c = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&lw[k]));
+      v[2 * k] = sc * (a.x + b.x + c.x);
+      v[2 * k + 1] = sc * (a.y + b.y + c.y);
     }
-    const float sc = row < nrows ? f[row / nh] : 0.f;
-    const float v[8] = {sc * a.x, sc * a.y, sc * a.z, sc * a.w, sc * b.x, sc * b.y, sc * b.z, sc * b.w};
-    store8(x, umma::boff(row, ch * 8), v);
+    store8(dst, o, v);
   }
 }
 
@@ -477,6 +507,7 @@ __global__ void __launch_bounds__(kGradThreads, kF32<E> ? 1 : 2) bwd_grads_kerne
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int q = warp & 3, hh = warp >> 2, row = 16 * q + lane;
   const bool rv = lane < 16;  // this lane holds row `row` of the 64-row accumulators
+  const float inh = 1.f / (float)p.nh;
   const int c = blockIdx.x % p.nchunks;
   const long long bh = blockIdx.x / p.nchunks;
   const long long t0 = (long long)c * p.C;
@@ -599,13 +630,13 @@ __global__ void __launch_bounds__(kGradThreads, kF32<E> ? 1 : 2) bwd_grads_kerne
     um::ld_bind(r2, w);
     if (rv) {
       // decay: -W <- -P^ (K S) (rhs of U = T^{-1} (V - P^ K S)), P's read factors D
-      const float ph = DEC ? (row < Mc ? Pt[row / p.nh] : 0.f) : 1.f;
+      const float ph = DEC ? (row < Mc ? Pt[tok_of(row, inh)] : 0.f) : 1.f;
 #pragma unroll
       for (int i = 0; i < 16; ++i) {
         const int cl = c0 + i;
         const bool rd = cl < (row + 1) * p.nh && cl < Mc;
         v[i] = rd ? v[i] * bs[cl] : 0.f;
-        if constexpr (DEC) v[i] *= rd && row < Cc ? Ft[row * kFLd + cl / p.nh] : 0.f;
+        if constexpr (DEC) v[i] *= rd && row < Cc ? Ft[row * kFLd + tok_of(cl, inh)] : 0.f;
         w[i] = -ph * w[i];
       }
       store16(P, row, c0, v);
@@ -735,12 +766,13 @@ __global__ void __launch_bounds__(kGradThreads, kF32<E> ? 1 : 2) bwd_grads_kerne
         const float x = (rv && cl < (row + 1) * p.nh && cl < Mc) ? ds[i] : 0.f;
         const float y = (rv && cl < row && cl < Mc) ? dk[i] : 0.f;
         if constexpr (DEC) {
-          const float fd = rv && row < Cc ? Ft[row * kFLd + cl / p.nh] : 0.f;           // D[t][l]
-          const float fe = rv && row < Mc ? Ft[(row / p.nh) * kFLd + cl / p.nh] : 0.f;  // E[i][l]
+          const int tl = tok_of(cl, inh), tr = tok_of(row, inh);
+          const float fd = rv && row < Cc ? Ft[row * kFLd + tl] : 0.f;     // D[t][l]
+          const float fe = rv && row < Mc ? Ft[tr * kFLd + tl] : 0.f;      // E[i][l]
           const float xr = x * qk[i] * fd, yt = y * kk[i] * fe;
           e[i] = xr + yt;
-          const double wr = cl / p.nh < row ? (double)(xr * bs[cl]) : 0.0;         // span (tau(l), t]
-          const double wt = cl / p.nh < row / p.nh ? (double)(yt * bs[cl]) : 0.0;  // span (tau(l), tau(i)]
+          const double wr = tl < row ? (double)(xr * bs[cl]) : 0.0;  // span (tau(l), t]
+          const double wt = tl < tr ? (double)(yt * bs[cl]) : 0.0;   // span (tau(l), tau(i)]
           rsR += wr;
           rsT += wt;
           eg[i] = wr + wt;
@@ -856,7 +888,7 @@ __global__ void __launch_bounds__(kGradThreads, kF32<E> ? 1 : 2) bwd_grads_kerne
     if (okw && rv && row < Mc) {
       const float b = DEC ? bs[row] * cm[row] : bs[row];
       if constexpr (DEC) {  // -G S^T rows take P^; its K-weighted sum is the gradient of P^
-        const float ph = Pt[row / p.nh];
+        const float ph = Pt[tok_of(row, inh)];
         float d = 0.f;
 #pragma unroll
         for (int i = 0; i < 16; ++i) {
@@ -884,7 +916,7 @@ __global__ void __launch_bounds__(kGradThreads, kF32<E> ? 1 : 2) bwd_grads_kerne
                     (cpart[(4 * h2 + 2) * 32 + cl] + cpart[(4 * h2 + 3) * 32 + cl]);
     p.dbeta[bh * rows + r0 + tid] = fromf<E>(d);
     if constexpr (DEC)  // carry factor c_m: span (tau(m), Ct - 1]
-      carS[tid] = tid / p.nh < Cc - 1 ? (double)(bs[tid] * cm[tid] * ru) : 0.0;
+      carS[tid] = tok_of(tid, inh) < Cc - 1 ? (double)(bs[tid] * cm[tid] * ru) : 0.0;
   }
   if constexpr (DEC) {
     if (tid >= Mc && tid < 64) carS[tid] = 0.0;
@@ -1288,6 +1320,7 @@ __global__ void __launch_bounds__(kPrepThreads, 1) prep_f32_kernel(const TcArgs<
   const int Cc = (int)min((long long)p.C, p.T - t0), Mc = Cc * p.nh;
   const long long r0 = t0 * p.nh, rows = p.T * p.nh;
   const long long blk = bh * p.nchunks + c;
+  const float inh = 1.f / (float)p.nh;
 
   if (warp == 0) um::alloc(tbase_s, 256);
   if (tid == 0) {
@@ -1336,7 +1369,7 @@ __global__ void __launch_bounds__(kPrepThreads, 1) prep_f32_kernel(const TcArgs<
 #pragma unroll
         for (int i = 0; i < 16; ++i) {
           float x = c0 + i < r ? v[i] * bs[c0 + i] : 0.f;
-          if constexpr (DEC) x *= c0 + i < r ? Ft[(r / p.nh) * kFLd + (c0 + i) / p.nh] : 0.f;
+          if constexpr (DEC) x *= c0 + i < r ? Ft[tok_of(r, inh) * kFLd + tok_of(c0 + i, inh)] : 0.f;
           Tf[r * kF32Ld + c0 + i] = x;
         }
       } else {
@@ -1345,7 +1378,7 @@ __global__ void __launch_bounds__(kPrepThreads, 1) prep_f32_kernel(const TcArgs<
         for (int i = 0; i < 16; ++i) {
           const bool rd = c0 + i < (ti + 1) * p.nh && c0 + i < Mc;
           v[i] = rd ? v[i] : 0.f;
-          if constexpr (DEC) v[i] *= rd ? Ft[ti * kFLd + (c0 + i) / p.nh] : 0.f;
+          if constexpr (DEC) v[i] *= rd ? Ft[ti * kFLd + tok_of(c0 + i, inh)] : 0.f;
         }
         store16(P, ti, c0, v);
       }
@@ -1361,9 +1394,9 @@ __global__ void __launch_bounds__(kPrepThreads, 1) prep_f32_kernel(const TcArgs<
     for (int j = 0; j < 8; ++j) v[j] = ch * 8 + j <= row ? Xf[row * kF32Ld + ch * 8 + j] : 0.f;
     store8(Ti, um::boff(row, ch * 8), v);
   }
-  if constexpr (DEC) {  // P^ K over Tf / Xf (the inverse is done with them)
+  if constexpr (DEC) {  // P^ K over Tf / Xf (the inverse is done with them), from K's levels
     __syncthreads();
-    stage_scaled_f32<NTH>(Ks, p.K + (bh * rows + r0) * p.dk, p.dk, Mc, p.dk >> 3, Pt, p.nh);
+    scale_rows_levels<NTH>(Ks, K, Mc, Pt, inh);
   }
   to_mma();
   if (okw && tid == 64) {  // T^{-1} (three contiguous levels) to `saved`; its tiles stay untouched
@@ -1382,8 +1415,8 @@ __global__ void __launch_bounds__(kPrepThreads, 1) prep_f32_kernel(const TcArgs<
   const int row = 16 * q + lane;  // M = 64 accumulators: lanes 0-15 hold rows
   const bool rv = lane < 16;
   const uint32_t lb = tb + ((uint32_t)(32 * q) << 16) + 32 * hh;
-  if constexpr (DEC)  // c K over P^ K (level 3 has read it)
-    stage_scaled_f32<NTH>(Ks, p.K + (bh * rows + r0) * p.dk, p.dk, Mc, p.dk >> 3, cm, 1);
+  if constexpr (DEC)  // c K over P^ K (level 3 has read it), from K's levels
+    scale_rows_levels<NTH>(Ks, K, Mc, cm, 1.f);
 #pragma unroll
   for (int half = 0; half < 2; ++half) {  // beta W (over Q), beta U' (over V)
     const int c0 = 32 * hh + 16 * half;
