@@ -433,8 +433,9 @@ class DeltaWorkload(ScanWorkload):
 
     def __init__(self, dtype=torch.bfloat16, name="cfg5", B=8, T=8192, H=8, d=64, chunk=64):
         super().__init__(dtype)
-        if dtype != torch.bfloat16:  # fp32 / fp16 inputs run the CUDA-core kernels
+        if dtype != torch.bfloat16:  # fp32 inputs: three-level operands, fp32-grade products
             self.compute_dtype = "f32"
+            self.workload = self.workload.replace("bf16 in", "fp32 in")
         self.B, self.T, self.H, self.d, self.chunk, self.name = B, T, H, d, chunk, name
         self.D = H * d  # elems = B*T*H*d_v
         e = self.esize

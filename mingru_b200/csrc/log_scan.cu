@@ -489,7 +489,6 @@ constexpr long long kColTmax = 1024;
 // Longest segment of NS segments per channel (T <= kColTmax).
 template <int NS>
 constexpr int col_maxlen() { return (int)(kColTmax / NS) + 1; }
-constexpr int kColMaxLen = col_maxlen<kColSegs>();
 constexpr float kColLinLo = -30.f, kColLinHi = 20.f;  // linear-domain envelope of log values
 
 // Segments per channel of a W-channel group (see the geometry: 16 x 32 or 8 x 64).
