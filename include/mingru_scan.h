@@ -272,7 +272,11 @@ int mgs_affine_scan_bwd(const void* A, const void* Bm, const void* Abar, const v
 
 size_t mgs_angle_scan_workspace_size(int64_t B, int64_t T, int64_t n, int R, int k,
                                      int brickwall, int dtype);
-/* 0 when the sequential kernels are used (the backward then needs `h`). */
+/* Register look-back kernels: k*k floats per block and time tile (the linear
+ * part of each forward tile aggregate, which the backward reuses transposed);
+ * a forward that will be differentiated passes a buffer of this size as
+ * `carries` (NULL otherwise) and the backward gets the same buffer back.
+ * 0 when the sequential kernels are used. */
 size_t mgs_angle_scan_carry_size(int64_t B, int64_t T, int64_t n, int R, int k, int brickwall,
                                  int dtype);
 
@@ -284,7 +288,8 @@ int mgs_angle_scan_fwd(const void* theta, const void* scale, const void* gamma, 
 
 /* Backward: (dtheta, dscale, dgamma, db, dh0) of sum(h * grad_h). dscale /
  * dgamma are written only when has_scale / has_decay (the caller zeroes them
- * otherwise). `h` may be NULL on the register path (it uses `carries`). */
+ * otherwise). Both paths read the stored states `h`; the register path also
+ * needs the forward's `carries`. */
 int mgs_angle_scan_bwd(const void* theta, const void* scale, const void* gamma, const void* b,
                        const void* h0, const int32_t* perm, const float* sgn, const int32_t* p2p,
                        const void* h, const void* grad_h, const void* carries, void* dtheta,

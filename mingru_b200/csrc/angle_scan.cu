@@ -20,15 +20,13 @@
 //
 // Design. One lane owns one (b, block); the state is a k-vector in registers
 // and each step applies the rotations directly (never a k x k matrix). For
-// chunk parallelism the aggregate of a run of steps is the affine map
+// chunk parallelism the aggregate of a tile of steps is the affine map
 // [P | q] (k x (k+1)), obtained by pushing the k+1 columns of [I | 0]
-// through the same rotations; aggregates compose as [P2 P1 | P2 q1 + q2],
-// the initial state enters as the element [0 | h0]. Warp aggregates compose
-// in shared memory and the windowed decoupled look-back links tiles. The
-// backward carries the adjoint with M_t^T through the same affine monoid,
-// rebuilds h_{t-1} from the forward's chunk carries (the state at each tile
-// start, k floats per lane) instead of reading the stored outputs, and
-// recomputes cos/sin once per angle. The fast kernels derive the planes of
+// through the same rotations, and tiles are linked by a decoupled look-back
+// along each lane's chain. The backward carries the adjoint with M_t^T: over
+// the same tile its aggregate is [P^T | q'], so it reuses the forward's P
+// (the carries) and pushes only q'; it reads h_{t-1} from the stored outputs
+// and recomputes cos/sin once per angle. The fast kernels derive the planes of
 // round r from (k, r) -- the brick-wall layout both mixers build
 // (min_gru.py:2544-2549, 2202-2219): planes (i, i+1 mod k) for
 // i = r%2, r%2+2, ... -- and are used when the caller vouches for that
@@ -59,46 +57,13 @@ struct Args {
   E* dgamma;
   E* db;
   E* dh0;
-  float* carries;   // (tiles, K, 32) state at each tile start
+  float* carries;   // fast kernels: (items, K*K, 128) linear part of each forward tile aggregate
+  float* lin;       // where the forward's tile linear parts live (carries, or the workspace)
+  long long lin_ld; // floats per work item in `lin`
   long long T_, n, sper, nstrips, nchunks, ntiles;
   int R, K, has_scale, has_decay;
   Lookback lb;
 };
-
-// Affine monoid on k x (k+1) maps x -> P x + q, stored row-major [P | q].
-template <int K>
-struct AffMonoid {
-  static constexpr int W = K + 1;
-  static constexpr int NF = K * W;
-  __device__ static void identity(float (&x)[NF]) {
-#pragma unroll
-    for (int i = 0; i < K; ++i)
-#pragma unroll
-      for (int j = 0; j < W; ++j) x[i * W + j] = (i == j) ? 1.f : 0.f;
-  }
-  // earlier e then later l: [Pl Pe | Pl qe + ql]; column by column, so o may alias e.
-  __device__ static void combine(const float (&e)[NF], const float (&l)[NF], float (&o)[NF]) {
-#pragma unroll
-    for (int j = 0; j < W; ++j) {
-      float col[K];
-#pragma unroll
-      for (int i = 0; i < K; ++i) {
-        float s = j == K ? l[i * W + K] : 0.f;
-#pragma unroll
-        for (int q = 0; q < K; ++q) s = fmaf(l[i * W + q], e[q * W + j], s);
-        col[i] = s;
-      }
-#pragma unroll
-      for (int i = 0; i < K; ++i) o[i * W + j] = col[i];
-    }
-  }
-};
-
-// acc <- acc then later (the monoids' combine may write over its earlier operand).
-template <class M, int NF>
-__device__ __forceinline__ void combine_into(float (&acc)[NF], const float (&later)[NF]) {
-  M::combine(acc, later, acc);
-}
 
 // Per-step coefficients of one lane: cos/sin of its R*K/2 angles, gamma, scale.
 template <int K, int R>
@@ -106,19 +71,6 @@ struct StepCoef {
   float c[R * (K / 2)], s[R * (K / 2)];
   float gamma, scale;
 };
-
-template <typename E, int K, int R>
-__device__ __forceinline__ void load_coef(const Args<E>& p, size_t st, StepCoef<K, R>& cf) {
-  constexpr int NA = R * (K / 2);
-  float th[NA];
-  const E* tp = p.theta + st * NA;
-#pragma unroll
-  for (int i = 0; i < NA; ++i) th[i] = to_f32<E>(__ldcs(tp + i));
-#pragma unroll
-  for (int i = 0; i < NA; ++i) sincosf(th[i], &cf.s[i], &cf.c[i]);
-  cf.gamma = p.has_decay ? to_f32<E>(__ldcs(p.gamma + st)) : 1.f;
-  cf.scale = p.has_scale ? to_f32<E>(__ldcs(p.scale + st)) : 1.f;
-}
 
 // Plane m of round r: (i, j) = ((r%2 + 2m) % K, (i + 1) % K).
 template <int K>
@@ -170,47 +122,146 @@ __device__ __forceinline__ void apply_Mt(float (&a)[K], const StepCoef<K, R>& cf
   if (hs) a[1] *= cf.scale;
 }
 
-// X <- M X + [0 | bvec] on all K+1 columns of the aggregate. Without a scale
-// M = gamma R (R a product of rotations), so the P columns can take R alone
-// (pd = false) and the caller multiplies them by the product of the gammas
-// once per tile: the decay then costs K multiplies per step instead of K^2 + K.
-template <int K, int R>
-__device__ __forceinline__ void agg_step(float (&X)[K * (K + 1)], const StepCoef<K, R>& cf,
-                                         const float (&bv)[K], bool hs, bool hd, bool pd) {
-#pragma unroll
-  for (int j = 0; j <= K; ++j) {
-    float col[K];
-#pragma unroll
-    for (int i = 0; i < K; ++i) col[i] = X[i * (K + 1) + j];
-    apply_M<K, R>(col, cf, hs, j == K ? hd : pd);
-#pragma unroll
-    for (int i = 0; i < K; ++i) X[i * (K + 1) + j] = col[i] + (j == K ? bv[i] : 0.f);
+// cos / sin of the fast kernels' angles. Method: Cody-Waite reduction by
+// pi/2 (W. J. Cody and W. Waite, Software Manual for the Elementary
+// Functions, 1980) with a two-part fp32 pi/2 in fused multiply-adds -- the
+// first product is exact, so r = x - k pi/2 takes one rounding -- then
+// near-minimax polynomials on |r| <= 1.0005 pi/4, fitted for this file by
+// Lawson's iteratively reweighted least squares in fp64 and rounded to fp32:
+//   sin r = r + r^3 (S1 + S2 r^2 + S3 r^4)
+//   cos r = 1 + r^2 (C1 + C2 r^2 + C3 r^4 + C4 r^6)
+// and the quadrant k mod 4 read from the low bits of the rounding sum
+// x (2/pi) + 1.5 2^23. Two angles go through one chain of paired FP32
+// instructions. Measured in an fp32 emulation over |x| <= 8192 against fp64:
+// absolute error <= 1.3 2^-24 for both; larger |x|, inf and NaN take
+// sincosf. About a third of the instructions of two sincosf calls.
+constexpr float kTwoOverPi = 0x1.45f306p-1f, kRoundMagic = 0x1.8p23f;
+constexpr float kPio2Hi = 0x1.921fb6p+0f, kPio2Lo = -0x1.777a5cp-25f;
+constexpr float kSinP1 = -0x1.555546p-3f, kSinP2 = 0x1.110736p-7f, kSinP3 = -0x1.994226p-13f;
+constexpr float kCosP1 = -0x1.0p-1f, kCosP2 = 0x1.55553ep-5f, kCosP3 = -0x1.6c0878p-10f,
+                kCosP4 = 0x1.99327p-16f;
+constexpr float kSinCosFastArg = 8192.f;
+
+__device__ __noinline__ float2 sincos_wide(float x) {  // (sin, cos) of a large or non-finite x
+  float s, c;
+  sincosf(x, &s, &c);
+  return make_float2(s, c);
+}
+
+// Polynomial values (s, c) at r, rotated into quadrant j mod 4.
+__device__ __forceinline__ void sincos_quadrant(float s, float c, unsigned j, float& so,
+                                                float& co) {
+  const bool sw = (j & 1u) != 0u;
+  so = __uint_as_float(__float_as_uint(sw ? c : s) ^ ((j & 2u) << 30));
+  co = __uint_as_float(__float_as_uint(sw ? s : c) ^ (((j + 1u) & 2u) << 30));
+}
+
+__device__ __forceinline__ float2 dup2(float x) { return make_float2(x, x); }
+
+__device__ __forceinline__ void sincos_pair(float xa, float xb, float& sa, float& ca, float& sb,
+                                            float& cb) {
+  const float2 x = make_float2(xa, xb);
+  const float2 t = __ffma2_rn(x, dup2(kTwoOverPi), dup2(kRoundMagic));
+  const float2 k = __fadd2_rn(t, dup2(-kRoundMagic));
+  float2 r = __ffma2_rn(k, dup2(-kPio2Hi), x);
+  r = __ffma2_rn(k, dup2(-kPio2Lo), r);
+  const float2 r2 = __fmul2_rn(r, r);
+  float2 ps = __ffma2_rn(dup2(kSinP3), r2, dup2(kSinP2));
+  ps = __ffma2_rn(ps, r2, dup2(kSinP1));
+  const float2 s = __ffma2_rn(__fmul2_rn(r2, r), ps, r);
+  float2 pc = __ffma2_rn(dup2(kCosP4), r2, dup2(kCosP3));
+  pc = __ffma2_rn(pc, r2, dup2(kCosP2));
+  pc = __ffma2_rn(pc, r2, dup2(kCosP1));
+  const float2 c = __ffma2_rn(r2, pc, dup2(1.f));
+  sincos_quadrant(s.x, c.x, __float_as_uint(t.x), sa, ca);
+  sincos_quadrant(s.y, c.y, __float_as_uint(t.y), sb, cb);
+  if (!(fabsf(xa) <= kSinCosFastArg)) {
+    const float2 w = sincos_wide(xa);
+    sa = w.x;
+    ca = w.y;
+  }
+  if (!(fabsf(xb) <= kSinCosFastArg)) {
+    const float2 w = sincos_wide(xb);
+    sb = w.x;
+    cb = w.y;
   }
 }
 
-// Reverse aggregate step: Q <- M^T (g + Q), P <- M^T P (columns 0..K-1 = P,
-// K = Q); pd as in agg_step.
-template <int K, int R>
-__device__ __forceinline__ void ragg_step(float (&X)[K * (K + 1)], const StepCoef<K, R>& cf,
-                                          const float (&g)[K], bool hs, bool hd, bool pd) {
+__device__ __forceinline__ void sincos_one(float x, float& so, float& co) {
+  const float t = fmaf(x, kTwoOverPi, kRoundMagic);
+  const float k = t - kRoundMagic;
+  float r = fmaf(k, -kPio2Hi, x);
+  r = fmaf(k, -kPio2Lo, r);
+  const float r2 = r * r;
+  const float ps = fmaf(fmaf(kSinP3, r2, kSinP2), r2, kSinP1);
+  const float s = fmaf(r2 * r, ps, r);
+  const float pc = fmaf(fmaf(fmaf(kCosP4, r2, kCosP3), r2, kCosP2), r2, kCosP1);
+  const float c = fmaf(r2, pc, 1.f);
+  sincos_quadrant(s, c, __float_as_uint(t), so, co);
+  if (!(fabsf(x) <= kSinCosFastArg)) {
+    const float2 w = sincos_wide(x);
+    so = w.x;
+    co = w.y;
+  }
+}
+
+// (sin, cos) of n angles.
+template <int N>
+__device__ __forceinline__ void sincos_n(const float (&a)[N], float* s, float* c) {
 #pragma unroll
-  for (int j = 0; j <= K; ++j) {
-    float col[K];
+  for (int i = 0; i + 1 < N; i += 2) sincos_pair(a[i], a[i + 1], s[i], c[i], s[i + 1], c[i + 1]);
+  if (N & 1) sincos_one(a[N - 1], s[N - 1], c[N - 1]);
+}
+
+// A forward tile aggregate x -> P x + q keeps its linear part P (K x K) as
+// K/2 pairs of columns, Pp[i][m] = (P[i][2m], P[i][2m+1]): one sm_100 paired
+// FP32 instruction (__ffma2_rn / __fmul2_rn, per component the same rounding
+// as fmaf / a product) then advances two columns, so the per-step push of the
+// K columns of P issues half the instructions of a column-by-column push and
+// gives the same bits.
+// Plane rotations of round r on a pair of columns (rotate() on each column).
+template <int K>
+__device__ __forceinline__ void rotate2(float2 (&v)[K], const float* c, const float* s, int r) {
+  const int st = r & 1;
 #pragma unroll
-    for (int i = 0; i < K; ++i) col[i] = X[i * (K + 1) + j] + (j == K ? g[i] : 0.f);
-    apply_Mt<K, R>(col, cf, hs, j == K ? hd : pd);
-#pragma unroll
-    for (int i = 0; i < K; ++i) X[i * (K + 1) + j] = col[i];
+  for (int m = 0; m < K / 2; ++m) {
+    const int i = st ? ((1 + 2 * m) % K) : (2 * m);
+    const int j = (i + 1) % K;
+    const float2 C = dup2(c[m]), S = dup2(s[m]), NS = dup2(-s[m]);
+    const float2 vi = v[i], vj = v[j];
+    v[i] = __ffma2_rn(C, vi, __fmul2_rn(NS, vj));
+    v[j] = __ffma2_rn(S, vi, __fmul2_rn(C, vj));
   }
 }
 
 template <int K>
-__device__ __forceinline__ void fold_state(float (&X)[K * (K + 1)], const float (&h)[K]) {
+__device__ __forceinline__ void lin_identity(float2 (&Pp)[K][K / 2]) {
 #pragma unroll
-  for (int i = 0; i < K; ++i) {
+  for (int i = 0; i < K; ++i)
 #pragma unroll
-    for (int j = 0; j < K; ++j) X[i * (K + 1) + j] = 0.f;
-    X[i * (K + 1) + K] = h[i];
+    for (int m = 0; m < K / 2; ++m)
+      Pp[i][m] = make_float2(i == 2 * m ? 1.f : 0.f, i == 2 * m + 1 ? 1.f : 0.f);
+}
+
+// P <- M P. Without a scale M = gamma R (R a product of rotations), so the P
+// columns take R alone (pd = false) and the caller multiplies them by the
+// product of the gammas once per tile: the decay then costs nothing per step.
+template <int K, int R>
+__device__ __forceinline__ void lin_step(float2 (&Pp)[K][K / 2], const StepCoef<K, R>& cf,
+                                         bool hs, bool pd) {
+#pragma unroll
+  for (int m = 0; m < K / 2; ++m) {
+    float2 col[K];
+#pragma unroll
+    for (int i = 0; i < K; ++i) col[i] = Pp[i][m];
+    if (hs) col[1] = __fmul2_rn(col[1], dup2(cf.scale));
+#pragma unroll
+    for (int r = 0; r < R; ++r) rotate2<K>(col, cf.c + r * (K / 2), cf.s + r * (K / 2), r);
+    if (pd)
+#pragma unroll
+      for (int i = 0; i < K; ++i) col[i] = __fmul2_rn(col[i], dup2(cf.gamma));
+#pragma unroll
+    for (int i = 0; i < K; ++i) Pp[i][m] = col[i];
   }
 }
 
@@ -231,15 +282,20 @@ __device__ __forceinline__ void store_k(E* dst, const float (&o)[K]) {
 // One thread owns one (b, block) lane over a time tile of L steps; a CTA is
 // 128 consecutive lanes of one tile (a work item, handed out in order by an
 // atomic counter: all lanes' tile 0 first). Per item:
-//   1. aggregate: push the k+1 columns of [I | 0] through the tile's steps
-//      (forward: M_t, backward: M_t^T with the upstream gradient injected);
+//   1. aggregate: the forward pushes the k columns of I (in pairs, see
+//      lin_step) and the column 0 through the tile's steps M_t, giving
+//      x -> P x + q; the backward's aggregate over the same tile is
+//      a -> P^T a + q', so it takes P from the forward (saved as the
+//      carries, one K x K matrix per lane and tile) and pushes only the
+//      adjoint column q' (M_t^T with the upstream gradient injected);
 //   2. publish it, then look back along the lane's own chain for the nearest
 //      earlier tile whose carried vector (state, or adjoint) is published,
 //      and apply the aggregates in between to it (k x (k+1) times a vector:
 //      no k x k compositions); publish this tile's outgoing vector;
 //   3. replay the tile from its incoming vector, writing the outputs.
-// Per lane and tile the workspace holds a flag, the aggregate and the
-// outgoing vector, 128 lanes interleaved so a warp's accesses coalesce.
+// Per lane and tile the workspace holds a flag, q and the outgoing vector
+// (and P when no carries are kept), 128 lanes interleaved so a warp's
+// accesses coalesce.
 
 template <int W>
 struct VecWord;  // the vector type moving W bytes
@@ -277,17 +333,6 @@ struct Vec {  // N elements of E as the widest aligned vector chunks
     }
   }
 };
-
-template <typename E, int K, int R>
-__device__ __forceinline__ void load_coef_v(const Args<E>& p, size_t st, StepCoef<K, R>& cf) {
-  constexpr int NA = R * (K / 2);
-  float th[NA];
-  Vec<E, NA>::load(p.theta + st * NA, th);
-#pragma unroll
-  for (int i = 0; i < NA; ++i) sincosf(th[i], &cf.s[i], &cf.c[i]);
-  cf.gamma = p.has_decay ? to_f32<E>(__ldcs(p.gamma + st)) : 1.f;
-  cf.scale = p.has_scale ? to_f32<E>(__ldcs(p.scale + st)) : 1.f;
-}
 
 // Loaded-but-unconverted inputs of one step, so the loads of later steps can
 // be issued before the current step is computed (software prefetch).
@@ -328,8 +373,7 @@ struct StepIn {
   __device__ __forceinline__ void coef(StepCoef<K, R>& cf, bool hs, bool hd) const {
     float a[R * (K / 2)];
     th.get(a);
-#pragma unroll
-    for (int i = 0; i < R * (K / 2); ++i) sincosf(a[i], &cf.s[i], &cf.c[i]);
+    sincos_n<R * (K / 2)>(a, cf.s, cf.c);
     cf.gamma = hd ? to_f32<E>(gam) : 1.f;
     cf.scale = hs ? to_f32<E>(sc) : 1.f;
   }
@@ -357,7 +401,7 @@ constexpr int kLanes = 128;  // lanes (threads) per work item
 
 struct TileRec {  // one work item's records in the workspace
   unsigned* flag;  // [128]
-  float* agg;      // [NF][128]
+  float* agg;      // [NF][128]: P row-major (f = i*K + c < K*K, when kept here), then q
   float* vec;      // [K][128]
 };
 
@@ -395,11 +439,13 @@ __device__ __forceinline__ unsigned wait_flag(const unsigned* f, unsigned* err) 
 
 // Carried vector entering `item`: walk back along the lane's chain (stride
 // `G` items) to the nearest published vector, then apply the aggregates of
-// the items in between, oldest first: v <- P v + q.
-template <int K>
+// the items in between, oldest first: v <- L v + q, where L is P (forward) or
+// P^T (TR, backward) of the forward tile behind that item (`lin_at(j)`, row-
+// major, 128 lanes interleaved) and q is the item's published column.
+template <int K, bool TR, class LinAt>
 __device__ __forceinline__ void look_back(unsigned char* ws, long long items, unsigned* err,
-                                          long long item, long long G, float (&v)[K]) {
-  constexpr int W = K + 1;
+                                          long long item, long long G, LinAt lin_at,
+                                          float (&v)[K]) {
   const int t = threadIdx.x;
   long long j = item - G;
   int nagg = 0;
@@ -416,12 +462,14 @@ __device__ __forceinline__ void look_back(unsigned char* ws, long long items, un
   }
   for (int q = nagg; q >= 1; --q) {
     const TileRec r = rec_of<K>(ws, items, item - q * G);
+    const float* P = lin_at(item - q * G);
     float o[K];
 #pragma unroll
     for (int i = 0; i < K; ++i) {
-      float s = r.agg[(i * W + K) * kLanes + t];
+      float s = r.agg[(K * K + i) * kLanes + t];
 #pragma unroll
-      for (int c = 0; c < K; ++c) s = fmaf(r.agg[(i * W + c) * kLanes + t], v[c], s);
+      for (int c = 0; c < K; ++c)
+        s = fmaf(P[(TR ? c * K + i : i * K + c) * kLanes + t], v[c], s);
       o[i] = s;
     }
 #pragma unroll
@@ -430,10 +478,23 @@ __device__ __forceinline__ void look_back(unsigned char* ws, long long items, un
 }
 
 template <int K>
-__device__ __forceinline__ void publish_agg(const TileRec& r, const float (&X)[K * (K + 1)]) {
+__device__ __forceinline__ void store_lin(float* P, const float2 (&Pp)[K][K / 2]) {
   const int t = threadIdx.x;
 #pragma unroll
-  for (int f = 0; f < K * (K + 1); ++f) r.agg[f * kLanes + t] = X[f];
+  for (int i = 0; i < K; ++i)
+#pragma unroll
+    for (int m = 0; m < K / 2; ++m) {
+      P[(i * K + 2 * m) * kLanes + t] = Pp[i][m].x;
+      P[(i * K + 2 * m + 1) * kLanes + t] = Pp[i][m].y;
+    }
+}
+
+// The item's q column, then flag 1 (its P is already in place).
+template <int K>
+__device__ __forceinline__ void publish_agg(const TileRec& r, const float (&q)[K]) {
+  const int t = threadIdx.x;
+#pragma unroll
+  for (int i = 0; i < K; ++i) r.agg[(K * K + i) * kLanes + t] = q[i];
   st_release_u32(r.flag + t, 1u);
 }
 
@@ -445,22 +506,8 @@ __device__ __forceinline__ void publish_vec(const TileRec& r, const float (&v)[K
   st_release_u32(r.flag + t, 2u);
 }
 
-// v_out = P v_in + q for the aggregate X = [P | q].
-template <int K>
-__device__ __forceinline__ void apply_agg(const float (&X)[K * (K + 1)], const float (&vi)[K],
-                                          float (&vo)[K]) {
-#pragma unroll
-  for (int i = 0; i < K; ++i) {
-    float s = X[i * (K + 1) + K];
-#pragma unroll
-    for (int c = 0; c < K; ++c) s = fmaf(X[i * (K + 1) + c], vi[c], s);
-    vo[i] = s;
-  }
-}
-
 template <typename E, int K, int R>
-__global__ void __launch_bounds__(kLanes) fwd_tile_kernel(Args<E> p) {
-  constexpr int NF = K * (K + 1);
+__global__ void __launch_bounds__(kLanes, 3) fwd_tile_kernel(Args<E> p) {
   __shared__ unsigned s_item;
   const bool hs = p.has_scale != 0, hd = p.has_decay != 0;
   if (threadIdx.x == 0) s_item = atomicAdd(p.lb.counter, 1u);
@@ -483,8 +530,11 @@ __global__ void __launch_bounds__(kLanes) fwd_tile_kernel(Args<E> p) {
     const size_t st = lane0 + t * p.n;
     q.load(p, st, p.b + st * K, nullptr, hs, hd);
   };
-  float X[NF];
-  AffMonoid<K>::identity(X);
+  float2 Pp[K][K / 2];
+  lin_identity<K>(Pp);
+  float qv[K];
+#pragma unroll
+  for (int i = 0; i < K; ++i) qv[i] = 0.f;
   const bool pd = hd && hs;  // decay inside the P columns only when a scale is present
   float gprod = 1.f;
   stream_steps<1, SI>(t0, t1 - t0, 1, load, [&](const SI& q, long long) {
@@ -492,24 +542,38 @@ __global__ void __launch_bounds__(kLanes) fwd_tile_kernel(Args<E> p) {
     q.coef(cf, hs, hd);
     float bv[K];
     q.x.get(bv);
-    agg_step<K, R>(X, cf, bv, hs, hd, pd);
+    lin_step<K, R>(Pp, cf, hs, pd);
+    apply_M<K, R>(qv, cf, hs, hd);
+#pragma unroll
+    for (int i = 0; i < K; ++i) qv[i] += bv[i];
     gprod *= cf.gamma;
   });
   if (hd && !pd)
 #pragma unroll
     for (int i = 0; i < K; ++i)
 #pragma unroll
-      for (int j = 0; j < K; ++j) X[i * (K + 1) + j] *= gprod;
+      for (int m = 0; m < K / 2; ++m) Pp[i][m] = __fmul2_rn(Pp[i][m], dup2(gprod));
+  store_lin<K>(p.lin + item * p.lin_ld, Pp);
   float v[K];
   if (tile == 0) {
     Vec<E, K>::load(p.h0 + ((size_t)bi * p.n + blk) * K, v);
   } else {
-    publish_agg<K>(me, X);
-    look_back<K>(ws, items, p.lb.err, item, G, v);
+    publish_agg<K>(me, qv);
+    look_back<K, false>(ws, items, p.lb.err, item, G,
+                        [&](long long j) { return p.lin + j * p.lin_ld; }, v);
   }
   {
     float vo[K];
-    apply_agg<K>(X, v, vo);
+#pragma unroll
+    for (int i = 0; i < K; ++i) {
+      float s = qv[i];
+#pragma unroll
+      for (int m = 0; m < K / 2; ++m) {
+        s = fmaf(Pp[i][m].x, v[2 * m], s);
+        s = fmaf(Pp[i][m].y, v[2 * m + 1], s);
+      }
+      vo[i] = s;
+    }
     publish_vec<K>(me, vo);
   }
   stream_steps<2, SI>(t0, t1 - t0, 1, load, [&](const SI& q, long long t) {
@@ -526,7 +590,7 @@ __global__ void __launch_bounds__(kLanes) fwd_tile_kernel(Args<E> p) {
 
 template <typename E, int K, int R>
 __global__ void __launch_bounds__(kLanes) bwd_tile_kernel(Args<E> p) {
-  constexpr int NF = K * (K + 1), H = K / 2;
+  constexpr int H = K / 2;
   __shared__ unsigned s_item;
   const bool hs = p.has_scale != 0, hd = p.has_decay != 0;
   if (threadIdx.x == 0) s_item = atomicAdd(p.lb.counter, 1u);
@@ -550,34 +614,43 @@ __global__ void __launch_bounds__(kLanes) bwd_tile_kernel(Args<E> p) {
     const size_t st = lane0 + t * p.n;
     q.load(p, st, p.gout + st * K, nullptr, hs, hd);
   };
-  float X[NF];
-  AffMonoid<K>::identity(X);
-  const bool pd = hd && hs;  // decay inside the P columns only when a scale is present
-  float gprod = 1.f;
+  // Adjoint column of this tile's aggregate; its linear part is P^T of the
+  // forward tile (saved by the forward in `lin`).
+  float qv[K];
+#pragma unroll
+  for (int i = 0; i < K; ++i) qv[i] = 0.f;
   stream_steps<1, SA>(t1 - 1, t1 - t0, -1, load_a, [&](const SA& q, long long) {
     StepCoef<K, R> cf;
     q.coef(cf, hs, hd);
     float g[K];
     q.x.get(g);
-    ragg_step<K, R>(X, cf, g, hs, hd, pd);
-    gprod *= cf.gamma;
+#pragma unroll
+    for (int i = 0; i < K; ++i) qv[i] += g[i];
+    apply_Mt<K, R>(qv, cf, hs, hd);
   });
-  if (hd && !pd)
-#pragma unroll
-    for (int i = 0; i < K; ++i)
-#pragma unroll
-      for (int j = 0; j < K; ++j) X[i * (K + 1) + j] *= gprod;
+  auto lin_at = [&](long long j) {  // backward item j -> the forward item of its tile
+    const long long rt = j / G;
+    return p.lin + ((p.ntiles - 1 - rt) * G + (j - rt * G)) * p.lin_ld;
+  };
   float y[K];
   if (rtile == 0) {
 #pragma unroll
     for (int i = 0; i < K; ++i) y[i] = 0.f;
   } else {
-    publish_agg<K>(me, X);
-    look_back<K>(ws, items, p.lb.err, item, G, y);
+    publish_agg<K>(me, qv);
+    look_back<K, true>(ws, items, p.lb.err, item, G, lin_at, y);
   }
   {
+    const float* P = lin_at(item);
+    const int t = threadIdx.x;
     float yo[K];
-    apply_agg<K>(X, y, yo);
+#pragma unroll
+    for (int i = 0; i < K; ++i) {
+      float s = qv[i];
+#pragma unroll
+      for (int c = 0; c < K; ++c) s = fmaf(P[(c * K + i) * kLanes + t], y[c], s);
+      yo[i] = s;
+    }
     publish_vec<K>(me, yo);
   }
   using SB = StepIn<E, K, R, true>;
@@ -783,6 +856,14 @@ int launch_fast(bool fwd, Args<E>& p, const Geometry& g, void* ws, cudaStream_t 
   MGS_CUDA_OK(cudaMemsetAsync(ws, 0, 256 + (size_t)g.items * kLanes * 4, st));
   p.lb.counter = static_cast<unsigned*>(ws);
   p.lb.err = static_cast<unsigned*>(ws) + 1;
+  if (p.carries != nullptr) {  // the forward keeps each tile's P for the backward
+    p.lin = p.carries;
+    p.lin_ld = (long long)K * K * kLanes;
+  } else {  // forward without a backward to follow: P only for the look-back
+    p.lin = reinterpret_cast<float*>(static_cast<unsigned char*>(ws) + 256 +
+                                     (size_t)g.items * kLanes * 4);
+    p.lin_ld = (long long)K * (K + 1) * kLanes;
+  }
   p.nstrips = g.G;
   p.nchunks = g.L;
   p.ntiles = g.ntiles;
@@ -797,8 +878,11 @@ inline size_t workspace_bytes(const Geometry& g, int k) {
   return g.fast ? 256 + (size_t)g.items * kLanes * 4 * (1 + g.nf + k) : 256;
 }
 
-// The fast backward reads the forward's stored states: no carries.
-inline size_t carry_bytes(const Geometry&, int) { return 0; }
+// The fast kernels' carries: the linear part P (k x k) of every forward tile
+// aggregate, which the backward's tile aggregates use transposed.
+inline size_t carry_bytes(const Geometry& g, int k) {
+  return g.fast ? (size_t)g.items * kLanes * k * k * 4 : 0;
+}
 
 template <typename E>
 int run(bool fwd, const Args<E>& a0, long long B, long long T, long long n, int R, int k,
@@ -821,7 +905,7 @@ int run(bool fwd, const Args<E>& a0, long long B, long long T, long long n, int 
     return MGS_WORKSPACE_TOO_SMALL;
   if (g.fast) {
     if (g.items > 0x7fffffffLL) return MGS_UNSUPPORTED;
-    if (!fwd && p.out == nullptr) return MGS_BAD_SHAPE;
+    if (!fwd && (p.out == nullptr || p.carries == nullptr)) return MGS_BAD_SHAPE;
     p.sper = B * n;
     int rc = MGS_UNSUPPORTED;
     with_kr(k, R, [&]<int K, int RR>() { rc = launch_fast<E, K, RR>(fwd, p, g, ws, st); });

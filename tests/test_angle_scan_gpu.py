@@ -118,3 +118,76 @@ def test_full_config4(cuda):
     d = C.angle_full_config4()
     ref_h, ref_g = oracle_ref(d, 0, 1)
     check(run(d, cuda, 0, 1), ref_h, ref_g, 0, 1, EAGER_DEV["angle_full_config4"], "config4")
+
+
+@pytest.mark.parametrize("hs,hd", [(0, 1), (1, 1), (0, 0)])
+def test_forward_without_grad(cuda, hs, hd):
+    """A forward with nothing to differentiate keeps the tiles' linear parts
+    in the workspace instead of the saved carries; its output must be the
+    same bits as the autograd forward's (and meet the oracle)."""
+    import mingru_b200 as mb
+
+    k, R = (2, 1) if hs else (8, 2)
+    d = make_inputs(3, 700, 45, R, k, seed=11, has_scale=hs, has_decay=hd)
+    t = lambda key: torch.as_tensor(d[key], dtype=torch.float32, device=cuda)
+    args = [t(x) for x in ("theta", "scale", "gamma", "b", "h0")]
+    meta = [torch.as_tensor(d["perm"], dtype=torch.int32, device=cuda),
+            torch.as_tensor(d["sgn"], dtype=torch.float32, device=cuda),
+            torch.as_tensor(d["p2p"], dtype=torch.int32, device=cuda)]
+    with torch.no_grad():
+        h_ng = mb.angle_scan_impl(*args, *meta, has_scale=hs, has_decay=hd)
+    h_g = mb.angle_scan_impl(*[a.clone().requires_grad_(True) for a in args], *meta,
+                             has_scale=hs, has_decay=hd)
+    mb.raise_device_error(cuda)
+    assert torch.equal(h_ng, h_g.detach())
+    if hd:  # with decay the states stay bounded and fp32 meets the forward bar
+        ref_h, _ = oracle_ref(d, hs, hd)
+        np.testing.assert_allclose(f64(h_ng), ref_h, **FWD)
+
+
+def test_step_angles_match_fp64(cuda):
+    """One step of a k=2, R=1 rotation from h0 = (1, 0) with b = 0 and no
+    decay returns (cos theta, sin theta) exactly as the fast kernels compute
+    them (their own reduction by pi/2 and polynomials; sincosf beyond
+    |theta| > 8192). Bars: absolute error <= 2^-23 against fp64 on the
+    polynomial range (the method's bound is 1.3 * 2^-24), <= 2^-22 where
+    sincosf takes over, and within 2^-22 of CUDA's own fp32 sin / cos."""
+    import math
+
+    import mingru_b200 as mb
+
+    g = torch.Generator().manual_seed(5)
+    k = torch.arange(-5000, 5001, dtype=torch.float64)
+    parts = [
+        (torch.rand(1 << 18, generator=g, dtype=torch.float64) * 2 - 1) * math.pi,
+        (torch.rand(1 << 16, generator=g, dtype=torch.float64) * 2 - 1) * 8192,
+        k * math.pi / 2, (k + 0.5) * math.pi / 2,
+        torch.tensor([0.0, -0.0, 1e-30, -1e-30, 8191.9, -8191.9]),
+    ]
+    fast = torch.cat(parts).float()
+    wide = torch.cat([(torch.rand(4096, generator=g, dtype=torch.float64) * 2 - 1) * 1e6,
+                      torch.tensor([8192.5, -8192.5, 1e20, -3e38])]).float()
+    theta = torch.cat([fast, wide])
+    n = theta.numel()
+    th = theta.to(cuda).view(1, 1, n, 1, 1)
+    ones = torch.ones(1, 1, n, device=cuda)
+    b = torch.zeros(1, 1, n, 2, device=cuda)
+    h0 = torch.zeros(1, n, 2, device=cuda)
+    h0[..., 0] = 1.0
+    perm, sgn, p2p = (torch.as_tensor(x, device=cuda) for x in C.brickwall(1, 2))
+    h = mb.angle_scan_impl(th, ones, ones, b, h0, perm.int(), sgn.float(), p2p.int(),
+                           has_scale=0, has_decay=0)
+    mb.raise_device_error(cuda)
+    got_c, got_s = h[0, 0, :, 0].double().cpu(), h[0, 0, :, 1].double().cpu()
+    t64 = theta.double()
+    ec, es = (got_c - torch.cos(t64)).abs(), (got_s - torch.sin(t64)).abs()
+    nf = fast.numel()
+    print(f"fast range: max |cos err| {ec[:nf].max():.3e}, |sin err| {es[:nf].max():.3e}; "
+          f"sincosf range: {ec[nf:].max():.3e}, {es[nf:].max():.3e}")
+    assert ec[:nf].max() <= 2.0 ** -23 and es[:nf].max() <= 2.0 ** -23
+    assert ec[nf:].max() <= 2.0 ** -22 and es[nf:].max() <= 2.0 ** -22
+    tc = th.view(-1)
+    dc = (h[0, 0, :, 0] - torch.cos(tc)).abs().max().item()
+    ds = (h[0, 0, :, 1] - torch.sin(tc)).abs().max().item()
+    print(f"against CUDA fp32 cos / sin: {dc:.3e} {ds:.3e}")
+    assert dc <= 2.0 ** -22 and ds <= 2.0 ** -22
