@@ -96,9 +96,25 @@ def test_vs_oracle(cuda, case):
           str(case))
 
 
+# Wider lane groups of the fast kernels: a partial last group of 128 lanes
+# spanning two batch rows, k = 4, R = 3 with a ragged last tile, and a scale.
+# The states stay bounded (decay), so fp32 meets the bar directly.
+WIDE_CASES = [(3, 300, 68, 2, 8, 0, 1), (2, 200, 64, 2, 4, 0, 1), (1, 257, 128, 3, 8, 0, 1),
+              (2, 150, 72, 2, 8, 1, 1)]
+
+
+@pytest.mark.parametrize("case", WIDE_CASES)
+def test_wide_groups_vs_oracle(cuda, case):
+    B, T, n, R, k, hs, hd = case
+    d = make_inputs(B, T, n, R, k, seed=sum(case), has_scale=hs, has_decay=hd)
+    ref_h, ref_g = oracle_ref(d, hs, hd)
+    check(run(d, cuda, hs, hd), ref_h, ref_g, hs, hd, None, str(case))
+
+
+@pytest.mark.parametrize("n", [9, 72])
 @pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
-def test_half_inputs(cuda, dtype):
-    d = make_inputs(2, 40, 9, 2, 8, seed=4, has_scale=0, has_decay=1)
+def test_half_inputs(cuda, dtype, n):
+    d = make_inputs(2, 40, n, 2, 8, seed=4, has_scale=0, has_decay=1)
     rnd = lambda x: torch.as_tensor(x, dtype=torch.float32).to(dtype).double().numpy()
     for key in ("theta", "scale", "gamma", "b", "h0", "grad_h"):
         d[key] = rnd(d[key])
