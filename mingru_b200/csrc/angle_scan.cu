@@ -437,43 +437,81 @@ __device__ __forceinline__ unsigned wait_flag(const unsigned* f, unsigned* err) 
   return v;
 }
 
+// One look-back hop's payload: the linear part L of the forward tile behind
+// the item (row-major, from `lin`) and the item's published column q.
+template <int K>
+__device__ __forceinline__ void hop_load(const float* P, const float* agg, float (&h)[K * K + K]) {
+  const int t = threadIdx.x;
+#pragma unroll
+  for (int f = 0; f < K * K; ++f) h[f] = __ldcg(P + f * kLanes + t);
+#pragma unroll
+  for (int i = 0; i < K; ++i) h[K * K + i] = __ldcg(agg + (K * K + i) * kLanes + t);
+}
+
+// v <- L v + q with L = P (forward) or P^T (TR, backward).
+template <int K, bool TR>
+__device__ __forceinline__ void hop_apply(const float (&h)[K * K + K], float (&v)[K]) {
+  float o[K];
+#pragma unroll
+  for (int i = 0; i < K; ++i) {
+    float s = h[K * K + i];
+#pragma unroll
+    for (int c = 0; c < K; ++c) s = fmaf(h[TR ? c * K + i : i * K + c], v[c], s);
+    o[i] = s;
+  }
+#pragma unroll
+  for (int i = 0; i < K; ++i) v[i] = o[i];
+}
+
 // Carried vector entering `item`: walk back along the lane's chain (stride
 // `G` items) to the nearest published vector, then apply the aggregates of
 // the items in between, oldest first: v <- L v + q, where L is P (forward) or
 // P^T (TR, backward) of the forward tile behind that item (`lin_at(j)`, row-
 // major, 128 lanes interleaved) and q is the item's published column.
+// The walk reads the flags of 8 predecessors per round trip (relaxed loads,
+// then one acquire fence), not one flag per round trip; each hop's payload
+// (72 loads) then costs about one memory latency.
 template <int K, bool TR, class LinAt>
 __device__ __forceinline__ void look_back(unsigned char* ws, long long items, unsigned* err,
                                           long long item, long long G, LinAt lin_at,
                                           float (&v)[K]) {
+  constexpr int kBatch = 8;
   const int t = threadIdx.x;
-  long long j = item - G;
+  long long j = item - G;  // nearest predecessor not examined yet
   int nagg = 0;
+  unsigned fv = 0u;        // flag of the item where the walk stops
   while (true) {
-    const TileRec r = rec_of<K>(ws, items, j);
-    const unsigned f = wait_flag(r.flag + t, err);
-    if (f == 2u || j < G) {
+    unsigned f[kBatch];
 #pragma unroll
-      for (int i = 0; i < K; ++i) v[i] = f == 2u ? r.vec[i * kLanes + t] : 0.f;
-      break;
+    for (int i = 0; i < kBatch; ++i) {
+      const long long jj = j - i * G;
+      f[i] = jj >= 0 ? ld_relaxed_u32(rec_of<K>(ws, items, jj).flag + t) : 2u;
     }
-    ++nagg;
-    j -= G;
+    int i = 0;
+    bool stop = false;
+    for (; i < kBatch; ++i) {
+      const long long jj = j - i * G;
+      if (f[i] == 0u) f[i] = wait_flag(rec_of<K>(ws, items, jj).flag + t, err);
+      if (f[i] == 2u || jj < G) {
+        stop = true;
+        fv = f[i];
+        break;
+      }
+    }
+    nagg += i;
+    j -= (long long)i * G;
+    if (stop) break;
   }
-  for (int q = nagg; q >= 1; --q) {
-    const TileRec r = rec_of<K>(ws, items, item - q * G);
-    const float* P = lin_at(item - q * G);
-    float o[K];
+  asm volatile("fence.acq_rel.gpu;" ::: "memory");  // the flags read above -> their payloads
+  {
+    const TileRec r = rec_of<K>(ws, items, j);
 #pragma unroll
-    for (int i = 0; i < K; ++i) {
-      float s = r.agg[(K * K + i) * kLanes + t];
-#pragma unroll
-      for (int c = 0; c < K; ++c)
-        s = fmaf(P[(TR ? c * K + i : i * K + c) * kLanes + t], v[c], s);
-      o[i] = s;
-    }
-#pragma unroll
-    for (int i = 0; i < K; ++i) v[i] = o[i];
+    for (int i = 0; i < K; ++i) v[i] = fv == 2u ? __ldcg(r.vec + i * kLanes + t) : 0.f;
+  }
+  for (long long q = nagg; q >= 1; --q) {
+    float h[K * K + K];
+    hop_load<K>(lin_at(item - q * G), rec_of<K>(ws, items, item - q * G).agg, h);
+    hop_apply<K, TR>(h, v);
   }
 }
 
@@ -553,7 +591,8 @@ __global__ void __launch_bounds__(kLanes, 3) fwd_tile_kernel(Args<E> p) {
     for (int i = 0; i < K; ++i)
 #pragma unroll
       for (int m = 0; m < K / 2; ++m) Pp[i][m] = __fmul2_rn(Pp[i][m], dup2(gprod));
-  store_lin<K>(p.lin + item * p.lin_ld, Pp);
+  float* Pme = p.lin + item * p.lin_ld;
+  store_lin<K>(Pme, Pp);
   float v[K];
   if (tile == 0) {
     Vec<E, K>::load(p.h0 + ((size_t)bi * p.n + blk) * K, v);
@@ -563,15 +602,13 @@ __global__ void __launch_bounds__(kLanes, 3) fwd_tile_kernel(Args<E> p) {
                         [&](long long j) { return p.lin + j * p.lin_ld; }, v);
   }
   {
+    // own P read back (this thread's stores), so it holds no registers during the look-back
     float vo[K];
 #pragma unroll
     for (int i = 0; i < K; ++i) {
       float s = qv[i];
 #pragma unroll
-      for (int m = 0; m < K / 2; ++m) {
-        s = fmaf(Pp[i][m].x, v[2 * m], s);
-        s = fmaf(Pp[i][m].y, v[2 * m + 1], s);
-      }
+      for (int c = 0; c < K; ++c) s = fmaf(Pme[(i * K + c) * kLanes + threadIdx.x], v[c], s);
       vo[i] = s;
     }
     publish_vec<K>(me, vo);
@@ -824,13 +861,37 @@ inline bool with_kr(int k, int R, F&& f) {
   return false;
 }
 
-// Steps per tile: long enough to amortise the per-tile aggregate and records,
-// short enough to leave several work items per SM.
+inline int sm_count() {
+  int dev = 0, n = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return 148;
+  if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0)
+    return 148;
+  return n;
+}
+
+// Steps per tile. Work items run in waves of `slots` CTAs (three per SM,
+// less a sixteenth of headroom); an item costs its two passes (2L steps) plus
+// a look-back whose length grows with the tiles of one lane in flight at
+// once (about 0.2 step per such tile, measured at config 4). L in [8, 64]
+// minimises (waves, rounded up) x (2L + look-back), the longer L on ties.
+// Config 4 (1024 lanes, T = 4096, 148 SMs): L = 40, 824 items in two waves
+// (L = 32 gave 1024 items, 2.3 waves, and a third, mostly idle, wave).
 inline long long tile_steps(long long lanes, long long T) {
   const long long G = (lanes + kLanes - 1) / kLanes;
-  long long L = 64;
-  while (L > 8 && G * ((T + L - 1) / L) < 4LL * 148) L >>= 1;
-  return L;
+  const long long slots = 3LL * sm_count(), eff = slots - slots / 16;
+  long long best = 8;
+  double best_cost = 1e300;
+  for (long long L = 8; L <= 64; ++L) {
+    const long long tiles = (T + L - 1) / L, items = G * tiles;
+    const long long waves = (items + eff - 1) / eff;
+    const double in_flight = (double)(items < slots ? items : slots) / (double)G;
+    const double cost = (double)waves * (2.0 * (double)(L < T ? L : T) + 0.2 * in_flight);
+    if (cost <= best_cost) {
+      best_cost = cost;
+      best = L;
+    }
+  }
+  return best;
 }
 
 inline bool geometry(long long B, long long T, long long n, int R, int k, int brickwall,
