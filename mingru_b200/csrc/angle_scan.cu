@@ -872,16 +872,17 @@ inline int sm_count() {
 // Steps per tile. Work items run in waves of `slots` CTAs (three per SM,
 // less a sixteenth of headroom); an item costs its two passes (2L steps) plus
 // a look-back whose length grows with the tiles of one lane in flight at
-// once (about 0.2 step per such tile, measured at config 4). L in [8, 64]
+// once (about 0.2 step per such tile, measured at config 4). L in [8, 128]
 // minimises (waves, rounded up) x (2L + look-back), the longer L on ties.
-// Config 4 (1024 lanes, T = 4096, 148 SMs): L = 40, 824 items in two waves
-// (L = 32 gave 1024 items, 2.3 waves, and a third, mostly idle, wave).
+// Config 4 (1024 lanes, T = 4096, 148 SMs): L = 79, 416 items in one wave
+// (measured: 445 us per fwd + bwd against 463 us for L = 40 in two waves,
+// 497 us for L = 128, 479 us for L = 32 in 2.3 waves).
 inline long long tile_steps(long long lanes, long long T) {
   const long long G = (lanes + kLanes - 1) / kLanes;
   const long long slots = 3LL * sm_count(), eff = slots - slots / 16;
   long long best = 8;
   double best_cost = 1e300;
-  for (long long L = 8; L <= 64; ++L) {
+  for (long long L = 8; L <= 128; ++L) {
     const long long tiles = (T + L - 1) / L, items = G * tiles;
     const long long waves = (items + eff - 1) / eff;
     const double in_flight = (double)(items < slots ? items : slots) / (double)G;
