@@ -793,6 +793,98 @@ def run_reference(args, w) -> None:
     print(json.dumps(line), flush=True)
 
 
+REF_DIR = Path(__file__).resolve().parent / "baseline" / "_ref"
+
+
+def ref_forward_fn(w, ref):
+    """The reference's own GPU entry for this workload's op (its Triton kernels,
+    MINGRU_SCAN=triton), taking the same arguments as `w.forward`; or the reason
+    there is none. `ref` is the reference package."""
+    ts = ref.triton_scans
+    if isinstance(w, GateScanWorkload):
+        return None, "the reference has no fused gate kernel (MinGRU builds its scan inputs in torch)"
+    if isinstance(w, LogScanWorkload):
+        return (lambda lc, lv: (ref.parallel_scan_log(lc, lv),)), None
+    if isinstance(w, LinearScanWorkload):
+        return ref.linear_scan, None
+    if isinstance(w, MatrixScanWorkload):
+        return ref.matrix_scan, None
+    if isinstance(w, AngleScanWorkload):
+        def angle(theta, gamma, b, h0):
+            w._const(theta.device)
+            return (ts.angle_scan_impl(theta, w.scale, gamma, b, h0, *w.meta,
+                                       has_scale=0, has_decay=1),)
+        return angle, None
+    if isinstance(w, GatedDeltaWorkload):
+        return None, "the reference runs the decay-active delta rule eagerly only (no kernel)"
+    if isinstance(w, DeltaWorkload):
+        if w.dtype != torch.float32:
+            return None, "the reference's Triton delta kernel takes fp32 inputs only (use cfg5-fp32)"
+        return (lambda Q, K, V, beta: ts.delta_scan_impl(Q, K, V, beta, w.H0,
+                                                         chunk_size=w.chunk)), None
+    return None, f"no reference GPU entry for {w.name}"
+
+
+def run_reference_gpu(args, w) -> None:
+    """The reference's own Triton kernels for the same op, inputs and step on
+    this GPU (rank 0 only): its public op + autograd with MINGRU_SCAN=triton,
+    from the reference package in baseline/_ref. Eager steps (the reference's
+    ops launch from Python), each timed with CUDA events, median reported; each
+    step alone after an L2 flush where the footprint fits L2, as for this
+    library's line."""
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    base = {"impl": "reference-gpu", "metric": "scan fwd+bwd Gelem/s", "unit": "Gelem/s",
+            "config": w.config(1)}
+    os.environ["MINGRU_SCAN"] = "triton"
+    if not (REF_DIR / "mingru").is_dir():
+        print(json.dumps({**base, "unavailable": "reference package not in baseline/_ref"}))
+        return
+    sys.path.insert(0, str(REF_DIR))
+    import mingru as ref
+    import mingru.triton_scans  # noqa: F401  (the reference imports it lazily)
+
+    ok = ref.triton_scans.available()
+    if ok is not True:
+        print(json.dumps({**base, "unavailable": f"reference Triton path unavailable: {ok}"}))
+        return
+    fwd, why = ref_forward_fn(w, ref)
+    if fwd is None:
+        print(json.dumps({**base, "unavailable": why}))
+        return
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    st = w.device_setup(w.host_inputs(0), dev)
+
+    def step():
+        outs = fwd(*st["ins"])
+        return torch.autograd.grad(outs, st["ins"], st["cots"])
+
+    for _ in range(args.warmup):  # the first call JIT-compiles the kernels
+        step()
+    torch.cuda.synchronize(dev)
+    evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+           for _ in range(args.steps)]
+    flush = (torch.empty(FLUSH_BYTES, dtype=torch.uint8, device=dev)
+             if w.footprint_bytes < L2_FLUSH_THRESHOLD else None)
+    for i, (a, b) in enumerate(evs):
+        if flush is not None:
+            flush.fill_(i & 255)
+        a.record()
+        step()
+        b.record()
+    torch.cuda.synchronize(dev)
+    ms = statistics.median(a.elapsed_time(b) for a, b in evs)
+    print(json.dumps({
+        **base, "value": w.elems / (ms * 1e-3) / 1e9, "n_gpus": 1, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
+        "dtype": w.compute_dtype, "data": "synthetic (seeded, BASELINE shapes)",
+        "reference": f"mingru {ref.__version__} Triton kernels (MINGRU_SCAN=triton), "
+                     "JIT-compiled for this GPU; median of per-step CUDA-event times",
+    }), flush=True)
+
+
 def capture(fn, dev, warm: int = 2, stream=None):
     """Capture fn() (a fixed sequence of launches on the current stream) in a CUDA graph."""
     side = stream if stream is not None else torch.cuda.Stream(dev)
@@ -1543,7 +1635,9 @@ def main() -> None:
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=1000)
     ap.add_argument("--warmup", type=int, default=5)
-    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--impl", choices=["ours", "reference", "reference-gpu"], default="ours",
+                    help="reference: the reference's CPU path (the oracle port); reference-gpu: "
+                         "the reference's own Triton kernels on this GPU, if baseline/_ref holds it")
     ap.add_argument("--config", choices=sorted(WORKLOADS) + ["stack", "stack-step", "cfg1-sp",
                                                               "cfg2-sp"],
                     default="cfg2")
@@ -1571,9 +1665,9 @@ def main() -> None:
     args = ap.parse_args()
     args.warmup = max(3, args.warmup)  # timing rule: at least 3 untimed warm-up steps
     if args.config in ("cfg1-sp", "cfg2-sp"):
-        if args.impl == "reference":
-            print(json.dumps({"impl": "reference", "unavailable": "the sliced scan has no "
-                              "reference CPU arm (the reference arm times the scan path)"}))
+        if args.impl != "ours":
+            print(json.dumps({"impl": args.impl, "unavailable": "the sliced scan has no "
+                              "reference arm (the reference arms time the scan path)"}))
             return
         if int(os.environ.get("WORLD_SIZE", "1")) > 1:
             run_sp_dist(args)
@@ -1581,9 +1675,9 @@ def main() -> None:
             run_sp(args)
         return
     if args.config in ("stack", "stack-step"):
-        if args.impl == "reference":
-            print(json.dumps({"impl": "reference", "unavailable": "the stack benches have no "
-                              "reference CPU arm (the reference arm times the scan path)"}))
+        if args.impl != "ours":
+            print(json.dumps({"impl": args.impl, "unavailable": "the stack benches have no "
+                              "reference arm (the reference arms time the scan path)"}))
             return
         (run_stack if args.config == "stack" else run_stack_step)(args)
         return
@@ -1592,6 +1686,8 @@ def main() -> None:
         w.B = args.batch
     if args.impl == "reference":
         run_reference(args, w)
+    elif args.impl == "reference-gpu":
+        run_reference_gpu(args, w)
     else:
         run_ours(args, w)
 
