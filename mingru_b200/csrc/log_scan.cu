@@ -763,7 +763,7 @@ __device__ __forceinline__ float col_scan_fwd(float A, float B, float s0, float*
 // GATE: the MinGRU gate-fused form (maps 0, 1 = k, x~ (B, T, D); log h_0 from
 // p.lh0): each lane turns its segment's k, x~ into log a, log b in place first.
 template <typename E, int W, bool GATE = false, int NS = kColSegs>
-__global__ void __launch_bounds__(NS * W, NS == kColSegs ? 16 / W : 1)
+__global__ void __launch_bounds__(NS * W, NS == kColSegs ? 16 / W : 2)
     fwd_col_kernel(Args<E> p, const __grid_constant__ ColMaps maps) {
   extern __shared__ __align__(128) unsigned char col_raw[];
   const ColSmem<E, W> sm(col_raw, p.T_, 2);
@@ -917,7 +917,7 @@ __device__ __forceinline__ void col_bwd_body(const Args<E>& p, const ColSmem<E, 
 // GATE: maps 0, 1 = k, x~; 3, 4 = dk, dx~ (all (B, T, D)); log h_0 and its
 // gradient in p.lh0 / p.dlh0.
 template <typename E, int W, bool GATE = false, int NS = kColSegs>
-__global__ void __launch_bounds__(NS * W, NS == kColSegs ? 16 / W : 1)
+__global__ void __launch_bounds__(NS * W, NS == kColSegs ? 16 / W : 2)
     bwd_col_kernel(Args<E> p, const __grid_constant__ ColMaps maps) {
   extern __shared__ __align__(128) unsigned char col_raw[];
   const ColSmem<E, W> sm(col_raw, p.T_, 3);
