@@ -1649,7 +1649,10 @@ def main() -> None:
     ap.add_argument("--stack-layers", type=int, default=4)
     ap.add_argument("--stack-mixers", default="log,signed,rotation,givens",
                     help="comma-separated mixers, cycled over the layers")
-    ap.add_argument("--e2e-steps", type=int, default=5)
+    ap.add_argument("--e2e-steps", type=int, default=20,
+                    help="steps of the e2e pipeline (at most --steps); the first step's copy-in "
+                         "and the last step's copy-out overlap nothing, so few steps understate "
+                         "the steady state")
     ap.add_argument("--ref-rows", type=int, default=2,
                     help="batch rows of each CPU sample (reference arm and cpu_baseline)")
     ap.add_argument("--scaling", choices=["weak", "strong"], default="weak",
