@@ -376,7 +376,7 @@ class AngleScanWorkload(ScanWorkload):
         g = torch.Generator().manual_seed(seed)
         n, k, R = self.n, self.k, self.R
         theta = (torch.rand(rows, self.T, n, R, k // 2, generator=g) * 2 - 1) * math.pi
-        theta[:, :, :, 1, k // 2 - 1] = 0.0  # plane (k-1, 0) of round 1 fixed: 7 live rotations
+        theta[:, :, :, 1, k // 2 - 1] = 0.0  # plane (k-1, 0) of the second rotation layer fixed: 7 live rotations
         gamma = torch.sigmoid(torch.randn(rows, self.T, n, generator=g))
         b = torch.randn(rows, self.T, n, k, generator=g)
         h0 = torch.zeros(rows, n, k)
