@@ -1271,6 +1271,7 @@ def run_stack(args) -> None:
         "data": "synthetic (seeded), random-init weights",
         "config": {"workload": "MinGRUStack fwd+bwd+AdamW step (CUDA graph)", "B_per_gpu": B,
                    "T": T, "d_model": D, "n_layers": L, "mixers": mixers,
+                   "projections": "tf32" if args.tf32 else "fp32",
                    "windows": f"median of {len(wins)} windows of {args.steps} steps"},
         "eager_ms_per_step": eager_ms,
         "graph_speedup": eager_ms / per_step,
@@ -1579,6 +1580,7 @@ def run_stack_step(args) -> None:
         "data": "synthetic (seeded), random-init weights",
         "config": {"workload": "MinGRUStack.step, one token per stream (CUDA graph)",
                    "streams_per_gpu": B, "d_model": D, "n_layers": L, "mixers": mixers,
+                   "projections": "tf32" if args.tf32 else "fp32",
                    "windows": f"median of {len(wins)} windows of {args.steps} steps"},
         "eager_ms_per_step": eager_ms,
         "graph_speedup": eager_ms / per_tok,
@@ -1647,6 +1649,9 @@ def main() -> None:
     ap.add_argument("--stack-t", type=int, default=1024)
     ap.add_argument("--stack-d", type=int, default=512)
     ap.add_argument("--stack-layers", type=int, default=4)
+    ap.add_argument("--tf32", action="store_true",
+                    help="stack benches: let torch run the fp32 projections on TF32 tensor cores "
+                         "(default: exact fp32, as torch and the reference default to)")
     ap.add_argument("--stack-mixers", default="log,signed,rotation,givens",
                     help="comma-separated mixers, cycled over the layers")
     ap.add_argument("--e2e-steps", type=int, default=20,
@@ -1682,6 +1687,8 @@ def main() -> None:
             print(json.dumps({"impl": args.impl, "unavailable": "the stack benches have no "
                               "reference arm (the reference arms time the scan path)"}))
             return
+        torch.backends.cuda.matmul.allow_tf32 = args.tf32
+        torch.backends.cudnn.allow_tf32 = args.tf32
         (run_stack if args.config == "stack" else run_stack_step)(args)
         return
     w = WORKLOADS[args.config]()
